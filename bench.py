@@ -1,0 +1,416 @@
+"""Benchmark of the decode-shaped MLX-affine quantized product on B200.
+
+Workload (one "step"): the decode GEMV sweep -- x bf16 N(0,1), W N(0, 0.02^2) quantized
+affine group 64 at bits {2,3,4,8}, shapes N x K in {17408x5120, 5120x17408, 6144x5120},
+M in {1, 8}: 24 products.  All M=1 products run before the M=8 ones, so the ~550 MB of
+packed weights a step streams evict each other from the 126 MB L2 between reuses.
+
+Reported metric: achieved algorithmic HBM GB/s over the whole step
+(bytes = codes + bf16 scales/biases + x + y per product), device-timed with CUDA events,
+max over ranks.  With --gpus N each rank runs an independent replica (the decode product
+does not shard; weak scaling).
+
+--impl reference times the CPU restatement of the same operator (the reference's own
+implementation is MLX on Apple silicon and cannot run here) on a bounded sample of the
+same workload, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "qwen38-mlx-swift_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+SHAPES = [(17408, 5120), (5120, 17408), (6144, 5120)]
+BITS = [2, 3, 4, 8]
+MS = [1, 8]
+GROUP = 64
+METRIC = "qmm decode HBM GB/s (% of 8 TB/s); MoE expert-stack tokens/s at 1/2/4/8 B200"
+
+
+def algo_bytes(M, N, K, bits, group=GROUP):
+    return N * K * bits // 8 + N * (K // group) * 2 * 2 + 2 * M * K + 2 * M * N
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.t:
+            self.t.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def physical_index(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        parts = [p for p in vis.split(",") if p.strip()]
+        if local_rank < len(parts) and parts[local_rank].strip().isdigit():
+            return int(parts[local_rank])
+    return local_rank
+
+
+def build_case_weights(torch, O, dev, bits, N, K, seed, copies=1):
+    """Quantized weights for one (bits, shape): generated once on the CPU oracle for the
+    first copy; extra copies are device clones (distinct memory, same values)."""
+    w = O.normal_f32(seed, (N, K), 0.02)
+    c, s, b = O.quantize(w, GROUP, bits)
+    del w
+    tc = torch.from_numpy(c.view(np.int32)).to(dev)
+    ts = torch.from_numpy(s.view(np.int16)).view(torch.bfloat16).to(dev)
+    tb = torch.from_numpy(b.view(np.int16)).view(torch.bfloat16).to(dev)
+    out = [(tc, ts, tb)]
+    for _ in range(copies - 1):
+        out.append((tc.clone(), ts.clone(), tb.clone()))
+    return out
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import oracle as O
+    import q38
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+
+    cases = []  # (M, N, K, bits, weight triple)
+    weights = {}
+    for bi, bits in enumerate(BITS):
+        for si, (N, K) in enumerate(SHAPES):
+            weights[(bits, N, K)] = build_case_weights(torch, O, dev, bits, N, K, 1000 + 10 * bi + si)[0]
+    for M in MS:
+        for bits in BITS:
+            for (N, K) in SHAPES:
+                cases.append((M, N, K, bits))
+    xs = {(M, K): torch.from_numpy(O.normal_bf16(77 + M + K, (M, K)).view(np.int16)).view(torch.bfloat16).to(dev)
+          for M in MS for (_, K) in SHAPES}
+    ys = {(M, N): torch.empty((M, N), dtype=torch.bfloat16, device=dev) for M in MS for (N, _) in SHAPES}
+    step_bytes = sum(algo_bytes(M, N, K, b) for (M, N, K, b) in cases)
+
+    ctx = q38.context(dev)
+    stream = torch.cuda.current_stream(dev)
+    lib = q38._lib
+    lib.q38_ctx_set_stream(ctx, stream.cuda_stream)
+
+    def call(M, N, K, bits, x, y):
+        c, s, b = weights[(bits, N, K)]
+        st = lib.q38_quantized_matmul(ctx, x.data_ptr(), M, K, 0, c.data_ptr(), s.data_ptr(), b.data_ptr(),
+                                      0, N, 1, GROUP, bits, 0, y.data_ptr())
+        if st != 0:
+            raise RuntimeError(lib.q38_last_error(ctx).decode())
+
+    def step():
+        for (M, N, K, bits) in cases:
+            call(M, N, K, bits, xs[(M, K)], ys[(M, N)])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # ---------------------------------------------------------------- timed region
+    sampler = ClockSampler(physical_index(local_rank))
+    sampler.start()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * step_bytes / (ms * 1e-3) / 1e9
+
+    # per-case breakdown (same stream, events per case, averaged over a few passes)
+    per_case = []
+    reps = 3
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in cases]
+    acc = [0.0] * len(cases)
+    for _ in range(reps):
+        for i, (M, N, K, bits) in enumerate(cases):
+            evs[i][0].record(stream)
+            call(M, N, K, bits, xs[(M, K)], ys[(M, N)])
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+        for i in range(len(cases)):
+            acc[i] += evs[i][0].elapsed_time(evs[i][1])
+    for i, (M, N, K, bits) in enumerate(cases):
+        us = acc[i] / reps * 1e3
+        per_case.append({"bits": bits, "M": M, "N": N, "K": K, "us": round(us, 2),
+                         "GBps": round(algo_bytes(M, N, K, bits) / (us * 1e-6) / 1e9, 1)})
+
+    # roofline of the dominant kernel: 4-bit 17408x5120 M=1, rotating 4 weight copies
+    # (4 x 50 MB > L2) so every launch streams from HBM
+    peak, peak_kind = measured_peaks()
+    rot = build_case_weights(torch, O, dev, 4, 17408, 5120, 4242, copies=4)
+    xr = xs[(1, 5120)]
+    yr = ys[(1, 17408)]
+    nrep = 200
+    for i in range(8):
+        c, s, b = rot[i % 4]
+        lib.q38_quantized_matmul(ctx, xr.data_ptr(), 1, 5120, 0, c.data_ptr(), s.data_ptr(), b.data_ptr(), 0,
+                                 17408, 1, GROUP, 4, 0, yr.data_ptr())
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    r0.record(stream)
+    for i in range(nrep):
+        c, s, b = rot[i % 4]
+        lib.q38_quantized_matmul(ctx, xr.data_ptr(), 1, 5120, 0, c.data_ptr(), s.data_ptr(), b.data_ptr(), 0,
+                                 17408, 1, GROUP, 4, 0, yr.data_ptr())
+    r1.record(stream)
+    torch.cuda.synchronize()
+    launch_us = r0.elapsed_time(r1) / nrep * 1e3
+    rbytes = algo_bytes(1, 17408, 5120, 4)
+    achieved = rbytes / (launch_us * 1e-6) / 1e9
+    roofline = {"bound": "hbm", "kernel": "qgemv_main<4,1> (+ qgemv_prep) 17408x5120 4-bit M=1",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                "frac_of_8TBps": round(achieved / 8000.0, 4),
+                "algorithmic_bytes_per_launch": rbytes, "launch_us": round(launch_us, 2),
+                "traffic": None}
+    tr = os.path.join(ROOT, "profiles", "qgemv_traffic.json")
+    if os.path.exists(tr):
+        roofline["traffic"] = json.load(open(tr)).get("bytes_per_launch")
+    del rot
+
+    # e2e through the public API with host buffers: H2D of each product's x from pinned
+    # memory, the product, D2H of y -- all inside the timed region
+    hx = {k: v.cpu().pin_memory() for k, v in xs.items()}
+    hy = {k: torch.empty(v.shape, dtype=v.dtype).pin_memory() for k, v in ys.items()}
+    dx = {k: torch.empty_like(v) for k, v in xs.items()}
+    h2d = sum(2 * M * K for (M, N, K, b) in cases)
+    d2h = sum(2 * M * N for (M, N, K, b) in cases)
+
+    def e2e_step():
+        for (M, N, K, bits) in cases:
+            dx[(M, K)].copy_(hx[(M, K)], non_blocking=True)
+            y = q38.quantized_matmul(dx[(M, K)], *weights[(bits, N, K)], True, GROUP, bits)
+            hy[(M, N)].copy_(y, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    a1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = a0.elapsed_time(a1) / args.steps
+    if dist:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {"value": round(world * step_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)}
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(O, seconds=args.cpu_seconds)
+
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02^2) weights quantized by the oracle)",
+        "config": {"workload": "decode GEMV sweep: bits {2,3,4,8} x NxK {17408x5120, 5120x17408, 6144x5120} "
+                               "x M {1,8}, affine group 64, 24 products per step",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2: 550 MB of packed weights per step, M=1 pass before M=8 pass",
+                   "step_bytes": step_bytes},
+        "frac_of_8TBps": round(value / world / 8000.0, 4),
+        "roofline": roofline,
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "clocks": clocks,
+        "gpu_launches": 2 * len(cases) * args.steps,
+        "cases": per_case,
+    }
+    return line
+
+
+def cpu_baseline(O, seconds: float = 12.0, threads: int = 0):
+    """Oracle restatement of the same products on the host cores (bounded sample: the
+    6144x5120 shape at every bit width, M=1 and M=8, repeated until `seconds`)."""
+    if threads:
+        O.set_threads(threads)
+    cores = O.threads()
+    sample = []
+    for bits in BITS:
+        c, s, b = O.quantize(O.normal_f32(5000 + bits, (6144, 5120), 0.02), GROUP, bits)
+        for M in MS:
+            sample.append((M, bits, c, s, b, O.normal_bf16(5100 + M, (M, 5120))))
+    total_bytes, t0, n = 0, time.perf_counter(), 0
+    while True:
+        for (M, bits, c, s, b, x) in sample:
+            O.qmm(x, c, s, b, GROUP, bits)
+            total_bytes += algo_bytes(M, 6144, 5120, bits)
+            n += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(total_bytes / dt / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"{n} products of 6144x5120 (bits 2/3/4/8, M 1 and 8) in {dt:.1f} s"}
+
+
+def run_reference(args, rank, world):
+    """CPU reference arm: the oracle restatement on the host cores, rank 0 only."""
+    if rank != 0:
+        return None
+    import oracle as O
+    per_step = []
+    for _ in range(args.warmup):
+        cpu_baseline(O, seconds=0.5)
+    for _ in range(args.steps):
+        per_step.append(cpu_baseline(O, seconds=args.ref_seconds))
+    v = statistics.median(p["value"] for p in per_step)
+    base = per_step[0]
+    return {
+        "metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "decode GEMV sweep (bounded sample: 6144x5120 at bits 2/3/4/8, M 1 and 8)",
+                   "parallelism": "host CPU"},
+        "impl": "reference",
+        "cpu_baseline": {"value": v, "unit": "GB/s", "cores": base["cores"], "kind": "port",
+                         "sample": base["sample"]},
+        "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "MLX (the reference's implementation of this path) runs only on Apple silicon; "
+                "this arm times the C restatement of its CPU semantics",
+    }
+
+
+def run_profile_case(args):
+    """Small fixed workload for ncu captures: `--profile-bits` product of 17408x5120 at
+    M=`--profile-m`, 4 rotated weight copies (> L2), 12 launches."""
+    import torch
+    import oracle as O
+    import q38
+
+    dev = torch.device("cuda", 0)
+    bits, M, N, K = args.profile_bits, args.profile_m, 17408, 5120
+    rot = build_case_weights(torch, O, dev, bits, N, K, 4242, copies=4)
+    x = torch.from_numpy(O.normal_bf16(9, (M, K)).view(np.int16)).view(torch.bfloat16).to(dev)
+    ys = []
+    for i in range(12):
+        ys.append(q38.quantized_matmul(x, *rot[i % 4], True, GROUP, bits))
+    torch.cuda.synchronize()
+    q38.check_device()
+    print(json.dumps({"profile_case": {"bits": bits, "M": M, "N": N, "K": K, "launches": 12,
+                                       "algorithmic_bytes_per_launch": algo_bytes(M, N, K, bits)}}))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--profile-case", action="store_true")
+    ap.add_argument("--profile-bits", type=int, default=4)
+    ap.add_argument("--profile-m", type=int, default=1)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--ref-seconds", type=float, default=8.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus if args.gpus == 1 else 1)))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.profile_case:
+        run_profile_case(args)
+        return
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+    else:
+        line = run_ours(args, rank, world, local_rank)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,165 @@
+/*
+ * q38.h -- C ABI of the B200 (sm_100a) MLX-affine quantized matrix-product library.
+ *
+ * The library replaces the MLX operators that the Qwen3.8 MLX Swift models call for
+ * every quantized projection: quantizedMM / gatherQuantizedMM / dequantized /
+ * quantize / hadamardTransform, and the QuantizedLinear, QuantizedSwitchLinear and
+ * SwitchGLU modules built on them.  Argument meaning follows those operators; the
+ * packed layout is MLX's on-disk layout, so checkpoint tensors are passed unchanged:
+ *
+ *   weight  uint32 [.., N, K*bits/32]   code k of a row at bit k*bits of the row's
+ *                                       little-endian bitstream (LSB first)
+ *   scales  bf16   [.., N, K/group]     w = scale * q + bias, per group along K
+ *   biases  bf16   [.., N, K/group]     (nullable: treated as zero)
+ *
+ * Conventions
+ *   - Every pointer argument is a DEVICE pointer (cudaMalloc'd, or any memory the
+ *     device can address) unless stated otherwise; the caller owns all buffers.
+ *   - Every call is enqueued on the context's stream (q38_ctx_set_stream) and returns
+ *     without synchronising.  Calls never abort the process: they return a status and
+ *     q38_last_error(ctx) describes the most recent failure.
+ *   - A context belongs to one device and one host thread at a time; calls on one
+ *     context are not re-entrant.  The context owns a device workspace that grows on
+ *     demand (the growth itself synchronises the device); q38_ctx_reserve pre-sizes it
+ *     so that steady-state calls allocate nothing (and can be captured in a CUDA graph).
+ *   - Device kernels never spin without bound: a wait that exceeds about one second
+ *     records Q38_ERR_DEVICE_TIMEOUT in the context's device status word, which
+ *     q38_ctx_check_device reads.
+ */
+#ifndef Q38_H
+#define Q38_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(_WIN32)
+#define Q38_API __declspec(dllexport)
+#else
+#define Q38_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum q38_status {
+    Q38_OK = 0,
+    Q38_ERR_INVALID_ARGUMENT = 1, /* shape, pointer or parameter rejected */
+    Q38_ERR_UNSUPPORTED = 2,      /* valid MLX arguments this build does not implement */
+    Q38_ERR_CUDA = 3,             /* a CUDA runtime call failed */
+    Q38_ERR_OUT_OF_MEMORY = 4,    /* workspace growth failed */
+    Q38_ERR_DEVICE_TIMEOUT = 5,   /* a bounded device-side wait expired */
+    Q38_ERR_COMM = 6              /* a collective failed or timed out */
+} q38_status;
+
+typedef enum q38_dtype {
+    Q38_BF16 = 0,
+    Q38_F16 = 1,
+    Q38_F32 = 2
+} q38_dtype;
+
+/* MLX QuantizationMode; only .affine is implemented. */
+typedef enum q38_mode {
+    Q38_MODE_AFFINE = 0
+} q38_mode;
+
+typedef struct q38_ctx q38_ctx;
+
+/* ------------------------------------------------------------------ context */
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+Q38_API int q38_version(void);
+Q38_API const char* q38_status_string(q38_status status);
+
+/* Create a context on `device` (cudaSetDevice index).  The context starts on the
+ * legacy default stream. */
+Q38_API q38_status q38_ctx_create(int device, q38_ctx** out);
+Q38_API q38_status q38_ctx_destroy(q38_ctx* ctx);
+/* `stream` is a cudaStream_t (NULL = legacy default stream). */
+Q38_API q38_status q38_ctx_set_stream(q38_ctx* ctx, void* stream);
+Q38_API void* q38_ctx_get_stream(const q38_ctx* ctx);
+/* Grow the device workspace to at least `bytes` now (synchronises the device). */
+Q38_API q38_status q38_ctx_reserve(q38_ctx* ctx, size_t bytes);
+Q38_API size_t q38_ctx_workspace_bytes(const q38_ctx* ctx);
+/* Synchronise the stream and return Q38_ERR_DEVICE_TIMEOUT if any kernel recorded a
+ * bounded-wait expiry since the last check (the word is then cleared). */
+Q38_API q38_status q38_ctx_check_device(q38_ctx* ctx);
+/* Message of the last failed call on this context ("" if none). */
+Q38_API const char* q38_last_error(const q38_ctx* ctx);
+
+/* ------------------------------------------------------------- operators */
+
+/* quantizedMM -- replaces MLX.quantizedMM(x, w, scales:, biases:, transpose:,
+ * groupSize:, bits:, mode:) as called by QuantizedLinear.callAsFunction
+ * (Sources/Qwen38Core/FlashNext/Qwen4ExpPrequantized.swift:156-159; packed shapes built
+ * at :77-106).  transpose != 0: y[M,N] = x[M,K] . dequant(w)[N,K]^T with w uint32
+ * [N, K*bits/32] and scales/biases [N, K/group_size].  x and y share `x_dtype`
+ * (bf16 or f16); scales/biases use `scales_dtype`.  Accumulation is fp32.
+ * bits in {2,3,4,5,6,8}; group_size in {32,64,128}; transpose == 0 is rejected with
+ * Q38_ERR_UNSUPPORTED (no call site in the reference uses it). */
+Q38_API q38_status q38_quantized_matmul(q38_ctx* ctx, const void* x, int64_t M, int64_t K,
+                                q38_dtype x_dtype, const uint32_t* w, const void* scales,
+                                const void* biases, q38_dtype scales_dtype, int64_t N,
+                                int transpose, int group_size, int bits, q38_mode mode,
+                                void* y);
+
+/* gatherQuantizedMM -- replaces MLX.gatherQuantizedMM(x, w, scales:, biases:,
+ * lhsIndices:, rhsIndices:, transpose:, groupSize:, bits:, sortedIndices:) behind
+ * QuantizedSwitchLinear.callAsFunction (Vendor/mlx-swift-lm-local.patch:184-218):
+ * out[p] (M x N) = x[lhs[p]] (M x K) . dequant(w[rhs[p]])^T for p < P, with
+ * x [Bx, M, K], w [E, N, K*bits/32], scales/biases [E, N, K/group_size], out [P, M, N].
+ * lhs_indices may be NULL (lhs[p] = p, requires Bx >= P).  sorted_indices is MLX's hint
+ * that rhs is non-decreasing; results do not depend on it.  Indices are int32. */
+Q38_API q38_status q38_gather_quantized_matmul(q38_ctx* ctx, const void* x, int64_t Bx, int64_t M,
+                                       int64_t K, q38_dtype x_dtype, const uint32_t* w,
+                                       const void* scales, const void* biases,
+                                       q38_dtype scales_dtype, int64_t E, int64_t N,
+                                       const int32_t* lhs_indices, const int32_t* rhs_indices,
+                                       int64_t P, int transpose, int group_size, int bits,
+                                       q38_mode mode, int sorted_indices, void* out);
+
+/* dequantized -- replaces MLX.dequantized(w, scales:, biases:, groupSize:, bits:, mode:)
+ * (Sources/Qwen38Core/FlashNext/Qwen4ExpCheckpointLayerLoader.swift:299-305,
+ * Qwen4ExpPrequantized.swift:146-151): out[rows, K] = scale*q + bias, computed in fp32
+ * and stored as `out_dtype` (round to nearest even for bf16/f16). */
+Q38_API q38_status q38_dequantize(q38_ctx* ctx, const uint32_t* w, const void* scales,
+                          const void* biases, q38_dtype scales_dtype, int64_t rows, int64_t K,
+                          int group_size, int bits, q38_mode mode, void* out,
+                          q38_dtype out_dtype);
+
+/* quantize -- replaces mx.quantize(w, group_size:, bits:, mode: "affine")
+ * (Scripts/qwen4-exp-requantize-experts.py:246-251): w [rows, K] of `w_dtype` ->
+ * codes uint32 [rows, K*bits/32], scales/biases [rows, K/group_size] of `scales_dtype`.
+ * Per group the larger-magnitude extreme is represented exactly (MLX affine rule). */
+Q38_API q38_status q38_quantize(q38_ctx* ctx, const void* w, q38_dtype w_dtype, int64_t rows,
+                        int64_t K, int group_size, int bits, q38_mode mode, uint32_t* codes,
+                        void* scales, void* biases, q38_dtype scales_dtype);
+
+/* Unpacked integer codes q[rows, K] (one byte each) of a packed weight; the
+ * bit-exactness probe of the packed format. */
+Q38_API q38_status q38_unpack_codes(q38_ctx* ctx, const uint32_t* w, int64_t rows, int64_t K, int bits,
+                            uint8_t* q);
+
+/* hadamardRotate -- replaces the rotation of Qwen38HadamardQuantizedLinear /
+ * Qwen38HadamardQuantizedEmbedding (Sources/Qwen38Core/Bonsai2/
+ * Qwen38HadamardModules.swift:10-19): fp32(x) * signs (forward) or signs applied after
+ * the transform (inverse), normalised Walsh-Hadamard transform (Sylvester order) over
+ * blocks of `block` along the last axis, scaled by 1/sqrt(block), cast back to x_dtype.
+ * x, y [rows, D]; signs fp32 [D] or NULL (all +1); block a power of two <= 8192. */
+Q38_API q38_status q38_hadamard_rotate(q38_ctx* ctx, const void* x, int64_t rows, int64_t D,
+                               q38_dtype x_dtype, const float* signs, int block, int inverse,
+                               void* y);
+
+/* Qwen38HadamardQuantizedLinear.callAsFunction (Bonsai2/Qwen38HadamardModules.swift:37-39):
+ * y = quantizedMM(hadamardRotate(x, signs, block), w, ...).  The rotated activations
+ * are rounded to x_dtype before the product, as in the reference. */
+Q38_API q38_status q38_hadamard_quantized_matmul(q38_ctx* ctx, const void* x, int64_t M, int64_t K,
+                                         q38_dtype x_dtype, const float* signs, int block,
+                                         const uint32_t* w, const void* scales,
+                                         const void* biases, q38_dtype scales_dtype, int64_t N,
+                                         int group_size, int bits, void* y);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* Q38_H */

@@ -1,0 +1,364 @@
+// C ABI entry points of libq38: context management, argument validation (the checks
+// MLX's operators perform, reported as status codes instead of process aborts) and
+// dispatch to the kernels.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "q38_internal.h"
+
+namespace q38 {
+
+q38_status fail(q38_ctx* ctx, q38_status st, const char* fmt, ...) {
+    if (ctx) {
+        char buf[512];
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(buf, sizeof(buf), fmt, ap);
+        va_end(ap);
+        ctx->last_error = buf;
+    }
+    return st;
+}
+
+q38_status check_launch(q38_ctx* ctx, const char* what) {
+    const cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) return Q38_OK;
+    return fail(ctx, Q38_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+q38_status ensure_workspace(q38_ctx* ctx, size_t bytes) {
+    if (bytes <= ctx->workspace_bytes) return Q38_OK;
+    size_t want = align_up(bytes + bytes / 4, 1 << 20);
+    if (ctx->workspace) {
+        cudaStreamSynchronize(ctx->stream);
+        cudaFree(ctx->workspace);
+        ctx->workspace = nullptr;
+        ctx->workspace_bytes = 0;
+    }
+    if (cudaMalloc(&ctx->workspace, want) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(ctx, Q38_ERR_OUT_OF_MEMORY, "workspace of %zu bytes could not be allocated", want);
+    }
+    ctx->workspace_bytes = want;
+    return Q38_OK;
+}
+
+q38_status ensure_aux(q38_ctx* ctx, size_t bytes, void** out) {
+    if (bytes > ctx->aux_bytes) {
+        const size_t want = align_up(bytes + bytes / 4, 1 << 20);
+        if (ctx->aux) {
+            cudaStreamSynchronize(ctx->stream);
+            cudaFree(ctx->aux);
+            ctx->aux = nullptr;
+            ctx->aux_bytes = 0;
+        }
+        if (cudaMalloc(&ctx->aux, want) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(ctx, Q38_ERR_OUT_OF_MEMORY, "activation buffer of %zu bytes could not be allocated", want);
+        }
+        ctx->aux_bytes = want;
+    }
+    *out = ctx->aux;
+    return Q38_OK;
+}
+
+q38_status ensure_zero_region(q38_ctx* ctx, size_t counters, size_t accs, uint32_t** cnt,
+                              float** acc) {
+    if (counters > ctx->zcnt_cap || accs > ctx->zacc_cap || !ctx->zws) {
+        size_t nc = counters > ctx->zcnt_cap ? align_up(counters + counters / 4, 1024) : ctx->zcnt_cap;
+        size_t na = accs > ctx->zacc_cap ? align_up(accs + accs / 4, 1 << 16) : ctx->zacc_cap;
+        if (nc == 0) nc = 1024;
+        if (na == 0) na = 1 << 16;
+        if (ctx->zws) {
+            cudaStreamSynchronize(ctx->stream);
+            cudaFree(ctx->zws);
+            ctx->zws = nullptr;
+        }
+        const size_t bytes = align_up(nc * 4, 256) + na * 4;
+        if (cudaMalloc(&ctx->zws, bytes) != cudaSuccess) {
+            cudaGetLastError();
+            ctx->zcnt_cap = ctx->zacc_cap = 0;
+            return fail(ctx, Q38_ERR_OUT_OF_MEMORY, "accumulator region of %zu bytes could not be allocated", bytes);
+        }
+        if (cudaMemset(ctx->zws, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+            return fail(ctx, Q38_ERR_CUDA, "accumulator region could not be cleared");
+        }
+        ctx->zcnt_cap = nc;
+        ctx->zacc_cap = na;
+    }
+    *cnt = static_cast<uint32_t*>(ctx->zws);
+    *acc = reinterpret_cast<float*>(static_cast<uint8_t*>(ctx->zws) + align_up(ctx->zcnt_cap * 4, 256));
+    return Q38_OK;
+}
+
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, size_t elem_bytes, const void* base,
+                 uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows,
+                 CUtensorMapSwizzle swz) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * elem_bytes};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace q38
+
+using namespace q38;
+
+namespace {
+
+bool valid_bits(int bits) {
+    return bits == 2 || bits == 3 || bits == 4 || bits == 5 || bits == 6 || bits == 8;
+}
+
+bool valid_dtype(q38_dtype d) { return d == Q38_BF16 || d == Q38_F16 || d == Q38_F32; }
+
+// The packing precondition of the reference (FlashNext/Qwen4ExpPrequantized.swift:60-72):
+// K*bits % 32 == 0 and K % group == 0.
+q38_status check_format(q38_ctx* ctx, const char* op, int64_t K, int group, int bits, q38_mode mode) {
+    if (mode != Q38_MODE_AFFINE) return fail(ctx, Q38_ERR_UNSUPPORTED, "%s: only affine mode is implemented", op);
+    if (!valid_bits(bits)) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "%s: bits must be one of 2,3,4,5,6,8 (got %d)", op, bits);
+    if (group != 32 && group != 64 && group != 128)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "%s: group_size must be 32, 64 or 128 (got %d)", op, group);
+    if (K <= 0 || K % group) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "%s: K=%lld is not a multiple of group_size %d", op, (long long)K, group);
+    if ((K * bits) % 32) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "%s: K*bits=%lld is not a multiple of 32", op, (long long)(K * bits));
+    return Q38_OK;
+}
+
+q38_status set_device(q38_ctx* ctx) {
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return check_launch(ctx, "cudaSetDevice");
+    return Q38_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int q38_version(void) { return 100; }
+
+const char* q38_status_string(q38_status s) {
+    switch (s) {
+        case Q38_OK: return "ok";
+        case Q38_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case Q38_ERR_UNSUPPORTED: return "unsupported";
+        case Q38_ERR_CUDA: return "cuda error";
+        case Q38_ERR_OUT_OF_MEMORY: return "out of memory";
+        case Q38_ERR_DEVICE_TIMEOUT: return "device wait timed out";
+        case Q38_ERR_COMM: return "communication error";
+    }
+    return "unknown status";
+}
+
+q38_status q38_ctx_create(int device, q38_ctx** out) {
+    if (!out) return Q38_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+        cudaGetLastError();
+        return Q38_ERR_INVALID_ARGUMENT;
+    }
+    q38_ctx* c = new q38_ctx();
+    c->device = device;
+    if (cudaSetDevice(device) != cudaSuccess ||
+        cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+        cudaMalloc(&c->d_status, sizeof(uint32_t)) != cudaSuccess ||
+        cudaMemset(c->d_status, 0, sizeof(uint32_t)) != cudaSuccess) {
+        cudaGetLastError();
+        delete c;
+        return Q38_ERR_CUDA;
+    }
+    *out = c;
+    return Q38_OK;
+}
+
+q38_status q38_ctx_destroy(q38_ctx* ctx) {
+    if (!ctx) return Q38_OK;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    if (ctx->workspace) cudaFree(ctx->workspace);
+    if (ctx->zws) cudaFree(ctx->zws);
+    if (ctx->aux) cudaFree(ctx->aux);
+    if (ctx->d_status) cudaFree(ctx->d_status);
+    delete ctx;
+    return Q38_OK;
+}
+
+q38_status q38_ctx_set_stream(q38_ctx* ctx, void* stream) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    ctx->stream = static_cast<cudaStream_t>(stream);
+    return Q38_OK;
+}
+
+void* q38_ctx_get_stream(const q38_ctx* ctx) { return ctx ? ctx->stream : nullptr; }
+
+q38_status q38_ctx_reserve(q38_ctx* ctx, size_t bytes) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    q38_status st = set_device(ctx);
+    if (st != Q38_OK) return st;
+    return ensure_workspace(ctx, bytes);
+}
+
+size_t q38_ctx_workspace_bytes(const q38_ctx* ctx) { return ctx ? ctx->workspace_bytes : 0; }
+
+q38_status q38_ctx_check_device(q38_ctx* ctx) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    q38_status st = set_device(ctx);
+    if (st != Q38_OK) return st;
+    uint32_t v = 0;
+    if (cudaStreamSynchronize(ctx->stream) != cudaSuccess ||
+        cudaMemcpy(&v, ctx->d_status, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess)
+        return check_launch(ctx, "check_device");
+    if (v) {
+        cudaMemset(ctx->d_status, 0, sizeof(uint32_t));
+        if (v & Q38_DEV_TIMEOUT)
+            return fail(ctx, Q38_ERR_DEVICE_TIMEOUT, "a device-side wait exceeded its limit (status 0x%x)", v);
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "an index argument was out of range (status 0x%x)", v);
+    }
+    return Q38_OK;
+}
+
+const char* q38_last_error(const q38_ctx* ctx) { return ctx ? ctx->last_error.c_str() : ""; }
+
+q38_status q38_quantized_matmul(q38_ctx* ctx, const void* x, int64_t M, int64_t K, q38_dtype x_dtype,
+                                const uint32_t* w, const void* scales, const void* biases,
+                                q38_dtype scales_dtype, int64_t N, int transpose, int group_size,
+                                int bits, q38_mode mode, void* y) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    q38_status st = check_format(ctx, "quantized_matmul", K, group_size, bits, mode);
+    if (st != Q38_OK) return st;
+    if (!transpose) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: transpose=false is not implemented");
+    if (x_dtype != Q38_BF16 && x_dtype != Q38_F16)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "quantized_matmul: x must be bf16 or f16");
+    if (!valid_dtype(scales_dtype)) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "quantized_matmul: bad scales dtype");
+    if (M < 0 || N <= 0) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "quantized_matmul: bad shape M=%lld N=%lld", (long long)M, (long long)N);
+    if (M == 0) return Q38_OK;
+    if (!x || !w || !scales || !y) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "quantized_matmul: null pointer");
+    if ((st = set_device(ctx)) != Q38_OK) return st;
+    if (qgemv_fast_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w, scales, biases, y))
+        return qgemv_fast(ctx, x, M, K, w, scales, biases, N, bits, y);
+    return qmm_generic(ctx, x, M, K, x_dtype, w, scales, biases, scales_dtype, N, group_size, bits, y);
+}
+
+
+
+q38_status q38_dequantize(q38_ctx* ctx, const uint32_t* w, const void* scales, const void* biases,
+                          q38_dtype scales_dtype, int64_t rows, int64_t K, int group_size, int bits,
+                          q38_mode mode, void* out, q38_dtype out_dtype) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    q38_status st = check_format(ctx, "dequantize", K, group_size, bits, mode);
+    if (st != Q38_OK) return st;
+    if (!valid_dtype(scales_dtype) || !valid_dtype(out_dtype))
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "dequantize: bad dtype");
+    if (rows < 0) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "dequantize: rows < 0");
+    if (rows == 0) return Q38_OK;
+    if (!w || !scales || !out) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "dequantize: null pointer");
+    if ((st = set_device(ctx)) != Q38_OK) return st;
+    return dequantize_launch(ctx, w, scales, biases, scales_dtype, rows, K, group_size, bits, out, out_dtype);
+}
+
+q38_status q38_quantize(q38_ctx* ctx, const void* w, q38_dtype w_dtype, int64_t rows, int64_t K,
+                        int group_size, int bits, q38_mode mode, uint32_t* codes, void* scales,
+                        void* biases, q38_dtype scales_dtype) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    q38_status st = check_format(ctx, "quantize", K, group_size, bits, mode);
+    if (st != Q38_OK) return st;
+    if (!valid_dtype(w_dtype) || !valid_dtype(scales_dtype))
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "quantize: bad dtype");
+    if (rows < 0) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "quantize: rows < 0");
+    if (rows == 0) return Q38_OK;
+    if (!w || !codes || !scales || !biases) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "quantize: null pointer");
+    if ((st = set_device(ctx)) != Q38_OK) return st;
+    return quantize_launch(ctx, w, w_dtype, rows, K, group_size, bits, codes, scales, biases, scales_dtype);
+}
+
+q38_status q38_unpack_codes(q38_ctx* ctx, const uint32_t* w, int64_t rows, int64_t K, int bits, uint8_t* q) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    if (!valid_bits(bits) || K <= 0 || (K * bits) % 32 || rows < 0)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "unpack_codes: bad shape or bits");
+    if (rows == 0) return Q38_OK;
+    if (!w || !q) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "unpack_codes: null pointer");
+    q38_status st = set_device(ctx);
+    if (st != Q38_OK) return st;
+    return unpack_launch(ctx, w, rows, K, bits, q);
+}
+
+q38_status q38_hadamard_rotate(q38_ctx* ctx, const void* x, int64_t rows, int64_t D, q38_dtype x_dtype,
+                               const float* signs, int block, int inverse, void* y) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    if (block < 2 || block > 8192 || (block & (block - 1)))
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "hadamard_rotate: block must be a power of two in [2, 8192]");
+    if (D <= 0 || D % block) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "hadamard_rotate: Hadamard block does not divide activation width");
+    if (x_dtype != Q38_BF16 && x_dtype != Q38_F16) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "hadamard_rotate: x must be bf16 or f16");
+    if (rows < 0) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "hadamard_rotate: rows < 0");
+    if (rows == 0) return Q38_OK;
+    if (!x || !y) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "hadamard_rotate: null pointer");
+    q38_status st = set_device(ctx);
+    if (st != Q38_OK) return st;
+    return hadamard_launch(ctx, x, rows, D, x_dtype, signs, block, inverse, y);
+}
+
+q38_status q38_hadamard_quantized_matmul(q38_ctx* ctx, const void* x, int64_t M, int64_t K, q38_dtype x_dtype,
+                                         const float* signs, int block, const uint32_t* w, const void* scales,
+                                         const void* biases, q38_dtype scales_dtype, int64_t N, int group_size,
+                                         int bits, void* y) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    if (M < 0 || K <= 0) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "hadamard_quantized_matmul: bad shape");
+    if (M == 0) return Q38_OK;
+    if (!x || !w || !scales || !y) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "hadamard_quantized_matmul: null pointer");
+    q38_status st = set_device(ctx);
+    if (st != Q38_OK) return st;
+    // The rotated activations (rounded to x_dtype, as the reference does before the
+    // product) live in the context's activation buffer.
+    void* xr = nullptr;
+    if ((st = ensure_aux(ctx, static_cast<size_t>(M) * K * 2, &xr)) != Q38_OK) return st;
+    st = q38_hadamard_rotate(ctx, x, M, K, x_dtype, signs, block, 0, xr);
+    if (st != Q38_OK) return st;
+    return q38_quantized_matmul(ctx, xr, M, K, x_dtype, w, scales, biases, scales_dtype, N, 1, group_size, bits,
+                                Q38_MODE_AFFINE, y);
+}
+
+q38_status q38_gather_quantized_matmul(q38_ctx* ctx, const void* x, int64_t Bx, int64_t M, int64_t K,
+                                       q38_dtype x_dtype, const uint32_t* w, const void* scales,
+                                       const void* biases, q38_dtype scales_dtype, int64_t E, int64_t N,
+                                       const int32_t* lhs_indices, const int32_t* rhs_indices, int64_t P,
+                                       int transpose, int group_size, int bits, q38_mode mode,
+                                       int sorted_indices, void* out) {
+    (void)sorted_indices;
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    q38_status st = check_format(ctx, "gather_quantized_matmul", K, group_size, bits, mode);
+    if (st != Q38_OK) return st;
+    if (!transpose) return fail(ctx, Q38_ERR_UNSUPPORTED, "gather_quantized_matmul: transpose=false is not implemented");
+    if (x_dtype != Q38_BF16 && x_dtype != Q38_F16)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "gather_quantized_matmul: x must be bf16 or f16");
+    if (!valid_dtype(scales_dtype)) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "gather_quantized_matmul: bad scales dtype");
+    if (Bx <= 0 || M < 0 || E <= 0 || N <= 0 || P < 0)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "gather_quantized_matmul: bad shape");
+    if (!lhs_indices && Bx < P)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "gather_quantized_matmul: lhs_indices NULL requires Bx >= P");
+    if (P == 0 || M == 0) return Q38_OK;
+    if (!x || !w || !scales || !rhs_indices || !out)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "gather_quantized_matmul: null pointer");
+    if ((st = set_device(ctx)) != Q38_OK) return st;
+    return gather_generic(ctx, x, Bx, M, K, x_dtype, w, scales, biases, scales_dtype, E, N, lhs_indices,
+                          rhs_indices, P, group_size, bits, out);
+}
+
+}  // extern "C"

@@ -1,0 +1,143 @@
+// Block-diagonal normalised Walsh-Hadamard rotation of activations (Bonsai 2 packs).
+//
+// Replaces hadamardRotate (Sources/Qwen38Core/Bonsai2/Qwen38HadamardModules.swift:10-19):
+// fp32 copy of x, signs multiplied before the transform (forward) or after it (inverse),
+// Sylvester-order transform over blocks of `block` along the last axis, scaled by
+// 1/sqrt(block), cast back to the input dtype.  Butterfly stage h combines elements j and
+// j+h as (a+b, a-b) for h = 1, 2, 4, ...; each butterfly is one IEEE add/subtract of the
+// same two operands as the CPU restatement, so results agree bit for bit.
+#include "ptx.cuh"
+
+namespace q38 {
+namespace {
+
+template <typename T>
+__device__ __forceinline__ float ld_f32(const T* p);
+template <>
+__device__ __forceinline__ float ld_f32<__nv_bfloat16>(const __nv_bfloat16* p) {
+    return __bfloat162float(*p);
+}
+template <>
+__device__ __forceinline__ float ld_f32<__half>(const __half* p) {
+    return __half2float(*p);
+}
+template <typename T>
+__device__ __forceinline__ void st_f32(T* p, float v);
+template <>
+__device__ __forceinline__ void st_f32<__nv_bfloat16>(__nv_bfloat16* p, float v) {
+    *p = __float2bfloat16_rn(v);
+}
+template <>
+__device__ __forceinline__ void st_f32<__half>(__half* p, float v) {
+    *p = __float2half_rn(v);
+}
+
+// One warp per (row, block); lane holds E = block/32 consecutive elements.
+template <typename T, int E>
+__global__ void __launch_bounds__(256) fwht_warp_kernel(const T* __restrict__ x, int64_t nblocks,
+                                                        int64_t D, const float* __restrict__ signs,
+                                                        int inverse, float scale,
+                                                        T* __restrict__ y) {
+    constexpr int BLOCK = 32 * E;
+    const int lane = threadIdx.x & 31;
+    const int64_t bid = blockIdx.x * 8LL + (threadIdx.x >> 5);
+    if (bid >= nblocks) return;
+    const int64_t per_row = D / BLOCK;
+    const int64_t row = bid / per_row, col0 = (bid % per_row) * BLOCK + lane * E;
+    const T* src = x + row * D + col0;
+    float v[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+        float f = ld_f32(src + i);
+        if (!inverse && signs) f = f * signs[col0 + i];
+        v[i] = f;
+    }
+#pragma unroll
+    for (int h = 1; h < E; h <<= 1)
+#pragma unroll
+        for (int i = 0; i < E; ++i)
+            if ((i & h) == 0) {
+                const float a = v[i], b = v[i + h];
+                v[i] = a + b;
+                v[i + h] = a - b;
+            }
+#pragma unroll
+    for (int lh = 1; lh < 32; lh <<= 1) {
+        const bool upper = (lane & lh) != 0;
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+            const float p = __shfl_xor_sync(0xffffffffu, v[i], lh);
+            v[i] = upper ? (p - v[i]) : (v[i] + p);
+        }
+    }
+    T* dst = y + row * D + col0;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+        float f = v[i] * scale;
+        if (inverse && signs) f = f * signs[col0 + i];
+        st_f32(dst + i, f);
+    }
+}
+
+// One CTA per (row, block) through shared memory, any power-of-two block <= 8192.
+template <typename T>
+__global__ void __launch_bounds__(512) fwht_smem_kernel(const T* __restrict__ x, int64_t D,
+                                                        int block, const float* __restrict__ signs,
+                                                        int inverse, float scale,
+                                                        T* __restrict__ y) {
+    extern __shared__ float sv[];
+    const int64_t per_row = D / block;
+    const int64_t row = blockIdx.x / per_row, col0 = (blockIdx.x % per_row) * block;
+    for (int i = threadIdx.x; i < block; i += blockDim.x) {
+        float f = ld_f32(x + row * D + col0 + i);
+        if (!inverse && signs) f = f * signs[col0 + i];
+        sv[i] = f;
+    }
+    __syncthreads();
+    for (int h = 1; h < block; h <<= 1) {
+        for (int p = threadIdx.x; p < block / 2; p += blockDim.x) {
+            const int j = (p / h) * 2 * h + (p % h);
+            const float a = sv[j], b = sv[j + h];
+            sv[j] = a + b;
+            sv[j + h] = a - b;
+        }
+        __syncthreads();
+    }
+    for (int i = threadIdx.x; i < block; i += blockDim.x) {
+        float f = sv[i] * scale;
+        if (inverse && signs) f = f * signs[col0 + i];
+        st_f32(y + row * D + col0 + i, f);
+    }
+}
+
+template <typename T>
+q38_status launch(q38_ctx* ctx, const void* x, int64_t rows, int64_t D, const float* signs,
+                  int block, int inverse, void* y) {
+    const float scale = 1.0f / sqrtf(static_cast<float>(block));
+    const int64_t nblocks = rows * (D / block);
+    const T* xs = static_cast<const T*>(x);
+    T* ys = static_cast<T*>(y);
+    const unsigned grid = static_cast<unsigned>((nblocks + 7) / 8);
+    switch (block) {
+        case 256: fwht_warp_kernel<T, 8><<<grid, 256, 0, ctx->stream>>>(xs, nblocks, D, signs, inverse, scale, ys); break;
+        case 512: fwht_warp_kernel<T, 16><<<grid, 256, 0, ctx->stream>>>(xs, nblocks, D, signs, inverse, scale, ys); break;
+        case 1024: fwht_warp_kernel<T, 32><<<grid, 256, 0, ctx->stream>>>(xs, nblocks, D, signs, inverse, scale, ys); break;
+        default: {
+            if (nblocks > 0x7fffffffLL) return fail(ctx, Q38_ERR_UNSUPPORTED, "hadamard_rotate: too many blocks");
+            const int threads = block / 2 < 512 ? (block / 2 < 32 ? 32 : block / 2) : 512;
+            fwht_smem_kernel<T><<<static_cast<unsigned>(nblocks), threads, block * sizeof(float), ctx->stream>>>(
+                xs, D, block, signs, inverse, scale, ys);
+        }
+    }
+    return check_launch(ctx, "hadamard_rotate");
+}
+
+}  // namespace
+
+q38_status hadamard_launch(q38_ctx* ctx, const void* x, int64_t rows, int64_t D, q38_dtype xd,
+                           const float* signs, int block, int inverse, void* y) {
+    if (xd == Q38_BF16) return launch<__nv_bfloat16>(ctx, x, rows, D, signs, block, inverse, y);
+    return launch<__half>(ctx, x, rows, D, signs, block, inverse, y);
+}
+
+}  // namespace q38

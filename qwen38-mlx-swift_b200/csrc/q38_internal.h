@@ -1,0 +1,98 @@
+// Internal declarations shared by the translation units of libq38.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "../../include/q38.h"
+
+// Device-side status bits (ctx->d_status).
+#define Q38_DEV_TIMEOUT 1u
+#define Q38_DEV_BAD_INDEX 2u
+
+struct q38_ctx {
+    int device = 0;
+    int num_sms = 0;
+    cudaStream_t stream = nullptr;
+    void* workspace = nullptr;  // scratch; grows on demand, no content invariant
+    size_t workspace_bytes = 0;
+    // Zero-at-rest accumulators: every kernel that uses them returns them to zero.
+    // Layout: [counters: zcnt_cap uint32][pad to 256][fp32 partial sums: zacc_cap floats]
+    void* zws = nullptr;
+    size_t zcnt_cap = 0, zacc_cap = 0;
+    void* aux = nullptr;  // activation-sized intermediates (rotated x, MoE buffers)
+    size_t aux_bytes = 0;
+    uint32_t* d_status = nullptr;  // device status word (timeouts)
+    std::string last_error;
+};
+
+namespace q38 {
+
+// Records the message on the context and returns the status.
+q38_status fail(q38_ctx* ctx, q38_status st, const char* fmt, ...);
+
+// Checks the most recent launch; converts a CUDA error into Q38_ERR_CUDA.
+q38_status check_launch(q38_ctx* ctx, const char* what);
+
+// Makes sure the scratch workspace holds at least `bytes`.
+q38_status ensure_workspace(q38_ctx* ctx, size_t bytes);
+// Makes sure the activation buffer holds `bytes`; returns its address.
+q38_status ensure_aux(q38_ctx* ctx, size_t bytes, void** out);
+// Makes sure the zero-at-rest region holds `counters` uint32 and `accs` floats; returns
+// their device addresses.  Growth reallocates and zero-fills (synchronising the device).
+q38_status ensure_zero_region(q38_ctx* ctx, size_t counters, size_t accs, uint32_t** cnt,
+                              float** acc);
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Driver entry point for cuTensorMapEncodeTiled (resolved once, no libcuda link).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled();
+
+// 2-D tiled tensor map over a row-major [rows, cols] array.
+bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, size_t elem_bytes, const void* base,
+                 uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows,
+                 CUtensorMapSwizzle swz);
+
+// ---- kernel launchers (each returns Q38_OK or an error recorded on ctx) ----
+
+// Decode-shaped product (M <= 16, group 64, K % 512 == 0, bits 2/3/4/8, bf16).
+bool qgemv_fast_supported(int64_t M, int64_t K, int group, int bits, q38_dtype xd,
+                          q38_dtype sd, const void* x, const void* w, const void* s,
+                          const void* b, const void* y);
+q38_status qgemv_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w,
+                      const void* s, const void* b, int64_t N, int bits, void* y);
+
+// General product, any supported shape (CUDA cores; correctness path for odd shapes).
+q38_status qmm_generic(q38_ctx* ctx, const void* x, int64_t M, int64_t K, q38_dtype xd,
+                       const uint32_t* w, const void* s, const void* b, q38_dtype sd,
+                       int64_t N, int group, int bits, void* y);
+
+// Gathered product of the general path (any supported shape).
+q38_status gather_generic(q38_ctx* ctx, const void* x, int64_t Bx, int64_t M, int64_t K, q38_dtype xd,
+                          const uint32_t* w, const void* s, const void* b, q38_dtype sd, int64_t E,
+                          int64_t N, const int32_t* lhs, const int32_t* rhs, int64_t P, int group,
+                          int bits, void* out);
+
+q38_status dequantize_launch(q38_ctx* ctx, const uint32_t* w, const void* s, const void* b,
+                             q38_dtype sd, int64_t rows, int64_t K, int group, int bits,
+                             void* out, q38_dtype od);
+q38_status quantize_launch(q38_ctx* ctx, const void* w, q38_dtype wd, int64_t rows, int64_t K,
+                           int group, int bits, uint32_t* codes, void* s, void* b,
+                           q38_dtype sd);
+q38_status unpack_launch(q38_ctx* ctx, const uint32_t* w, int64_t rows, int64_t K, int bits,
+                         uint8_t* q);
+q38_status hadamard_launch(q38_ctx* ctx, const void* x, int64_t rows, int64_t D, q38_dtype xd,
+                           const float* signs, int block, int inverse, void* y);
+
+}  // namespace q38

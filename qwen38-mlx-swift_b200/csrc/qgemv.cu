@@ -1,0 +1,587 @@
+// Decode-shaped MLX-affine quantized product: y[M,N] = x[M,K] . dequant(W)[N,K]^T for
+// M <= 16, group 64, K % 512 == 0, bits 2/3/4/8, bf16 activations and scales.
+//
+// Replaces the Metal `qmv` kernel behind MLX.quantizedMM (QuantizedLinear.callAsFunction,
+// Sources/Qwen38Core/FlashNext/Qwen4ExpPrequantized.swift:156-159).
+//
+// Design (HBM-bound: the packed codes are the stream):
+//  * Work unit = 16 weight rows x 512 k ("subunit").  A CTA owns a contiguous range of
+//    subunits in (64-row tile, k-chunk, 16-row subtile) order, so every CTA streams the
+//    same number of bytes (+-1 subunit) whatever N and K are.
+//  * One producer warp streams each (tile, chunk) stage with TMA: the codes of the
+//    active 16-row subtiles (swizzled boxes), the 64x8 bf16 scales and biases, and the
+//    chunk's pre-arranged activation fragments.  Four consumer warps each own one
+//    16-row subtile.  Stages cycle through an mbarrier ring.
+//  * Codes are turned into bf16 operands without integer->float conversion: a code
+//    masked into the mantissa of 0x4300 (bf16 128.0) reads as 128 + 2^p*q.  A tiny
+//    prologue kernel permutes and scales the activations (x * 2^-p) into the MMA
+//    fragment order that matches the extraction, and precomputes per-group sums.
+//    One m16n8k16 bf16 MMA then dots 16 codes x 8 tokens; per group
+//    D = sum(q*x) + 128*sum(x'), and y += scale*D.  The -128*scale*sum(x') and
+//    bias*sum(x) terms of all 8 groups of a chunk are folded into two extra MMA
+//    steps whose operands are the scales/biases and hi/lo bf16 splits of the sums.
+//  * Subtiles split across CTAs accumulate through fp32 atomics into a workspace; the
+//    warp that completes a subtile (per-subtile chunk counter) writes y and returns the
+//    workspace and counter to zero, so no per-call clearing is needed.
+//  * The main kernel is launched with programmatic dependent launch: its producer
+//    streams the first stages of weights while the prologue kernel is still running.
+#include "ptx.cuh"
+
+namespace q38 {
+namespace {
+
+using namespace dev;
+
+constexpr int KC = 512;        // k per chunk
+constexpr int GROUPS = 8;      // groups of 64 per chunk
+constexpr int NCW = 4;         // consumer warps (one 16-row subtile each)
+constexpr int THREADS = (NCW + 1) * 32;
+constexpr uint32_t MAGIC = 0x43004300u;  // bf16 128.0 in both halves
+
+template <int BITS>
+struct Fmt {
+    static constexpr int SPG = BITS == 8 ? 8 : 4;     // k16 MMA steps per group
+    static constexpr int NP = 2 * SPG;                 // bf16x2 pairs per thread-row-group
+    static constexpr int SW = BITS == 3 ? 64 : 128;    // swizzle span of a code box (bytes)
+    static constexpr int ROW_BYTES = KC * BITS / 8;    // code bytes per row per chunk
+    static constexpr int ROW_WORDS = ROW_BYTES / 4;
+    static constexpr int BOXES = ROW_BYTES / SW;       // code boxes per subtile
+    static constexpr int SUB_BYTES = 16 * ROW_BYTES;   // code bytes per subtile
+    static constexpr int XF_PER_M = 256 * SPG + 64;    // fragment bytes per token per chunk
+    static constexpr uint32_t MASK = BITS == 2 ? 0u : BITS == 3 ? 0x00070070u : 0x000F000Fu;
+};
+
+// ---------------------------------------------------------------------------------
+// Pair tables: for bf16x2 operand q of a thread's 16 codes (per row and group), the
+// code index feeding its low and high half and the power-of-two weight the code has
+// inside that half (the activation is pre-multiplied by the inverse).
+// ---------------------------------------------------------------------------------
+template <int BITS>
+__host__ __device__ constexpr int pair_code(int q, int hi) {
+    if (BITS == 2) return q + (hi ? 8 : 0);
+    if (BITS == 3) return q < 4 ? q + (hi ? 4 : 0) : q + 4 + (hi ? 4 : 0);
+    if (BITS == 4) return (q / 4) * 8 + (q % 4) + (hi ? 4 : 0);
+    /* 8 */ return (q / 4) * 4 + ((q % 4) >> 1) + (hi ? 2 : 0);
+}
+
+// Multiplier applied to the activation for the slot (1 / weight of the code's bits).
+template <int BITS>
+__host__ __device__ constexpr float pair_mult(int q, int hi) {
+    if (BITS == 2) {
+        const int pos = (q % 3 == 0) ? 0 : (q % 3 == 1) ? 2 : 4;  // q: 0,1,2,3,4,5,6,7
+        return pos == 0 ? 1.0f : pos == 2 ? 0.25f : 0.0625f;
+    }
+    if (BITS == 3) return hi ? 1.0f : 0.0625f;
+    if (BITS == 4) return 1.0f;
+    /* 8: odd q = high nibble, weight 16 */ return (q & 1) ? 16.0f : 1.0f;
+}
+
+// Extract the NP bf16x2 operands of one thread-row-group from its code window.
+// w[] holds the window: bits 2 -> 1 word, 3 -> 2 words (48 valid bits), 4 -> 2, 8 -> 4.
+template <int BITS>
+__device__ __forceinline__ void extract(const uint32_t* w, uint32_t* a) {
+    if constexpr (BITS == 2) {
+        const uint32_t v = w[0], v6 = v >> 6, v12 = v >> 12;
+        a[0] = (v & 0x00030003u) | MAGIC;
+        a[1] = (v & 0x000C000Cu) | MAGIC;
+        a[2] = (v & 0x00300030u) | MAGIC;
+        a[3] = (v6 & 0x00030003u) | MAGIC;
+        a[4] = (v6 & 0x000C000Cu) | MAGIC;
+        a[5] = (v6 & 0x00300030u) | MAGIC;
+        a[6] = (v12 & 0x00030003u) | MAGIC;
+        a[7] = (v12 & 0x000C000Cu) | MAGIC;
+    } else if constexpr (BITS == 3) {
+        const uint32_t A = w[0], B = w[1];
+        constexpr uint32_t m = 0x00070070u;
+        a[0] = ((A << 4) & m) | MAGIC;
+        a[1] = ((A << 1) & m) | MAGIC;
+        a[2] = ((A >> 2) & m) | MAGIC;
+        a[3] = ((A >> 5) & m) | MAGIC;
+        a[4] = (__funnelshift_r(A, B, 20) & m) | MAGIC;
+        a[5] = (__funnelshift_r(A, B, 23) & m) | MAGIC;
+        a[6] = (__funnelshift_r(A, B, 26) & m) | MAGIC;
+        a[7] = (__funnelshift_r(A, B, 29) & m) | MAGIC;
+    } else {
+        constexpr int NW = BITS == 4 ? 2 : 4;
+#pragma unroll
+        for (int i = 0; i < NW; ++i) {
+            const uint32_t v = w[i];
+            a[4 * i + 0] = (v & 0x000F000Fu) | MAGIC;
+            a[4 * i + 1] = ((v >> 4) & 0x000F000Fu) | MAGIC;
+            a[4 * i + 2] = ((v >> 8) & 0x000F000Fu) | MAGIC;
+            a[4 * i + 3] = ((v >> 12) & 0x000F000Fu) | MAGIC;
+        }
+    }
+}
+
+// Byte offset of word `wi` of subtile row `r` inside a subtile's swizzled code block
+// (boxes of 16 rows x SW bytes, TMA swizzle of 16-byte chunks within SW-byte rows).
+template <int SW>
+__device__ __forceinline__ uint32_t code_off(int r, int wi) {
+    constexpr int WPB = SW / 4;  // words per box row
+    const int box = wi / WPB, iw = wi % WPB;
+    const int swz = SW == 128 ? (r & 7) : ((r >> 1) & 3);
+    return box * (16 * SW) + r * SW + ((((iw >> 2) ^ swz)) << 4) + (iw & 3) * 4;
+}
+
+// Load the code window of (subtile row r, group gi) for lane-quarter t.
+template <int BITS>
+__device__ __forceinline__ void load_window(const uint8_t* sub, int r, int gi, int t,
+                                            uint32_t* w) {
+    if constexpr (BITS == 2) {
+        w[0] = *reinterpret_cast<const uint32_t*>(sub + code_off<128>(r, 4 * gi + t));
+    } else if constexpr (BITS == 4) {
+        const uint2 v = *reinterpret_cast<const uint2*>(sub + code_off<128>(r, 8 * gi + 2 * t));
+        w[0] = v.x;
+        w[1] = v.y;
+    } else if constexpr (BITS == 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(sub + code_off<128>(r, 16 * gi + 4 * t));
+        w[0] = v.x;
+        w[1] = v.y;
+        w[2] = v.z;
+        w[3] = v.w;
+    } else {  // 3 bits: the thread's 48 bits start at bit 48t of the group's 192
+        const int k0 = 6 * gi + ((t * 3) >> 1);  // t: 0,1,2,3 -> word 0,1,3,4
+        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(sub + code_off<64>(r, k0));
+        const uint32_t w1 = *reinterpret_cast<const uint32_t*>(sub + code_off<64>(r, k0 + 1));
+        if (t & 1) {
+            w[0] = __funnelshift_r(w0, w1, 16);
+            w[1] = w1 >> 16;
+        } else {
+            w[0] = w0;
+            w[1] = w1;
+        }
+    }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    return static_cast<uint32_t>(f32_to_bf16_bits(lo)) |
+           (static_cast<uint32_t>(f32_to_bf16_bits(hi)) << 16);
+}
+
+// ---------------------------------------------------------------------------------
+// Prologue: activation fragments + per-group sums, one CTA per 512-k chunk.
+// Layout per chunk (M tokens): [group 8][half SPG/2][m][t 4][16 B], then the bias-step
+// fragments [sigma 2][m][t 4][8 B].
+// ---------------------------------------------------------------------------------
+template <int BITS>
+__global__ void __launch_bounds__(256) qgemv_prep(const __nv_bfloat16* __restrict__ x, int M,
+                                                  int K, uint8_t* __restrict__ xfrag) {
+    using F = Fmt<BITS>;
+    griddep_launch_dependents();
+    __shared__ float s_xs[GROUPS][16], s_xp[GROUPS][16];
+    const int c = blockIdx.x;
+    uint8_t* base = xfrag + static_cast<size_t>(c) * M * F::XF_PER_M;
+    const int items = GROUPS * M * 4;
+    for (int i = threadIdx.x; i < items; i += blockDim.x) {
+        const int t = i & 3, gm = i >> 2, m = gm % M, gi = gm / M;
+        const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(m) * K +
+                                                          c * KC + gi * 64 + t * 16);
+        const uint4 u0 = src[0], u1 = src[1];
+        const uint32_t raw[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+        float xv[16];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            xv[2 * j] = bf16_bits_to_f32(raw[j] & 0xFFFFu);
+            xv[2 * j + 1] = bf16_bits_to_f32(raw[j] >> 16);
+        }
+        float xs = 0.f, xp = 0.f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) xs += xv[j];
+        uint32_t* dst = reinterpret_cast<uint32_t*>(base);
+#pragma unroll
+        for (int q = 0; q < F::NP; ++q) {
+            const float lo = xv[pair_code<BITS>(q, 0)] * pair_mult<BITS>(q, 0);
+            const float hi = xv[pair_code<BITS>(q, 1)] * pair_mult<BITS>(q, 1);
+            xp += lo + hi;
+            const size_t off = ((static_cast<size_t>(gi) * (F::SPG / 2) + q / 4) * M + m) * 64 +
+                               t * 16 + (q % 4) * 4;
+            dst[off / 4] = pack_bf16x2(lo, hi);
+        }
+        xs += __shfl_xor_sync(0xffffffffu, xs, 1);
+        xs += __shfl_xor_sync(0xffffffffu, xs, 2);
+        xp += __shfl_xor_sync(0xffffffffu, xp, 1);
+        xp += __shfl_xor_sync(0xffffffffu, xp, 2);
+        if (t == 0) {
+            s_xs[gi][m] = xs;
+            s_xp[gi][m] = xp;
+        }
+    }
+    __syncthreads();
+    uint8_t* bias = base + static_cast<size_t>(GROUPS) * (F::SPG / 2) * M * 64;
+    for (int i = threadIdx.x; i < 8 * M; i += blockDim.x) {
+        const int t = i & 3, mm = i >> 2, m = mm % M, sigma = mm / M;
+        uint32_t out[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int gi = 4 * sigma + 2 * h + (t >> 1);
+            const float v = (t & 1) ? s_xs[gi][m] : s_xp[gi][m];
+            const float vhi = bf16_bits_to_f32(f32_to_bf16_bits(v));
+            const float vlo = v - vhi;
+            const float f = (t & 1) ? 1.0f : -128.0f;
+            out[h] = pack_bf16x2(vhi * f, vlo * f);
+        }
+        uint32_t* d = reinterpret_cast<uint32_t*>(bias + (static_cast<size_t>(sigma) * M + m) * 32 +
+                                                  t * 8);
+        d[0] = out[0];
+        d[1] = out[1];
+    }
+}
+
+// ---------------------------------------------------------------------------------
+// Main kernel.
+// ---------------------------------------------------------------------------------
+struct MainArgs {
+    const uint8_t* xfrag;
+    __nv_bfloat16* y;
+    float* ws;
+    uint32_t* cnt;
+    uint32_t* status;
+    int M, N, C, tiles, stages, stage_bytes, has_bias;
+};
+
+template <int NT>
+__device__ __forceinline__ void flush_subtile(const float (&acc)[NT][4], int tile, int warp,
+                                              int nchunks, const MainArgs& a, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    const int r0 = tile * 64 + warp * 16 + g;
+    const int sub = tile * 4 + warp;
+    if (nchunks == a.C) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int r = r0 + ((e >> 1) << 3), m = nt * 8 + 2 * t + (e & 1);
+                if (r < a.N && m < a.M) a.y[static_cast<size_t>(m) * a.N + r] = __float2bfloat16_rn(acc[nt][e]);
+            }
+        return;
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int r = r0 + ((e >> 1) << 3), m = nt * 8 + 2 * t + (e & 1);
+            if (r < a.N && m < a.M) atomicAdd(a.ws + static_cast<size_t>(m) * a.N + r, acc[nt][e]);
+        }
+    __threadfence();
+    __syncwarp();
+    uint32_t last = 0;
+    if (lane == 0) {
+        const uint32_t old = atomicAdd(a.cnt + sub, static_cast<uint32_t>(nchunks));
+        last = (old + nchunks == static_cast<uint32_t>(a.C));
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence();
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int r = r0 + ((e >> 1) << 3), m = nt * 8 + 2 * t + (e & 1);
+            if (r < a.N && m < a.M) {
+                float* p = a.ws + static_cast<size_t>(m) * a.N + r;
+                a.y[static_cast<size_t>(m) * a.N + r] = __float2bfloat16_rn(__ldcg(p));
+                __stcg(p, 0.0f);
+            }
+        }
+    if (lane == 0) a.cnt[sub] = 0;
+}
+
+template <int BITS, int NT>
+__global__ void __launch_bounds__(THREADS) qgemv_main(const __grid_constant__ CUtensorMap map_codes,
+                                                      const __grid_constant__ CUtensorMap map_scales,
+                                                      const __grid_constant__ CUtensorMap map_biases,
+                                                      const MainArgs a) {
+    using F = Fmt<BITS>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + a.stages;
+    uint8_t* stage0 = smem + 1024;
+
+    const long long total_sub = static_cast<long long>(a.tiles) * a.C * 4;
+    const long long s0 = total_sub * blockIdx.x / gridDim.x;
+    const long long s1 = total_sub * (blockIdx.x + 1) / gridDim.x;
+    if (s1 <= s0) return;
+    const long long st_first = s0 / 4;
+    const int nst = static_cast<int>((s1 - 1) / 4 - st_first + 1);
+    const int xf_bytes = a.M * F::XF_PER_M;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < a.stages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], NCW);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == NCW) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            prefetch_tensormap(&map_codes);
+            prefetch_tensormap(&map_scales);
+            if (a.has_bias) prefetch_tensormap(&map_biases);
+            bool waited = false;
+            int issued_xf = 0;  // stages whose activation fragments are issued
+            for (int i = 0; i < nst; ++i) {
+                const int slot = i % a.stages;
+                const uint32_t ph = (i / a.stages) & 1;
+                if (i >= a.stages && !mbar_wait(&empty[slot], ph ^ 1, a.status)) return;
+                const long long st = st_first + i;
+                const int tile = static_cast<int>(st / a.C), chunk = static_cast<int>(st % a.C);
+                const int sub_lo = static_cast<int>(s0 - 4 * st > 0 ? s0 - 4 * st : 0);
+                const int sub_hi = static_cast<int>(s1 - 4 * st < 4 ? s1 - 4 * st : 4);
+                uint8_t* sbase = stage0 + static_cast<size_t>(slot) * a.stage_bytes;
+                int nact = 0;
+                for (int s = sub_lo; s < sub_hi; ++s) nact += (tile * 64 + 16 * s < a.N);
+                const uint32_t bytes = nact * F::SUB_BYTES + 1024 + (a.has_bias ? 1024 : 0) + xf_bytes;
+                mbar_arrive_expect_tx(&full[slot], bytes);
+                for (int s = sub_lo; s < sub_hi; ++s) {
+                    if (tile * 64 + 16 * s >= a.N) continue;
+#pragma unroll
+                    for (int bx = 0; bx < F::BOXES; ++bx)
+                        tma_load_2d(sbase + s * F::SUB_BYTES + bx * 16 * F::SW, &map_codes, &full[slot],
+                                    chunk * F::ROW_WORDS + bx * (F::SW / 4), tile * 64 + 16 * s);
+                }
+                uint8_t* sc = sbase + NCW * F::SUB_BYTES;
+                tma_load_2d(sc, &map_scales, &full[slot], chunk * GROUPS, tile * 64);
+                if (a.has_bias) tma_load_2d(sc + 1024, &map_biases, &full[slot], chunk * GROUPS, tile * 64);
+                // Activation fragments come from the prologue kernel: wait for it only
+                // once the ring is full of weight loads.
+                if (!waited && (i == a.stages - 1 || i == nst - 1)) {
+                    griddep_wait();
+                    waited = true;
+                }
+                if (waited) {
+                    for (; issued_xf <= i; ++issued_xf) {
+                        const long long sti = st_first + issued_xf;
+                        const int ci = static_cast<int>(sti % a.C);
+                        const int sl = issued_xf % a.stages;
+                        uint8_t* dst = stage0 + static_cast<size_t>(sl) * a.stage_bytes + NCW * F::SUB_BYTES + 2048;
+                        bulk_load(dst, a.xfrag + static_cast<size_t>(ci) * xf_bytes, xf_bytes, &full[sl]);
+                    }
+                }
+            }
+        }
+        return;
+    }
+
+    // -------------------------------------------------------------- consumers
+    const int g = lane >> 2, t = lane & 3;
+    float acc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+    int cur_tile = -1, nchunks = 0;
+    const int srow0 = warp * 16 + g, srow1 = srow0 + 8;
+    for (int i = 0; i < nst; ++i) {
+        const int slot = i % a.stages;
+        const uint32_t ph = (i / a.stages) & 1;
+        const long long st = st_first + i;
+        const int tile = static_cast<int>(st / a.C);
+        const int sub_lo = static_cast<int>(s0 - 4 * st > 0 ? s0 - 4 * st : 0);
+        const int sub_hi = static_cast<int>(s1 - 4 * st < 4 ? s1 - 4 * st : 4);
+        if (tile != cur_tile) {
+            if (nchunks > 0) flush_subtile<NT>(acc, cur_tile, warp, nchunks, a, lane);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+            cur_tile = tile;
+            nchunks = 0;
+        }
+        const bool active = warp >= sub_lo && warp < sub_hi && tile * 64 + 16 * warp < a.N;
+        if (!mbar_wait(&full[slot], ph, a.status)) return;
+        if (active) {
+            const uint8_t* sbase = stage0 + static_cast<size_t>(slot) * a.stage_bytes;
+            const uint8_t* sub = sbase + warp * F::SUB_BYTES;
+            const uint16_t* scl = reinterpret_cast<const uint16_t*>(sbase + NCW * F::SUB_BYTES);
+            const uint16_t* bia = scl + 512;
+            const uint8_t* xf = sbase + NCW * F::SUB_BYTES + 2048;
+#pragma unroll 1
+            for (int gi = 0; gi < GROUPS; ++gi) {
+                uint32_t w0[4], w1[4], a0[F::NP], a1[F::NP];
+                load_window<BITS>(sub, g, gi, t, w0);
+                load_window<BITS>(sub, g + 8, gi, t, w1);
+                uint32_t xb[NT][F::NP];
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    const int m = nt * 8 + g;
+#pragma unroll
+                    for (int h = 0; h < F::SPG / 2; ++h) {
+                        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                        if (m < a.M)
+                            v = *reinterpret_cast<const uint4*>(
+                                xf + ((static_cast<size_t>(gi) * (F::SPG / 2) + h) * a.M + m) * 64 + t * 16);
+                        xb[nt][4 * h + 0] = v.x;
+                        xb[nt][4 * h + 1] = v.y;
+                        xb[nt][4 * h + 2] = v.z;
+                        xb[nt][4 * h + 3] = v.w;
+                    }
+                }
+                extract<BITS>(w0, a0);
+                extract<BITS>(w1, a1);
+                float d[NT][4];
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) d[nt][e] = 0.f;
+#pragma unroll
+                for (int j = 0; j < F::SPG; ++j)
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+                        mma_bf16_16816(d[nt], a0[2 * j], a1[2 * j], a0[2 * j + 1], a1[2 * j + 1],
+                                       xb[nt][2 * j], xb[nt][2 * j + 1], d[nt]);
+                const float sc0 = bf16_bits_to_f32(scl[srow0 * GROUPS + gi]);
+                const float sc1 = bf16_bits_to_f32(scl[srow1 * GROUPS + gi]);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    acc[nt][0] = fmaf(sc0, d[nt][0], acc[nt][0]);
+                    acc[nt][1] = fmaf(sc0, d[nt][1], acc[nt][1]);
+                    acc[nt][2] = fmaf(sc1, d[nt][2], acc[nt][2]);
+                    acc[nt][3] = fmaf(sc1, d[nt][3], acc[nt][3]);
+                }
+            }
+            // bias and offset terms of the chunk's 8 groups: two MMA steps
+            const uint8_t* bf = xf + static_cast<size_t>(GROUPS) * (F::SPG / 2) * a.M * 64;
+#pragma unroll
+            for (int sigma = 0; sigma < 2; ++sigma) {
+                const int ga = 4 * sigma + (t >> 1), gb = ga + 2;
+                const uint16_t* src = (t & 1) ? bia : scl;
+                const bool use = !(t & 1) || a.has_bias;
+                const uint32_t v0a = use ? src[srow0 * GROUPS + ga] * 0x00010001u : 0u;
+                const uint32_t v1a = use ? src[srow1 * GROUPS + ga] * 0x00010001u : 0u;
+                const uint32_t v0b = use ? src[srow0 * GROUPS + gb] * 0x00010001u : 0u;
+                const uint32_t v1b = use ? src[srow1 * GROUPS + gb] * 0x00010001u : 0u;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    const int m = nt * 8 + g;
+                    uint2 bb = make_uint2(0u, 0u);
+                    if (m < a.M)
+                        bb = *reinterpret_cast<const uint2*>(bf + (static_cast<size_t>(sigma) * a.M + m) * 32 + t * 8);
+                    mma_bf16_16816(acc[nt], v0a, v1a, v0b, v1b, bb.x, bb.y, acc[nt]);
+                }
+            }
+            ++nchunks;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    if (nchunks > 0) flush_subtile<NT>(acc, cur_tile, warp, nchunks, a, lane);
+}
+
+template <int BITS, int NT>
+q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, const void* s,
+                  const void* b, int N, void* y) {
+    using F = Fmt<BITS>;
+    const int C = K / KC;
+    const int tiles = (N + 63) / 64;
+    const size_t xf_bytes = static_cast<size_t>(M) * F::XF_PER_M;
+    q38_status st = ensure_workspace(ctx, C * xf_bytes);
+    if (st != Q38_OK) return st;
+    uint32_t* cnt = nullptr;
+    float* part = nullptr;
+    st = ensure_zero_region(ctx, static_cast<size_t>((N + 15) / 16), static_cast<size_t>(M) * N, &cnt, &part);
+    if (st != Q38_OK) return st;
+    uint8_t* wsb = static_cast<uint8_t*>(ctx->workspace);
+
+    CUtensorMap mc, ms, mb;
+    const uint64_t kw = static_cast<uint64_t>(K) * BITS / 32;
+    if (!make_map_2d(&mc, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w, kw, N, F::SW / 4, 16,
+                     F::SW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map_2d(&ms, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s, K / 64, N, GROUPS, 64,
+                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b ? b : s, K / 64, N, GROUPS, 64,
+                     CU_TENSOR_MAP_SWIZZLE_NONE))
+        return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: tensor map encoding failed");
+
+    const int stage_bytes = static_cast<int>(align_up(NCW * F::SUB_BYTES + 2048 + xf_bytes, 1024));
+    int stages = (100 * 1024) / stage_bytes;
+    if (stages > 8) stages = 8;
+    if (stages < 2) stages = 2;
+    int smem = 2048 + stages * stage_bytes;
+    while (smem > 227 * 1024 && stages > 2) {
+        --stages;
+        smem = 2048 + stages * stage_bytes;
+    }
+    if (smem > 227 * 1024) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: stage too large");
+
+    auto kmain = qgemv_main<BITS, NT>;
+    static bool configured[64] = {};  // per template instance and device
+    if (ctx->device < 64 && !configured[ctx->device]) {
+        if (cudaFuncSetAttribute(kmain, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
+            return check_launch(ctx, "cudaFuncSetAttribute");
+        configured[ctx->device] = true;
+    }
+    int occ = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kmain, THREADS, smem);
+    if (occ < 1) occ = 1;
+    const long long total_sub = static_cast<long long>(tiles) * C * 4;
+    long long grid = static_cast<long long>(ctx->num_sms) * occ;
+    if (grid > total_sub) grid = total_sub;
+
+    qgemv_prep<BITS><<<C, 256, 0, ctx->stream>>>(static_cast<const __nv_bfloat16*>(x), M, K, wsb);
+    st = check_launch(ctx, "qgemv_prep");
+    if (st != Q38_OK) return st;
+
+    MainArgs args;
+    args.xfrag = wsb;
+    args.y = static_cast<__nv_bfloat16*>(y);
+    args.ws = part;
+    args.cnt = cnt;
+    args.status = ctx->d_status;
+    args.M = M;
+    args.N = N;
+    args.C = C;
+    args.tiles = tiles;
+    args.stages = stages;
+    args.stage_bytes = stage_bytes;
+    args.has_bias = b != nullptr;
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kmain, mc, ms, mb, args) != cudaSuccess)
+        return check_launch(ctx, "qgemv_main");
+    return check_launch(ctx, "qgemv_main");
+}
+
+}  // namespace
+
+bool qgemv_fast_supported(int64_t M, int64_t K, int group, int bits, q38_dtype xd, q38_dtype sd,
+                          const void* x, const void* w, const void* s, const void* b,
+                          const void* y) {
+    if (M < 1 || M > 16 || group != 64 || K % KC != 0 || K <= 0) return false;
+    if (bits != 2 && bits != 3 && bits != 4 && bits != 8) return false;
+    if (xd != Q38_BF16 || sd != Q38_BF16) return false;
+    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    if (!al(x) || !al(w) || !al(s) || (b && !al(b))) return false;
+    (void)y;
+    return true;
+}
+
+q38_status qgemv_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w,
+                      const void* s, const void* b, int64_t N, int bits, void* y) {
+    const int m = static_cast<int>(M), k = static_cast<int>(K), n = static_cast<int>(N);
+    const bool two = M > 8;
+    switch (bits) {
+        case 2: return two ? launch<2, 2>(ctx, x, m, k, w, s, b, n, y) : launch<2, 1>(ctx, x, m, k, w, s, b, n, y);
+        case 3: return two ? launch<3, 2>(ctx, x, m, k, w, s, b, n, y) : launch<3, 1>(ctx, x, m, k, w, s, b, n, y);
+        case 4: return two ? launch<4, 2>(ctx, x, m, k, w, s, b, n, y) : launch<4, 1>(ctx, x, m, k, w, s, b, n, y);
+        case 8: return two ? launch<8, 2>(ctx, x, m, k, w, s, b, n, y) : launch<8, 1>(ctx, x, m, k, w, s, b, n, y);
+    }
+    return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: bits %d not on the fast path", bits);
+}
+
+}  // namespace q38

@@ -1,0 +1,318 @@
+"""Python binding of libq38 (the sm_100a MLX-affine quantized-matmul library).
+
+This is a thin ctypes layer over the C ABI declared in include/q38.h.  Tensors are
+torch CUDA tensors (torch provides device memory and streams only); every call goes
+to libq38.so on the tensor's device and current torch stream.  There is no fallback:
+if libq38.so is missing, importing this module raises.
+
+Operator functions mirror the MLX operators the reference calls (argument names and
+meaning as at the reference call sites); the module classes mirror MLXNN/MLXLMCommon's
+QuantizedLinear, QuantizedSwitchLinear and SwitchGLU and the reference's
+Qwen38HadamardQuantizedLinear.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libq38.so")
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(f"libq38.so not found at {LIB_PATH}; build it with "
+                      f"python {os.path.join(_HERE, 'build.py')}")
+
+_lib = C.CDLL(LIB_PATH)
+
+Q38_OK = 0
+_STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported", 3: "cuda error", 4: "out of memory",
+           5: "device wait timed out", 6: "communication error"}
+BF16, F16, F32 = 0, 1, 2
+_DTYPE = {torch.bfloat16: BF16, torch.float16: F16, torch.float32: F32}
+
+_P, _I, _i, _S = C.c_void_p, C.c_int64, C.c_int, C.c_size_t
+
+
+def _sig(name, args, res=C.c_int):
+    fn = getattr(_lib, name)
+    fn.argtypes = args
+    fn.restype = res
+    return fn
+
+
+_sig("q38_version", [])
+_sig("q38_status_string", [_i], C.c_char_p)
+_sig("q38_ctx_create", [_i, C.POINTER(_P)])
+_sig("q38_ctx_destroy", [_P])
+_sig("q38_ctx_set_stream", [_P, _P])
+_sig("q38_ctx_get_stream", [_P], _P)
+_sig("q38_ctx_reserve", [_P, _S])
+_sig("q38_ctx_workspace_bytes", [_P], _S)
+_sig("q38_ctx_check_device", [_P])
+_sig("q38_last_error", [_P], C.c_char_p)
+_sig("q38_quantized_matmul", [_P, _P, _I, _I, _i, _P, _P, _P, _i, _I, _i, _i, _i, _i, _P])
+_sig("q38_gather_quantized_matmul",
+     [_P, _P, _I, _I, _I, _i, _P, _P, _P, _i, _I, _I, _P, _P, _I, _i, _i, _i, _i, _i, _P])
+_sig("q38_dequantize", [_P, _P, _P, _P, _i, _I, _I, _i, _i, _i, _P, _i])
+_sig("q38_quantize", [_P, _P, _i, _I, _I, _i, _i, _i, _P, _P, _P, _i])
+_sig("q38_unpack_codes", [_P, _P, _I, _I, _i, _P])
+_sig("q38_hadamard_rotate", [_P, _P, _I, _I, _i, _P, _i, _i, _P])
+_sig("q38_hadamard_quantized_matmul", [_P, _P, _I, _I, _i, _P, _i, _P, _P, _P, _i, _I, _i, _i, _P])
+
+
+class Q38Error(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{_STATUS.get(status, status)}: {message}")
+        self.status = status
+
+
+class Q38ArgumentError(Q38Error, ValueError):
+    pass
+
+
+_ctx_lock = threading.Lock()
+_ctxs: dict[tuple[int, int], int] = {}
+
+
+def context(device: int | torch.device | None = None) -> int:
+    """Context handle for `device` on this host thread (created on first use)."""
+    if device is None:
+        device = torch.cuda.current_device()
+    if isinstance(device, torch.device):
+        device = device.index if device.index is not None else torch.cuda.current_device()
+    key = (threading.get_ident(), int(device))
+    with _ctx_lock:
+        h = _ctxs.get(key)
+        if h is None:
+            p = _P()
+            st = _lib.q38_ctx_create(int(device), C.byref(p))
+            if st != Q38_OK:
+                raise Q38Error(st, f"context creation on device {device} failed")
+            h = p.value
+            _ctxs[key] = h
+    return h
+
+
+def _bind(t: torch.Tensor) -> int:
+    ctx = context(t.device)
+    _lib.q38_ctx_set_stream(ctx, torch.cuda.current_stream(t.device).cuda_stream)
+    return ctx
+
+
+def _check(ctx: int, st: int) -> None:
+    if st != Q38_OK:
+        msg = (_lib.q38_last_error(ctx) or b"").decode()
+        if st in (1,):
+            raise Q38ArgumentError(st, msg)
+        raise Q38Error(st, msg)
+
+
+def check_device(device=None) -> None:
+    """Synchronise and raise if a kernel reported a timeout or an out-of-range index."""
+    ctx = context(device)
+    _lib.q38_ctx_set_stream(ctx, torch.cuda.current_stream(device).cuda_stream)
+    _check(ctx, _lib.q38_ctx_check_device(ctx))
+
+
+def reserve(nbytes: int, device=None) -> None:
+    ctx = context(device)
+    _check(ctx, _lib.q38_ctx_reserve(ctx, int(nbytes)))
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _need(t: torch.Tensor, name: str):
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _as_u32(w: torch.Tensor) -> torch.Tensor:
+    if w.dtype == torch.int32:
+        return w
+    if w.dtype == torch.uint32:
+        return w.view(torch.int32)
+    raise ValueError("packed weight must be uint32 (or int32 bit-identical storage)")
+
+
+# ----------------------------------------------------------------------- operators
+
+def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
+                     biases: torch.Tensor | None = None, transpose: bool = True,
+                     group_size: int = 64, bits: int = 4, mode: str = "affine") -> torch.Tensor:
+    """MLX.quantizedMM: x[..., K] . dequant(w)^T -> [..., N] (transpose=true)."""
+    if mode != "affine":
+        raise Q38Error(2, f"mode {mode!r} is not implemented")
+    _need(x, "x"), _need(w, "w"), _need(scales, "scales")
+    if biases is not None:
+        _need(biases, "biases")
+    w = _as_u32(w)
+    K = x.shape[-1]
+    N = w.shape[0]
+    M = x.numel() // K if K else 0
+    y = torch.empty(x.shape[:-1] + (N,), dtype=x.dtype, device=x.device)
+    ctx = _bind(x)
+    _check(ctx, _lib.q38_quantized_matmul(ctx, _ptr(x), M, K, _DTYPE[x.dtype], _ptr(w), _ptr(scales),
+                                          _ptr(biases), _DTYPE[scales.dtype], N, int(transpose),
+                                          group_size, bits, 0, _ptr(y)))
+    return y
+
+
+def gather_qmm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
+               biases: torch.Tensor | None = None, lhs_indices: torch.Tensor | None = None,
+               rhs_indices: torch.Tensor | None = None, transpose: bool = True,
+               group_size: int = 64, bits: int = 4, mode: str = "affine",
+               sorted_indices: bool = False) -> torch.Tensor:
+    """MLX.gatherQuantizedMM with flattened batch: x [Bx, M, K], w [E, N, K*bits/32],
+    rhs_indices [P] (int32), lhs_indices [P] or None -> out [P, M, N]."""
+    if mode != "affine":
+        raise Q38Error(2, f"mode {mode!r} is not implemented")
+    if rhs_indices is None:
+        raise ValueError("rhs_indices is required")
+    _need(x, "x"), _need(w, "w"), _need(scales, "scales"), _need(rhs_indices, "rhs_indices")
+    w = _as_u32(w)
+    Bx, M, K = x.shape
+    E, N = w.shape[0], w.shape[1]
+    P = rhs_indices.numel()
+    out = torch.empty((P, M, N), dtype=x.dtype, device=x.device)
+    ctx = _bind(x)
+    _check(ctx, _lib.q38_gather_quantized_matmul(
+        ctx, _ptr(x), Bx, M, K, _DTYPE[x.dtype], _ptr(w), _ptr(scales), _ptr(biases),
+        _DTYPE[scales.dtype], E, N, _ptr(lhs_indices), _ptr(rhs_indices), P, int(transpose),
+        group_size, bits, 0, int(sorted_indices), _ptr(out)))
+    return out
+
+
+def dequantize(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor | None = None,
+               group_size: int = 64, bits: int = 4, mode: str = "affine",
+               out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """MLX.dequantized: w [..., K*bits/32] -> [..., K] = scale*q + bias."""
+    if mode != "affine":
+        raise Q38Error(2, f"mode {mode!r} is not implemented")
+    _need(w, "w"), _need(scales, "scales")
+    w = _as_u32(w)
+    K = w.shape[-1] * 32 // bits
+    rows = w.numel() // w.shape[-1]
+    od = out_dtype or scales.dtype
+    out = torch.empty(w.shape[:-1] + (K,), dtype=od, device=w.device)
+    ctx = _bind(w)
+    _check(ctx, _lib.q38_dequantize(ctx, _ptr(w), _ptr(scales), _ptr(biases), _DTYPE[scales.dtype],
+                                    rows, K, group_size, bits, 0, _ptr(out), _DTYPE[od]))
+    return out
+
+
+def quantize(w: torch.Tensor, group_size: int = 64, bits: int = 4, mode: str = "affine",
+             scales_dtype: torch.dtype | None = None):
+    """mx.quantize(mode="affine"): w [..., K] -> (codes uint32 [..., K*bits/32], scales, biases)."""
+    if mode != "affine":
+        raise Q38Error(2, f"mode {mode!r} is not implemented")
+    _need(w, "w")
+    K = w.shape[-1]
+    rows = w.numel() // K
+    sd = scales_dtype or (w.dtype if w.dtype != torch.float32 else torch.bfloat16)
+    codes = torch.empty(w.shape[:-1] + (K * bits // 32,), dtype=torch.int32, device=w.device)
+    s = torch.empty(w.shape[:-1] + (K // group_size,), dtype=sd, device=w.device)
+    b = torch.empty_like(s)
+    ctx = _bind(w)
+    _check(ctx, _lib.q38_quantize(ctx, _ptr(w), _DTYPE[w.dtype], rows, K, group_size, bits, 0,
+                                  _ptr(codes), _ptr(s), _ptr(b), _DTYPE[sd]))
+    return codes.view(torch.uint32), s, b
+
+
+def unpack_codes(w: torch.Tensor, bits: int) -> torch.Tensor:
+    _need(w, "w")
+    w = _as_u32(w)
+    K = w.shape[-1] * 32 // bits
+    rows = w.numel() // w.shape[-1]
+    q = torch.empty(w.shape[:-1] + (K,), dtype=torch.uint8, device=w.device)
+    ctx = _bind(w)
+    _check(ctx, _lib.q38_unpack_codes(ctx, _ptr(w), rows, K, bits, _ptr(q)))
+    return q
+
+
+def hadamard_rotate(x: torch.Tensor, signs: torch.Tensor | None, block: int,
+                    inverse: bool = False) -> torch.Tensor:
+    """hadamardRotate of Bonsai2/Qwen38HadamardModules.swift:10-19."""
+    _need(x, "x")
+    if signs is not None:
+        _need(signs, "signs")
+        if signs.dtype != torch.float32:
+            signs = signs.float().contiguous()
+    D = x.shape[-1]
+    rows = x.numel() // D
+    y = torch.empty_like(x)
+    ctx = _bind(x)
+    _check(ctx, _lib.q38_hadamard_rotate(ctx, _ptr(x), rows, D, _DTYPE[x.dtype], _ptr(signs), block,
+                                         int(inverse), _ptr(y)))
+    return y
+
+
+# ------------------------------------------------------------------------- modules
+
+class QuantizedLinear:
+    """MLXNN.QuantizedLinear: parameters `weight` (packed uint32), `scales`, `biases`,
+    optional `bias`; callAsFunction = quantizedMM(x, weight, ..., transpose: true) + bias."""
+
+    def __init__(self, weight, scales, biases=None, bias=None, group_size: int = 64, bits: int = 4,
+                 mode: str = "affine"):
+        self.weight, self.scales, self.biases, self.bias = weight, scales, biases, bias
+        self.group_size, self.bits, self.mode = group_size, bits, mode
+
+    @property
+    def shape(self):
+        return (self.weight.shape[0], self.weight.shape[-1] * 32 // self.bits)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        y = quantized_matmul(x, self.weight, self.scales, self.biases, True, self.group_size,
+                             self.bits, self.mode)
+        return y if self.bias is None else y + self.bias
+
+
+class HadamardQuantizedLinear(QuantizedLinear):
+    """Qwen38HadamardQuantizedLinear (Bonsai2/Qwen38HadamardModules.swift:24-40): rotate the
+    input (signs before the transform), round to x's dtype, then the quantized product."""
+
+    def __init__(self, source: QuantizedLinear, signs: torch.Tensor | None, block: int):
+        super().__init__(source.weight, source.scales, source.biases, source.bias,
+                         source.group_size, source.bits, source.mode)
+        self.signs = None if signs is None else signs.float().contiguous()
+        self.block = block
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        _need(x, "x")
+        K = x.shape[-1]
+        M = x.numel() // K
+        N = self.weight.shape[0]
+        y = torch.empty(x.shape[:-1] + (N,), dtype=x.dtype, device=x.device)
+        ctx = _bind(x)
+        _check(ctx, _lib.q38_hadamard_quantized_matmul(
+            ctx, _ptr(x), M, K, _DTYPE[x.dtype], _ptr(self.signs), self.block, _ptr(_as_u32(self.weight)),
+            _ptr(self.scales), _ptr(self.biases), _DTYPE[self.scales.dtype], N, self.group_size,
+            self.bits, _ptr(y)))
+        return y if self.bias is None else y + self.bias
+
+
+class QuantizedSwitchLinear:
+    """MLXLMCommon.QuantizedSwitchLinear: expert-stacked packed weight [E, N, K*bits/32];
+    callAsFunction(x, indices) = gatherQuantizedMM(x, weight, ..., rhsIndices: indices)."""
+
+    def __init__(self, weight, scales, biases=None, group_size: int = 64, bits: int = 4,
+                 mode: str = "affine"):
+        self.weight, self.scales, self.biases = weight, scales, biases
+        self.group_size, self.bits, self.mode = group_size, bits, mode
+
+    def __call__(self, x: torch.Tensor, indices: torch.Tensor, sorted_indices: bool = False):
+        """x [T, K] (one row per token), indices [T, k] -> [T, k, N]."""
+        T, K = x.shape
+        k = indices.shape[-1]
+        idx = indices.reshape(-1).to(torch.int32).contiguous()
+        lhs = torch.arange(T, device=x.device, dtype=torch.int32).repeat_interleave(k)
+        out = gather_qmm(x.reshape(T, 1, K).contiguous(), self.weight, self.scales, self.biases,
+                         lhs, idx, True, self.group_size, self.bits, self.mode, sorted_indices)
+        return out.reshape(T, k, -1)

@@ -1,0 +1,208 @@
+"""GPU parity of the quantized product and the format kernels against the CPU oracle.
+
+Every call goes through libq38.so's C ABI (q38.py is a ctypes layer).  Bar: unpacked
+codes, quantize/dequantize and the Hadamard rotation bit-exact; products within
+max|y - y_oracle| <= 2e-2 * RMS(y_oracle) (fp32 accumulation on both sides).
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-2
+
+
+def dev_bf16(a: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16).cuda()
+
+
+def dev_u32(a: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int32)).cuda()
+
+
+def host_bf16(t: torch.Tensor) -> np.ndarray:
+    return t.view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def make_weight(seed, N, K, bits, group=64):
+    w = O.normal_f32(seed, (N, K), 0.02)
+    return O.quantize(w, group, bits)
+
+
+def check_close(y_gpu_bf16: np.ndarray, y_ref: np.ndarray, tol=TOL):
+    y = O.bf16_to_f32(y_gpu_bf16).astype(np.float64)
+    ref = y_ref.astype(np.float64)
+    rms = np.sqrt((ref ** 2).mean())
+    err = np.abs(y - ref).max()
+    assert np.isfinite(y).all()
+    assert err <= tol * rms, f"max err {err:.4g} > {tol} * rms {rms:.4g}"
+    return err / rms
+
+
+@pytest.mark.parametrize("bits", [2, 3, 4, 8])
+@pytest.mark.parametrize("M", [1, 3, 8, 9, 16])
+@pytest.mark.parametrize("NK", [(200, 512), (1000, 2048), (64, 1536)])
+def test_qmm_decode_parity(q38, bits, M, NK):
+    N, K = NK
+    c, s, b = make_weight(100 + bits, N, K, bits)
+    x = O.normal_bf16(7 + M, (M, K))
+    ref = O.qmm(x, c, s, b, 64, bits, f32=True)
+    y = q38.quantized_matmul(dev_bf16(x), dev_u32(c), dev_bf16(s), dev_bf16(b), True, 64, bits)
+    torch.cuda.synchronize()
+    check_close(host_bf16(y), ref)
+
+
+@pytest.mark.parametrize("bits", [4, 3])
+def test_qmm_without_biases(q38, bits):
+    N, K, M = 128, 1024, 4
+    c, s, _ = make_weight(300, N, K, bits)
+    x = O.normal_bf16(301, (M, K))
+    ref = O.qmm(x, c, s, None, 64, bits, f32=True)
+    y = q38.quantized_matmul(dev_bf16(x), dev_u32(c), dev_bf16(s), None, True, 64, bits)
+    check_close(host_bf16(y), ref)
+
+
+def test_qmm_config0_single_4bit(q38):
+    """x bf16 [16, 4096], W [11008, 4096] N(0, 0.02^2) quantized 4-bit g64."""
+    c, s, b = make_weight(2026, 11008, 4096, 4)
+    x = O.normal_bf16(2027, (16, 4096))
+    ref = O.qmm(x, c, s, b, 64, 4, f32=True)
+    y = q38.quantized_matmul(dev_bf16(x), dev_u32(c), dev_bf16(s), dev_bf16(b), True, 64, 4)
+    check_close(host_bf16(y), ref)
+
+
+@pytest.mark.parametrize("bits", [2, 3, 4, 8])
+@pytest.mark.parametrize("NK", [(17408, 5120), (5120, 17408), (6144, 5120)])
+def test_qmm_decode_sweep_shapes(q38, bits, NK):
+    """The decode sweep's full shapes at M=1 and M=8."""
+    N, K = NK
+    c, s, b = make_weight(4000 + bits + N, N, K, bits)
+    for M in (1, 8):
+        x = O.normal_bf16(4100 + M, (M, K))
+        ref = O.qmm(x, c, s, b, 64, bits, f32=True)
+        y = q38.quantized_matmul(dev_bf16(x), dev_u32(c), dev_bf16(s), dev_bf16(b), True, 64, bits)
+        check_close(host_bf16(y), ref)
+
+
+def test_workspace_returns_to_zero_between_calls(q38):
+    """Split subtiles accumulate in a shared workspace that each call restores to zero:
+    interleaving shapes and repeating calls must give identical results."""
+    ca = make_weight(501, 5120, 17408, 4)
+    cb = make_weight(502, 1000, 2048, 2)
+    xa = O.normal_bf16(503, (8, 17408))
+    xb = O.normal_bf16(504, (3, 2048))
+    Wa = [dev_u32(ca[0]), dev_bf16(ca[1]), dev_bf16(ca[2])]
+    Wb = [dev_u32(cb[0]), dev_bf16(cb[1]), dev_bf16(cb[2])]
+    ya1 = q38.quantized_matmul(dev_bf16(xa), *Wa, True, 64, 4)
+    yb1 = q38.quantized_matmul(dev_bf16(xb), *Wb, True, 64, 2)
+    ya2 = q38.quantized_matmul(dev_bf16(xa), *Wa, True, 64, 4)
+    yb2 = q38.quantized_matmul(dev_bf16(xb), *Wb, True, 64, 2)
+    torch.cuda.synchronize()
+    assert torch.equal(ya1, ya2) and torch.equal(yb1, yb2)
+    q38.check_device()
+
+
+@pytest.mark.parametrize("group,bits,K,xdt", [(32, 4, 256, torch.bfloat16), (128, 2, 512, torch.bfloat16),
+                                              (64, 5, 320, torch.bfloat16), (64, 6, 192, torch.bfloat16),
+                                              (64, 4, 576, torch.float16), (64, 3, 128, torch.bfloat16)])
+def test_qmm_general_shapes(q38, group, bits, K, xdt):
+    N, M = 96, 37
+    c, s, b = make_weight(600 + bits, N, K, bits, group)
+    x = O.normal_bf16(601, (M, K))
+    ref = O.qmm(x, c, s, b, group, bits, f32=True)
+    xt = dev_bf16(x).to(xdt)
+    st, bt = dev_bf16(s).to(xdt), dev_bf16(b).to(xdt)
+    y = q38.quantized_matmul(xt, dev_u32(c), st, bt, True, group, bits)
+    check_close(host_bf16(y.to(torch.bfloat16)), ref)
+
+
+@pytest.mark.parametrize("bits", [2, 3, 4, 5, 6, 8])
+def test_unpack_codes_bit_exact(q38, bits):
+    c, _, _ = make_weight(700 + bits, 37, 512, bits)
+    q = q38.unpack_codes(dev_u32(c), bits).cpu().numpy()
+    np.testing.assert_array_equal(q, O.unpack(c, 512, bits))
+
+
+@pytest.mark.parametrize("bits", [2, 3, 4, 8])
+@pytest.mark.parametrize("group", [32, 64, 128])
+def test_quantize_bit_exact(q38, bits, group):
+    w = O.normal_f32(800 + bits, (45, 1024), 0.02)
+    c, s, b = O.quantize(w, group, bits)
+    gc, gs, gb = q38.quantize(torch.from_numpy(w).cuda(), group, bits, scales_dtype=torch.bfloat16)
+    np.testing.assert_array_equal(gc.view(torch.int32).cpu().numpy().view(np.uint32), c)
+    np.testing.assert_array_equal(host_bf16(gs), s)
+    np.testing.assert_array_equal(host_bf16(gb), b)
+
+
+@pytest.mark.parametrize("bits", [2, 3, 4, 8])
+def test_dequantize_bit_exact(q38, bits):
+    c, s, b = make_weight(900 + bits, 33, 512, bits)
+    d = q38.dequantize(dev_u32(c), dev_bf16(s), dev_bf16(b), 64, bits, out_dtype=torch.float32)
+    np.testing.assert_array_equal(d.cpu().numpy(), O.dequantize(c, s, b, 64, bits))
+
+
+@pytest.mark.parametrize("block", [64, 256, 512, 1024, 2048])
+@pytest.mark.parametrize("inverse", [False, True])
+def test_hadamard_bit_exact(q38, block, inverse):
+    D = 4096
+    x = O.normal_bf16(1000 + block, (5, D))
+    signs = np.where((np.arange(D) * 7) % 5 < 2, -1.0, 1.0).astype(np.float32)
+    ref = O.hadamard_rotate(x, block, signs, inverse)
+    y = q38.hadamard_rotate(dev_bf16(x), torch.from_numpy(signs).cuda(), block, inverse)
+    np.testing.assert_array_equal(host_bf16(y), ref)
+    ref0 = O.hadamard_rotate(x, block, None, inverse)
+    y0 = q38.hadamard_rotate(dev_bf16(x), None, block, inverse)
+    np.testing.assert_array_equal(host_bf16(y0), ref0)
+
+
+@pytest.mark.parametrize("M", [1, 8])
+def test_bonsai_hadamard_ternary_projection(q38, M):
+    """Bonsai-style: ternary 2-bit codes, bias = -scale, x rotated by block-256 FWHT."""
+    N, K = 1024, 5120
+    c, s, b = O.ternary(1100, N, K)
+    x = O.normal_bf16(1101, (M, K))
+    xr = O.hadamard_rotate(x, 256, None)
+    ref = O.qmm(xr, c, s, b, 64, 2, f32=True)
+    lin = q38.HadamardQuantizedLinear(q38.QuantizedLinear(dev_u32(c), dev_bf16(s), dev_bf16(b), None, 64, 2),
+                                      None, 256)
+    y = lin(dev_bf16(x))
+    check_close(host_bf16(y), ref)
+
+
+def test_gather_qmm_parity(q38):
+    E, N, K = 8, 96, 512
+    c, s, b = make_weight(1200, E * N, K, 3)
+    c, s, b = c.reshape(E, N, -1), s.reshape(E, N, -1), b.reshape(E, N, -1)
+    x = O.normal_bf16(1201, (4, 2, K))
+    lhs = np.array([0, 3, 1, 1, 2], np.int32)
+    rhs = np.array([7, 0, 7, 2, 5], np.int32)
+    ref = O.gather_qmm(x, c, s, b, lhs, rhs, 64, 3)
+    out = q38.gather_qmm(dev_bf16(x), dev_u32(c), dev_bf16(s), dev_bf16(b),
+                         torch.from_numpy(lhs).cuda(), torch.from_numpy(rhs).cuda(), True, 64, 3)
+    for p in range(5):
+        check_close(host_bf16(out[p]), O.bf16_to_f32(ref[p]).astype(np.float64), tol=2e-2)
+
+
+def test_gather_qmm_bad_index_is_reported(q38):
+    E, N, K = 2, 32, 128
+    c, s, b = make_weight(1300, E * N, K, 4)
+    x = O.normal_bf16(1301, (1, 1, K))
+    rhs = torch.tensor([5], dtype=torch.int32, device="cuda")
+    q38.gather_qmm(dev_bf16(x), dev_u32(c.reshape(E, N, -1)), dev_bf16(s.reshape(E, N, -1)),
+                   dev_bf16(b.reshape(E, N, -1)), None, rhs, True, 64, 4)
+    with pytest.raises(q38.Q38ArgumentError):
+        q38.check_device()
+    q38.check_device()  # cleared
+
+
+def test_argument_errors(q38):
+    x = torch.zeros(2, 100, dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros(8, 100 * 4 // 32, dtype=torch.int32, device="cuda")
+    s = torch.zeros(8, 2, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(q38.Q38ArgumentError):
+        q38.quantized_matmul(x, w, s, s, True, 64, 4)  # K not a multiple of the group
+    with pytest.raises(q38.Q38Error):
+        q38.quantized_matmul(x, w, s, s, False, 50, 4)
