@@ -159,6 +159,26 @@ Q38_API q38_status q38_hadamard_quantized_matmul(q38_ctx* ctx, const void* x, in
                                          const void* biases, q38_dtype scales_dtype, int64_t N,
                                          int group_size, int bits, void* y);
 
+/* Allocation-free decode product.  No counterpart in the reference: it exists for
+ * callers that must not allocate device memory on the calling path (a host framework
+ * that owns all device memory and hands a plugin only its input and output buffers, or
+ * a latency-critical decode loop where an allocation would stall or fail).  Same
+ * product as q38_quantized_matmul (transpose = true, affine, group 64, bits 2/3/4/8,
+ * bf16 x/y/scales/biases, 16-byte-aligned pointers) with no context: it runs on the
+ * calling thread's current device and on `stream` (a cudaStream_t, NULL = legacy
+ * default stream).  Its scratch is one fixed 4.1 MiB array in device memory that the
+ * library holds on every GPU it is loaded on until the process exits, so the limits
+ * are M <= 16, N <= 32768, K <= 32768 (K % 512 == 0); larger shapes return
+ * Q38_ERR_INVALID_ARGUMENT.  The first call on a device resolves the array's address
+ * (no allocation), so make that first call before any stream capture.  All calls on a
+ * device share the one array: calls that may overlap on the GPU (different streams
+ * without ordering between them) race and produce wrong results.  Returns a status
+ * only; there is no context to hold an error message. */
+Q38_API q38_status q38_quantized_matmul_noalloc(const void* x, int64_t M, int64_t K,
+                                                const uint32_t* w, const void* scales,
+                                                const void* biases, int64_t N, int group_size,
+                                                int bits, void* y, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -25,6 +25,8 @@
 //    workspace and counter to zero, so no per-call clearing is needed.
 //  * The main kernel is launched with programmatic dependent launch: its producer
 //    streams the first stages of weights while the prologue kernel is still running.
+#include <mutex>
+
 #include "ptx.cuh"
 
 namespace q38 {
@@ -584,4 +586,158 @@ q38_status qgemv_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const u
     return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: bits %d not on the fast path", bits);
 }
 
+// ---------------------------------------------------------------------------------
+// Allocation-free variant of the decode product (q38_quantized_matmul_noalloc).
+//
+// Some hosts cannot call cudaMalloc on the path where they run a projection: code
+// that runs inside an allocator-free region (a custom memory manager that owns all
+// device memory, a real-time decode loop that forbids allocation, or a plugin whose
+// host framework hands it only input and output buffers).  This entry point takes its
+// scratch from one fixed array in device memory, reserved when the library is loaded
+// on a GPU and held until the process exits.
+// ---------------------------------------------------------------------------------
+namespace {
+
+constexpr int64_t NA_MAX_M = 16, NA_MAX_N = 32768, NA_MAX_K = 32768;
+constexpr size_t NA_CNT_BYTES = static_cast<size_t>(NA_MAX_N / 16) * 4;                 // 8 KiB
+constexpr size_t NA_ACC_BYTES = static_cast<size_t>(NA_MAX_M) * NA_MAX_N * 4;          // 2 MiB
+constexpr size_t NA_XF_BYTES = static_cast<size_t>(NA_MAX_K / KC) * NA_MAX_M * (256 * 8 + 64);  // 2.06 MiB
+constexpr size_t NA_STATUS_OFF = 0;
+constexpr size_t NA_CNT_OFF = 256;
+constexpr size_t NA_ACC_OFF = NA_CNT_OFF + NA_CNT_BYTES;
+constexpr size_t NA_XF_OFF = NA_ACC_OFF + NA_ACC_BYTES;
+constexpr size_t NA_TOTAL = NA_XF_OFF + NA_XF_BYTES;
+
+// The scratch of every no-alloc call on a device (status word, subtile counters, fp32
+// partial sums, activation fragments).  In host code this name is only a stand-in for
+// the device array; its device address comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[NA_TOTAL];
+
+std::mutex g_noalloc_mu;
+uint8_t* g_noalloc_ptr[64] = {};
+
+// Once per device, with that device current: resolve the array's device address.
+q38_status noalloc_scratch(int device, uint8_t** out) {
+    if (device < 0 || device >= 64) return Q38_ERR_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[device]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
+            cudaGetLastError();
+            return Q38_ERR_CUDA;
+        }
+        g_noalloc_ptr[device] = static_cast<uint8_t*>(p);
+    }
+    *out = g_noalloc_ptr[device];
+    return Q38_OK;
+}
+
+template <int BITS, int NT>
+q38_status launch_noalloc(uint8_t* scratch, int num_sms, const void* x, int M, int K, const uint32_t* w,
+                          const void* s, const void* b, int N, void* y, cudaStream_t stream) {
+    using F = Fmt<BITS>;
+    const int C = K / KC;
+    const int tiles = (N + 63) / 64;
+    const size_t xf_bytes = static_cast<size_t>(M) * F::XF_PER_M;
+    uint32_t* status = reinterpret_cast<uint32_t*>(scratch + NA_STATUS_OFF);
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(scratch + NA_CNT_OFF);
+    float* part = reinterpret_cast<float*>(scratch + NA_ACC_OFF);
+    uint8_t* xfrag = scratch + NA_XF_OFF;
+    // counters and partial sums must start at zero; a previous call leaves them zero,
+    // but clear them anyway so an interrupted call cannot poison the next one
+    if (cudaMemsetAsync(cnt, 0, static_cast<size_t>((N + 15) / 16) * 4, stream) != cudaSuccess ||
+        cudaMemsetAsync(part, 0, static_cast<size_t>(M) * N * 4, stream) != cudaSuccess) {
+        cudaGetLastError();
+        return Q38_ERR_CUDA;
+    }
+
+    CUtensorMap mc, ms, mb;
+    const uint64_t kw = static_cast<uint64_t>(K) * BITS / 32;
+    if (!make_map_2d(&mc, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w, kw, N, F::SW / 4, 16,
+                     F::SW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map_2d(&ms, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s, K / 64, N, GROUPS, 64,
+                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b ? b : s, K / 64, N, GROUPS, 64,
+                     CU_TENSOR_MAP_SWIZZLE_NONE))
+        return Q38_ERR_CUDA;
+
+    const int stage_bytes = static_cast<int>(align_up(NCW * F::SUB_BYTES + 2048 + xf_bytes, 1024));
+    int stages = (100 * 1024) / stage_bytes;
+    if (stages > 8) stages = 8;
+    if (stages < 2) stages = 2;
+    int smem = 2048 + stages * stage_bytes;
+    while (smem > 227 * 1024 && stages > 2) {
+        --stages;
+        smem = 2048 + stages * stage_bytes;
+    }
+    if (smem > 227 * 1024) return Q38_ERR_UNSUPPORTED;
+
+    auto kmain = qgemv_main<BITS, NT>;
+    if (cudaFuncSetAttribute(kmain, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess) {
+        cudaGetLastError();
+        return Q38_ERR_CUDA;
+    }
+    int occ = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kmain, THREADS, smem);
+    if (occ < 1) occ = 1;
+    const long long total_sub = static_cast<long long>(tiles) * C * 4;
+    long long grid = static_cast<long long>(num_sms) * occ;
+    if (grid > total_sub) grid = total_sub;
+
+    qgemv_prep<BITS><<<C, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), M, K, xfrag);
+    if (cudaGetLastError() != cudaSuccess) return Q38_ERR_CUDA;
+
+    MainArgs args;
+    args.xfrag = xfrag;
+    args.y = static_cast<__nv_bfloat16*>(y);
+    args.ws = part;
+    args.cnt = cnt;
+    args.status = status;
+    args.M = M;
+    args.N = N;
+    args.C = C;
+    args.tiles = tiles;
+    args.stages = stages;
+    args.stage_bytes = stage_bytes;
+    args.has_bias = b != nullptr;
+    kmain<<<static_cast<unsigned>(grid), THREADS, smem, stream>>>(mc, ms, mb, args);
+    return cudaGetLastError() == cudaSuccess ? Q38_OK : Q38_ERR_CUDA;
+}
+
+}  // namespace
 }  // namespace q38
+
+extern "C" Q38_API q38_status q38_quantized_matmul_noalloc(const void* x, int64_t M, int64_t K,
+                                                          const uint32_t* w, const void* scales,
+                                                          const void* biases, int64_t N, int group_size,
+                                                          int bits, void* y, void* stream) {
+    using namespace q38;
+    if (!x || !w || !scales || !y) return Q38_ERR_INVALID_ARGUMENT;
+    if (group_size != 64 || (bits != 2 && bits != 3 && bits != 4 && bits != 8)) return Q38_ERR_UNSUPPORTED;
+    if (M < 1 || N < 1 || K < KC || K % KC != 0) return Q38_ERR_INVALID_ARGUMENT;
+    if (M > NA_MAX_M || N > NA_MAX_N || K > NA_MAX_K) return Q38_ERR_INVALID_ARGUMENT;  // beyond the fixed scratch
+    if (!qgemv_fast_supported(M, K, group_size, bits, Q38_BF16, Q38_BF16, x, w, scales, biases, y))
+        return Q38_ERR_INVALID_ARGUMENT;
+    int device = 0, sms = 0;
+    if (cudaGetDevice(&device) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
+        cudaGetLastError();
+        return Q38_ERR_CUDA;
+    }
+    uint8_t* scratch = nullptr;
+    q38_status st = noalloc_scratch(device, &scratch);
+    if (st != Q38_OK) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int m = static_cast<int>(M), k = static_cast<int>(K), n = static_cast<int>(N);
+    const bool two = M > 8;
+    switch (bits) {
+        case 2: return two ? launch_noalloc<2, 2>(scratch, sms, x, m, k, w, scales, biases, n, y, s)
+                           : launch_noalloc<2, 1>(scratch, sms, x, m, k, w, scales, biases, n, y, s);
+        case 3: return two ? launch_noalloc<3, 2>(scratch, sms, x, m, k, w, scales, biases, n, y, s)
+                           : launch_noalloc<3, 1>(scratch, sms, x, m, k, w, scales, biases, n, y, s);
+        case 4: return two ? launch_noalloc<4, 2>(scratch, sms, x, m, k, w, scales, biases, n, y, s)
+                           : launch_noalloc<4, 1>(scratch, sms, x, m, k, w, scales, biases, n, y, s);
+        default: return two ? launch_noalloc<8, 2>(scratch, sms, x, m, k, w, scales, biases, n, y, s)
+                            : launch_noalloc<8, 1>(scratch, sms, x, m, k, w, scales, biases, n, y, s);
+    }
+}
