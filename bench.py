@@ -51,44 +51,40 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """Polls nvidia-smi for SM clocks and throttle reasons while the timed work runs."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, period: float = 0.05):
         self.index = index
-        self.proc = None
+        self.period = period
         self.lines: list[str] = []
+        self.stop_evt = threading.Event()
         self.t = None
+        self.ok = True
+
+    def _poll(self):
+        while not self.stop_evt.is_set():
+            try:
+                r = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                    "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=10)
+                if r.returncode == 0:
+                    self.lines += [ln.strip() for ln in r.stdout.splitlines() if ln.strip()]
+            except (OSError, subprocess.SubprocessError):
+                self.ok = False
+                return
+            self.stop_evt.wait(self.period)
 
     def start(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except (OSError, FileNotFoundError):
-            self.proc = None
-            return
-        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t = threading.Thread(target=self._poll, daemon=True)
         self.t.start()
 
-    def _read(self):
-        for ln in self.proc.stdout:
-            self.lines.append(ln.strip())
-
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
+        self.stop_evt.set()
         if self.t:
-            self.t.join(timeout=2)
+            self.t.join(timeout=15)
         sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
@@ -103,8 +99,9 @@ class ClockSampler:
             for n, v in zip(names, f[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(smax) if smax else None,
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax),
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
@@ -161,10 +158,10 @@ def run_ours(args, rank, world, local_rank):
     ctx = q38.context(dev)
     stream = torch.cuda.current_stream(dev)
     lib = q38._lib
-    lib.q38_ctx_set_stream(ctx, stream.cuda_stream)
 
-    def call(M, N, K, bits, x, y):
-        c, s, b = weights[(bits, N, K)]
+    def call(M, N, K, bits, x, y, w=None):
+        c, s, b = w if w is not None else weights[(bits, N, K)]
+        lib.q38_ctx_set_stream(ctx, torch.cuda.current_stream(dev).cuda_stream)
         st = lib.q38_quantized_matmul(ctx, x.data_ptr(), M, K, 0, c.data_ptr(), s.data_ptr(), b.data_ptr(),
                                       0, N, 1, GROUP, bits, 0, y.data_ptr())
         if st != 0:
@@ -178,16 +175,31 @@ def run_ours(args, rank, world, local_rank):
         step()
     torch.cuda.synchronize()
 
-    # ---------------------------------------------------------------- timed region
+    def capture(fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        torch.cuda.synchronize()
+        return g
+
+    # One step = one replay of a CUDA graph holding the 24 products (48 kernel launches);
+    # replays are timed with CUDA events on the replaying stream.
+    step_graph = capture(step)
     sampler = ClockSampler(physical_index(local_rank))
     sampler.start()
+    for _ in range(max(args.warmup, 200)):
+        step_graph.replay()
+    torch.cuda.synchronize()
+    q38.check_device(dev)
+
+    # ---------------------------------------------------------------- timed region
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        step()
+        step_graph.replay()
     e1.record(stream)
     torch.cuda.synchronize()
     if dist:
@@ -200,41 +212,43 @@ def run_ours(args, rank, world, local_rank):
         ms = float(t.item())
     value = world * step_bytes / (ms * 1e-3) / 1e9
 
-    # per-case breakdown (same stream, events per case, averaged over a few passes)
+    # eager (no graph) step time, for reference: includes host launch overhead
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(3):
+        step()
+    f1.record(stream)
+    torch.cuda.synchronize()
+    eager_ms = f0.elapsed_time(f1) / 3
+
+    # per-case breakdown: a graph of 8 back-to-back launches of each product
     per_case = []
-    reps = 3
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in cases]
-    acc = [0.0] * len(cases)
-    for _ in range(reps):
-        for i, (M, N, K, bits) in enumerate(cases):
-            evs[i][0].record(stream)
-            call(M, N, K, bits, xs[(M, K)], ys[(M, N)])
-            evs[i][1].record(stream)
+    for (M, N, K, bits) in cases:
+        g = capture(lambda: [call(M, N, K, bits, xs[(M, K)], ys[(M, N)]) for _ in range(8)])
+        g.replay()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for _ in range(3):
+            g.replay()
+        c1.record(stream)
         torch.cuda.synchronize()
-        for i in range(len(cases)):
-            acc[i] += evs[i][0].elapsed_time(evs[i][1])
-    for i, (M, N, K, bits) in enumerate(cases):
-        us = acc[i] / reps * 1e3
+        us = c0.elapsed_time(c1) / 24 * 1e3
         per_case.append({"bits": bits, "M": M, "N": N, "K": K, "us": round(us, 2),
                          "GBps": round(algo_bytes(M, N, K, bits) / (us * 1e-6) / 1e9, 1)})
+        del g
 
     # roofline of the dominant kernel: 4-bit 17408x5120 M=1, rotating 4 weight copies
-    # (4 x 50 MB > L2) so every launch streams from HBM
+    # (4 x 50 MB > L2) so every launch streams from HBM; 200 launches in one graph
     peak, peak_kind = measured_peaks()
     rot = build_case_weights(torch, O, dev, 4, 17408, 5120, 4242, copies=4)
     xr = xs[(1, 5120)]
     yr = ys[(1, 17408)]
     nrep = 200
-    for i in range(8):
-        c, s, b = rot[i % 4]
-        lib.q38_quantized_matmul(ctx, xr.data_ptr(), 1, 5120, 0, c.data_ptr(), s.data_ptr(), b.data_ptr(), 0,
-                                 17408, 1, GROUP, 4, 0, yr.data_ptr())
+    rg = capture(lambda: [call(1, 17408, 5120, 4, xr, yr, rot[i % 4]) for i in range(nrep)])
+    rg.replay()
     r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     r0.record(stream)
-    for i in range(nrep):
-        c, s, b = rot[i % 4]
-        lib.q38_quantized_matmul(ctx, xr.data_ptr(), 1, 5120, 0, c.data_ptr(), s.data_ptr(), b.data_ptr(), 0,
-                                 17408, 1, GROUP, 4, 0, yr.data_ptr())
+    rg.replay()
     r1.record(stream)
     torch.cuda.synchronize()
     launch_us = r0.elapsed_time(r1) / nrep * 1e3
@@ -245,11 +259,13 @@ def run_ours(args, rank, world, local_rank):
                 "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                 "frac_of_8TBps": round(achieved / 8000.0, 4),
                 "algorithmic_bytes_per_launch": rbytes, "launch_us": round(launch_us, 2),
+                "timing": "CUDA events around one graph replay of 200 launches (prologue + main kernel each)",
                 "traffic": None}
     tr = os.path.join(ROOT, "profiles", "qgemv_traffic.json")
     if os.path.exists(tr):
         roofline["traffic"] = json.load(open(tr)).get("bytes_per_launch")
-    del rot
+    del rg, rot, step_graph
+    torch.cuda.synchronize()
 
     # e2e through the public API with host buffers: H2D of each product's x from pinned
     # memory, the product, D2H of y -- all inside the timed region
@@ -302,13 +318,15 @@ def run_ours(args, rank, world, local_rank):
                                "x M {1,8}, affine group 64, 24 products per step",
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2: 550 MB of packed weights per step, M=1 pass before M=8 pass",
-                   "step_bytes": step_bytes},
+                   "step_bytes": step_bytes,
+                   "timing": "one CUDA-graph replay per step (48 launches), CUDA events, max over ranks"},
         "frac_of_8TBps": round(value / world / 8000.0, 4),
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": e2e,
         "clocks": clocks,
         "gpu_launches": 2 * len(cases) * args.steps,
+        "eager_ms_per_step": round(eager_ms, 4),
         "cases": per_case,
     }
     return line
@@ -391,7 +409,7 @@ def main():
     ap.add_argument("--profile-bits", type=int, default=4)
     ap.add_argument("--profile-m", type=int, default=1)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)

@@ -20,6 +20,9 @@
 //    D = sum(q*x) + 128*sum(x'), and y += scale*D.  The -128*scale*sum(x') and
 //    bias*sum(x) terms of all 8 groups of a chunk are folded into two extra MMA
 //    steps whose operands are the scales/biases and hi/lo bf16 splits of the sums.
+//  * Consumers do no address arithmetic in the inner loop: swizzled code offsets are
+//    precomputed per thread, fragments are token-major so their offsets are constants,
+//    and the 8 groups of a stage are unrolled so their MMA chains overlap.
 //  * Subtiles split across CTAs accumulate through fp32 atomics into a workspace; the
 //    warp that completes a subtile (per-subtile chunk counter) writes y and returns the
 //    workspace and counter to zero, so no per-call clearing is needed.
@@ -49,8 +52,8 @@ struct Fmt {
     static constexpr int ROW_WORDS = ROW_BYTES / 4;
     static constexpr int BOXES = ROW_BYTES / SW;       // code boxes per subtile
     static constexpr int SUB_BYTES = 16 * ROW_BYTES;   // code bytes per subtile
-    static constexpr int XF_PER_M = 256 * SPG + 64;    // fragment bytes per token per chunk
-    static constexpr uint32_t MASK = BITS == 2 ? 0u : BITS == 3 ? 0x00070070u : 0x000F000Fu;
+    static constexpr int XF_FRAG = 256 * SPG;          // fragment bytes per token per chunk
+    static constexpr int XF_PER_M = XF_FRAG + 64;      // + bias-step fragments
 };
 
 // ---------------------------------------------------------------------------------
@@ -118,6 +121,7 @@ __device__ __forceinline__ void extract(const uint32_t* w, uint32_t* a) {
 
 // Byte offset of word `wi` of subtile row `r` inside a subtile's swizzled code block
 // (boxes of 16 rows x SW bytes, TMA swizzle of 16-byte chunks within SW-byte rows).
+// Rows r and r+8 share the swizzle, so row r+8 sits exactly 8*SW bytes after row r.
 template <int SW>
 __device__ __forceinline__ uint32_t code_off(int r, int wi) {
     constexpr int WPB = SW / 4;  // words per box row
@@ -126,33 +130,39 @@ __device__ __forceinline__ uint32_t code_off(int r, int wi) {
     return box * (16 * SW) + r * SW + ((((iw >> 2) ^ swz)) << 4) + (iw & 3) * 4;
 }
 
-// Load the code window of (subtile row r, group gi) for lane-quarter t.
+// First (and for 3 bits, second) word of the window of (row r, group gi, quarter t).
 template <int BITS>
-__device__ __forceinline__ void load_window(const uint8_t* sub, int r, int gi, int t,
+__device__ __forceinline__ void window_words(int gi, int t, int& w0, int& w1) {
+    if constexpr (BITS == 3) {
+        w0 = 6 * gi + ((t * 3) >> 1);  // t: 0,1,2,3 -> word 0,1,3,4 (bit 48t of the group)
+        w1 = w0 + 1;
+    } else {
+        w0 = gi * 2 * BITS + t * (BITS / 2);
+        w1 = w0;
+    }
+}
+
+// Load the code window at precomputed offsets (3 bits: two words, realigned for odd t).
+template <int BITS>
+__device__ __forceinline__ void load_window(const uint8_t* p, uint32_t offA, uint32_t offB, bool odd,
                                             uint32_t* w) {
     if constexpr (BITS == 2) {
-        w[0] = *reinterpret_cast<const uint32_t*>(sub + code_off<128>(r, 4 * gi + t));
+        w[0] = *reinterpret_cast<const uint32_t*>(p + offA);
     } else if constexpr (BITS == 4) {
-        const uint2 v = *reinterpret_cast<const uint2*>(sub + code_off<128>(r, 8 * gi + 2 * t));
+        const uint2 v = *reinterpret_cast<const uint2*>(p + offA);
         w[0] = v.x;
         w[1] = v.y;
     } else if constexpr (BITS == 8) {
-        const uint4 v = *reinterpret_cast<const uint4*>(sub + code_off<128>(r, 16 * gi + 4 * t));
+        const uint4 v = *reinterpret_cast<const uint4*>(p + offA);
         w[0] = v.x;
         w[1] = v.y;
         w[2] = v.z;
         w[3] = v.w;
-    } else {  // 3 bits: the thread's 48 bits start at bit 48t of the group's 192
-        const int k0 = 6 * gi + ((t * 3) >> 1);  // t: 0,1,2,3 -> word 0,1,3,4
-        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(sub + code_off<64>(r, k0));
-        const uint32_t w1 = *reinterpret_cast<const uint32_t*>(sub + code_off<64>(r, k0 + 1));
-        if (t & 1) {
-            w[0] = __funnelshift_r(w0, w1, 16);
-            w[1] = w1 >> 16;
-        } else {
-            w[0] = w0;
-            w[1] = w1;
-        }
+    } else {
+        const uint32_t a = *reinterpret_cast<const uint32_t*>(p + offA);
+        const uint32_t b = *reinterpret_cast<const uint32_t*>(p + offB);
+        w[0] = odd ? __funnelshift_r(a, b, 16) : a;
+        w[1] = odd ? (b >> 16) : b;
     }
 }
 
@@ -163,8 +173,9 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 
 // ---------------------------------------------------------------------------------
 // Prologue: activation fragments + per-group sums, one CTA per 512-k chunk.
-// Layout per chunk (M tokens): [group 8][half SPG/2][m][t 4][16 B], then the bias-step
-// fragments [sigma 2][m][t 4][8 B].
+// Layout per chunk, token-major with a per-token stride of XF_PER_M bytes:
+//   [m][group 8][half SPG/2][t 4][16 B]  then  [sigma 2][t 4][8 B] (bias-step operands).
+// A 64-byte tail per token shifts consecutive tokens by 16 banks.
 // ---------------------------------------------------------------------------------
 template <int BITS>
 __global__ void __launch_bounds__(256) qgemv_prep(const __nv_bfloat16* __restrict__ x, int M,
@@ -190,15 +201,13 @@ __global__ void __launch_bounds__(256) qgemv_prep(const __nv_bfloat16* __restric
         float xs = 0.f, xp = 0.f;
 #pragma unroll
         for (int j = 0; j < 16; ++j) xs += xv[j];
-        uint32_t* dst = reinterpret_cast<uint32_t*>(base);
+        uint32_t* dst = reinterpret_cast<uint32_t*>(base + m * F::XF_PER_M + gi * (F::SPG / 2) * 64 + t * 16);
 #pragma unroll
         for (int q = 0; q < F::NP; ++q) {
             const float lo = xv[pair_code<BITS>(q, 0)] * pair_mult<BITS>(q, 0);
             const float hi = xv[pair_code<BITS>(q, 1)] * pair_mult<BITS>(q, 1);
             xp += lo + hi;
-            const size_t off = ((static_cast<size_t>(gi) * (F::SPG / 2) + q / 4) * M + m) * 64 +
-                               t * 16 + (q % 4) * 4;
-            dst[off / 4] = pack_bf16x2(lo, hi);
+            dst[(q / 4) * 16 + (q % 4)] = pack_bf16x2(lo, hi);
         }
         xs += __shfl_xor_sync(0xffffffffu, xs, 1);
         xs += __shfl_xor_sync(0xffffffffu, xs, 2);
@@ -210,7 +219,6 @@ __global__ void __launch_bounds__(256) qgemv_prep(const __nv_bfloat16* __restric
         }
     }
     __syncthreads();
-    uint8_t* bias = base + static_cast<size_t>(GROUPS) * (F::SPG / 2) * M * 64;
     for (int i = threadIdx.x; i < 8 * M; i += blockDim.x) {
         const int t = i & 3, mm = i >> 2, m = mm % M, sigma = mm / M;
         uint32_t out[2];
@@ -223,8 +231,7 @@ __global__ void __launch_bounds__(256) qgemv_prep(const __nv_bfloat16* __restric
             const float f = (t & 1) ? 1.0f : -128.0f;
             out[h] = pack_bf16x2(vhi * f, vlo * f);
         }
-        uint32_t* d = reinterpret_cast<uint32_t*>(bias + (static_cast<size_t>(sigma) * M + m) * 32 +
-                                                  t * 8);
+        uint32_t* d = reinterpret_cast<uint32_t*>(base + m * F::XF_PER_M + F::XF_FRAG + sigma * 32 + t * 8);
         d[0] = out[0];
         d[1] = out[1];
     }
@@ -290,7 +297,7 @@ __device__ __forceinline__ void flush_subtile(const float (&acc)[NT][4], int til
 }
 
 template <int BITS, int NT>
-__global__ void __launch_bounds__(THREADS) qgemv_main(const __grid_constant__ CUtensorMap map_codes,
+__global__ void __launch_bounds__(THREADS, NT == 1 ? 3 : 2) qgemv_main(const __grid_constant__ CUtensorMap map_codes,
                                                       const __grid_constant__ CUtensorMap map_scales,
                                                       const __grid_constant__ CUtensorMap map_biases,
                                                       const MainArgs a) {
@@ -302,12 +309,14 @@ __global__ void __launch_bounds__(THREADS) qgemv_main(const __grid_constant__ CU
     uint64_t* empty = full + a.stages;
     uint8_t* stage0 = smem + 1024;
 
-    const long long total_sub = static_cast<long long>(a.tiles) * a.C * 4;
-    const long long s0 = total_sub * blockIdx.x / gridDim.x;
-    const long long s1 = total_sub * (blockIdx.x + 1) / gridDim.x;
+    // subunit range of this CTA (host guarantees tiles * C * 4 < 2^31)
+    const int total_sub = a.tiles * a.C * 4;
+    const int s0 = static_cast<int>(static_cast<long long>(total_sub) * blockIdx.x / gridDim.x);
+    const int s1 = static_cast<int>(static_cast<long long>(total_sub) * (blockIdx.x + 1) / gridDim.x);
     if (s1 <= s0) return;
-    const long long st_first = s0 / 4;
-    const int nst = static_cast<int>((s1 - 1) / 4 - st_first + 1);
+    const int st_first = s0 >> 2, st_last = (s1 - 1) >> 2;
+    const int nst = st_last - st_first + 1;
+    const int lo_first = s0 - 4 * st_first, hi_last = s1 - 4 * st_last;
     const int xf_bytes = a.M * F::XF_PER_M;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -327,15 +336,14 @@ __global__ void __launch_bounds__(THREADS) qgemv_main(const __grid_constant__ CU
             prefetch_tensormap(&map_scales);
             if (a.has_bias) prefetch_tensormap(&map_biases);
             bool waited = false;
-            int issued_xf = 0;  // stages whose activation fragments are issued
+            int issued_xf = 0, xf_chunk = st_first % a.C;  // fragments issued so far, their next chunk
+            int tile = st_first / a.C, chunk = st_first % a.C;
             for (int i = 0; i < nst; ++i) {
                 const int slot = i % a.stages;
                 const uint32_t ph = (i / a.stages) & 1;
                 if (i >= a.stages && !mbar_wait(&empty[slot], ph ^ 1, a.status)) return;
-                const long long st = st_first + i;
-                const int tile = static_cast<int>(st / a.C), chunk = static_cast<int>(st % a.C);
-                const int sub_lo = static_cast<int>(s0 - 4 * st > 0 ? s0 - 4 * st : 0);
-                const int sub_hi = static_cast<int>(s1 - 4 * st < 4 ? s1 - 4 * st : 4);
+                const int sub_lo = i == 0 ? lo_first : 0;
+                const int sub_hi = i == nst - 1 ? hi_last : 4;
                 uint8_t* sbase = stage0 + static_cast<size_t>(slot) * a.stage_bytes;
                 int nact = 0;
                 for (int s = sub_lo; s < sub_hi; ++s) nact += (tile * 64 + 16 * s < a.N);
@@ -359,12 +367,15 @@ __global__ void __launch_bounds__(THREADS) qgemv_main(const __grid_constant__ CU
                 }
                 if (waited) {
                     for (; issued_xf <= i; ++issued_xf) {
-                        const long long sti = st_first + issued_xf;
-                        const int ci = static_cast<int>(sti % a.C);
                         const int sl = issued_xf % a.stages;
                         uint8_t* dst = stage0 + static_cast<size_t>(sl) * a.stage_bytes + NCW * F::SUB_BYTES + 2048;
-                        bulk_load(dst, a.xfrag + static_cast<size_t>(ci) * xf_bytes, xf_bytes, &full[sl]);
+                        bulk_load(dst, a.xfrag + static_cast<size_t>(xf_chunk) * xf_bytes, xf_bytes, &full[sl]);
+                        if (++xf_chunk == a.C) xf_chunk = 0;
                     }
+                }
+                if (++chunk == a.C) {
+                    chunk = 0;
+                    ++tile;
                 }
             }
         }
@@ -373,20 +384,42 @@ __global__ void __launch_bounds__(THREADS) qgemv_main(const __grid_constant__ CU
 
     // -------------------------------------------------------------- consumers
     const int g = lane >> 2, t = lane & 3;
+    const bool odd = (t & 1) != 0;
+    // swizzled code offsets of (row g, group gi); row g+8 is 8*SW bytes further
+    uint32_t offA[GROUPS], offB[GROUPS];
+#pragma unroll
+    for (int gi = 0; gi < GROUPS; ++gi) {
+        int w0, w1;
+        window_words<BITS>(gi, t, w0, w1);
+        offA[gi] = code_off<F::SW>(g, w0);
+        offB[gi] = code_off<F::SW>(g, w1);
+    }
+    constexpr uint32_t ROW8 = 8 * F::SW;
+    // activation fragments: token m = nt*8 + g, quarter t
+    uint32_t xoff[NT];
+    bool xval[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const int m = nt * 8 + g;
+        xval[nt] = m < a.M;
+        xoff[nt] = (xval[nt] ? m : 0) * F::XF_PER_M + t * 16;
+    }
+    const int srow0 = warp * 16 + g;  // scale row of row g (row g+8 is 64 halfwords further)
+    const bool use_bias_operand = !odd || a.has_bias;
+    const int ga0 = t >> 1;           // bias step: group offset of operand pair 0
+
     float acc[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
     int cur_tile = -1, nchunks = 0;
-    const int srow0 = warp * 16 + g, srow1 = srow0 + 8;
+    int tile = st_first / a.C, chunk = st_first % a.C;
     for (int i = 0; i < nst; ++i) {
         const int slot = i % a.stages;
         const uint32_t ph = (i / a.stages) & 1;
-        const long long st = st_first + i;
-        const int tile = static_cast<int>(st / a.C);
-        const int sub_lo = static_cast<int>(s0 - 4 * st > 0 ? s0 - 4 * st : 0);
-        const int sub_hi = static_cast<int>(s1 - 4 * st < 4 ? s1 - 4 * st : 4);
+        const int sub_lo = i == 0 ? lo_first : 0;
+        const int sub_hi = i == nst - 1 ? hi_last : 4;
         if (tile != cur_tile) {
             if (nchunks > 0) flush_subtile<NT>(acc, cur_tile, warp, nchunks, a, lane);
 #pragma unroll
@@ -401,70 +434,78 @@ __global__ void __launch_bounds__(THREADS) qgemv_main(const __grid_constant__ CU
         if (active) {
             const uint8_t* sbase = stage0 + static_cast<size_t>(slot) * a.stage_bytes;
             const uint8_t* sub = sbase + warp * F::SUB_BYTES;
-            const uint16_t* scl = reinterpret_cast<const uint16_t*>(sbase + NCW * F::SUB_BYTES);
+            const uint16_t* scl = reinterpret_cast<const uint16_t*>(sbase + NCW * F::SUB_BYTES) + srow0 * GROUPS;
             const uint16_t* bia = scl + 512;
             const uint8_t* xf = sbase + NCW * F::SUB_BYTES + 2048;
-#pragma unroll 1
-            for (int gi = 0; gi < GROUPS; ++gi) {
-                uint32_t w0[4], w1[4], a0[F::NP], a1[F::NP];
-                load_window<BITS>(sub, g, gi, t, w0);
-                load_window<BITS>(sub, g + 8, gi, t, w1);
-                uint32_t xb[NT][F::NP];
+            // two groups per iteration: independent MMA chains interleaved step by step
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    const int m = nt * 8 + g;
+            for (int gp = 0; gp < GROUPS; gp += 2) {
+                uint32_t w[2][2][4], ar[2][2][F::NP], xb[2][NT][F::NP];
 #pragma unroll
-                    for (int h = 0; h < F::SPG / 2; ++h) {
-                        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                        if (m < a.M)
-                            v = *reinterpret_cast<const uint4*>(
-                                xf + ((static_cast<size_t>(gi) * (F::SPG / 2) + h) * a.M + m) * 64 + t * 16);
-                        xb[nt][4 * h + 0] = v.x;
-                        xb[nt][4 * h + 1] = v.y;
-                        xb[nt][4 * h + 2] = v.z;
-                        xb[nt][4 * h + 3] = v.w;
-                    }
+                for (int u = 0; u < 2; ++u) {
+                    const int gi = gp + u;
+                    load_window<BITS>(sub, offA[gi], offB[gi], odd, w[u][0]);
+                    load_window<BITS>(sub + ROW8, offA[gi], offB[gi], odd, w[u][1]);
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int h = 0; h < F::SPG / 2; ++h) {
+                            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                            if (xval[nt])
+                                v = *reinterpret_cast<const uint4*>(xf + xoff[nt] + (gi * (F::SPG / 2) + h) * 64);
+                            xb[u][nt][4 * h + 0] = v.x;
+                            xb[u][nt][4 * h + 1] = v.y;
+                            xb[u][nt][4 * h + 2] = v.z;
+                            xb[u][nt][4 * h + 3] = v.w;
+                        }
                 }
-                extract<BITS>(w0, a0);
-                extract<BITS>(w1, a1);
-                float d[NT][4];
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
+                for (int u = 0; u < 2; ++u) {
+                    extract<BITS>(w[u][0], ar[u][0]);
+                    extract<BITS>(w[u][1], ar[u][1]);
+                }
+                float d[2][NT][4];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) d[nt][e] = 0.f;
+                for (int u = 0; u < 2; ++u)
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) d[u][nt][e] = 0.f;
 #pragma unroll
                 for (int j = 0; j < F::SPG; ++j)
 #pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
-                        mma_bf16_16816(d[nt], a0[2 * j], a1[2 * j], a0[2 * j + 1], a1[2 * j + 1],
-                                       xb[nt][2 * j], xb[nt][2 * j + 1], d[nt]);
-                const float sc0 = bf16_bits_to_f32(scl[srow0 * GROUPS + gi]);
-                const float sc1 = bf16_bits_to_f32(scl[srow1 * GROUPS + gi]);
+                    for (int u = 0; u < 2; ++u)
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    acc[nt][0] = fmaf(sc0, d[nt][0], acc[nt][0]);
-                    acc[nt][1] = fmaf(sc0, d[nt][1], acc[nt][1]);
-                    acc[nt][2] = fmaf(sc1, d[nt][2], acc[nt][2]);
-                    acc[nt][3] = fmaf(sc1, d[nt][3], acc[nt][3]);
+                        for (int nt = 0; nt < NT; ++nt)
+                            mma_bf16_16816(d[u][nt], ar[u][0][2 * j], ar[u][1][2 * j], ar[u][0][2 * j + 1],
+                                           ar[u][1][2 * j + 1], xb[u][nt][2 * j], xb[u][nt][2 * j + 1], d[u][nt]);
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const float sc0 = bf16_bits_to_f32(scl[gp + u]);
+                    const float sc1 = bf16_bits_to_f32(scl[64 + gp + u]);
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        acc[nt][0] = fmaf(sc0, d[u][nt][0], acc[nt][0]);
+                        acc[nt][1] = fmaf(sc0, d[u][nt][1], acc[nt][1]);
+                        acc[nt][2] = fmaf(sc1, d[u][nt][2], acc[nt][2]);
+                        acc[nt][3] = fmaf(sc1, d[u][nt][3], acc[nt][3]);
+                    }
                 }
             }
             // bias and offset terms of the chunk's 8 groups: two MMA steps
-            const uint8_t* bf = xf + static_cast<size_t>(GROUPS) * (F::SPG / 2) * a.M * 64;
+            const uint16_t* src = odd ? bia : scl;
 #pragma unroll
             for (int sigma = 0; sigma < 2; ++sigma) {
-                const int ga = 4 * sigma + (t >> 1), gb = ga + 2;
-                const uint16_t* src = (t & 1) ? bia : scl;
-                const bool use = !(t & 1) || a.has_bias;
-                const uint32_t v0a = use ? src[srow0 * GROUPS + ga] * 0x00010001u : 0u;
-                const uint32_t v1a = use ? src[srow1 * GROUPS + ga] * 0x00010001u : 0u;
-                const uint32_t v0b = use ? src[srow0 * GROUPS + gb] * 0x00010001u : 0u;
-                const uint32_t v1b = use ? src[srow1 * GROUPS + gb] * 0x00010001u : 0u;
+                const int ga = 4 * sigma + ga0, gb = ga + 2;
+                const uint32_t v0a = use_bias_operand ? src[ga] * 0x00010001u : 0u;
+                const uint32_t v1a = use_bias_operand ? src[64 + ga] * 0x00010001u : 0u;
+                const uint32_t v0b = use_bias_operand ? src[gb] * 0x00010001u : 0u;
+                const uint32_t v1b = use_bias_operand ? src[64 + gb] * 0x00010001u : 0u;
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
-                    const int m = nt * 8 + g;
                     uint2 bb = make_uint2(0u, 0u);
-                    if (m < a.M)
-                        bb = *reinterpret_cast<const uint2*>(bf + (static_cast<size_t>(sigma) * a.M + m) * 32 + t * 8);
+                    if (xval[nt])
+                        bb = *reinterpret_cast<const uint2*>(xf + xoff[nt] - t * 16 + F::XF_FRAG + sigma * 32 + t * 8);
                     mma_bf16_16816(acc[nt], v0a, v1a, v0b, v1b, bb.x, bb.y, acc[nt]);
                 }
             }
@@ -472,91 +513,152 @@ __global__ void __launch_bounds__(THREADS) qgemv_main(const __grid_constant__ CU
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
+        if (++chunk == a.C) {
+            chunk = 0;
+            ++tile;
+        }
     }
     if (nchunks > 0) flush_subtile<NT>(acc, cur_tile, warp, nchunks, a, lane);
 }
 
-template <int BITS, int NT>
-q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, const void* s,
-                  const void* b, int N, void* y) {
+// Launch geometry shared by the context path and the allocation-free path.
+struct Plan {
+    int C, tiles, stage_bytes, stages, smem;
+    size_t xf_bytes;
+};
+
+template <int BITS>
+bool make_plan(int M, int K, int N, Plan& p) {
     using F = Fmt<BITS>;
-    const int C = K / KC;
-    const int tiles = (N + 63) / 64;
-    const size_t xf_bytes = static_cast<size_t>(M) * F::XF_PER_M;
-    q38_status st = ensure_workspace(ctx, C * xf_bytes);
-    if (st != Q38_OK) return st;
-    uint32_t* cnt = nullptr;
-    float* part = nullptr;
-    st = ensure_zero_region(ctx, static_cast<size_t>((N + 15) / 16), static_cast<size_t>(M) * N, &cnt, &part);
-    if (st != Q38_OK) return st;
-    uint8_t* wsb = static_cast<uint8_t*>(ctx->workspace);
-
-    CUtensorMap mc, ms, mb;
-    const uint64_t kw = static_cast<uint64_t>(K) * BITS / 32;
-    if (!make_map_2d(&mc, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w, kw, N, F::SW / 4, 16,
-                     F::SW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B) ||
-        !make_map_2d(&ms, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s, K / 64, N, GROUPS, 64,
-                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b ? b : s, K / 64, N, GROUPS, 64,
-                     CU_TENSOR_MAP_SWIZZLE_NONE))
-        return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: tensor map encoding failed");
-
-    const int stage_bytes = static_cast<int>(align_up(NCW * F::SUB_BYTES + 2048 + xf_bytes, 1024));
-    int stages = (100 * 1024) / stage_bytes;
-    if (stages > 8) stages = 8;
+    p.C = K / KC;
+    p.tiles = (N + 63) / 64;
+    if (static_cast<long long>(p.tiles) * p.C * 4 >= (1LL << 31)) return false;
+    p.xf_bytes = static_cast<size_t>(M) * F::XF_PER_M;
+    p.stage_bytes = static_cast<int>(align_up(NCW * F::SUB_BYTES + 2048 + p.xf_bytes, 1024));
+    // about 72 KiB of ring per CTA lets three CTAs (12 consumer warps) share an SM
+    int stages = (72 * 1024) / p.stage_bytes;
+    if (stages > 6) stages = 6;
     if (stages < 2) stages = 2;
-    int smem = 2048 + stages * stage_bytes;
+    int smem = 2048 + stages * p.stage_bytes;
     while (smem > 227 * 1024 && stages > 2) {
         --stages;
-        smem = 2048 + stages * stage_bytes;
+        smem = 2048 + stages * p.stage_bytes;
     }
-    if (smem > 227 * 1024) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: stage too large");
+    p.stages = stages;
+    p.smem = smem;
+    return smem <= 227 * 1024;
+}
 
+// Encodes the three tensor maps of a weight (codes, scales, biases).
+template <int BITS>
+bool make_maps(const uint32_t* w, const void* s, const void* b, int K, int N, CUtensorMap* mc,
+               CUtensorMap* ms, CUtensorMap* mb) {
+    using F = Fmt<BITS>;
+    const uint64_t kw = static_cast<uint64_t>(K) * BITS / 32;
+    return make_map_2d(mc, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w, kw, N, F::SW / 4, 16,
+                       F::SW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B) &&
+           make_map_2d(ms, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s, K / 64, N, GROUPS, 64,
+                       CU_TENSOR_MAP_SWIZZLE_NONE) &&
+           make_map_2d(mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b ? b : s, K / 64, N, GROUPS, 64,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+// Launches prologue + main kernel with the given scratch.  Returns a CUDA error code.
+template <int BITS, int NT>
+cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x, int M, int K,
+                           const CUtensorMap& mc, const CUtensorMap& ms, const CUtensorMap& mb,
+                           bool has_bias, int N, void* y, uint8_t* xfrag, float* part, uint32_t* cnt,
+                           uint32_t* status, cudaStream_t stream) {
     auto kmain = qgemv_main<BITS, NT>;
-    static bool configured[64] = {};  // per template instance and device
-    if (ctx->device < 64 && !configured[ctx->device]) {
-        if (cudaFuncSetAttribute(kmain, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
-            return check_launch(ctx, "cudaFuncSetAttribute");
-        configured[ctx->device] = true;
-    }
+    // per template instance and device: smem opt-in and occupancy at the largest ring
+    static std::mutex mu;
+    static bool configured[64] = {};
+    static int occ_smem[64][16] = {}, occ_val[64][16] = {};
+    if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
     int occ = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kmain, THREADS, smem);
-    if (occ < 1) occ = 1;
-    const long long total_sub = static_cast<long long>(tiles) * C * 4;
-    long long grid = static_cast<long long>(ctx->num_sms) * occ;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!configured[device]) {
+            cudaError_t e = cudaFuncSetAttribute(kmain, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+            if (e != cudaSuccess) return e;
+            configured[device] = true;
+        }
+        int slot = -1;
+        for (int i = 0; i < 16; ++i) {
+            if (occ_smem[device][i] == p.smem) {
+                occ = occ_val[device][i];
+                break;
+            }
+            if (occ_smem[device][i] == 0 && slot < 0) slot = i;
+        }
+        if (occ == 0) {
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kmain, THREADS, p.smem);
+            if (occ < 1) occ = 1;
+            if (slot >= 0) {
+                occ_smem[device][slot] = p.smem;
+                occ_val[device][slot] = occ;
+            }
+        }
+    }
+    const long long total_sub = static_cast<long long>(p.tiles) * p.C * 4;
+    long long grid = static_cast<long long>(num_sms) * occ;
     if (grid > total_sub) grid = total_sub;
 
-    qgemv_prep<BITS><<<C, 256, 0, ctx->stream>>>(static_cast<const __nv_bfloat16*>(x), M, K, wsb);
-    st = check_launch(ctx, "qgemv_prep");
-    if (st != Q38_OK) return st;
+    qgemv_prep<BITS><<<p.C, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), M, K, xfrag);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
 
     MainArgs args;
-    args.xfrag = wsb;
+    args.xfrag = xfrag;
     args.y = static_cast<__nv_bfloat16*>(y);
     args.ws = part;
     args.cnt = cnt;
-    args.status = ctx->d_status;
+    args.status = status;
     args.M = M;
     args.N = N;
-    args.C = C;
-    args.tiles = tiles;
-    args.stages = stages;
-    args.stage_bytes = stage_bytes;
-    args.has_bias = b != nullptr;
+    args.C = p.C;
+    args.tiles = p.tiles;
+    args.stages = p.stages;
+    args.stage_bytes = p.stage_bytes;
+    args.has_bias = has_bias;
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(grid));
     cfg.blockDim = dim3(THREADS);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = ctx->stream;
+    cfg.dynamicSmemBytes = p.smem;
+    cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, kmain, mc, ms, mb, args) != cudaSuccess)
-        return check_launch(ctx, "qgemv_main");
-    return check_launch(ctx, "qgemv_main");
+    e = cudaLaunchKernelEx(&cfg, kmain, mc, ms, mb, args);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+template <int BITS, int NT>
+q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, const void* s,
+                  const void* b, int N, void* y) {
+    Plan p;
+    if (!make_plan<BITS>(M, K, N, p)) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: shape too large");
+    q38_status st = ensure_workspace(ctx, p.C * p.xf_bytes);
+    if (st != Q38_OK) return st;
+    uint32_t* cnt = nullptr;
+    float* part = nullptr;
+    st = ensure_zero_region(ctx, static_cast<size_t>((N + 15) / 16), static_cast<size_t>(M) * N, &cnt, &part);
+    if (st != Q38_OK) return st;
+    CUtensorMap mc, ms, mb;
+    if (!make_maps<BITS>(w, s, b, K, N, &mc, &ms, &mb))
+        return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: tensor map encoding failed");
+    const cudaError_t e = launch_kernels<BITS, NT>(p, ctx->device, ctx->num_sms, x, M, K, mc, ms, mb, b != nullptr, N,
+                                                   y, static_cast<uint8_t*>(ctx->workspace), part, cnt,
+                                                   ctx->d_status, ctx->stream);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: launch failed: %s", cudaGetErrorString(e));
+    }
+    return Q38_OK;
 }
 
 }  // namespace
@@ -633,12 +735,11 @@ q38_status noalloc_scratch(int device, uint8_t** out) {
 }
 
 template <int BITS, int NT>
-q38_status launch_noalloc(uint8_t* scratch, int num_sms, const void* x, int M, int K, const uint32_t* w,
-                          const void* s, const void* b, int N, void* y, cudaStream_t stream) {
-    using F = Fmt<BITS>;
-    const int C = K / KC;
-    const int tiles = (N + 63) / 64;
-    const size_t xf_bytes = static_cast<size_t>(M) * F::XF_PER_M;
+q38_status launch_noalloc(uint8_t* scratch, int device, int num_sms, const void* x, int M, int K,
+                          const uint32_t* w, const void* s, const void* b, int N, void* y,
+                          cudaStream_t stream) {
+    Plan p;
+    if (!make_plan<BITS>(M, K, N, p)) return Q38_ERR_UNSUPPORTED;
     uint32_t* status = reinterpret_cast<uint32_t*>(scratch + NA_STATUS_OFF);
     uint32_t* cnt = reinterpret_cast<uint32_t*>(scratch + NA_CNT_OFF);
     float* part = reinterpret_cast<float*>(scratch + NA_ACC_OFF);
@@ -650,58 +751,15 @@ q38_status launch_noalloc(uint8_t* scratch, int num_sms, const void* x, int M, i
         cudaGetLastError();
         return Q38_ERR_CUDA;
     }
-
     CUtensorMap mc, ms, mb;
-    const uint64_t kw = static_cast<uint64_t>(K) * BITS / 32;
-    if (!make_map_2d(&mc, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w, kw, N, F::SW / 4, 16,
-                     F::SW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B) ||
-        !make_map_2d(&ms, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s, K / 64, N, GROUPS, 64,
-                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b ? b : s, K / 64, N, GROUPS, 64,
-                     CU_TENSOR_MAP_SWIZZLE_NONE))
-        return Q38_ERR_CUDA;
-
-    const int stage_bytes = static_cast<int>(align_up(NCW * F::SUB_BYTES + 2048 + xf_bytes, 1024));
-    int stages = (100 * 1024) / stage_bytes;
-    if (stages > 8) stages = 8;
-    if (stages < 2) stages = 2;
-    int smem = 2048 + stages * stage_bytes;
-    while (smem > 227 * 1024 && stages > 2) {
-        --stages;
-        smem = 2048 + stages * stage_bytes;
-    }
-    if (smem > 227 * 1024) return Q38_ERR_UNSUPPORTED;
-
-    auto kmain = qgemv_main<BITS, NT>;
-    if (cudaFuncSetAttribute(kmain, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess) {
+    if (!make_maps<BITS>(w, s, b, K, N, &mc, &ms, &mb)) return Q38_ERR_CUDA;
+    const cudaError_t e = launch_kernels<BITS, NT>(p, device, num_sms, x, M, K, mc, ms, mb, b != nullptr, N, y,
+                                                   xfrag, part, cnt, status, stream);
+    if (e != cudaSuccess) {
         cudaGetLastError();
         return Q38_ERR_CUDA;
     }
-    int occ = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kmain, THREADS, smem);
-    if (occ < 1) occ = 1;
-    const long long total_sub = static_cast<long long>(tiles) * C * 4;
-    long long grid = static_cast<long long>(num_sms) * occ;
-    if (grid > total_sub) grid = total_sub;
-
-    qgemv_prep<BITS><<<C, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), M, K, xfrag);
-    if (cudaGetLastError() != cudaSuccess) return Q38_ERR_CUDA;
-
-    MainArgs args;
-    args.xfrag = xfrag;
-    args.y = static_cast<__nv_bfloat16*>(y);
-    args.ws = part;
-    args.cnt = cnt;
-    args.status = status;
-    args.M = M;
-    args.N = N;
-    args.C = C;
-    args.tiles = tiles;
-    args.stages = stages;
-    args.stage_bytes = stage_bytes;
-    args.has_bias = b != nullptr;
-    kmain<<<static_cast<unsigned>(grid), THREADS, smem, stream>>>(mc, ms, mb, args);
-    return cudaGetLastError() == cudaSuccess ? Q38_OK : Q38_ERR_CUDA;
+    return Q38_OK;
 }
 
 }  // namespace
@@ -731,13 +789,13 @@ extern "C" Q38_API q38_status q38_quantized_matmul_noalloc(const void* x, int64_
     const int m = static_cast<int>(M), k = static_cast<int>(K), n = static_cast<int>(N);
     const bool two = M > 8;
     switch (bits) {
-        case 2: return two ? launch_noalloc<2, 2>(scratch, sms, x, m, k, w, scales, biases, n, y, s)
-                           : launch_noalloc<2, 1>(scratch, sms, x, m, k, w, scales, biases, n, y, s);
-        case 3: return two ? launch_noalloc<3, 2>(scratch, sms, x, m, k, w, scales, biases, n, y, s)
-                           : launch_noalloc<3, 1>(scratch, sms, x, m, k, w, scales, biases, n, y, s);
-        case 4: return two ? launch_noalloc<4, 2>(scratch, sms, x, m, k, w, scales, biases, n, y, s)
-                           : launch_noalloc<4, 1>(scratch, sms, x, m, k, w, scales, biases, n, y, s);
-        default: return two ? launch_noalloc<8, 2>(scratch, sms, x, m, k, w, scales, biases, n, y, s)
-                            : launch_noalloc<8, 1>(scratch, sms, x, m, k, w, scales, biases, n, y, s);
+        case 2: return two ? launch_noalloc<2, 2>(scratch, device, sms, x, m, k, w, scales, biases, n, y, s)
+                           : launch_noalloc<2, 1>(scratch, device, sms, x, m, k, w, scales, biases, n, y, s);
+        case 3: return two ? launch_noalloc<3, 2>(scratch, device, sms, x, m, k, w, scales, biases, n, y, s)
+                           : launch_noalloc<3, 1>(scratch, device, sms, x, m, k, w, scales, biases, n, y, s);
+        case 4: return two ? launch_noalloc<4, 2>(scratch, device, sms, x, m, k, w, scales, biases, n, y, s)
+                           : launch_noalloc<4, 1>(scratch, device, sms, x, m, k, w, scales, biases, n, y, s);
+        default: return two ? launch_noalloc<8, 2>(scratch, device, sms, x, m, k, w, scales, biases, n, y, s)
+                            : launch_noalloc<8, 1>(scratch, device, sms, x, m, k, w, scales, biases, n, y, s);
     }
 }
