@@ -23,9 +23,9 @@
 //  * Consumers do no address arithmetic in the inner loop: swizzled code offsets are
 //    precomputed per thread, fragments are token-major so their offsets are constants,
 //    and the 8 groups of a stage are unrolled so their MMA chains overlap.
-//  * Subtiles split across CTAs accumulate through fp32 atomics into a workspace; the
-//    warp that completes a subtile (per-subtile chunk counter) writes y and returns the
-//    workspace and counter to zero, so no per-call clearing is needed.
+//  * Every warp adds its subtile partial sums into an fp32 workspace with fire-and-forget
+//    reductions (no fences or counters in the main kernel); a small epilogue kernel
+//    converts the sums to y and zeroes them again, so no per-call clearing is needed.
 //  * The main kernel is launched with programmatic dependent launch: its producer
 //    streams the first stages of weights while the prologue kernel is still running.
 #include <mutex>
@@ -181,7 +181,11 @@ template <int BITS>
 __global__ void __launch_bounds__(256) qgemv_prep(const __nv_bfloat16* __restrict__ x, int M,
                                                   int K, uint8_t* __restrict__ xfrag) {
     using F = Fmt<BITS>;
+    // Let the main kernel start streaming weights now; x is produced by the previous
+    // kernel on the stream, and the fragment buffer is read by the previous product:
+    // both are touched only after that kernel has completed.
     griddep_launch_dependents();
+    griddep_wait();
     __shared__ float s_xs[GROUPS][16], s_xp[GROUPS][16];
     const int c = blockIdx.x;
     uint8_t* base = xfrag + static_cast<size_t>(c) * M * F::XF_PER_M;
@@ -244,27 +248,18 @@ struct MainArgs {
     const uint8_t* xfrag;
     __nv_bfloat16* y;
     float* ws;
-    uint32_t* cnt;
     uint32_t* status;
     int M, N, C, tiles, stages, stage_bytes, has_bias;
 };
 
+// Adds a warp's partial sums of one 16-row subtile into the fp32 workspace.  The
+// reductions are fire-and-forget (no fence, no counter): the epilogue kernel, which
+// runs after this grid has completed, converts the sums to y and zeroes them again.
 template <int NT>
 __device__ __forceinline__ void flush_subtile(const float (&acc)[NT][4], int tile, int warp,
-                                              int nchunks, const MainArgs& a, int lane) {
+                                              const MainArgs& a, int lane) {
     const int g = lane >> 2, t = lane & 3;
     const int r0 = tile * 64 + warp * 16 + g;
-    const int sub = tile * 4 + warp;
-    if (nchunks == a.C) {
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int r = r0 + ((e >> 1) << 3), m = nt * 8 + 2 * t + (e & 1);
-                if (r < a.N && m < a.M) a.y[static_cast<size_t>(m) * a.N + r] = __float2bfloat16_rn(acc[nt][e]);
-            }
-        return;
-    }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -272,28 +267,17 @@ __device__ __forceinline__ void flush_subtile(const float (&acc)[NT][4], int til
             const int r = r0 + ((e >> 1) << 3), m = nt * 8 + 2 * t + (e & 1);
             if (r < a.N && m < a.M) atomicAdd(a.ws + static_cast<size_t>(m) * a.N + r, acc[nt][e]);
         }
-    __threadfence();
-    __syncwarp();
-    uint32_t last = 0;
-    if (lane == 0) {
-        const uint32_t old = atomicAdd(a.cnt + sub, static_cast<uint32_t>(nchunks));
-        last = (old + nchunks == static_cast<uint32_t>(a.C));
+}
+
+// y = bf16(partial sums); the sums are returned to zero for the next product.
+__global__ void __launch_bounds__(256) qgemv_epilogue(float* __restrict__ ws, __nv_bfloat16* __restrict__ y,
+                                                      int total) {
+    griddep_launch_dependents();
+    griddep_wait();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        y[i] = __float2bfloat16_rn(__ldcg(ws + i));
+        __stcg(ws + i, 0.0f);
     }
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) return;
-    __threadfence();
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int r = r0 + ((e >> 1) << 3), m = nt * 8 + 2 * t + (e & 1);
-            if (r < a.N && m < a.M) {
-                float* p = a.ws + static_cast<size_t>(m) * a.N + r;
-                a.y[static_cast<size_t>(m) * a.N + r] = __float2bfloat16_rn(__ldcg(p));
-                __stcg(p, 0.0f);
-            }
-        }
-    if (lane == 0) a.cnt[sub] = 0;
 }
 
 template <int BITS, int NT>
@@ -328,6 +312,9 @@ __global__ void __launch_bounds__(THREADS, NT == 1 ? 3 : 2) qgemv_main(const __g
         fence_mbar_init();
     }
     __syncthreads();
+    // The next product's prologue may start now: it waits for this grid before writing
+    // anything this grid reads.
+    griddep_launch_dependents();
 
     if (warp == NCW) {
         // ------------------------------------------------------------ producer
@@ -383,6 +370,9 @@ __global__ void __launch_bounds__(THREADS, NT == 1 ? 3 : 2) qgemv_main(const __g
     }
 
     // -------------------------------------------------------------- consumers
+    // Partial sums, counters and y may still be in use by the previous product on the
+    // stream until the prologue kernel (which waits for it) has completed.
+    griddep_wait();
     const int g = lane >> 2, t = lane & 3;
     const bool odd = (t & 1) != 0;
     // swizzled code offsets of (row g, group gi); row g+8 is 8*SW bytes further
@@ -421,7 +411,7 @@ __global__ void __launch_bounds__(THREADS, NT == 1 ? 3 : 2) qgemv_main(const __g
         const int sub_lo = i == 0 ? lo_first : 0;
         const int sub_hi = i == nst - 1 ? hi_last : 4;
         if (tile != cur_tile) {
-            if (nchunks > 0) flush_subtile<NT>(acc, cur_tile, warp, nchunks, a, lane);
+            if (nchunks > 0) flush_subtile<NT>(acc, cur_tile, warp, a, lane);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -518,7 +508,7 @@ __global__ void __launch_bounds__(THREADS, NT == 1 ? 3 : 2) qgemv_main(const __g
             ++tile;
         }
     }
-    if (nchunks > 0) flush_subtile<NT>(acc, cur_tile, warp, nchunks, a, lane);
+    if (nchunks > 0) flush_subtile<NT>(acc, cur_tile, warp, a, lane);
 }
 
 // Launch geometry shared by the context path and the allocation-free path.
@@ -567,7 +557,7 @@ bool make_maps(const uint32_t* w, const void* s, const void* b, int K, int N, CU
 template <int BITS, int NT>
 cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x, int M, int K,
                            const CUtensorMap& mc, const CUtensorMap& ms, const CUtensorMap& mb,
-                           bool has_bias, int N, void* y, uint8_t* xfrag, float* part, uint32_t* cnt,
+                           bool has_bias, int N, void* y, uint8_t* xfrag, float* part,
                            uint32_t* status, cudaStream_t stream) {
     auto kmain = qgemv_main<BITS, NT>;
     // per template instance and device: smem opt-in and occupancy at the largest ring
@@ -604,15 +594,22 @@ cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x
     long long grid = static_cast<long long>(num_sms) * occ;
     if (grid > total_sub) grid = total_sub;
 
-    qgemv_prep<BITS><<<p.C, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), M, K, xfrag);
-    cudaError_t e = cudaGetLastError();
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t pcfg = {};
+    pcfg.gridDim = dim3(static_cast<unsigned>(p.C));
+    pcfg.blockDim = dim3(256);
+    pcfg.stream = stream;
+    pcfg.attrs = attr;
+    pcfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&pcfg, qgemv_prep<BITS>, static_cast<const __nv_bfloat16*>(x), M, K, xfrag);
     if (e != cudaSuccess) return e;
 
     MainArgs args;
     args.xfrag = xfrag;
     args.y = static_cast<__nv_bfloat16*>(y);
     args.ws = part;
-    args.cnt = cnt;
     args.status = status;
     args.M = M;
     args.N = N;
@@ -627,12 +624,21 @@ cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x
     cfg.blockDim = dim3(THREADS);
     cfg.dynamicSmemBytes = p.smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&cfg, kmain, mc, ms, mb, args);
+    if (e != cudaSuccess) return e;
+
+    const int total = M * N;
+    int eblocks = (total + 255) / 256;
+    if (eblocks > num_sms * 4) eblocks = num_sms * 4;
+    cudaLaunchConfig_t ecfg = {};
+    ecfg.gridDim = dim3(static_cast<unsigned>(eblocks));
+    ecfg.blockDim = dim3(256);
+    ecfg.stream = stream;
+    ecfg.attrs = attr;
+    ecfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&ecfg, qgemv_epilogue, part, static_cast<__nv_bfloat16*>(y), total);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
@@ -644,15 +650,15 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
     if (!make_plan<BITS>(M, K, N, p)) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: shape too large");
     q38_status st = ensure_workspace(ctx, p.C * p.xf_bytes);
     if (st != Q38_OK) return st;
-    uint32_t* cnt = nullptr;
+    uint32_t* cnt = nullptr;  // (no counters are used)
     float* part = nullptr;
-    st = ensure_zero_region(ctx, static_cast<size_t>((N + 15) / 16), static_cast<size_t>(M) * N, &cnt, &part);
+    st = ensure_zero_region(ctx, 0, static_cast<size_t>(M) * N, &cnt, &part);
     if (st != Q38_OK) return st;
     CUtensorMap mc, ms, mb;
     if (!make_maps<BITS>(w, s, b, K, N, &mc, &ms, &mb))
         return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: tensor map encoding failed");
     const cudaError_t e = launch_kernels<BITS, NT>(p, ctx->device, ctx->num_sms, x, M, K, mc, ms, mb, b != nullptr, N,
-                                                   y, static_cast<uint8_t*>(ctx->workspace), part, cnt,
+                                                   y, static_cast<uint8_t*>(ctx->workspace), part,
                                                    ctx->d_status, ctx->stream);
     if (e != cudaSuccess) {
         cudaGetLastError();
@@ -701,17 +707,15 @@ q38_status qgemv_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const u
 namespace {
 
 constexpr int64_t NA_MAX_M = 16, NA_MAX_N = 32768, NA_MAX_K = 32768;
-constexpr size_t NA_CNT_BYTES = static_cast<size_t>(NA_MAX_N / 16) * 4;                 // 8 KiB
 constexpr size_t NA_ACC_BYTES = static_cast<size_t>(NA_MAX_M) * NA_MAX_N * 4;          // 2 MiB
 constexpr size_t NA_XF_BYTES = static_cast<size_t>(NA_MAX_K / KC) * NA_MAX_M * (256 * 8 + 64);  // 2.06 MiB
 constexpr size_t NA_STATUS_OFF = 0;
-constexpr size_t NA_CNT_OFF = 256;
-constexpr size_t NA_ACC_OFF = NA_CNT_OFF + NA_CNT_BYTES;
+constexpr size_t NA_ACC_OFF = 256;
 constexpr size_t NA_XF_OFF = NA_ACC_OFF + NA_ACC_BYTES;
 constexpr size_t NA_TOTAL = NA_XF_OFF + NA_XF_BYTES;
 
-// The scratch of every no-alloc call on a device (status word, subtile counters, fp32
-// partial sums, activation fragments).  In host code this name is only a stand-in for
+// The scratch of every no-alloc call on a device (status word, fp32 partial sums,
+// activation fragments).  In host code this name is only a stand-in for
 // the device array; its device address comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[NA_TOTAL];
 
@@ -741,20 +745,18 @@ q38_status launch_noalloc(uint8_t* scratch, int device, int num_sms, const void*
     Plan p;
     if (!make_plan<BITS>(M, K, N, p)) return Q38_ERR_UNSUPPORTED;
     uint32_t* status = reinterpret_cast<uint32_t*>(scratch + NA_STATUS_OFF);
-    uint32_t* cnt = reinterpret_cast<uint32_t*>(scratch + NA_CNT_OFF);
     float* part = reinterpret_cast<float*>(scratch + NA_ACC_OFF);
     uint8_t* xfrag = scratch + NA_XF_OFF;
-    // counters and partial sums must start at zero; a previous call leaves them zero,
-    // but clear them anyway so an interrupted call cannot poison the next one
-    if (cudaMemsetAsync(cnt, 0, static_cast<size_t>((N + 15) / 16) * 4, stream) != cudaSuccess ||
-        cudaMemsetAsync(part, 0, static_cast<size_t>(M) * N * 4, stream) != cudaSuccess) {
+    // the partial sums must start at zero; a previous call leaves them zero, but clear
+    // them anyway so an interrupted call cannot poison the next one
+    if (cudaMemsetAsync(part, 0, static_cast<size_t>(M) * N * 4, stream) != cudaSuccess) {
         cudaGetLastError();
         return Q38_ERR_CUDA;
     }
     CUtensorMap mc, ms, mb;
     if (!make_maps<BITS>(w, s, b, K, N, &mc, &ms, &mb)) return Q38_ERR_CUDA;
     const cudaError_t e = launch_kernels<BITS, NT>(p, device, num_sms, x, M, K, mc, ms, mb, b != nullptr, N, y,
-                                                   xfrag, part, cnt, status, stream);
+                                                   xfrag, part, status, stream);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return Q38_ERR_CUDA;
