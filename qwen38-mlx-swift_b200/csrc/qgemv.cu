@@ -30,7 +30,7 @@
 //    streams the first stages of weights while the prologue kernel is still running.
 #include <mutex>
 
-#include "ptx.cuh"
+#include "affine_codes.cuh"
 
 namespace q38 {
 namespace {
@@ -41,7 +41,6 @@ constexpr int KC = 512;        // k per chunk
 constexpr int GROUPS = 8;      // groups of 64 per chunk
 constexpr int NCW = 4;         // consumer warps (one 16-row subtile each)
 constexpr int THREADS = (NCW + 1) * 32;
-constexpr uint32_t MAGIC = 0x43004300u;  // bf16 128.0 in both halves
 
 template <int BITS>
 struct Fmt {
@@ -55,69 +54,6 @@ struct Fmt {
     static constexpr int XF_FRAG = 256 * SPG;          // fragment bytes per token per chunk
     static constexpr int XF_PER_M = XF_FRAG + 64;      // + bias-step fragments
 };
-
-// ---------------------------------------------------------------------------------
-// Pair tables: for bf16x2 operand q of a thread's 16 codes (per row and group), the
-// code index feeding its low and high half and the power-of-two weight the code has
-// inside that half (the activation is pre-multiplied by the inverse).
-// ---------------------------------------------------------------------------------
-template <int BITS>
-__host__ __device__ constexpr int pair_code(int q, int hi) {
-    if (BITS == 2) return q + (hi ? 8 : 0);
-    if (BITS == 3) return q < 4 ? q + (hi ? 4 : 0) : q + 4 + (hi ? 4 : 0);
-    if (BITS == 4) return (q / 4) * 8 + (q % 4) + (hi ? 4 : 0);
-    /* 8 */ return (q / 4) * 4 + ((q % 4) >> 1) + (hi ? 2 : 0);
-}
-
-// Multiplier applied to the activation for the slot (1 / weight of the code's bits).
-template <int BITS>
-__host__ __device__ constexpr float pair_mult(int q, int hi) {
-    if (BITS == 2) {
-        const int pos = (q % 3 == 0) ? 0 : (q % 3 == 1) ? 2 : 4;  // q: 0,1,2,3,4,5,6,7
-        return pos == 0 ? 1.0f : pos == 2 ? 0.25f : 0.0625f;
-    }
-    if (BITS == 3) return hi ? 1.0f : 0.0625f;
-    if (BITS == 4) return 1.0f;
-    /* 8: odd q = high nibble, weight 16 */ return (q & 1) ? 16.0f : 1.0f;
-}
-
-// Extract the NP bf16x2 operands of one thread-row-group from its code window.
-// w[] holds the window: bits 2 -> 1 word, 3 -> 2 words (48 valid bits), 4 -> 2, 8 -> 4.
-template <int BITS>
-__device__ __forceinline__ void extract(const uint32_t* w, uint32_t* a) {
-    if constexpr (BITS == 2) {
-        const uint32_t v = w[0], v6 = v >> 6, v12 = v >> 12;
-        a[0] = (v & 0x00030003u) | MAGIC;
-        a[1] = (v & 0x000C000Cu) | MAGIC;
-        a[2] = (v & 0x00300030u) | MAGIC;
-        a[3] = (v6 & 0x00030003u) | MAGIC;
-        a[4] = (v6 & 0x000C000Cu) | MAGIC;
-        a[5] = (v6 & 0x00300030u) | MAGIC;
-        a[6] = (v12 & 0x00030003u) | MAGIC;
-        a[7] = (v12 & 0x000C000Cu) | MAGIC;
-    } else if constexpr (BITS == 3) {
-        const uint32_t A = w[0], B = w[1];
-        constexpr uint32_t m = 0x00070070u;
-        a[0] = ((A << 4) & m) | MAGIC;
-        a[1] = ((A << 1) & m) | MAGIC;
-        a[2] = ((A >> 2) & m) | MAGIC;
-        a[3] = ((A >> 5) & m) | MAGIC;
-        a[4] = (__funnelshift_r(A, B, 20) & m) | MAGIC;
-        a[5] = (__funnelshift_r(A, B, 23) & m) | MAGIC;
-        a[6] = (__funnelshift_r(A, B, 26) & m) | MAGIC;
-        a[7] = (__funnelshift_r(A, B, 29) & m) | MAGIC;
-    } else {
-        constexpr int NW = BITS == 4 ? 2 : 4;
-#pragma unroll
-        for (int i = 0; i < NW; ++i) {
-            const uint32_t v = w[i];
-            a[4 * i + 0] = (v & 0x000F000Fu) | MAGIC;
-            a[4 * i + 1] = ((v >> 4) & 0x000F000Fu) | MAGIC;
-            a[4 * i + 2] = ((v >> 8) & 0x000F000Fu) | MAGIC;
-            a[4 * i + 3] = ((v >> 12) & 0x000F000Fu) | MAGIC;
-        }
-    }
-}
 
 // Byte offset of word `wi` of subtile row `r` inside a subtile's swizzled code block
 // (boxes of 16 rows x SW bytes, TMA swizzle of 16-byte chunks within SW-byte rows).
@@ -166,10 +102,6 @@ __device__ __forceinline__ void load_window(const uint8_t* p, uint32_t offA, uin
     }
 }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-    return static_cast<uint32_t>(f32_to_bf16_bits(lo)) |
-           (static_cast<uint32_t>(f32_to_bf16_bits(hi)) << 16);
-}
 
 // ---------------------------------------------------------------------------------
 // Prologue: activation fragments + per-group sums, one CTA per 512-k chunk.
