@@ -1,21 +1,24 @@
 // Prefill-shaped MLX-affine quantized product on the 5th-generation tensor cores:
-// y[M,N] = x[M,K] . dequant(W)[N,K]^T for M > 16 tokens, group 64, K % 128 == 0,
+// y[M,N] = x[M,K] . dequant(W)[N,K]^T for M > 16 tokens, group 64, K % 512 == 0,
 // bits 2/3/4, bf16 activations and scales.  Replaces the Metal `qmm` kernel behind
 // MLX.quantizedMM (QuantizedLinear.callAsFunction,
 // Sources/Qwen38Core/FlashNext/Qwen4ExpPrequantized.swift:156-159) for prompt-sized inputs.
 //
-// Roles per CTA (one CTA per SM, persistent over 128-row x 128-token output tiles):
-//   warp 0     TMA producer: per 128-k stage, the activation tile (two 128-byte-swizzled
-//              64-element boxes), the weight rows' packed codes (swizzled box) and the
-//              8-group scale/bias boxes, into a ring of stages.
-//   warp 1     allocates TMEM; issues tcgen05.mma (M = 128 weight rows, N = 128 tokens,
-//              K = 16) with the weights as the TMEM operand and the activations as the
-//              shared-memory operand, accumulating the tile in TMEM (double-buffered).
-//   warps 2-5  dequantize: one thread per weight row turns its 128 codes per stage into
-//              exact bf16 weights w = scale*q + bias (magic-number extraction, bf16x2
-//              subtract and fused multiply-add, one rounding) and stores them to a TMEM
-//              operand slot with tcgen05.st -- the weights never pass through shared memory.
-//   warps 6-9  epilogue: read a finished accumulator tile from TMEM, convert to bf16, store.
+// CTA pairs (clusters of 2 on one SM pair), persistent over 256-row x 256-token output
+// tiles.  The pair's MMA is tcgen05.mma.cta_group::2 with M = 256 weight rows (128 in
+// each CTA's TMEM) and N = 256 tokens (128 staged in each CTA's shared memory), so every
+// byte a CTA stages feeds twice the math of a single-CTA 128x128 tile.  Roles per CTA:
+//   warp 0      TMA producer: per 128-k stage, the CTA's 128 tokens of activations (two
+//               128-byte-swizzled 64-element boxes, completion counted on the leader's
+//               barrier), its 128 weight rows' packed codes and 8-group scale/bias boxes.
+//   warp 1      allocates the pair's TMEM; in the leader, issues the pair MMAs (A = the
+//               dequantized weights in TMEM, B = activations in shared memory, D in TMEM).
+//   warps 2-5   dequantize: one thread per weight row turns its 128 codes per stage into
+//               exact bf16 weights w = scale*q + bias (magic-number extraction, bf16x2
+//               subtract and fused multiply-add, one rounding) and stores them into a TMEM
+//               operand slot with tcgen05.st -- the weights never pass through shared memory.
+//   warps 6-13  epilogue: two warps per TMEM lane quarter drain the finished accumulator
+//               (128 rows x 256 tokens per CTA), convert to bf16 and store.
 // The extraction yields codes in a fixed permuted order, some pre-multiplied by 2^p; the
 // prologue kernel writes the activations permuted and scaled by 2^-p to match, so the
 // products pair up exactly: sum_k' (2^p w_k)(2^-p x_k) = sum_k w_k x_k.
@@ -26,19 +29,22 @@
 namespace q38 {
 namespace {
 
-constexpr int P_ROWS = 128;   // weight rows per tile (MMA M, TMEM lanes)
-constexpr int P_TOK = 128;    // tokens per tile (MMA N)
-constexpr int P_KS = 128;     // k per stage (2 groups)
-constexpr int P_ASLOTS = 4;   // TMEM weight-operand slots, 64 columns each
-constexpr int P_THREADS = 10 * 32;
-constexpr uint32_t P_IDESC = idesc_bf16_f32(P_ROWS, P_TOK);
+constexpr int P_ROWS = 128;    // weight rows per CTA (TMEM lanes); a pair covers 2 x 128 (MMA M)
+constexpr int P_TOK = 256;     // tokens per pair tile (MMA N)
+constexpr int P_HTOK = 128;    // tokens staged per CTA (its half of N)
+constexpr int P_KS = 128;      // k per stage (2 groups)
+constexpr int P_ASLOTS = 4;    // TMEM weight-operand slots, 64 columns each (columns 0-255)
+constexpr uint32_t P_DCOL = 256;  // accumulator: columns 256-511, one per token of the tile
+constexpr int P_EPI_WARPS = 8;
+constexpr int P_THREADS = (6 + P_EPI_WARPS) * 32;
+constexpr uint32_t P_IDESC = idesc_bf16_f32(2 * P_ROWS, P_TOK);
 
 template <int BITS>
 struct PF {
     static constexpr int CODE_W = 4 * BITS;               // code words per row per stage
     static constexpr int CODE_B = P_ROWS * CODE_W * 4;    // 4 / 6 / 8 KiB
     static constexpr int SW = BITS == 2 ? 32 : BITS == 4 ? 64 : 0;  // code box swizzle span
-    static constexpr int X_B = 2 * P_TOK * 128;           // two 64-element 128-byte-swizzled boxes
+    static constexpr int X_B = 2 * P_HTOK * 128;          // two 64-element 128-byte-swizzled boxes
     static constexpr int SB_B = 2 * 2048;                 // scales + biases, {8 groups, 128 rows}
     static constexpr int STAGE = (X_B + CODE_B + SB_B + 1023) / 1024 * 1024;
 };
@@ -84,17 +90,28 @@ __global__ void __launch_bounds__(256) qgemm_prep(const __nv_bfloat16* __restric
 struct PArgs {
     __nv_bfloat16* y;
     uint32_t* status;
-    int M, N, K, nN, ntiles, stages, has_bias;
+    int M, N, K, nR, ntiles, stages, has_bias;
 };
 
-__device__ __forceinline__ bool p_wait(uint64_t* bar, uint32_t parity, uint32_t* status, volatile int* abort) {
-    if (mbar_try_wait(bar, parity)) return true;
+// Bounded mbarrier wait.  On expiry records the timeout and raises the abort flag of both
+// CTAs of the pair, so every role of both leaves its loop at its next wait.
+struct Abort {
+    volatile int* local;
+    uint32_t peer;  // the other CTA's flag (cluster address)
+    uint32_t* status;
+};
+
+template <bool CLUSTER>
+__device__ __forceinline__ bool p_wait(uint64_t* bar, uint32_t parity, const Abort& ab) {
+    auto poll = [&]() { return CLUSTER ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity); };
+    if (poll()) return true;
     const long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity)) {
-        if (*abort) return false;
+    while (!poll()) {
+        if (*ab.local) return false;
         if (clock64() - t0 > kWaitLimitCycles) {
-            if (status) atomicOr(status, Q38_DEV_TIMEOUT);
-            *abort = 1;
+            if (ab.status) atomicOr(ab.status, Q38_DEV_TIMEOUT);
+            *ab.local = 1;
+            st_shared_cluster_u32(ab.peer, 1u);
             return false;
         }
     }
@@ -103,8 +120,9 @@ __device__ __forceinline__ bool p_wait(uint64_t* bar, uint32_t parity, uint32_t*
 
 // Every lane waits (each observes the phase, so TMA-written data is visible to it); the
 // warp then agrees on the outcome so that the .sync.aligned TMEM accesses stay convergent.
-__device__ __forceinline__ bool p_wait_warp(uint64_t* bar, uint32_t parity, uint32_t* status, volatile int* abort) {
-    const bool ok = p_wait(bar, parity, status, abort);
+template <bool CLUSTER>
+__device__ __forceinline__ bool p_wait_warp(uint64_t* bar, uint32_t parity, const Abort& ab) {
+    const bool ok = p_wait<CLUSTER>(bar, parity, ab);
     return __all_sync(0xffffffffu, ok);
 }
 
@@ -121,7 +139,8 @@ __device__ __forceinline__ uint32_t bf2_fma(uint32_t a, uint32_t b, uint32_t c) 
 // Words of group gg (0/1) of the stage for this row -> exact bf16 weights (x 2^p) in
 // A-column order, 32 bf16x2 values.
 template <int BITS>
-__device__ __forceinline__ void dequant_group(const uint8_t* codes, int row, int gg, float s, float b, uint32_t* a) {
+__device__ __forceinline__ void dequant_group(const uint8_t* codes, int row, int gg, uint32_t sbits, uint32_t bbits,
+                                              uint32_t* a) {
     using F = PF<BITS>;
     constexpr int GW = 2 * BITS;  // words per row per group
     uint32_t w[8];
@@ -147,7 +166,15 @@ __device__ __forceinline__ void dequant_group(const uint8_t* codes, int row, int
             w[4 * i + 3] = v.w;
         }
     }
-    const uint32_t s2 = pack_bf16x2(s, s);
+    // s and 2^p b as bf16x2 with integer operations only: the scale broadcast, and the
+    // bias times a power of two, exact in fp32 and so exactly the bf16 in its high half.
+    const uint32_t s2 = sbits * 0x10001u;
+    const float bf = bf16_bits_to_f32(bbits);
+    uint32_t b2[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+        b2[q] = (__float_as_uint(bf * (1.0f / pair_mult<BITS>(q, 0))) >> 16) |
+                (__float_as_uint(bf * (1.0f / pair_mult<BITS>(q, 1))) & 0xFFFF0000u);
 #pragma unroll
     for (int tq = 0; tq < 4; ++tq) {
         uint32_t win[2];
@@ -171,8 +198,7 @@ __device__ __forceinline__ void dequant_group(const uint8_t* codes, int row, int
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
             // v - 128 = 2^p q exactly; a = s * (2^p q) + 2^p b, rounded once
-            const uint32_t b2 = pack_bf16x2(b / pair_mult<BITS>(q, 0), b / pair_mult<BITS>(q, 1));
-            a[tq * 8 + q] = bf2_fma(bf2_sub(v[q], MAGIC), s2, b2);
+            a[tq * 8 + q] = bf2_fma(bf2_sub(v[q], MAGIC), s2, b2[q]);
         }
     }
 }
@@ -187,45 +213,49 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
-    uint64_t* stage_full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* stage_empty = stage_full + 8;
-    uint64_t* a_full = stage_empty + 8;
-    uint64_t* a_free = a_full + P_ASLOTS;
-    uint64_t* d_full = a_free + P_ASLOTS;
-    uint64_t* d_free = d_full + 2;
-    uint64_t* final_bar = d_free + 2;
+    uint64_t* w_full = reinterpret_cast<uint64_t*>(smem);  // codes + scales landed (local)
+    uint64_t* x_full = w_full + 8;       // both CTAs' activation halves landed (leader)
+    uint64_t* stage_empty = x_full + 8;  // local dequant done + pair MMAs done (local)
+    uint64_t* a_full = stage_empty + 8;  // both CTAs' weight slots written (leader)
+    uint64_t* a_free = a_full + P_ASLOTS;  // pair MMAs reading the slot done (local)
+    uint64_t* d_full = a_free + P_ASLOTS;  // tile accumulated (local)
+    uint64_t* d_free = d_full + 1;         // both CTAs' accumulators drained (leader)
+    uint64_t* final_bar = d_free + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
-    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     uint8_t* stages = smem + 1024;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
     const int ksteps = a.K / P_KS;
     if (threadIdx.x == 0) {
         for (int i = 0; i < a.stages; ++i) {
-            mbar_init(&stage_full[i], 1);
-            mbar_init(&stage_empty[i], 5);  // 4 dequant warps + the MMA commit
+            mbar_init(&w_full[i], 1);
+            mbar_init(&x_full[i], 1);
+            mbar_init(&stage_empty[i], 5);  // 4 dequant warps + the pair-MMA commit
         }
         for (int i = 0; i < P_ASLOTS; ++i) {
-            mbar_init(&a_full[i], 4);
+            mbar_init(&a_full[i], 8);  // 4 dequant warps in each CTA
             mbar_init(&a_free[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&d_full[i], 1);
-            mbar_init(&d_free[i], 4);
-        }
+        mbar_init(d_full, 1);
+        mbar_init(d_free, 2 * P_EPI_WARPS);
         mbar_init(final_bar, 1);
-        *abort = 0;
+        *abort_flag = 0;
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, 512);
-        tmem_relinquish();
+        tmem_alloc_pair(tmem_slot, 512);
+        tmem_relinquish_pair();
     }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();
     tc_fence_after();
     griddep_launch_dependents();
     const uint32_t tmem = *tmem_slot;
+    const Abort ab{abort_flag, mapa_shared(const_cast<int*>(abort_flag), rank ^ 1u), a.status};
 
     if (warp == 0) {
         // ---------------------------------------------------------------- producer
@@ -234,28 +264,30 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
             prefetch_tensormap(&map_codes);
             prefetch_tensormap(&map_scales);
             if (a.has_bias) prefetch_tensormap(&map_biases);
-            const uint32_t bytes = F::X_B + F::CODE_B + 2048u * (a.has_bias ? 2u : 1u);
+            const uint32_t wbytes = F::CODE_B + 2048u * (a.has_bias ? 2u : 1u);
             bool waited = false;
             int gs = 0;
-            for (int tile = blockIdx.x; tile < a.ntiles && !*abort; tile += gridDim.x) {
-                const int n0 = (tile % a.nN) * P_ROWS, m0 = (tile / a.nN) * P_TOK;
+            for (int tile = pair; tile < a.ntiles && !*abort_flag; tile += npairs) {
+                const int n0 = (tile % a.nR) * (2 * P_ROWS) + rank * P_ROWS;
+                const int m0 = (tile / a.nR) * P_TOK + rank * P_HTOK;
                 for (int ks = 0; ks < ksteps; ++ks, ++gs) {
                     const int slot = gs % a.stages;
-                    if (gs >= a.stages && !p_wait(&stage_empty[slot], ((gs / a.stages) - 1) & 1, a.status, abort))
-                        break;
+                    if (gs >= a.stages && !p_wait<false>(&stage_empty[slot], ((gs / a.stages) - 1) & 1, ab)) break;
                     uint8_t* st = stages + static_cast<size_t>(slot) * F::STAGE;
                     const int k0 = ks * P_KS;
-                    mbar_arrive_expect_tx(&stage_full[slot], bytes);
-                    tma_load_2d(st + F::X_B, &map_codes, &stage_full[slot], k0 * BITS / 32, n0);
-                    tma_load_2d(st + F::X_B + F::CODE_B, &map_scales, &stage_full[slot], (k0 / 512) * 8, n0);
+                    mbar_arrive_expect_tx(&w_full[slot], wbytes);
+                    tma_load_2d(st + F::X_B, &map_codes, &w_full[slot], k0 * BITS / 32, n0);
+                    tma_load_2d(st + F::X_B + F::CODE_B, &map_scales, &w_full[slot], (k0 / 512) * 8, n0);
                     if (a.has_bias)
-                        tma_load_2d(st + F::X_B + F::CODE_B + 2048, &map_biases, &stage_full[slot], (k0 / 512) * 8, n0);
+                        tma_load_2d(st + F::X_B + F::CODE_B + 2048, &map_biases, &w_full[slot], (k0 / 512) * 8, n0);
                     if (!waited) {
                         griddep_wait();  // the permuted activations come from the prologue kernel
                         waited = true;
                     }
-                    tma_load_2d(st, &map_x, &stage_full[slot], k0, m0);
-                    tma_load_2d(st + P_TOK * 128, &map_x, &stage_full[slot], k0 + 64, m0);
+                    if (leader) mbar_arrive_expect_tx(&x_full[slot], 2 * F::X_B);
+                    const uint32_t xbar = mapa_shared(&x_full[slot], 0);
+                    tma_load_2d_pair(st, &map_x, xbar, k0, m0);
+                    tma_load_2d_pair(st + P_HTOK * 128, &map_x, xbar, k0 + 64, m0);
                 }
             }
             // No copy may still be landing when the CTA exits (matters only after an abort:
@@ -263,23 +295,22 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
             const int last = gs < a.stages ? gs : a.stages;
             for (int i = 1; i <= last; ++i) {
                 const int g = gs - i;
-                mbar_wait(&stage_full[g % a.stages], (g / a.stages) & 1, a.status);
+                mbar_wait(&w_full[g % a.stages], (g / a.stages) & 1, a.status);
+                if (leader) mbar_wait(&x_full[g % a.stages], (g / a.stages) & 1, a.status);
             }
         }
     } else if (warp == 1) {
-        // --------------------------------------------------------------- MMA issuer
-        if (lane == 0) {
+        // -------------------------------------------------- pair MMA issuer (leader)
+        if (leader && lane == 0) {
             int gs = 0, tc = 0;
-            for (int tile = blockIdx.x; tile < a.ntiles && !*abort; tile += gridDim.x, ++tc) {
-                const int db = tc & 1;
-                if (tc >= 2 && !p_wait(&d_free[db], ((tc >> 1) - 1) & 1, a.status, abort)) break;
+            for (int tile = pair; tile < a.ntiles && !*abort_flag; tile += npairs, ++tc) {
+                if (tc >= 1 && !p_wait<true>(d_free, (tc - 1) & 1, ab)) break;
                 tc_fence_after();
-                const uint32_t dcol = tmem + 256 + db * P_TOK;
                 bool ok = true;
                 for (int ks = 0; ks < ksteps; ++ks, ++gs) {
                     const int slot = gs % a.stages, as = gs % P_ASLOTS;
-                    if (!p_wait(&stage_full[slot], (gs / a.stages) & 1, a.status, abort) ||
-                        !p_wait(&a_full[as], (gs / P_ASLOTS) & 1, a.status, abort)) {
+                    if (!p_wait<false>(&x_full[slot], (gs / a.stages) & 1, ab) ||
+                        !p_wait<true>(&a_full[as], (gs / P_ASLOTS) & 1, ab)) {
                         ok = false;
                         break;
                     }
@@ -287,17 +318,18 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
                     const uint32_t xs = smem_u32(stages + static_cast<size_t>(slot) * F::STAGE);
 #pragma unroll
                     for (int kk = 0; kk < 8; ++kk) {
-                        const uint64_t bd = smem_desc(xs + (kk >> 2) * (P_TOK * 128) + (kk & 3) * 32, 16, 1024, 2);
-                        tc_mma_ts(dcol, tmem + as * 64 + kk * 8, bd, P_IDESC, (ks > 0 || kk > 0) ? 1u : 0u);
+                        const uint64_t bd = smem_desc(xs + (kk >> 2) * (P_HTOK * 128) + (kk & 3) * 32, 16, 1024, 2);
+                        tc_mma_ts_pair(tmem + P_DCOL, tmem + as * 64 + kk * 8, bd, P_IDESC,
+                                       (ks > 0 || kk > 0) ? 1u : 0u);
                     }
-                    tc_commit(&stage_empty[slot]);
-                    tc_commit(&a_free[as]);
+                    tc_commit_pair(&stage_empty[slot], 3);
+                    tc_commit_pair(&a_free[as], 3);
                 }
                 if (!ok) break;
-                tc_commit(&d_full[db]);
+                tc_commit_pair(d_full, 3);
             }
             // every MMA (and its TMEM reads) has finished before the teardown frees TMEM
-            tc_commit(final_bar);
+            tc_commit_pair(final_bar, 1);
             mbar_wait(final_bar, 0, a.status);
         }
     } else if (warp < 6) {
@@ -305,72 +337,111 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+        const uint32_t a_full_leader = mapa_shared(a_full, 0);
         int gs = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
+        for (int tile = pair; tile < a.ntiles && ok; tile += npairs) {
             for (int ks = 0; ks < ksteps; ++ks, ++gs) {
                 const int slot = gs % a.stages, as = gs % P_ASLOTS;
-                if (!p_wait_warp(&stage_full[slot], (gs / a.stages) & 1, a.status, abort)) {
-                    ok = false;
-                    break;
-                }
-                if (gs >= P_ASLOTS && !p_wait_warp(&a_free[as], ((gs / P_ASLOTS) - 1) & 1, a.status, abort)) {
+                if (!p_wait_warp<false>(&w_full[slot], (gs / a.stages) & 1, ab) ||
+                    (gs >= P_ASLOTS && !p_wait_warp<false>(&a_free[as], ((gs / P_ASLOTS) - 1) & 1, ab))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint8_t* st = stages + static_cast<size_t>(slot) * F::STAGE;
-                const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + F::X_B + F::CODE_B) + row * 8 +
-                                     ((ks * P_KS / 64) & 7);
-                const float s0 = bf16_bits_to_f32(sc[0]), s1 = bf16_bits_to_f32(sc[1]);
-                const float b0 = a.has_bias ? bf16_bits_to_f32(sc[1024]) : 0.f;
-                const float b1 = a.has_bias ? bf16_bits_to_f32(sc[1025]) : 0.f;
+                const uint32_t* sb = reinterpret_cast<const uint32_t*>(st + F::X_B + F::CODE_B);
+                const uint32_t s01 = sb[row * 4 + (ks & 3)];
+                const uint32_t b01 = a.has_bias ? sb[512 + row * 4 + (ks & 3)] : 0u;
                 uint32_t av[32];
-                dequant_group<BITS>(st + F::X_B, row, 0, s0, b0, av);
+                dequant_group<BITS>(st + F::X_B, row, 0, s01 & 0xFFFFu, b01 & 0xFFFFu, av);
                 tmem_st32(tmem + lane_off + as * 64, av);
-                dequant_group<BITS>(st + F::X_B, row, 1, s1, b1, av);
+                dequant_group<BITS>(st + F::X_B, row, 1, s01 >> 16, b01 >> 16, av);
                 tmem_st32(tmem + lane_off + as * 64 + 32, av);
                 tc_wait_st();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive(&a_full[as]);
                     mbar_arrive(&stage_empty[slot]);
+                    mbar_arrive_cluster(a_full_leader + as * 8);
                 }
             }
         }
     } else {
         // ---------------------------------------------------------------- epilogue
-        const int quarter = warp & 3;
+        const int quarter = warp & 3, half = (warp - 6) >> 2;
         const int row = quarter * 32 + lane;
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+        const uint32_t d_free_leader = mapa_shared(d_free, 0);
         int tc = 0;
-        for (int tile = blockIdx.x; tile < a.ntiles; tile += gridDim.x, ++tc) {
-            const int db = tc & 1;
-            if (!p_wait_warp(&d_full[db], (tc >> 1) & 1, a.status, abort)) break;
+        for (int tile = pair; tile < a.ntiles; tile += npairs, ++tc) {
+            if (!p_wait_warp<false>(d_full, tc & 1, ab)) break;
             tc_fence_after();
-            const int n = (tile % a.nN) * P_ROWS + row, m0 = (tile / a.nN) * P_TOK;
+            const int n = (tile % a.nR) * (2 * P_ROWS) + rank * P_ROWS + row;
+            const int m0 = (tile / a.nR) * P_TOK + half * (P_TOK / 2);
 #pragma unroll 1
-            for (int ch = 0; ch < P_TOK / 32; ++ch) {
+            for (int ch = 0; ch < P_TOK / 64; ++ch) {
                 float v[32];
-                tmem_ld32(tmem + lane_off + 256 + db * P_TOK + ch * 32, v);
-                if (n < a.N) {
+                tmem_ld32(tmem + lane_off + P_DCOL + half * (P_TOK / 2) + ch * 32, v);
+                const int mc = m0 + ch * 32;
+                const int mlim = n < a.N ? min(32, a.M - mc) : 0;
+                __nv_bfloat16* out = a.y + static_cast<size_t>(mc) * a.N + n;
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const int m = m0 + ch * 32 + i;
-                        if (m < a.M) a.y[static_cast<size_t>(m) * a.N + n] = __float2bfloat16_rn(v[i]);
-                    }
+                for (int i = 0; i < 32; ++i) {
+                    if (i < mlim) *out = __float2bfloat16_rn(v[i]);
+                    out += a.N;
                 }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&d_free[db]);
+            if (lane == 0) mbar_arrive_cluster(d_free_leader);
         }
     }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem, 512);
+    if (warp == 1) tmem_dealloc_pair(tmem, 512);
+}
+
+struct PairLaunch {
+    int smem = 0;
+    int max_pairs = 0;
+};
+
+template <int BITS>
+q38_status pair_config(q38_ctx* ctx, int smem, PairLaunch* out) {
+    static std::mutex mu;
+    static PairLaunch cached[64];
+    std::lock_guard<std::mutex> lk(mu);
+    const int dev = ctx->device;
+    if (dev < 64 && cached[dev].max_pairs > 0) {
+        *out = cached[dev];
+        return Q38_OK;
+    }
+    auto kmain = qgemm_tc<BITS>;
+    if (cudaFuncSetAttribute(kmain, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        return check_launch(ctx, "cudaFuncSetAttribute");
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * (ctx->num_sms / 2));
+    cfg.blockDim = dim3(P_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kmain, &cfg) != cudaSuccess)
+        return check_launch(ctx, "cudaOccupancyMaxActiveClusters");
+    if (clusters < 1) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: no CTA pair fits on this device");
+    PairLaunch pl;
+    pl.smem = smem;
+    pl.max_pairs = clusters;
+    if (dev < 64) cached[dev] = pl;
+    *out = pl;
+    return Q38_OK;
 }
 
 template <int BITS>
@@ -385,7 +456,7 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
     const CUtensorMapSwizzle cswz = F::SW == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                                     : F::SW == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
                                                   : CU_TENSOR_MAP_SWIZZLE_NONE;
-    if (!make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xp, K, M, 64, P_TOK, CU_TENSOR_MAP_SWIZZLE_128B) ||
+    if (!make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xp, K, M, 64, P_HTOK, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_map_2d(&mc, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w, static_cast<uint64_t>(K) * BITS / 32, N,
                      F::CODE_W, P_ROWS, cswz) ||
         !make_map_2d(&ms, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s, K / 64, N, 8, P_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
@@ -396,26 +467,20 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
     int stages = (227 * 1024 - 2048) / F::STAGE;
     if (stages > 8) stages = 8;
     if (stages < 2) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: prefill stage too large");
-    const int smem = 2048 + stages * F::STAGE;
+    PairLaunch pl;
+    if ((st = pair_config<BITS>(ctx, 2048 + stages * F::STAGE, &pl)) != Q38_OK) return st;
 
-    auto kmain = qgemm_tc<BITS>;
-    static std::mutex mu;
-    static bool configured[64] = {};
-    {
-        std::lock_guard<std::mutex> lk(mu);
-        if (ctx->device < 64 && !configured[ctx->device]) {
-            if (cudaFuncSetAttribute(kmain, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
-                return check_launch(ctx, "cudaFuncSetAttribute");
-            configured[ctx->device] = true;
-        }
-    }
-    const int nN = (N + P_ROWS - 1) / P_ROWS, nM = (M + P_TOK - 1) / P_TOK;
-    const int ntiles = nN * nM;
-    const int grid = ntiles < ctx->num_sms ? ntiles : ctx->num_sms;
+    const int nR = (N + 2 * P_ROWS - 1) / (2 * P_ROWS), nT = (M + P_TOK - 1) / P_TOK;
+    const int ntiles = nR * nT;
+    const int pairs = ntiles < pl.max_pairs ? ntiles : pl.max_pairs;
 
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     const long long items = static_cast<long long>(M) * (K / 64);
     cudaLaunchConfig_t pcfg = {};
     pcfg.gridDim = dim3(static_cast<unsigned>((items + 255) / 256));
@@ -433,18 +498,19 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
     args.M = M;
     args.N = N;
     args.K = K;
-    args.nN = nN;
+    args.nR = nR;
     args.ntiles = ntiles;
     args.stages = stages;
     args.has_bias = b != nullptr;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
     cfg.blockDim = dim3(P_THREADS);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = pl.smem;
     cfg.stream = ctx->stream;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, kmain, mx, mc, ms, mb, args) != cudaSuccess) return check_launch(ctx, "qgemm_tc");
+    cfg.numAttrs = 2;
+    if (cudaLaunchKernelEx(&cfg, qgemm_tc<BITS>, mx, mc, ms, mb, args) != cudaSuccess)
+        return check_launch(ctx, "qgemm_tc");
     return check_launch(ctx, "qgemm_tc");
 }
 
