@@ -35,8 +35,10 @@ constexpr int P_HTOK = 128;    // tokens staged per CTA (its half of N)
 constexpr int P_KS = 128;      // k per stage (2 groups)
 constexpr int P_ASLOTS = 4;    // TMEM weight-operand slots, 64 columns each (columns 0-255)
 constexpr uint32_t P_DCOL = 256;  // accumulator: columns 256-511, one per token of the tile
-constexpr int P_EPI_WARPS = 8;
-constexpr int P_THREADS = (6 + P_EPI_WARPS) * 32;
+constexpr int P_DEQ_WARPS = 8;  // two sets of four (one warp per TMEM lane quarter), alternate stages
+constexpr int P_EPI_WARPS = 4;
+constexpr int P_WARP_DEQ0 = 3, P_WARP_EPI0 = P_WARP_DEQ0 + P_DEQ_WARPS;
+constexpr int P_THREADS = (P_WARP_EPI0 + P_EPI_WARPS) * 32;
 constexpr uint32_t P_IDESC = idesc_bf16_f32(2 * P_ROWS, P_TOK);
 
 template <int BITS>
@@ -46,7 +48,11 @@ struct PF {
     static constexpr int SW = BITS == 2 ? 32 : BITS == 4 ? 64 : 0;  // code box swizzle span
     static constexpr int X_B = 2 * P_HTOK * 128;          // two 64-element 128-byte-swizzled boxes
     static constexpr int SB_B = 2 * 2048;                 // scales + biases, {8 groups, 128 rows}
-    static constexpr int STAGE = (X_B + CODE_B + SB_B + 1023) / 1024 * 1024;
+    static constexpr int W_STAGE = (CODE_B + SB_B + 1023) / 1024 * 1024;
+    static constexpr int X_STAGES = 5;
+    static constexpr int W_STAGES_MAX = (227 * 1024 - 2048 - X_STAGES * X_B) / W_STAGE;
+    static constexpr int W_STAGES = W_STAGES_MAX > 8 ? 8 : W_STAGES_MAX;
+    static constexpr int SMEM = 2048 + X_STAGES * X_B + W_STAGES * W_STAGE;
 };
 
 // ---------------------------------------------------------------------------------
@@ -56,8 +62,8 @@ struct PF {
 template <int BITS>
 __global__ void __launch_bounds__(256) qgemm_prep(const __nv_bfloat16* __restrict__ x, int64_t M, int K,
                                                   __nv_bfloat16* __restrict__ xp) {
-    griddep_launch_dependents();
     griddep_wait();
+    griddep_launch_dependents();
     const int G = K / 64;
     const int64_t item = blockIdx.x * 256LL + threadIdx.x;  // (token, group)
     if (item >= M * G) return;
@@ -90,7 +96,7 @@ __global__ void __launch_bounds__(256) qgemm_prep(const __nv_bfloat16* __restric
 struct PArgs {
     __nv_bfloat16* y;
     uint32_t* status;
-    int M, N, K, nR, ntiles, stages, has_bias;
+    int M, N, K, nR, ntiles, has_bias;
 };
 
 // Bounded mbarrier wait.  On expiry records the timeout and raises the abort flag of both
@@ -210,31 +216,39 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
                                                         const __grid_constant__ CUtensorMap map_biases,
                                                         const PArgs a) {
     using F = PF<BITS>;
+    constexpr int SX = F::X_STAGES, SW = F::W_STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
-    uint64_t* w_full = reinterpret_cast<uint64_t*>(smem);  // codes + scales landed (local)
-    uint64_t* x_full = w_full + 8;       // both CTAs' activation halves landed (leader)
-    uint64_t* stage_empty = x_full + 8;  // local dequant done + pair MMAs done (local)
-    uint64_t* a_full = stage_empty + 8;  // both CTAs' weight slots written (leader)
-    uint64_t* a_free = a_full + P_ASLOTS;  // pair MMAs reading the slot done (local)
-    uint64_t* d_full = a_free + P_ASLOTS;  // tile accumulated (local)
-    uint64_t* d_free = d_full + 1;         // both CTAs' accumulators drained (leader)
+    uint64_t* x_full = reinterpret_cast<uint64_t*>(smem);  // both CTAs' activation halves landed (leader)
+    uint64_t* x_empty = x_full + 8;                        // pair MMAs reading the slot done (local)
+    uint64_t* w_full = x_empty + 8;                        // codes + scales landed (local)
+    uint64_t* w_empty = w_full + 8;                        // dequant warps done reading (local)
+    uint64_t* a_full = w_empty + 8;                        // both CTAs' weight slots written (leader)
+    uint64_t* a_free = a_full + P_ASLOTS;                  // pair MMAs reading the slot done (local)
+    uint64_t* d_full = a_free + P_ASLOTS;                  // tile accumulated (local)
+    uint64_t* d_free = d_full + 1;                         // both CTAs' accumulators drained (leader)
     uint64_t* final_bar = d_free + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    uint8_t* stages = smem + 1024;
+    uint8_t* xring = smem + 1024;
+    uint8_t* wring = xring + SX * F::X_B;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
     const bool leader = rank == 0;
     const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
     const int ksteps = a.K / P_KS;
+    const int my_tiles = pair < a.ntiles ? (a.ntiles - 1 - pair) / npairs + 1 : 0;
+    const int total = my_tiles * ksteps;  // stages this pair runs
     if (threadIdx.x == 0) {
-        for (int i = 0; i < a.stages; ++i) {
-            mbar_init(&w_full[i], 1);
+        for (int i = 0; i < SX; ++i) {
             mbar_init(&x_full[i], 1);
-            mbar_init(&stage_empty[i], 5);  // 4 dequant warps + the pair-MMA commit
+            mbar_init(&x_empty[i], 1);
+        }
+        for (int i = 0; i < SW; ++i) {
+            mbar_init(&w_full[i], 1);
+            mbar_init(&w_empty[i], 4);
         }
         for (int i = 0; i < P_ASLOTS; ++i) {
             mbar_init(&a_full[i], 8);  // 4 dequant warps in each CTA
@@ -258,131 +272,127 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
     const Abort ab{abort_flag, mapa_shared(const_cast<int*>(abort_flag), rank ^ 1u), a.status};
 
     if (warp == 0) {
-        // ---------------------------------------------------------------- producer
+        // ------------------------------------------------------- activation producer
         if (lane == 0) {
             prefetch_tensormap(&map_x);
+            griddep_wait();  // the permuted activations come from the prologue kernel
+            int gs = 0;
+            for (; gs < total && !*abort_flag; ++gs) {
+                const int slot = gs % SX, tile = pair + (gs / ksteps) * npairs, ks = gs % ksteps;
+                if (gs >= SX && !p_wait<false>(&x_empty[slot], ((gs / SX) - 1) & 1, ab)) break;
+                const int m0 = (tile / a.nR) * P_TOK + rank * P_HTOK, k0 = ks * P_KS;
+                uint8_t* st = xring + slot * F::X_B;
+                if (leader) mbar_arrive_expect_tx(&x_full[slot], 2 * F::X_B);
+                const uint32_t xbar = mapa_shared(&x_full[slot], 0);
+                tma_load_2d_pair(st, &map_x, xbar, k0, m0);
+                tma_load_2d_pair(st + P_HTOK * 128, &map_x, xbar, k0 + 64, m0);
+            }
+            // No copy may still be landing when the CTA exits (matters only after an abort:
+            // otherwise the MMAs have consumed every fill).
+            if (leader)
+                for (int i = 1; i <= (gs < SX ? gs : SX); ++i)
+                    mbar_wait(&x_full[(gs - i) % SX], ((gs - i) / SX) & 1, a.status);
+        }
+    } else if (warp == 2) {
+        // ----------------------------------------------------------- weight producer
+        if (lane == 0) {
             prefetch_tensormap(&map_codes);
             prefetch_tensormap(&map_scales);
             if (a.has_bias) prefetch_tensormap(&map_biases);
             const uint32_t wbytes = F::CODE_B + 2048u * (a.has_bias ? 2u : 1u);
-            bool waited = false;
             int gs = 0;
-            for (int tile = pair; tile < a.ntiles && !*abort_flag; tile += npairs) {
-                const int n0 = (tile % a.nR) * (2 * P_ROWS) + rank * P_ROWS;
-                const int m0 = (tile / a.nR) * P_TOK + rank * P_HTOK;
-                for (int ks = 0; ks < ksteps; ++ks, ++gs) {
-                    const int slot = gs % a.stages;
-                    if (gs >= a.stages && !p_wait<false>(&stage_empty[slot], ((gs / a.stages) - 1) & 1, ab)) break;
-                    uint8_t* st = stages + static_cast<size_t>(slot) * F::STAGE;
-                    const int k0 = ks * P_KS;
-                    mbar_arrive_expect_tx(&w_full[slot], wbytes);
-                    tma_load_2d(st + F::X_B, &map_codes, &w_full[slot], k0 * BITS / 32, n0);
-                    tma_load_2d(st + F::X_B + F::CODE_B, &map_scales, &w_full[slot], (k0 / 512) * 8, n0);
-                    if (a.has_bias)
-                        tma_load_2d(st + F::X_B + F::CODE_B + 2048, &map_biases, &w_full[slot], (k0 / 512) * 8, n0);
-                    if (!waited) {
-                        griddep_wait();  // the permuted activations come from the prologue kernel
-                        waited = true;
-                    }
-                    if (leader) mbar_arrive_expect_tx(&x_full[slot], 2 * F::X_B);
-                    const uint32_t xbar = mapa_shared(&x_full[slot], 0);
-                    tma_load_2d_pair(st, &map_x, xbar, k0, m0);
-                    tma_load_2d_pair(st + P_HTOK * 128, &map_x, xbar, k0 + 64, m0);
-                }
+            for (; gs < total && !*abort_flag; ++gs) {
+                const int slot = gs % SW, tile = pair + (gs / ksteps) * npairs, ks = gs % ksteps;
+                if (gs >= SW && !p_wait<false>(&w_empty[slot], ((gs / SW) - 1) & 1, ab)) break;
+                const int n0 = (tile % a.nR) * (2 * P_ROWS) + rank * P_ROWS, k0 = ks * P_KS;
+                uint8_t* st = wring + slot * F::W_STAGE;
+                mbar_arrive_expect_tx(&w_full[slot], wbytes);
+                tma_load_2d(st, &map_codes, &w_full[slot], k0 * BITS / 32, n0);
+                tma_load_2d(st + F::CODE_B, &map_scales, &w_full[slot], (k0 / 512) * 8, n0);
+                if (a.has_bias) tma_load_2d(st + F::CODE_B + 2048, &map_biases, &w_full[slot], (k0 / 512) * 8, n0);
             }
-            // No copy may still be landing when the CTA exits (matters only after an abort:
-            // otherwise the consumers have already waited for every fill).
-            const int last = gs < a.stages ? gs : a.stages;
-            for (int i = 1; i <= last; ++i) {
-                const int g = gs - i;
-                mbar_wait(&w_full[g % a.stages], (g / a.stages) & 1, a.status);
-                if (leader) mbar_wait(&x_full[g % a.stages], (g / a.stages) & 1, a.status);
-            }
+            for (int i = 1; i <= (gs < SW ? gs : SW); ++i)
+                mbar_wait(&w_full[(gs - i) % SW], ((gs - i) / SW) & 1, a.status);
         }
     } else if (warp == 1) {
         // -------------------------------------------------- pair MMA issuer (leader)
         if (leader && lane == 0) {
-            int gs = 0, tc = 0;
-            for (int tile = pair; tile < a.ntiles && !*abort_flag; tile += npairs, ++tc) {
+            int gs = 0;
+            bool ok = true;
+            for (int tc = 0; tc < my_tiles && ok && !*abort_flag; ++tc) {
                 if (tc >= 1 && !p_wait<true>(d_free, (tc - 1) & 1, ab)) break;
                 tc_fence_after();
-                bool ok = true;
                 for (int ks = 0; ks < ksteps; ++ks, ++gs) {
-                    const int slot = gs % a.stages, as = gs % P_ASLOTS;
-                    if (!p_wait<false>(&x_full[slot], (gs / a.stages) & 1, ab) ||
+                    const int xs = gs % SX, as = gs % P_ASLOTS;
+                    if (!p_wait<false>(&x_full[xs], (gs / SX) & 1, ab) ||
                         !p_wait<true>(&a_full[as], (gs / P_ASLOTS) & 1, ab)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t xs = smem_u32(stages + static_cast<size_t>(slot) * F::STAGE);
+                    const uint32_t xa = smem_u32(xring + xs * F::X_B);
 #pragma unroll
                     for (int kk = 0; kk < 8; ++kk) {
-                        const uint64_t bd = smem_desc(xs + (kk >> 2) * (P_HTOK * 128) + (kk & 3) * 32, 16, 1024, 2);
+                        const uint64_t bd = smem_desc(xa + (kk >> 2) * (P_HTOK * 128) + (kk & 3) * 32, 16, 1024, 2);
                         tc_mma_ts_pair(tmem + P_DCOL, tmem + as * 64 + kk * 8, bd, P_IDESC,
                                        (ks > 0 || kk > 0) ? 1u : 0u);
                     }
-                    tc_commit_pair(&stage_empty[slot], 3);
+                    tc_commit_pair(&x_empty[xs], 3);
                     tc_commit_pair(&a_free[as], 3);
                 }
-                if (!ok) break;
-                tc_commit_pair(d_full, 3);
+                if (ok) tc_commit_pair(d_full, 3);
             }
             // every MMA (and its TMEM reads) has finished before the teardown frees TMEM
             tc_commit_pair(final_bar, 1);
             mbar_wait(final_bar, 0, a.status);
         }
-    } else if (warp < 6) {
+    } else if (warp < P_WARP_EPI0) {
         // ----------------------------------------------------------------- dequant
+        // Set 0 dequantizes the even stages, set 1 the odd ones; within a set, one warp
+        // per TMEM lane quarter, one thread per weight row.
+        const int set = (warp - P_WARP_DEQ0) >> 2;
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
         const uint32_t a_full_leader = mapa_shared(a_full, 0);
-        int gs = 0;
-        bool ok = true;
-        for (int tile = pair; tile < a.ntiles && ok; tile += npairs) {
-            for (int ks = 0; ks < ksteps; ++ks, ++gs) {
-                const int slot = gs % a.stages, as = gs % P_ASLOTS;
-                if (!p_wait_warp<false>(&w_full[slot], (gs / a.stages) & 1, ab) ||
-                    (gs >= P_ASLOTS && !p_wait_warp<false>(&a_free[as], ((gs / P_ASLOTS) - 1) & 1, ab))) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint8_t* st = stages + static_cast<size_t>(slot) * F::STAGE;
-                const uint32_t* sb = reinterpret_cast<const uint32_t*>(st + F::X_B + F::CODE_B);
-                const uint32_t s01 = sb[row * 4 + (ks & 3)];
-                const uint32_t b01 = a.has_bias ? sb[512 + row * 4 + (ks & 3)] : 0u;
-                uint32_t av[32];
-                dequant_group<BITS>(st + F::X_B, row, 0, s01 & 0xFFFFu, b01 & 0xFFFFu, av);
-                tmem_st32(tmem + lane_off + as * 64, av);
-                dequant_group<BITS>(st + F::X_B, row, 1, s01 >> 16, b01 >> 16, av);
-                tmem_st32(tmem + lane_off + as * 64 + 32, av);
-                tc_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&stage_empty[slot]);
-                    mbar_arrive_cluster(a_full_leader + as * 8);
-                }
-            }
+        for (int gs = set; gs < total; gs += 2) {
+            const int slot = gs % SW, as = gs % P_ASLOTS, ks = gs % ksteps;
+            if (!p_wait_warp<false>(&w_full[slot], (gs / SW) & 1, ab) ||
+                (gs >= P_ASLOTS && !p_wait_warp<false>(&a_free[as], ((gs / P_ASLOTS) - 1) & 1, ab)))
+                break;
+            tc_fence_after();
+            const uint8_t* st = wring + slot * F::W_STAGE;
+            const uint32_t* sb = reinterpret_cast<const uint32_t*>(st + F::CODE_B);
+            const uint32_t s01 = sb[row * 4 + (ks & 3)];
+            const uint32_t b01 = a.has_bias ? sb[512 + row * 4 + (ks & 3)] : 0u;
+            uint32_t av[32];
+            dequant_group<BITS>(st, row, 0, s01 & 0xFFFFu, b01 & 0xFFFFu, av);
+            tmem_st32(tmem + lane_off + as * 64, av);
+            dequant_group<BITS>(st, row, 1, s01 >> 16, b01 >> 16, av);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&w_empty[slot]);  // codes read; the slot may refill
+            tmem_st32(tmem + lane_off + as * 64 + 32, av);
+            tc_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(a_full_leader + as * 8);
         }
     } else {
         // ---------------------------------------------------------------- epilogue
-        const int quarter = warp & 3, half = (warp - 6) >> 2;
+        const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
         const uint32_t d_free_leader = mapa_shared(d_free, 0);
-        int tc = 0;
-        for (int tile = pair; tile < a.ntiles; tile += npairs, ++tc) {
+        for (int tc = 0; tc < my_tiles; ++tc) {
             if (!p_wait_warp<false>(d_full, tc & 1, ab)) break;
             tc_fence_after();
+            const int tile = pair + tc * npairs;
             const int n = (tile % a.nR) * (2 * P_ROWS) + rank * P_ROWS + row;
-            const int m0 = (tile / a.nR) * P_TOK + half * (P_TOK / 2);
+            const int m0 = (tile / a.nR) * P_TOK;
 #pragma unroll 1
-            for (int ch = 0; ch < P_TOK / 64; ++ch) {
+            for (int ch = 0; ch < P_TOK / 32; ++ch) {
                 float v[32];
-                tmem_ld32(tmem + lane_off + P_DCOL + half * (P_TOK / 2) + ch * 32, v);
+                tmem_ld32(tmem + lane_off + P_DCOL + ch * 32, v);
                 const int mc = m0 + ch * 32;
                 const int mlim = n < a.N ? min(32, a.M - mc) : 0;
                 __nv_bfloat16* out = a.y + static_cast<size_t>(mc) * a.N + n;
@@ -464,11 +474,9 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
                      CU_TENSOR_MAP_SWIZZLE_NONE))
         return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: tensor map encoding failed");
 
-    int stages = (227 * 1024 - 2048) / F::STAGE;
-    if (stages > 8) stages = 8;
-    if (stages < 2) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: prefill stage too large");
+    static_assert(F::W_STAGES >= 4 && F::SMEM <= 227 * 1024, "prefill stages do not fit");
     PairLaunch pl;
-    if ((st = pair_config<BITS>(ctx, 2048 + stages * F::STAGE, &pl)) != Q38_OK) return st;
+    if ((st = pair_config<BITS>(ctx, F::SMEM, &pl)) != Q38_OK) return st;
 
     const int nR = (N + 2 * P_ROWS - 1) / (2 * P_ROWS), nT = (M + P_TOK - 1) / P_TOK;
     const int ntiles = nR * nT;
@@ -500,7 +508,6 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
     args.K = K;
     args.nR = nR;
     args.ntiles = ntiles;
-    args.stages = stages;
     args.has_bias = b != nullptr;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
