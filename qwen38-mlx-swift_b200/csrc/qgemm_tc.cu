@@ -8,16 +8,20 @@
 // tiles.  The pair's MMA is tcgen05.mma.cta_group::2 with M = 256 weight rows (128 in
 // each CTA's TMEM) and N = 256 tokens (128 staged in each CTA's shared memory), so every
 // byte a CTA stages feeds twice the math of a single-CTA 128x128 tile.  Roles per CTA:
-//   warp 0      TMA producer: per 128-k stage, the CTA's 128 tokens of activations (two
-//               128-byte-swizzled 64-element boxes, completion counted on the leader's
-//               barrier), its 128 weight rows' packed codes and 8-group scale/bias boxes.
+//   warp 0      activation producer: per 128-k stage, the CTA's 128 tokens of permuted
+//               activations (two 128-byte-swizzled 64-element TMA boxes) into a 5-deep
+//               ring, completion counted on the pair leader's barrier.
 //   warp 1      allocates the pair's TMEM; in the leader, issues the pair MMAs (A = the
 //               dequantized weights in TMEM, B = activations in shared memory, D in TMEM).
-//   warps 2-5   dequantize: one thread per weight row turns its 128 codes per stage into
-//               exact bf16 weights w = scale*q + bias (magic-number extraction, bf16x2
-//               subtract and fused multiply-add, one rounding) and stores them into a TMEM
-//               operand slot with tcgen05.st -- the weights never pass through shared memory.
-//   warps 6-13  epilogue: two warps per TMEM lane quarter drain the finished accumulator
+//   warp 2      weight producer: the CTA's 128 weight rows' packed codes (swizzled box) and
+//               8-group scale/bias boxes into a separate ring, so the small weight stages
+//               run ahead of the large activation stages.
+//   warps 3-10  dequantize, two sets of four alternating stages: one thread per weight row
+//               turns its 128 codes per stage into exact bf16 weights w = scale*q + bias
+//               (magic-number extraction, bf16x2 subtract and fused multiply-add, one
+//               rounding) and stores them into a TMEM operand slot with tcgen05.st -- the
+//               weights never pass through shared memory.
+//   warps 11-18 epilogue: two warps per TMEM lane quarter drain the finished accumulator
 //               (128 rows x 256 tokens per CTA), convert to bf16 and store.
 // The extraction yields codes in a fixed permuted order, some pre-multiplied by 2^p; the
 // prologue kernel writes the activations permuted and scaled by 2^-p to match, so the
@@ -36,7 +40,7 @@ constexpr int P_KS = 128;      // k per stage (2 groups)
 constexpr int P_ASLOTS = 4;    // TMEM weight-operand slots, 64 columns each (columns 0-255)
 constexpr uint32_t P_DCOL = 256;  // accumulator: columns 256-511, one per token of the tile
 constexpr int P_DEQ_WARPS = 8;  // two sets of four (one warp per TMEM lane quarter), alternate stages
-constexpr int P_EPI_WARPS = 4;
+constexpr int P_EPI_WARPS = 8;  // two per TMEM lane quarter, one per half of the tile's tokens
 constexpr int P_WARP_DEQ0 = 3, P_WARP_EPI0 = P_WARP_DEQ0 + P_DEQ_WARPS;
 constexpr int P_THREADS = (P_WARP_EPI0 + P_EPI_WARPS) * 32;
 constexpr uint32_t P_IDESC = idesc_bf16_f32(2 * P_ROWS, P_TOK);
@@ -357,21 +361,22 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
         const uint32_t a_full_leader = mapa_shared(a_full, 0);
         for (int gs = set; gs < total; gs += 2) {
             const int slot = gs % SW, as = gs % P_ASLOTS, ks = gs % ksteps;
-            if (!p_wait_warp<false>(&w_full[slot], (gs / SW) & 1, ab) ||
-                (gs >= P_ASLOTS && !p_wait_warp<false>(&a_free[as], ((gs / P_ASLOTS) - 1) & 1, ab)))
-                break;
-            tc_fence_after();
+            if (!p_wait_warp<false>(&w_full[slot], (gs / SW) & 1, ab)) break;
+            // Dequantize into registers first: the TMEM slot is waited for only afterwards,
+            // so the arithmetic overlaps the MMAs that still read the slot.
             const uint8_t* st = wring + slot * F::W_STAGE;
             const uint32_t* sb = reinterpret_cast<const uint32_t*>(st + F::CODE_B);
             const uint32_t s01 = sb[row * 4 + (ks & 3)];
             const uint32_t b01 = a.has_bias ? sb[512 + row * 4 + (ks & 3)] : 0u;
-            uint32_t av[32];
-            dequant_group<BITS>(st, row, 0, s01 & 0xFFFFu, b01 & 0xFFFFu, av);
-            tmem_st32(tmem + lane_off + as * 64, av);
-            dequant_group<BITS>(st, row, 1, s01 >> 16, b01 >> 16, av);
+            uint32_t av0[32], av1[32];
+            dequant_group<BITS>(st, row, 0, s01 & 0xFFFFu, b01 & 0xFFFFu, av0);
+            dequant_group<BITS>(st, row, 1, s01 >> 16, b01 >> 16, av1);
             __syncwarp();
             if (lane == 0) mbar_arrive(&w_empty[slot]);  // codes read; the slot may refill
-            tmem_st32(tmem + lane_off + as * 64 + 32, av);
+            if (gs >= P_ASLOTS && !p_wait_warp<false>(&a_free[as], ((gs / P_ASLOTS) - 1) & 1, ab)) break;
+            tc_fence_after();
+            tmem_st32(tmem + lane_off + as * 64, av0);
+            tmem_st32(tmem + lane_off + as * 64 + 32, av1);
             tc_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -379,7 +384,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
         }
     } else {
         // ---------------------------------------------------------------- epilogue
-        const int quarter = warp & 3;
+        const int quarter = warp & 3, half = (warp - P_WARP_EPI0) >> 2;
         const int row = quarter * 32 + lane;
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
         const uint32_t d_free_leader = mapa_shared(d_free, 0);
@@ -388,11 +393,11 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
             tc_fence_after();
             const int tile = pair + tc * npairs;
             const int n = (tile % a.nR) * (2 * P_ROWS) + rank * P_ROWS + row;
-            const int m0 = (tile / a.nR) * P_TOK;
+            const int m0 = (tile / a.nR) * P_TOK + half * (P_TOK / 2);
 #pragma unroll 1
-            for (int ch = 0; ch < P_TOK / 32; ++ch) {
+            for (int ch = 0; ch < P_TOK / 64; ++ch) {
                 float v[32];
-                tmem_ld32(tmem + lane_off + P_DCOL + ch * 32, v);
+                tmem_ld32(tmem + lane_off + P_DCOL + half * (P_TOK / 2) + ch * 32, v);
                 const int mc = m0 + ch * 32;
                 const int mlim = n < a.N ? min(32, a.M - mc) : 0;
                 __nv_bfloat16* out = a.y + static_cast<size_t>(mc) * a.N + n;
