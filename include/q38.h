@@ -159,6 +159,50 @@ Q38_API q38_status q38_hadamard_quantized_matmul(q38_ctx* ctx, const void* x, in
                                          const void* biases, q38_dtype scales_dtype, int64_t N,
                                          int group_size, int bits, void* y);
 
+/* ------------------------------------------------------------------ sparse MoE layer
+ * Replaces the pieces of Qwen4ExpSparseMoE.callAsFunction
+ * (Sources/Qwen38Core/FlashNext/Qwen4ExpSparseMoE.swift:275-294): the router (gate Linear,
+ * softmax(precise:), argPartition, takeAlong, renormalisation, :208-214 and :275-281), the
+ * SwitchGLU's sort of (token, slot) pairs by expert, and SwitchGLU + weightedExpertSum
+ * (:294, built at :225-232) over QuantizedSwitchLinear gate/up/down projections
+ * (Vendor/mlx-swift-lm-local.patch:184-218). */
+
+/* Router: logits = bf16(x . wr^T) (fp32 accumulation), probs = bf16(softmax_fp32(logits)),
+ * the top_k experts per token in canonical order (probability descending, expert id
+ * ascending on ties), scores = probs[indices], divided by bf16(sum of the k scores) when
+ * normalize != 0.  x bf16 [T, H], wr bf16 [E, H] (H % 64 == 0, E <= 1024, top_k <= 32);
+ * indices int32 [T, top_k]; scores bf16 [T, top_k]; probs bf16 [T, E] or NULL. */
+Q38_API q38_status q38_moe_route(q38_ctx* ctx, const void* x, int64_t T, int64_t H, q38_dtype x_dtype,
+                                 const void* wr, int64_t E, int top_k, int normalize, int32_t* indices,
+                                 void* scores, void* probs);
+
+/* The same selection from given bf16 logits [T, E]. */
+Q38_API q38_status q38_moe_route_logits(q38_ctx* ctx, const void* logits, int64_t T, int64_t E, int top_k,
+                                        int normalize, int32_t* indices, void* scores, void* probs);
+
+/* Stable sort of the `pairs` flat (token, slot) entries of `indices` by expert:
+ * perm[j] = flat index of the j-th pair in expert order (pairs of one expert in flat
+ * order), offsets[E + 1] = start of each expert's run (offsets[E] = number of valid pairs).
+ * Indices outside [0, E) are placed after all experts and reported by
+ * q38_ctx_check_device as an invalid argument. */
+Q38_API q38_status q38_moe_sort(q38_ctx* ctx, const int32_t* indices, int64_t pairs, int64_t E, int32_t* perm,
+                                int32_t* offsets);
+
+/* SwitchGLU + weightedExpertSum: for every token t and slot s with expert e = indices[t, s]
+ *   g = bf16(x_t . Wg[e]^T), u = bf16(x_t . Wu[e]^T), h = bf16(silu(g) * u),
+ *   y_ts = bf16(h . Wd[e]^T), out_t = bf16(sum_s scores[t, s] * y_ts).
+ * x bf16 [T, H]; indices int32 / scores bf16 [T, top_k]; gate/up codes [E, I, H*bits/32],
+ * scales/biases bf16 [E, I, H/64]; down codes [E, H, I*bits/32], scales/biases
+ * [E, H, I/64]; out bf16 [T, H].  Biases are given for all three projections or none.
+ * Implemented for group 64, bits 2/3/4, H % 512 == 0, I % 512 == 0, E <= 1024.  Uses the
+ * context's activation buffer (about T*top_k*(2H + I)*2 bytes). */
+Q38_API q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int64_t I, int64_t E,
+                                  int top_k, const int32_t* indices, const void* scores,
+                                  const uint32_t* gate_w, const void* gate_scales, const void* gate_biases,
+                                  const uint32_t* up_w, const void* up_scales, const void* up_biases,
+                                  const uint32_t* down_w, const void* down_scales, const void* down_biases,
+                                  q38_dtype dtype, int group_size, int bits, void* out);
+
 /* Allocation-free decode product.  No counterpart in the reference: it exists for
  * callers that must not allocate device memory on the calling path (a host framework
  * that owns all device memory and hands a plugin only its input and output buffers, or

@@ -1,0 +1,682 @@
+// The sparse-MoE layer of Flash-Next (Qwen4ExpSparseMoE.callAsFunction,
+// Sources/Qwen38Core/FlashNext/Qwen4ExpSparseMoE.swift:275-294): router, expert sort and
+// SwitchGLU with the score-weighted combine.
+//
+//   router   logits = bf16(x . Wr^T) (fp32 accumulation; CUDA cores for a few tokens, a
+//            tcgen05 GEMM for prompts), probs = bf16(softmax_fp32(logits)), top-k in the
+//            canonical order (probability descending, expert id ascending on ties),
+//            scores = probs[idx] renormalised by bf16(sum) when asked (:208-214, :275-281).
+//            The softmax fixes its arithmetic: exp by Cody-Waite reduction and a degree-7
+//            Taylor polynomial (fused multiply-adds), the sum as 32 per-lane strided sums
+//            folded by a butterfly, IEEE division -- so equal logits give bit-equal
+//            probabilities, indices and scores on any implementation that follows it.
+//   sort     stable counting sort of the T*k (token, slot) pairs by expert: perm, per-expert
+//            offsets and the inverse permutation (SwitchGLU's sort by expert).
+//   SwitchGLU per pair down(silu(gate(x)) * up(x)) on the selected expert, as grouped
+//            tcgen05 products over expert-sorted pairs (qgemm_grouped.cu), then
+//            out_t = bf16(sum_k score_tk * y_tk) in slot order.
+#include <algorithm>
+#include <mutex>
+
+#include "moe_internal.h"
+#include "tc_pipeline.cuh"
+
+namespace q38 {
+namespace {
+
+// ------------------------------------------------------------------------- router
+// exp(x) for x <= 0: n = rint(x log2 e), r = x - n ln2 (ln2 split in a high part with
+// trailing zero bits and a low part), e^r by its Taylor polynomial to degree 7 in Horner
+// form with fused multiply-adds, times 2^n; 0 below -87.
+__device__ __forceinline__ float router_exp(float x) {
+    if (x < -87.0f) return 0.0f;
+    const float n = rintf(x * 1.44269504088896341f);
+    float r = __fmaf_rn(-n, 0.693145751953125f, x);
+    r = __fmaf_rn(-n, 1.42860682030941723e-6f, r);
+    float p = 1.0f / 5040.0f;
+    p = __fmaf_rn(p, r, 1.0f / 720.0f);
+    p = __fmaf_rn(p, r, 1.0f / 120.0f);
+    p = __fmaf_rn(p, r, 1.0f / 24.0f);
+    p = __fmaf_rn(p, r, 1.0f / 6.0f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    const int ni = static_cast<int>(n);
+    return __fmul_rn(p, __uint_as_float(static_cast<uint32_t>(ni + 127) << 23));
+}
+
+// logits for a few tokens on CUDA cores: block = 8 warps x 4 experts, 8 tokens staged in
+// shared memory; each lane accumulates 8-element slices, the warp reduces.
+__global__ void __launch_bounds__(256) router_logits_small(const __nv_bfloat16* __restrict__ x, int T, int H,
+                                                           const __nv_bfloat16* __restrict__ wr, int E,
+                                                           __nv_bfloat16* __restrict__ logits) {
+    extern __shared__ uint4 xs4[];
+    const int t0 = blockIdx.y * 8;
+    const int nt = min(8, T - t0);
+    const int vec = H / 8;
+    for (int i = threadIdx.x; i < 8 * vec; i += 256) {
+        const int t = i / vec;
+        xs4[i] = t < nt ? reinterpret_cast<const uint4*>(x + static_cast<size_t>(t0 + t) * H)[i % vec]
+                        : make_uint4(0, 0, 0, 0);
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int e0 = blockIdx.x * 32 + warp * 4;
+    float acc[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int t = 0; t < 8; ++t) acc[i][t] = 0.0f;
+    for (int v = lane; v < vec; v += 32) {
+        float wv[4][8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int e = min(e0 + i, E - 1);
+            const uint4 u = reinterpret_cast<const uint4*>(wr + static_cast<size_t>(e) * H)[v];
+            const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                wv[i][2 * j] = bf16_bits_to_f32(q[j] & 0xFFFFu);
+                wv[i][2 * j + 1] = bf16_bits_to_f32(q[j] >> 16);
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const uint4 u = xs4[t * vec + v];
+            const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+            float xv[8];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                xv[2 * j] = bf16_bits_to_f32(q[j] & 0xFFFFu);
+                xv[2 * j + 1] = bf16_bits_to_f32(q[j] >> 16);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][t] = fmaf(wv[i][j], xv[j], acc[i][t]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            float v = acc[i][t];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0 && t < nt && e0 + i < E)
+                logits[static_cast<size_t>(t0 + t) * E + e0 + i] = __float2bfloat16_rn(v);
+        }
+}
+
+// logits for prompts on the tensor cores: one CTA per 128 tokens x 256 experts, both
+// operands TMA-loaded with the 128-byte swizzle (64-element k boxes, 4-stage ring), the
+// fp32 accumulator in TMEM, four warps drain it.
+constexpr int R_STAGES = 4;
+constexpr int R_A = 128 * 128, R_B = 256 * 128;
+
+__global__ void __launch_bounds__(128, 1) router_logits_tc(const __grid_constant__ CUtensorMap map_x,
+                                                           const __grid_constant__ CUtensorMap map_w, int T, int H,
+                                                           int E, __nv_bfloat16* __restrict__ logits,
+                                                           uint32_t* status) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + R_STAGES;
+    uint64_t* done = empty + R_STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint8_t* ring = smem + 1024;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t0 = blockIdx.x * 128, e0 = blockIdx.y * 256;
+    const int ksteps = H / 64;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < R_STAGES; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_init(done, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 256);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool ok = true;
+    if (warp == 0 && lane == 0) {
+        for (int ks = 0; ks < ksteps; ++ks) {
+            const int s = ks % R_STAGES;
+            if (ks >= R_STAGES && !mbar_wait(&empty[s], ((ks / R_STAGES) - 1) & 1, status)) break;
+            uint8_t* st = ring + s * (R_A + R_B);
+            mbar_arrive_expect_tx(&full[s], R_A + R_B);
+            tma_load_2d(st, &map_x, &full[s], ks * 64, t0);
+            tma_load_2d(st + R_A, &map_w, &full[s], ks * 64, e0);
+        }
+    } else if (warp == 1 && lane == 0) {
+        const uint32_t idesc = idesc_bf16_f32(128, 256);
+        for (int ks = 0; ks < ksteps && ok; ++ks) {
+            const int s = ks % R_STAGES;
+            if (!mbar_wait(&full[s], (ks / R_STAGES) & 1, status)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t a = smem_u32(ring + s * (R_A + R_B));
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+                tc_mma_ss(tmem, smem_desc(a + kk * 32, 16, 1024, 2), smem_desc(a + R_A + kk * 32, 16, 1024, 2), idesc,
+                          (ks > 0 || kk > 0) ? 1u : 0u);
+            tc_commit(&empty[s]);
+        }
+        tc_commit(done);
+    }
+    __syncwarp();
+    // all four warps: wait for the accumulator, drain 128 tokens x 256 experts
+    const bool got = mbar_wait(done, 0, status);
+    tc_fence_after();
+    const int t = t0 + warp * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+#pragma unroll 1
+    for (int ch = 0; ch < 8; ++ch) {
+        float v[32];
+        tmem_ld32(tmem + lane_off + ch * 32, v);
+        if (got && t < T) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const int e = e0 + ch * 32 + i;
+                if (e < E) logits[static_cast<size_t>(t) * E + e] = __float2bfloat16_rn(v[i]);
+            }
+        }
+    }
+    // drain outstanding loads before the CTA exits (only matters after a timeout)
+    if (warp == 0 && lane == 0)
+        for (int ks = max(0, ksteps - R_STAGES); ks < ksteps; ++ks)
+            mbar_wait(&full[ks % R_STAGES], (ks / R_STAGES) & 1, status);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, 256);
+}
+
+// softmax + top-k, one warp per token; lane l holds experts l, l+32, ...
+constexpr int R_MAXJ = 32;  // E <= 1024
+
+__global__ void __launch_bounds__(256) router_topk(const __nv_bfloat16* __restrict__ logits, int T, int E,
+                                                   int top_k, int normalize, int32_t* __restrict__ indices,
+                                                   __nv_bfloat16* __restrict__ scores,
+                                                   __nv_bfloat16* __restrict__ probs) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 8 + warp;
+    if (t >= T) return;
+    const uint16_t* l = reinterpret_cast<const uint16_t*>(logits) + static_cast<size_t>(t) * E;
+    const int nj = (E + 31) / 32;
+    float v[R_MAXJ];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < R_MAXJ; ++j) {
+        const int e = lane + 32 * j;
+        v[j] = (j < nj && e < E) ? bf16_bits_to_f32(l[e]) : -INFINITY;
+        mx = fmaxf(mx, v[j]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float part = 0.0f;
+#pragma unroll
+    for (int j = 0; j < R_MAXJ; ++j) {
+        const int e = lane + 32 * j;
+        if (j < nj && e < E) {
+            v[j] = router_exp(__fsub_rn(v[j], mx));
+            part = __fadd_rn(part, v[j]);
+        } else {
+            v[j] = -1.0f;  // never selected: probabilities are >= 0
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, o));
+    uint32_t taken = 0;
+#pragma unroll
+    for (int j = 0; j < R_MAXJ; ++j) {
+        const int e = lane + 32 * j;
+        if (j < nj && e < E) {
+            const uint16_t pb = f32_to_bf16_bits(__fdiv_rn(v[j], part));
+            v[j] = bf16_bits_to_f32(pb);
+            if (probs) reinterpret_cast<uint16_t*>(probs)[static_cast<size_t>(t) * E + e] = pb;
+        }
+    }
+    float ssum = 0.0f;
+    float sel[32];
+    int selidx[32];
+    for (int r = 0; r < top_k; ++r) {
+        float bv = -2.0f;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < R_MAXJ; ++j)
+            if (!((taken >> j) & 1u) && v[j] > bv) {  // first maximum = lowest id in this lane
+                bv = v[j];
+                bi = lane + 32 * j;
+            }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+        sel[r] = bv;
+        selidx[r] = bi;
+        ssum = __fadd_rn(ssum, bv);
+    }
+    if (lane == 0) {
+        const float denom = bf16_bits_to_f32(f32_to_bf16_bits(ssum));
+        for (int r = 0; r < top_k; ++r) {
+            indices[static_cast<size_t>(t) * top_k + r] = selidx[r];
+            const float sc = normalize ? __fdiv_rn(sel[r], denom) : sel[r];
+            scores[static_cast<size_t>(t) * top_k + r] = __float2bfloat16_rn(sc);
+        }
+    }
+}
+
+// --------------------------------------------------------------------------- sort
+// One block of 32 warps.  Warp w owns a contiguous segment of the pairs; per-warp,
+// per-expert counts give every (warp, expert) run its start, then each warp places its
+// pairs in order -- a stable counting sort.  Indices outside [0, E) are counted in an
+// extra bucket E after all experts and flagged.
+__global__ void __launch_bounds__(1024, 1) moe_sort_kernel(const int32_t* __restrict__ idx, int P, int E,
+                                                           int32_t* __restrict__ perm, int32_t* __restrict__ offsets,
+                                                           int32_t* __restrict__ inv, uint32_t* status) {
+    extern __shared__ int32_t cnt[];  // [32][E + 1]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int B = E + 1;
+    for (int i = threadIdx.x; i < 32 * B; i += 1024) cnt[i] = 0;
+    __syncthreads();
+    const int seg = (P + 31) / 32;
+    const int s0 = warp * seg, s1 = min(P, s0 + seg);
+    for (int base = s0; base < s1; base += 32) {
+        const int p = base + lane;
+        const bool act = p < s1;
+        int e = act ? idx[p] : -1;
+        if (act && (e < 0 || e >= E)) {
+            atomicOr(status, Q38_DEV_BAD_INDEX);
+            e = E;
+        }
+        const unsigned am = __ballot_sync(0xffffffffu, act);
+        if (act) {
+            const unsigned m = __match_any_sync(am, e);
+            if ((__ffs(m) - 1) == lane) cnt[warp * B + e] += __popc(m);
+        }
+        __syncwarp();
+    }
+    __syncthreads();
+    // per expert: exclusive prefix over warps, total
+    for (int e = threadIdx.x; e < B; e += 1024) {
+        int run = 0;
+        for (int w = 0; w < 32; ++w) {
+            const int c = cnt[w * B + e];
+            cnt[w * B + e] = run;
+            run += c;
+        }
+        inv[e] = run;  // scratch: totals (inv is rewritten below)
+    }
+    __syncthreads();
+    if (warp == 0) {  // exclusive scan of the totals over experts, 32 at a time
+        int carry = 0;
+        for (int b0 = 0; b0 < B; b0 += 32) {
+            const int e = b0 + lane;
+            const int v = e < B ? inv[e] : 0;
+            int incl = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int n = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += n;
+            }
+            if (e < B) offsets[e] = carry + incl - v;
+            carry += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (lane == 0) offsets[B] = carry;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 32 * B; i += 1024) cnt[i] += offsets[i % B];
+    __syncthreads();
+    for (int base = s0; base < s1; base += 32) {
+        const int p = base + lane;
+        const bool act = p < s1;
+        int e = act ? idx[p] : -1;
+        if (act && (e < 0 || e >= E)) e = E;
+        const unsigned am = __ballot_sync(0xffffffffu, act);
+        if (act) {
+            const unsigned m = __match_any_sync(am, e);
+            const int pos = cnt[warp * B + e] + __popc(m & ((1u << lane) - 1u));
+            perm[pos] = p;
+            inv[p] = pos;
+            __syncwarp(am);
+            if ((__ffs(m) - 1) == lane) cnt[warp * B + e] += __popc(m);
+        }
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------- tile lists
+// Per expert: ceil(n_e / 128) runs of pairs, each crossed with the row blocks of the
+// gate/up (I / 64) and down (H / 128) products.
+__global__ void __launch_bounds__(1024, 1) moe_tiles_kernel(const int32_t* __restrict__ offsets, int E,
+                                                            int rb_gu, int rb_d, MoeTile* __restrict__ gu,
+                                                            MoeTile* __restrict__ dn, int* __restrict__ counts) {
+    __shared__ int warp_tot[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int e = threadIdx.x;  // E <= 1024: one expert per thread
+    const int n = e < E ? offsets[e + 1] - offsets[e] : 0;
+    const int runs = (n + 127) / 128;
+    int incl = runs;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        const int w = warp_tot[lane];
+        int wi = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, wi, o);
+            if (lane >= o) wi += v;
+        }
+        warp_tot[lane] = wi - w;  // exclusive warp offsets
+        if (lane == 31) {
+            counts[0] = wi * rb_gu;
+            counts[1] = wi * rb_d;
+        }
+    }
+    __syncthreads();
+    const int base = warp_tot[warp] + incl - runs;
+    for (int r = 0; r < runs; ++r) {
+        const int p0 = offsets[e] + r * 128, np = min(128, n - r * 128);
+        for (int b = 0; b < rb_gu; ++b) gu[(base + r) * rb_gu + b] = MoeTile{e, b, p0, np};
+        for (int b = 0; b < rb_d; ++b) dn[(base + r) * rb_d + b] = MoeTile{e, b, p0, np};
+    }
+}
+
+// ------------------------------------------------------------------------ combine
+// out[t] = bf16(sum_k score[t,k] * y[inv[t*k + k']]) in slot order (fp32).
+__global__ void __launch_bounds__(256) moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int H,
+                                                          const int32_t* __restrict__ inv,
+                                                          const int32_t* __restrict__ idx,
+                                                          const __nv_bfloat16* __restrict__ scores, int top_k, int E,
+                                                          __nv_bfloat16* __restrict__ out) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const int t = blockIdx.x;
+    for (int c = threadIdx.x * 8; c < H; c += 256 * 8) {
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int s = 0; s < top_k; ++s) {
+            const int p = t * top_k + s;
+            const int e = idx[p];
+            if (e < 0 || e >= E) continue;
+            const float sc = __bfloat162float(scores[p]);
+            const uint4 u = *reinterpret_cast<const uint4*>(y + static_cast<size_t>(inv[p]) * H + c);
+            const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                acc[2 * j] = __fadd_rn(acc[2 * j], __fmul_rn(sc, bf16_bits_to_f32(q[j] & 0xFFFFu)));
+                acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], __fmul_rn(sc, bf16_bits_to_f32(q[j] >> 16)));
+            }
+        }
+        uint4 o;
+        o.x = pack_bf16x2(acc[0], acc[1]);
+        o.y = pack_bf16x2(acc[2], acc[3]);
+        o.z = pack_bf16x2(acc[4], acc[5]);
+        o.w = pack_bf16x2(acc[6], acc[7]);
+        *reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H + c) = o;
+    }
+}
+
+q38_status set_dev(q38_ctx* ctx) {
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return check_launch(ctx, "cudaSetDevice");
+    return Q38_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+q38_status topk_launch(q38_ctx* ctx, const void* logits, int64_t T, int64_t E, int top_k, int normalize,
+                       int32_t* indices, void* scores, void* probs) {
+    router_topk<<<static_cast<unsigned>((T + 7) / 8), 256, 0, ctx->stream>>>(
+        static_cast<const __nv_bfloat16*>(logits), static_cast<int>(T), static_cast<int>(E), top_k, normalize, indices,
+        static_cast<__nv_bfloat16*>(scores), static_cast<__nv_bfloat16*>(probs));
+    return check_launch(ctx, "router_topk");
+}
+
+q38_status logits_launch(q38_ctx* ctx, const void* x, int64_t T, int64_t H, const void* wr, int64_t E, void* logits) {
+    if (T <= 64) {
+        const size_t sm = static_cast<size_t>(16) * H;
+        static std::mutex mu;
+        static bool big[64] = {};
+        if (sm > 48 * 1024) {
+            std::lock_guard<std::mutex> lk(mu);
+            if (ctx->device < 64 && !big[ctx->device]) {
+                if (cudaFuncSetAttribute(router_logits_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         200 * 1024) != cudaSuccess)
+                    return check_launch(ctx, "cudaFuncSetAttribute");
+                big[ctx->device] = true;
+            }
+        }
+        dim3 grid(static_cast<unsigned>((E + 31) / 32), static_cast<unsigned>((T + 7) / 8));
+        router_logits_small<<<grid, 256, sm, ctx->stream>>>(static_cast<const __nv_bfloat16*>(x), static_cast<int>(T),
+                                                            static_cast<int>(H), static_cast<const __nv_bfloat16*>(wr),
+                                                            static_cast<int>(E), static_cast<__nv_bfloat16*>(logits));
+        return check_launch(ctx, "router_logits_small");
+    }
+    CUtensorMap mx, mw;
+    if (!make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, H, T, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, wr, H, E, 64, 256, CU_TENSOR_MAP_SWIZZLE_128B))
+        return fail(ctx, Q38_ERR_CUDA, "moe_route: tensor map encoding failed");
+    const int smem = 2048 + R_STAGES * (R_A + R_B);
+    static std::mutex mu2;
+    static bool cfg[64] = {};
+    {
+        std::lock_guard<std::mutex> lk(mu2);
+        if (ctx->device < 64 && !cfg[ctx->device]) {
+            if (cudaFuncSetAttribute(router_logits_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+                return check_launch(ctx, "cudaFuncSetAttribute");
+            cfg[ctx->device] = true;
+        }
+    }
+    dim3 grid(static_cast<unsigned>((T + 127) / 128), static_cast<unsigned>((E + 255) / 256));
+    router_logits_tc<<<grid, 128, smem, ctx->stream>>>(mx, mw, static_cast<int>(T), static_cast<int>(H),
+                                                      static_cast<int>(E), static_cast<__nv_bfloat16*>(logits),
+                                                      ctx->d_status);
+    return check_launch(ctx, "router_logits_tc");
+}
+
+q38_status sort_launch(q38_ctx* ctx, const int32_t* idx, int64_t P, int64_t E, int32_t* perm, int32_t* offsets,
+                       int32_t* inv) {
+    const size_t sm = static_cast<size_t>(32) * (E + 1) * 4;
+    static std::mutex mu;
+    static bool cfg[64] = {};
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (ctx->device < 64 && !cfg[ctx->device]) {
+            if (cudaFuncSetAttribute(moe_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024) !=
+                cudaSuccess)
+                return check_launch(ctx, "cudaFuncSetAttribute");
+            cfg[ctx->device] = true;
+        }
+    }
+    moe_sort_kernel<<<1, 1024, sm, ctx->stream>>>(idx, static_cast<int>(P), static_cast<int>(E), perm, offsets, inv,
+                                                  ctx->d_status);
+    return check_launch(ctx, "moe_sort");
+}
+
+}  // namespace
+}  // namespace q38
+
+using namespace q38;
+
+extern "C" {
+
+q38_status q38_moe_route(q38_ctx* ctx, const void* x, int64_t T, int64_t H, q38_dtype x_dtype, const void* wr,
+                         int64_t E, int top_k, int normalize, int32_t* indices, void* scores, void* probs) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    if (x_dtype != Q38_BF16) return fail(ctx, Q38_ERR_UNSUPPORTED, "moe_route: x and the router weight must be bf16");
+    if (T < 0 || H <= 0 || H % 64 || E < 1 || E > 1024 || top_k < 1 || top_k > 32 || top_k > E)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT,
+                    "moe_route: need H %% 64 == 0, 1 <= E <= 1024, 1 <= top_k <= min(32, E) (H=%lld E=%lld k=%d)",
+                    (long long)H, (long long)E, top_k);
+    if (T == 0) return Q38_OK;
+    if (!x || !wr || !indices || !scores) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_route: null pointer");
+    if (!aligned16(x) || !aligned16(wr)) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_route: x and wr must be 16-byte aligned");
+    q38_status st = set_dev(ctx);
+    if (st != Q38_OK) return st;
+    if ((st = ensure_workspace(ctx, static_cast<size_t>(T) * E * 2)) != Q38_OK) return st;
+    void* logits = ctx->workspace;
+    if ((st = logits_launch(ctx, x, T, H, wr, E, logits)) != Q38_OK) return st;
+    return topk_launch(ctx, logits, T, E, top_k, normalize, indices, scores, probs);
+}
+
+q38_status q38_moe_route_logits(q38_ctx* ctx, const void* logits, int64_t T, int64_t E, int top_k, int normalize,
+                                int32_t* indices, void* scores, void* probs) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    if (T < 0 || E < 1 || E > 1024 || top_k < 1 || top_k > 32 || top_k > E)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_route_logits: need 1 <= E <= 1024, 1 <= top_k <= min(32, E)");
+    if (T == 0) return Q38_OK;
+    if (!logits || !indices || !scores) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_route_logits: null pointer");
+    q38_status st = set_dev(ctx);
+    if (st != Q38_OK) return st;
+    return topk_launch(ctx, logits, T, E, top_k, normalize, indices, scores, probs);
+}
+
+q38_status q38_moe_sort(q38_ctx* ctx, const int32_t* indices, int64_t pairs, int64_t E, int32_t* perm,
+                        int32_t* offsets) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    if (pairs < 0 || pairs > (1 << 30) || E < 1 || E > 1024)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_sort: need 1 <= E <= 1024");
+    if (!indices || !perm || !offsets) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_sort: null pointer");
+    q38_status st = set_dev(ctx);
+    if (st != Q38_OK) return st;
+    // offsets has E + 1 entries for the caller; the kernel also writes a bad-index bucket
+    void* scratch;
+    const size_t inv_bytes = align_up(static_cast<size_t>(std::max<int64_t>(pairs, E + 2)) * 4, 256);
+    if ((st = ensure_aux(ctx, inv_bytes + align_up(static_cast<size_t>(E + 2) * 4, 256), &scratch)) != Q38_OK)
+        return st;
+    int32_t* inv = static_cast<int32_t*>(scratch);
+    int32_t* off2 = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(scratch) + inv_bytes);
+    if ((st = sort_launch(ctx, indices, pairs, E, perm, off2, inv)) != Q38_OK) return st;
+    if (cudaMemcpyAsync(offsets, off2, static_cast<size_t>(E + 1) * 4, cudaMemcpyDeviceToDevice, ctx->stream) !=
+        cudaSuccess)
+        return check_launch(ctx, "moe_sort offsets");
+    return Q38_OK;
+}
+
+q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int64_t I, int64_t E, int top_k,
+                          const int32_t* indices, const void* scores, const uint32_t* gate_w, const void* gate_s,
+                          const void* gate_b, const uint32_t* up_w, const void* up_s, const void* up_b,
+                          const uint32_t* down_w, const void* down_s, const void* down_b, q38_dtype dtype,
+                          int group_size, int bits, void* out) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    if (dtype != Q38_BF16) return fail(ctx, Q38_ERR_UNSUPPORTED, "switch_glu: x, scales, biases and out must be bf16");
+    if (group_size != 64 || (bits != 2 && bits != 3 && bits != 4))
+        return fail(ctx, Q38_ERR_UNSUPPORTED, "switch_glu: implemented for group 64, bits 2/3/4 (got %d, %d)",
+                    group_size, bits);
+    if (T < 0 || H <= 0 || I <= 0 || H % 512 || I % 512 || E < 1 || E > 1024 || top_k < 1 || top_k > E)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT,
+                    "switch_glu: need H %% 512 == 0, I %% 512 == 0, 1 <= E <= 1024, 1 <= top_k <= E");
+    if ((gate_b == nullptr) != (up_b == nullptr) || (gate_b == nullptr) != (down_b == nullptr))
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "switch_glu: biases must be given for all three projections or none");
+    if (T == 0) return Q38_OK;
+    if (!x || !indices || !scores || !gate_w || !gate_s || !up_w || !up_s || !down_w || !down_s || !out)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "switch_glu: null pointer");
+    const int64_t P = T * top_k;
+    if (P > (1 << 24)) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "switch_glu: more than 2^24 (token, slot) pairs");
+    q38_status st = set_dev(ctx);
+    if (st != Q38_OK) return st;
+
+    const int rb_gu = static_cast<int>(I / 64), rb_d = static_cast<int>(H / 128);
+    const int64_t max_runs = std::min<int64_t>(E, P) + P / 128 + 1;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off += align_up(bytes, 256);
+        return o;
+    };
+    const size_t o_perm = take(P * 4), o_inv = take(std::max<int64_t>(P, E + 2) * 4), o_off = take((E + 2) * 4);
+    const size_t o_cnt = take(16), o_gu = take(max_runs * rb_gu * sizeof(MoeTile)),
+                 o_dn = take(max_runs * rb_d * sizeof(MoeTile));
+    const size_t o_xs = take(static_cast<size_t>(P) * H * 2), o_h = take(static_cast<size_t>(P) * I * 2),
+                 o_y = take(static_cast<size_t>(P) * H * 2);
+    void* base;
+    if ((st = ensure_aux(ctx, off, &base)) != Q38_OK) return st;
+    uint8_t* b8 = static_cast<uint8_t*>(base);
+    int32_t* perm = reinterpret_cast<int32_t*>(b8 + o_perm);
+    int32_t* inv = reinterpret_cast<int32_t*>(b8 + o_inv);
+    int32_t* offs = reinterpret_cast<int32_t*>(b8 + o_off);
+    int* counts = reinterpret_cast<int*>(b8 + o_cnt);
+    MoeTile* gu = reinterpret_cast<MoeTile*>(b8 + o_gu);
+    MoeTile* dn = reinterpret_cast<MoeTile*>(b8 + o_dn);
+    void* xs = b8 + o_xs;
+    void* hp = b8 + o_h;
+    void* y = b8 + o_y;
+
+    if ((st = sort_launch(ctx, indices, P, E, perm, offs, inv)) != Q38_OK) return st;
+    moe_tiles_kernel<<<1, 1024, 0, ctx->stream>>>(offs, static_cast<int>(E), rb_gu, rb_d, gu, dn, counts);
+    if ((st = check_launch(ctx, "moe_tiles")) != Q38_OK) return st;
+    if ((st = moe_gather_launch(ctx, x, static_cast<int>(H), perm, static_cast<int>(P), top_k, xs, bits)) != Q38_OK)
+        return st;
+    GroupedProblem g;
+    g.x = xs;
+    g.pairs = static_cast<int>(P);
+    g.K = static_cast<int>(H);
+    g.w0 = gate_w;
+    g.w1 = up_w;
+    g.s0 = gate_s;
+    g.s1 = up_s;
+    g.b0 = gate_b;
+    g.b1 = up_b;
+    g.E = static_cast<int>(E);
+    g.rows_per_expert = static_cast<int>(I);
+    g.tiles = gu;
+    g.ntiles = counts;
+    g.max_tiles = static_cast<int>(max_runs * rb_gu);
+    g.out = hp;
+    g.out_ld = static_cast<int>(I);
+    if ((st = grouped_gate_up(ctx, g, bits)) != Q38_OK) return st;
+    GroupedProblem d;
+    d.x = hp;
+    d.pairs = static_cast<int>(P);
+    d.K = static_cast<int>(I);
+    d.w0 = down_w;
+    d.w1 = down_w;
+    d.s0 = down_s;
+    d.s1 = down_s;
+    d.b0 = down_b;
+    d.b1 = down_b;
+    d.E = static_cast<int>(E);
+    d.rows_per_expert = static_cast<int>(H);
+    d.tiles = dn;
+    d.ntiles = counts + 1;
+    d.max_tiles = static_cast<int>(max_runs * rb_d);
+    d.out = y;
+    d.out_ld = static_cast<int>(H);
+    if ((st = grouped_down(ctx, d, bits)) != Q38_OK) return st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(T));
+    cfg.blockDim = dim3(256);
+    cfg.stream = ctx->stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, moe_combine_kernel, static_cast<const __nv_bfloat16*>(y), static_cast<int>(H),
+                           static_cast<const int32_t*>(inv), indices, static_cast<const __nv_bfloat16*>(scores), top_k,
+                           static_cast<int>(E), static_cast<__nv_bfloat16*>(out)) != cudaSuccess)
+        return check_launch(ctx, "moe_combine");
+    return check_launch(ctx, "moe_combine");
+}
+
+}  // extern "C"

@@ -28,7 +28,7 @@
 // products pair up exactly: sum_k' (2^p w_k)(2^-p x_k) = sum_k w_k x_k.
 #include <mutex>
 
-#include "affine_codes.cuh"
+#include "tc_pipeline.cuh"
 
 namespace q38 {
 namespace {
@@ -47,9 +47,8 @@ constexpr uint32_t P_IDESC = idesc_bf16_f32(2 * P_ROWS, P_TOK);
 
 template <int BITS>
 struct PF {
-    static constexpr int CODE_W = 4 * BITS;               // code words per row per stage
-    static constexpr int CODE_B = P_ROWS * CODE_W * 4;    // 4 / 6 / 8 KiB
-    static constexpr int SW = BITS == 2 ? 32 : BITS == 4 ? 64 : 0;  // code box swizzle span
+    static constexpr int CODE_W = CodeLayout<BITS>::CODE_W;  // code words per row per stage
+    static constexpr int CODE_B = P_ROWS * CODE_W * 4;       // 4 / 6 / 8 KiB
     static constexpr int X_B = 2 * P_HTOK * 128;          // two 64-element 128-byte-swizzled boxes
     static constexpr int SB_B = 2 * 2048;                 // scales + biases, {8 groups, 128 rows}
     static constexpr int W_STAGE = (CODE_B + SB_B + 1023) / 1024 * 1024;
@@ -59,10 +58,8 @@ struct PF {
     static constexpr int SMEM = 2048 + X_STAGES * X_B + W_STAGES * W_STAGE;
 };
 
-// ---------------------------------------------------------------------------------
 // Prologue: x' = activations permuted within each 64-group into extraction order and
-// scaled by 2^-p (slot k' = 2*col + half, col = quarter*8 + pair).
-// ---------------------------------------------------------------------------------
+// scaled by 2^-p, so that the dequantized weights pair with them in the MMA.
 template <int BITS>
 __global__ void __launch_bounds__(256) qgemm_prep(const __nv_bfloat16* __restrict__ x, int64_t M, int K,
                                                   __nv_bfloat16* __restrict__ xp) {
@@ -73,28 +70,7 @@ __global__ void __launch_bounds__(256) qgemm_prep(const __nv_bfloat16* __restric
     if (item >= M * G) return;
     const int64_t m = item / G;
     const int g = static_cast<int>(item % G);
-    const uint4* src = reinterpret_cast<const uint4*>(x + m * K + g * 64);
-    float xv[64];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const uint4 u = src[i];
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            xv[8 * i + 2 * j] = bf16_bits_to_f32(w[j] & 0xFFFFu);
-            xv[8 * i + 2 * j + 1] = bf16_bits_to_f32(w[j] >> 16);
-        }
-    }
-    uint32_t out[32];
-#pragma unroll
-    for (int col = 0; col < 32; ++col) {
-        const int tq = col / 8, q = col % 8;
-        out[col] = pack_bf16x2(xv[16 * tq + pair_code<BITS>(q, 0)] * pair_mult<BITS>(q, 0),
-                               xv[16 * tq + pair_code<BITS>(q, 1)] * pair_mult<BITS>(q, 1));
-    }
-    uint4* dst = reinterpret_cast<uint4*>(xp + m * K + g * 64);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) dst[i] = make_uint4(out[4 * i], out[4 * i + 1], out[4 * i + 2], out[4 * i + 3]);
+    permute_group<BITS>(x + m * K + g * 64, xp + m * K + g * 64);
 }
 
 struct PArgs {
@@ -102,116 +78,6 @@ struct PArgs {
     uint32_t* status;
     int M, N, K, nR, ntiles, has_bias;
 };
-
-// Bounded mbarrier wait.  On expiry records the timeout and raises the abort flag of both
-// CTAs of the pair, so every role of both leaves its loop at its next wait.
-struct Abort {
-    volatile int* local;
-    uint32_t peer;  // the other CTA's flag (cluster address)
-    uint32_t* status;
-};
-
-template <bool CLUSTER>
-__device__ __forceinline__ bool p_wait(uint64_t* bar, uint32_t parity, const Abort& ab) {
-    auto poll = [&]() { return CLUSTER ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity); };
-    if (poll()) return true;
-    const long long t0 = clock64();
-    while (!poll()) {
-        if (*ab.local) return false;
-        if (clock64() - t0 > kWaitLimitCycles) {
-            if (ab.status) atomicOr(ab.status, Q38_DEV_TIMEOUT);
-            *ab.local = 1;
-            st_shared_cluster_u32(ab.peer, 1u);
-            return false;
-        }
-    }
-    return true;
-}
-
-// Every lane waits (each observes the phase, so TMA-written data is visible to it); the
-// warp then agrees on the outcome so that the .sync.aligned TMEM accesses stay convergent.
-template <bool CLUSTER>
-__device__ __forceinline__ bool p_wait_warp(uint64_t* bar, uint32_t parity, const Abort& ab) {
-    const bool ok = p_wait<CLUSTER>(bar, parity, ab);
-    return __all_sync(0xffffffffu, ok);
-}
-
-__device__ __forceinline__ uint32_t bf2_sub(uint32_t a, uint32_t b) {
-    __nv_bfloat162 r = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&b));
-    return *reinterpret_cast<uint32_t*>(&r);
-}
-__device__ __forceinline__ uint32_t bf2_fma(uint32_t a, uint32_t b, uint32_t c) {
-    __nv_bfloat162 r = __hfma2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&b),
-                               *reinterpret_cast<__nv_bfloat162*>(&c));
-    return *reinterpret_cast<uint32_t*>(&r);
-}
-
-// Words of group gg (0/1) of the stage for this row -> exact bf16 weights (x 2^p) in
-// A-column order, 32 bf16x2 values.
-template <int BITS>
-__device__ __forceinline__ void dequant_group(const uint8_t* codes, int row, int gg, uint32_t sbits, uint32_t bbits,
-                                              uint32_t* a) {
-    using F = PF<BITS>;
-    constexpr int GW = 2 * BITS;  // words per row per group
-    uint32_t w[8];
-    if constexpr (BITS == 3) {
-        const uint2* p = reinterpret_cast<const uint2*>(codes + row * F::CODE_W * 4 + gg * GW * 4);
-#pragma unroll
-        for (int i = 0; i < 3; ++i) {
-            const uint2 v = p[i];
-            w[2 * i] = v.x;
-            w[2 * i + 1] = v.y;
-        }
-    } else {
-        constexpr int CPR = F::SW / 16;         // 16-byte chunks per code row
-        constexpr int GC = GW / 4;              // chunks per group: 1 (2-bit), 2 (4-bit)
-        const int swz = F::SW == 64 ? ((row >> 1) & 3) : ((row >> 2) & 1);
-#pragma unroll
-        for (int i = 0; i < GC; ++i) {
-            const int c = gg * GC + i;
-            const uint4 v = *reinterpret_cast<const uint4*>(codes + row * F::SW + (((c ^ swz) & (CPR - 1)) << 4));
-            w[4 * i] = v.x;
-            w[4 * i + 1] = v.y;
-            w[4 * i + 2] = v.z;
-            w[4 * i + 3] = v.w;
-        }
-    }
-    // s and 2^p b as bf16x2 with integer operations only: the scale broadcast, and the
-    // bias times a power of two, exact in fp32 and so exactly the bf16 in its high half.
-    const uint32_t s2 = sbits * 0x10001u;
-    const float bf = bf16_bits_to_f32(bbits);
-    uint32_t b2[8];
-#pragma unroll
-    for (int q = 0; q < 8; ++q)
-        b2[q] = (__float_as_uint(bf * (1.0f / pair_mult<BITS>(q, 0))) >> 16) |
-                (__float_as_uint(bf * (1.0f / pair_mult<BITS>(q, 1))) & 0xFFFF0000u);
-#pragma unroll
-    for (int tq = 0; tq < 4; ++tq) {
-        uint32_t win[2];
-        if constexpr (BITS == 2) {
-            win[0] = w[tq];
-        } else if constexpr (BITS == 4) {
-            win[0] = w[2 * tq];
-            win[1] = w[2 * tq + 1];
-        } else {
-            const int k0 = (3 * tq) >> 1;
-            if (tq & 1) {
-                win[0] = __funnelshift_r(w[k0], w[k0 + 1], 16);
-                win[1] = w[k0 + 1] >> 16;
-            } else {
-                win[0] = w[k0];
-                win[1] = w[k0 + 1];
-            }
-        }
-        uint32_t v[8];
-        extract<BITS>(win, v);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            // v - 128 = 2^p q exactly; a = s * (2^p q) + 2^p b, rounded once
-            a[tq * 8 + q] = bf2_fma(bf2_sub(v[q], MAGIC), s2, b2[q]);
-        }
-    }
-}
 
 template <int BITS>
 __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__ CUtensorMap map_x,
@@ -273,7 +139,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
     tc_fence_after();
     griddep_launch_dependents();
     const uint32_t tmem = *tmem_slot;
-    const Abort ab{abort_flag, mapa_shared(const_cast<int*>(abort_flag), rank ^ 1u), a.status};
+    const Abort ab{abort_flag, mapa_shared(const_cast<int*>(abort_flag), rank ^ 1u), a.status, true};
 
     if (warp == 0) {
         // ------------------------------------------------------- activation producer
@@ -468,9 +334,7 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
     __nv_bfloat16* xp = static_cast<__nv_bfloat16*>(ctx->workspace);
 
     CUtensorMap mx, mc, ms, mb;
-    const CUtensorMapSwizzle cswz = F::SW == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
-                                    : F::SW == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
-                                                  : CU_TENSOR_MAP_SWIZZLE_NONE;
+    const CUtensorMapSwizzle cswz = code_swizzle<BITS>();
     if (!make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xp, K, M, 64, P_HTOK, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_map_2d(&mc, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w, static_cast<uint64_t>(K) * BITS / 32, N,
                      F::CODE_W, P_ROWS, cswz) ||

@@ -61,6 +61,10 @@ _sig("q38_quantize", [_P, _P, _i, _I, _I, _i, _i, _i, _P, _P, _P, _i])
 _sig("q38_unpack_codes", [_P, _P, _I, _I, _i, _P])
 _sig("q38_hadamard_rotate", [_P, _P, _I, _I, _i, _P, _i, _i, _P])
 _sig("q38_hadamard_quantized_matmul", [_P, _P, _I, _I, _i, _P, _i, _P, _P, _P, _i, _I, _i, _i, _P])
+_sig("q38_moe_route", [_P, _P, _I, _I, _i, _P, _I, _i, _i, _P, _P, _P])
+_sig("q38_moe_route_logits", [_P, _P, _I, _I, _i, _i, _P, _P, _P])
+_sig("q38_moe_sort", [_P, _P, _I, _I, _P, _P])
+_sig("q38_switch_glu", [_P, _P, _I, _I, _I, _I, _i, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _i, _i, _i, _P])
 
 
 class Q38Error(RuntimeError):
@@ -253,6 +257,68 @@ def hadamard_rotate(x: torch.Tensor, signs: torch.Tensor | None, block: int,
     return y
 
 
+def moe_route(x: torch.Tensor, wr: torch.Tensor, top_k: int, normalize: bool = True,
+              want_probs: bool = False):
+    """Router of Qwen4ExpSparseMoE (FlashNext/Qwen4ExpSparseMoE.swift:208-214, :275-281):
+    x bf16 [T, H], wr bf16 [E, H] -> (indices int32 [T, k], scores bf16 [T, k][, probs [T, E]])
+    in canonical order (probability descending, expert id ascending on ties)."""
+    _need(x, "x"), _need(wr, "wr")
+    H = x.shape[-1]
+    T = x.numel() // H
+    E = wr.shape[0]
+    idx = torch.empty((T, top_k), dtype=torch.int32, device=x.device)
+    sc = torch.empty((T, top_k), dtype=torch.bfloat16, device=x.device)
+    pr = torch.empty((T, E), dtype=torch.bfloat16, device=x.device) if want_probs else None
+    ctx = _bind(x)
+    _check(ctx, _lib.q38_moe_route(ctx, _ptr(x), T, H, _DTYPE[x.dtype], _ptr(wr), E, top_k, int(normalize),
+                                   _ptr(idx), _ptr(sc), _ptr(pr)))
+    return (idx, sc, pr) if want_probs else (idx, sc)
+
+
+def moe_route_logits(logits: torch.Tensor, top_k: int, normalize: bool = True, want_probs: bool = False):
+    """The router's selection from given bf16 logits [T, E]."""
+    _need(logits, "logits")
+    T, E = logits.shape
+    idx = torch.empty((T, top_k), dtype=torch.int32, device=logits.device)
+    sc = torch.empty((T, top_k), dtype=torch.bfloat16, device=logits.device)
+    pr = torch.empty((T, E), dtype=torch.bfloat16, device=logits.device) if want_probs else None
+    ctx = _bind(logits)
+    _check(ctx, _lib.q38_moe_route_logits(ctx, _ptr(logits), T, E, top_k, int(normalize), _ptr(idx), _ptr(sc),
+                                          _ptr(pr)))
+    return (idx, sc, pr) if want_probs else (idx, sc)
+
+
+def moe_sort(indices: torch.Tensor, num_experts: int):
+    """Stable sort of the flat (token, slot) pairs by expert -> (perm [P], offsets [E + 1])."""
+    _need(indices, "indices")
+    P = indices.numel()
+    perm = torch.empty(P, dtype=torch.int32, device=indices.device)
+    offsets = torch.empty(num_experts + 1, dtype=torch.int32, device=indices.device)
+    ctx = _bind(indices)
+    _check(ctx, _lib.q38_moe_sort(ctx, _ptr(indices), P, num_experts, _ptr(perm), _ptr(offsets)))
+    return perm, offsets
+
+
+def switch_glu(x: torch.Tensor, indices: torch.Tensor, scores: torch.Tensor, gate, up, down,
+               group_size: int = 64, bits: int = 3) -> torch.Tensor:
+    """SwitchGLU + weightedExpertSum (FlashNext/Qwen4ExpSparseMoE.swift:294): gate/up/down are
+    (codes, scales, biases) triples of expert-stacked weights; x bf16 [T, H] -> bf16 [T, H]."""
+    _need(x, "x"), _need(indices, "indices"), _need(scores, "scores")
+    T, H = x.shape
+    k = indices.shape[-1]
+    gw, gs, gb = gate
+    uw, us, ub = up
+    dw, ds, db = down
+    E, I = gw.shape[0], gw.shape[1]
+    out = torch.empty_like(x)
+    ctx = _bind(x)
+    _check(ctx, _lib.q38_switch_glu(ctx, _ptr(x), T, H, I, E, k, _ptr(indices), _ptr(scores),
+                                    _ptr(_as_u32(gw)), _ptr(gs), _ptr(gb), _ptr(_as_u32(uw)), _ptr(us), _ptr(ub),
+                                    _ptr(_as_u32(dw)), _ptr(ds), _ptr(db), _DTYPE[x.dtype], group_size, bits,
+                                    _ptr(out)))
+    return out
+
+
 # ------------------------------------------------------------------------- modules
 
 class QuantizedLinear:
@@ -316,3 +382,28 @@ class QuantizedSwitchLinear:
         out = gather_qmm(x.reshape(T, 1, K).contiguous(), self.weight, self.scales, self.biases,
                          lhs, idx, True, self.group_size, self.bits, self.mode, sorted_indices)
         return out.reshape(T, k, -1)
+
+
+class SwitchGLU:
+    """MLXLMCommon.SwitchGLU over QuantizedSwitchLinear gate/up/down projections with the
+    weighted expert sum of Qwen4ExpSparseMoE: __call__(x, indices, scores) -> [T, H]."""
+
+    def __init__(self, gate: QuantizedSwitchLinear, up: QuantizedSwitchLinear, down: QuantizedSwitchLinear):
+        self.gate, self.up, self.down = gate, up, down
+
+    def __call__(self, x: torch.Tensor, indices: torch.Tensor, scores: torch.Tensor) -> torch.Tensor:
+        g, u, d = self.gate, self.up, self.down
+        return switch_glu(x, indices, scores, (g.weight, g.scales, g.biases), (u.weight, u.scales, u.biases),
+                          (d.weight, d.scales, d.biases), g.group_size, g.bits)
+
+
+class SparseMoeBlock:
+    """Routed-expert part of Qwen4ExpSparseMoE.callAsFunction (FlashNext/Qwen4ExpSparseMoE.swift:275-294):
+    router (unquantized gate Linear, softmax, top-k, renormalisation) then SwitchGLU."""
+
+    def __init__(self, router_weight: torch.Tensor, switch: SwitchGLU, top_k: int, normalize: bool = True):
+        self.router_weight, self.switch, self.top_k, self.normalize = router_weight, switch, top_k, normalize
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        idx, sc = moe_route(x, self.router_weight, self.top_k, self.normalize)
+        return self.switch(x, idx, sc)

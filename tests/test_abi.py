@@ -30,7 +30,8 @@ def lib():
 def test_header_declares_entry_points():
     names = declared_symbols()
     for must in ("q38_quantized_matmul", "q38_gather_quantized_matmul", "q38_dequantize",
-                 "q38_quantize", "q38_unpack_codes", "q38_hadamard_rotate"):
+                 "q38_quantize", "q38_unpack_codes", "q38_hadamard_rotate", "q38_moe_route",
+                 "q38_moe_route_logits", "q38_moe_sort", "q38_switch_glu"):
         assert must in names
 
 

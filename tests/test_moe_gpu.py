@@ -1,0 +1,166 @@
+"""GPU parity of the sparse-MoE layer (router, expert sort, SwitchGLU) against the oracle,
+through libq38.so's C ABI.
+
+Bars: router indices, scores and probabilities bit-exact given identical logits; the sort
+permutation and offsets bit-exact; SwitchGLU outputs within max|y - y_oracle| <=
+2e-2 * RMS(y_oracle).  Router decisions from x (logits computed on each side with its
+own fp32 summation order) must agree except at a probability tie at the top-k boundary.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from test_qmm_gpu import check_close, dev_bf16, host_bf16
+
+pytestmark = pytest.mark.gpu
+
+
+def dev_i32(a):
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32)).cuda()
+
+
+@pytest.mark.parametrize("normalize", [True, False])
+@pytest.mark.parametrize("T,E,k,dist", [(200, 512, 10, "uniform8"), (64, 512, 10, "normal"),
+                                        (33, 64, 4, "normal"), (5, 1000, 32, "uniform8"), (7, 8, 8, "normal")])
+def test_router_selection_bit_exact(q38, T, E, k, dist, normalize):
+    rng = np.random.default_rng(T * 1000 + E + k)
+    raw = rng.uniform(-8, 8, (T, E)) if dist == "uniform8" else rng.normal(0, 1.5, (T, E))
+    logits = O.f32_to_bf16(raw.astype(np.float32))
+    idx, sc, pr = O.route_from_logits(logits, k, normalize)
+    gi, gs, gp = q38.moe_route_logits(dev_bf16(logits), k, normalize, want_probs=True)
+    np.testing.assert_array_equal(host_bf16(gp), pr)
+    np.testing.assert_array_equal(gi.cpu().numpy(), idx)
+    np.testing.assert_array_equal(host_bf16(gs), sc)
+
+
+def test_router_ties_take_the_lower_expert_id(q38):
+    logits = O.f32_to_bf16(np.zeros((3, 64), np.float32))  # all probabilities equal
+    logits[1, 40] = O.f32_to_bf16(np.array([2.0], np.float32))[0]
+    gi, _ = q38.moe_route_logits(dev_bf16(logits), 6)
+    idx, _, _ = O.route_from_logits(logits, 6)
+    np.testing.assert_array_equal(gi.cpu().numpy(), idx)
+    assert list(idx[0]) == [0, 1, 2, 3, 4, 5] and idx[1][0] == 40
+
+
+@pytest.mark.parametrize("T", [1, 8, 64, 300, 4096])
+def test_router_from_activations(q38, T):
+    """Flash-Next router: H 2048, 512 experts, top-10; x N(0,1), Wr N(0, 0.02^2).  T <= 64
+    takes the CUDA-core logits, larger T the tcgen05 GEMM."""
+    H, E, k = 2048, 512, 10
+    x = O.normal_bf16(7000 + T, (T, H))
+    wr = O.normal_bf16(7001, (E, H), 0.02)
+    idx, sc, pr = O.moe_route(x, wr, k, True, want_probs=True)
+    gi, gs, gp = q38.moe_route(dev_bf16(x), dev_bf16(wr), k, True, want_probs=True)
+    gi, gp = gi.cpu().numpy(), O.bf16_to_f32(host_bf16(gp))
+    pf = O.bf16_to_f32(pr)
+    # probabilities: the same up to one bf16 rounding of a logit
+    assert np.abs(gp - pf).max() <= 2e-2 * pf.max()
+    flips = 0
+    for t in range(T):
+        if set(gi[t]) != set(idx[t]):
+            srt = np.sort(pf[t])[::-1]
+            assert srt[k - 1] - srt[k] <= 2 * 2.0 ** -8 * srt[k - 1], "selection differs away from a near-tie"
+            flips += 1
+    assert flips <= max(2, T // 100)
+    # where the selection agrees, the canonical order and scores agree too
+    same = [t for t in range(T) if (gi[t] == idx[t]).all()]
+    assert len(same) >= T - flips - max(2, T // 100)
+
+
+@pytest.mark.parametrize("P,E", [(1, 8), (10, 512), (80, 512), (640, 512), (40960, 512), (5000, 1000)])
+def test_sort_by_expert_bit_exact(q38, P, E):
+    rng = np.random.default_rng(P + E)
+    ind = rng.integers(0, E, size=P).astype(np.int32)
+    perm, off = O.sort_by_expert(ind, E)
+    gperm, goff = q38.moe_sort(dev_i32(ind), E)
+    np.testing.assert_array_equal(goff.cpu().numpy(), off)
+    np.testing.assert_array_equal(gperm.cpu().numpy(), perm)
+
+
+def test_sort_reports_bad_index(q38):
+    ind = np.array([1, 2, 9, 0], np.int32)
+    perm, off = q38.moe_sort(dev_i32(ind), 4)
+    with pytest.raises(q38.Q38ArgumentError):
+        q38.check_device()
+    assert list(off.cpu().numpy()) == [0, 1, 2, 3, 3]
+    assert list(perm.cpu().numpy()[:3]) == [3, 0, 1]
+    q38.check_device()
+
+
+def make_experts(q38, seed, E, I, H, bits):
+    """Expert stacks quantized on the GPU (bit-exact with the oracle's quantizer), copied back
+    for the oracle."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    trip = []
+    for (n, k) in ((I, H), (I, H), (H, I)):
+        w = torch.randn((E * n, k), generator=g, device="cuda") * 0.02
+        c, s, b = q38.quantize(w, 64, bits, scales_dtype=torch.bfloat16)
+        trip.append(((c.view(torch.int32).view(E, n, -1), s.view(E, n, -1), b.view(E, n, -1)),
+                     (c.view(torch.int32).cpu().numpy().view(np.uint32).reshape(E, n, -1),
+                      host_bf16(s).reshape(E, n, -1), host_bf16(b).reshape(E, n, -1))))
+        del w
+    return [t[0] for t in trip], [t[1] for t in trip]
+
+
+def route_inputs(T, E, k, seed):
+    rng = np.random.default_rng(seed)
+    logits = O.f32_to_bf16(rng.normal(0, 1.0, (T, E)).astype(np.float32))
+    idx, sc, _ = O.route_from_logits(logits, k, True)
+    return idx, sc
+
+
+@pytest.mark.parametrize("bits", [3, 2, 4])
+@pytest.mark.parametrize("T,E,k,H,I", [(5, 16, 4, 512, 512), (64, 32, 10, 2048, 512), (1, 32, 10, 2048, 512),
+                                       (300, 8, 2, 1024, 1024)])
+def test_switch_glu_parity(q38, bits, T, E, k, H, I):
+    dev, host = make_experts(q38, 8000 + bits + T, E, I, H, bits)
+    x = O.normal_bf16(8100 + T, (T, H))
+    idx, sc = route_inputs(T, E, k, 8200 + T)
+    ref = O.switch_glu(x, idx, sc, *host, 64, bits)
+    out = q38.switch_glu(dev_bf16(x), dev_i32(idx), dev_bf16(sc), *dev, 64, bits)
+    torch.cuda.synchronize()
+    q38.check_device()
+    check_close(host_bf16(out), O.bf16_to_f32(ref).astype(np.float64))
+
+
+def test_switch_glu_without_biases(q38):
+    T, E, k, H, I, bits = 20, 8, 3, 512, 512, 3
+    dev, host = make_experts(q38, 8300, E, I, H, bits)
+    dev = [(c, s, None) for (c, s, b) in dev]
+    host = [(c, s, None) for (c, s, b) in host]
+    x = O.normal_bf16(8301, (T, H))
+    idx, sc = route_inputs(T, E, k, 8302)
+    ref = O.switch_glu(x, idx, sc, *host, 64, bits)
+    out = q38.switch_glu(dev_bf16(x), dev_i32(idx), dev_bf16(sc), *dev, 64, bits)
+    check_close(host_bf16(out), O.bf16_to_f32(ref).astype(np.float64))
+
+
+def test_switch_glu_prompt_sampled_tokens(q38):
+    """4096 tokens over 64 experts (about 640 pairs per expert: runs of 128 pairs, several
+    per expert); 8 sampled tokens checked against the oracle (a token's output depends only
+    on its own row, experts and scores)."""
+    T, E, k, H, I, bits = 4096, 64, 10, 2048, 512, 3
+    dev, host = make_experts(q38, 8400, E, I, H, bits)
+    x = O.normal_bf16(8401, (T, H))
+    idx, sc = route_inputs(T, E, k, 8402)
+    out = q38.switch_glu(dev_bf16(x), dev_i32(idx), dev_bf16(sc), *dev, 64, bits)
+    torch.cuda.synchronize()
+    q38.check_device()
+    rows = np.array([0, 1, 127, 128, 2000, 3001, 4094, 4095])
+    ref = O.switch_glu(np.ascontiguousarray(x[rows]), idx[rows], sc[rows], *host, 64, bits)
+    check_close(host_bf16(out[torch.from_numpy(rows).cuda()]), O.bf16_to_f32(ref).astype(np.float64))
+
+
+def test_sparse_moe_block_end_to_end(q38):
+    """Router + SwitchGLU through the module classes (Flash-Next shapes, 32 experts)."""
+    T, E, k, H, I, bits = 16, 32, 10, 2048, 512, 3
+    dev, host = make_experts(q38, 8500, E, I, H, bits)
+    x = O.normal_bf16(8501, (T, H))
+    wr = O.normal_bf16(8502, (E, H), 0.02)
+    sw = q38.SwitchGLU(*[q38.QuantizedSwitchLinear(c, s, b, 64, bits) for (c, s, b) in dev])
+    block = q38.SparseMoeBlock(dev_bf16(wr), sw, k)
+    out = block(dev_bf16(x))
+    gi, gs = q38.moe_route(dev_bf16(x), dev_bf16(wr), k)
+    ref = O.switch_glu(x, gi.cpu().numpy(), host_bf16(gs), *host, 64, bits)
+    check_close(host_bf16(out), O.bf16_to_f32(ref).astype(np.float64))
