@@ -46,7 +46,7 @@ def lib():
             "q38o_route_from_logits": [_P, _I, _I, _i, _i, _P, _P, _P],
             "q38o_sort_by_expert": [_P, _I, _I, _P, _P],
             "q38o_switch_glu": [_P, _I, _I, _I, _I, _i, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
-                                _i, _i, _P],
+                                _i, _i, _i, _P],
             "q38o_hadamard_rotate": [_P, _I, _I, _P, _i, _i, _P],
         }
         for name, args in sig.items():
@@ -227,8 +227,11 @@ def sort_by_expert(indices, E: int):
     return perm, offsets
 
 
-def switch_glu(x, indices, scores, gate, up, down, group: int, bits: int) -> np.ndarray:
-    """gate/up/down are (codes, scales, biases) triples of expert-stacked weights."""
+def switch_glu(x, indices, scores, gate, up, down, group: int, bits: int,
+               weights_bf16: bool = False) -> np.ndarray:
+    """gate/up/down are (codes, scales, biases) triples of expert-stacked weights.
+    weights_bf16 rounds each dequantized weight once to bf16, as a bf16 tensor-core product
+    consumes it; otherwise weights are evaluated in fp32."""
     x = np.ascontiguousarray(x, dtype=np.uint16)
     T, H = x.shape
     E, I = gate[0].shape[0], gate[0].shape[1]
@@ -238,7 +241,7 @@ def switch_glu(x, indices, scores, gate, up, down, group: int, bits: int) -> np.
     _check(lib().q38o_switch_glu(_p(x), T, H, I, E, top_k,
                                  _p(np.ascontiguousarray(indices, dtype=np.int32)),
                                  _p(np.ascontiguousarray(scores, dtype=np.uint16)),
-                                 *[_p(a) for a in c], group, bits, _p(out)), "switch_glu")
+                                 *[_p(a) for a in c], group, bits, int(weights_bf16), _p(out)), "switch_glu")
     return out
 
 

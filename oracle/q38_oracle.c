@@ -458,16 +458,30 @@ typedef struct {
     const uint16_t* scores;
     const uint32_t *gw, *uw, *dw;
     const uint16_t *gs, *gb, *us, *ub, *ds, *db;
-    int group, bits;
+    int group, bits, weights_bf16;
     uint16_t* out;
 } glu_ctx;
 
 static float silu_f32(float v) { return v / (1.0f + expf(-v)); }
 
+/* Round an exactly known value (a double holding s*q + b without error: bf16 s and b
+ * have 8 significant bits, q < 2^8) to the nearest bf16, ties to even, in one step. */
+static float bf16_of_exact(double v) {
+    if (v == 0.0) return 0.0f;
+    int ex;
+    double m = frexp(v, &ex); /* v = m * 2^ex, 0.5 <= |m| < 1 */
+    return (float)ldexp(nearbyint(m * 256.0), ex - 8);
+}
+
+/* Dequantized row in fp32 (w = s*q + b evaluated in fp32), or -- weights_bf16 -- the
+ * weight operand of a bf16 tensor-core product: s*q + b rounded once to bf16. */
 static void dequant_row(const uint32_t* cr, const uint16_t* s, const uint16_t* b, int64_t K,
-                        int group, int bits, float* w) {
-    for (int64_t k = 0; k < K; ++k)
-        w[k] = bf(s[k / group]) * (float)get_code(cr, k, bits) + (b ? bf(b[k / group]) : 0.0f);
+                        int group, int bits, int weights_bf16, float* w) {
+    for (int64_t k = 0; k < K; ++k) {
+        const float sv = bf(s[k / group]), bv = b ? bf(b[k / group]) : 0.0f;
+        const uint32_t q = get_code(cr, k, bits);
+        w[k] = weights_bf16 ? bf16_of_exact((double)sv * (double)q + (double)bv) : sv * (float)q + bv;
+    }
 }
 
 /* SwitchGLU.callAsFunction + weightedExpertSum as used at
@@ -488,17 +502,17 @@ static void glu_tokens(void* p, int64_t t0, int64_t t1) {
             for (int64_t i = 0; i < I; ++i) {
                 int64_t row = e * I + i;
                 dequant_row(c->gw + row * c->kwh, c->gs + row * c->Gh,
-                            c->gb ? c->gb + row * c->Gh : NULL, H, c->group, c->bits, w);
+                            c->gb ? c->gb + row * c->Gh : NULL, H, c->group, c->bits, c->weights_bf16, w);
                 float g = round_bf(dot_f32(xt, w, (int)H));
                 dequant_row(c->uw + row * c->kwh, c->us + row * c->Gh,
-                            c->ub ? c->ub + row * c->Gh : NULL, H, c->group, c->bits, w);
+                            c->ub ? c->ub + row * c->Gh : NULL, H, c->group, c->bits, c->weights_bf16, w);
                 float u = round_bf(dot_f32(xt, w, (int)H));
                 h[i] = round_bf(silu_f32(g) * u);
             }
             for (int64_t j = 0; j < H; ++j) {
                 int64_t row = e * H + j;
                 dequant_row(c->dw + row * c->kwi, c->ds + row * c->Gi,
-                            c->db ? c->db + row * c->Gi : NULL, I, c->group, c->bits, w);
+                            c->db ? c->db + row * c->Gi : NULL, I, c->group, c->bits, c->weights_bf16, w);
                 float y = round_bf(dot_f32(h, w, (int)I));
                 acc[j] += score * y;
             }
@@ -515,7 +529,7 @@ int q38o_switch_glu(const uint16_t* x, int64_t T, int64_t H, int64_t I, int64_t 
                     const uint32_t* gw, const uint16_t* gs, const uint16_t* gb,
                     const uint32_t* uw, const uint16_t* us, const uint16_t* ub,
                     const uint32_t* dw, const uint16_t* ds, const uint16_t* db,
-                    int group, int bits, uint16_t* out) {
+                    int group, int bits, int weights_bf16, uint16_t* out) {
     if (!valid_bits(bits) || group <= 0 || H % group || I % group) return -1;
     if ((H * bits) % 32 || (I * bits) % 32) return -1;
     for (int64_t i = 0; i < T * top_k; ++i)
@@ -523,7 +537,7 @@ int q38o_switch_glu(const uint16_t* x, int64_t T, int64_t H, int64_t I, int64_t 
     float* xf = (float*)malloc((size_t)(T * H) * sizeof(float));
     for (int64_t i = 0; i < T * H; ++i) xf[i] = bf(x[i]);
     glu_ctx c = {xf, H, I, top_k, H * bits / 32, I * bits / 32, H / group, I / group,
-                 indices, scores, gw, uw, dw, gs, gb, us, ub, ds, db, group, bits, out};
+                 indices, scores, gw, uw, dw, gs, gb, us, ub, ds, db, group, bits, weights_bf16, out};
     parallel_for(T, glu_tokens, &c);
     free(xf);
     return 0;

@@ -83,13 +83,15 @@ int q38o_sort_by_expert(const int32_t* indices, int64_t pairs, int64_t E, int32_
  *   g = bf16(x_t . Wg[e]^T), u = bf16(x_t . Wu[e]^T), h = bf16(silu(g) * u),
  *   y_tk = bf16(h . Wd[e]^T), out_t = bf16(sum_k score_tk * y_tk).
  * x [T,H]; indices/scores [T,k]; gate/up codes [E, I, H*bits/32], scales [E, I, H/group];
- * down codes [E, H, I*bits/32], scales [E, H, I/group]. */
+ * down codes [E, H, I*bits/32], scales [E, H, I/group].
+ * weights_bf16 != 0 rounds every dequantized weight s*q + b once to bf16 (the operand of
+ * a bf16 tensor-core product) instead of evaluating it in fp32. */
 int q38o_switch_glu(const uint16_t* x, int64_t T, int64_t H, int64_t I, int64_t E, int top_k,
                     const int32_t* indices, const uint16_t* scores,
                     const uint32_t* gw, const uint16_t* gs, const uint16_t* gb,
                     const uint32_t* uw, const uint16_t* us, const uint16_t* ub,
                     const uint32_t* dw, const uint16_t* ds, const uint16_t* db,
-                    int group, int bits, uint16_t* out);
+                    int group, int bits, int weights_bf16, uint16_t* out);
 
 /* hadamardRotate: y = bf16( FWHT_block( fp32(x) * signs ) / sqrt(block) ) (forward), or
  * signs applied after the transform (inverse).  signs may be NULL (all +1). */

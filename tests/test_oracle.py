@@ -205,3 +205,33 @@ def test_gather_qmm_matches_per_expert_qmm():
     for p in range(4):
         ref = O.qmm(x[lhs[p]], c[rhs[p]], s[rhs[p]], b[rhs[p]], 64, 4)
         np.testing.assert_array_equal(out[p], ref)
+
+
+def test_switch_glu_bf16_weight_mode_matches_restatement():
+    """weights_bf16 rounds each dequantized weight once to bf16: equal to a dense
+    restatement that rounds the (exact) s*q + b to bf16 before the products."""
+    T, H, I, E, k = 4, 128, 64, 5, 2
+    x = O.normal_bf16(71, (T, H))
+    mk = lambda seed, shape: O.quantize(O.normal_f32(seed, shape, 0.02), 64, 3)
+    gate, up, down = mk(72, (E, I, H)), mk(73, (E, I, H)), mk(74, (E, H, I))
+    ind = np.array([[0, 4], [2, 1], [3, 3], [1, 0]], dtype=np.int32)
+    sc = O.f32_to_bf16(np.array([[0.7, 0.3], [0.5, 0.5], [0.6, 0.4], [0.2, 0.8]], dtype=np.float32))
+    out = O.bf16_to_f32(O.switch_glu(x, ind, sc, gate, up, down, 64, 3, weights_bf16=True))
+    rb = lambda a: O.bf16_to_f32(O.f32_to_bf16(np.asarray(a, np.float32)))
+
+    def wq(t, n, kk):
+        q = O.unpack(t[0].reshape(E * n, -1), kk, 3).astype(np.float64)
+        s = np.repeat(O.bf16_to_f32(t[1].reshape(E * n, -1)).astype(np.float64), 64, axis=1)
+        b = np.repeat(O.bf16_to_f32(t[2].reshape(E * n, -1)).astype(np.float64), 64, axis=1)
+        return rb(s * q + b).reshape(E, n, kk)  # s*q + b exact in float64, one rounding
+    G, U, D = wq(gate, I, H), wq(up, I, H), wq(down, H, I)
+    xf, s = O.bf16_to_f32(x), O.bf16_to_f32(sc)
+    ref = np.zeros((T, H), np.float32)
+    for t in range(T):
+        for j in range(k):
+            e = ind[t, j]
+            g, u = rb(G[e] @ xf[t]), rb(U[e] @ xf[t])
+            ref[t] += s[t, j] * rb(D[e] @ rb(g / (1 + np.exp(-g)) * u))
+    ref = rb(ref)
+    rms = np.sqrt((ref.astype(np.float64) ** 2).mean())
+    assert np.abs(out - ref).max() <= 2e-2 * rms
