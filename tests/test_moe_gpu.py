@@ -6,8 +6,11 @@ permutation and offsets bit-exact.  Router decisions from x (logits computed on 
 with its own fp32 summation order) must agree except at a probability tie at the top-k
 boundary.
 
-SwitchGLU outputs: max|y - y_oracle| <= 2e-2 * RMS(y_oracle), fp32 accumulation on both
-sides, against the oracle with weights_bf16: the tensor-core path multiplies bf16
+SwitchGLU outputs: |y - y_oracle| <= 2e-2 * RMS(y_oracle) + one bf16 step of |y_oracle|
+per element, fp32 accumulation on both sides.  The output is bf16 and its largest values
+are 5-10x its RMS, where one representable step (2^-8 relative) already exceeds 2e-2 * RMS:
+a different fp32 summation order may round the same value to the neighbouring bf16.
+The comparison is against the oracle with weights_bf16: the tensor-core path multiplies bf16
 operands, so each dequantized weight s*q + b is rounded once to bf16 before the product,
 and the oracle applies the same single rounding.  (Against fp32-evaluated weights the
 layer's own bf16 roundings of g, u, h and y_ts amplify that operand rounding to a few
@@ -19,9 +22,19 @@ import pytest
 import torch
 
 import oracle as O
-from test_qmm_gpu import check_close, dev_bf16, host_bf16
+from test_qmm_gpu import dev_bf16, host_bf16
 
 pytestmark = pytest.mark.gpu
+
+
+def check_close(y_gpu_bf16, y_ref, tol=2e-2):
+    y = O.bf16_to_f32(y_gpu_bf16).astype(np.float64)
+    ref = np.asarray(y_ref, dtype=np.float64)
+    assert np.isfinite(y).all()
+    rms = np.sqrt((ref ** 2).mean())
+    step = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(ref), 2.0 ** -126))) - 7)  # bf16 spacing at |ref|
+    excess = (np.abs(y - ref) - step).max()
+    assert excess <= tol * rms, f"max err beyond one bf16 step {excess:.4g} > {tol} * rms {rms:.4g}"
 
 
 def check_stat(y_gpu_bf16, y_ref):
