@@ -1,4 +1,6 @@
-"""Benchmark of the decode-shaped MLX-affine quantized product on B200.
+"""Benchmark of the MLX-affine quantized products on B200: the decode GEMV sweep (the
+headline line), plus the MoE expert-stack layer ("moe") and the prompt-shaped GEMM
+("prefill") as secondary objects of the same JSON line.
 
 Workload (one "step"): the decode GEMV sweep -- x bf16 N(0,1), W N(0, 0.02^2) quantized
 affine group 64 at bits {2,3,4,8}, shapes N x K in {17408x5120, 5120x17408, 6144x5120},
@@ -127,6 +129,171 @@ def build_case_weights(torch, O, dev, bits, N, K, seed, copies=1):
     for _ in range(copies - 1):
         out.append((tc.clone(), ts.clone(), tb.clone()))
     return out
+
+
+# ----------------------------------------------------------------------------- MoE
+MOE = {"H": 2048, "I": 512, "E": 512, "k": 10, "bits": 3}
+MOE_T = [1, 8, 64, 4096]
+
+
+def moe_expert_bytes():
+    H, I, bits = MOE["H"], MOE["I"], MOE["bits"]
+    per = 0
+    for (n, k) in ((I, H), (I, H), (H, I)):
+        per += n * k * bits // 8 + n * (k // GROUP) * 2 * 2
+    return per
+
+
+def build_moe(torch, q38, dev, seed=3030):
+    """Flash-Next-shaped expert stack: gate/up [512, 512, 2048], down [512, 2048, 512], each
+    N(0, 0.02^2) quantized 3-bit group 64 on the device (the quantizer is bit-exact with the
+    oracle's); router weight [512, 2048] bf16 N(0, 0.02^2)."""
+    H, I, E, bits = MOE["H"], MOE["I"], MOE["E"], MOE["bits"]
+    g = torch.Generator(device=dev).manual_seed(seed)
+    W = []
+    for (n, k) in ((I, H), (I, H), (H, I)):
+        w = torch.randn((E * n, k), generator=g, device=dev) * 0.02
+        c, s, b = q38.quantize(w, GROUP, bits, scales_dtype=torch.bfloat16)
+        W.append((c.view(torch.int32).view(E, n, -1), s.view(E, n, -1), b.view(E, n, -1)))
+        del w
+    wr = (torch.randn((E, H), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    sw = q38.SwitchGLU(*[q38.QuantizedSwitchLinear(c, s, b, GROUP, bits) for (c, s, b) in W])
+    return q38.SparseMoeBlock(wr, sw, MOE["k"]), g
+
+
+def run_moe(torch, q38, dev, stream, world, dist, quick=False):
+    """One MoE layer (router + SwitchGLU + combine) per step at each token count, timed as
+    CUDA-graph replays; each replay cycles through R different token batches so that the
+    experts a batch selects are not L2-resident from the previous one."""
+    blk, g = build_moe(torch, q38, dev)
+    H, k = MOE["H"], MOE["k"]
+    ebytes = moe_expert_bytes()
+    out = {}
+    for T in MOE_T:
+        R = 16 if T <= 64 else 2
+        reps = (5 if quick else 30) if T <= 64 else (2 if quick else 10)
+        xs = [torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16) for _ in range(R)]
+        for x in xs:
+            blk(x)
+        torch.cuda.synchronize()
+        touched = sum(int(torch.unique(q38.moe_route(x, blk.router_weight, k)[0]).numel()) for x in xs) / R
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            for x in xs:
+                blk(x)
+        gr.replay()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            gr.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * R)
+        if dist:
+            t = torch.tensor([us], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            us = float(t.item())
+        del gr
+        # e2e through the public API: host batch -> device, layer, result -> host
+        hx = xs[0].cpu().pin_memory()
+        hy = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+        dx = torch.empty_like(xs[0])
+        n_e2e = 3 if T == 4096 else 20
+
+        def e2e_once():
+            dx.copy_(hx, non_blocking=True)
+            hy.copy_(blk(dx), non_blocking=True)
+        e2e_once()
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(n_e2e):
+            e2e_once()
+        a1.record(stream)
+        torch.cuda.synchronize()
+        e2e_us = a0.elapsed_time(a1) * 1e3 / n_e2e
+        if dist:
+            t = torch.tensor([e2e_us], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_us = float(t.item())
+        wbytes = touched * ebytes + MOE["E"] * H * 2 + 2 * T * H * 2
+        flops = T * k * 2 * (3 * MOE["I"] * H) + T * 2 * H * MOE["E"]
+        out[str(T)] = {"tokens_per_s": round(world * T / (us * 1e-6), 1), "us_per_layer": round(us, 2),
+                       "experts_touched": round(touched, 1), "weight_GBps": round(wbytes / (us * 1e-6) / 1e9, 1),
+                       "TFLOPs": round(flops / (us * 1e-6) / 1e12, 2),
+                       "e2e_tokens_per_s": round(world * T / (e2e_us * 1e-6), 1),
+                       "e2e_h2d_bytes": T * H * 2, "e2e_d2h_bytes": T * H * 2}
+        del xs, hx, hy, dx
+    del blk
+    torch.cuda.synchronize()
+    return {"metric": "MoE expert-stack tokens/s (router + SwitchGLU + combine, one layer)",
+            "unit": "tokens/s", "per_T": out,
+            "config": {"workload": "Flash-Next MoE layer: hidden 2048, 512 experts, intermediate 512, top-10, "
+                                   "3-bit group 64, router [512, 2048] bf16",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "timing": "CUDA-graph replays cycling 16 (T<=64) or 2 (T=4096) token batches, CUDA events"},
+            "bytes_per_expert": ebytes}
+
+
+# ------------------------------------------------------------------------- prefill
+def run_prefill(torch, q38, dev, stream, world, dist, quick=False):
+    """Dense-27B MLP block products at 4096 tokens, 4-bit group 64: gate and up
+    (17408 x 5120) on x [4096, 5120], down (5120 x 17408) on h [4096, 17408]."""
+    M, D, F = 4096, 5120, 17408
+    g = torch.Generator(device=dev).manual_seed(4040)
+    mats = []
+    for (n, k) in ((F, D), (F, D), (D, F)):
+        w = torch.randn((n, k), generator=g, device=dev) * 0.02
+        c, s, b = q38.quantize(w, GROUP, 4, scales_dtype=torch.bfloat16)
+        mats.append((c.view(torch.int32), s, b))
+        del w
+    x = torch.randn((M, D), generator=g, device=dev).to(torch.bfloat16)
+    h = (torch.randn((M, F), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+
+    def layer():
+        q38.quantized_matmul(x, *mats[0], True, GROUP, 4)
+        q38.quantized_matmul(x, *mats[1], True, GROUP, 4)
+        q38.quantized_matmul(h, *mats[2], True, GROUP, 4)
+    layer()
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        layer()
+    gr.replay()
+    torch.cuda.synchronize()
+    reps = 3 if quick else 20
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        gr.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    if dist:
+        t = torch.tensor([us], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        us = float(t.item())
+    flops = 3 * 2 * M * F * D
+    peak = None
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        peak = float(json.load(open(p))["bf16_tflops"])
+    tf = flops / (us * 1e-6) / 1e12
+    del gr, mats, x, h
+    torch.cuda.synchronize()
+    return {"metric": "prefill quantized GEMM TFLOP/s (tensor pipe)", "unit": "TFLOP/s",
+            "value": round(world * tf, 1), "us_per_block": round(us, 1),
+            "frac_of_measured_bf16_peak": round(tf / peak, 4) if peak else None,
+            "tokens_per_s": round(world * M / (us * 1e-6), 1),
+            "config": {"workload": "4096 tokens x 4-bit g64 MLP products: gate, up 17408x5120; down 5120x17408 "
+                                   "(SiLU-gating between them not included)",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "timing": "CUDA-graph replay of the 3 products (3 x prologue + pair kernel), CUDA events"}}
 
 
 def run_ours(args, rank, world, local_rank):
@@ -300,6 +467,9 @@ def run_ours(args, rank, world, local_rank):
     e2e = {"value": round(world * step_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)}
 
+    moe = None if args.skip_moe else run_moe(torch, q38, dev, stream, world, dist, args.quick)
+    prefill = None if args.skip_prefill else run_prefill(torch, q38, dev, stream, world, dist, args.quick)
+
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_baseline(O, seconds=args.cpu_seconds)
@@ -328,6 +498,8 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": 3 * len(cases) * args.steps,
         "eager_ms_per_step": round(eager_ms, 4),
         "cases": per_case,
+        "moe": moe,
+        "prefill": prefill,
     }
     return line
 
@@ -403,11 +575,46 @@ def run_profile_case(args):
                                        "algorithmic_bytes_per_launch": algo_bytes(M, N, K, bits)}}))
 
 
+def run_profile_prefill(args):
+    """Small prompt-shaped case for ncu: 4-bit, M=1024 tokens, N=9472 (37 row pairs x 4 token
+    tiles = 148 pair tiles), K=5120; 3 products."""
+    import torch
+    import q38
+    dev = torch.device("cuda", 0)
+    M, N, K = 1024, 9472, 5120
+    g = torch.Generator(device=dev).manual_seed(5050)
+    c, s, b = q38.quantize(torch.randn((N, K), generator=g, device=dev) * 0.02, GROUP, 4, scales_dtype=torch.bfloat16)
+    x = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+    for _ in range(3):
+        y = q38.quantized_matmul(x, c.view(torch.int32), s, b, True, GROUP, 4)
+    torch.cuda.synchronize()
+    q38.check_device()
+    print(json.dumps({"profile_prefill": {"M": M, "N": N, "K": K, "bits": 4, "launches": 3,
+                                          "flops_per_launch": 2 * M * N * K, "mean_abs_y": float(y.float().abs().mean())}}))
+
+
+def run_profile_moe(args):
+    """One MoE layer (Flash-Next shapes) at T = --profile-t tokens, 2 calls, for ncu."""
+    import torch
+    import q38
+    dev = torch.device("cuda", 0)
+    blk, g = build_moe(torch, q38, dev)
+    x = torch.randn((args.profile_t, MOE["H"]), generator=g, device=dev).to(torch.bfloat16)
+    for _ in range(2):
+        y = blk(x)
+    torch.cuda.synchronize()
+    q38.check_device()
+    print(json.dumps({"profile_moe": {"T": args.profile_t, "calls": 2, "mean_abs_y": float(y.float().abs().mean())}}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--profile-case", action="store_true")
     ap.add_argument("--profile-bits", type=int, default=4)
     ap.add_argument("--profile-m", type=int, default=1)
+    ap.add_argument("--profile-prefill", action="store_true")
+    ap.add_argument("--profile-moe", action="store_true")
+    ap.add_argument("--profile-t", type=int, default=4096)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=3)
@@ -415,12 +622,21 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--ref-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--skip-moe", action="store_true")
+    ap.add_argument("--skip-prefill", action="store_true")
+    ap.add_argument("--quick", action="store_true", help="fewer replays in the MoE and prefill sections")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus if args.gpus == 1 else 1)))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.profile_case:
         run_profile_case(args)
+        return
+    if args.profile_prefill:
+        run_profile_prefill(args)
+        return
+    if args.profile_moe:
+        run_profile_moe(args)
         return
     if args.impl == "reference":
         line = run_reference(args, rank, world)

@@ -45,67 +45,54 @@ __device__ __forceinline__ float router_exp(float x) {
     return __fmul_rn(p, __uint_as_float(static_cast<uint32_t>(ni + 127) << 23));
 }
 
-// logits for a few tokens on CUDA cores: block = 8 warps x 4 experts, 8 tokens staged in
-// shared memory; each lane accumulates 8-element slices, the warp reduces.
-__global__ void __launch_bounds__(256) router_logits_small(const __nv_bfloat16* __restrict__ x, int T, int H,
+// logits for a few tokens on CUDA cores: one warp per expert (4 per block), up to 8
+// tokens staged in shared memory; each lane accumulates 8-element slices of the row, the
+// warp reduces.
+__global__ void __launch_bounds__(128) router_logits_small(const __nv_bfloat16* __restrict__ x, int T, int H,
                                                            const __nv_bfloat16* __restrict__ wr, int E,
                                                            __nv_bfloat16* __restrict__ logits) {
     extern __shared__ uint4 xs4[];
     const int t0 = blockIdx.y * 8;
     const int nt = min(8, T - t0);
     const int vec = H / 8;
-    for (int i = threadIdx.x; i < 8 * vec; i += 256) {
+    for (int i = threadIdx.x; i < 8 * vec; i += 128) {
         const int t = i / vec;
         xs4[i] = t < nt ? reinterpret_cast<const uint4*>(x + static_cast<size_t>(t0 + t) * H)[i % vec]
                         : make_uint4(0, 0, 0, 0);
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int e0 = blockIdx.x * 32 + warp * 4;
-    float acc[4][8];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int t = 0; t < 8; ++t) acc[i][t] = 0.0f;
+    const int e = blockIdx.x * 4 + warp;
+    if (e >= E) return;
+    const uint4* wrow = reinterpret_cast<const uint4*>(wr + static_cast<size_t>(e) * H);
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int v = lane; v < vec; v += 32) {
-        float wv[4][8];
+        const uint4 u = wrow[v];
+        const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+        float wv[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int e = min(e0 + i, E - 1);
-            const uint4 u = reinterpret_cast<const uint4*>(wr + static_cast<size_t>(e) * H)[v];
-            const uint32_t q[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                wv[i][2 * j] = bf16_bits_to_f32(q[j] & 0xFFFFu);
-                wv[i][2 * j + 1] = bf16_bits_to_f32(q[j] >> 16);
-            }
+        for (int j = 0; j < 4; ++j) {
+            wv[2 * j] = bf16_bits_to_f32(q[j] & 0xFFFFu);
+            wv[2 * j + 1] = bf16_bits_to_f32(q[j] >> 16);
         }
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
-            const uint4 u = xs4[t * vec + v];
-            const uint32_t q[4] = {u.x, u.y, u.z, u.w};
-            float xv[8];
+            const uint4 xu = xs4[t * vec + v];
+            const uint32_t xq[4] = {xu.x, xu.y, xu.z, xu.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                xv[2 * j] = bf16_bits_to_f32(q[j] & 0xFFFFu);
-                xv[2 * j + 1] = bf16_bits_to_f32(q[j] >> 16);
+                acc[t] = fmaf(wv[2 * j], bf16_bits_to_f32(xq[j] & 0xFFFFu), acc[t]);
+                acc[t] = fmaf(wv[2 * j + 1], bf16_bits_to_f32(xq[j] >> 16), acc[t]);
             }
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int j = 0; j < 8; ++j) acc[i][t] = fmaf(wv[i][j], xv[j], acc[i][t]);
         }
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int t = 0; t < 8; ++t) {
+        float v = acc[t];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-            float v = acc[i][t];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0 && t < nt && e0 + i < E)
-                logits[static_cast<size_t>(t0 + t) * E + e0 + i] = __float2bfloat16_rn(v);
-        }
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0 && t < nt) logits[static_cast<size_t>(t0 + t) * E + e] = __float2bfloat16_rn(v);
+    }
 }
 
 // logits for prompts on the tensor cores: one CTA per 128 tokens x 256 experts, both
@@ -466,8 +453,8 @@ q38_status logits_launch(q38_ctx* ctx, const void* x, int64_t T, int64_t H, cons
                 big[ctx->device] = true;
             }
         }
-        dim3 grid(static_cast<unsigned>((E + 31) / 32), static_cast<unsigned>((T + 7) / 8));
-        router_logits_small<<<grid, 256, sm, ctx->stream>>>(static_cast<const __nv_bfloat16*>(x), static_cast<int>(T),
+        dim3 grid(static_cast<unsigned>((E + 3) / 4), static_cast<unsigned>((T + 7) / 8));
+        router_logits_small<<<grid, 128, sm, ctx->stream>>>(static_cast<const __nv_bfloat16*>(x), static_cast<int>(T),
                                                             static_cast<int>(H), static_cast<const __nv_bfloat16*>(wr),
                                                             static_cast<int>(E), static_cast<__nv_bfloat16*>(logits));
         return check_launch(ctx, "router_logits_small");
