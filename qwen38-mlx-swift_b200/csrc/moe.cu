@@ -349,16 +349,16 @@ __global__ void __launch_bounds__(1024, 1) moe_sort_kernel(const int32_t* __rest
 }
 
 // ---------------------------------------------------------------------- tile lists
-// Per expert: ceil(n_e / 128) runs of pairs, each crossed with the row blocks of the
+// Per expert: ceil(n_e / run) runs of pairs, each crossed with the row blocks of the
 // gate/up (I / 64) and down (H / 128) products.
-__global__ void __launch_bounds__(1024, 1) moe_tiles_kernel(const int32_t* __restrict__ offsets, int E,
+__global__ void __launch_bounds__(1024, 1) moe_tiles_kernel(const int32_t* __restrict__ offsets, int E, int run,
                                                             int rb_gu, int rb_d, MoeTile* __restrict__ gu,
                                                             MoeTile* __restrict__ dn, int* __restrict__ counts) {
     __shared__ int warp_tot[32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int e = threadIdx.x;  // E <= 1024: one expert per thread
     const int n = e < E ? offsets[e + 1] - offsets[e] : 0;
-    const int runs = (n + 127) / 128;
+    const int runs = (n + run - 1) / run;
     int incl = runs;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -384,7 +384,7 @@ __global__ void __launch_bounds__(1024, 1) moe_tiles_kernel(const int32_t* __res
     __syncthreads();
     const int base = warp_tot[warp] + incl - runs;
     for (int r = 0; r < runs; ++r) {
-        const int p0 = offsets[e] + r * 128, np = min(128, n - r * 128);
+        const int p0 = offsets[e] + r * run, np = min(run, n - r * run);
         for (int b = 0; b < rb_gu; ++b) gu[(base + r) * rb_gu + b] = MoeTile{e, b, p0, np};
         for (int b = 0; b < rb_d; ++b) dn[(base + r) * rb_d + b] = MoeTile{e, b, p0, np};
     }
@@ -584,7 +584,9 @@ q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
     if (st != Q38_OK) return st;
 
     const int rb_gu = static_cast<int>(I / 64), rb_d = static_cast<int>(H / 128);
-    const int64_t max_runs = std::min<int64_t>(E, P) + P / 128 + 1;
+    // An expert receives at most one pair per token, so runs never exceed T pairs.
+    const int xr = T <= 32 ? 32 : T <= 64 ? 64 : 128;
+    const int64_t max_runs = std::min<int64_t>(E, P) + P / xr + 1;
     size_t off = 0;
     auto take = [&](size_t bytes) {
         const size_t o = off;
@@ -610,7 +612,7 @@ q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
     void* y = b8 + o_y;
 
     if ((st = sort_launch(ctx, indices, P, E, perm, offs, inv)) != Q38_OK) return st;
-    moe_tiles_kernel<<<1, 1024, 0, ctx->stream>>>(offs, static_cast<int>(E), rb_gu, rb_d, gu, dn, counts);
+    moe_tiles_kernel<<<1, 1024, 0, ctx->stream>>>(offs, static_cast<int>(E), xr, rb_gu, rb_d, gu, dn, counts);
     if ((st = check_launch(ctx, "moe_tiles")) != Q38_OK) return st;
     if ((st = moe_gather_launch(ctx, x, static_cast<int>(H), perm, static_cast<int>(P), top_k, xs, bits)) != Q38_OK)
         return st;
@@ -631,6 +633,7 @@ q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
     g.max_tiles = static_cast<int>(max_runs * rb_gu);
     g.out = hp;
     g.out_ld = static_cast<int>(I);
+    g.xr = xr;
     if ((st = grouped_gate_up(ctx, g, bits)) != Q38_OK) return st;
     GroupedProblem d;
     d.x = hp;
@@ -649,6 +652,7 @@ q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
     d.max_tiles = static_cast<int>(max_runs * rb_d);
     d.out = y;
     d.out_ld = static_cast<int>(H);
+    d.xr = xr;
     if ((st = grouped_down(ctx, d, bits)) != Q38_OK) return st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

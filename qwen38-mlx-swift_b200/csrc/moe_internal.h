@@ -6,7 +6,7 @@
 namespace q38 {
 
 // One tile of a grouped expert product: expert, block of weight rows, and a run of up to
-// 128 consecutive expert-sorted (token, slot) pairs starting at p0.
+// 32, 64 or 128 consecutive expert-sorted (token, slot) pairs starting at p0.
 struct MoeTile {
     int e, rb, p0, np;
 };
@@ -23,6 +23,7 @@ struct GroupedProblem {
     int max_tiles;       // host bound on *ntiles
     void* out;
     int out_ld;
+    int xr;              // longest run of pairs in a tile: 32, 64 or 128
 };
 
 q38_status grouped_gate_up(q38_ctx* ctx, const GroupedProblem& p, int bits);

@@ -35,13 +35,16 @@ constexpr int G_WARP_DEQ0 = 3, G_WARP_EPI0 = 11, G_EPI_WARPS = 4;
 constexpr int G_THREADS = (G_WARP_EPI0 + G_EPI_WARPS) * 32;
 constexpr int G_XBOX = 32;  // activation rows per TMA box
 
-template <int BITS>
+// XR: activation rows (pairs) staged per k-step, the longest run a tile may have.  Short
+// runs (few tokens per expert) get proportionally deeper activation rings for the same
+// 128 KiB, so the ring covers the TMA round trip.
+template <int BITS, int XR>
 struct GF {
     static constexpr int CODE_W = CodeLayout<BITS>::CODE_W;
     static constexpr int CODE_B = G_ROWS * CODE_W * 4;
-    static constexpr int X_B = 2 * G_TOK * 128;
+    static constexpr int X_B = 2 * XR * 128;
     static constexpr int W_STAGE = (CODE_B + 4096 + 1023) / 1024 * 1024;
-    static constexpr int X_STAGES = 4;
+    static constexpr int X_STAGES = (128 * 1024 / X_B) > 16 ? 16 : (128 * 1024 / X_B);
     static constexpr int EX_B = 32 * 64 * 2;  // up values of one 32-pair chunk (gate/up mode)
     static constexpr int W_MAX = (227 * 1024 - 2048 - X_STAGES * X_B - EX_B) / W_STAGE;
     static constexpr int W_STAGES = W_MAX > 8 ? 8 : W_MAX;
@@ -63,20 +66,20 @@ __device__ __forceinline__ void named_bar(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-template <int BITS, bool GATE_UP>
+template <int BITS, bool GATE_UP, int XR>
 __global__ void __launch_bounds__(G_THREADS, 1) qgemm_grouped(
     const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_c0,
     const __grid_constant__ CUtensorMap map_c1, const __grid_constant__ CUtensorMap map_s0,
     const __grid_constant__ CUtensorMap map_s1, const __grid_constant__ CUtensorMap map_b0,
     const __grid_constant__ CUtensorMap map_b1, const GArgs a) {
-    using F = GF<BITS>;
+    using F = GF<BITS, XR>;
     constexpr int SX = F::X_STAGES, SW = F::W_STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
     uint64_t* x_full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* x_empty = x_full + 8;
-    uint64_t* w_full = x_empty + 8;
+    uint64_t* x_empty = x_full + 16;
+    uint64_t* w_full = x_empty + 16;
     uint64_t* w_empty = w_full + 8;
     uint64_t* a_full = w_empty + 8;
     uint64_t* a_free = a_full + G_ASLOTS;
@@ -147,7 +150,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_grouped(
                     mbar_arrive_expect_tx(&x_full[slot], static_cast<uint32_t>(nb) * 2 * G_XBOX * 128);
                     for (int b = 0; b < nb; ++b)
                         for (int kh = 0; kh < 2; ++kh)
-                            tma_load_2d(st + kh * (G_TOK * 128) + b * (G_XBOX * 128), &map_x, &x_full[slot],
+                            tma_load_2d(st + kh * (XR * 128) + b * (G_XBOX * 128), &map_x, &x_full[slot],
                                         ks * G_KS + kh * 64, t.p0 + b * G_XBOX);
                 }
                 if (!ok) break;
@@ -213,7 +216,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_grouped(
                     const uint32_t xa = smem_u32(xring + xs * F::X_B);
 #pragma unroll
                     for (int kk = 0; kk < 8; ++kk) {
-                        const uint64_t bd = smem_desc(xa + (kk >> 2) * (G_TOK * 128) + (kk & 3) * 32, 16, 1024, 2);
+                        const uint64_t bd = smem_desc(xa + (kk >> 2) * (XR * 128) + (kk & 3) * 32, 16, 1024, 2);
                         tc_mma_ts(tmem + G_DCOL + db * G_TOK, tmem + as * 64 + kk * 8, bd, idesc,
                                   (ks > 0 || kk > 0) ? 1u : 0u);
                     }
@@ -317,11 +320,11 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_grouped(
     if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
-template <int BITS, bool GATE_UP>
-q38_status launch_grouped(q38_ctx* ctx, const GroupedProblem& p) {
-    using F = GF<BITS>;
+template <int BITS, bool GATE_UP, int XR>
+q38_status launch_grouped_xr(q38_ctx* ctx, const GroupedProblem& p) {
+    using F = GF<BITS, XR>;
     static_assert(F::W_STAGES >= 4 && F::SMEM <= 227 * 1024, "grouped stages do not fit");
-    auto kern = qgemm_grouped<BITS, GATE_UP>;
+    auto kern = qgemm_grouped<BITS, GATE_UP, XR>;
     static std::mutex mu;
     static bool configured[64] = {};
     {
@@ -377,6 +380,15 @@ q38_status launch_grouped(q38_ctx* ctx, const GroupedProblem& p) {
     if (cudaLaunchKernelEx(&cfg, kern, mx, mc0, mc1, ms0, ms1, mb0, mb1, args) != cudaSuccess)
         return check_launch(ctx, "qgemm_grouped");
     return check_launch(ctx, "qgemm_grouped");
+}
+
+template <int BITS, bool GATE_UP>
+q38_status launch_grouped(q38_ctx* ctx, const GroupedProblem& p) {
+    switch (p.xr) {
+        case 32: return launch_grouped_xr<BITS, GATE_UP, 32>(ctx, p);
+        case 64: return launch_grouped_xr<BITS, GATE_UP, 64>(ctx, p);
+        default: return launch_grouped_xr<BITS, GATE_UP, 128>(ctx, p);
+    }
 }
 
 }  // namespace
