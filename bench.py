@@ -161,6 +161,58 @@ def build_moe(torch, q38, dev, seed=3030):
     return q38.SparseMoeBlock(wr, sw, MOE["k"]), g
 
 
+def run_moe_ep(torch, q38, dev, stream, world, rank, dist, quick=False):
+    """Expert-parallel MoE layer: experts split contiguously over the ranks, T tokens per
+    rank (weak scaling), all-to-all dispatch and return over NCCL; eager steps (the
+    exchange sizes come back to the host), CUDA events, max over ranks."""
+    import parallel
+    H, I, E, k, bits = MOE["H"], MOE["I"], MOE["E"], MOE["k"], MOE["bits"]
+    epr = E // world
+    g = torch.Generator(device=dev).manual_seed(3030 + rank)
+    mine = []
+    for (n, kk) in ((I, H), (I, H), (H, I)):
+        w = torch.randn((epr * n, kk), generator=g, device=dev) * 0.02
+        c, s, b = q38.quantize(w, GROUP, bits, scales_dtype=torch.bfloat16)
+        mine.append((c.view(torch.int32).view(epr, n, -1), s.view(epr, n, -1), b.view(epr, n, -1)))
+        del w
+    gw = torch.Generator(device=dev).manual_seed(3131)  # router weight identical on all ranks
+    wr = (torch.randn((E, H), generator=gw, device=dev) * 0.02).to(torch.bfloat16)
+    moe = parallel.ExpertParallelMoE(wr, mine, E, k, GROUP, bits)
+    out = {}
+    for T in MOE_T:
+        R = 4 if T <= 64 else 2
+        reps = (3 if quick else 10) if T <= 64 else (2 if quick else 5)
+        xs = [torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16) for _ in range(R)]
+        for x in xs:
+            moe(x)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            for x in xs:
+                moe(x)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * R)
+        t = torch.tensor([us], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        us = float(t.item())
+        out[str(T)] = {"tokens_per_s": round(world * T / (us * 1e-6), 1), "us_per_layer": round(us, 2),
+                       "tokens_per_rank": T}
+        del xs
+    del moe, mine
+    torch.cuda.synchronize()
+    return {"metric": "MoE expert-stack tokens/s (router + SwitchGLU + combine, one layer)", "unit": "tokens/s",
+            "per_T": out,
+            "config": {"workload": "Flash-Next MoE layer: hidden 2048, 512 experts, intermediate 512, top-10, "
+                                   "3-bit group 64, router [512, 2048] bf16",
+                       "parallelism": f"expert parallel x{world} ({epr} experts per GPU), T tokens per GPU",
+                       "scaling": "weak",
+                       "timing": "eager layer calls (all-to-all sizes are read on the host), CUDA events, "
+                                 "max over ranks"}}
+
+
 def run_moe(torch, q38, dev, stream, world, dist, quick=False):
     """One MoE layer (router + SwitchGLU + combine) per step at each token count, timed as
     CUDA-graph replays; each replay cycles through R different token batches so that the
@@ -239,6 +291,55 @@ def run_moe(torch, q38, dev, stream, world, dist, quick=False):
 
 
 # ------------------------------------------------------------------------- prefill
+def run_prefill_tp(torch, q38, dev, stream, world, rank, dist, quick=False):
+    """Tensor-parallel dense MLP block at 4096 tokens, 4-bit: gate/up column-sharded,
+    down row-sharded, bf16 all-reduce over NCCL; the whole block (x replicated) per step,
+    strong scaling."""
+    import parallel
+    M, D, F = 4096, 5120, 17408
+    g = torch.Generator(device=dev).manual_seed(4040)
+    mats = []
+    for (n, k) in ((F, D), (F, D), (D, F)):
+        w = torch.randn((n, k), generator=g, device=dev) * 0.02
+        c, s, b = q38.quantize(w, GROUP, 4, scales_dtype=torch.bfloat16)
+        mats.append((c.view(torch.int32), s, b))
+        del w
+    mlp = parallel.TensorParallelMLP(*mats, GROUP, 4)
+    del mats
+    x = torch.randn((M, D), generator=g, device=dev).to(torch.bfloat16)
+    for _ in range(2):
+        mlp(x)
+    torch.cuda.synchronize()
+    reps = 3 if quick else 10
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        mlp(x)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    t = torch.tensor([us], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    us = float(t.item())
+    flops = 3 * 2 * M * F * D
+    peak = None
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        peak = float(json.load(open(p))["bf16_tflops"])
+    tf = flops / (us * 1e-6) / 1e12
+    del mlp, x
+    torch.cuda.synchronize()
+    return {"metric": "prefill quantized GEMM TFLOP/s (tensor pipe)", "unit": "TFLOP/s", "value": round(tf, 1),
+            "us_per_block": round(us, 1),
+            "frac_of_measured_bf16_peak_per_gpu": round(tf / world / peak, 4) if peak else None,
+            "tokens_per_s": round(M / (us * 1e-6), 1),
+            "config": {"workload": "4096 tokens x 4-bit g64 MLP block: gate, up 17408x5120 -> SiLU-gate -> "
+                                   "down 5120x17408, bf16 all-reduce",
+                       "parallelism": f"tensor parallel x{world}", "scaling": "strong",
+                       "timing": "eager block calls, CUDA events, max over ranks"}}
+
+
 def run_prefill(torch, q38, dev, stream, world, dist, quick=False):
     """Dense-27B MLP block products at 4096 tokens, 4-bit group 64: gate and up
     (17408 x 5120) on x [4096, 5120], down (5120 x 17408) on h [4096, 17408]."""
@@ -306,7 +407,8 @@ def run_ours(args, rank, world, local_rank):
     dist = None
     if world > 1:
         import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=dev)
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=180))
 
     cases = []  # (M, N, K, bits, weight triple)
     weights = {}
@@ -467,8 +569,12 @@ def run_ours(args, rank, world, local_rank):
     e2e = {"value": round(world * step_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)}
 
-    moe = None if args.skip_moe else run_moe(torch, q38, dev, stream, world, dist, args.quick)
-    prefill = None if args.skip_prefill else run_prefill(torch, q38, dev, stream, world, dist, args.quick)
+    if world > 1:
+        moe = None if args.skip_moe else run_moe_ep(torch, q38, dev, stream, world, rank, dist, args.quick)
+        prefill = None if args.skip_prefill else run_prefill_tp(torch, q38, dev, stream, world, rank, dist, args.quick)
+    else:
+        moe = None if args.skip_moe else run_moe(torch, q38, dev, stream, world, dist, args.quick)
+        prefill = None if args.skip_prefill else run_prefill(torch, q38, dev, stream, world, dist, args.quick)
 
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:

@@ -203,6 +203,26 @@ Q38_API q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_
                                   const uint32_t* down_w, const void* down_scales, const void* down_biases,
                                   q38_dtype dtype, int group_size, int bits, void* out);
 
+/* h = bf16(silu(g) * u) elementwise with silu(g) = g / (1 + exp(-g)) in fp32: the
+ * SiLU-gate between the gate/up and down projections of the dense MLP (MLX's compiled
+ * silu product).  g, u, h bf16 [n], 16-byte aligned. */
+Q38_API q38_status q38_silu_mul(q38_ctx* ctx, const void* g, const void* u, int64_t n, void* h);
+
+/* Expert-parallel dispatch (experts split contiguously, experts_per_rank per rank): for
+ * j < pairs, rows[j] = x[perm[j] / top_k] (bf16 [*, H]) and local_experts[j] =
+ * indices[perm[j]] % experts_per_rank, where perm orders the flat (token, slot) pairs by
+ * destination rank (q38_moe_sort of indices / experts_per_rank). */
+Q38_API q38_status q38_moe_dispatch_pack(q38_ctx* ctx, const void* x, int64_t H, const int32_t* indices,
+                                         const int32_t* perm, int64_t pairs, int top_k, int64_t experts_per_rank,
+                                         void* rows, int32_t* local_experts);
+
+/* weightedExpertSum over expert outputs held in dispatch order: out_t = bf16(sum_s
+ * scores[t, s] * y[j(t, s)]) in slot order, j(t, s) the position of pair t*top_k + s in
+ * perm.  Pairs whose index is outside [0, E) contribute nothing. */
+Q38_API q38_status q38_moe_combine(q38_ctx* ctx, const void* y, int64_t H, const int32_t* perm,
+                                   const int32_t* indices, const void* scores, int64_t T, int top_k, int64_t E,
+                                   void* out);
+
 /* Allocation-free decode product.  No counterpart in the reference: it exists for
  * callers that must not allocate device memory on the calling path (a host framework
  * that owns all device memory and hands a plugin only its input and output buffers, or

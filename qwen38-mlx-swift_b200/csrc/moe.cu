@@ -424,6 +424,54 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const __nv_bfloat16* _
     }
 }
 
+// h = bf16(silu(g) * u), silu(g) = g / (1 + exp(-g)) in fp32; 8 elements per thread.
+__global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* __restrict__ g,
+                                                       const __nv_bfloat16* __restrict__ u, int64_t n,
+                                                       __nv_bfloat16* __restrict__ h) {
+    const int64_t i = (blockIdx.x * 256LL + threadIdx.x) * 8;
+    if (i >= n) return;
+    if (i + 8 <= n) {
+        const uint4 gv = *reinterpret_cast<const uint4*>(g + i), uv = *reinterpret_cast<const uint4*>(u + i);
+        const uint32_t gq[4] = {gv.x, gv.y, gv.z, gv.w}, uq[4] = {uv.x, uv.y, uv.z, uv.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float g0 = bf16_bits_to_f32(gq[j] & 0xFFFFu), g1 = bf16_bits_to_f32(gq[j] >> 16);
+            const float u0 = bf16_bits_to_f32(uq[j] & 0xFFFFu), u1 = bf16_bits_to_f32(uq[j] >> 16);
+            o[j] = pack_bf16x2(g0 / (1.0f + expf(-g0)) * u0, g1 / (1.0f + expf(-g1)) * u1);
+        }
+        *reinterpret_cast<uint4*>(h + i) = make_uint4(o[0], o[1], o[2], o[3]);
+    } else {
+        for (int64_t j = i; j < n; ++j) {
+            const float gv = __bfloat162float(g[j]);
+            h[j] = __float2bfloat16_rn(gv / (1.0f + expf(-gv)) * __bfloat162float(u[j]));
+        }
+    }
+}
+
+// Expert-parallel dispatch: pair j of the destination order (perm) -> its token's row of
+// x and its expert's index within the destination rank's contiguous block of experts.
+__global__ void __launch_bounds__(256) moe_pack_kernel(const __nv_bfloat16* __restrict__ x, int H,
+                                                       const int32_t* __restrict__ idx,
+                                                       const int32_t* __restrict__ perm, int64_t P, int top_k,
+                                                       int epr, __nv_bfloat16* __restrict__ rows,
+                                                       int32_t* __restrict__ local_e) {
+    const int64_t j = blockIdx.x;
+    if (j >= P) return;
+    const int p = perm[j];
+    const int t = p / top_k;
+    if (threadIdx.x == 0) local_e[j] = idx[p] % epr;
+    const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * H);
+    uint4* dst = reinterpret_cast<uint4*>(rows + static_cast<size_t>(j) * H);
+    for (int c = threadIdx.x; c < H / 8; c += 256) dst[c] = src[c];
+}
+
+__global__ void __launch_bounds__(256) invert_perm_kernel(const int32_t* __restrict__ perm, int64_t P,
+                                                          int32_t* __restrict__ inv) {
+    const int64_t j = blockIdx.x * 256LL + threadIdx.x;
+    if (j < P) inv[perm[j]] = static_cast<int32_t>(j);
+}
+
 q38_status set_dev(q38_ctx* ctx) {
     if (cudaSetDevice(ctx->device) != cudaSuccess) return check_launch(ctx, "cudaSetDevice");
     return Q38_OK;
@@ -667,6 +715,60 @@ q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
                            static_cast<const int32_t*>(inv), indices, static_cast<const __nv_bfloat16*>(scores), top_k,
                            static_cast<int>(E), static_cast<__nv_bfloat16*>(out)) != cudaSuccess)
         return check_launch(ctx, "moe_combine");
+    return check_launch(ctx, "moe_combine");
+}
+
+q38_status q38_silu_mul(q38_ctx* ctx, const void* g, const void* u, int64_t n, void* h) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    if (n < 0) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "silu_mul: negative size");
+    if (n == 0) return Q38_OK;
+    if (!g || !u || !h) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "silu_mul: null pointer");
+    if (!aligned16(g) || !aligned16(u) || !aligned16(h))
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "silu_mul: pointers must be 16-byte aligned");
+    q38_status st = set_dev(ctx);
+    if (st != Q38_OK) return st;
+    const int64_t blocks = (n + 8 * 256 - 1) / (8 * 256);
+    silu_mul_kernel<<<static_cast<unsigned>(blocks), 256, 0, ctx->stream>>>(
+        static_cast<const __nv_bfloat16*>(g), static_cast<const __nv_bfloat16*>(u), n, static_cast<__nv_bfloat16*>(h));
+    return check_launch(ctx, "silu_mul");
+}
+
+q38_status q38_moe_dispatch_pack(q38_ctx* ctx, const void* x, int64_t H, const int32_t* indices, const int32_t* perm,
+                                 int64_t pairs, int top_k, int64_t experts_per_rank, void* rows,
+                                 int32_t* local_experts) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    if (H <= 0 || H % 8 || top_k < 1 || experts_per_rank < 1 || pairs < 0 || pairs > (1 << 30))
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_dispatch_pack: bad sizes");
+    if (pairs == 0) return Q38_OK;
+    if (!x || !indices || !perm || !rows || !local_experts)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_dispatch_pack: null pointer");
+    if (!aligned16(x) || !aligned16(rows)) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_dispatch_pack: rows must be 16-byte aligned");
+    q38_status st = set_dev(ctx);
+    if (st != Q38_OK) return st;
+    moe_pack_kernel<<<static_cast<unsigned>(pairs), 256, 0, ctx->stream>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<int>(H), indices, perm, pairs, top_k,
+        static_cast<int>(experts_per_rank), static_cast<__nv_bfloat16*>(rows), local_experts);
+    return check_launch(ctx, "moe_dispatch_pack");
+}
+
+q38_status q38_moe_combine(q38_ctx* ctx, const void* y, int64_t H, const int32_t* perm, const int32_t* indices,
+                           const void* scores, int64_t T, int top_k, int64_t E, void* out) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    if (H <= 0 || H % 8 || T < 0 || top_k < 1 || E < 1)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_combine: bad sizes");
+    if (T == 0) return Q38_OK;
+    if (!y || !perm || !indices || !scores || !out) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_combine: null pointer");
+    q38_status st = set_dev(ctx);
+    if (st != Q38_OK) return st;
+    const int64_t P = T * top_k;
+    void* scratch;
+    if ((st = ensure_aux(ctx, static_cast<size_t>(P) * 4, &scratch)) != Q38_OK) return st;
+    int32_t* inv = static_cast<int32_t*>(scratch);
+    invert_perm_kernel<<<static_cast<unsigned>((P + 255) / 256), 256, 0, ctx->stream>>>(perm, P, inv);
+    if ((st = check_launch(ctx, "moe_combine")) != Q38_OK) return st;
+    moe_combine_kernel<<<static_cast<unsigned>(T), 256, 0, ctx->stream>>>(
+        static_cast<const __nv_bfloat16*>(y), static_cast<int>(H), inv, indices,
+        static_cast<const __nv_bfloat16*>(scores), top_k, static_cast<int>(E), static_cast<__nv_bfloat16*>(out));
     return check_launch(ctx, "moe_combine");
 }
 

@@ -73,7 +73,7 @@ bool qgemv_fast_supported(int64_t M, int64_t K, int group, int bits, q38_dtype x
 q38_status qgemv_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w,
                       const void* s, const void* b, int64_t N, int bits, void* y);
 
-// Prompt-shaped product on the tensor cores (M >= 17, group 64, K % 512 == 0, bits 2/3/4,
+// Prompt-shaped product on the tensor cores (M >= 17, group 64, K % 128 == 0, bits 2/3/4,
 // bf16).  Uses the scratch workspace for the permuted activations (M*K bf16).
 bool qgemm_tc_supported(int64_t M, int64_t K, int group, int bits, q38_dtype xd, q38_dtype sd,
                         const void* x, const void* w, const void* s, const void* b, const void* y);

@@ -1,5 +1,5 @@
 // Prefill-shaped MLX-affine quantized product on the 5th-generation tensor cores:
-// y[M,N] = x[M,K] . dequant(W)[N,K]^T for M > 16 tokens, group 64, K % 512 == 0,
+// y[M,N] = x[M,K] . dequant(W)[N,K]^T for M > 16 tokens, group 64, K % 128 == 0,
 // bits 2/3/4, bf16 activations and scales.  Replaces the Metal `qmm` kernel behind
 // MLX.quantizedMM (QuantizedLinear.callAsFunction,
 // Sources/Qwen38Core/FlashNext/Qwen4ExpPrequantized.swift:156-159) for prompt-sized inputs.
@@ -13,9 +13,11 @@
 //               ring, completion counted on the pair leader's barrier.
 //   warp 1      allocates the pair's TMEM; in the leader, issues the pair MMAs (A = the
 //               dequantized weights in TMEM, B = activations in shared memory, D in TMEM).
-//   warp 2      weight producer: the CTA's 128 weight rows' packed codes (swizzled box) and
-//               8-group scale/bias boxes into a separate ring, so the small weight stages
-//               run ahead of the large activation stages.
+//   warp 2      weight producer: the CTA's 128 weight rows' packed codes (swizzled box)
+//               into a separate ring, so the small weight stages run ahead of the large
+//               activation stages.  Scales and biases (4 bytes per row and stage) are read
+//               by the dequantizing threads themselves, one stage ahead, which keeps the
+//               scale array's row stride free of TMA's 16-byte rule (K % 128 suffices).
 //   warps 3-10  dequantize, two sets of four alternating stages: one thread per weight row
 //               turns its 128 codes per stage into exact bf16 weights w = scale*q + bias
 //               (magic-number extraction, bf16x2 subtract and fused multiply-add, one
@@ -50,8 +52,7 @@ struct PF {
     static constexpr int CODE_W = CodeLayout<BITS>::CODE_W;  // code words per row per stage
     static constexpr int CODE_B = P_ROWS * CODE_W * 4;       // 4 / 6 / 8 KiB
     static constexpr int X_B = 2 * P_HTOK * 128;          // two 64-element 128-byte-swizzled boxes
-    static constexpr int SB_B = 2 * 2048;                 // scales + biases, {8 groups, 128 rows}
-    static constexpr int W_STAGE = (CODE_B + SB_B + 1023) / 1024 * 1024;
+    static constexpr int W_STAGE = (CODE_B + 1023) / 1024 * 1024;  // codes only
     static constexpr int X_STAGES = 5;
     static constexpr int W_STAGES_MAX = (227 * 1024 - 2048 - X_STAGES * X_B) / W_STAGE;
     static constexpr int W_STAGES = W_STAGES_MAX > 8 ? 8 : W_STAGES_MAX;
@@ -74,6 +75,8 @@ __global__ void __launch_bounds__(256) qgemm_prep(const __nv_bfloat16* __restric
 }
 
 struct PArgs {
+    const uint16_t* scales;  // [N, K/64] bf16 bits
+    const uint16_t* biases;  // same, or null
     __nv_bfloat16* y;
     uint32_t* status;
     int M, N, K, nR, ntiles, has_bias;
@@ -82,8 +85,6 @@ struct PArgs {
 template <int BITS>
 __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__ CUtensorMap map_x,
                                                         const __grid_constant__ CUtensorMap map_codes,
-                                                        const __grid_constant__ CUtensorMap map_scales,
-                                                        const __grid_constant__ CUtensorMap map_biases,
                                                         const PArgs a) {
     using F = PF<BITS>;
     constexpr int SX = F::X_STAGES, SW = F::W_STAGES;
@@ -167,9 +168,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
         // ----------------------------------------------------------- weight producer
         if (lane == 0) {
             prefetch_tensormap(&map_codes);
-            prefetch_tensormap(&map_scales);
-            if (a.has_bias) prefetch_tensormap(&map_biases);
-            const uint32_t wbytes = F::CODE_B + 2048u * (a.has_bias ? 2u : 1u);
+            const uint32_t wbytes = F::CODE_B;
             int gs = 0;
             for (; gs < total && !*abort_flag; ++gs) {
                 const int slot = gs % SW, tile = pair + (gs / ksteps) * npairs, ks = gs % ksteps;
@@ -178,8 +177,6 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
                 uint8_t* st = wring + slot * F::W_STAGE;
                 mbar_arrive_expect_tx(&w_full[slot], wbytes);
                 tma_load_2d(st, &map_codes, &w_full[slot], k0 * BITS / 32, n0);
-                tma_load_2d(st + F::CODE_B, &map_scales, &w_full[slot], (k0 / 512) * 8, n0);
-                if (a.has_bias) tma_load_2d(st + F::CODE_B + 2048, &map_biases, &w_full[slot], (k0 / 512) * 8, n0);
             }
             for (int i = 1; i <= (gs < SW ? gs : SW); ++i)
                 mbar_wait(&w_full[(gs - i) % SW], ((gs - i) / SW) & 1, a.status);
@@ -225,15 +222,30 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
         const int row = quarter * 32 + lane;
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
         const uint32_t a_full_leader = mapa_shared(a_full, 0);
+        // Scales and biases of the two groups of a stage come straight from global memory
+        // (4 bytes each per row), loaded one stage of this set ahead.
+        const int G = a.K / 64;
+        auto sb_load = [&](int g, uint32_t& sv, uint32_t& bv) {
+            sv = 0u;
+            bv = 0u;
+            if (g >= total) return;
+            const int tile = pair + (g / ksteps) * npairs;
+            const int n = (tile % a.nR) * (2 * P_ROWS) + rank * P_ROWS + row;
+            if (n >= a.N) return;
+            const size_t off = static_cast<size_t>(n) * G + 2 * (g % ksteps);
+            sv = __ldg(reinterpret_cast<const unsigned int*>(a.scales + off));
+            if (a.biases) bv = __ldg(reinterpret_cast<const unsigned int*>(a.biases + off));
+        };
+        uint32_t s_next, b_next;
+        sb_load(set, s_next, b_next);
         for (int gs = set; gs < total; gs += 2) {
-            const int slot = gs % SW, as = gs % P_ASLOTS, ks = gs % ksteps;
+            const int slot = gs % SW, as = gs % P_ASLOTS;
+            const uint32_t s01 = s_next, b01 = b_next;
+            sb_load(gs + 2, s_next, b_next);
             if (!p_wait_warp<false>(&w_full[slot], (gs / SW) & 1, ab)) break;
             // Dequantize into registers first: the TMEM slot is waited for only afterwards,
             // so the arithmetic overlaps the MMAs that still read the slot.
             const uint8_t* st = wring + slot * F::W_STAGE;
-            const uint32_t* sb = reinterpret_cast<const uint32_t*>(st + F::CODE_B);
-            const uint32_t s01 = sb[row * 4 + (ks & 3)];
-            const uint32_t b01 = a.has_bias ? sb[512 + row * 4 + (ks & 3)] : 0u;
             uint32_t av0[32], av1[32];
             dequant_group<BITS>(st, row, 0, s01 & 0xFFFFu, b01 & 0xFFFFu, av0);
             dequant_group<BITS>(st, row, 1, s01 >> 16, b01 >> 16, av1);
@@ -333,14 +345,11 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
     if (st != Q38_OK) return st;
     __nv_bfloat16* xp = static_cast<__nv_bfloat16*>(ctx->workspace);
 
-    CUtensorMap mx, mc, ms, mb;
+    CUtensorMap mx, mc;
     const CUtensorMapSwizzle cswz = code_swizzle<BITS>();
     if (!make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xp, K, M, 64, P_HTOK, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_map_2d(&mc, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w, static_cast<uint64_t>(K) * BITS / 32, N,
-                     F::CODE_W, P_ROWS, cswz) ||
-        !make_map_2d(&ms, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s, K / 64, N, 8, P_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b ? b : s, K / 64, N, 8, P_ROWS,
-                     CU_TENSOR_MAP_SWIZZLE_NONE))
+                     F::CODE_W, P_ROWS, cswz))
         return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: tensor map encoding failed");
 
     static_assert(F::W_STAGES >= 4 && F::SMEM <= 227 * 1024, "prefill stages do not fit");
@@ -370,6 +379,8 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
         return check_launch(ctx, "qgemm_prep");
 
     PArgs args;
+    args.scales = static_cast<const uint16_t*>(s);
+    args.biases = static_cast<const uint16_t*>(b);
     args.y = static_cast<__nv_bfloat16*>(y);
     args.status = ctx->d_status;
     args.M = M;
@@ -385,7 +396,7 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
     cfg.stream = ctx->stream;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    if (cudaLaunchKernelEx(&cfg, qgemm_tc<BITS>, mx, mc, ms, mb, args) != cudaSuccess)
+    if (cudaLaunchKernelEx(&cfg, qgemm_tc<BITS>, mx, mc, args) != cudaSuccess)
         return check_launch(ctx, "qgemm_tc");
     return check_launch(ctx, "qgemm_tc");
 }
@@ -394,7 +405,7 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
 
 bool qgemm_tc_supported(int64_t M, int64_t K, int group, int bits, q38_dtype xd, q38_dtype sd, const void* x,
                         const void* w, const void* s, const void* b, const void* y) {
-    if (M < 17 || M > (1 << 24) || group != 64 || K % 512 != 0 || K <= 0 || K > (1 << 20)) return false;
+    if (M < 17 || M > (1 << 24) || group != 64 || K % 128 != 0 || K <= 0 || K > (1 << 20)) return false;
     if (bits != 2 && bits != 3 && bits != 4) return false;
     if (xd != Q38_BF16 || sd != Q38_BF16) return false;
     auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };

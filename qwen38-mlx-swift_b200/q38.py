@@ -64,6 +64,9 @@ _sig("q38_hadamard_quantized_matmul", [_P, _P, _I, _I, _i, _P, _i, _P, _P, _P, _
 _sig("q38_moe_route", [_P, _P, _I, _I, _i, _P, _I, _i, _i, _P, _P, _P])
 _sig("q38_moe_route_logits", [_P, _P, _I, _I, _i, _i, _P, _P, _P])
 _sig("q38_moe_sort", [_P, _P, _I, _I, _P, _P])
+_sig("q38_silu_mul", [_P, _P, _P, _I, _P])
+_sig("q38_moe_dispatch_pack", [_P, _P, _I, _P, _P, _I, _i, _I, _P, _P])
+_sig("q38_moe_combine", [_P, _P, _I, _P, _P, _P, _I, _i, _I, _P])
 _sig("q38_switch_glu", [_P, _P, _I, _I, _I, _I, _i, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _i, _i, _i, _P])
 
 
@@ -316,6 +319,44 @@ def switch_glu(x: torch.Tensor, indices: torch.Tensor, scores: torch.Tensor, gat
                                     _ptr(_as_u32(gw)), _ptr(gs), _ptr(gb), _ptr(_as_u32(uw)), _ptr(us), _ptr(ub),
                                     _ptr(_as_u32(dw)), _ptr(ds), _ptr(db), _DTYPE[x.dtype], group_size, bits,
                                     _ptr(out)))
+    return out
+
+
+def silu_mul(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    """h = bf16(silu(g) * u), fp32 inside (the MLP's SiLU-gate)."""
+    _need(g, "g"), _need(u, "u")
+    if g.shape != u.shape or g.dtype != torch.bfloat16 or u.dtype != torch.bfloat16:
+        raise ValueError("silu_mul: g and u must be bf16 tensors of one shape")
+    h = torch.empty_like(g)
+    ctx = _bind(g)
+    _check(ctx, _lib.q38_silu_mul(ctx, _ptr(g), _ptr(u), g.numel(), _ptr(h)))
+    return h
+
+
+def moe_dispatch_pack(x: torch.Tensor, indices: torch.Tensor, perm: torch.Tensor, experts_per_rank: int):
+    """Rows of x and rank-local expert ids of the (token, slot) pairs in perm's order."""
+    _need(x, "x"), _need(indices, "indices"), _need(perm, "perm")
+    T, H = x.shape
+    k = indices.shape[-1]
+    P = perm.numel()
+    rows = torch.empty((P, H), dtype=x.dtype, device=x.device)
+    local = torch.empty((P,), dtype=torch.int32, device=x.device)
+    ctx = _bind(x)
+    _check(ctx, _lib.q38_moe_dispatch_pack(ctx, _ptr(x), H, _ptr(indices), _ptr(perm), P, k, experts_per_rank,
+                                           _ptr(rows), _ptr(local)))
+    return rows, local
+
+
+def moe_combine(y: torch.Tensor, perm: torch.Tensor, indices: torch.Tensor, scores: torch.Tensor,
+                num_experts: int) -> torch.Tensor:
+    """weightedExpertSum of expert outputs held in perm's order: [P, H] -> [T, H]."""
+    _need(y, "y"), _need(perm, "perm"), _need(indices, "indices"), _need(scores, "scores")
+    T, k = indices.shape
+    H = y.shape[-1]
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=indices.device)
+    ctx = _bind(indices)
+    _check(ctx, _lib.q38_moe_combine(ctx, _ptr(y), H, _ptr(perm), _ptr(indices), _ptr(scores), T, k,
+                                     num_experts, _ptr(out)))
     return out
 
 

@@ -1,0 +1,172 @@
+"""Host logic of the multi-GPU layouts on CPU: two gloo ranks run ExpertParallelMoE and
+TensorParallelMLP with the oracle standing in for the kernels.
+
+* Expert parallel: the routed output of every rank's tokens must equal, bit for bit, the
+  single-process oracle SwitchGLU on the same tokens -- the dispatch, the expert-local
+  products, the return and the slot-ordered combine reproduce its arithmetic exactly.
+* Tensor parallel: the all-reduced output must match the unsharded oracle MLP within
+  2e-2 * RMS plus one bf16 step of the output, with error RMS <= 1e-2 * RMS: every rank's
+  partial product is rounded to bf16 before the sum, and partials can exceed the total.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import oracle as O
+
+
+def bf(t):  # torch bf16 (CPU) -> numpy uint16 bits
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def tb(a):  # numpy uint16 bits -> torch bf16 (CPU)
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16)
+
+
+class OracleOps:
+    """The oracle behind the kernel interface of parallel.DeviceOps (CPU tensors)."""
+
+    def qmm(self, x, c, s, b, group, bits):
+        return tb(O.qmm(bf(x), c.numpy().view(np.uint32), bf(s), None if b is None else bf(b), group, bits))
+
+    def silu_mul(self, g, u):
+        gf, uf = O.bf16_to_f32(bf(g)), O.bf16_to_f32(bf(u))
+        return tb(O.f32_to_bf16((gf / (np.float32(1) + np.exp(-gf)) * uf).astype(np.float32)))
+
+    def route(self, x, wr, k, normalize=True):
+        idx, sc = O.moe_route(bf(x), bf(wr), k, normalize)
+        return torch.from_numpy(idx), tb(sc)
+
+    def sort(self, keys, n):
+        perm, off = O.sort_by_expert(keys.numpy(), n)
+        return torch.from_numpy(perm), torch.from_numpy(off)
+
+    def pack(self, x, idx, perm, epr):
+        k = idx.shape[1]
+        p = perm.numpy()
+        rows = x[torch.from_numpy(p // k)].contiguous()
+        loc = torch.from_numpy((idx.numpy().reshape(-1)[p] % epr).astype(np.int32))
+        return rows, loc
+
+    def local_experts(self, rows, loc, weights, group, bits):
+        n = rows.shape[0]
+        if n == 0:
+            return rows.clone()
+        ones = np.full((n, 1), O.f32_to_bf16(np.array([1.0], np.float32))[0], np.uint16)
+        w = [(c.numpy().view(np.uint32), bf(s), None if b is None else bf(b)) for (c, s, b) in weights]
+        return tb(O.switch_glu(bf(rows), loc.numpy().reshape(n, 1), ones, *w, group, bits))
+
+    def combine(self, y, perm, idx, sc, E):
+        T, k = idx.shape
+        inv = np.empty(T * k, np.int64)
+        inv[perm.numpy()] = np.arange(T * k)
+        yf, s = O.bf16_to_f32(bf(y)), O.bf16_to_f32(bf(sc))
+        out = np.zeros((T, y.shape[1]), np.float32)
+        for t in range(T):
+            for j in range(k):
+                out[t] += np.float32(s[t, j]) * yf[inv[t * k + j]]
+        return tb(O.f32_to_bf16(out))
+
+
+def free_port():
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]
+
+
+H, I, E, K_TOP, BITS = 256, 128, 8, 3, 3
+
+
+def moe_weights():
+    mk = lambda seed, shape: O.quantize(O.normal_f32(seed, shape, 0.05), 64, BITS)
+    return mk(11, (E, I, H)), mk(12, (E, I, H)), mk(13, (E, H, I))
+
+
+def ep_worker(rank, world, port, q):
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "qwen38-mlx-swift_b200"))
+    from parallel import ExpertParallelMoE
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        gate, up, down = moe_weights()
+        epr = E // world
+        sl = slice(rank * epr, (rank + 1) * epr)
+        mine = [(torch.from_numpy(c[sl].view(np.int32)), tb(s[sl]), tb(b[sl])) for (c, s, b) in (gate, up, down)]
+        wr = O.normal_bf16(14, (E, H), 0.05)
+        x = O.normal_bf16(100 + rank, (5 + rank, H))
+        moe = ExpertParallelMoE(tb(wr), mine, E, K_TOP, 64, BITS, ops=OracleOps())
+        out = moe(tb(x))
+        idx, sc = O.moe_route(x, wr, K_TOP, True)
+        ref = O.switch_glu(x, idx, sc, gate, up, down, 64, BITS)
+        q.put((rank, bool(np.array_equal(bf(out), ref)), int(np.abs(O.bf16_to_f32(bf(out)) - O.bf16_to_f32(ref)).max() * 1e6)))
+    finally:
+        dist.destroy_process_group()
+
+
+def tp_worker(rank, world, port, q):
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "qwen38-mlx-swift_b200"))
+    from parallel import TensorParallelMLP
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        D, F = 256, 512
+        mk = lambda seed, shape: O.quantize(O.normal_f32(seed, shape, 0.05), 64, 4)
+        gate, up, down = mk(21, (F, D)), mk(22, (F, D)), mk(23, (D, F))
+        to_t = lambda w: (torch.from_numpy(w[0].view(np.int32)), tb(w[1]), tb(w[2]))
+        x = O.normal_bf16(24, (7, D))
+        mlp = TensorParallelMLP(to_t(gate), to_t(up), to_t(down), 64, 4, ops=OracleOps(), reduce_dtype=torch.float32)
+        y = O.bf16_to_f32(bf(mlp(tb(x)))).astype(np.float64)
+        ops = OracleOps()
+        g, u = ops.qmm(tb(x), *to_t(gate), 64, 4), ops.qmm(tb(x), *to_t(up), 64, 4)
+        ref = O.bf16_to_f32(bf(ops.qmm(ops.silu_mul(g, u), *to_t(down), 64, 4))).astype(np.float64)
+        rms = np.sqrt((ref ** 2).mean())
+        step = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(ref), 2.0 ** -126))) - 7)
+        q.put((rank, float((np.abs(y - ref) - step).max() / rms), float(np.sqrt(((y - ref) ** 2).mean()) / rms)))
+    finally:
+        dist.destroy_process_group()
+
+
+def run2(fn):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=fn, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=240) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    return sorted(res)
+
+
+def test_expert_parallel_exchange_matches_single_process():
+    res = run2(ep_worker)
+    assert all(ok for (_, ok, _) in res), res
+
+
+def test_tensor_parallel_mlp_matches_unsharded():
+    res = run2(tp_worker)
+    assert all(err <= 2e-2 and erms <= 1e-2 for (_, err, erms) in res), res
+
+
+def test_shard_helpers_split_whole_groups_and_words():
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "qwen38-mlx-swift_b200"))
+    from parallel import shard_k, shard_rows
+    c, s, b = O.quantize(O.normal_f32(31, (64, 17408), 0.02), 64, 4)
+    ct, st, bt = torch.from_numpy(c.view(np.int32)), tb(s), tb(b)
+    parts = [shard_k(ct, st, bt, r, 8, 4) for r in range(8)]
+    assert all(p[0].shape == (64, 2176 * 4 // 32) and p[1].shape == (64, 34) for p in parts)
+    assert np.array_equal(np.concatenate([p[0].numpy() for p in parts], axis=1), c.view(np.int32))
+    rows = [shard_rows(ct, st, bt, r, 4) for r in range(4)]
+    assert np.array_equal(np.concatenate([p[0].numpy() for p in rows], axis=0), c.view(np.int32))
+    with pytest.raises(ValueError):
+        shard_k(ct, st, bt, 0, 3, 4)

@@ -20,7 +20,7 @@ pytestmark = pytest.mark.gpu
 
 @pytest.mark.parametrize("bits", [2, 3, 4])
 @pytest.mark.parametrize("M,N,K", [(17, 128, 512), (64, 200, 1024), (128, 256, 512), (200, 1000, 2048),
-                                   (333, 384, 1536)])
+                                   (333, 384, 1536), (300, 512, 2176), (96, 640, 1152), (257, 264, 128)])
 def test_prefill_parity(q38, bits, M, N, K):
     c, s, b = make_weight(5000 + bits + N, N, K, bits)
     x = O.normal_bf16(5100 + M, (M, K))
