@@ -631,9 +631,12 @@ q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
     q38_status st = set_dev(ctx);
     if (st != Q38_OK) return st;
 
-    const int rb_gu = static_cast<int>(I / 64), rb_d = static_cast<int>(H / 128);
-    // An expert receives at most one pair per token, so runs never exceed T pairs.
-    const int xr = T <= 32 ? 32 : T <= 64 ? 64 : 128;
+    // Few tokens: every expert sees a handful of pairs -> CUDA-core kernels with runs of
+    // up to 8 pairs.  Otherwise the grouped tensor-core kernels; an expert receives at most
+    // one pair per token, so runs never exceed T pairs.
+    const bool small = T <= 64;
+    const int xr = small ? moe_gemv_run_pairs() : 128;
+    const int rb_gu = static_cast<int>(small ? I / 32 : I / 64), rb_d = static_cast<int>(H / 128);
     const int64_t max_runs = std::min<int64_t>(E, P) + P / xr + 1;
     size_t off = 0;
     auto take = [&](size_t bytes) {
@@ -682,7 +685,7 @@ q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
     g.out = hp;
     g.out_ld = static_cast<int>(I);
     g.xr = xr;
-    if ((st = grouped_gate_up(ctx, g, bits)) != Q38_OK) return st;
+    if ((st = small ? moe_gemv_gate_up(ctx, g, bits) : grouped_gate_up(ctx, g, bits)) != Q38_OK) return st;
     GroupedProblem d;
     d.x = hp;
     d.pairs = static_cast<int>(P);
@@ -701,7 +704,7 @@ q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
     d.out = y;
     d.out_ld = static_cast<int>(H);
     d.xr = xr;
-    if ((st = grouped_down(ctx, d, bits)) != Q38_OK) return st;
+    if ((st = small ? moe_gemv_down(ctx, d, bits) : grouped_down(ctx, d, bits)) != Q38_OK) return st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
