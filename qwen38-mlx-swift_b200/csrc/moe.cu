@@ -636,7 +636,8 @@ q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
     // one pair per token, so runs never exceed T pairs.
     const bool small = T <= 64;
     const int xr = small ? moe_gemv_run_pairs() : 128;
-    const int rb_gu = static_cast<int>(small ? I / 32 : I / 64), rb_d = static_cast<int>(H / 128);
+    const int rb_gu = static_cast<int>(small ? I / moe_gemv_rows_per_tile(H) : I / 64);
+    const int rb_d = static_cast<int>(small ? H / moe_gemv_rows_per_tile(I) : H / 128);
     const int64_t max_runs = std::min<int64_t>(E, P) + P / xr + 1;
     size_t off = 0;
     auto take = [&](size_t bytes) {

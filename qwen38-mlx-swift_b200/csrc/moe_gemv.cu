@@ -23,6 +23,7 @@ namespace q38 {
 namespace {
 
 constexpr int MG_NP = 8;        // pairs per run
+constexpr int MG_WIN = 16;      // 16-code windows per thread slice (256 k)
 constexpr int MG_THREADS = 256;
 
 __device__ __forceinline__ float fma_bf16(uint32_t a_half_lo_hi, uint32_t b_half_lo_hi, float c, bool hi) {
@@ -39,25 +40,23 @@ __device__ __forceinline__ float fma_bf16(uint32_t a_half_lo_hi, uint32_t b_half
     return d;
 }
 
-// Code window (16 codes) w of a row -> 8 bf16x2 operands in extraction order.
+// Window wl (16 codes) of a slice held in registers -> 8 bf16x2 operands.
 template <int BITS>
-__device__ __forceinline__ void window_ops(const uint32_t* __restrict__ row, int w, uint32_t* v) {
+__device__ __forceinline__ void slice_window(const uint32_t* c, int wl, uint32_t* v) {
     uint32_t win[2];
     if constexpr (BITS == 2) {
-        win[0] = __ldg(row + w);
+        win[0] = c[wl];
     } else if constexpr (BITS == 4) {
-        const uint2 u = __ldg(reinterpret_cast<const uint2*>(row) + w);
-        win[0] = u.x;
-        win[1] = u.y;
+        win[0] = c[2 * wl];
+        win[1] = c[2 * wl + 1];
     } else {
-        const int k0 = (3 * w) >> 1;
-        const uint32_t a = __ldg(row + k0), b = __ldg(row + k0 + 1);
-        if (w & 1) {
-            win[0] = __funnelshift_r(a, b, 16);
-            win[1] = b >> 16;
+        const int k0 = (3 * wl) >> 1;
+        if (wl & 1) {
+            win[0] = __funnelshift_r(c[k0], c[k0 + 1], 16);
+            win[1] = c[k0 + 1] >> 16;
         } else {
-            win[0] = a;
-            win[1] = b;
+            win[0] = c[k0];
+            win[1] = c[k0 + 1];
         }
     }
     extract<BITS>(win, v);
@@ -69,8 +68,9 @@ __global__ void __launch_bounds__(MG_THREADS) moe_gemv_kernel(
     const uint32_t* __restrict__ w0, const uint32_t* __restrict__ w1, const uint16_t* __restrict__ s0,
     const uint16_t* __restrict__ s1, const uint16_t* __restrict__ b0, const uint16_t* __restrict__ b1,
     int rows_per_expert, __nv_bfloat16* __restrict__ out, int out_ld) {
-    constexpr int RW = GATE_UP ? 1 : 4;  // row warps (32 rows each)
-    constexpr int KW = 8 / RW;          // k-slices
+    // Slices of 256 k per row: KS = K / 256; the 8 warps split as KW k-warps x RW row-warps.
+    const int KS = K / (16 * MG_WIN);
+    const int KW = KS < 8 ? KS : 8, RW = 8 / KW;
     extern __shared__ __align__(16) uint8_t sm[];
     griddep_wait();
     griddep_launch_dependents();
@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(MG_THREADS) moe_gemv_kernel(
     const MoeTile t = tiles[blockIdx.x];
     const int nw = K / 16;  // code windows per row
     uint32_t* xsm = reinterpret_cast<uint32_t*>(sm);                   // [NP][K/2] bf16x2
-    float* red = reinterpret_cast<float*>(sm + MG_NP * K * 2);         // [KW][RW*32][2][NP]
+    float* red = reinterpret_cast<float*>(sm + MG_NP * K * 2);         // [8 warps][32][2][NP]
 
     // stage the run's activations
     const int np = t.np;
@@ -100,57 +100,86 @@ __global__ void __launch_bounds__(MG_THREADS) moe_gemv_kernel(
     float acc0[MG_NP], acc1[MG_NP];
 #pragma unroll
     for (int p = 0; p < MG_NP; ++p) acc0[p] = acc1[p] = 0.f;
-    const int wb = kw * (nw / KW), we = wb + nw / KW;
-    uint32_t s2a = 0, s2b = 0, b2a[8], b2b[8];
-    for (int w = wb; w < we; ++w) {
-        if (w == wb || (w & 3) == 0) {  // new group: scale broadcast and 2^p-scaled biases
-            const int g = w >> 2;
-            const uint32_t sa = __ldg(s0 + grow * G + g), ba = b0 ? __ldg(b0 + grow * G + g) : 0u;
-            s2a = sa * 0x10001u;
-            const float bfa = bf16_bits_to_f32(ba);
+    // This thread's slice: MG_WIN windows of 16 codes (MG_WIN/4 groups), loaded up front as
+    // 16-byte vectors so that one memory latency covers the whole slice.
+    constexpr int SW_WORDS = MG_WIN * BITS / 2;  // code words of the slice
+    for (int slice = kw; slice < KS; slice += KW) {
+    const int wb = slice * MG_WIN;
+    uint32_t ca[SW_WORDS], cb[GATE_UP ? SW_WORDS : 1];
+    {
+        const uint4* pa = reinterpret_cast<const uint4*>(c0 + wb * BITS / 2);
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-                b2a[q] = (__float_as_uint(bfa * (1.0f / pair_mult<BITS>(q, 0))) >> 16) |
-                         (__float_as_uint(bfa * (1.0f / pair_mult<BITS>(q, 1))) & 0xFFFF0000u);
-            if constexpr (GATE_UP) {
-                const uint32_t sb = __ldg(s1 + grow * G + g), bb = b1 ? __ldg(b1 + grow * G + g) : 0u;
-                s2b = sb * 0x10001u;
-                const float bfb = bf16_bits_to_f32(bb);
+        for (int i = 0; i < SW_WORDS / 4; ++i) {
+            const uint4 u = __ldg(pa + i);
+            ca[4 * i] = u.x; ca[4 * i + 1] = u.y; ca[4 * i + 2] = u.z; ca[4 * i + 3] = u.w;
+        }
+        if constexpr (GATE_UP) {
+            const uint4* pb = reinterpret_cast<const uint4*>(c1 + wb * BITS / 2);
 #pragma unroll
-                for (int q = 0; q < 8; ++q)
-                    b2b[q] = (__float_as_uint(bfb * (1.0f / pair_mult<BITS>(q, 0))) >> 16) |
-                             (__float_as_uint(bfb * (1.0f / pair_mult<BITS>(q, 1))) & 0xFFFF0000u);
+            for (int i = 0; i < SW_WORDS / 4; ++i) {
+                const uint4 u = __ldg(pb + i);
+                cb[4 * i] = u.x; cb[4 * i + 1] = u.y; cb[4 * i + 2] = u.z; cb[4 * i + 3] = u.w;
             }
         }
-        uint32_t va[8], vb[8];
-        window_ops<BITS>(c0, w, va);
+    }
+    constexpr int NG = MG_WIN / 4;
+    uint32_t sga[NG], bga[NG], sgb[NG], bgb[NG];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) va[q] = bf2_fma(bf2_sub(va[q], MAGIC), s2a, b2a[q]);
+    for (int i = 0; i < NG; ++i) {
+        const size_t gi = grow * G + wb / 4 + i;
+        sga[i] = __ldg(s0 + gi);
+        bga[i] = b0 ? __ldg(b0 + gi) : 0u;
         if constexpr (GATE_UP) {
-            window_ops<BITS>(c1, w, vb);
+            sgb[i] = __ldg(s1 + gi);
+            bgb[i] = b1 ? __ldg(b1 + gi) : 0u;
+        }
+    }
 #pragma unroll
-            for (int q = 0; q < 8; ++q) vb[q] = bf2_fma(bf2_sub(vb[q], MAGIC), s2b, b2b[q]);
+    for (int i = 0; i < NG; ++i) {
+        const uint32_t s2a = sga[i] * 0x10001u, s2b = GATE_UP ? sgb[i] * 0x10001u : 0u;
+        uint32_t b2a[8], b2b[8];
+        const float bfa = bf16_bits_to_f32(bga[i]), bfb = GATE_UP ? bf16_bits_to_f32(bgb[i]) : 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            b2a[q] = (__float_as_uint(bfa * (1.0f / pair_mult<BITS>(q, 0))) >> 16) |
+                     (__float_as_uint(bfa * (1.0f / pair_mult<BITS>(q, 1))) & 0xFFFF0000u);
+            b2b[q] = (__float_as_uint(bfb * (1.0f / pair_mult<BITS>(q, 0))) >> 16) |
+                     (__float_as_uint(bfb * (1.0f / pair_mult<BITS>(q, 1))) & 0xFFFF0000u);
         }
 #pragma unroll
-        for (int p = 0; p < MG_NP; ++p) {
-            if (p < np) {
-                const uint4* xq = reinterpret_cast<const uint4*>(xsm + p * (K / 2) + w * 8);
-                const uint4 xa = xq[0], xb = xq[1];
-                const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+        for (int j = 0; j < 4; ++j) {
+            const int wl = 4 * i + j, w = wb + wl;
+            uint32_t va[8], vb[8];
+            slice_window<BITS>(ca, wl, va);
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    acc0[p] = fma_bf16(va[q], xw[q], acc0[p], false);
-                    acc0[p] = fma_bf16(va[q], xw[q], acc0[p], true);
-                    if constexpr (GATE_UP) {
-                        acc1[p] = fma_bf16(vb[q], xw[q], acc1[p], false);
-                        acc1[p] = fma_bf16(vb[q], xw[q], acc1[p], true);
+            for (int q = 0; q < 8; ++q) va[q] = bf2_fma(bf2_sub(va[q], MAGIC), s2a, b2a[q]);
+            if constexpr (GATE_UP) {
+                slice_window<BITS>(cb, wl, vb);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) vb[q] = bf2_fma(bf2_sub(vb[q], MAGIC), s2b, b2b[q]);
+            }
+#pragma unroll
+            for (int p = 0; p < MG_NP; ++p) {
+                if (p < np) {
+                    const uint4* xq = reinterpret_cast<const uint4*>(xsm + p * (K / 2) + w * 8);
+                    const uint4 xa = xq[0], xb = xq[1];
+                    const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        acc0[p] = fma_bf16(va[q], xw[q], acc0[p], false);
+                        acc0[p] = fma_bf16(va[q], xw[q], acc0[p], true);
+                        if constexpr (GATE_UP) {
+                            acc1[p] = fma_bf16(vb[q], xw[q], acc1[p], false);
+                            acc1[p] = fma_bf16(vb[q], xw[q], acc1[p], true);
+                        }
                     }
                 }
             }
         }
     }
+    }  // slices
     // reduce the k-slices through shared memory
-    const int slot = (kw * (RW * 32) + rw * 32 + lane) * 2 * MG_NP;
+    const int slot = (warp * 32 + lane) * 2 * MG_NP;
 #pragma unroll
     for (int p = 0; p < MG_NP; ++p) {
         red[slot + p] = acc0[p];
@@ -162,7 +191,7 @@ __global__ void __launch_bounds__(MG_THREADS) moe_gemv_kernel(
 #pragma unroll
     for (int p = 0; p < MG_NP; ++p) f0[p] = f1[p] = 0.f;
     for (int k2 = 0; k2 < KW; ++k2) {
-        const int sl = (k2 * (RW * 32) + rw * 32 + lane) * 2 * MG_NP;
+        const int sl = ((k2 * RW + rw) * 32 + lane) * 2 * MG_NP;
 #pragma unroll
         for (int p = 0; p < MG_NP; ++p) {
             f0[p] += red[sl + p];
@@ -191,8 +220,7 @@ __global__ void __launch_bounds__(MG_THREADS) moe_gemv_kernel(
 
 template <int BITS, bool GATE_UP>
 q38_status launch_mg(q38_ctx* ctx, const GroupedProblem& p) {
-    constexpr int RW = GATE_UP ? 1 : 4, KW = 8 / RW;
-    const size_t smem = static_cast<size_t>(MG_NP) * p.K * 2 + static_cast<size_t>(KW) * RW * 32 * 2 * MG_NP * 4;
+    const size_t smem = static_cast<size_t>(MG_NP) * p.K * 2 + static_cast<size_t>(8) * 32 * 2 * MG_NP * 4;
     auto kern = moe_gemv_kernel<BITS, GATE_UP>;
     if (smem > 48 * 1024 &&
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
@@ -218,6 +246,11 @@ q38_status launch_mg(q38_ctx* ctx, const GroupedProblem& p) {
 }  // namespace
 
 int moe_gemv_run_pairs() { return MG_NP; }
+
+int moe_gemv_rows_per_tile(int64_t K) {
+    const int64_t ks = K / (16 * MG_WIN);
+    return 32 * static_cast<int>(8 / (ks < 8 ? ks : 8));
+}
 
 q38_status moe_gemv_gate_up(q38_ctx* ctx, const GroupedProblem& p, int bits) {
     switch (bits) {
