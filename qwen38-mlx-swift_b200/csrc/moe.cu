@@ -66,23 +66,30 @@ __global__ void __launch_bounds__(128) router_logits_small(const __nv_bfloat16* 
     if (e >= E) return;
     const uint4* wrow = reinterpret_cast<const uint4*>(wr + static_cast<size_t>(e) * H);
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int v = lane; v < vec; v += 32) {
-        const uint4 u = wrow[v];
-        const uint32_t q[4] = {u.x, u.y, u.z, u.w};
-        float wv[8];
+    for (int v0 = lane; v0 < vec; v0 += 32 * 8) {
+        uint4 wu[8];  // eight 16-byte loads in flight per lane
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            wv[2 * j] = bf16_bits_to_f32(q[j] & 0xFFFFu);
-            wv[2 * j + 1] = bf16_bits_to_f32(q[j] >> 16);
-        }
+        for (int i = 0; i < 8; ++i) wu[i] = v0 + 32 * i < vec ? __ldg(wrow + v0 + 32 * i) : make_uint4(0, 0, 0, 0);
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-            const uint4 xu = xs4[t * vec + v];
-            const uint32_t xq[4] = {xu.x, xu.y, xu.z, xu.w};
+        for (int i = 0; i < 8; ++i) {
+            const int v = v0 + 32 * i;
+            if (v >= vec) break;
+            const uint32_t q[4] = {wu[i].x, wu[i].y, wu[i].z, wu[i].w};
+            float wv[8];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                acc[t] = fmaf(wv[2 * j], bf16_bits_to_f32(xq[j] & 0xFFFFu), acc[t]);
-                acc[t] = fmaf(wv[2 * j + 1], bf16_bits_to_f32(xq[j] >> 16), acc[t]);
+                wv[2 * j] = bf16_bits_to_f32(q[j] & 0xFFFFu);
+                wv[2 * j + 1] = bf16_bits_to_f32(q[j] >> 16);
+            }
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                const uint4 xu = xs4[t * vec + v];
+                const uint32_t xq[4] = {xu.x, xu.y, xu.z, xu.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    acc[t] = fmaf(wv[2 * j], bf16_bits_to_f32(xq[j] & 0xFFFFu), acc[t]);
+                    acc[t] = fmaf(wv[2 * j + 1], bf16_bits_to_f32(xq[j] >> 16), acc[t]);
+                }
             }
         }
     }
@@ -270,28 +277,32 @@ __global__ void __launch_bounds__(256) router_topk(const __nv_bfloat16* __restri
 }
 
 // --------------------------------------------------------------------------- sort
-// One block of 32 warps.  Warp w owns a contiguous segment of the pairs; per-warp,
-// per-expert counts give every (warp, expert) run its start, then each warp places its
-// pairs in order -- a stable counting sort.  Indices outside [0, E) are counted in an
-// extra bucket E after all experts and flagged.
-__global__ void __launch_bounds__(1024, 1) moe_sort_kernel(const int32_t* __restrict__ idx, int P, int E,
-                                                           int32_t* __restrict__ perm, int32_t* __restrict__ offsets,
-                                                           int32_t* __restrict__ inv, uint32_t* status) {
-    extern __shared__ int32_t cnt[];  // [32][E + 1]
+// Stable counting sort of pairs by expert (key), indices outside [0, E) in an extra
+// bucket E after all experts (and flagged).  Pairs are cut into segments of up to 32 per
+// warp; per-warp, per-key counts give every (warp, key) run its start, and each warp then
+// places its pairs in order (ranks within a warp by __match_any_sync).
+//   * up to 1024 pairs: one block, one kernel;
+//   * more: blocks of 1024 pairs -- per-block counts, a scan over blocks and keys, and a
+//     placement pass that recomputes the per-warp counts.
+
+__device__ __forceinline__ int sort_key(const int32_t* idx, int p, int E, uint32_t* status, bool flag) {
+    int e = idx[p];
+    if (e < 0 || e >= E) {
+        if (flag) atomicOr(status, Q38_DEV_BAD_INDEX);
+        e = E;
+    }
+    return e;
+}
+
+// Per-warp counts of this block's segment into cnt[warp][B]; each warp walks pairs
+// [s0, s1) in chunks of 32.
+__device__ __forceinline__ void warp_counts(const int32_t* idx, int s0, int s1, int E, int B, int* cnt,
+                                            uint32_t* status, bool flag) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int B = E + 1;
-    for (int i = threadIdx.x; i < 32 * B; i += 1024) cnt[i] = 0;
-    __syncthreads();
-    const int seg = (P + 31) / 32;
-    const int s0 = warp * seg, s1 = min(P, s0 + seg);
     for (int base = s0; base < s1; base += 32) {
         const int p = base + lane;
         const bool act = p < s1;
-        int e = act ? idx[p] : -1;
-        if (act && (e < 0 || e >= E)) {
-            atomicOr(status, Q38_DEV_BAD_INDEX);
-            e = E;
-        }
+        const int e = act ? sort_key(idx, p, E, status, flag) : -1;
         const unsigned am = __ballot_sync(0xffffffffu, act);
         if (act) {
             const unsigned m = __match_any_sync(am, e);
@@ -299,42 +310,16 @@ __global__ void __launch_bounds__(1024, 1) moe_sort_kernel(const int32_t* __rest
         }
         __syncwarp();
     }
-    __syncthreads();
-    // per expert: exclusive prefix over warps, total
-    for (int e = threadIdx.x; e < B; e += 1024) {
-        int run = 0;
-        for (int w = 0; w < 32; ++w) {
-            const int c = cnt[w * B + e];
-            cnt[w * B + e] = run;
-            run += c;
-        }
-        inv[e] = run;  // scratch: totals (inv is rewritten below)
-    }
-    __syncthreads();
-    if (warp == 0) {  // exclusive scan of the totals over experts, 32 at a time
-        int carry = 0;
-        for (int b0 = 0; b0 < B; b0 += 32) {
-            const int e = b0 + lane;
-            const int v = e < B ? inv[e] : 0;
-            int incl = v;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int n = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += n;
-            }
-            if (e < B) offsets[e] = carry + incl - v;
-            carry += __shfl_sync(0xffffffffu, incl, 31);
-        }
-        if (lane == 0) offsets[B] = carry;
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < 32 * B; i += 1024) cnt[i] += offsets[i % B];
-    __syncthreads();
+}
+
+// Places the segment's pairs given cnt[warp][key] = global start of that warp's run.
+__device__ __forceinline__ void warp_place(const int32_t* idx, int s0, int s1, int E, int B, int* cnt,
+                                           int32_t* perm, int32_t* inv) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int base = s0; base < s1; base += 32) {
         const int p = base + lane;
         const bool act = p < s1;
-        int e = act ? idx[p] : -1;
-        if (act && (e < 0 || e >= E)) e = E;
+        const int e = act ? sort_key(idx, p, E, nullptr, false) : -1;
         const unsigned am = __ballot_sync(0xffffffffu, act);
         if (act) {
             const unsigned m = __match_any_sync(am, e);
@@ -346,6 +331,117 @@ __global__ void __launch_bounds__(1024, 1) moe_sort_kernel(const int32_t* __rest
         }
         __syncwarp();
     }
+}
+
+// exclusive prefix over the block's warps for every key, in place; block totals to tot[]
+__device__ __forceinline__ void warp_prefix(int* cnt, int nw, int B, int* tot) {
+    for (int e = threadIdx.x; e < B; e += blockDim.x) {
+        int run = 0;
+        for (int w = 0; w < nw; ++w) {
+            const int c = cnt[w * B + e];
+            cnt[w * B + e] = run;
+            run += c;
+        }
+        tot[e] = run;
+    }
+}
+
+// exclusive scan of tot[0..B) by warp 0 into out[0..B), out[B] = total
+__device__ __forceinline__ void key_scan(const int* tot, int B, int32_t* out) {
+    const int lane = threadIdx.x & 31;
+    if ((threadIdx.x >> 5) != 0) return;
+    int carry = 0;
+    for (int b0 = 0; b0 < B; b0 += 32) {
+        const int e = b0 + lane;
+        const int v = e < B ? tot[e] : 0;
+        int incl = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += n;
+        }
+        if (e < B) out[e] = carry + incl - v;
+        carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) out[B] = carry;
+}
+
+// one block, blockDim = 32 * nw with nw = ceil(P / 32) <= 32
+__global__ void __launch_bounds__(1024, 1) moe_sort_small(const int32_t* __restrict__ idx, int P, int E,
+                                                          int32_t* __restrict__ perm, int32_t* __restrict__ offsets,
+                                                          int32_t* __restrict__ inv, uint32_t* status) {
+    extern __shared__ int cnt[];  // [nw][B] then tot[B]
+    const int nw = blockDim.x >> 5, B = E + 1;
+    int* tot = cnt + nw * B;
+    for (int i = threadIdx.x; i < nw * B; i += blockDim.x) cnt[i] = 0;
+    __syncthreads();
+    const int warp = threadIdx.x >> 5;
+    const int s0 = warp * 32, s1 = min(P, s0 + 32);
+    warp_counts(idx, s0, s1, E, B, cnt, status, true);
+    __syncthreads();
+    warp_prefix(cnt, nw, B, tot);
+    __syncthreads();
+    key_scan(tot, B, offsets);
+    __syncthreads();
+    for (int i = threadIdx.x; i < nw * B; i += blockDim.x) cnt[i] += offsets[i % B];
+    __syncthreads();
+    warp_place(idx, s0, s1, E, B, cnt, perm, inv);
+}
+
+// blocks of 1024 pairs: per-block key totals -> gcnt[block][B]
+__global__ void __launch_bounds__(1024, 1) moe_sort_count(const int32_t* __restrict__ idx, int P, int E,
+                                                          int* __restrict__ gcnt, uint32_t* status) {
+    extern __shared__ int cnt[];  // [32][B]
+    const int B = E + 1;
+    for (int i = threadIdx.x; i < 32 * B; i += 1024) cnt[i] = 0;
+    __syncthreads();
+    const int warp = threadIdx.x >> 5;
+    const int s0 = blockIdx.x * 1024 + warp * 32, s1 = min(P, s0 + 32);
+    warp_counts(idx, s0, s1, E, B, cnt, status, true);
+    __syncthreads();
+    warp_prefix(cnt, 32, B, gcnt + static_cast<size_t>(blockIdx.x) * B);
+}
+
+// gcnt[block][key] -> global start of each block's run of each key; offsets
+__global__ void __launch_bounds__(1024, 1) moe_sort_scan(int* __restrict__ gcnt, int nblk, int E,
+                                                         int32_t* __restrict__ offsets) {
+    __shared__ int tot[1025];
+    const int B = E + 1;
+    for (int e = threadIdx.x; e < B; e += 1024) {
+        int run = 0;
+        for (int b = 0; b < nblk; ++b) {
+            const int c = gcnt[static_cast<size_t>(b) * B + e];
+            gcnt[static_cast<size_t>(b) * B + e] = run;
+            run += c;
+        }
+        tot[e] = run;
+    }
+    __syncthreads();
+    key_scan(tot, B, offsets);
+    __syncthreads();
+    for (int e = threadIdx.x; e < B; e += 1024) {
+        const int o = offsets[e];
+        for (int b = 0; b < nblk; ++b) gcnt[static_cast<size_t>(b) * B + e] += o;
+    }
+}
+
+__global__ void __launch_bounds__(1024, 1) moe_sort_place(const int32_t* __restrict__ idx, int P, int E,
+                                                          const int* __restrict__ gbase, int32_t* __restrict__ perm,
+                                                          int32_t* __restrict__ inv) {
+    extern __shared__ int cnt[];  // [32][B] then tot[B]
+    const int B = E + 1;
+    int* tot = cnt + 32 * B;
+    for (int i = threadIdx.x; i < 32 * B; i += 1024) cnt[i] = 0;
+    __syncthreads();
+    const int warp = threadIdx.x >> 5;
+    const int s0 = blockIdx.x * 1024 + warp * 32, s1 = min(P, s0 + 32);
+    warp_counts(idx, s0, s1, E, B, cnt, nullptr, false);
+    __syncthreads();
+    warp_prefix(cnt, 32, B, tot);
+    __syncthreads();
+    for (int i = threadIdx.x; i < 32 * B; i += 1024) cnt[i] += gbase[static_cast<size_t>(blockIdx.x) * B + i % B];
+    __syncthreads();
+    warp_place(idx, s0, s1, E, B, cnt, perm, inv);
 }
 
 // ---------------------------------------------------------------------- tile lists
@@ -529,23 +625,45 @@ q38_status logits_launch(q38_ctx* ctx, const void* x, int64_t T, int64_t H, cons
     return check_launch(ctx, "router_logits_tc");
 }
 
+// Scratch ints the sort needs beyond its outputs (per-block counts for large P).
+size_t sort_scratch_ints(int64_t P, int64_t E) {
+    return P > 1024 ? static_cast<size_t>((P + 1023) / 1024) * (E + 1) : 1;
+}
+
 q38_status sort_launch(q38_ctx* ctx, const int32_t* idx, int64_t P, int64_t E, int32_t* perm, int32_t* offsets,
-                       int32_t* inv) {
-    const size_t sm = static_cast<size_t>(32) * (E + 1) * 4;
+                       int32_t* inv, int* scratch) {
     static std::mutex mu;
     static bool cfg[64] = {};
     {
         std::lock_guard<std::mutex> lk(mu);
         if (ctx->device < 64 && !cfg[ctx->device]) {
-            if (cudaFuncSetAttribute(moe_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024) !=
-                cudaSuccess)
+            if (cudaFuncSetAttribute(moe_sort_small, cudaFuncAttributeMaxDynamicSharedMemorySize, 140 * 1024) !=
+                    cudaSuccess ||
+                cudaFuncSetAttribute(moe_sort_count, cudaFuncAttributeMaxDynamicSharedMemorySize, 140 * 1024) !=
+                    cudaSuccess ||
+                cudaFuncSetAttribute(moe_sort_place, cudaFuncAttributeMaxDynamicSharedMemorySize, 140 * 1024) !=
+                    cudaSuccess)
                 return check_launch(ctx, "cudaFuncSetAttribute");
             cfg[ctx->device] = true;
         }
     }
-    moe_sort_kernel<<<1, 1024, sm, ctx->stream>>>(idx, static_cast<int>(P), static_cast<int>(E), perm, offsets, inv,
-                                                  ctx->d_status);
-    return check_launch(ctx, "moe_sort");
+    const int B = static_cast<int>(E + 1);
+    if (P <= 1024) {
+        const int nw = P > 0 ? static_cast<int>((P + 31) / 32) : 1;
+        moe_sort_small<<<1, 32 * nw, static_cast<size_t>(nw + 1) * B * 4, ctx->stream>>>(
+            idx, static_cast<int>(P), static_cast<int>(E), perm, offsets, inv, ctx->d_status);
+        return check_launch(ctx, "moe_sort");
+    }
+    const int nblk = static_cast<int>((P + 1023) / 1024);
+    moe_sort_count<<<nblk, 1024, static_cast<size_t>(32) * B * 4, ctx->stream>>>(
+        idx, static_cast<int>(P), static_cast<int>(E), scratch, ctx->d_status);
+    q38_status st = check_launch(ctx, "moe_sort_count");
+    if (st != Q38_OK) return st;
+    moe_sort_scan<<<1, 1024, 0, ctx->stream>>>(scratch, nblk, static_cast<int>(E), offsets);
+    if ((st = check_launch(ctx, "moe_sort_scan")) != Q38_OK) return st;
+    moe_sort_place<<<nblk, 1024, static_cast<size_t>(33) * B * 4, ctx->stream>>>(
+        idx, static_cast<int>(P), static_cast<int>(E), scratch, perm, inv);
+    return check_launch(ctx, "moe_sort_place");
 }
 
 }  // namespace
@@ -596,12 +714,14 @@ q38_status q38_moe_sort(q38_ctx* ctx, const int32_t* indices, int64_t pairs, int
     if (st != Q38_OK) return st;
     // offsets has E + 1 entries for the caller; the kernel also writes a bad-index bucket
     void* scratch;
-    const size_t inv_bytes = align_up(static_cast<size_t>(std::max<int64_t>(pairs, E + 2)) * 4, 256);
-    if ((st = ensure_aux(ctx, inv_bytes + align_up(static_cast<size_t>(E + 2) * 4, 256), &scratch)) != Q38_OK)
+    const size_t inv_bytes = align_up(static_cast<size_t>(std::max<int64_t>(pairs, 1)) * 4, 256);
+    const size_t off_bytes = align_up(static_cast<size_t>(E + 2) * 4, 256);
+    if ((st = ensure_aux(ctx, inv_bytes + off_bytes + sort_scratch_ints(pairs, E) * 4, &scratch)) != Q38_OK)
         return st;
     int32_t* inv = static_cast<int32_t*>(scratch);
     int32_t* off2 = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(scratch) + inv_bytes);
-    if ((st = sort_launch(ctx, indices, pairs, E, perm, off2, inv)) != Q38_OK) return st;
+    int* sscr = reinterpret_cast<int*>(static_cast<uint8_t*>(scratch) + inv_bytes + off_bytes);
+    if ((st = sort_launch(ctx, indices, pairs, E, perm, off2, inv, sscr)) != Q38_OK) return st;
     if (cudaMemcpyAsync(offsets, off2, static_cast<size_t>(E + 1) * 4, cudaMemcpyDeviceToDevice, ctx->stream) !=
         cudaSuccess)
         return check_launch(ctx, "moe_sort offsets");
@@ -631,13 +751,9 @@ q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
     q38_status st = set_dev(ctx);
     if (st != Q38_OK) return st;
 
-    // Few tokens: every expert sees a handful of pairs -> CUDA-core kernels with runs of
-    // up to 8 pairs.  Otherwise the grouped tensor-core kernels; an expert receives at most
-    // one pair per token, so runs never exceed T pairs.
-    const bool small = T <= 64;
-    const int xr = small ? moe_gemv_run_pairs() : 128;
-    const int rb_gu = static_cast<int>(small ? I / moe_gemv_rows_per_tile(H) : I / 64);
-    const int rb_d = static_cast<int>(small ? H / moe_gemv_rows_per_tile(I) : H / 128);
+    const int rb_gu = static_cast<int>(I / 64), rb_d = static_cast<int>(H / 128);
+    // An expert receives at most one pair per token, so runs never exceed T pairs.
+    const int xr = T <= 32 ? 32 : T <= 64 ? 64 : 128;
     const int64_t max_runs = std::min<int64_t>(E, P) + P / xr + 1;
     size_t off = 0;
     auto take = [&](size_t bytes) {
@@ -645,7 +761,8 @@ q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
         off += align_up(bytes, 256);
         return o;
     };
-    const size_t o_perm = take(P * 4), o_inv = take(std::max<int64_t>(P, E + 2) * 4), o_off = take((E + 2) * 4);
+    const size_t o_perm = take(P * 4), o_inv = take(P * 4), o_off = take((E + 2) * 4),
+                 o_sscr = take(sort_scratch_ints(P, E) * 4);
     const size_t o_cnt = take(16), o_gu = take(max_runs * rb_gu * sizeof(MoeTile)),
                  o_dn = take(max_runs * rb_d * sizeof(MoeTile));
     const size_t o_xs = take(static_cast<size_t>(P) * H * 2), o_h = take(static_cast<size_t>(P) * I * 2),
@@ -663,7 +780,8 @@ q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
     void* hp = b8 + o_h;
     void* y = b8 + o_y;
 
-    if ((st = sort_launch(ctx, indices, P, E, perm, offs, inv)) != Q38_OK) return st;
+    if ((st = sort_launch(ctx, indices, P, E, perm, offs, inv, reinterpret_cast<int*>(b8 + o_sscr))) != Q38_OK)
+        return st;
     moe_tiles_kernel<<<1, 1024, 0, ctx->stream>>>(offs, static_cast<int>(E), xr, rb_gu, rb_d, gu, dn, counts);
     if ((st = check_launch(ctx, "moe_tiles")) != Q38_OK) return st;
     if ((st = moe_gather_launch(ctx, x, static_cast<int>(H), perm, static_cast<int>(P), top_k, xs, bits)) != Q38_OK)
@@ -686,7 +804,7 @@ q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
     g.out = hp;
     g.out_ld = static_cast<int>(I);
     g.xr = xr;
-    if ((st = small ? moe_gemv_gate_up(ctx, g, bits) : grouped_gate_up(ctx, g, bits)) != Q38_OK) return st;
+    if ((st = grouped_gate_up(ctx, g, bits)) != Q38_OK) return st;
     GroupedProblem d;
     d.x = hp;
     d.pairs = static_cast<int>(P);
@@ -705,7 +823,7 @@ q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
     d.out = y;
     d.out_ld = static_cast<int>(H);
     d.xr = xr;
-    if ((st = small ? moe_gemv_down(ctx, d, bits) : grouped_down(ctx, d, bits)) != Q38_OK) return st;
+    if ((st = grouped_down(ctx, d, bits)) != Q38_OK) return st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;

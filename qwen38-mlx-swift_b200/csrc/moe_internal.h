@@ -28,13 +28,6 @@ struct GroupedProblem {
 
 q38_status grouped_gate_up(q38_ctx* ctx, const GroupedProblem& p, int bits);
 q38_status grouped_down(q38_ctx* ctx, const GroupedProblem& p, int bits);
-// Few-token path on CUDA cores (csrc/moe_gemv.cu): tiles of moe_gemv_rows_per_tile(K)
-// weight rows (K = the product's reduction length), runs of at most
-// moe_gemv_run_pairs() pairs.
-int moe_gemv_run_pairs();
-int moe_gemv_rows_per_tile(int64_t K);
-q38_status moe_gemv_gate_up(q38_ctx* ctx, const GroupedProblem& p, int bits);
-q38_status moe_gemv_down(q38_ctx* ctx, const GroupedProblem& p, int bits);
 q38_status moe_gather_launch(q38_ctx* ctx, const void* x, int H, const int32_t* perm, int pairs, int top_k,
                              void* xs, int bits);
 
