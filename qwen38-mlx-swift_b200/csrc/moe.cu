@@ -51,6 +51,8 @@ __device__ __forceinline__ float router_exp(float x) {
 __global__ void __launch_bounds__(128) router_logits_small(const __nv_bfloat16* __restrict__ x, int T, int H,
                                                            const __nv_bfloat16* __restrict__ wr, int E,
                                                            __nv_bfloat16* __restrict__ logits) {
+    griddep_wait();  // inputs come from the previous kernel on the stream
+    griddep_launch_dependents();
     extern __shared__ uint4 xs4[];
     const int t0 = blockIdx.y * 8;
     const int nt = min(8, T - t0);
@@ -112,6 +114,8 @@ __global__ void __launch_bounds__(128, 1) router_logits_tc(const __grid_constant
                                                            const __grid_constant__ CUtensorMap map_w, int T, int H,
                                                            int E, __nv_bfloat16* __restrict__ logits,
                                                            uint32_t* status) {
+    griddep_wait();  // inputs come from the previous kernel on the stream
+    griddep_launch_dependents();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -202,6 +206,8 @@ __global__ void __launch_bounds__(256) router_topk(const __nv_bfloat16* __restri
                                                    int top_k, int normalize, int32_t* __restrict__ indices,
                                                    __nv_bfloat16* __restrict__ scores,
                                                    __nv_bfloat16* __restrict__ probs) {
+    griddep_wait();  // inputs come from the previous kernel on the stream
+    griddep_launch_dependents();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * 8 + warp;
     if (t >= T) return;
@@ -370,6 +376,8 @@ __device__ __forceinline__ void key_scan(const int* tot, int B, int32_t* out) {
 __global__ void __launch_bounds__(1024, 1) moe_sort_small(const int32_t* __restrict__ idx, int P, int E,
                                                           int32_t* __restrict__ perm, int32_t* __restrict__ offsets,
                                                           int32_t* __restrict__ inv, uint32_t* status) {
+    griddep_wait();  // inputs come from the previous kernel on the stream
+    griddep_launch_dependents();
     extern __shared__ int cnt[];  // [nw][B] then tot[B]
     const int nw = blockDim.x >> 5, B = E + 1;
     int* tot = cnt + nw * B;
@@ -391,6 +399,8 @@ __global__ void __launch_bounds__(1024, 1) moe_sort_small(const int32_t* __restr
 // blocks of 1024 pairs: per-block key totals -> gcnt[block][B]
 __global__ void __launch_bounds__(1024, 1) moe_sort_count(const int32_t* __restrict__ idx, int P, int E,
                                                           int* __restrict__ gcnt, uint32_t* status) {
+    griddep_wait();  // inputs come from the previous kernel on the stream
+    griddep_launch_dependents();
     extern __shared__ int cnt[];  // [32][B]
     const int B = E + 1;
     for (int i = threadIdx.x; i < 32 * B; i += 1024) cnt[i] = 0;
@@ -405,6 +415,8 @@ __global__ void __launch_bounds__(1024, 1) moe_sort_count(const int32_t* __restr
 // gcnt[block][key] -> global start of each block's run of each key; offsets
 __global__ void __launch_bounds__(1024, 1) moe_sort_scan(int* __restrict__ gcnt, int nblk, int E,
                                                          int32_t* __restrict__ offsets) {
+    griddep_wait();  // inputs come from the previous kernel on the stream
+    griddep_launch_dependents();
     __shared__ int tot[1025];
     const int B = E + 1;
     for (int e = threadIdx.x; e < B; e += 1024) {
@@ -428,6 +440,8 @@ __global__ void __launch_bounds__(1024, 1) moe_sort_scan(int* __restrict__ gcnt,
 __global__ void __launch_bounds__(1024, 1) moe_sort_place(const int32_t* __restrict__ idx, int P, int E,
                                                           const int* __restrict__ gbase, int32_t* __restrict__ perm,
                                                           int32_t* __restrict__ inv) {
+    griddep_wait();  // inputs come from the previous kernel on the stream
+    griddep_launch_dependents();
     extern __shared__ int cnt[];  // [32][B] then tot[B]
     const int B = E + 1;
     int* tot = cnt + 32 * B;
@@ -450,6 +464,8 @@ __global__ void __launch_bounds__(1024, 1) moe_sort_place(const int32_t* __restr
 __global__ void __launch_bounds__(1024, 1) moe_tiles_kernel(const int32_t* __restrict__ offsets, int E, int run,
                                                             int rb_gu, int rb_d, MoeTile* __restrict__ gu,
                                                             MoeTile* __restrict__ dn, int* __restrict__ counts) {
+    griddep_wait();  // inputs come from the previous kernel on the stream
+    griddep_launch_dependents();
     __shared__ int warp_tot[32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int e = threadIdx.x;  // E <= 1024: one expert per thread
@@ -524,6 +540,8 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const __nv_bfloat16* _
 __global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* __restrict__ g,
                                                        const __nv_bfloat16* __restrict__ u, int64_t n,
                                                        __nv_bfloat16* __restrict__ h) {
+    griddep_wait();  // inputs come from the previous kernel on the stream
+    griddep_launch_dependents();
     const int64_t i = (blockIdx.x * 256LL + threadIdx.x) * 8;
     if (i >= n) return;
     if (i + 8 <= n) {
@@ -552,6 +570,8 @@ __global__ void __launch_bounds__(256) moe_pack_kernel(const __nv_bfloat16* __re
                                                        const int32_t* __restrict__ perm, int64_t P, int top_k,
                                                        int epr, __nv_bfloat16* __restrict__ rows,
                                                        int32_t* __restrict__ local_e) {
+    griddep_wait();  // inputs come from the previous kernel on the stream
+    griddep_launch_dependents();
     const int64_t j = blockIdx.x;
     if (j >= P) return;
     const int p = perm[j];
@@ -564,8 +584,30 @@ __global__ void __launch_bounds__(256) moe_pack_kernel(const __nv_bfloat16* __re
 
 __global__ void __launch_bounds__(256) invert_perm_kernel(const int32_t* __restrict__ perm, int64_t P,
                                                           int32_t* __restrict__ inv) {
+    griddep_wait();  // inputs come from the previous kernel on the stream
+    griddep_launch_dependents();
     const int64_t j = blockIdx.x * 256LL + threadIdx.x;
     if (j < P) inv[perm[j]] = static_cast<int32_t>(j);
+}
+
+// Launch with programmatic dependent launch: the kernel may be scheduled while the
+// previous kernel on the stream finishes; every kernel here waits for it (griddepcontrol)
+// before touching memory.
+template <typename... KArgs, typename... Args>
+q38_status launch_pdl(q38_ctx* ctx, const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                      Args... args) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+    return check_launch(ctx, what);
 }
 
 q38_status set_dev(q38_ctx* ctx) {
@@ -577,10 +619,9 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 q38_status topk_launch(q38_ctx* ctx, const void* logits, int64_t T, int64_t E, int top_k, int normalize,
                        int32_t* indices, void* scores, void* probs) {
-    router_topk<<<static_cast<unsigned>((T + 7) / 8), 256, 0, ctx->stream>>>(
-        static_cast<const __nv_bfloat16*>(logits), static_cast<int>(T), static_cast<int>(E), top_k, normalize, indices,
-        static_cast<__nv_bfloat16*>(scores), static_cast<__nv_bfloat16*>(probs));
-    return check_launch(ctx, "router_topk");
+    return launch_pdl(ctx, "router_topk", router_topk, dim3(static_cast<unsigned>((T + 7) / 8)), dim3(256), 0,
+                      static_cast<const __nv_bfloat16*>(logits), static_cast<int>(T), static_cast<int>(E), top_k,
+                      normalize, indices, static_cast<__nv_bfloat16*>(scores), static_cast<__nv_bfloat16*>(probs));
 }
 
 q38_status logits_launch(q38_ctx* ctx, const void* x, int64_t T, int64_t H, const void* wr, int64_t E, void* logits) {
@@ -598,10 +639,10 @@ q38_status logits_launch(q38_ctx* ctx, const void* x, int64_t T, int64_t H, cons
             }
         }
         dim3 grid(static_cast<unsigned>((E + 3) / 4), static_cast<unsigned>((T + 7) / 8));
-        router_logits_small<<<grid, 128, sm, ctx->stream>>>(static_cast<const __nv_bfloat16*>(x), static_cast<int>(T),
-                                                            static_cast<int>(H), static_cast<const __nv_bfloat16*>(wr),
-                                                            static_cast<int>(E), static_cast<__nv_bfloat16*>(logits));
-        return check_launch(ctx, "router_logits_small");
+        return launch_pdl(ctx, "router_logits_small", router_logits_small, grid, dim3(128), sm,
+                          static_cast<const __nv_bfloat16*>(x), static_cast<int>(T), static_cast<int>(H),
+                          static_cast<const __nv_bfloat16*>(wr), static_cast<int>(E),
+                          static_cast<__nv_bfloat16*>(logits));
     }
     CUtensorMap mx, mw;
     if (!make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, H, T, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -619,10 +660,8 @@ q38_status logits_launch(q38_ctx* ctx, const void* x, int64_t T, int64_t H, cons
         }
     }
     dim3 grid(static_cast<unsigned>((T + 127) / 128), static_cast<unsigned>((E + 255) / 256));
-    router_logits_tc<<<grid, 128, smem, ctx->stream>>>(mx, mw, static_cast<int>(T), static_cast<int>(H),
-                                                      static_cast<int>(E), static_cast<__nv_bfloat16*>(logits),
-                                                      ctx->d_status);
-    return check_launch(ctx, "router_logits_tc");
+    return launch_pdl(ctx, "router_logits_tc", router_logits_tc, grid, dim3(128), smem, mx, mw, static_cast<int>(T),
+                      static_cast<int>(H), static_cast<int>(E), static_cast<__nv_bfloat16*>(logits), ctx->d_status);
 }
 
 // Scratch ints the sort needs beyond its outputs (per-block counts for large P).
@@ -650,20 +689,19 @@ q38_status sort_launch(q38_ctx* ctx, const int32_t* idx, int64_t P, int64_t E, i
     const int B = static_cast<int>(E + 1);
     if (P <= 1024) {
         const int nw = P > 0 ? static_cast<int>((P + 31) / 32) : 1;
-        moe_sort_small<<<1, 32 * nw, static_cast<size_t>(nw + 1) * B * 4, ctx->stream>>>(
-            idx, static_cast<int>(P), static_cast<int>(E), perm, offsets, inv, ctx->d_status);
-        return check_launch(ctx, "moe_sort");
+        return launch_pdl(ctx, "moe_sort", moe_sort_small, dim3(1), dim3(32 * nw), static_cast<size_t>(nw + 1) * B * 4,
+                          idx, static_cast<int>(P), static_cast<int>(E), perm, offsets, inv, ctx->d_status);
     }
     const int nblk = static_cast<int>((P + 1023) / 1024);
-    moe_sort_count<<<nblk, 1024, static_cast<size_t>(32) * B * 4, ctx->stream>>>(
-        idx, static_cast<int>(P), static_cast<int>(E), scratch, ctx->d_status);
-    q38_status st = check_launch(ctx, "moe_sort_count");
+    q38_status st = launch_pdl(ctx, "moe_sort_count", moe_sort_count, dim3(nblk), dim3(1024),
+                               static_cast<size_t>(32) * B * 4, idx, static_cast<int>(P), static_cast<int>(E), scratch,
+                               ctx->d_status);
     if (st != Q38_OK) return st;
-    moe_sort_scan<<<1, 1024, 0, ctx->stream>>>(scratch, nblk, static_cast<int>(E), offsets);
-    if ((st = check_launch(ctx, "moe_sort_scan")) != Q38_OK) return st;
-    moe_sort_place<<<nblk, 1024, static_cast<size_t>(33) * B * 4, ctx->stream>>>(
-        idx, static_cast<int>(P), static_cast<int>(E), scratch, perm, inv);
-    return check_launch(ctx, "moe_sort_place");
+    if ((st = launch_pdl(ctx, "moe_sort_scan", moe_sort_scan, dim3(1), dim3(1024), 0, scratch, nblk,
+                         static_cast<int>(E), offsets)) != Q38_OK)
+        return st;
+    return launch_pdl(ctx, "moe_sort_place", moe_sort_place, dim3(nblk), dim3(1024), static_cast<size_t>(33) * B * 4,
+                      idx, static_cast<int>(P), static_cast<int>(E), scratch, perm, inv);
 }
 
 }  // namespace
@@ -782,8 +820,9 @@ q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
 
     if ((st = sort_launch(ctx, indices, P, E, perm, offs, inv, reinterpret_cast<int*>(b8 + o_sscr))) != Q38_OK)
         return st;
-    moe_tiles_kernel<<<1, 1024, 0, ctx->stream>>>(offs, static_cast<int>(E), xr, rb_gu, rb_d, gu, dn, counts);
-    if ((st = check_launch(ctx, "moe_tiles")) != Q38_OK) return st;
+    if ((st = launch_pdl(ctx, "moe_tiles", moe_tiles_kernel, dim3(1), dim3(1024), 0, offs, static_cast<int>(E), xr,
+                         rb_gu, rb_d, gu, dn, counts)) != Q38_OK)
+        return st;
     if ((st = moe_gather_launch(ctx, x, static_cast<int>(H), perm, static_cast<int>(P), top_k, xs, bits)) != Q38_OK)
         return st;
     GroupedProblem g;
@@ -850,9 +889,9 @@ q38_status q38_silu_mul(q38_ctx* ctx, const void* g, const void* u, int64_t n, v
     q38_status st = set_dev(ctx);
     if (st != Q38_OK) return st;
     const int64_t blocks = (n + 8 * 256 - 1) / (8 * 256);
-    silu_mul_kernel<<<static_cast<unsigned>(blocks), 256, 0, ctx->stream>>>(
-        static_cast<const __nv_bfloat16*>(g), static_cast<const __nv_bfloat16*>(u), n, static_cast<__nv_bfloat16*>(h));
-    return check_launch(ctx, "silu_mul");
+    return launch_pdl(ctx, "silu_mul", silu_mul_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+                      static_cast<const __nv_bfloat16*>(g), static_cast<const __nv_bfloat16*>(u), n,
+                      static_cast<__nv_bfloat16*>(h));
 }
 
 q38_status q38_moe_dispatch_pack(q38_ctx* ctx, const void* x, int64_t H, const int32_t* indices, const int32_t* perm,
@@ -867,10 +906,9 @@ q38_status q38_moe_dispatch_pack(q38_ctx* ctx, const void* x, int64_t H, const i
     if (!aligned16(x) || !aligned16(rows)) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_dispatch_pack: rows must be 16-byte aligned");
     q38_status st = set_dev(ctx);
     if (st != Q38_OK) return st;
-    moe_pack_kernel<<<static_cast<unsigned>(pairs), 256, 0, ctx->stream>>>(
-        static_cast<const __nv_bfloat16*>(x), static_cast<int>(H), indices, perm, pairs, top_k,
-        static_cast<int>(experts_per_rank), static_cast<__nv_bfloat16*>(rows), local_experts);
-    return check_launch(ctx, "moe_dispatch_pack");
+    return launch_pdl(ctx, "moe_dispatch_pack", moe_pack_kernel, dim3(static_cast<unsigned>(pairs)), dim3(256), 0,
+                      static_cast<const __nv_bfloat16*>(x), static_cast<int>(H), indices, perm, pairs, top_k,
+                      static_cast<int>(experts_per_rank), static_cast<__nv_bfloat16*>(rows), local_experts);
 }
 
 q38_status q38_moe_combine(q38_ctx* ctx, const void* y, int64_t H, const int32_t* perm, const int32_t* indices,
@@ -886,12 +924,13 @@ q38_status q38_moe_combine(q38_ctx* ctx, const void* y, int64_t H, const int32_t
     void* scratch;
     if ((st = ensure_aux(ctx, static_cast<size_t>(P) * 4, &scratch)) != Q38_OK) return st;
     int32_t* inv = static_cast<int32_t*>(scratch);
-    invert_perm_kernel<<<static_cast<unsigned>((P + 255) / 256), 256, 0, ctx->stream>>>(perm, P, inv);
-    if ((st = check_launch(ctx, "moe_combine")) != Q38_OK) return st;
-    moe_combine_kernel<<<static_cast<unsigned>(T), 256, 0, ctx->stream>>>(
-        static_cast<const __nv_bfloat16*>(y), static_cast<int>(H), inv, indices,
-        static_cast<const __nv_bfloat16*>(scores), top_k, static_cast<int>(E), static_cast<__nv_bfloat16*>(out));
-    return check_launch(ctx, "moe_combine");
+    if ((st = launch_pdl(ctx, "moe_combine", invert_perm_kernel, dim3(static_cast<unsigned>((P + 255) / 256)),
+                         dim3(256), 0, perm, P, inv)) != Q38_OK)
+        return st;
+    return launch_pdl(ctx, "moe_combine", moe_combine_kernel, dim3(static_cast<unsigned>(T)), dim3(256), 0,
+                      static_cast<const __nv_bfloat16*>(y), static_cast<int>(H), static_cast<const int32_t*>(inv),
+                      indices, static_cast<const __nv_bfloat16*>(scores), top_k, static_cast<int>(E),
+                      static_cast<__nv_bfloat16*>(out));
 }
 
 }  // extern "C"
