@@ -45,19 +45,20 @@ __device__ __forceinline__ float router_exp(float x) {
     return __fmul_rn(p, __uint_as_float(static_cast<uint32_t>(ni + 127) << 23));
 }
 
-// logits for a few tokens on CUDA cores: one warp per expert (4 per block), up to 8
+// logits for a few tokens on CUDA cores: one warp per expert (4 per block), NT (1-8)
 // tokens staged in shared memory; each lane accumulates 8-element slices of the row, the
 // warp reduces.
+template <int NT>
 __global__ void __launch_bounds__(128) router_logits_small(const __nv_bfloat16* __restrict__ x, int T, int H,
                                                            const __nv_bfloat16* __restrict__ wr, int E,
                                                            __nv_bfloat16* __restrict__ logits) {
     griddep_wait();  // inputs come from the previous kernel on the stream
     griddep_launch_dependents();
     extern __shared__ uint4 xs4[];
-    const int t0 = blockIdx.y * 8;
-    const int nt = min(8, T - t0);
+    const int t0 = blockIdx.y * NT;
+    const int nt = min(NT, T - t0);
     const int vec = H / 8;
-    for (int i = threadIdx.x; i < 8 * vec; i += 128) {
+    for (int i = threadIdx.x; i < NT * vec; i += 128) {
         const int t = i / vec;
         xs4[i] = t < nt ? reinterpret_cast<const uint4*>(x + static_cast<size_t>(t0 + t) * H)[i % vec]
                         : make_uint4(0, 0, 0, 0);
@@ -67,7 +68,9 @@ __global__ void __launch_bounds__(128) router_logits_small(const __nv_bfloat16* 
     const int e = blockIdx.x * 4 + warp;
     if (e >= E) return;
     const uint4* wrow = reinterpret_cast<const uint4*>(wr + static_cast<size_t>(e) * H);
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    float acc[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
     for (int v0 = lane; v0 < vec; v0 += 32 * 8) {
         uint4 wu[8];  // eight 16-byte loads in flight per lane
 #pragma unroll
@@ -84,7 +87,7 @@ __global__ void __launch_bounds__(128) router_logits_small(const __nv_bfloat16* 
                 wv[2 * j + 1] = bf16_bits_to_f32(q[j] >> 16);
             }
 #pragma unroll
-            for (int t = 0; t < 8; ++t) {
+            for (int t = 0; t < NT; ++t) {
                 const uint4 xu = xs4[t * vec + v];
                 const uint32_t xq[4] = {xu.x, xu.y, xu.z, xu.w};
 #pragma unroll
@@ -96,7 +99,7 @@ __global__ void __launch_bounds__(128) router_logits_small(const __nv_bfloat16* 
         }
     }
 #pragma unroll
-    for (int t = 0; t < 8; ++t) {
+    for (int t = 0; t < NT; ++t) {
         float v = acc[t];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -199,9 +202,10 @@ __global__ void __launch_bounds__(128, 1) router_logits_tc(const __grid_constant
     if (warp == 1) tmem_dealloc(tmem, 256);
 }
 
-// softmax + top-k, one warp per token; lane l holds experts l, l+32, ...
-constexpr int R_MAXJ = 32;  // E <= 1024
-
+// softmax + top-k, one warp per token; lane l holds experts l, l+32, ... (NJ per lane).
+// The r-th winner is kept by lane r; the renormalisation sum accumulates in selection
+// order on every lane.
+template <int NJ>
 __global__ void __launch_bounds__(256) router_topk(const __nv_bfloat16* __restrict__ logits, int T, int E,
                                                    int top_k, int normalize, int32_t* __restrict__ indices,
                                                    __nv_bfloat16* __restrict__ scores,
@@ -212,52 +216,49 @@ __global__ void __launch_bounds__(256) router_topk(const __nv_bfloat16* __restri
     const int t = blockIdx.x * 8 + warp;
     if (t >= T) return;
     const uint16_t* l = reinterpret_cast<const uint16_t*>(logits) + static_cast<size_t>(t) * E;
-    const int nj = (E + 31) / 32;
-    float v[R_MAXJ];
+    float v[NJ];
     float mx = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < R_MAXJ; ++j) {
+    for (int j = 0; j < NJ; ++j) {
         const int e = lane + 32 * j;
-        v[j] = (j < nj && e < E) ? bf16_bits_to_f32(l[e]) : -INFINITY;
+        v[j] = e < E ? bf16_bits_to_f32(l[e]) : -INFINITY;
         mx = fmaxf(mx, v[j]);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float part = 0.0f;
 #pragma unroll
-    for (int j = 0; j < R_MAXJ; ++j) {
-        const int e = lane + 32 * j;
-        if (j < nj && e < E) {
+    for (int j = 0; j < NJ; ++j) {
+        if (lane + 32 * j < E) {
             v[j] = router_exp(__fsub_rn(v[j], mx));
             part = __fadd_rn(part, v[j]);
-        } else {
-            v[j] = -1.0f;  // never selected: probabilities are >= 0
         }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, o));
-    uint32_t taken = 0;
 #pragma unroll
-    for (int j = 0; j < R_MAXJ; ++j) {
+    for (int j = 0; j < NJ; ++j) {
         const int e = lane + 32 * j;
-        if (j < nj && e < E) {
+        if (e < E) {
             const uint16_t pb = f32_to_bf16_bits(__fdiv_rn(v[j], part));
             v[j] = bf16_bits_to_f32(pb);
             if (probs) reinterpret_cast<uint16_t*>(probs)[static_cast<size_t>(t) * E + e] = pb;
+        } else {
+            v[j] = -1.0f;  // never selected: probabilities are >= 0
         }
     }
-    float ssum = 0.0f;
-    float sel[32];
-    int selidx[32];
+    float ssum = 0.0f, my_v = 0.0f;
+    int my_i = 0;
     for (int r = 0; r < top_k; ++r) {
         float bv = -2.0f;
-        int bi = 0x7fffffff;
+        int bj = 0;
 #pragma unroll
-        for (int j = 0; j < R_MAXJ; ++j)
-            if (!((taken >> j) & 1u) && v[j] > bv) {  // first maximum = lowest id in this lane
+        for (int j = 0; j < NJ; ++j)
+            if (v[j] > bv) {  // first maximum = lowest id in this lane
                 bv = v[j];
-                bi = lane + 32 * j;
+                bj = j;
             }
+        int bi = lane + 32 * bj;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -267,18 +268,21 @@ __global__ void __launch_bounds__(256) router_topk(const __nv_bfloat16* __restri
                 bi = oi;
             }
         }
-        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-        sel[r] = bv;
-        selidx[r] = bi;
+        if ((bi & 31) == lane) {
+#pragma unroll
+            for (int j = 0; j < NJ; ++j)
+                if (j == (bi >> 5)) v[j] = -3.0f;  // taken
+        }
+        if (lane == r) {
+            my_v = bv;
+            my_i = bi;
+        }
         ssum = __fadd_rn(ssum, bv);
     }
-    if (lane == 0) {
+    if (lane < top_k) {
         const float denom = bf16_bits_to_f32(f32_to_bf16_bits(ssum));
-        for (int r = 0; r < top_k; ++r) {
-            indices[static_cast<size_t>(t) * top_k + r] = selidx[r];
-            const float sc = normalize ? __fdiv_rn(sel[r], denom) : sel[r];
-            scores[static_cast<size_t>(t) * top_k + r] = __float2bfloat16_rn(sc);
-        }
+        indices[static_cast<size_t>(t) * top_k + lane] = my_i;
+        scores[static_cast<size_t>(t) * top_k + lane] = __float2bfloat16_rn(normalize ? __fdiv_rn(my_v, denom) : my_v);
     }
 }
 
@@ -619,30 +623,51 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 q38_status topk_launch(q38_ctx* ctx, const void* logits, int64_t T, int64_t E, int top_k, int normalize,
                        int32_t* indices, void* scores, void* probs) {
-    return launch_pdl(ctx, "router_topk", router_topk, dim3(static_cast<unsigned>((T + 7) / 8)), dim3(256), 0,
-                      static_cast<const __nv_bfloat16*>(logits), static_cast<int>(T), static_cast<int>(E), top_k,
-                      normalize, indices, static_cast<__nv_bfloat16*>(scores), static_cast<__nv_bfloat16*>(probs));
+    const dim3 grid(static_cast<unsigned>((T + 7) / 8));
+    auto go = [&](auto kern) {
+        return launch_pdl(ctx, "router_topk", kern, grid, dim3(256), 0, static_cast<const __nv_bfloat16*>(logits),
+                          static_cast<int>(T), static_cast<int>(E), top_k, normalize, indices,
+                          static_cast<__nv_bfloat16*>(scores), static_cast<__nv_bfloat16*>(probs));
+    };
+    if (E <= 128) return go(router_topk<4>);
+    if (E <= 256) return go(router_topk<8>);
+    if (E <= 512) return go(router_topk<16>);
+    return go(router_topk<32>);
 }
 
 q38_status logits_launch(q38_ctx* ctx, const void* x, int64_t T, int64_t H, const void* wr, int64_t E, void* logits) {
     if (T <= 64) {
-        const size_t sm = static_cast<size_t>(16) * H;
+        const int nt = T >= 8 ? 8 : T >= 4 ? 4 : T >= 2 ? 2 : 1;
+        const size_t sm = static_cast<size_t>(2) * nt * H;
         static std::mutex mu;
         static bool big[64] = {};
         if (sm > 48 * 1024) {
             std::lock_guard<std::mutex> lk(mu);
             if (ctx->device < 64 && !big[ctx->device]) {
-                if (cudaFuncSetAttribute(router_logits_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                if (cudaFuncSetAttribute(router_logits_small<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         200 * 1024) != cudaSuccess ||
+                    cudaFuncSetAttribute(router_logits_small<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         200 * 1024) != cudaSuccess ||
+                    cudaFuncSetAttribute(router_logits_small<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         200 * 1024) != cudaSuccess ||
+                    cudaFuncSetAttribute(router_logits_small<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          200 * 1024) != cudaSuccess)
                     return check_launch(ctx, "cudaFuncSetAttribute");
                 big[ctx->device] = true;
             }
         }
-        dim3 grid(static_cast<unsigned>((E + 3) / 4), static_cast<unsigned>((T + 7) / 8));
-        return launch_pdl(ctx, "router_logits_small", router_logits_small, grid, dim3(128), sm,
-                          static_cast<const __nv_bfloat16*>(x), static_cast<int>(T), static_cast<int>(H),
-                          static_cast<const __nv_bfloat16*>(wr), static_cast<int>(E),
-                          static_cast<__nv_bfloat16*>(logits));
+        const dim3 grid(static_cast<unsigned>((E + 3) / 4), static_cast<unsigned>((T + nt - 1) / nt));
+        auto go = [&](auto kern) {
+            return launch_pdl(ctx, "router_logits_small", kern, grid, dim3(128), sm, static_cast<const __nv_bfloat16*>(x),
+                              static_cast<int>(T), static_cast<int>(H), static_cast<const __nv_bfloat16*>(wr),
+                              static_cast<int>(E), static_cast<__nv_bfloat16*>(logits));
+        };
+        switch (nt) {
+            case 1: return go(router_logits_small<1>);
+            case 2: return go(router_logits_small<2>);
+            case 4: return go(router_logits_small<4>);
+            default: return go(router_logits_small<8>);
+        }
     }
     CUtensorMap mx, mw;
     if (!make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, H, T, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
