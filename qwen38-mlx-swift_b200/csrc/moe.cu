@@ -247,31 +247,29 @@ __global__ void __launch_bounds__(256) router_topk(const __nv_bfloat16* __restri
             v[j] = -1.0f;  // never selected: probabilities are >= 0
         }
     }
+    // Selection on 32-bit keys: the probability's bf16 bits (order-preserving for values
+    // >= 0) above 0xFFFF - expert id, so one warp max picks the largest probability and,
+    // among equal ones, the lowest id.  Taken and padding entries have key 0.
+    uint32_t key[NJ];
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+        const int e = lane + 32 * j;
+        key[j] = e < E ? (static_cast<uint32_t>(f32_to_bf16_bits(v[j])) << 16) | (0xFFFFu - static_cast<uint32_t>(e))
+                       : 0u;
+    }
     float ssum = 0.0f, my_v = 0.0f;
     int my_i = 0;
     for (int r = 0; r < top_k; ++r) {
-        float bv = -2.0f;
-        int bj = 0;
+        uint32_t m = 0;
 #pragma unroll
-        for (int j = 0; j < NJ; ++j)
-            if (v[j] > bv) {  // first maximum = lowest id in this lane
-                bv = v[j];
-                bj = j;
-            }
-        int bi = lane + 32 * bj;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) {
-                bv = ov;
-                bi = oi;
-            }
-        }
+        for (int j = 0; j < NJ; ++j) m = max(m, key[j]);
+        m = __reduce_max_sync(0xffffffffu, m);
+        const int bi = static_cast<int>(0xFFFFu - (m & 0xFFFFu));
+        const float bv = bf16_bits_to_f32(m >> 16);
         if ((bi & 31) == lane) {
 #pragma unroll
             for (int j = 0; j < NJ; ++j)
-                if (j == (bi >> 5)) v[j] = -3.0f;  // taken
+                if (j == (bi >> 5)) key[j] = 0u;  // taken
         }
         if (lane == r) {
             my_v = bv;
@@ -356,48 +354,60 @@ __device__ __forceinline__ void warp_prefix(int* cnt, int nw, int B, int* tot) {
     }
 }
 
-// exclusive scan of tot[0..B) by warp 0 into out[0..B), out[B] = total
-__device__ __forceinline__ void key_scan(const int* tot, int B, int32_t* out) {
-    const int lane = threadIdx.x & 31;
-    if ((threadIdx.x >> 5) != 0) return;
-    int carry = 0;
-    for (int b0 = 0; b0 < B; b0 += 32) {
-        const int e = b0 + lane;
-        const int v = e < B ? tot[e] : 0;
-        int incl = v;
+// exclusive scan of tot[0..B) (B <= 2048) by the whole block into out[0..B), out[B] = total;
+// every thread of the block calls it; blockDim.x == 1024
+__device__ __forceinline__ void key_scan_block(const int* tot, int B, int32_t* out, int* wsum) {
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int a = 2 * t < B ? tot[2 * t] : 0, b = 2 * t + 1 < B ? tot[2 * t + 1] : 0;
+    const int v = a + b;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+    }
+    if (lane == 31) wsum[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        const int w = wsum[lane];
+        int wi = w;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const int n = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += n;
+            const int n = __shfl_up_sync(0xffffffffu, wi, o);
+            if (lane >= o) wi += n;
         }
-        if (e < B) out[e] = carry + incl - v;
-        carry += __shfl_sync(0xffffffffu, incl, 31);
+        wsum[lane] = wi - w;
+        if (lane == 31) wsum[32] = wi;
     }
-    if (lane == 0) out[B] = carry;
+    __syncthreads();
+    const int ex = wsum[warp] + incl - v;
+    if (2 * t < B) out[2 * t] = ex;
+    if (2 * t + 1 < B) out[2 * t + 1] = ex + a;
+    if (t == 0) out[B] = wsum[32];
 }
 
-// one block, blockDim = 32 * nw with nw = ceil(P / 32) <= 32
-__global__ void __launch_bounds__(1024, 1) moe_sort_small(const int32_t* __restrict__ idx, int P, int E,
+// one block of 1024 threads for up to 1024 pairs; nw = ceil(P / 32) warps hold pairs
+__global__ void __launch_bounds__(1024, 1) moe_sort_small(const int32_t* __restrict__ idx, int P, int E, int nw,
                                                           int32_t* __restrict__ perm, int32_t* __restrict__ offsets,
                                                           int32_t* __restrict__ inv, uint32_t* status) {
     griddep_wait();  // inputs come from the previous kernel on the stream
     griddep_launch_dependents();
-    extern __shared__ int cnt[];  // [nw][B] then tot[B]
-    const int nw = blockDim.x >> 5, B = E + 1;
+    extern __shared__ int cnt[];  // [nw][B] then tot[B] then 33 warp sums
+    const int B = E + 1;
     int* tot = cnt + nw * B;
-    for (int i = threadIdx.x; i < nw * B; i += blockDim.x) cnt[i] = 0;
+    int* wsum = tot + B;
+    for (int i = threadIdx.x; i < nw * B; i += 1024) cnt[i] = 0;
     __syncthreads();
     const int warp = threadIdx.x >> 5;
-    const int s0 = warp * 32, s1 = min(P, s0 + 32);
-    warp_counts(idx, s0, s1, E, B, cnt, status, true);
+    if (warp < nw) warp_counts(idx, warp * 32, min(P, warp * 32 + 32), E, B, cnt, status, true);
     __syncthreads();
     warp_prefix(cnt, nw, B, tot);
     __syncthreads();
-    key_scan(tot, B, offsets);
+    key_scan_block(tot, B, offsets, wsum);
     __syncthreads();
-    for (int i = threadIdx.x; i < nw * B; i += blockDim.x) cnt[i] += offsets[i % B];
+    for (int i = threadIdx.x; i < nw * B; i += 1024) cnt[i] += offsets[i % B];
     __syncthreads();
-    warp_place(idx, s0, s1, E, B, cnt, perm, inv);
+    if (warp < nw) warp_place(idx, warp * 32, min(P, warp * 32 + 32), E, B, cnt, perm, inv);
 }
 
 // blocks of 1024 pairs: per-block key totals -> gcnt[block][B]
@@ -432,8 +442,9 @@ __global__ void __launch_bounds__(1024, 1) moe_sort_scan(int* __restrict__ gcnt,
         }
         tot[e] = run;
     }
+    __shared__ int wsum[33];
     __syncthreads();
-    key_scan(tot, B, offsets);
+    key_scan_block(tot, B, offsets, wsum);
     __syncthreads();
     for (int e = threadIdx.x; e < B; e += 1024) {
         const int o = offsets[e];
@@ -714,8 +725,9 @@ q38_status sort_launch(q38_ctx* ctx, const int32_t* idx, int64_t P, int64_t E, i
     const int B = static_cast<int>(E + 1);
     if (P <= 1024) {
         const int nw = P > 0 ? static_cast<int>((P + 31) / 32) : 1;
-        return launch_pdl(ctx, "moe_sort", moe_sort_small, dim3(1), dim3(32 * nw), static_cast<size_t>(nw + 1) * B * 4,
-                          idx, static_cast<int>(P), static_cast<int>(E), perm, offsets, inv, ctx->d_status);
+        return launch_pdl(ctx, "moe_sort", moe_sort_small, dim3(1), dim3(1024),
+                          static_cast<size_t>(nw + 1) * B * 4 + 33 * 4, idx, static_cast<int>(P), static_cast<int>(E),
+                          nw, perm, offsets, inv, ctx->d_status);
     }
     const int nblk = static_cast<int>((P + 1023) / 1024);
     q38_status st = launch_pdl(ctx, "moe_sort_count", moe_sort_count, dim3(nblk), dim3(1024),
