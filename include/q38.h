@@ -194,6 +194,7 @@ Q38_API q38_status q38_moe_sort(q38_ctx* ctx, const int32_t* indices, int64_t pa
  * x bf16 [T, H]; indices int32 / scores bf16 [T, top_k]; gate/up codes [E, I, H*bits/32],
  * scales/biases bf16 [E, I, H/64]; down codes [E, H, I*bits/32], scales/biases
  * [E, H, I/64]; out bf16 [T, H].  Biases are given for all three projections or none.
+ * An index of -1 marks an empty slot: it contributes nothing and is not an error.
  * Implemented for group 64, bits 2/3/4, H % 512 == 0, I % 512 == 0, E <= 1024.  Uses the
  * context's activation buffer (about T*top_k*(2H + I)*2 bytes). */
 Q38_API q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int64_t I, int64_t E,
@@ -222,6 +223,25 @@ Q38_API q38_status q38_moe_dispatch_pack(q38_ctx* ctx, const void* x, int64_t H,
 Q38_API q38_status q38_moe_combine(q38_ctx* ctx, const void* y, int64_t H, const int32_t* perm,
                                    const int32_t* indices, const void* scores, int64_t T, int top_k, int64_t E,
                                    void* out);
+
+/* Expert-parallel exchange with one row per (token, destination rank).  Experts are split
+ * contiguously, experts_per_rank per rank.
+ *   q38_moe_ep_plan: rowpos[t * world + r] = the row token t sends to rank r (rank-major,
+ *     tokens ascending within a rank), or -1 when none of its experts lives on r;
+ *     counts[r] = rows for rank r.  One block; indices int32 [T, top_k].
+ *   q38_moe_ep_pack: rows[rowpos] = x[t] (bf16 [*, H]); meta int32 [rows, 2 * top_k] =
+ *     the rank-local expert of each slot or -1 (expert elsewhere), then the slot scores'
+ *     bf16 bits.  The receiving rank runs q38_switch_glu on the rows with those indices
+ *     and scores (slots of -1 contribute nothing), which yields each row's partial sum.
+ *   q38_moe_ep_reduce: out[t] = bf16(sum over r, in rank order, of partial[rowpos[t, r]])
+ *     with fp32 accumulation. */
+Q38_API q38_status q38_moe_ep_plan(q38_ctx* ctx, const int32_t* indices, int64_t T, int top_k,
+                                   int64_t experts_per_rank, int world, int32_t* rowpos, int32_t* counts);
+Q38_API q38_status q38_moe_ep_pack(q38_ctx* ctx, const void* x, int64_t H, const int32_t* indices, const void* scores,
+                                   int64_t T, int top_k, int64_t experts_per_rank, int world, const int32_t* rowpos,
+                                   void* rows, int32_t* meta);
+Q38_API q38_status q38_moe_ep_reduce(q38_ctx* ctx, const void* partial, int64_t H, const int32_t* rowpos, int64_t T,
+                                     int world, void* out);
 
 /* Allocation-free decode product.  No counterpart in the reference: it exists for
  * callers that must not allocate device memory on the calling path (a host framework

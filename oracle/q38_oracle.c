@@ -498,6 +498,7 @@ static void glu_tokens(void* p, int64_t t0, int64_t t1) {
         for (int64_t j = 0; j < H; ++j) acc[j] = 0.0f;
         for (int64_t s = 0; s < c->top_k; ++s) {
             int64_t e = c->indices[t * c->top_k + s];
+            if (e < 0) continue; /* -1: an empty slot (expert-parallel partial sums) */
             float score = bf(c->scores[t * c->top_k + s]);
             for (int64_t i = 0; i < I; ++i) {
                 int64_t row = e * I + i;
@@ -533,7 +534,7 @@ int q38o_switch_glu(const uint16_t* x, int64_t T, int64_t H, int64_t I, int64_t 
     if (!valid_bits(bits) || group <= 0 || H % group || I % group) return -1;
     if ((H * bits) % 32 || (I * bits) % 32) return -1;
     for (int64_t i = 0; i < T * top_k; ++i)
-        if (indices[i] < 0 || indices[i] >= E) return -2;
+        if (indices[i] < -1 || indices[i] >= E) return -2;
     float* xf = (float*)malloc((size_t)(T * H) * sizeof(float));
     for (int64_t i = 0; i < T * H; ++i) xf[i] = bf(x[i]);
     glu_ctx c = {xf, H, I, top_k, H * bits / 32, I * bits / 32, H / group, I / group,

@@ -85,7 +85,8 @@ int q38o_sort_by_expert(const int32_t* indices, int64_t pairs, int64_t E, int32_
  * x [T,H]; indices/scores [T,k]; gate/up codes [E, I, H*bits/32], scales [E, I, H/group];
  * down codes [E, H, I*bits/32], scales [E, H, I/group].
  * weights_bf16 != 0 rounds every dequantized weight s*q + b once to bf16 (the operand of
- * a bf16 tensor-core product) instead of evaluating it in fp32. */
+ * a bf16 tensor-core product) instead of evaluating it in fp32.  An index of -1 marks an
+ * empty slot that contributes nothing. */
 int q38o_switch_glu(const uint16_t* x, int64_t T, int64_t H, int64_t I, int64_t E, int top_k,
                     const int32_t* indices, const uint16_t* scores,
                     const uint32_t* gw, const uint16_t* gs, const uint16_t* gb,

@@ -286,17 +286,19 @@ __global__ void __launch_bounds__(256) router_topk(const __nv_bfloat16* __restri
 
 // --------------------------------------------------------------------------- sort
 // Stable counting sort of pairs by expert (key), indices outside [0, E) in an extra
-// bucket E after all experts (and flagged).  Pairs are cut into segments of up to 32 per
+// bucket E after all experts (flagged unless -1, the empty-slot marker).  Pairs are cut into segments of up to 32 per
 // warp; per-warp, per-key counts give every (warp, key) run its start, and each warp then
 // places its pairs in order (ranks within a warp by __match_any_sync).
 //   * up to 1024 pairs: one block, one kernel;
 //   * more: blocks of 1024 pairs -- per-block counts, a scan over blocks and keys, and a
 //     placement pass that recomputes the per-warp counts.
 
+// -1 marks an empty slot (expert-parallel partial sums): sorted after all experts like an
+// invalid index, but not reported.
 __device__ __forceinline__ int sort_key(const int32_t* idx, int p, int E, uint32_t* status, bool flag) {
     int e = idx[p];
     if (e < 0 || e >= E) {
-        if (flag) atomicOr(status, Q38_DEV_BAD_INDEX);
+        if (flag && e != -1) atomicOr(status, Q38_DEV_BAD_INDEX);
         e = E;
     }
     return e;
@@ -623,6 +625,110 @@ q38_status launch_pdl(q38_ctx* ctx, const char* what, void (*kern)(KArgs...), di
     cfg.numAttrs = 1;
     cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
     return check_launch(ctx, what);
+}
+
+// Expert-parallel dispatch plan, one block: token t sends one row to every rank owning one
+// of its experts; rows are laid out rank-major, tokens ascending within a rank.
+// rowpos[t * world + r] = row index or -1; counts[r] = rows for rank r.
+__global__ void __launch_bounds__(1024, 1) ep_plan_kernel(const int32_t* __restrict__ idx, int T, int top_k, int epr,
+                                                          int world, int32_t* __restrict__ rowpos,
+                                                          int32_t* __restrict__ counts) {
+    griddep_wait();  // inputs come from the previous kernel on the stream
+    griddep_launch_dependents();
+    __shared__ int wsum[33];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int base = 0;
+    for (int r = 0; r < world; ++r) {
+        const int start = base;
+        for (int t0 = 0; t0 < T; t0 += 1024) {
+            const int t = t0 + threadIdx.x;
+            int f = 0;
+            if (t < T)
+                for (int s2 = 0; s2 < top_k; ++s2) {
+                    const int e = idx[static_cast<size_t>(t) * top_k + s2];
+                    f |= (e >= 0 && e / epr == r);
+                }
+            int incl = f;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int n = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += n;
+            }
+            if (lane == 31) wsum[warp] = incl;
+            __syncthreads();
+            if (warp == 0) {
+                const int w = wsum[lane];
+                int wi = w;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int n = __shfl_up_sync(0xffffffffu, wi, o);
+                    if (lane >= o) wi += n;
+                }
+                wsum[lane] = wi - w;
+                if (lane == 31) wsum[32] = wi;
+            }
+            __syncthreads();
+            if (t < T) rowpos[static_cast<size_t>(t) * world + r] = f ? base + wsum[warp] + incl - f : -1;
+            base += wsum[32];
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) counts[r] = base - start;
+    }
+}
+
+// rows[rowpos[t, r]] = x[t]; meta row = local expert per slot (or -1 when the slot's expert
+// lives elsewhere) followed by the slot scores' bf16 bits.
+__global__ void __launch_bounds__(256) ep_pack_kernel(const __nv_bfloat16* __restrict__ x, int H,
+                                                      const int32_t* __restrict__ idx,
+                                                      const __nv_bfloat16* __restrict__ scores, int top_k, int epr,
+                                                      int world, const int32_t* __restrict__ rowpos,
+                                                      __nv_bfloat16* __restrict__ rows, int32_t* __restrict__ meta) {
+    griddep_wait();  // inputs come from the previous kernel on the stream
+    griddep_launch_dependents();
+    const int t = blockIdx.x;
+    const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * H);
+    for (int r = 0; r < world; ++r) {
+        const int row = rowpos[static_cast<size_t>(t) * world + r];
+        if (row < 0) continue;
+        uint4* dst = reinterpret_cast<uint4*>(rows + static_cast<size_t>(row) * H);
+        for (int c = threadIdx.x; c < H / 8; c += 256) dst[c] = src[c];
+        if (threadIdx.x < top_k) {
+            const int e = idx[static_cast<size_t>(t) * top_k + threadIdx.x];
+            int32_t* m = meta + static_cast<size_t>(row) * 2 * top_k;
+            m[threadIdx.x] = (e >= 0 && e / epr == r) ? e % epr : -1;
+            m[top_k + threadIdx.x] =
+                reinterpret_cast<const uint16_t*>(scores)[static_cast<size_t>(t) * top_k + threadIdx.x];
+        }
+    }
+}
+
+// out[t] = bf16(sum over ranks r, in rank order, of partial[rowpos[t, r]]) in fp32
+__global__ void __launch_bounds__(256) ep_reduce_kernel(const __nv_bfloat16* __restrict__ partial, int H,
+                                                        const int32_t* __restrict__ rowpos, int world,
+                                                        __nv_bfloat16* __restrict__ out) {
+    griddep_wait();  // inputs come from the previous kernel on the stream
+    griddep_launch_dependents();
+    const int t = blockIdx.x;
+    for (int c = threadIdx.x * 8; c < H; c += 256 * 8) {
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int r = 0; r < world; ++r) {
+            const int row = rowpos[static_cast<size_t>(t) * world + r];
+            if (row < 0) continue;
+            const uint4 u = *reinterpret_cast<const uint4*>(partial + static_cast<size_t>(row) * H + c);
+            const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                acc[2 * j] = __fadd_rn(acc[2 * j], bf16_bits_to_f32(q[j] & 0xFFFFu));
+                acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], bf16_bits_to_f32(q[j] >> 16));
+            }
+        }
+        uint4 o;
+        o.x = pack_bf16x2(acc[0], acc[1]);
+        o.y = pack_bf16x2(acc[2], acc[3]);
+        o.z = pack_bf16x2(acc[4], acc[5]);
+        o.w = pack_bf16x2(acc[6], acc[7]);
+        *reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H + c) = o;
+    }
 }
 
 q38_status set_dev(q38_ctx* ctx) {
@@ -967,6 +1073,49 @@ q38_status q38_moe_combine(q38_ctx* ctx, const void* y, int64_t H, const int32_t
     return launch_pdl(ctx, "moe_combine", moe_combine_kernel, dim3(static_cast<unsigned>(T)), dim3(256), 0,
                       static_cast<const __nv_bfloat16*>(y), static_cast<int>(H), static_cast<const int32_t*>(inv),
                       indices, static_cast<const __nv_bfloat16*>(scores), top_k, static_cast<int>(E),
+                      static_cast<__nv_bfloat16*>(out));
+}
+
+q38_status q38_moe_ep_plan(q38_ctx* ctx, const int32_t* indices, int64_t T, int top_k, int64_t experts_per_rank,
+                           int world, int32_t* rowpos, int32_t* counts) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    if (T < 0 || top_k < 1 || experts_per_rank < 1 || world < 1 || world > 1024)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_ep_plan: bad sizes");
+    if (!indices || !rowpos || !counts) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_ep_plan: null pointer");
+    q38_status st = set_dev(ctx);
+    if (st != Q38_OK) return st;
+    return launch_pdl(ctx, "moe_ep_plan", ep_plan_kernel, dim3(1), dim3(1024), 0, indices, static_cast<int>(T), top_k,
+                      static_cast<int>(experts_per_rank), world, rowpos, counts);
+}
+
+q38_status q38_moe_ep_pack(q38_ctx* ctx, const void* x, int64_t H, const int32_t* indices, const void* scores,
+                           int64_t T, int top_k, int64_t experts_per_rank, int world, const int32_t* rowpos,
+                           void* rows, int32_t* meta) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    if (T < 0 || H <= 0 || H % 8 || top_k < 1 || top_k > 256 || experts_per_rank < 1 || world < 1)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_ep_pack: bad sizes");
+    if (T == 0) return Q38_OK;
+    if (!x || !indices || !scores || !rowpos || !rows || !meta)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_ep_pack: null pointer");
+    if (!aligned16(x) || !aligned16(rows)) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_ep_pack: rows must be 16-byte aligned");
+    q38_status st = set_dev(ctx);
+    if (st != Q38_OK) return st;
+    return launch_pdl(ctx, "moe_ep_pack", ep_pack_kernel, dim3(static_cast<unsigned>(T)), dim3(256), 0,
+                      static_cast<const __nv_bfloat16*>(x), static_cast<int>(H), indices,
+                      static_cast<const __nv_bfloat16*>(scores), top_k, static_cast<int>(experts_per_rank), world,
+                      rowpos, static_cast<__nv_bfloat16*>(rows), meta);
+}
+
+q38_status q38_moe_ep_reduce(q38_ctx* ctx, const void* partial, int64_t H, const int32_t* rowpos, int64_t T,
+                             int world, void* out) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    if (T < 0 || H <= 0 || H % 8 || world < 1) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_ep_reduce: bad sizes");
+    if (T == 0) return Q38_OK;
+    if (!partial || !rowpos || !out) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_ep_reduce: null pointer");
+    q38_status st = set_dev(ctx);
+    if (st != Q38_OK) return st;
+    return launch_pdl(ctx, "moe_ep_reduce", ep_reduce_kernel, dim3(static_cast<unsigned>(T)), dim3(256), 0,
+                      static_cast<const __nv_bfloat16*>(partial), static_cast<int>(H), rowpos, world,
                       static_cast<__nv_bfloat16*>(out));
 }
 

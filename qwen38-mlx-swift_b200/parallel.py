@@ -7,9 +7,11 @@ compute on libq38.
   prefill configuration.
 * ExpertParallelMoE -- the routed experts of the Flash-Next sparse MoE layer
   (FlashNext/Qwen4ExpSparseMoE.swift:275-294) split contiguously over the ranks: each rank
-  routes its own tokens, sends every (token, slot) pair's activation row to the rank that
-  owns the pair's expert (all-to-all), runs SwitchGLU on what it received, returns the
-  expert outputs (all-to-all) and forms the score-weighted sum at home.
+  routes its own tokens and sends each token's activation row once to every rank that owns
+  one of its experts (all-to-all), with the rank-local expert ids and router scores of its
+  slots; the receiving rank runs SwitchGLU over its experts only (other slots marked -1),
+  which gives the token's partial score-weighted sum; the partial rows return (all-to-all)
+  and the home rank adds them in rank order.
 
 The compute goes through an `ops` object (DeviceOps = libq38 on the GPU); tests substitute
 CPU restatements to check the exchange bookkeeping without a GPU.
@@ -36,20 +38,17 @@ class DeviceOps:
     def route(self, x, wr, k, normalize=True):
         return self.q.moe_route(x, wr, k, normalize)
 
-    def sort(self, keys, n):
-        return self.q.moe_sort(keys, n)
+    def ep_plan(self, idx, epr, world):
+        return self.q.moe_ep_plan(idx, epr, world)
 
-    def pack(self, x, idx, perm, epr):
-        return self.q.moe_dispatch_pack(x, idx, perm, epr)
+    def ep_pack(self, x, idx, sc, rowpos, epr, rows_total):
+        return self.q.moe_ep_pack(x, idx, sc, rowpos, epr, rows_total)
 
-    def local_experts(self, rows, local_e, weights, group, bits):
-        n = rows.shape[0]
-        ones = torch.ones((n, 1), dtype=torch.bfloat16, device=rows.device)
-        (gw, gs, gb), (uw, us, ub), (dw, ds, db) = weights
-        return self.q.switch_glu(rows, local_e.view(n, 1), ones, (gw, gs, gb), (uw, us, ub), (dw, ds, db), group, bits)
+    def partial_experts(self, rows, local_idx, scores, weights, group, bits):
+        return self.q.switch_glu(rows, local_idx, scores, *weights, group, bits)
 
-    def combine(self, y, perm, idx, sc, E):
-        return self.q.moe_combine(y, perm, idx, sc, E)
+    def ep_reduce(self, partial, rowpos):
+        return self.q.moe_ep_reduce(partial, rowpos)
 
 
 def _rank_world(group=None):
@@ -144,21 +143,20 @@ class ExpertParallelMoE:
 
     def __call__(self, x):
         o = self.ops
-        idx, sc = o.route(x, self.wr, self.k, self.normalize)
+        k = self.k
+        idx, sc = o.route(x, self.wr, k, self.normalize)
         if self.world == 1:
-            return o.combine(o.local_experts(*o.pack(x, idx, torch.arange(idx.numel(), dtype=torch.int32,
-                                                                                 device=idx.device), self.epr),
-                                             self.experts, self.group, self.bits),
-                             torch.arange(idx.numel(), dtype=torch.int32, device=idx.device), idx, sc, self.E)
-        dest = torch.div(idx, self.epr, rounding_mode="floor").to(torch.int32).reshape(-1).contiguous()
-        perm, off = o.sort(dest, self.world)
-        send_t = (off[1:] - off[:-1]).to(torch.int64)
+            return o.partial_experts(x, idx, sc, self.experts, self.group, self.bits)
+        rowpos, counts = o.ep_plan(idx, self.epr, self.world)
+        send_t = counts.to(torch.int64)
         recv_t = torch.empty_like(send_t)
         dist.all_to_all_single(recv_t, send_t, group=self.pg)
         send, recv = send_t.tolist(), recv_t.tolist()
-        rows, loc = o.pack(x, idx, perm, self.epr)
+        rows, meta = o.ep_pack(x, idx, sc, rowpos, self.epr, sum(send))
         rrows = _exchange(rows, send, recv, self.pg)
-        rloc = _exchange(loc, send, recv, self.pg)
-        y = o.local_experts(rrows, rloc, self.experts, self.group, self.bits)
-        back = _exchange(y, recv, send, self.pg)
-        return o.combine(back, perm, idx, sc, self.E)
+        rmeta = _exchange(meta, send, recv, self.pg)
+        lidx = rmeta[:, :k].contiguous()
+        lsc = rmeta[:, k:].to(torch.int16).view(torch.bfloat16).contiguous()
+        part = o.partial_experts(rrows, lidx, lsc, self.experts, self.group, self.bits)
+        back = _exchange(part, recv, send, self.pg)
+        return o.ep_reduce(back, rowpos)

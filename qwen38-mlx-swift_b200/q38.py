@@ -67,6 +67,9 @@ _sig("q38_moe_sort", [_P, _P, _I, _I, _P, _P])
 _sig("q38_silu_mul", [_P, _P, _P, _I, _P])
 _sig("q38_moe_dispatch_pack", [_P, _P, _I, _P, _P, _I, _i, _I, _P, _P])
 _sig("q38_moe_combine", [_P, _P, _I, _P, _P, _P, _I, _i, _I, _P])
+_sig("q38_moe_ep_plan", [_P, _P, _I, _i, _I, _i, _P, _P])
+_sig("q38_moe_ep_pack", [_P, _P, _I, _P, _P, _I, _i, _I, _i, _P, _P, _P])
+_sig("q38_moe_ep_reduce", [_P, _P, _I, _P, _I, _i, _P])
 _sig("q38_switch_glu", [_P, _P, _I, _I, _I, _I, _i, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _i, _i, _i, _P])
 
 
@@ -357,6 +360,43 @@ def moe_combine(y: torch.Tensor, perm: torch.Tensor, indices: torch.Tensor, scor
     ctx = _bind(indices)
     _check(ctx, _lib.q38_moe_combine(ctx, _ptr(y), H, _ptr(perm), _ptr(indices), _ptr(scores), T, k,
                                      num_experts, _ptr(out)))
+    return out
+
+
+def moe_ep_plan(indices: torch.Tensor, experts_per_rank: int, world: int):
+    """-> (rowpos int32 [T, world], counts int32 [world]) of the one-row-per-(token, rank)
+    expert-parallel dispatch."""
+    _need(indices, "indices")
+    T, k = indices.shape
+    rowpos = torch.empty((T, world), dtype=torch.int32, device=indices.device)
+    counts = torch.empty((world,), dtype=torch.int32, device=indices.device)
+    ctx = _bind(indices)
+    _check(ctx, _lib.q38_moe_ep_plan(ctx, _ptr(indices), T, k, experts_per_rank, world, _ptr(rowpos), _ptr(counts)))
+    return rowpos, counts
+
+
+def moe_ep_pack(x: torch.Tensor, indices: torch.Tensor, scores: torch.Tensor, rowpos: torch.Tensor,
+                experts_per_rank: int, rows_total: int):
+    """-> (rows bf16 [rows_total, H], meta int32 [rows_total, 2k])."""
+    _need(x, "x"), _need(indices, "indices"), _need(scores, "scores"), _need(rowpos, "rowpos")
+    T, H = x.shape
+    k = indices.shape[1]
+    world = rowpos.shape[1]
+    rows = torch.empty((rows_total, H), dtype=x.dtype, device=x.device)
+    meta = torch.empty((rows_total, 2 * k), dtype=torch.int32, device=x.device)
+    ctx = _bind(x)
+    _check(ctx, _lib.q38_moe_ep_pack(ctx, _ptr(x), H, _ptr(indices), _ptr(scores), T, k, experts_per_rank, world,
+                                     _ptr(rowpos), _ptr(rows), _ptr(meta)))
+    return rows, meta
+
+
+def moe_ep_reduce(partial: torch.Tensor, rowpos: torch.Tensor) -> torch.Tensor:
+    _need(partial, "partial"), _need(rowpos, "rowpos")
+    T, world = rowpos.shape
+    H = partial.shape[1]
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=rowpos.device)
+    ctx = _bind(rowpos)
+    _check(ctx, _lib.q38_moe_ep_reduce(ctx, _ptr(partial), H, _ptr(rowpos), T, world, _ptr(out)))
     return out
 
 
