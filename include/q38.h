@@ -229,9 +229,10 @@ Q38_API q38_status q38_moe_combine(q38_ctx* ctx, const void* y, int64_t H, const
  *   q38_moe_ep_plan: rowpos[t * world + r] = the row token t sends to rank r (rank-major,
  *     tokens ascending within a rank), or -1 when none of its experts lives on r;
  *     counts[r] = rows for rank r.  One block; indices int32 [T, top_k].
- *   q38_moe_ep_pack: rows[rowpos] = x[t] (bf16 [*, H]); meta int32 [rows, 2 * top_k] =
- *     the rank-local expert of each slot or -1 (expert elsewhere), then the slot scores'
- *     bf16 bits.  The receiving rank runs q38_switch_glu on the rows with those indices
+ *   q38_moe_ep_pack: rows[rowpos] = x[t] (bf16, row stride rows_ld >= H, a multiple of 8);
+ *     meta (int32, row stride meta_ld >= 2 * top_k) = the rank-local expert of each slot
+ *     or -1 (expert elsewhere), then the slot scores' bf16 bits.  meta may point into the
+ *     rows buffer (at column H) so that one exchange moves both.  The receiving rank runs q38_switch_glu on the rows with those indices
  *     and scores (slots of -1 contribute nothing), which yields each row's partial sum.
  *   q38_moe_ep_reduce: out[t] = bf16(sum over r, in rank order, of partial[rowpos[t, r]])
  *     with fp32 accumulation. */
@@ -239,7 +240,7 @@ Q38_API q38_status q38_moe_ep_plan(q38_ctx* ctx, const int32_t* indices, int64_t
                                    int64_t experts_per_rank, int world, int32_t* rowpos, int32_t* counts);
 Q38_API q38_status q38_moe_ep_pack(q38_ctx* ctx, const void* x, int64_t H, const int32_t* indices, const void* scores,
                                    int64_t T, int top_k, int64_t experts_per_rank, int world, const int32_t* rowpos,
-                                   void* rows, int32_t* meta);
+                                   void* rows, int64_t rows_ld, int32_t* meta, int64_t meta_ld);
 Q38_API q38_status q38_moe_ep_reduce(q38_ctx* ctx, const void* partial, int64_t H, const int32_t* rowpos, int64_t T,
                                      int world, void* out);
 

@@ -682,7 +682,8 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const __nv_bfloat16* __res
                                                       const int32_t* __restrict__ idx,
                                                       const __nv_bfloat16* __restrict__ scores, int top_k, int epr,
                                                       int world, const int32_t* __restrict__ rowpos,
-                                                      __nv_bfloat16* __restrict__ rows, int32_t* __restrict__ meta) {
+                                                      __nv_bfloat16* __restrict__ rows, int64_t rows_ld,
+                                                      int32_t* __restrict__ meta, int64_t meta_ld) {
     griddep_wait();  // inputs come from the previous kernel on the stream
     griddep_launch_dependents();
     const int t = blockIdx.x;
@@ -690,11 +691,11 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const __nv_bfloat16* __res
     for (int r = 0; r < world; ++r) {
         const int row = rowpos[static_cast<size_t>(t) * world + r];
         if (row < 0) continue;
-        uint4* dst = reinterpret_cast<uint4*>(rows + static_cast<size_t>(row) * H);
+        uint4* dst = reinterpret_cast<uint4*>(rows + static_cast<size_t>(row) * rows_ld);
         for (int c = threadIdx.x; c < H / 8; c += 256) dst[c] = src[c];
         if (threadIdx.x < top_k) {
             const int e = idx[static_cast<size_t>(t) * top_k + threadIdx.x];
-            int32_t* m = meta + static_cast<size_t>(row) * 2 * top_k;
+            int32_t* m = meta + static_cast<size_t>(row) * meta_ld;
             m[threadIdx.x] = (e >= 0 && e / epr == r) ? e % epr : -1;
             m[top_k + threadIdx.x] =
                 reinterpret_cast<const uint16_t*>(scores)[static_cast<size_t>(t) * top_k + threadIdx.x];
@@ -966,7 +967,8 @@ q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
     if ((st = launch_pdl(ctx, "moe_tiles", moe_tiles_kernel, dim3(1), dim3(1024), 0, offs, static_cast<int>(E), xr,
                          rb_gu, rb_d, gu, dn, counts)) != Q38_OK)
         return st;
-    if ((st = moe_gather_launch(ctx, x, static_cast<int>(H), perm, static_cast<int>(P), top_k, xs, bits)) != Q38_OK)
+    if ((st = moe_gather_launch(ctx, x, static_cast<int>(H), perm, static_cast<int>(P), top_k, offs + E, xs, bits)) !=
+        Q38_OK)
         return st;
     GroupedProblem g;
     g.x = xs;
@@ -1090,10 +1092,11 @@ q38_status q38_moe_ep_plan(q38_ctx* ctx, const int32_t* indices, int64_t T, int 
 
 q38_status q38_moe_ep_pack(q38_ctx* ctx, const void* x, int64_t H, const int32_t* indices, const void* scores,
                            int64_t T, int top_k, int64_t experts_per_rank, int world, const int32_t* rowpos,
-                           void* rows, int32_t* meta) {
+                           void* rows, int64_t rows_ld, int32_t* meta, int64_t meta_ld) {
     if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
-    if (T < 0 || H <= 0 || H % 8 || top_k < 1 || top_k > 256 || experts_per_rank < 1 || world < 1)
-        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_ep_pack: bad sizes");
+    if (T < 0 || H <= 0 || H % 8 || top_k < 1 || top_k > 256 || experts_per_rank < 1 || world < 1 || rows_ld < H ||
+        rows_ld % 8 || meta_ld < 2 * top_k)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_ep_pack: bad sizes or strides");
     if (T == 0) return Q38_OK;
     if (!x || !indices || !scores || !rowpos || !rows || !meta)
         return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "moe_ep_pack: null pointer");
@@ -1103,7 +1106,7 @@ q38_status q38_moe_ep_pack(q38_ctx* ctx, const void* x, int64_t H, const int32_t
     return launch_pdl(ctx, "moe_ep_pack", ep_pack_kernel, dim3(static_cast<unsigned>(T)), dim3(256), 0,
                       static_cast<const __nv_bfloat16*>(x), static_cast<int>(H), indices,
                       static_cast<const __nv_bfloat16*>(scores), top_k, static_cast<int>(experts_per_rank), world,
-                      rowpos, static_cast<__nv_bfloat16*>(rows), meta);
+                      rowpos, static_cast<__nv_bfloat16*>(rows), rows_ld, meta, meta_ld);
 }
 
 q38_status q38_moe_ep_reduce(q38_ctx* ctx, const void* partial, int64_t H, const int32_t* rowpos, int64_t T,

@@ -28,7 +28,9 @@ struct GroupedProblem {
 
 q38_status grouped_gate_up(q38_ctx* ctx, const GroupedProblem& p, int bits);
 q38_status grouped_down(q38_ctx* ctx, const GroupedProblem& p, int bits);
+// xs[j] = permute(x[perm[j] / top_k]) for j < min(pairs, *valid) (valid: device count of
+// pairs with an expert, i.e. offsets[E] of the sort).
 q38_status moe_gather_launch(q38_ctx* ctx, const void* x, int H, const int32_t* perm, int pairs, int top_k,
-                             void* xs, int bits);
+                             const int32_t* valid, void* xs, int bits);
 
 }  // namespace q38

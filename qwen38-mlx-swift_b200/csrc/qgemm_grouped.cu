@@ -414,19 +414,21 @@ q38_status grouped_down(q38_ctx* ctx, const GroupedProblem& p, int bits) {
 template <int BITS>
 __global__ void __launch_bounds__(256) moe_gather_kernel(const __nv_bfloat16* __restrict__ x, int H,
                                                          const int32_t* __restrict__ perm, int pairs, int top_k,
+                                                         const int32_t* __restrict__ valid,
                                                          __nv_bfloat16* __restrict__ xs) {
     griddep_wait();
     griddep_launch_dependents();
     const int G = H / 64;
     const int64_t item = blockIdx.x * 256LL + threadIdx.x;
-    if (item >= static_cast<int64_t>(pairs) * G) return;
+    // pairs past *valid (empty or invalid slots, sorted after every expert) feed no tile
+    if (item >= static_cast<int64_t>(min(pairs, *valid)) * G) return;
     const int j = static_cast<int>(item / G), g = static_cast<int>(item % G);
     const int t = perm[j] / top_k;
     permute_group<BITS>(x + static_cast<size_t>(t) * H + g * 64, xs + static_cast<size_t>(j) * H + g * 64);
 }
 
 q38_status moe_gather_launch(q38_ctx* ctx, const void* x, int H, const int32_t* perm, int pairs, int top_k,
-                             void* xs, int bits) {
+                             const int32_t* valid, void* xs, int bits) {
     const long long items = static_cast<long long>(pairs) * (H / 64);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -441,9 +443,9 @@ q38_status moe_gather_launch(q38_ctx* ctx, const void* x, int H, const int32_t* 
     __nv_bfloat16* o = static_cast<__nv_bfloat16*>(xs);
     cudaError_t e;
     switch (bits) {
-        case 2: e = cudaLaunchKernelEx(&cfg, moe_gather_kernel<2>, xb, H, perm, pairs, top_k, o); break;
-        case 3: e = cudaLaunchKernelEx(&cfg, moe_gather_kernel<3>, xb, H, perm, pairs, top_k, o); break;
-        default: e = cudaLaunchKernelEx(&cfg, moe_gather_kernel<4>, xb, H, perm, pairs, top_k, o); break;
+        case 2: e = cudaLaunchKernelEx(&cfg, moe_gather_kernel<2>, xb, H, perm, pairs, top_k, valid, o); break;
+        case 3: e = cudaLaunchKernelEx(&cfg, moe_gather_kernel<3>, xb, H, perm, pairs, top_k, valid, o); break;
+        default: e = cudaLaunchKernelEx(&cfg, moe_gather_kernel<4>, xb, H, perm, pairs, top_k, valid, o); break;
     }
     (void)e;
     return check_launch(ctx, "moe_gather");

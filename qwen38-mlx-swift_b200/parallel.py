@@ -44,6 +44,9 @@ class DeviceOps:
     def ep_pack(self, x, idx, sc, rowpos, epr, rows_total):
         return self.q.moe_ep_pack(x, idx, sc, rowpos, epr, rows_total)
 
+    def ep_unpack(self, packed, H, k):
+        return self.q.split_ep_packed(packed, H, k)
+
     def partial_experts(self, rows, local_idx, scores, weights, group, bits):
         return self.q.switch_glu(rows, local_idx, scores, *weights, group, bits)
 
@@ -152,11 +155,9 @@ class ExpertParallelMoE:
         recv_t = torch.empty_like(send_t)
         dist.all_to_all_single(recv_t, send_t, group=self.pg)
         send, recv = send_t.tolist(), recv_t.tolist()
-        rows, meta = o.ep_pack(x, idx, sc, rowpos, self.epr, sum(send))
-        rrows = _exchange(rows, send, recv, self.pg)
-        rmeta = _exchange(meta, send, recv, self.pg)
-        lidx = rmeta[:, :k].contiguous()
-        lsc = rmeta[:, k:].to(torch.int16).view(torch.bfloat16).contiguous()
+        # one exchange moves each row with its slot metadata: [rows, H + 4k] bf16
+        packed = o.ep_pack(x, idx, sc, rowpos, self.epr, sum(send))
+        rrows, lidx, lsc = o.ep_unpack(_exchange(packed, send, recv, self.pg), x.shape[1], k)
         part = o.partial_experts(rrows, lidx, lsc, self.experts, self.group, self.bits)
         back = _exchange(part, recv, send, self.pg)
         return o.ep_reduce(back, rowpos)

@@ -68,7 +68,7 @@ _sig("q38_silu_mul", [_P, _P, _P, _I, _P])
 _sig("q38_moe_dispatch_pack", [_P, _P, _I, _P, _P, _I, _i, _I, _P, _P])
 _sig("q38_moe_combine", [_P, _P, _I, _P, _P, _P, _I, _i, _I, _P])
 _sig("q38_moe_ep_plan", [_P, _P, _I, _i, _I, _i, _P, _P])
-_sig("q38_moe_ep_pack", [_P, _P, _I, _P, _P, _I, _i, _I, _i, _P, _P, _P])
+_sig("q38_moe_ep_pack", [_P, _P, _I, _P, _P, _I, _i, _I, _i, _P, _P, _I, _P, _I])
 _sig("q38_moe_ep_reduce", [_P, _P, _I, _P, _I, _i, _P])
 _sig("q38_switch_glu", [_P, _P, _I, _I, _I, _I, _i, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _i, _i, _i, _P])
 
@@ -376,18 +376,29 @@ def moe_ep_plan(indices: torch.Tensor, experts_per_rank: int, world: int):
 
 
 def moe_ep_pack(x: torch.Tensor, indices: torch.Tensor, scores: torch.Tensor, rowpos: torch.Tensor,
-                experts_per_rank: int, rows_total: int):
-    """-> (rows bf16 [rows_total, H], meta int32 [rows_total, 2k])."""
+                experts_per_rank: int, rows_total: int) -> torch.Tensor:
+    """-> packed bf16 [rows_total, H + 4k rounded up to 8]: each row = the token's activations,
+    then its slot metadata (k rank-local expert ids or -1, then k score bit patterns, as
+    int32)."""
     _need(x, "x"), _need(indices, "indices"), _need(scores, "scores"), _need(rowpos, "rowpos")
     T, H = x.shape
     k = indices.shape[1]
     world = rowpos.shape[1]
-    rows = torch.empty((rows_total, H), dtype=x.dtype, device=x.device)
-    meta = torch.empty((rows_total, 2 * k), dtype=torch.int32, device=x.device)
+    ld = H + (4 * k + 7) // 8 * 8  # rows stay 16-byte aligned
+    packed = torch.empty((rows_total, ld), dtype=x.dtype, device=x.device)
+    meta = packed[:, H:]
     ctx = _bind(x)
     _check(ctx, _lib.q38_moe_ep_pack(ctx, _ptr(x), H, _ptr(indices), _ptr(scores), T, k, experts_per_rank, world,
-                                     _ptr(rowpos), _ptr(rows), _ptr(meta)))
-    return rows, meta
+                                     _ptr(rowpos), _ptr(packed), ld, meta.data_ptr() if rows_total else None, ld // 2))
+    return packed
+
+
+def split_ep_packed(packed: torch.Tensor, H: int, k: int):
+    """packed [R, H + 4k (+ padding)] -> (rows [R, H], rank-local expert ids int32 [R, k],
+    scores bf16 [R, k])."""
+    rows = packed[:, :H].contiguous()
+    meta = packed[:, H:H + 4 * k].contiguous().view(torch.int32)
+    return rows, meta[:, :k].contiguous(), meta[:, k:].to(torch.int16).view(torch.bfloat16).contiguous()
 
 
 def moe_ep_reduce(partial: torch.Tensor, rowpos: torch.Tensor) -> torch.Tensor:

@@ -72,7 +72,11 @@ class OracleOps:
                 rows[row] = x[t]
                 meta[row, :k] = np.where(i[t] // epr == r, i[t] % epr, -1)
                 meta[row, k:] = sbits[t]
-        return rows, torch.from_numpy(meta)
+        return torch.cat([rows, torch.from_numpy(meta).view(torch.bfloat16)], dim=1)
+
+    def ep_unpack(self, packed, H, k):
+        meta = packed[:, H:].contiguous().view(torch.int32)
+        return packed[:, :H].contiguous(), meta[:, :k].contiguous(), meta[:, k:].to(torch.int16).view(torch.bfloat16)
 
     def partial_experts(self, rows, lidx, lsc, weights, group, bits):
         n = rows.shape[0]

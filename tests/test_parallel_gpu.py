@@ -92,15 +92,14 @@ def test_ep_exchange_kernels_single_gpu(q38):
         np.testing.assert_array_equal(rp[m, r], base + np.arange(cnt[r]))
         assert (rp[~m, r] == -1).all()
         base += cnt[r]
-    rows, meta = q38.moe_ep_pack(x, idx, sc, rowpos, epr, sum(cnt))
+    packed = q38.moe_ep_pack(x, idx, sc, rowpos, epr, sum(cnt))
     parts = []
     off = 0
     for r in range(world):
-        rr, mm = rows[off:off + cnt[r]], meta[off:off + cnt[r]]
+        rr, lidx, lsc = q38.split_ep_packed(packed[off:off + cnt[r]], H, k)
         ws = [(c[r * epr:(r + 1) * epr].contiguous(), s[r * epr:(r + 1) * epr].contiguous(),
                b[r * epr:(r + 1) * epr].contiguous()) for (c, s, b) in dev]
-        lsc = mm[:, k:].to(torch.int16).view(torch.bfloat16).contiguous()
-        parts.append(q38.switch_glu(rr.contiguous(), mm[:, :k].contiguous(), lsc, *ws, 64, bits))
+        parts.append(q38.switch_glu(rr, lidx, lsc, *ws, 64, bits))
         off += cnt[r]
     out = q38.moe_ep_reduce(torch.cat(parts), rowpos)
     assert torch.equal(out, rank_partials_sum(q38, x, idx, sc, dev, epr, world))
