@@ -107,11 +107,12 @@ __global__ void __launch_bounds__(128) router_logits_small(const __nv_bfloat16* 
     }
 }
 
-// logits for prompts on the tensor cores: one CTA per 128 tokens x 256 experts, both
-// operands TMA-loaded with the 128-byte swizzle (64-element k boxes, 4-stage ring), the
-// fp32 accumulator in TMEM, four warps drain it.
-constexpr int R_STAGES = 4;
-constexpr int R_A = 128 * 128, R_B = 256 * 128;
+// logits for prompts on the tensor cores: one CTA per 128 tokens x 128 experts, both
+// operands TMA-loaded with the 128-byte swizzle (64-element k boxes, 6-stage ring), the
+// fp32 accumulator in TMEM, four warps drain it with 16-byte stores.
+constexpr int R_STAGES = 6;
+constexpr int R_N = 128;
+constexpr int R_A = 128 * 128, R_B = R_N * 128;
 
 __global__ void __launch_bounds__(128, 1) router_logits_tc(const __grid_constant__ CUtensorMap map_x,
                                                            const __grid_constant__ CUtensorMap map_w, int T, int H,
@@ -128,7 +129,7 @@ __global__ void __launch_bounds__(128, 1) router_logits_tc(const __grid_constant
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     uint8_t* ring = smem + 1024;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t0 = blockIdx.x * 128, e0 = blockIdx.y * 256;
+    const int t0 = blockIdx.x * 128, e0 = blockIdx.y * R_N;
     const int ksteps = H / 64;
     if (threadIdx.x == 0) {
         for (int i = 0; i < R_STAGES; ++i) {
@@ -139,7 +140,7 @@ __global__ void __launch_bounds__(128, 1) router_logits_tc(const __grid_constant
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, 256);
+        tmem_alloc(tmem_slot, R_N);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -157,7 +158,7 @@ __global__ void __launch_bounds__(128, 1) router_logits_tc(const __grid_constant
             tma_load_2d(st + R_A, &map_w, &full[s], ks * 64, e0);
         }
     } else if (warp == 1 && lane == 0) {
-        const uint32_t idesc = idesc_bf16_f32(128, 256);
+        const uint32_t idesc = idesc_bf16_f32(128, R_N);
         for (int ks = 0; ks < ksteps && ok; ++ks) {
             const int s = ks % R_STAGES;
             if (!mbar_wait(&full[s], (ks / R_STAGES) & 1, status)) {
@@ -180,14 +181,22 @@ __global__ void __launch_bounds__(128, 1) router_logits_tc(const __grid_constant
     tc_fence_after();
     const int t = t0 + warp * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const bool vec = (E % 8) == 0;
 #pragma unroll 1
-    for (int ch = 0; ch < 8; ++ch) {
+    for (int ch = 0; ch < R_N / 32; ++ch) {
         float v[32];
         tmem_ld32(tmem + lane_off + ch * 32, v);
-        if (got && t < T) {
+        const int ec = e0 + ch * 32;
+        if (got && t < T && vec && ec + 32 <= E) {
+            uint4* dst = reinterpret_cast<uint4*>(logits + static_cast<size_t>(t) * E + ec);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                dst[q] = make_uint4(pack_bf16x2(v[8 * q], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
+                                    pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+        } else if (got && t < T) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-                const int e = e0 + ch * 32 + i;
+                const int e = ec + i;
                 if (e < E) logits[static_cast<size_t>(t) * E + e] = __float2bfloat16_rn(v[i]);
             }
         }
@@ -199,7 +208,7 @@ __global__ void __launch_bounds__(128, 1) router_logits_tc(const __grid_constant
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem, 256);
+    if (warp == 1) tmem_dealloc(tmem, R_N);
 }
 
 // softmax + top-k, one warp per token; lane l holds experts l, l+32, ... (NJ per lane).
@@ -789,7 +798,7 @@ q38_status logits_launch(q38_ctx* ctx, const void* x, int64_t T, int64_t H, cons
     }
     CUtensorMap mx, mw;
     if (!make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, H, T, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, wr, H, E, 64, 256, CU_TENSOR_MAP_SWIZZLE_128B))
+        !make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, wr, H, E, 64, R_N, CU_TENSOR_MAP_SWIZZLE_128B))
         return fail(ctx, Q38_ERR_CUDA, "moe_route: tensor map encoding failed");
     const int smem = 2048 + R_STAGES * (R_A + R_B);
     static std::mutex mu2;
@@ -802,7 +811,7 @@ q38_status logits_launch(q38_ctx* ctx, const void* x, int64_t T, int64_t H, cons
             cfg[ctx->device] = true;
         }
     }
-    dim3 grid(static_cast<unsigned>((T + 127) / 128), static_cast<unsigned>((E + 255) / 256));
+    dim3 grid(static_cast<unsigned>((T + 127) / 128), static_cast<unsigned>((E + R_N - 1) / R_N));
     return launch_pdl(ctx, "router_logits_tc", router_logits_tc, grid, dim3(128), smem, mx, mw, static_cast<int>(T),
                       static_cast<int>(H), static_cast<int>(E), static_cast<__nv_bfloat16*>(logits), ctx->d_status);
 }
