@@ -47,12 +47,15 @@ constexpr int P_WARP_DEQ0 = 3, P_WARP_EPI0 = P_WARP_DEQ0 + P_DEQ_WARPS;
 constexpr int P_THREADS = (P_WARP_EPI0 + P_EPI_WARPS) * 32;
 constexpr uint32_t P_IDESC = idesc_bf16_f32(2 * P_ROWS, P_TOK);
 
-template <int BITS>
+// SB_TMA: scales/biases ride in the weight stage as {8 groups, 128 rows} TMA boxes (needs
+// K % 512 == 0 for the 16-byte row stride of the scale arrays); otherwise the dequantizing
+// threads read them from global memory one stage ahead.
+template <int BITS, bool SB_TMA>
 struct PF {
     static constexpr int CODE_W = CodeLayout<BITS>::CODE_W;  // code words per row per stage
     static constexpr int CODE_B = P_ROWS * CODE_W * 4;       // 4 / 6 / 8 KiB
     static constexpr int X_B = 2 * P_HTOK * 128;          // two 64-element 128-byte-swizzled boxes
-    static constexpr int W_STAGE = (CODE_B + 1023) / 1024 * 1024;  // codes only
+    static constexpr int W_STAGE = (CODE_B + (SB_TMA ? 4096 : 0) + 1023) / 1024 * 1024;
     static constexpr int X_STAGES = 5;
     static constexpr int W_STAGES_MAX = (227 * 1024 - 2048 - X_STAGES * X_B) / W_STAGE;
     static constexpr int W_STAGES = W_STAGES_MAX > 8 ? 8 : W_STAGES_MAX;
@@ -82,11 +85,13 @@ struct PArgs {
     int M, N, K, nR, ntiles, has_bias;
 };
 
-template <int BITS>
+template <int BITS, bool SB_TMA>
 __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__ CUtensorMap map_x,
                                                         const __grid_constant__ CUtensorMap map_codes,
+                                                        const __grid_constant__ CUtensorMap map_scales,
+                                                        const __grid_constant__ CUtensorMap map_biases,
                                                         const PArgs a) {
-    using F = PF<BITS>;
+    using F = PF<BITS, SB_TMA>;
     constexpr int SX = F::X_STAGES, SW = F::W_STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -168,7 +173,11 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
         // ----------------------------------------------------------- weight producer
         if (lane == 0) {
             prefetch_tensormap(&map_codes);
-            const uint32_t wbytes = F::CODE_B;
+            if (SB_TMA) {
+                prefetch_tensormap(&map_scales);
+                if (a.has_bias) prefetch_tensormap(&map_biases);
+            }
+            const uint32_t wbytes = F::CODE_B + (SB_TMA ? 2048u * (a.has_bias ? 2u : 1u) : 0u);
             int gs = 0;
             for (; gs < total && !*abort_flag; ++gs) {
                 const int slot = gs % SW, tile = pair + (gs / ksteps) * npairs, ks = gs % ksteps;
@@ -177,6 +186,11 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
                 uint8_t* st = wring + slot * F::W_STAGE;
                 mbar_arrive_expect_tx(&w_full[slot], wbytes);
                 tma_load_2d(st, &map_codes, &w_full[slot], k0 * BITS / 32, n0);
+                if (SB_TMA) {
+                    tma_load_2d(st + F::CODE_B, &map_scales, &w_full[slot], (k0 / 512) * 8, n0);
+                    if (a.has_bias)
+                        tma_load_2d(st + F::CODE_B + 2048, &map_biases, &w_full[slot], (k0 / 512) * 8, n0);
+                }
             }
             for (int i = 1; i <= (gs < SW ? gs : SW); ++i)
                 mbar_wait(&w_full[(gs - i) % SW], ((gs - i) / SW) & 1, a.status);
@@ -228,7 +242,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
         auto sb_load = [&](int g, uint32_t& sv, uint32_t& bv) {
             sv = 0u;
             bv = 0u;
-            if (g >= total) return;
+            if (SB_TMA || g >= total) return;
             const int tile = pair + (g / ksteps) * npairs;
             const int n = (tile % a.nR) * (2 * P_ROWS) + rank * P_ROWS + row;
             if (n >= a.N) return;
@@ -240,12 +254,18 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
         sb_load(set, s_next, b_next);
         for (int gs = set; gs < total; gs += 2) {
             const int slot = gs % SW, as = gs % P_ASLOTS;
-            const uint32_t s01 = s_next, b01 = b_next;
+            uint32_t s01 = s_next, b01 = b_next;
             sb_load(gs + 2, s_next, b_next);
             if (!p_wait_warp<false>(&w_full[slot], (gs / SW) & 1, ab)) break;
             // Dequantize into registers first: the TMEM slot is waited for only afterwards,
             // so the arithmetic overlaps the MMAs that still read the slot.
             const uint8_t* st = wring + slot * F::W_STAGE;
+            if (SB_TMA) {
+                const uint32_t* sb = reinterpret_cast<const uint32_t*>(st + F::CODE_B);
+                const int ks = gs % ksteps;
+                s01 = sb[row * 4 + (ks & 3)];
+                b01 = a.has_bias ? sb[512 + row * 4 + (ks & 3)] : 0u;
+            }
             uint32_t av0[32], av1[32];
             dequant_group<BITS>(st, row, 0, s01 & 0xFFFFu, b01 & 0xFFFFu, av0);
             dequant_group<BITS>(st, row, 1, s01 >> 16, b01 >> 16, av1);
@@ -301,7 +321,7 @@ struct PairLaunch {
     int max_pairs = 0;
 };
 
-template <int BITS>
+template <int BITS, bool SB_TMA>
 q38_status pair_config(q38_ctx* ctx, int smem, PairLaunch* out) {
     static std::mutex mu;
     static PairLaunch cached[64];
@@ -311,7 +331,7 @@ q38_status pair_config(q38_ctx* ctx, int smem, PairLaunch* out) {
         *out = cached[dev];
         return Q38_OK;
     }
-    auto kmain = qgemm_tc<BITS>;
+    auto kmain = qgemm_tc<BITS, SB_TMA>;
     if (cudaFuncSetAttribute(kmain, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
         return check_launch(ctx, "cudaFuncSetAttribute");
     cudaLaunchConfig_t cfg = {};
@@ -337,24 +357,28 @@ q38_status pair_config(q38_ctx* ctx, int smem, PairLaunch* out) {
     return Q38_OK;
 }
 
-template <int BITS>
+template <int BITS, bool SB_TMA>
 q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, const void* s, const void* b,
                   int N, void* y) {
-    using F = PF<BITS>;
+    using F = PF<BITS, SB_TMA>;
     q38_status st = ensure_workspace(ctx, static_cast<size_t>(M) * K * 2);
     if (st != Q38_OK) return st;
     __nv_bfloat16* xp = static_cast<__nv_bfloat16*>(ctx->workspace);
 
-    CUtensorMap mx, mc;
+    CUtensorMap mx, mc, ms = {}, mb = {};
     const CUtensorMapSwizzle cswz = code_swizzle<BITS>();
     if (!make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xp, K, M, 64, P_HTOK, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_map_2d(&mc, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w, static_cast<uint64_t>(K) * BITS / 32, N,
-                     F::CODE_W, P_ROWS, cswz))
+                     F::CODE_W, P_ROWS, cswz) ||
+        (SB_TMA && (!make_map_2d(&ms, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s, K / 64, N, 8, P_ROWS,
+                                 CU_TENSOR_MAP_SWIZZLE_NONE) ||
+                    !make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b ? b : s, K / 64, N, 8, P_ROWS,
+                                 CU_TENSOR_MAP_SWIZZLE_NONE))))
         return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: tensor map encoding failed");
 
     static_assert(F::W_STAGES >= 4 && F::SMEM <= 227 * 1024, "prefill stages do not fit");
     PairLaunch pl;
-    if ((st = pair_config<BITS>(ctx, F::SMEM, &pl)) != Q38_OK) return st;
+    if ((st = pair_config<BITS, SB_TMA>(ctx, F::SMEM, &pl)) != Q38_OK) return st;
 
     const int nR = (N + 2 * P_ROWS - 1) / (2 * P_ROWS), nT = (M + P_TOK - 1) / P_TOK;
     const int ntiles = nR * nT;
@@ -396,7 +420,7 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
     cfg.stream = ctx->stream;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    if (cudaLaunchKernelEx(&cfg, qgemm_tc<BITS>, mx, mc, args) != cudaSuccess)
+    if (cudaLaunchKernelEx(&cfg, qgemm_tc<BITS, SB_TMA>, mx, mc, ms, mb, args) != cudaSuccess)
         return check_launch(ctx, "qgemm_tc");
     return check_launch(ctx, "qgemm_tc");
 }
@@ -415,10 +439,11 @@ bool qgemm_tc_supported(int64_t M, int64_t K, int group, int bits, q38_dtype xd,
 q38_status qgemm_tc_run(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w, const void* s,
                         const void* b, int64_t N, int bits, void* y) {
     const int m = static_cast<int>(M), k = static_cast<int>(K), n = static_cast<int>(N);
+    const bool tma_scales = k % 512 == 0;
     switch (bits) {
-        case 2: return launch<2>(ctx, x, m, k, w, s, b, n, y);
-        case 3: return launch<3>(ctx, x, m, k, w, s, b, n, y);
-        default: return launch<4>(ctx, x, m, k, w, s, b, n, y);
+        case 2: return tma_scales ? launch<2, true>(ctx, x, m, k, w, s, b, n, y) : launch<2, false>(ctx, x, m, k, w, s, b, n, y);
+        case 3: return tma_scales ? launch<3, true>(ctx, x, m, k, w, s, b, n, y) : launch<3, false>(ctx, x, m, k, w, s, b, n, y);
+        default: return tma_scales ? launch<4, true>(ctx, x, m, k, w, s, b, n, y) : launch<4, false>(ctx, x, m, k, w, s, b, n, y);
     }
 }
 
