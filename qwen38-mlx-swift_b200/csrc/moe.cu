@@ -121,8 +121,7 @@ __global__ void __launch_bounds__(128, 1) router_logits_tc(const __grid_constant
     griddep_wait();  // inputs come from the previous kernel on the stream
     griddep_launch_dependents();
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* smem = smem_align1024(smem_raw);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + R_STAGES;
     uint64_t* done = empty + R_STAGES;

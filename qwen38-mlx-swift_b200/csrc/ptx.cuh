@@ -15,6 +15,13 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// Dynamic shared memory rounded up to a 1024-byte boundary (the 128-byte swizzle atoms
+// need it).  Done by pointer arithmetic on the shared array itself, so the compiler still
+// knows the result is a shared-memory address and emits shared loads through it.
+__device__ __forceinline__ uint8_t* smem_align1024(uint8_t* raw) {
+    return raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u);
+}
+
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
                  : "memory");

@@ -75,8 +75,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_grouped(
     using F = GF<BITS, XR>;
     constexpr int SX = F::X_STAGES, SW = F::W_STAGES;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* smem = smem_align1024(smem_raw);
     uint64_t* x_full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* x_empty = x_full + 16;
     uint64_t* w_full = x_empty + 16;

@@ -94,8 +94,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
     using F = PF<BITS, SB_TMA>;
     constexpr int SX = F::X_STAGES, SW = F::W_STAGES;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* smem = smem_align1024(smem_raw);
     uint64_t* x_full = reinterpret_cast<uint64_t*>(smem);  // both CTAs' activation halves landed (leader)
     uint64_t* x_empty = x_full + 8;                        // pair MMAs reading the slot done (local)
     uint64_t* w_full = x_empty + 8;                        // codes + scales landed (local)

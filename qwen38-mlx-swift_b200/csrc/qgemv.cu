@@ -219,8 +219,7 @@ __global__ void __launch_bounds__(THREADS, NT == 1 ? 3 : 2) qgemv_main(const __g
                                                       const MainArgs a) {
     using F = Fmt<BITS>;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* smem = smem_align1024(smem_raw);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + a.stages;
     uint8_t* stage0 = smem + 1024;
