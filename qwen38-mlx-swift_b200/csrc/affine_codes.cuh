@@ -16,6 +16,11 @@ using namespace dev;
 
 constexpr uint32_t MAGIC = 0x43004300u;  // bf16 128.0 in both halves
 
+// The same constant read from constant memory.  The compiler cannot turn it into an
+// immediate, so it stays in a register and `(code & mask) | magic` compiles to one
+// three-input logic instruction; with two immediates it compiles to two.
+__constant__ uint32_t c_magic = MAGIC;
+
 // ---------------------------------------------------------------------------------
 // Pair tables: for bf16x2 operand q of a thread's 16 codes (per row and group), the
 // code index feeding its low and high half and the power-of-two weight the code has
@@ -45,6 +50,7 @@ __host__ __device__ constexpr float pair_mult(int q, int hi) {
 // w[] holds the window: bits 2 -> 1 word, 3 -> 2 words (48 valid bits), 4 -> 2, 8 -> 4.
 template <int BITS>
 __device__ __forceinline__ void extract(const uint32_t* w, uint32_t* a) {
+    const uint32_t MAGIC = c_magic;
     if constexpr (BITS == 2) {
         const uint32_t v = w[0], v6 = v >> 6, v12 = v >> 12;
         a[0] = (v & 0x00030003u) | MAGIC;
