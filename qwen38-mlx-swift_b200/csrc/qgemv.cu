@@ -9,26 +9,29 @@
 //    subunits in (64-row tile, k-chunk, 16-row subtile) order, so every CTA streams the
 //    same number of bytes (+-1 subunit) whatever N and K are.
 //  * One producer warp streams each (tile, chunk) stage with TMA: the codes of the
-//    active 16-row subtiles (swizzled boxes), the 64x8 bf16 scales and biases, and the
-//    chunk's pre-arranged activation fragments.  Four consumer warps each own one
-//    16-row subtile.  Stages cycle through an mbarrier ring.
+//    active 16-row subtiles (swizzled boxes) and the 64x8 bf16 scales and biases.  One
+//    activation warp writes the chunk's activation fragments into the same stage, built
+//    from x in global memory.  Four consumer warps each own one 16-row subtile.  Stages
+//    cycle through an mbarrier ring.
 //  * Codes are turned into bf16 operands without integer->float conversion: a code
-//    masked into the mantissa of 0x4300 (bf16 128.0) reads as 128 + 2^p*q.  A tiny
-//    prologue kernel permutes and scales the activations (x * 2^-p) into the MMA
-//    fragment order that matches the extraction, and precomputes per-group sums.
-//    One m16n8k16 bf16 MMA then dots 16 codes x 8 tokens; per group
-//    D = sum(q*x) + 128*sum(x'), and y += scale*D.  The -128*scale*sum(x') and
-//    bias*sum(x) terms of all 8 groups of a chunk are folded into two extra MMA
+//    masked into the mantissa of 0x4300 (bf16 128.0) reads as 128 + 2^p*q.  The
+//    activation fragments hold x permuted and scaled (x * 2^-p) into the order that
+//    matches the extraction, plus per-group sums.  One m16n8k16 bf16 MMA dots 16 codes
+//    of 16 rows with 8 columns; per group D = sum(q*x) + 128*sum(x'), and y += scale*D.
+//  * The 8 columns are (group slot, token) pairs, so a product serves 8/MP groups of
+//    MP tokens at once and each accumulator set spans several groups: the scales are
+//    applied once per chunk, not after every group's MMA chain.  The -128*scale*sum(x')
+//    and bias*sum(x) terms of all 8 groups of a chunk are folded into two extra MMA
 //    steps whose operands are the scales/biases and hi/lo bf16 splits of the sums.
 //  * Consumers do no address arithmetic in the inner loop: swizzled code offsets are
-//    precomputed per thread, fragments are token-major so their offsets are constants,
-//    and the 8 groups of a stage are unrolled so their MMA chains overlap.
+//    precomputed per thread and the fragment offsets are constants.
 //  * Every warp adds its subtile partial sums into an fp32 workspace with fire-and-forget
 //    reductions (no fences or counters in the main kernel); a small epilogue kernel
 //    converts the sums to y and zeroes them again, so no per-call clearing is needed.
 //  * The main kernel is launched with programmatic dependent launch: its producer
-//    streams the first stages of weights while the prologue kernel is still running.
+//    streams the first stages of weights while the previous kernel is still running.
 #include <mutex>
+#include <type_traits>
 
 #include "affine_codes.cuh"
 
@@ -40,7 +43,7 @@ using namespace dev;
 constexpr int KC = 512;        // k per chunk
 constexpr int GROUPS = 8;      // groups of 64 per chunk
 constexpr int NCW = 4;         // consumer warps (one 16-row subtile each)
-constexpr int THREADS = (NCW + 1) * 32;
+constexpr int THREADS = (NCW + 2) * 32;  // + weight producer + activation warp
 
 template <int BITS>
 struct Fmt {
@@ -104,47 +107,45 @@ __device__ __forceinline__ void load_window(const uint8_t* p, uint32_t offA, uin
 
 
 // ---------------------------------------------------------------------------------
-// Prologue: activation fragments + per-group sums, one CTA per 512-k chunk.
-// Layout per chunk, token-major with a per-token stride of XF_PER_M bytes:
-//   [m][group 8][half SPG/2][t 4][16 B]  then  [sigma 2][t 4][8 B] (bias-step operands).
-// A 64-byte tail per token shifts consecutive tokens by 16 banks.
+// Activation fragments of one 512-k chunk, written by one warp.
+// Layout per token m (stride XF_PER_M bytes):
+//   [group 8][k-step pair SPG/2][t 4][16 B]  then  [t 4][16 B]
+// The first part holds x' (x permuted into extraction order and scaled by 2^-p) as
+// bf16x2 MMA B operands.  The second holds, for lane quarter t, the B operands of the
+// offset-and-bias steps: groups 2t and 2t+1 of -128 * sum(x') and of sum(x), each split
+// into a bf16 high part (words 0, 1) and the bf16 of the remainder (words 2, 3).
 // ---------------------------------------------------------------------------------
 template <int BITS>
-__global__ void __launch_bounds__(256) qgemv_prep(const __nv_bfloat16* __restrict__ x, int M,
-                                                  int K, uint8_t* __restrict__ xfrag) {
+__device__ __forceinline__ void build_fragments(const uint8_t* xc, int M, uint8_t* base, float (*s_xs)[16],
+                                                float (*s_xp)[16], int lane) {
     using F = Fmt<BITS>;
-    // Let the main kernel start streaming weights now; x is produced by the previous
-    // kernel on the stream, and the fragment buffer is read by the previous product:
-    // both are touched only after that kernel has completed.
-    griddep_launch_dependents();
-    griddep_wait();
-    __shared__ float s_xs[GROUPS][16], s_xp[GROUPS][16];
-    const int c = blockIdx.x;
-    uint8_t* base = xfrag + static_cast<size_t>(c) * M * F::XF_PER_M;
+    constexpr uint32_t ONE2 = 0x3F803F80u;  // bf16x2 (1, 1)
+    // 32 * M items: every iteration has all 32 lanes, and lanes 4i..4i+3 share (group, token)
     const int items = GROUPS * M * 4;
-    for (int i = threadIdx.x; i < items; i += blockDim.x) {
+    for (int i = lane; i < items; i += 32) {
         const int t = i & 3, gm = i >> 2, m = gm % M, gi = gm / M;
-        const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(m) * K +
-                                                          c * KC + gi * 64 + t * 16);
+        const uint4* src = reinterpret_cast<const uint4*>(xc + m * (KC * 2) + (gi * 64 + t * 16) * 2);
         const uint4 u0 = src[0], u1 = src[1];
         const uint32_t raw[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-        float xv[16];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            xv[2 * j] = bf16_bits_to_f32(raw[j] & 0xFFFFu);
-            xv[2 * j + 1] = bf16_bits_to_f32(raw[j] >> 16);
-        }
         float xs = 0.f, xp = 0.f;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) xs += xv[j];
+        for (int j = 0; j < 8; ++j) xs = fma2_bf16_f32(raw[j], ONE2, xs);
         uint32_t* dst = reinterpret_cast<uint32_t*>(base + m * F::XF_PER_M + gi * (F::SPG / 2) * 64 + t * 16);
 #pragma unroll
         for (int q = 0; q < F::NP; ++q) {
-            const float lo = xv[pair_code<BITS>(q, 0)] * pair_mult<BITS>(q, 0);
-            const float hi = xv[pair_code<BITS>(q, 1)] * pair_mult<BITS>(q, 1);
-            xp += lo + hi;
-            dst[(q / 4) * 16 + (q % 4)] = pack_bf16x2(lo, hi);
+            // pair (code a, code b) = (element a, element b) of the 16, as one bf16x2
+            const int ea = pair_code<BITS>(q, 0), eb = pair_code<BITS>(q, 1);
+            const uint32_t lo = (ea & 1) ? (raw[ea >> 1] >> 16) : (raw[ea >> 1] & 0xFFFFu);
+            const uint32_t hi = (eb & 1) ? (raw[eb >> 1] & 0xFFFF0000u) : (raw[eb >> 1] << 16);
+            uint32_t pr = lo | hi;
+            const float ma = pair_mult<BITS>(q, 0), mb = pair_mult<BITS>(q, 1);
+            if (ma != 1.0f || mb != 1.0f)
+                pr = mul_bf16x2(pr, (static_cast<uint32_t>(f32_to_bf16_bits(ma))) |
+                                        (static_cast<uint32_t>(f32_to_bf16_bits(mb)) << 16));
+            if (BITS != 4) xp = fma2_bf16_f32(pr, ONE2, xp);
+            dst[(q / 4) * 16 + (q % 4)] = pr;
         }
+        if (BITS == 4) xp = xs;  // every factor is 1
         xs += __shfl_xor_sync(0xffffffffu, xs, 1);
         xs += __shfl_xor_sync(0xffffffffu, xs, 2);
         xp += __shfl_xor_sync(0xffffffffu, xp, 1);
@@ -154,51 +155,79 @@ __global__ void __launch_bounds__(256) qgemv_prep(const __nv_bfloat16* __restric
             s_xp[gi][m] = xp;
         }
     }
-    __syncthreads();
-    for (int i = threadIdx.x; i < 8 * M; i += blockDim.x) {
-        const int t = i & 3, mm = i >> 2, m = mm % M, sigma = mm / M;
-        uint32_t out[2];
+    __syncwarp();
+    // offset-and-bias operands of quarter t: groups 2t, 2t+1
+    for (int i = lane; i < 4 * M; i += 32) {
+        const int t = i & 3, m = i >> 2;
+        float v[4] = {-128.0f * s_xp[2 * t][m], -128.0f * s_xp[2 * t + 1][m], s_xs[2 * t][m], s_xs[2 * t + 1][m]};
+        uint32_t hb[4], lb[4];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int gi = 4 * sigma + 2 * h + (t >> 1);
-            const float v = (t & 1) ? s_xs[gi][m] : s_xp[gi][m];
-            const float vhi = bf16_bits_to_f32(f32_to_bf16_bits(v));
-            const float vlo = v - vhi;
-            const float f = (t & 1) ? 1.0f : -128.0f;
-            out[h] = pack_bf16x2(vhi * f, vlo * f);
+        for (int j = 0; j < 4; ++j) {
+            hb[j] = f32_to_bf16_bits(v[j]);
+            lb[j] = f32_to_bf16_bits(v[j] - bf16_bits_to_f32(hb[j]));
         }
-        uint32_t* d = reinterpret_cast<uint32_t*>(base + m * F::XF_PER_M + F::XF_FRAG + sigma * 32 + t * 8);
-        d[0] = out[0];
-        d[1] = out[1];
+        *reinterpret_cast<uint4*>(base + m * F::XF_PER_M + F::XF_FRAG + t * 16) =
+            make_uint4(hb[0] | (hb[1] << 16), hb[2] | (hb[3] << 16), lb[0] | (lb[1] << 16), lb[2] | (lb[3] << 16));
     }
+    __syncwarp();
 }
 
 // ---------------------------------------------------------------------------------
 // Main kernel.
 // ---------------------------------------------------------------------------------
 struct MainArgs {
-    const uint8_t* xfrag;
+    const __nv_bfloat16* x;
     __nv_bfloat16* y;
     float* ws;
     uint32_t* status;
-    int M, N, C, tiles, stages, stage_bytes, has_bias;
+    int M, N, K, C, tiles, stages, stage_bytes, has_bias;
 };
 
-// Adds a warp's partial sums of one 16-row subtile into the fp32 workspace.  The
-// reductions are fire-and-forget (no fence, no counter): the epilogue kernel, which
-// runs after this grid has completed, converts the sums to y and zeroes them again.
-template <int NT>
-__device__ __forceinline__ void flush_subtile(const float (&acc)[NT][4], int tile, int warp,
-                                              const MainArgs& a, int lane) {
+// Accumulator columns.  An m16n8k16 product has 8 columns; with MP (1, 2, 4 or 8) token
+// columns per group, one product serves 8/MP groups at once: column n = slot * MP + token,
+// and the B operand of group g is non-zero only in the columns of its slot (g mod 8/MP).
+// The MMAs of a chunk therefore accumulate 8/MP groups into one register set, and the
+// per-group scales are applied once per chunk instead of once per group.
+
+// Adds a warp's partial sums of one 16-row subtile into the fp32 workspace after summing
+// the columns that belong to the same token.  The reductions are fire-and-forget (no
+// fence, no counter): the epilogue kernel, which runs after this grid has completed,
+// converts the sums to y and zeroes them again.
+template <int MP, int TB>
+__device__ __forceinline__ void flush_subtile(float (&acc)[TB][4], int tile, int warp, const MainArgs& a,
+                                              int lane) {
     const int g = lane >> 2, t = lane & 3;
     const int r0 = tile * 64 + warp * 16 + g;
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    for (int tb = 0; tb < TB; ++tb) {
+        if (MP == 1) {  // every column is token 0
+            float v0 = acc[tb][0] + acc[tb][1], v2 = acc[tb][2] + acc[tb][3];
+            v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
+            v2 += __shfl_xor_sync(0xffffffffu, v2, 1);
+            v0 += __shfl_xor_sync(0xffffffffu, v0, 2);
+            v2 += __shfl_xor_sync(0xffffffffu, v2, 2);
+            if (t == 0) {
+                if (r0 < a.N) atomicAdd(a.ws + r0, v0);
+                if (r0 + 8 < a.N) atomicAdd(a.ws + r0 + 8, v2);
+            }
+            continue;
+        }
+        float v[4] = {acc[tb][0], acc[tb][1], acc[tb][2], acc[tb][3]};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            const int r = r0 + ((e >> 1) << 3), m = nt * 8 + 2 * t + (e & 1);
-            if (r < a.N && m < a.M) atomicAdd(a.ws + static_cast<size_t>(m) * a.N + r, acc[nt][e]);
+            if (MP <= 2) v[e] += __shfl_xor_sync(0xffffffffu, v[e], 1);
+            if (MP <= 4) v[e] += __shfl_xor_sync(0xffffffffu, v[e], 2);
         }
+        const int writers = MP <= 2 ? 1 : MP / 2;
+        if (t < writers) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int r = r0 + ((e >> 1) << 3);
+                const int m = tb * 8 + (2 * t + (e & 1)) % MP;
+                if (r < a.N && m < a.M) atomicAdd(a.ws + static_cast<size_t>(m) * a.N + r, v[e]);
+            }
+        }
+    }
 }
 
 // y = bf16(partial sums); the sums are returned to zero for the next product.
@@ -212,60 +241,90 @@ __global__ void __launch_bounds__(256) qgemv_epilogue(float* __restrict__ ws, __
     }
 }
 
-template <int BITS, int NT>
-__global__ void __launch_bounds__(THREADS, NT == 1 ? 3 : 2) qgemv_main(const __grid_constant__ CUtensorMap map_codes,
-                                                      const __grid_constant__ CUtensorMap map_scales,
-                                                      const __grid_constant__ CUtensorMap map_biases,
-                                                      const MainArgs a) {
+// Shared memory: [0, 1 KiB) barriers, [1, 3 KiB) zeros (B operand of columns that do not
+// belong to a group), [3 KiB, ...) the stage ring, then two activation-fragment slots and
+// one staging copy of a chunk of x.
+constexpr int ZERO_OFF = 1024, ZERO_BYTES = 2048, RING_OFF = 3072;
+constexpr int MAX_DYN_SMEM = 226 * 1024;  // 227 KiB per CTA less the static per-group sums
+
+template <int BITS, int MP, int TB>
+__global__ void __launch_bounds__(THREADS, TB == 1 ? 3 : 2) qgemv_main(const __grid_constant__ CUtensorMap map_codes,
+                                                                      const __grid_constant__ CUtensorMap map_scales,
+                                                                      const __grid_constant__ CUtensorMap map_biases,
+                                                                      const MainArgs a) {
     using F = Fmt<BITS>;
+    constexpr int GPER = 8 / MP;                 // groups sharing one accumulator set
+    constexpr int UG = BITS == 8 ? 1 : 2;        // groups extracted together
+    constexpr int FLUSH = TB == 1 ? GROUPS : UG; // groups between scale applications
+    constexpr int LIVE = TB == 1 ? MP : UG;      // accumulator sets alive between applications
+    constexpr int SPLIT = (TB == 1 && MP <= 2 && UG == 2) ? 2 : 1;  // shorter MMA chains
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_align1024(smem_raw);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + a.stages;
-    uint8_t* stage0 = smem + 1024;
+    uint64_t* xfull = empty + a.stages;
+    uint64_t* xempty = xfull + 2;
+    const uint8_t* zeros = smem + ZERO_OFF;
+    uint8_t* stage0 = smem + RING_OFF;
+    uint8_t* xslots = stage0 + static_cast<size_t>(a.stages) * a.stage_bytes;
+    const int xslot_bytes = a.M * F::XF_PER_M;
+    uint8_t* xstage = xslots + 2 * xslot_bytes;
+    __shared__ float s_xs[GROUPS][16], s_xp[GROUPS][16];
 
-    // subunit range of this CTA (host guarantees tiles * C * 4 < 2^31)
-    const int total_sub = a.tiles * a.C * 4;
+    // Subunit range of this CTA in (chunk, tile, subtile) order: a CTA covers one or two
+    // chunks of k, so its activation fragments are built once per chunk.
+    const int total_sub = a.tiles * a.C * 4;  // host guarantees < 2^31
     const int s0 = static_cast<int>(static_cast<long long>(total_sub) * blockIdx.x / gridDim.x);
     const int s1 = static_cast<int>(static_cast<long long>(total_sub) * (blockIdx.x + 1) / gridDim.x);
     if (s1 <= s0) return;
     const int st_first = s0 >> 2, st_last = (s1 - 1) >> 2;
     const int nst = st_last - st_first + 1;
     const int lo_first = s0 - 4 * st_first, hi_last = s1 - 4 * st_last;
-    const int xf_bytes = a.M * F::XF_PER_M;
+    const int chunk_first = st_first / a.tiles;
+    const int nch = st_last / a.tiles - chunk_first + 1;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < ZERO_BYTES / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(smem + ZERO_OFF)[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (!a.has_bias)  // the bias operands of the offset-and-bias steps are then zeros
+        for (int i = threadIdx.x; i < a.stages * 64; i += blockDim.x)
+            reinterpret_cast<uint4*>(stage0 + static_cast<size_t>(i >> 6) * a.stage_bytes + NCW * F::SUB_BYTES +
+                                     1024)[i & 63] = make_uint4(0u, 0u, 0u, 0u);
     if (threadIdx.x == 0) {
         for (int i = 0; i < a.stages; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], NCW);
         }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&xfull[i], 1);
+            mbar_init(&xempty[i], NCW);
+        }
         fence_mbar_init();
     }
     __syncthreads();
-    // The next product's prologue may start now: it waits for this grid before writing
-    // anything this grid reads.
+    // The next kernel on the stream may start now: it waits for this grid before reading
+    // or writing anything this grid touches.
     griddep_launch_dependents();
 
     if (warp == NCW) {
-        // ------------------------------------------------------------ producer
+        // ------------------------------------------------------------ weight producer
+        // Streams codes, scales and biases; they are read-only inputs, so the ring fills
+        // while the previous kernel on the stream is still finishing.
         if (lane == 0) {
             prefetch_tensormap(&map_codes);
             prefetch_tensormap(&map_scales);
             if (a.has_bias) prefetch_tensormap(&map_biases);
-            bool waited = false;
-            int issued_xf = 0, xf_chunk = st_first % a.C;  // fragments issued so far, their next chunk
-            int tile = st_first / a.C, chunk = st_first % a.C;
+            int chunk = st_first / a.tiles, tile = st_first % a.tiles;
+            int slot = 0;
+            uint32_t ph = 0;
             for (int i = 0; i < nst; ++i) {
-                const int slot = i % a.stages;
-                const uint32_t ph = (i / a.stages) & 1;
                 if (i >= a.stages && !mbar_wait(&empty[slot], ph ^ 1, a.status)) return;
                 const int sub_lo = i == 0 ? lo_first : 0;
                 const int sub_hi = i == nst - 1 ? hi_last : 4;
                 uint8_t* sbase = stage0 + static_cast<size_t>(slot) * a.stage_bytes;
                 int nact = 0;
                 for (int s = sub_lo; s < sub_hi; ++s) nact += (tile * 64 + 16 * s < a.N);
-                const uint32_t bytes = nact * F::SUB_BYTES + 1024 + (a.has_bias ? 1024 : 0) + xf_bytes;
+                const uint32_t bytes = nact * F::SUB_BYTES + 1024 + (a.has_bias ? 1024 : 0);
                 mbar_arrive_expect_tx(&full[slot], bytes);
                 for (int s = sub_lo; s < sub_hi; ++s) {
                     if (tile * 64 + 16 * s >= a.N) continue;
@@ -277,32 +336,44 @@ __global__ void __launch_bounds__(THREADS, NT == 1 ? 3 : 2) qgemv_main(const __g
                 uint8_t* sc = sbase + NCW * F::SUB_BYTES;
                 tma_load_2d(sc, &map_scales, &full[slot], chunk * GROUPS, tile * 64);
                 if (a.has_bias) tma_load_2d(sc + 1024, &map_biases, &full[slot], chunk * GROUPS, tile * 64);
-                // Activation fragments come from the prologue kernel: wait for it only
-                // once the ring is full of weight loads.
-                if (!waited && (i == a.stages - 1 || i == nst - 1)) {
-                    griddep_wait();
-                    waited = true;
+                if (++slot == a.stages) {
+                    slot = 0;
+                    ph ^= 1;
                 }
-                if (waited) {
-                    for (; issued_xf <= i; ++issued_xf) {
-                        const int sl = issued_xf % a.stages;
-                        uint8_t* dst = stage0 + static_cast<size_t>(sl) * a.stage_bytes + NCW * F::SUB_BYTES + 2048;
-                        bulk_load(dst, a.xfrag + static_cast<size_t>(xf_chunk) * xf_bytes, xf_bytes, &full[sl]);
-                        if (++xf_chunk == a.C) xf_chunk = 0;
-                    }
-                }
-                if (++chunk == a.C) {
-                    chunk = 0;
-                    ++tile;
+                if (++tile == a.tiles) {
+                    tile = 0;
+                    ++chunk;
                 }
             }
         }
         return;
     }
 
+    if (warp == NCW + 1) {
+        // ------------------------------------------------------------ activation warp
+        // x is written by the previous kernel on the stream: wait for it to complete.
+        griddep_wait();
+        for (int ci = 0; ci < nch; ++ci) {
+            const int c = chunk_first + ci;
+            // all of the chunk's copies in flight at once
+            for (int p = lane; p < a.M * (KC / 8); p += 32) {
+                const int m = p / (KC / 8), q = p % (KC / 8);
+                cp_async16(xstage + m * (KC * 2) + q * 16, a.x + static_cast<size_t>(m) * a.K + c * KC + q * 8);
+            }
+            cp_async_commit();
+            const bool ok = ci < 2 || mbar_wait(&xempty[ci & 1], ((ci >> 1) & 1) ^ 1, a.status);
+            cp_async_wait<0>();
+            __syncwarp();
+            if (!ok) return;
+            build_fragments<BITS>(xstage, a.M, xslots + (ci & 1) * xslot_bytes, s_xs, s_xp, lane);
+            if (lane == 0) mbar_arrive(&xfull[ci & 1]);
+        }
+        return;
+    }
+
     // -------------------------------------------------------------- consumers
-    // Partial sums, counters and y may still be in use by the previous product on the
-    // stream until the prologue kernel (which waits for it) has completed.
+    // The partial sums may still be in use by the previous product's epilogue until it
+    // has completed.
     griddep_wait();
     const int g = lane >> 2, t = lane & 3;
     const bool odd = (t & 1) != 0;
@@ -316,39 +387,45 @@ __global__ void __launch_bounds__(THREADS, NT == 1 ? 3 : 2) qgemv_main(const __g
         offB[gi] = code_off<F::SW>(g, w1);
     }
     constexpr uint32_t ROW8 = 8 * F::SW;
-    // activation fragments: token m = nt*8 + g, quarter t
-    uint32_t xoff[NT];
-    bool xval[NT];
+    // B operand of column g (this lane's column): token and group slot
+    const int ml = g % MP, gsl = g / MP;
+    int tok[TB];
+    bool tval[TB];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-        const int m = nt * 8 + g;
-        xval[nt] = m < a.M;
-        xoff[nt] = (xval[nt] ? m : 0) * F::XF_PER_M + t * 16;
+    for (int tb = 0; tb < TB; ++tb) {
+        tok[tb] = TB == 1 ? ml : tb * 8 + g;
+        tval[tb] = tok[tb] < a.M;
     }
     const int srow0 = warp * 16 + g;  // scale row of row g (row g+8 is 64 halfwords further)
-    const bool use_bias_operand = !odd || a.has_bias;
-    const int ga0 = t >> 1;           // bias step: group offset of operand pair 0
 
-    float acc[NT][4];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
-    int cur_tile = -1, nchunks = 0;
-    int tile = st_first / a.C, chunk = st_first % a.C;
+    int cur_ci = -1;
+    const uint8_t* xf = xslots;
+    // per group: where this lane's B operand comes from (its fragments, or zeros)
+    const uint8_t* pg[TB == 1 ? GROUPS : TB];
+    int chunk = st_first / a.tiles, tile = st_first % a.tiles;
+    int slot = 0;
+    uint32_t ph = 0;
     for (int i = 0; i < nst; ++i) {
-        const int slot = i % a.stages;
-        const uint32_t ph = (i / a.stages) & 1;
         const int sub_lo = i == 0 ? lo_first : 0;
         const int sub_hi = i == nst - 1 ? hi_last : 4;
-        if (tile != cur_tile) {
-            if (nchunks > 0) flush_subtile<NT>(acc, cur_tile, warp, a, lane);
+        const int ci = chunk - chunk_first;
+        if (ci != cur_ci) {
+            // the previous chunk's fragments are no longer needed; wait for this chunk's
+            if (cur_ci >= 0) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&xempty[cur_ci & 1]);
+            }
+            if (!mbar_wait(&xfull[ci & 1], (ci >> 1) & 1, a.status)) return;
+            cur_ci = ci;
+            xf = xslots + (ci & 1) * xslot_bytes;
+            if (TB == 1) {
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
+                for (int gi = 0; gi < (TB == 1 ? GROUPS : TB); ++gi)
+                    pg[gi] = (tval[0] && gi % GPER == gsl) ? xf + tok[0] * F::XF_PER_M + t * 16 : zeros;
+            } else {
 #pragma unroll
-                for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
-            cur_tile = tile;
-            nchunks = 0;
+                for (int tb = 0; tb < TB; ++tb) pg[tb] = tval[tb] ? xf + tok[tb] * F::XF_PER_M + t * 16 : zeros;
+            }
         }
         const bool active = warp >= sub_lo && warp < sub_hi && tile * 64 + 16 * warp < a.N;
         if (!mbar_wait(&full[slot], ph, a.status)) return;
@@ -356,96 +433,115 @@ __global__ void __launch_bounds__(THREADS, NT == 1 ? 3 : 2) qgemv_main(const __g
             const uint8_t* sbase = stage0 + static_cast<size_t>(slot) * a.stage_bytes;
             const uint8_t* sub = sbase + warp * F::SUB_BYTES;
             const uint16_t* scl = reinterpret_cast<const uint16_t*>(sbase + NCW * F::SUB_BYTES) + srow0 * GROUPS;
-            const uint16_t* bia = scl + 512;
-            const uint8_t* xf = sbase + NCW * F::SUB_BYTES + 2048;
-            // two groups per iteration: independent MMA chains interleaved step by step
+            // scales of rows g and g+8 for groups 2t, 2t+1 (one word each), biases likewise
+            const uint32_t* sw = reinterpret_cast<const uint32_t*>(scl) + t;
+            const uint32_t s_g = sw[0], s_g8 = sw[32], b_g = sw[256], b_g8 = sw[256 + 32];
+            float acc[TB][4];
 #pragma unroll
-            for (int gp = 0; gp < GROUPS; gp += 2) {
-                uint32_t w[2][2][4], ar[2][2][F::NP], xb[2][NT][F::NP];
+            for (int tb = 0; tb < TB; ++tb)
 #pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const int gi = gp + u;
-                    load_window<BITS>(sub, offA[gi], offB[gi], odd, w[u][0]);
-                    load_window<BITS>(sub + ROW8, offA[gi], offB[gi], odd, w[u][1]);
+                for (int e = 0; e < 4; ++e) acc[tb][e] = 0.f;
+            float d[LIVE * SPLIT][TB][4];
 #pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
+            for (int gb = 0; gb < GROUPS; gb += UG) {
+                if (gb % FLUSH == 0) {
 #pragma unroll
-                        for (int h = 0; h < F::SPG / 2; ++h) {
-                            uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                            if (xval[nt])
-                                v = *reinterpret_cast<const uint4*>(xf + xoff[nt] + (gi * (F::SPG / 2) + h) * 64);
-                            xb[u][nt][4 * h + 0] = v.x;
-                            xb[u][nt][4 * h + 1] = v.y;
-                            xb[u][nt][4 * h + 2] = v.z;
-                            xb[u][nt][4 * h + 3] = v.w;
-                        }
+                    for (int s = 0; s < LIVE * SPLIT; ++s)
+#pragma unroll
+                        for (int tb = 0; tb < TB; ++tb)
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) d[s][tb][e] = 0.f;
+                }
+                uint32_t w[UG][2][4], ar[UG][2][F::NP];
+#pragma unroll
+                for (int u = 0; u < UG; ++u) {
+                    load_window<BITS>(sub, offA[gb + u], offB[gb + u], odd, w[u][0]);
+                    load_window<BITS>(sub + ROW8, offA[gb + u], offB[gb + u], odd, w[u][1]);
+                }
+                uint2 xb[UG][TB][F::SPG];
+#pragma unroll
+                for (int u = 0; u < UG; ++u) {
+                    const int gi = gb + u;
+#pragma unroll
+                    for (int tb = 0; tb < TB; ++tb) {
+                        const uint8_t* p = TB == 1 ? pg[gi % (TB == 1 ? GROUPS : TB)] : pg[tb % (TB == 1 ? GROUPS : TB)];
+#pragma unroll
+                        for (int j = 0; j < F::SPG; ++j)
+                            xb[u][tb][j] = *reinterpret_cast<const uint2*>(p + (gi * (F::SPG / 2) + j / 2) * 64 + (j & 1) * 8);
+                    }
                 }
 #pragma unroll
-                for (int u = 0; u < 2; ++u) {
+                for (int u = 0; u < UG; ++u) {
                     extract<BITS>(w[u][0], ar[u][0]);
                     extract<BITS>(w[u][1], ar[u][1]);
                 }
-                float d[2][NT][4];
-#pragma unroll
-                for (int u = 0; u < 2; ++u)
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) d[u][nt][e] = 0.f;
 #pragma unroll
                 for (int j = 0; j < F::SPG; ++j)
 #pragma unroll
-                    for (int u = 0; u < 2; ++u)
+                    for (int u = 0; u < UG; ++u) {
+                        const int gi = gb + u;
+                        const int s = ((gi / GPER) % LIVE) + (SPLIT > 1 ? LIVE * u : 0);
 #pragma unroll
-                        for (int nt = 0; nt < NT; ++nt)
-                            mma_bf16_16816(d[u][nt], ar[u][0][2 * j], ar[u][1][2 * j], ar[u][0][2 * j + 1],
-                                           ar[u][1][2 * j + 1], xb[u][nt][2 * j], xb[u][nt][2 * j + 1], d[u][nt]);
+                        for (int tb = 0; tb < TB; ++tb)
+                            mma_bf16_16816(d[s][tb], ar[u][0][2 * j], ar[u][1][2 * j], ar[u][0][2 * j + 1],
+                                           ar[u][1][2 * j + 1], xb[u][tb][j].x, xb[u][tb][j].y, d[s][tb]);
+                    }
+                if ((gb + UG) % FLUSH == 0) {
+                    // scale the finished sets: column 2t + c of set s belongs to group
+                    // (set index) * GPER + (2t + c) / MP
+                    const int gset0 = (gb + UG - FLUSH) / GPER;  // absolute index of live set 0
 #pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const float sc0 = bf16_bits_to_f32(scl[gp + u]);
-                    const float sc1 = bf16_bits_to_f32(scl[64 + gp + u]);
+                    for (int s = 0; s < LIVE; ++s) {
 #pragma unroll
-                    for (int nt = 0; nt < NT; ++nt) {
-                        acc[nt][0] = fmaf(sc0, d[u][nt][0], acc[nt][0]);
-                        acc[nt][1] = fmaf(sc0, d[u][nt][1], acc[nt][1]);
-                        acc[nt][2] = fmaf(sc1, d[u][nt][2], acc[nt][2]);
-                        acc[nt][3] = fmaf(sc1, d[u][nt][3], acc[nt][3]);
+                        for (int e = 0; e < 4; ++e) {
+                            float sc;
+                            if (MP == 1) {  // groups 2t, 2t+1: the words loaded above
+                                const uint32_t wv = (e >> 1) ? s_g8 : s_g;
+                                sc = __uint_as_float((e & 1) ? (wv & 0xFFFF0000u) : (wv << 16));
+                            } else {
+                                const int gi = (gset0 + s) * GPER + (2 * t) / MP;
+                                sc = bf16_bits_to_f32(scl[((e >> 1) << 6) + gi]);
+                            }
+#pragma unroll
+                            for (int tb = 0; tb < TB; ++tb) {
+                                float v = d[s][tb][e];
+                                if (SPLIT > 1) v += d[s + LIVE][tb][e];
+                                acc[tb][e] = fmaf(sc, v, acc[tb][e]);
+                            }
+                        }
                     }
                 }
             }
-            // bias and offset terms of the chunk's 8 groups: two MMA steps
-            const uint16_t* src = odd ? bia : scl;
+            // offset and bias terms of the chunk's 8 groups: two MMA steps (high and low
+            // parts of the sums) into column (slot 0, token), which the flush adds to the
+            // token's other columns.  A = (scales of groups 0-7, biases of groups 0-7).
 #pragma unroll
-            for (int sigma = 0; sigma < 2; ++sigma) {
-                const int ga = 4 * sigma + ga0, gb = ga + 2;
-                const uint32_t v0a = use_bias_operand ? src[ga] * 0x00010001u : 0u;
-                const uint32_t v1a = use_bias_operand ? src[64 + ga] * 0x00010001u : 0u;
-                const uint32_t v0b = use_bias_operand ? src[gb] * 0x00010001u : 0u;
-                const uint32_t v1b = use_bias_operand ? src[64 + gb] * 0x00010001u : 0u;
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    uint2 bb = make_uint2(0u, 0u);
-                    if (xval[nt])
-                        bb = *reinterpret_cast<const uint2*>(xf + xoff[nt] - t * 16 + F::XF_FRAG + sigma * 32 + t * 8);
-                    mma_bf16_16816(acc[nt], v0a, v1a, v0b, v1b, bb.x, bb.y, acc[nt]);
-                }
+            for (int tb = 0; tb < TB; ++tb) {
+                uint4 bb = make_uint4(0u, 0u, 0u, 0u);
+                const int mt = tb * 8 + g;  // token of column g in slot 0
+                if (mt < a.M && (TB > 1 || g < MP))
+                    bb = *reinterpret_cast<const uint4*>(xf + mt * F::XF_PER_M + F::XF_FRAG + t * 16);
+                mma_bf16_16816(acc[tb], s_g, s_g8, b_g, b_g8, bb.x, bb.y, acc[tb]);
+                mma_bf16_16816(acc[tb], s_g, s_g8, b_g, b_g8, bb.z, bb.w, acc[tb]);
             }
-            ++nchunks;
+            flush_subtile<MP, TB>(acc, tile, warp, a, lane);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
-        if (++chunk == a.C) {
-            chunk = 0;
-            ++tile;
+        if (++slot == a.stages) {
+            slot = 0;
+            ph ^= 1;
+        }
+        if (++tile == a.tiles) {
+            tile = 0;
+            ++chunk;
         }
     }
-    if (nchunks > 0) flush_subtile<NT>(acc, cur_tile, warp, a, lane);
 }
 
 // Launch geometry shared by the context path and the allocation-free path.
 struct Plan {
     int C, tiles, stage_bytes, stages, smem;
-    size_t xf_bytes;
 };
 
 template <int BITS>
@@ -454,20 +550,22 @@ bool make_plan(int M, int K, int N, Plan& p) {
     p.C = K / KC;
     p.tiles = (N + 63) / 64;
     if (static_cast<long long>(p.tiles) * p.C * 4 >= (1LL << 31)) return false;
-    p.xf_bytes = static_cast<size_t>(M) * F::XF_PER_M;
-    p.stage_bytes = static_cast<int>(align_up(NCW * F::SUB_BYTES + 2048 + p.xf_bytes, 1024));
-    // about 72 KiB of ring per CTA lets three CTAs (12 consumer warps) share an SM
-    int stages = (72 * 1024) / p.stage_bytes;
+    p.stage_bytes = NCW * F::SUB_BYTES + 2048;  // a multiple of 1 KiB
+    const int xbytes = 2 * M * F::XF_PER_M + M * KC * 2;  // fragment slots + staging copy of x
+    // 76 KiB per CTA in all (ring, header, zeros, fragments, alignment slack, 1 KiB of
+    // static sums) lets three CTAs (12 consumer warps) share an SM; 113 KiB two
+    const int budget = (M > 8 ? 113 : 76) * 1024 - 1024 - RING_OFF - 1024 - xbytes;
+    int stages = budget / p.stage_bytes;
     if (stages > 6) stages = 6;
     if (stages < 2) stages = 2;
-    int smem = 2048 + stages * p.stage_bytes;
-    while (smem > 227 * 1024 && stages > 2) {
+    int smem = 1024 + RING_OFF + stages * p.stage_bytes + xbytes;  // + alignment slack
+    while (smem > MAX_DYN_SMEM && stages > 2) {
         --stages;
-        smem = 2048 + stages * p.stage_bytes;
+        smem = 1024 + RING_OFF + stages * p.stage_bytes + xbytes;
     }
     p.stages = stages;
     p.smem = smem;
-    return smem <= 227 * 1024;
+    return smem <= MAX_DYN_SMEM;
 }
 
 // Encodes the three tensor maps of a weight (codes, scales, biases).
@@ -484,13 +582,12 @@ bool make_maps(const uint32_t* w, const void* s, const void* b, int K, int N, CU
                        CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
-// Launches prologue + main kernel with the given scratch.  Returns a CUDA error code.
-template <int BITS, int NT>
+// Launches the main kernel and the epilogue with the given scratch.  Returns a CUDA error code.
+template <int BITS, int MP, int TB>
 cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x, int M, int K,
                            const CUtensorMap& mc, const CUtensorMap& ms, const CUtensorMap& mb,
-                           bool has_bias, int N, void* y, uint8_t* xfrag, float* part,
-                           uint32_t* status, cudaStream_t stream) {
-    auto kmain = qgemv_main<BITS, NT>;
+                           bool has_bias, int N, void* y, float* part, uint32_t* status, cudaStream_t stream) {
+    auto kmain = qgemv_main<BITS, MP, TB>;
     // per template instance and device: smem opt-in and occupancy at the largest ring
     static std::mutex mu;
     static bool configured[64] = {};
@@ -500,7 +597,7 @@ cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x
     {
         std::lock_guard<std::mutex> lk(mu);
         if (!configured[device]) {
-            cudaError_t e = cudaFuncSetAttribute(kmain, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+            cudaError_t e = cudaFuncSetAttribute(kmain, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_DYN_SMEM);
             if (e != cudaSuccess) return e;
             configured[device] = true;
         }
@@ -528,22 +625,15 @@ cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cudaLaunchConfig_t pcfg = {};
-    pcfg.gridDim = dim3(static_cast<unsigned>(p.C));
-    pcfg.blockDim = dim3(256);
-    pcfg.stream = stream;
-    pcfg.attrs = attr;
-    pcfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&pcfg, qgemv_prep<BITS>, static_cast<const __nv_bfloat16*>(x), M, K, xfrag);
-    if (e != cudaSuccess) return e;
 
     MainArgs args;
-    args.xfrag = xfrag;
+    args.x = static_cast<const __nv_bfloat16*>(x);
     args.y = static_cast<__nv_bfloat16*>(y);
     args.ws = part;
     args.status = status;
     args.M = M;
     args.N = N;
+    args.K = K;
     args.C = p.C;
     args.tiles = p.tiles;
     args.stages = p.stages;
@@ -557,7 +647,7 @@ cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kmain, mc, ms, mb, args);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kmain, mc, ms, mb, args);
     if (e != cudaSuccess) return e;
 
     const int total = M * N;
@@ -574,28 +664,35 @@ cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x
     return cudaGetLastError();
 }
 
-template <int BITS, int NT>
+template <int BITS, int MP, int TB>
 q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, const void* s,
                   const void* b, int N, void* y) {
     Plan p;
     if (!make_plan<BITS>(M, K, N, p)) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: shape too large");
-    q38_status st = ensure_workspace(ctx, p.C * p.xf_bytes);
-    if (st != Q38_OK) return st;
     uint32_t* cnt = nullptr;  // (no counters are used)
     float* part = nullptr;
-    st = ensure_zero_region(ctx, 0, static_cast<size_t>(M) * N, &cnt, &part);
+    q38_status st = ensure_zero_region(ctx, 0, static_cast<size_t>(M) * N, &cnt, &part);
     if (st != Q38_OK) return st;
     CUtensorMap mc, ms, mb;
     if (!make_maps<BITS>(w, s, b, K, N, &mc, &ms, &mb))
         return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: tensor map encoding failed");
-    const cudaError_t e = launch_kernels<BITS, NT>(p, ctx->device, ctx->num_sms, x, M, K, mc, ms, mb, b != nullptr, N,
-                                                   y, static_cast<uint8_t*>(ctx->workspace), part,
-                                                   ctx->d_status, ctx->stream);
+    const cudaError_t e = launch_kernels<BITS, MP, TB>(p, ctx->device, ctx->num_sms, x, M, K, mc, ms, mb,
+                                                       b != nullptr, N, y, part, ctx->d_status, ctx->stream);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: launch failed: %s", cudaGetErrorString(e));
     }
     return Q38_OK;
+}
+
+// Token layout by M: MP token columns per group slot, TB blocks of 8 tokens.
+template <int BITS, typename L>
+q38_status dispatch_m(int M, L&& run) {
+    if (M == 1) return run(std::integral_constant<int, 1>(), std::integral_constant<int, 1>());
+    if (M == 2) return run(std::integral_constant<int, 2>(), std::integral_constant<int, 1>());
+    if (M <= 4) return run(std::integral_constant<int, 4>(), std::integral_constant<int, 1>());
+    if (M <= 8) return run(std::integral_constant<int, 8>(), std::integral_constant<int, 1>());
+    return run(std::integral_constant<int, 8>(), std::integral_constant<int, 2>());
 }
 
 }  // namespace
@@ -615,12 +712,17 @@ bool qgemv_fast_supported(int64_t M, int64_t K, int group, int bits, q38_dtype x
 q38_status qgemv_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w,
                       const void* s, const void* b, int64_t N, int bits, void* y) {
     const int m = static_cast<int>(M), k = static_cast<int>(K), n = static_cast<int>(N);
-    const bool two = M > 8;
+    auto go = [&](auto bits_c) {
+        constexpr int B = decltype(bits_c)::value;
+        return dispatch_m<B>(m, [&](auto mp, auto tb) {
+            return launch<B, decltype(mp)::value, decltype(tb)::value>(ctx, x, m, k, w, s, b, n, y);
+        });
+    };
     switch (bits) {
-        case 2: return two ? launch<2, 2>(ctx, x, m, k, w, s, b, n, y) : launch<2, 1>(ctx, x, m, k, w, s, b, n, y);
-        case 3: return two ? launch<3, 2>(ctx, x, m, k, w, s, b, n, y) : launch<3, 1>(ctx, x, m, k, w, s, b, n, y);
-        case 4: return two ? launch<4, 2>(ctx, x, m, k, w, s, b, n, y) : launch<4, 1>(ctx, x, m, k, w, s, b, n, y);
-        case 8: return two ? launch<8, 2>(ctx, x, m, k, w, s, b, n, y) : launch<8, 1>(ctx, x, m, k, w, s, b, n, y);
+        case 2: return go(std::integral_constant<int, 2>());
+        case 3: return go(std::integral_constant<int, 3>());
+        case 4: return go(std::integral_constant<int, 4>());
+        case 8: return go(std::integral_constant<int, 8>());
     }
     return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: bits %d not on the fast path", bits);
 }
@@ -638,15 +740,12 @@ q38_status qgemv_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const u
 namespace {
 
 constexpr int64_t NA_MAX_M = 16, NA_MAX_N = 32768, NA_MAX_K = 32768;
-constexpr size_t NA_ACC_BYTES = static_cast<size_t>(NA_MAX_M) * NA_MAX_N * 4;          // 2 MiB
-constexpr size_t NA_XF_BYTES = static_cast<size_t>(NA_MAX_K / KC) * NA_MAX_M * (256 * 8 + 64);  // 2.06 MiB
+constexpr size_t NA_ACC_BYTES = static_cast<size_t>(NA_MAX_M) * NA_MAX_N * 4;  // 2 MiB
 constexpr size_t NA_STATUS_OFF = 0;
 constexpr size_t NA_ACC_OFF = 256;
-constexpr size_t NA_XF_OFF = NA_ACC_OFF + NA_ACC_BYTES;
-constexpr size_t NA_TOTAL = NA_XF_OFF + NA_XF_BYTES;
+constexpr size_t NA_TOTAL = NA_ACC_OFF + NA_ACC_BYTES;
 
-// The scratch of every no-alloc call on a device (status word, fp32 partial sums,
-// activation fragments).  In host code this name is only a stand-in for
+// The scratch of every no-alloc call on a device (status word, fp32 partial sums).  In host code this name is only a stand-in for
 // the device array; its device address comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[NA_TOTAL];
 
@@ -669,7 +768,7 @@ q38_status noalloc_scratch(int device, uint8_t** out) {
     return Q38_OK;
 }
 
-template <int BITS, int NT>
+template <int BITS, int MP, int TB>
 q38_status launch_noalloc(uint8_t* scratch, int device, int num_sms, const void* x, int M, int K,
                           const uint32_t* w, const void* s, const void* b, int N, void* y,
                           cudaStream_t stream) {
@@ -677,7 +776,6 @@ q38_status launch_noalloc(uint8_t* scratch, int device, int num_sms, const void*
     if (!make_plan<BITS>(M, K, N, p)) return Q38_ERR_UNSUPPORTED;
     uint32_t* status = reinterpret_cast<uint32_t*>(scratch + NA_STATUS_OFF);
     float* part = reinterpret_cast<float*>(scratch + NA_ACC_OFF);
-    uint8_t* xfrag = scratch + NA_XF_OFF;
     // the partial sums must start at zero; a previous call leaves them zero, but clear
     // them anyway so an interrupted call cannot poison the next one
     if (cudaMemsetAsync(part, 0, static_cast<size_t>(M) * N * 4, stream) != cudaSuccess) {
@@ -686,8 +784,8 @@ q38_status launch_noalloc(uint8_t* scratch, int device, int num_sms, const void*
     }
     CUtensorMap mc, ms, mb;
     if (!make_maps<BITS>(w, s, b, K, N, &mc, &ms, &mb)) return Q38_ERR_CUDA;
-    const cudaError_t e = launch_kernels<BITS, NT>(p, device, num_sms, x, M, K, mc, ms, mb, b != nullptr, N, y,
-                                                   xfrag, part, status, stream);
+    const cudaError_t e = launch_kernels<BITS, MP, TB>(p, device, num_sms, x, M, K, mc, ms, mb, b != nullptr, N,
+                                                       y, part, status, stream);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return Q38_ERR_CUDA;
@@ -720,15 +818,17 @@ extern "C" Q38_API q38_status q38_quantized_matmul_noalloc(const void* x, int64_
     if (st != Q38_OK) return st;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int m = static_cast<int>(M), k = static_cast<int>(K), n = static_cast<int>(N);
-    const bool two = M > 8;
+    auto go = [&](auto bits_c) {
+        constexpr int B = decltype(bits_c)::value;
+        return dispatch_m<B>(m, [&](auto mp, auto tb) {
+            return launch_noalloc<B, decltype(mp)::value, decltype(tb)::value>(scratch, device, sms, x, m, k, w,
+                                                                              scales, biases, n, y, s);
+        });
+    };
     switch (bits) {
-        case 2: return two ? launch_noalloc<2, 2>(scratch, device, sms, x, m, k, w, scales, biases, n, y, s)
-                           : launch_noalloc<2, 1>(scratch, device, sms, x, m, k, w, scales, biases, n, y, s);
-        case 3: return two ? launch_noalloc<3, 2>(scratch, device, sms, x, m, k, w, scales, biases, n, y, s)
-                           : launch_noalloc<3, 1>(scratch, device, sms, x, m, k, w, scales, biases, n, y, s);
-        case 4: return two ? launch_noalloc<4, 2>(scratch, device, sms, x, m, k, w, scales, biases, n, y, s)
-                           : launch_noalloc<4, 1>(scratch, device, sms, x, m, k, w, scales, biases, n, y, s);
-        default: return two ? launch_noalloc<8, 2>(scratch, device, sms, x, m, k, w, scales, biases, n, y, s)
-                            : launch_noalloc<8, 1>(scratch, device, sms, x, m, k, w, scales, biases, n, y, s);
+        case 2: return go(std::integral_constant<int, 2>());
+        case 3: return go(std::integral_constant<int, 3>());
+        case 4: return go(std::integral_constant<int, 4>());
+        default: return go(std::integral_constant<int, 8>());
     }
 }
