@@ -446,7 +446,10 @@ q38_status moe_gather_launch(q38_ctx* ctx, const void* x, int H, const int32_t* 
         case 3: e = cudaLaunchKernelEx(&cfg, moe_gather_kernel<3>, xb, H, perm, pairs, top_k, valid, o); break;
         default: e = cudaLaunchKernelEx(&cfg, moe_gather_kernel<4>, xb, H, perm, pairs, top_k, valid, o); break;
     }
-    (void)e;
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(ctx, Q38_ERR_CUDA, "moe_gather: launch failed: %s", cudaGetErrorString(e));
+    }
     return check_launch(ctx, "moe_gather");
 }
 

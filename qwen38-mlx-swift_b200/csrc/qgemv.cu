@@ -42,8 +42,9 @@ using namespace dev;
 
 constexpr int KC = 512;        // k per chunk
 constexpr int GROUPS = 8;      // groups of 64 per chunk
-constexpr int NCW = 4;         // consumer warps (one 16-row subtile each)
-constexpr int THREADS = (NCW + 2) * 32;  // + weight producer + activation warp
+constexpr int NCW = 4;         // 16-row subtiles per stage (one consumer warp each)
+constexpr int WG = 2;          // consumer warp groups; group j takes the stages i with i % WG == j
+constexpr int THREADS = (NCW * WG + 2) * 32;  // + weight producer + activation warp
 
 template <int BITS>
 struct Fmt {
@@ -58,15 +59,16 @@ struct Fmt {
     static constexpr int XF_PER_M = XF_FRAG + 64;      // + bias-step fragments
 };
 
-// Byte offset of word `wi` of subtile row `r` inside a subtile's swizzled code block
-// (boxes of 16 rows x SW bytes, TMA swizzle of 16-byte chunks within SW-byte rows).
-// Rows r and r+8 share the swizzle, so row r+8 sits exactly 8*SW bytes after row r.
+// Byte offset of word `wi` of row `r` (of the subtile's 16) inside a subtile's codes.  A
+// stage holds BOXES column boxes of 64 rows x SW bytes (TMA swizzle of 16-byte chunks
+// within SW-byte rows); a subtile's rows start 16*SW bytes into each box.  Rows r and r+8
+// share the swizzle, so row r+8 sits exactly 8*SW bytes after row r.
 template <int SW>
 __device__ __forceinline__ uint32_t code_off(int r, int wi) {
     constexpr int WPB = SW / 4;  // words per box row
     const int box = wi / WPB, iw = wi % WPB;
     const int swz = SW == 128 ? (r & 7) : ((r >> 1) & 3);
-    return box * (16 * SW) + r * SW + ((((iw >> 2) ^ swz)) << 4) + (iw & 3) * 4;
+    return box * (64 * SW) + r * SW + ((((iw >> 2) ^ swz)) << 4) + (iw & 3) * 4;
 }
 
 // First (and for 3 bits, second) word of the window of (row r, group gi, quarter t).
@@ -175,6 +177,11 @@ __device__ __forceinline__ void build_fragments(const uint8_t* xc, int M, uint8_
 // ---------------------------------------------------------------------------------
 // Main kernel.
 // ---------------------------------------------------------------------------------
+// Tensor maps of one weight: codes in 16-row and 64-row boxes, scales, biases.
+struct WeightMaps {
+    CUtensorMap codes16, codes64, scales, biases;
+};
+
 struct MainArgs {
     const __nv_bfloat16* x;
     __nv_bfloat16* y;
@@ -248,9 +255,7 @@ constexpr int ZERO_OFF = 1024, ZERO_BYTES = 2048, RING_OFF = 3072;
 constexpr int MAX_DYN_SMEM = 226 * 1024;  // 227 KiB per CTA less the static per-group sums
 
 template <int BITS, int MP, int TB>
-__global__ void __launch_bounds__(THREADS, TB == 1 ? 3 : 2) qgemv_main(const __grid_constant__ CUtensorMap map_codes,
-                                                                      const __grid_constant__ CUtensorMap map_scales,
-                                                                      const __grid_constant__ CUtensorMap map_biases,
+__global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 1 ? 2 : 1)) qgemv_main(const __grid_constant__ WeightMaps maps,
                                                                       const MainArgs a) {
     using F = Fmt<BITS>;
     constexpr int GPER = 8 / MP;                 // groups sharing one accumulator set
@@ -297,7 +302,7 @@ __global__ void __launch_bounds__(THREADS, TB == 1 ? 3 : 2) qgemv_main(const __g
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&xfull[i], 1);
-            mbar_init(&xempty[i], NCW);
+            mbar_init(&xempty[i], NCW * WG);
         }
         fence_mbar_init();
     }
@@ -306,14 +311,15 @@ __global__ void __launch_bounds__(THREADS, TB == 1 ? 3 : 2) qgemv_main(const __g
     // or writing anything this grid touches.
     griddep_launch_dependents();
 
-    if (warp == NCW) {
+    if (warp == NCW * WG) {
         // ------------------------------------------------------------ weight producer
         // Streams codes, scales and biases; they are read-only inputs, so the ring fills
         // while the previous kernel on the stream is still finishing.
         if (lane == 0) {
-            prefetch_tensormap(&map_codes);
-            prefetch_tensormap(&map_scales);
-            if (a.has_bias) prefetch_tensormap(&map_biases);
+            prefetch_tensormap(&maps.codes16);
+            prefetch_tensormap(&maps.codes64);
+            prefetch_tensormap(&maps.scales);
+            if (a.has_bias) prefetch_tensormap(&maps.biases);
             int chunk = st_first / a.tiles, tile = st_first % a.tiles;
             int slot = 0;
             uint32_t ph = 0;
@@ -322,20 +328,31 @@ __global__ void __launch_bounds__(THREADS, TB == 1 ? 3 : 2) qgemv_main(const __g
                 const int sub_lo = i == 0 ? lo_first : 0;
                 const int sub_hi = i == nst - 1 ? hi_last : 4;
                 uint8_t* sbase = stage0 + static_cast<size_t>(slot) * a.stage_bytes;
+                // whole 64-row tiles inside the matrix in one box per column range,
+                // otherwise one 16-row box per active subtile
+                const bool whole = sub_lo == 0 && sub_hi == 4 && tile * 64 + 64 <= a.N;
                 int nact = 0;
                 for (int s = sub_lo; s < sub_hi; ++s) nact += (tile * 64 + 16 * s < a.N);
+                if (whole) nact = 4;
                 const uint32_t bytes = nact * F::SUB_BYTES + 1024 + (a.has_bias ? 1024 : 0);
                 mbar_arrive_expect_tx(&full[slot], bytes);
-                for (int s = sub_lo; s < sub_hi; ++s) {
-                    if (tile * 64 + 16 * s >= a.N) continue;
+                if (whole) {
 #pragma unroll
                     for (int bx = 0; bx < F::BOXES; ++bx)
-                        tma_load_2d(sbase + s * F::SUB_BYTES + bx * 16 * F::SW, &map_codes, &full[slot],
-                                    chunk * F::ROW_WORDS + bx * (F::SW / 4), tile * 64 + 16 * s);
+                        tma_load_2d(sbase + bx * 64 * F::SW, &maps.codes64, &full[slot],
+                                    chunk * F::ROW_WORDS + bx * (F::SW / 4), tile * 64);
+                } else {
+                    for (int s = sub_lo; s < sub_hi; ++s) {
+                        if (tile * 64 + 16 * s >= a.N) continue;
+#pragma unroll
+                        for (int bx = 0; bx < F::BOXES; ++bx)
+                            tma_load_2d(sbase + bx * 64 * F::SW + s * 16 * F::SW, &maps.codes16, &full[slot],
+                                        chunk * F::ROW_WORDS + bx * (F::SW / 4), tile * 64 + 16 * s);
+                    }
                 }
                 uint8_t* sc = sbase + NCW * F::SUB_BYTES;
-                tma_load_2d(sc, &map_scales, &full[slot], chunk * GROUPS, tile * 64);
-                if (a.has_bias) tma_load_2d(sc + 1024, &map_biases, &full[slot], chunk * GROUPS, tile * 64);
+                tma_load_2d(sc, &maps.scales, &full[slot], chunk * GROUPS, tile * 64);
+                if (a.has_bias) tma_load_2d(sc + 1024, &maps.biases, &full[slot], chunk * GROUPS, tile * 64);
                 if (++slot == a.stages) {
                     slot = 0;
                     ph ^= 1;
@@ -349,7 +366,7 @@ __global__ void __launch_bounds__(THREADS, TB == 1 ? 3 : 2) qgemv_main(const __g
         return;
     }
 
-    if (warp == NCW + 1) {
+    if (warp == NCW * WG + 1) {
         // ------------------------------------------------------------ activation warp
         // x is written by the previous kernel on the stream: wait for it to complete.
         griddep_wait();
@@ -375,6 +392,8 @@ __global__ void __launch_bounds__(THREADS, TB == 1 ? 3 : 2) qgemv_main(const __g
     // The partial sums may still be in use by the previous product's epilogue until it
     // has completed.
     griddep_wait();
+    const int wgrp = warp / NCW;  // this warp's group: it computes the stages i with i % WG == wgrp
+    const int sw_i = warp % NCW;  // and, in each, subtile sw_i
     const int g = lane >> 2, t = lane & 3;
     const bool odd = (t & 1) != 0;
     // swizzled code offsets of (row g, group gi); row g+8 is 8*SW bytes further
@@ -396,7 +415,7 @@ __global__ void __launch_bounds__(THREADS, TB == 1 ? 3 : 2) qgemv_main(const __g
         tok[tb] = TB == 1 ? ml : tb * 8 + g;
         tval[tb] = tok[tb] < a.M;
     }
-    const int srow0 = warp * 16 + g;  // scale row of row g (row g+8 is 64 halfwords further)
+    const int srow0 = sw_i * 16 + g;  // scale row of row g (row g+8 is 64 halfwords further)
 
     int cur_ci = -1;
     const uint8_t* xf = xslots;
@@ -405,6 +424,7 @@ __global__ void __launch_bounds__(THREADS, TB == 1 ? 3 : 2) qgemv_main(const __g
     int chunk = st_first / a.tiles, tile = st_first % a.tiles;
     int slot = 0;
     uint32_t ph = 0;
+    int own = 0;  // i % WG
     for (int i = 0; i < nst; ++i) {
         const int sub_lo = i == 0 ? lo_first : 0;
         const int sub_hi = i == nst - 1 ? hi_last : 4;
@@ -427,16 +447,17 @@ __global__ void __launch_bounds__(THREADS, TB == 1 ? 3 : 2) qgemv_main(const __g
                 for (int tb = 0; tb < TB; ++tb) pg[tb] = tval[tb] ? xf + tok[tb] * F::XF_PER_M + t * 16 : zeros;
             }
         }
-        const bool active = warp >= sub_lo && warp < sub_hi && tile * 64 + 16 * warp < a.N;
-        if (!mbar_wait(&full[slot], ph, a.status)) return;
+        const bool mine = own == wgrp;
+        const bool active = mine && sw_i >= sub_lo && sw_i < sub_hi && tile * 64 + 16 * sw_i < a.N;
+        if (mine && !mbar_wait(&full[slot], ph, a.status)) return;
+        float acc[TB][4];
         if (active) {
             const uint8_t* sbase = stage0 + static_cast<size_t>(slot) * a.stage_bytes;
-            const uint8_t* sub = sbase + warp * F::SUB_BYTES;
+            const uint8_t* sub = sbase + sw_i * 16 * F::SW;
             const uint16_t* scl = reinterpret_cast<const uint16_t*>(sbase + NCW * F::SUB_BYTES) + srow0 * GROUPS;
             // scales of rows g and g+8 for groups 2t, 2t+1 (one word each), biases likewise
             const uint32_t* sw = reinterpret_cast<const uint32_t*>(scl) + t;
             const uint32_t s_g = sw[0], s_g8 = sw[32], b_g = sw[256], b_g8 = sw[256 + 32];
-            float acc[TB][4];
 #pragma unroll
             for (int tb = 0; tb < TB; ++tb)
 #pragma unroll
@@ -524,10 +545,15 @@ __global__ void __launch_bounds__(THREADS, TB == 1 ? 3 : 2) qgemv_main(const __g
                 mma_bf16_16816(acc[tb], s_g, s_g8, b_g, b_g8, bb.x, bb.y, acc[tb]);
                 mma_bf16_16816(acc[tb], s_g, s_g8, b_g, b_g8, bb.z, bb.w, acc[tb]);
             }
-            flush_subtile<MP, TB>(acc, tile, warp, a, lane);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
+        // Release the stage before adding the sums to the workspace: the arrive orders this
+        // warp's earlier memory operations, and the reductions have not completed yet.
+        if (mine) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        if (active) flush_subtile<MP, TB>(acc, tile, sw_i, a, lane);
+        if (++own == WG) own = 0;
         if (++slot == a.stages) {
             slot = 0;
             ph ^= 1;
@@ -554,9 +580,9 @@ bool make_plan(int M, int K, int N, Plan& p) {
     const int xbytes = 2 * M * F::XF_PER_M + M * KC * 2;  // fragment slots + staging copy of x
     // 76 KiB per CTA in all (ring, header, zeros, fragments, alignment slack, 1 KiB of
     // static sums) lets three CTAs (12 consumer warps) share an SM; 113 KiB two
-    const int budget = (M > 8 ? 113 : 76) * 1024 - 1024 - RING_OFF - 1024 - xbytes;
+    const int budget = (WG == 1 ? (M > 8 ? 113 : 76) : (M > 8 ? 226 : 113)) * 1024 - 1024 - RING_OFF - 1024 - xbytes;
     int stages = budget / p.stage_bytes;
-    if (stages > 6) stages = 6;
+    if (stages > 8) stages = 8;
     if (stages < 2) stages = 2;
     int smem = 1024 + RING_OFF + stages * p.stage_bytes + xbytes;  // + alignment slack
     while (smem > MAX_DYN_SMEM && stages > 2) {
@@ -568,25 +594,24 @@ bool make_plan(int M, int K, int N, Plan& p) {
     return smem <= MAX_DYN_SMEM;
 }
 
-// Encodes the three tensor maps of a weight (codes, scales, biases).
+// Encodes the tensor maps of a weight (codes in two box heights, scales, biases).
 template <int BITS>
-bool make_maps(const uint32_t* w, const void* s, const void* b, int K, int N, CUtensorMap* mc,
-               CUtensorMap* ms, CUtensorMap* mb) {
+bool make_maps(const uint32_t* w, const void* s, const void* b, int K, int N, WeightMaps* m) {
     using F = Fmt<BITS>;
     const uint64_t kw = static_cast<uint64_t>(K) * BITS / 32;
-    return make_map_2d(mc, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w, kw, N, F::SW / 4, 16,
-                       F::SW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B) &&
-           make_map_2d(ms, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s, K / 64, N, GROUPS, 64,
+    const CUtensorMapSwizzle swz = F::SW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    return make_map_2d(&m->codes16, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w, kw, N, F::SW / 4, 16, swz) &&
+           make_map_2d(&m->codes64, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w, kw, N, F::SW / 4, 64, swz) &&
+           make_map_2d(&m->scales, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s, K / 64, N, GROUPS, 64,
                        CU_TENSOR_MAP_SWIZZLE_NONE) &&
-           make_map_2d(mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b ? b : s, K / 64, N, GROUPS, 64,
+           make_map_2d(&m->biases, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b ? b : s, K / 64, N, GROUPS, 64,
                        CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 // Launches the main kernel and the epilogue with the given scratch.  Returns a CUDA error code.
 template <int BITS, int MP, int TB>
 cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x, int M, int K,
-                           const CUtensorMap& mc, const CUtensorMap& ms, const CUtensorMap& mb,
-                           bool has_bias, int N, void* y, float* part, uint32_t* status, cudaStream_t stream) {
+                           const WeightMaps& maps, bool has_bias, int N, void* y, float* part, uint32_t* status, cudaStream_t stream) {
     auto kmain = qgemv_main<BITS, MP, TB>;
     // per template instance and device: smem opt-in and occupancy at the largest ring
     static std::mutex mu;
@@ -647,7 +672,7 @@ cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kmain, mc, ms, mb, args);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kmain, maps, args);
     if (e != cudaSuccess) return e;
 
     const int total = M * N;
@@ -673,10 +698,10 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
     float* part = nullptr;
     q38_status st = ensure_zero_region(ctx, 0, static_cast<size_t>(M) * N, &cnt, &part);
     if (st != Q38_OK) return st;
-    CUtensorMap mc, ms, mb;
-    if (!make_maps<BITS>(w, s, b, K, N, &mc, &ms, &mb))
+    WeightMaps maps;
+    if (!make_maps<BITS>(w, s, b, K, N, &maps))
         return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: tensor map encoding failed");
-    const cudaError_t e = launch_kernels<BITS, MP, TB>(p, ctx->device, ctx->num_sms, x, M, K, mc, ms, mb,
+    const cudaError_t e = launch_kernels<BITS, MP, TB>(p, ctx->device, ctx->num_sms, x, M, K, maps,
                                                        b != nullptr, N, y, part, ctx->d_status, ctx->stream);
     if (e != cudaSuccess) {
         cudaGetLastError();
@@ -782,9 +807,9 @@ q38_status launch_noalloc(uint8_t* scratch, int device, int num_sms, const void*
         cudaGetLastError();
         return Q38_ERR_CUDA;
     }
-    CUtensorMap mc, ms, mb;
-    if (!make_maps<BITS>(w, s, b, K, N, &mc, &ms, &mb)) return Q38_ERR_CUDA;
-    const cudaError_t e = launch_kernels<BITS, MP, TB>(p, device, num_sms, x, M, K, mc, ms, mb, b != nullptr, N,
+    WeightMaps maps;
+    if (!make_maps<BITS>(w, s, b, K, N, &maps)) return Q38_ERR_CUDA;
+    const cudaError_t e = launch_kernels<BITS, MP, TB>(p, device, num_sms, x, M, K, maps, b != nullptr, N,
                                                        y, part, status, stream);
     if (e != cudaSuccess) {
         cudaGetLastError();
