@@ -85,6 +85,50 @@ __device__ __forceinline__ void extract(const uint32_t* w, uint32_t* a) {
     }
 }
 
+// ---------------------------------------------------------------------------------
+// f16 variant for 4- and 8-bit codes.  f16 1024.0 (0x6400) has a 10-bit mantissa, so a
+// code masked into it at bit p < 10 - bits reads as 1024 + 2^p * q: nibbles at bit 0 and
+// bit 4 of a half, and whole bytes at bit 0, need no shift.
+//   4 bits: word v -> (n0,n4), 16*(n1,n5), (n2,n6), 16*(n3,n7)   [v, v >> 8]
+//   8 bits: word v -> (b0,b2), (b1,b3)                           [v, v >> 8]
+// ---------------------------------------------------------------------------------
+constexpr uint32_t MAGIC16 = 0x64006400u;  // f16 1024.0 in both halves
+__constant__ uint32_t c_magic16 = MAGIC16;
+
+template <int BITS>
+__host__ __device__ constexpr int pair_code16(int q, int hi) {
+    if (BITS == 4) return (q / 4) * 8 + (q % 4) + (hi ? 4 : 0);
+    /* 8 */ return (q / 2) * 4 + (q % 2) + (hi ? 2 : 0);
+}
+
+template <int BITS>
+__host__ __device__ constexpr float pair_mult16(int q, int) {
+    return (BITS == 4 && (q & 1)) ? 0.0625f : 1.0f;
+}
+
+// The 8 f16x2 operands of one thread-row-group (16 codes: 2 words of 4-bit, 4 of 8-bit).
+template <int BITS>
+__device__ __forceinline__ void extract16(const uint32_t* w, uint32_t* a) {
+    const uint32_t M16 = c_magic16;
+    if constexpr (BITS == 4) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const uint32_t v = w[i], v8 = v >> 8;
+            a[4 * i + 0] = (v & 0x000F000Fu) | M16;
+            a[4 * i + 1] = (v & 0x00F000F0u) | M16;
+            a[4 * i + 2] = (v8 & 0x000F000Fu) | M16;
+            a[4 * i + 3] = (v8 & 0x00F000F0u) | M16;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t v = w[i];
+            a[2 * i + 0] = (v & 0x00FF00FFu) | M16;
+            a[2 * i + 1] = ((v >> 8) & 0x00FF00FFu) | M16;
+        }
+    }
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return static_cast<uint32_t>(f32_to_bf16_bits(lo)) |
            (static_cast<uint32_t>(f32_to_bf16_bits(hi)) << 16);

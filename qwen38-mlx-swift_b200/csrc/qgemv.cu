@@ -48,8 +48,10 @@ constexpr int THREADS = (NCW * WG + 2) * 32;  // + weight producer + activation 
 
 template <int BITS>
 struct Fmt {
-    static constexpr int SPG = BITS == 8 ? 8 : 4;     // k16 MMA steps per group
-    static constexpr int NP = 2 * SPG;                 // bf16x2 pairs per thread-row-group
+    static constexpr bool F16 = BITS == 4 || BITS == 8;  // f16 operands (else bf16)
+    static constexpr int SPG = 4;                      // k16 MMA steps per group
+    static constexpr int NP = 2 * SPG;                 // operand pairs per thread-row-group
+    static constexpr float OFFSET = F16 ? 1024.0f : 128.0f;  // value of the magic number
     static constexpr int SW = BITS == 3 ? 64 : 128;    // swizzle span of a code box (bytes)
     static constexpr int ROW_BYTES = KC * BITS / 8;    // code bytes per row per chunk
     static constexpr int ROW_WORDS = ROW_BYTES / 4;
@@ -113,7 +115,8 @@ __device__ __forceinline__ void load_window(const uint8_t* p, uint32_t offA, uin
 // Layout per token m (stride XF_PER_M bytes):
 //   [group 8][k-step pair SPG/2][t 4][16 B]  then  [t 4][16 B]
 // The first part holds x' (x permuted into extraction order and scaled by 2^-p) as
-// bf16x2 MMA B operands.  The second holds, for lane quarter t, the B operands of the
+// MMA B operands: f16x2 for 4- and 8-bit codes (after a power-of-two range factor of
+// the chunk, kept after the token blocks), bf16x2 otherwise.  The second holds, for lane quarter t, the B operands of the
 // offset-and-bias steps: groups 2t and 2t+1 of -128 * sum(x') and of sum(x), each split
 // into a bf16 high part (words 0, 1) and the bf16 of the remainder (words 2, 3).
 // ---------------------------------------------------------------------------------
@@ -122,6 +125,22 @@ __device__ __forceinline__ void build_fragments(const uint8_t* xc, int M, uint8_
                                                 float (*s_xp)[16], int lane) {
     using F = Fmt<BITS>;
     constexpr uint32_t ONE2 = 0x3F803F80u;  // bf16x2 (1, 1)
+    // f16 operands: scale the chunk by 2^-e so that its largest |x| stays below 2^15; the
+    // consumers multiply the group scales by 2^e (stored after the token blocks).
+    float down = 1.0f;
+    if constexpr (F::F16) {
+        uint32_t mx = 0;
+        const uint32_t* xw = reinterpret_cast<const uint32_t*>(xc);
+        for (int p = lane; p < M * (KC / 2); p += 32) {
+            const uint32_t wv = xw[p];
+            mx = max(mx, max(wv & 0x7FFFu, (wv >> 16) & 0x7FFFu));
+        }
+        mx = __reduce_max_sync(0xffffffffu, mx);
+        const int E = static_cast<int>(mx >> 7);  // bf16 exponent field of the largest |x|
+        const int esh = E > 141 ? E - 141 : 0;
+        down = __uint_as_float(static_cast<uint32_t>(127 - esh) << 23);
+        if (lane == 0) *reinterpret_cast<float*>(base + M * F::XF_PER_M) = __uint_as_float(static_cast<uint32_t>(127 + esh) << 23);
+    }
     // 32 * M items: every iteration has all 32 lanes, and lanes 4i..4i+3 share (group, token)
     const int items = GROUPS * M * 4;
     for (int i = lane; i < items; i += 32) {
@@ -135,19 +154,31 @@ __device__ __forceinline__ void build_fragments(const uint8_t* xc, int M, uint8_
         uint32_t* dst = reinterpret_cast<uint32_t*>(base + m * F::XF_PER_M + gi * (F::SPG / 2) * 64 + t * 16);
 #pragma unroll
         for (int q = 0; q < F::NP; ++q) {
-            // pair (code a, code b) = (element a, element b) of the 16, as one bf16x2
-            const int ea = pair_code<BITS>(q, 0), eb = pair_code<BITS>(q, 1);
+            // pair (code a, code b) = (element a, element b) of the 16
+            const int ea = F::F16 ? pair_code16<BITS>(q, 0) : pair_code<BITS>(q, 0);
+            const int eb = F::F16 ? pair_code16<BITS>(q, 1) : pair_code<BITS>(q, 1);
             const uint32_t lo = (ea & 1) ? (raw[ea >> 1] >> 16) : (raw[ea >> 1] & 0xFFFFu);
             const uint32_t hi = (eb & 1) ? (raw[eb >> 1] & 0xFFFF0000u) : (raw[eb >> 1] << 16);
-            uint32_t pr = lo | hi;
-            const float ma = pair_mult<BITS>(q, 0), mb = pair_mult<BITS>(q, 1);
-            if (ma != 1.0f || mb != 1.0f)
-                pr = mul_bf16x2(pr, (static_cast<uint32_t>(f32_to_bf16_bits(ma))) |
-                                        (static_cast<uint32_t>(f32_to_bf16_bits(mb)) << 16));
-            if (BITS != 4) xp = fma2_bf16_f32(pr, ONE2, xp);
-            dst[(q / 4) * 16 + (q % 4)] = pr;
+            const uint32_t pr = lo | hi;  // bf16x2 (x_a, x_b)
+            const float ma = F::F16 ? pair_mult16<BITS>(q, 0) : pair_mult<BITS>(q, 0);
+            const float mb = F::F16 ? pair_mult16<BITS>(q, 1) : pair_mult<BITS>(q, 1);
+            const uint32_t mult2 = static_cast<uint32_t>(f32_to_bf16_bits(ma)) |
+                                   (static_cast<uint32_t>(f32_to_bf16_bits(mb)) << 16);
+            if constexpr (F::F16) {
+                // f16x2 of (x_a * ma, x_b * mb) * 2^-e, rounded once (exact unless tiny)
+                const float fa = __uint_as_float(lo << 16) * (ma * down);
+                const float fb = __uint_as_float(hi & 0xFFFF0000u) * (mb * down);
+                uint32_t h2;
+                asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(fb), "f"(fa));
+                dst[(q / 4) * 16 + (q % 4)] = h2;
+                if (BITS != 8) xp = fma2_bf16_f32(pr, mult2, xp);
+            } else {
+                const uint32_t scaled = (ma != 1.0f || mb != 1.0f) ? mul_bf16x2(pr, mult2) : pr;
+                if (BITS != 4) xp = fma2_bf16_f32(scaled, ONE2, xp);
+                dst[(q / 4) * 16 + (q % 4)] = scaled;
+            }
         }
-        if (BITS == 4) xp = xs;  // every factor is 1
+        if (BITS == 8) xp = xs;  // every factor is 1
         xs += __shfl_xor_sync(0xffffffffu, xs, 1);
         xs += __shfl_xor_sync(0xffffffffu, xs, 2);
         xp += __shfl_xor_sync(0xffffffffu, xp, 1);
@@ -161,7 +192,8 @@ __device__ __forceinline__ void build_fragments(const uint8_t* xc, int M, uint8_
     // offset-and-bias operands of quarter t: groups 2t, 2t+1
     for (int i = lane; i < 4 * M; i += 32) {
         const int t = i & 3, m = i >> 2;
-        float v[4] = {-128.0f * s_xp[2 * t][m], -128.0f * s_xp[2 * t + 1][m], s_xs[2 * t][m], s_xs[2 * t + 1][m]};
+        float v[4] = {-F::OFFSET * s_xp[2 * t][m], -F::OFFSET * s_xp[2 * t + 1][m], s_xs[2 * t][m],
+                      s_xs[2 * t + 1][m]};
         uint32_t hb[4], lb[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -259,7 +291,7 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
                                                                       const MainArgs a) {
     using F = Fmt<BITS>;
     constexpr int GPER = 8 / MP;                 // groups sharing one accumulator set
-    constexpr int UG = BITS == 8 ? 1 : 2;        // groups extracted together
+    constexpr int UG = 2;                        // groups extracted together
     constexpr int FLUSH = TB == 1 ? GROUPS : UG; // groups between scale applications
     constexpr int LIVE = TB == 1 ? MP : UG;      // accumulator sets alive between applications
     constexpr int SPLIT = (TB == 1 && MP <= 2 && UG == 2) ? 2 : 1;  // shorter MMA chains
@@ -272,7 +304,7 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
     const uint8_t* zeros = smem + ZERO_OFF;
     uint8_t* stage0 = smem + RING_OFF;
     uint8_t* xslots = stage0 + static_cast<size_t>(a.stages) * a.stage_bytes;
-    const int xslot_bytes = a.M * F::XF_PER_M;
+    const int xslot_bytes = a.M * F::XF_PER_M + 16;  // + the chunk's f16 range factor
     uint8_t* xstage = xslots + 2 * xslot_bytes;
     __shared__ float s_xs[GROUPS][16], s_xp[GROUPS][16];
 
@@ -419,6 +451,7 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
 
     int cur_ci = -1;
     const uint8_t* xf = xslots;
+    float xup = 1.0f;  // range factor of the chunk's f16 activations
     // per group: where this lane's B operand comes from (its fragments, or zeros)
     const uint8_t* pg[TB == 1 ? GROUPS : TB];
     int chunk = st_first / a.tiles, tile = st_first % a.tiles;
@@ -438,6 +471,7 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
             if (!mbar_wait(&xfull[ci & 1], (ci >> 1) & 1, a.status)) return;
             cur_ci = ci;
             xf = xslots + (ci & 1) * xslot_bytes;
+            if (F::F16) xup = *reinterpret_cast<const float*>(xf + a.M * F::XF_PER_M);
             if (TB == 1) {
 #pragma unroll
                 for (int gi = 0; gi < (TB == 1 ? GROUPS : TB); ++gi)
@@ -463,23 +497,13 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
 #pragma unroll
                 for (int e = 0; e < 4; ++e) acc[tb][e] = 0.f;
             float d[LIVE * SPLIT][TB][4];
-#pragma unroll
-            for (int gb = 0; gb < GROUPS; gb += UG) {
-                if (gb % FLUSH == 0) {
-#pragma unroll
-                    for (int s = 0; s < LIVE * SPLIT; ++s)
-#pragma unroll
-                        for (int tb = 0; tb < TB; ++tb)
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) d[s][tb][e] = 0.f;
-                }
-                uint32_t w[UG][2][4], ar[UG][2][F::NP];
+            // code windows and B operands of a pair of groups; loaded one pair ahead
+            auto load_pair = [&](int gb, uint32_t (&w)[UG][2][4], uint2 (&xb)[UG][TB][F::SPG]) {
 #pragma unroll
                 for (int u = 0; u < UG; ++u) {
                     load_window<BITS>(sub, offA[gb + u], offB[gb + u], odd, w[u][0]);
                     load_window<BITS>(sub + ROW8, offA[gb + u], offB[gb + u], odd, w[u][1]);
                 }
-                uint2 xb[UG][TB][F::SPG];
 #pragma unroll
                 for (int u = 0; u < UG; ++u) {
                     const int gi = gb + u;
@@ -491,10 +515,44 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
                             xb[u][tb][j] = *reinterpret_cast<const uint2*>(p + (gi * (F::SPG / 2) + j / 2) * 64 + (j & 1) * 8);
                     }
                 }
+            };
+            uint32_t wn[UG][2][4];
+            uint2 xn[UG][TB][F::SPG];
+            load_pair(0, wn, xn);
+#pragma unroll
+            for (int gb = 0; gb < GROUPS; gb += UG) {
+                if (gb % FLUSH == 0) {
+#pragma unroll
+                    for (int s = 0; s < LIVE * SPLIT; ++s)
+#pragma unroll
+                        for (int tb = 0; tb < TB; ++tb)
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) d[s][tb][e] = 0.f;
+                }
+                uint32_t w[UG][2][4], ar[UG][2][F::NP];
+                uint2 xb[UG][TB][F::SPG];
+#pragma unroll
+                for (int u = 0; u < UG; ++u)
+#pragma unroll
+                    for (int r = 0; r < 2; ++r)
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) w[u][r][k] = wn[u][r][k];
+#pragma unroll
+                for (int u = 0; u < UG; ++u)
+#pragma unroll
+                    for (int tb = 0; tb < TB; ++tb)
+#pragma unroll
+                        for (int j = 0; j < F::SPG; ++j) xb[u][tb][j] = xn[u][tb][j];
+                if (gb + UG < GROUPS) load_pair(gb + UG, wn, xn);
 #pragma unroll
                 for (int u = 0; u < UG; ++u) {
-                    extract<BITS>(w[u][0], ar[u][0]);
-                    extract<BITS>(w[u][1], ar[u][1]);
+                    if constexpr (F::F16) {
+                        extract16<BITS>(w[u][0], ar[u][0]);
+                        extract16<BITS>(w[u][1], ar[u][1]);
+                    } else {
+                        extract<BITS>(w[u][0], ar[u][0]);
+                        extract<BITS>(w[u][1], ar[u][1]);
+                    }
                 }
 #pragma unroll
                 for (int j = 0; j < F::SPG; ++j)
@@ -503,9 +561,14 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
                         const int gi = gb + u;
                         const int s = ((gi / GPER) % LIVE) + (SPLIT > 1 ? LIVE * u : 0);
 #pragma unroll
-                        for (int tb = 0; tb < TB; ++tb)
-                            mma_bf16_16816(d[s][tb], ar[u][0][2 * j], ar[u][1][2 * j], ar[u][0][2 * j + 1],
-                                           ar[u][1][2 * j + 1], xb[u][tb][j].x, xb[u][tb][j].y, d[s][tb]);
+                        for (int tb = 0; tb < TB; ++tb) {
+                            if constexpr (F::F16)
+                                mma_f16_16816(d[s][tb], ar[u][0][2 * j], ar[u][1][2 * j], ar[u][0][2 * j + 1],
+                                              ar[u][1][2 * j + 1], xb[u][tb][j].x, xb[u][tb][j].y, d[s][tb]);
+                            else
+                                mma_bf16_16816(d[s][tb], ar[u][0][2 * j], ar[u][1][2 * j], ar[u][0][2 * j + 1],
+                                               ar[u][1][2 * j + 1], xb[u][tb][j].x, xb[u][tb][j].y, d[s][tb]);
+                        }
                     }
                 if ((gb + UG) % FLUSH == 0) {
                     // scale the finished sets: column 2t + c of set s belongs to group
@@ -523,6 +586,7 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
                                 const int gi = (gset0 + s) * GPER + (2 * t) / MP;
                                 sc = bf16_bits_to_f32(scl[((e >> 1) << 6) + gi]);
                             }
+                            if (F::F16) sc *= xup;
 #pragma unroll
                             for (int tb = 0; tb < TB; ++tb) {
                                 float v = d[s][tb][e];
@@ -577,7 +641,7 @@ bool make_plan(int M, int K, int N, Plan& p) {
     p.tiles = (N + 63) / 64;
     if (static_cast<long long>(p.tiles) * p.C * 4 >= (1LL << 31)) return false;
     p.stage_bytes = NCW * F::SUB_BYTES + 2048;  // a multiple of 1 KiB
-    const int xbytes = 2 * M * F::XF_PER_M + M * KC * 2;  // fragment slots + staging copy of x
+    const int xbytes = 2 * (M * F::XF_PER_M + 16) + M * KC * 2;  // fragment slots + staging copy of x
     // 76 KiB per CTA in all (ring, header, zeros, fragments, alignment slack, 1 KiB of
     // static sums) lets three CTAs (12 consumer warps) share an SM; 113 KiB two
     const int budget = (WG == 1 ? (M > 8 ? 113 : 76) : (M > 8 ? 226 : 113)) * 1024 - 1024 - RING_OFF - 1024 - xbytes;
