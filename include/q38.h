@@ -251,7 +251,7 @@ Q38_API q38_status q38_moe_ep_reduce(q38_ctx* ctx, const void* partial, int64_t 
  * product as q38_quantized_matmul (transpose = true, affine, group 64, bits 2/3/4/8,
  * bf16 x/y/scales/biases, 16-byte-aligned pointers) with no context: it runs on the
  * calling thread's current device and on `stream` (a cudaStream_t, NULL = legacy
- * default stream).  Its scratch is one fixed 4.1 MiB array in device memory that the
+ * default stream).  Its scratch is one fixed 2 MiB array in device memory that the
  * library holds on every GPU it is loaded on until the process exits, so the limits
  * are M <= 16, N <= 32768, K <= 32768 (K % 512 == 0); larger shapes return
  * Q38_ERR_INVALID_ARGUMENT.  The first call on a device resolves the array's address
