@@ -672,6 +672,40 @@ bool make_maps(const uint32_t* w, const void* s, const void* b, int K, int N, We
                        CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
+// Encoded maps of recently used weights.  A decode loop calls the same projections again
+// and again, and the encoding depends only on the pointers and the shape, so a hit is
+// always valid (a new weight at an old address with the same shape encodes identically).
+template <int BITS>
+bool cached_maps(const uint32_t* w, const void* s, const void* b, int K, int N, WeightMaps* maps) {
+    struct Entry {
+        const void* w;
+        const void* s;
+        const void* b;
+        int K, N;
+        bool used;
+        WeightMaps maps;
+    };
+    static std::mutex mu;
+    static Entry cache[64];
+    const uintptr_t h = (reinterpret_cast<uintptr_t>(w) >> 8) ^ (reinterpret_cast<uintptr_t>(s) >> 6) ^
+                        static_cast<uintptr_t>(K) * 31u ^ static_cast<uintptr_t>(N) * 17u;
+    Entry& e = cache[(h ^ (h >> 12)) & 63u];
+    std::lock_guard<std::mutex> lk(mu);
+    if (e.used && e.w == w && e.s == s && e.b == b && e.K == K && e.N == N) {
+        *maps = e.maps;
+        return true;
+    }
+    if (!make_maps<BITS>(w, s, b, K, N, maps)) return false;
+    e.w = w;
+    e.s = s;
+    e.b = b;
+    e.K = K;
+    e.N = N;
+    e.maps = *maps;
+    e.used = true;
+    return true;
+}
+
 // Launches the main kernel and the epilogue with the given scratch.  Returns a CUDA error code.
 template <int BITS, int MP, int TB>
 cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x, int M, int K,
@@ -763,7 +797,7 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
     q38_status st = ensure_zero_region(ctx, 0, static_cast<size_t>(M) * N, &cnt, &part);
     if (st != Q38_OK) return st;
     WeightMaps maps;
-    if (!make_maps<BITS>(w, s, b, K, N, &maps))
+    if (!cached_maps<BITS>(w, s, b, K, N, &maps))
         return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: tensor map encoding failed");
     const cudaError_t e = launch_kernels<BITS, MP, TB>(p, ctx->device, ctx->num_sms, x, M, K, maps,
                                                        b != nullptr, N, y, part, ctx->d_status, ctx->stream);
@@ -872,7 +906,7 @@ q38_status launch_noalloc(uint8_t* scratch, int device, int num_sms, const void*
         return Q38_ERR_CUDA;
     }
     WeightMaps maps;
-    if (!make_maps<BITS>(w, s, b, K, N, &maps)) return Q38_ERR_CUDA;
+    if (!cached_maps<BITS>(w, s, b, K, N, &maps)) return Q38_ERR_CUDA;
     const cudaError_t e = launch_kernels<BITS, MP, TB>(p, device, num_sms, x, M, K, maps, b != nullptr, N,
                                                        y, part, status, stream);
     if (e != cudaSuccess) {

@@ -106,10 +106,24 @@ def context(device: int | torch.device | None = None) -> int:
     return h
 
 
+_tls = threading.local()
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _bind(t: torch.Tensor) -> int:
-    ctx = context(t.device)
-    _lib.q38_ctx_set_stream(ctx, torch.cuda.current_stream(t.device).cuda_stream)
-    return ctx
+    """This thread's context for t's device, bound to the current torch stream."""
+    dev = t.get_device()
+    slots = getattr(_tls, "slots", None)
+    if slots is None:
+        slots = _tls.slots = {}
+    ent = slots.get(dev)
+    if ent is None:
+        ent = slots[dev] = [context(dev), None]
+    stream = _raw_stream(dev) if _raw_stream is not None else torch.cuda.current_stream(t.device).cuda_stream
+    if stream != ent[1]:
+        _lib.q38_ctx_set_stream(ent[0], stream)
+        ent[1] = stream
+    return ent[0]
 
 
 def _check(ctx: int, st: int) -> None:
@@ -124,6 +138,11 @@ def check_device(device=None) -> None:
     """Synchronise and raise if a kernel reported a timeout or an out-of-range index."""
     ctx = context(device)
     _lib.q38_ctx_set_stream(ctx, torch.cuda.current_stream(device).cuda_stream)
+    slots = getattr(_tls, "slots", None)
+    if slots:  # the context's stream was set here, not by _bind: bind again next time
+        for ent in slots.values():
+            if ent[0] == ctx:
+                ent[1] = None
     _check(ctx, _lib.q38_ctx_check_device(ctx))
 
 
