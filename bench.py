@@ -131,6 +131,52 @@ def build_case_weights(torch, O, dev, bits, N, K, seed, copies=1):
     return out
 
 
+# ------------------------------------------------------------------------ gate/up
+def run_gate_up(torch, q38, O, dev, stream, quick=False):
+    """Gate and up projections of the dense MLP at decode (4-bit, 17408x5120 each, M 1 and 8):
+    q38_quantized_gate_up (one pass over both weights, SiLU-gate in the epilogue) against
+    the same work as two products and the SiLU product.  CUDA-graph replays over 4 weight
+    pairs (357 MB, more than L2), CUDA events."""
+    N, K, bits, copies = 17408, 5120, 4, 4
+    gw = build_case_weights(torch, O, dev, bits, N, K, 6101, copies)
+    uw = build_case_weights(torch, O, dev, bits, N, K, 6102, copies)
+    nbytes = 2 * (N * K * bits // 8 + N * (K // GROUP) * 4)
+    out = {}
+    reps = 40 if quick else 200
+    for M in (1, 8):
+        x = torch.randn((M, K), device=dev).to(torch.bfloat16)
+
+        def fused():
+            for i in range(reps):
+                q38.quantized_gate_up(x, gw[i % copies], uw[i % copies], GROUP, bits)
+
+        def separate():
+            for i in range(reps):
+                q38.silu_mul(q38.quantized_matmul(x, *gw[i % copies], True, GROUP, bits),
+                             q38.quantized_matmul(x, *uw[i % copies], True, GROUP, bits))
+
+        res = {}
+        for name, fn in (("fused", fused), ("separate", separate)):
+            fn()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                fn()
+            g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            res[name] = e0.elapsed_time(e1) * 1e3 / reps
+            del g
+        out[str(M)] = {"fused_us": round(res["fused"], 2), "separate_us": round(res["separate"], 2),
+                       "fused_GBps": round(nbytes / (res["fused"] * 1e-6) / 1e9, 1)}
+    return {"workload": "MLP gate+up at decode: 4-bit g64, gate and up 17408x5120, h = silu(gate) * up",
+            "bytes_per_call": nbytes, "per_M": out}
+
+
 # ----------------------------------------------------------------------------- MoE
 MOE = {"H": 2048, "I": 512, "E": 512, "k": 10, "bits": 3}
 MOE_T = [1, 8, 64, 4096]
@@ -575,6 +621,7 @@ def run_ours(args, rank, world, local_rank):
     else:
         moe = None if args.skip_moe else run_moe(torch, q38, dev, stream, world, dist, args.quick)
         prefill = None if args.skip_prefill else run_prefill(torch, q38, dev, stream, world, dist, args.quick)
+    gate_up = None if (args.skip_prefill or world > 1) else run_gate_up(torch, q38, O, dev, stream, args.quick)
 
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
@@ -606,6 +653,7 @@ def run_ours(args, rank, world, local_rank):
         "cases": per_case,
         "moe": moe,
         "prefill": prefill,
+        "gate_up": gate_up,
     }
     return line
 

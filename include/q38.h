@@ -244,6 +244,21 @@ Q38_API q38_status q38_moe_ep_pack(q38_ctx* ctx, const void* x, int64_t H, const
 Q38_API q38_status q38_moe_ep_reduce(q38_ctx* ctx, const void* partial, int64_t H, const int32_t* rowpos, int64_t T,
                                      int world, void* out);
 
+/* Gate and up projections of a gated MLP in one call:
+ *   h[M, N] = bf16( silu(bf16(x . dequant(Wg)^T)) * bf16(x . dequant(Wu)^T) ),
+ * the `silu(gate(x)) * up(x)` of the reference's MLPs (the fused gate/up pattern of
+ * Sources/Qwen38Core/FlashNext/Qwen4ExpFusion.swift:158-186; the shared expert and the
+ * dense Qwen3.5 MLP), with the rounding of two bf16 QuantizedLinear outputs followed by the
+ * SiLU product.  Wg and Wu are two packed weights of the same shape [N, K*bits/32] with
+ * their own scales/biases (both biased or neither).  For M <= 16 tokens (decode) one
+ * streaming pass reads both weights and applies the SiLU-gate in its epilogue; larger M
+ * runs the two products and the SiLU product in sequence. */
+Q38_API q38_status q38_quantized_gate_up(q38_ctx* ctx, const void* x, int64_t M, int64_t K, q38_dtype x_dtype,
+                                         const uint32_t* w_gate, const void* s_gate, const void* b_gate,
+                                         const uint32_t* w_up, const void* s_up, const void* b_up,
+                                         q38_dtype scales_dtype, int64_t N, int group_size, int bits,
+                                         q38_mode mode, void* h);
+
 /* Allocation-free decode product.  No counterpart in the reference: it exists for
  * callers that must not allocate device memory on the calling path (a host framework
  * that owns all device memory and hands a plugin only its input and output buffers, or

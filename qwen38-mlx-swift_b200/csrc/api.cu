@@ -261,6 +261,36 @@ q38_status q38_quantized_matmul(q38_ctx* ctx, const void* x, int64_t M, int64_t 
 
 
 
+q38_status q38_quantized_gate_up(q38_ctx* ctx, const void* x, int64_t M, int64_t K, q38_dtype x_dtype,
+                                 const uint32_t* w_gate, const void* s_gate, const void* b_gate,
+                                 const uint32_t* w_up, const void* s_up, const void* b_up, q38_dtype scales_dtype,
+                                 int64_t N, int group_size, int bits, q38_mode mode, void* h) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    q38_status st = check_format(ctx, "quantized_gate_up", K, group_size, bits, mode);
+    if (st != Q38_OK) return st;
+    if (x_dtype != Q38_BF16) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "quantized_gate_up: x must be bf16");
+    if (!valid_dtype(scales_dtype)) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "quantized_gate_up: bad scales dtype");
+    if (M < 0 || N <= 0) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "quantized_gate_up: bad shape M=%lld N=%lld", (long long)M, (long long)N);
+    if (M == 0) return Q38_OK;
+    if (!x || !w_gate || !s_gate || !w_up || !s_up || !h)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "quantized_gate_up: null pointer");
+    if ((b_gate == nullptr) != (b_up == nullptr))
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "quantized_gate_up: gate and up must both have biases or neither");
+    if ((st = set_device(ctx)) != Q38_OK) return st;
+    if (qgemv_fast_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w_gate, s_gate, b_gate, h) &&
+        qgemv_fast_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w_up, s_up, b_up, h))
+        return qgemv_gate_up_fast(ctx, x, M, K, w_gate, s_gate, b_gate, w_up, s_up, b_up, N, bits, h);
+    // otherwise: gate product into h, up product into the auxiliary buffer, then h = silu(h) * up
+    void* up = nullptr;
+    if ((st = ensure_aux(ctx, static_cast<size_t>(M) * N * 2, &up)) != Q38_OK) return st;
+    if ((st = q38_quantized_matmul(ctx, x, M, K, x_dtype, w_gate, s_gate, b_gate, scales_dtype, N, 1, group_size,
+                                   bits, mode, h)) != Q38_OK ||
+        (st = q38_quantized_matmul(ctx, x, M, K, x_dtype, w_up, s_up, b_up, scales_dtype, N, 1, group_size, bits,
+                                   mode, up)) != Q38_OK)
+        return st;
+    return q38_silu_mul(ctx, h, up, M * N, h);
+}
+
 q38_status q38_dequantize(q38_ctx* ctx, const uint32_t* w, const void* scales, const void* biases,
                           q38_dtype scales_dtype, int64_t rows, int64_t K, int group_size, int bits,
                           q38_mode mode, void* out, q38_dtype out_dtype) {

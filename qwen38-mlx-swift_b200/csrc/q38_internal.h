@@ -72,6 +72,11 @@ bool qgemv_fast_supported(int64_t M, int64_t K, int group, int bits, q38_dtype x
                           const void* b, const void* y);
 q38_status qgemv_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w,
                       const void* s, const void* b, int64_t N, int bits, void* y);
+// h = bf16(silu(x.Wg^T) * (x.Wu^T)) in one decode pass (same conditions as qgemv_fast for
+// both weights, which must both have biases or neither).
+q38_status qgemv_gate_up_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* wg,
+                              const void* sg, const void* bg, const uint32_t* wu, const void* su, const void* bu,
+                              int64_t N, int bits, void* h);
 
 // Prompt-shaped product on the tensor cores (M >= 17, group 64, K % 128 == 0, bits 2/3/4,
 // bf16).  Uses the scratch workspace for the permuted activations (M*K bf16).

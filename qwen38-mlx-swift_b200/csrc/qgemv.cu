@@ -214,12 +214,15 @@ struct WeightMaps {
     CUtensorMap codes16, codes64, scales, biases;
 };
 
+// The tiles cover one weight of N rows, or two (gate and up of an MLP): tiles [0, tiles_a)
+// are rows of the first, the rest rows of the second, whose partial sums go to workspace
+// columns [N, 2N) (row length ld = N or 2N).
 struct MainArgs {
     const __nv_bfloat16* x;
     __nv_bfloat16* y;
     float* ws;
     uint32_t* status;
-    int M, N, K, C, tiles, stages, stage_bytes, has_bias;
+    int M, N, K, C, tiles, tiles_a, ld, stages, stage_bytes, has_bias;
 };
 
 // Accumulator columns.  An m16n8k16 product has 8 columns; with MP (1, 2, 4 or 8) token
@@ -236,7 +239,9 @@ template <int MP, int TB>
 __device__ __forceinline__ void flush_subtile(float (&acc)[TB][4], int tile, int warp, const MainArgs& a,
                                               int lane) {
     const int g = lane >> 2, t = lane & 3;
-    const int r0 = tile * 64 + warp * 16 + g;
+    const bool second = tile >= a.tiles_a;
+    const int r0 = (second ? tile - a.tiles_a : tile) * 64 + warp * 16 + g;  // row within its weight
+    float* ws = a.ws + (second ? a.N : 0);
 #pragma unroll
     for (int tb = 0; tb < TB; ++tb) {
         if (MP == 1) {  // every column is token 0
@@ -246,8 +251,8 @@ __device__ __forceinline__ void flush_subtile(float (&acc)[TB][4], int tile, int
             v0 += __shfl_xor_sync(0xffffffffu, v0, 2);
             v2 += __shfl_xor_sync(0xffffffffu, v2, 2);
             if (t == 0) {
-                if (r0 < a.N) atomicAdd(a.ws + r0, v0);
-                if (r0 + 8 < a.N) atomicAdd(a.ws + r0 + 8, v2);
+                if (r0 < a.N) atomicAdd(ws + r0, v0);
+                if (r0 + 8 < a.N) atomicAdd(ws + r0 + 8, v2);
             }
             continue;
         }
@@ -263,7 +268,7 @@ __device__ __forceinline__ void flush_subtile(float (&acc)[TB][4], int tile, int
             for (int e = 0; e < 4; ++e) {
                 const int r = r0 + ((e >> 1) << 3);
                 const int m = tb * 8 + (2 * t + (e & 1)) % MP;
-                if (r < a.N && m < a.M) atomicAdd(a.ws + static_cast<size_t>(m) * a.N + r, v[e]);
+                if (r < a.N && m < a.M) atomicAdd(ws + static_cast<size_t>(m) * a.ld + r, v[e]);
             }
         }
     }
@@ -286,8 +291,27 @@ __global__ void __launch_bounds__(256) qgemv_epilogue(float* __restrict__ ws, __
 constexpr int ZERO_OFF = 1024, ZERO_BYTES = 2048, RING_OFF = 3072;
 constexpr int MAX_DYN_SMEM = 226 * 1024;  // 227 KiB per CTA less the static per-group sums
 
+// Gate/up epilogue: h = bf16(silu(g) * u) with g = bf16(gate sums), u = bf16(up sums),
+// the rounding of an MLP whose gate and up projections return bf16; the sums [M][2N]
+// are returned to zero.
+__global__ void __launch_bounds__(256) qgemv_epilogue_glu(float* __restrict__ ws, __nv_bfloat16* __restrict__ h,
+                                                          int N, int total) {
+    griddep_launch_dependents();
+    griddep_wait();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const int m = i / N, n = i - m * N;
+        float* wg = ws + static_cast<size_t>(m) * 2 * N + n;
+        const float g = bf16_bits_to_f32(f32_to_bf16_bits(__ldcg(wg)));
+        const float u = bf16_bits_to_f32(f32_to_bf16_bits(__ldcg(wg + N)));
+        h[i] = __float2bfloat16_rn(g / (1.0f + expf(-g)) * u);
+        __stcg(wg, 0.0f);
+        __stcg(wg + N, 0.0f);
+    }
+}
+
 template <int BITS, int MP, int TB>
 __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 1 ? 2 : 1)) qgemv_main(const __grid_constant__ WeightMaps maps,
+                                                                      const __grid_constant__ WeightMaps maps_b,
                                                                       const MainArgs a) {
     using F = Fmt<BITS>;
     constexpr int GPER = 8 / MP;                 // groups sharing one accumulator set
@@ -352,6 +376,12 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
             prefetch_tensormap(&maps.codes64);
             prefetch_tensormap(&maps.scales);
             if (a.has_bias) prefetch_tensormap(&maps.biases);
+            if (a.tiles_a < a.tiles) {
+                prefetch_tensormap(&maps_b.codes16);
+                prefetch_tensormap(&maps_b.codes64);
+                prefetch_tensormap(&maps_b.scales);
+                if (a.has_bias) prefetch_tensormap(&maps_b.biases);
+            }
             int chunk = st_first / a.tiles, tile = st_first % a.tiles;
             int slot = 0;
             uint32_t ph = 0;
@@ -360,31 +390,34 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
                 const int sub_lo = i == 0 ? lo_first : 0;
                 const int sub_hi = i == nst - 1 ? hi_last : 4;
                 uint8_t* sbase = stage0 + static_cast<size_t>(slot) * a.stage_bytes;
+                const bool second = tile >= a.tiles_a;
+                const WeightMaps& wm = second ? maps_b : maps;
+                const int lt = second ? tile - a.tiles_a : tile;  // tile within its weight
                 // whole 64-row tiles inside the matrix in one box per column range,
                 // otherwise one 16-row box per active subtile
-                const bool whole = sub_lo == 0 && sub_hi == 4 && tile * 64 + 64 <= a.N;
+                const bool whole = sub_lo == 0 && sub_hi == 4 && lt * 64 + 64 <= a.N;
                 int nact = 0;
-                for (int s = sub_lo; s < sub_hi; ++s) nact += (tile * 64 + 16 * s < a.N);
+                for (int s = sub_lo; s < sub_hi; ++s) nact += (lt * 64 + 16 * s < a.N);
                 if (whole) nact = 4;
                 const uint32_t bytes = nact * F::SUB_BYTES + 1024 + (a.has_bias ? 1024 : 0);
                 mbar_arrive_expect_tx(&full[slot], bytes);
                 if (whole) {
 #pragma unroll
                     for (int bx = 0; bx < F::BOXES; ++bx)
-                        tma_load_2d(sbase + bx * 64 * F::SW, &maps.codes64, &full[slot],
-                                    chunk * F::ROW_WORDS + bx * (F::SW / 4), tile * 64);
+                        tma_load_2d(sbase + bx * 64 * F::SW, &wm.codes64, &full[slot],
+                                    chunk * F::ROW_WORDS + bx * (F::SW / 4), lt * 64);
                 } else {
                     for (int s = sub_lo; s < sub_hi; ++s) {
-                        if (tile * 64 + 16 * s >= a.N) continue;
+                        if (lt * 64 + 16 * s >= a.N) continue;
 #pragma unroll
                         for (int bx = 0; bx < F::BOXES; ++bx)
-                            tma_load_2d(sbase + bx * 64 * F::SW + s * 16 * F::SW, &maps.codes16, &full[slot],
-                                        chunk * F::ROW_WORDS + bx * (F::SW / 4), tile * 64 + 16 * s);
+                            tma_load_2d(sbase + bx * 64 * F::SW + s * 16 * F::SW, &wm.codes16, &full[slot],
+                                        chunk * F::ROW_WORDS + bx * (F::SW / 4), lt * 64 + 16 * s);
                     }
                 }
                 uint8_t* sc = sbase + NCW * F::SUB_BYTES;
-                tma_load_2d(sc, &maps.scales, &full[slot], chunk * GROUPS, tile * 64);
-                if (a.has_bias) tma_load_2d(sc + 1024, &maps.biases, &full[slot], chunk * GROUPS, tile * 64);
+                tma_load_2d(sc, &wm.scales, &full[slot], chunk * GROUPS, lt * 64);
+                if (a.has_bias) tma_load_2d(sc + 1024, &wm.biases, &full[slot], chunk * GROUPS, lt * 64);
                 if (++slot == a.stages) {
                     slot = 0;
                     ph ^= 1;
@@ -482,7 +515,8 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
             }
         }
         const bool mine = own == wgrp;
-        const bool active = mine && sw_i >= sub_lo && sw_i < sub_hi && tile * 64 + 16 * sw_i < a.N;
+        const int lt = tile >= a.tiles_a ? tile - a.tiles_a : tile;  // tile within its weight
+        const bool active = mine && sw_i >= sub_lo && sw_i < sub_hi && lt * 64 + 16 * sw_i < a.N;
         if (mine && !mbar_wait(&full[slot], ph, a.status)) return;
         float acc[TB][4];
         if (active) {
@@ -635,10 +669,10 @@ struct Plan {
 };
 
 template <int BITS>
-bool make_plan(int M, int K, int N, Plan& p) {
+bool make_plan(int M, int K, int N, Plan& p, bool two_weights = false) {
     using F = Fmt<BITS>;
     p.C = K / KC;
-    p.tiles = (N + 63) / 64;
+    p.tiles = (N + 63) / 64 * (two_weights ? 2 : 1);
     if (static_cast<long long>(p.tiles) * p.C * 4 >= (1LL << 31)) return false;
     p.stage_bytes = NCW * F::SUB_BYTES + 2048;  // a multiple of 1 KiB
     const int xbytes = 2 * (M * F::XF_PER_M + 16) + M * KC * 2;  // fragment slots + staging copy of x
@@ -708,8 +742,11 @@ bool cached_maps(const uint32_t* w, const void* s, const void* b, int K, int N, 
 
 // Launches the main kernel and the epilogue with the given scratch.  Returns a CUDA error code.
 template <int BITS, int MP, int TB>
+// With `maps_b` the tiles cover two weights of N rows each (gate, then up) and the epilogue
+// writes y = bf16(silu(gate) * up) [M, N]; the partial sums then take M x 2N floats.
 cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x, int M, int K,
-                           const WeightMaps& maps, bool has_bias, int N, void* y, float* part, uint32_t* status, cudaStream_t stream) {
+                           const WeightMaps& maps, bool has_bias, int N, void* y, float* part, uint32_t* status,
+                           cudaStream_t stream, const WeightMaps* maps_b = nullptr) {
     auto kmain = qgemv_main<BITS, MP, TB>;
     // per template instance and device: smem opt-in and occupancy at the largest ring
     static std::mutex mu;
@@ -759,6 +796,8 @@ cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x
     args.K = K;
     args.C = p.C;
     args.tiles = p.tiles;
+    args.tiles_a = maps_b ? p.tiles / 2 : p.tiles;
+    args.ld = maps_b ? 2 * N : N;
     args.stages = p.stages;
     args.stage_bytes = p.stage_bytes;
     args.has_bias = has_bias;
@@ -770,7 +809,7 @@ cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kmain, maps, args);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kmain, maps, maps_b ? *maps_b : maps, args);
     if (e != cudaSuccess) return e;
 
     const int total = M * N;
@@ -782,7 +821,8 @@ cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x
     ecfg.stream = stream;
     ecfg.attrs = attr;
     ecfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&ecfg, qgemv_epilogue, part, static_cast<__nv_bfloat16*>(y), total);
+    e = maps_b ? cudaLaunchKernelEx(&ecfg, qgemv_epilogue_glu, part, static_cast<__nv_bfloat16*>(y), N, total)
+               : cudaLaunchKernelEx(&ecfg, qgemv_epilogue, part, static_cast<__nv_bfloat16*>(y), total);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
@@ -804,6 +844,28 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
     if (e != cudaSuccess) {
         cudaGetLastError();
         return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: launch failed: %s", cudaGetErrorString(e));
+    }
+    return Q38_OK;
+}
+
+// Gate and up projections of an MLP in one pass: h = bf16(silu(x.Wg^T) * (x.Wu^T)).
+template <int BITS, int MP, int TB>
+q38_status launch_gate_up(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* wg, const void* sg,
+                          const void* bg, const uint32_t* wu, const void* su, const void* bu, int N, void* h) {
+    Plan p;
+    if (!make_plan<BITS>(M, K, N, p, true)) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_gate_up: shape too large");
+    uint32_t* cnt = nullptr;
+    float* part = nullptr;
+    q38_status st = ensure_zero_region(ctx, 0, static_cast<size_t>(M) * 2 * N, &cnt, &part);
+    if (st != Q38_OK) return st;
+    WeightMaps mg, mu;
+    if (!cached_maps<BITS>(wg, sg, bg, K, N, &mg) || !cached_maps<BITS>(wu, su, bu, K, N, &mu))
+        return fail(ctx, Q38_ERR_CUDA, "quantized_gate_up: tensor map encoding failed");
+    const cudaError_t e = launch_kernels<BITS, MP, TB>(p, ctx->device, ctx->num_sms, x, M, K, mg, bg != nullptr, N, h,
+                                                       part, ctx->d_status, ctx->stream, &mu);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(ctx, Q38_ERR_CUDA, "quantized_gate_up: launch failed: %s", cudaGetErrorString(e));
     }
     return Q38_OK;
 }
@@ -848,6 +910,25 @@ q38_status qgemv_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const u
         case 8: return go(std::integral_constant<int, 8>());
     }
     return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: bits %d not on the fast path", bits);
+}
+
+q38_status qgemv_gate_up_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* wg,
+                              const void* sg, const void* bg, const uint32_t* wu, const void* su, const void* bu,
+                              int64_t N, int bits, void* h) {
+    const int m = static_cast<int>(M), k = static_cast<int>(K), n = static_cast<int>(N);
+    auto go = [&](auto bits_c) {
+        constexpr int B = decltype(bits_c)::value;
+        return dispatch_m<B>(m, [&](auto mp, auto tb) {
+            return launch_gate_up<B, decltype(mp)::value, decltype(tb)::value>(ctx, x, m, k, wg, sg, bg, wu, su, bu, n, h);
+        });
+    };
+    switch (bits) {
+        case 2: return go(std::integral_constant<int, 2>());
+        case 3: return go(std::integral_constant<int, 3>());
+        case 4: return go(std::integral_constant<int, 4>());
+        case 8: return go(std::integral_constant<int, 8>());
+    }
+    return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_gate_up: bits %d not on the fast path", bits);
 }
 
 // ---------------------------------------------------------------------------------

@@ -54,6 +54,7 @@ _sig("q38_ctx_workspace_bytes", [_P], _S)
 _sig("q38_ctx_check_device", [_P])
 _sig("q38_last_error", [_P], C.c_char_p)
 _sig("q38_quantized_matmul", [_P, _P, _I, _I, _i, _P, _P, _P, _i, _I, _i, _i, _i, _i, _P])
+_sig("q38_quantized_gate_up", [_P, _P, _I, _I, _i, _P, _P, _P, _P, _P, _P, _i, _I, _i, _i, _i, _P])
 _sig("q38_gather_quantized_matmul",
      [_P, _P, _I, _I, _I, _i, _P, _P, _P, _i, _I, _I, _P, _P, _I, _i, _i, _i, _i, _i, _P])
 _sig("q38_dequantize", [_P, _P, _P, _P, _i, _I, _I, _i, _i, _i, _P, _i])
@@ -191,6 +192,34 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
                                           _ptr(biases), _DTYPE[scales.dtype], N, int(transpose),
                                           group_size, bits, 0, _ptr(y)))
     return y
+
+
+def quantized_gate_up(x: torch.Tensor, gate, up, group_size: int = 64, bits: int = 4,
+                      mode: str = "affine") -> torch.Tensor:
+    """silu(gate(x)) * up(x) of a gated MLP, each projection a bf16 QuantizedLinear
+    (transpose=true): gate and up are (w, scales, biases) triples of one shape.  Decode-sized
+    x (<= 16 tokens) reads both weights in one pass with the SiLU-gate in its epilogue."""
+    if mode != "affine":
+        raise Q38Error(2, f"mode {mode!r} is not implemented")
+    wg, sg, bg = gate
+    wu, su, bu = up
+    for t, n in ((x, "x"), (wg, "gate w"), (sg, "gate scales"), (wu, "up w"), (su, "up scales")):
+        _need(t, n)
+    for t, n in ((bg, "gate biases"), (bu, "up biases")):
+        if t is not None:
+            _need(t, n)
+    wg, wu = _as_u32(wg), _as_u32(wu)
+    if wg.shape != wu.shape or sg.shape != su.shape:
+        raise ValueError("quantized_gate_up: gate and up weights must have one shape")
+    K = x.shape[-1]
+    N = wg.shape[0]
+    M = x.numel() // K if K else 0
+    h = torch.empty(x.shape[:-1] + (N,), dtype=x.dtype, device=x.device)
+    ctx = _bind(x)
+    _check(ctx, _lib.q38_quantized_gate_up(ctx, _ptr(x), M, K, _DTYPE[x.dtype], _ptr(wg), _ptr(sg), _ptr(bg),
+                                           _ptr(wu), _ptr(su), _ptr(bu), _DTYPE[sg.dtype], N, group_size, bits,
+                                           0, _ptr(h)))
+    return h
 
 
 def gather_qmm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,

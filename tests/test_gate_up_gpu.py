@@ -1,0 +1,115 @@
+"""GPU parity of q38_quantized_gate_up: h = bf16(silu(bf16(x.Wg^T)) * bf16(x.Wu^T)).
+
+Checked against (1) the same computation composed from the existing operators
+(quantized_matmul twice, then silu_mul): the fused decode pass sums the fp32 partials in
+a different order than two separate products, so a bf16 output may differ by one
+representable step; bar max|h - h_ref| <= 2e-2 * RMS(h_ref) + one bf16 step of |h_ref|,
+the bar of the SwitchGLU tests.  (2) The CPU oracle's two products passed through the
+same roundings: g and u may each differ from the oracle by the product bar (2e-2 * RMS
+plus one bf16 step), and h = silu(g) * u carries both, so each element of h must lie
+within those input errors propagated to first order,
+  |silu'(g) * u| * (2e-2 RMS(g) + step(g)) + |silu(g)| * (2e-2 RMS(u) + step(u)) + step(h),
+and the RMS of the error must stay below 1e-2 * RMS(h).  Repeated calls must give the same
+result (the partial-sum workspace is returned to zero by every call).
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from test_qmm_gpu import dev_bf16, dev_u32, host_bf16, make_weight
+
+pytestmark = pytest.mark.gpu
+
+
+def bf16_round(a):
+    return O.bf16_to_f32(O.f32_to_bf16(np.asarray(a, np.float32))).astype(np.float64)
+
+
+def check_h(h, ref):
+    h = O.bf16_to_f32(h).astype(np.float64)
+    ref = np.asarray(ref, np.float64)
+    rms = np.sqrt((ref ** 2).mean())
+    step = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(ref), 2.0 ** -126))) - 7)
+    assert np.isfinite(h).all()
+    excess = (np.abs(h - ref) - step).max()
+    assert excess <= 2e-2 * rms, f"max excess {excess:.4g} > 2e-2 * rms {rms:.4g}"
+
+
+def step_of(v):
+    return 2.0 ** (np.floor(np.log2(np.maximum(np.abs(v), 2.0 ** -126))) - 7)
+
+
+def check_oracle(h, gu):
+    g, u = gu
+    sig = 1.0 / (1.0 + np.exp(-g))
+    ref = g * sig * u
+    dsilu = sig * (1.0 + g * (1.0 - sig))
+    rms_g, rms_u = np.sqrt((g ** 2).mean()), np.sqrt((u ** 2).mean())
+    bound = (np.abs(dsilu * u) * (2e-2 * rms_g + step_of(g)) + np.abs(g * sig) * (2e-2 * rms_u + step_of(u))
+             + step_of(ref))
+    h = O.bf16_to_f32(h).astype(np.float64)
+    assert np.isfinite(h).all()
+    worst = (np.abs(h - ref) / bound).max()
+    assert worst <= 1.0, f"an element exceeds its propagated bound by {worst:.3g}x"
+    rms = np.sqrt((ref ** 2).mean())
+    erms = np.sqrt(((h - ref) ** 2).mean())
+    assert erms <= 1e-2 * rms, f"error rms {erms:.4g} > 1e-2 * rms {rms:.4g}"
+
+
+def oracle_gate_up(x, gate, up, bits):
+    g = bf16_round(O.qmm(x, *gate, 64, bits, f32=True))
+    u = bf16_round(O.qmm(x, *up, 64, bits, f32=True))
+    return g, u
+
+
+def run(q38, bits, M, N, K, biased=True, seed=0):
+    gate = make_weight(300 + seed + bits, N, K, bits)
+    up = make_weight(400 + seed + bits, N, K, bits)
+    if not biased:
+        gate, up = (gate[0], gate[1], None), (up[0], up[1], None)
+    x = O.normal_bf16(500 + seed + M, (M, K))
+    dg = (dev_u32(gate[0]), dev_bf16(gate[1]), None if gate[2] is None else dev_bf16(gate[2]))
+    du = (dev_u32(up[0]), dev_bf16(up[1]), None if up[2] is None else dev_bf16(up[2]))
+    dx = dev_bf16(x)
+    h = q38.quantized_gate_up(dx, dg, du, 64, bits)
+    h2 = q38.quantized_gate_up(dx, dg, du, 64, bits)
+    comp = q38.silu_mul(q38.quantized_matmul(dx, *dg, True, 64, bits), q38.quantized_matmul(dx, *du, True, 64, bits))
+    torch.cuda.synchronize()
+    q38.check_device()
+    return x, gate, up, host_bf16(h), host_bf16(h2), host_bf16(comp)
+
+
+@pytest.mark.parametrize("bits", [2, 3, 4, 8])
+@pytest.mark.parametrize("M", [1, 3, 8, 16])
+@pytest.mark.parametrize("NK", [(200, 512), (1000, 2048)])
+def test_gate_up_decode(q38, bits, M, NK):
+    N, K = NK
+    x, gate, up, h, h2, comp = run(q38, bits, M, N, K)
+    check_h(h, O.bf16_to_f32(comp))
+    check_h(h2, O.bf16_to_f32(comp))
+    check_oracle(h, oracle_gate_up(x, gate, up, bits))
+
+
+@pytest.mark.parametrize("bits", [4, 3])
+def test_gate_up_without_biases(q38, bits):
+    x, gate, up, h, h2, comp = run(q38, bits, 2, 384, 1024, biased=False, seed=7)
+    check_h(h, O.bf16_to_f32(comp))
+    check_oracle(h, oracle_gate_up(x, gate, up, bits))
+
+
+@pytest.mark.parametrize("bits", [2, 4])
+def test_gate_up_prompt_sized(q38, bits):
+    # 64 tokens: the two products and the SiLU product run in sequence
+    x, gate, up, h, h2, comp = run(q38, bits, 64, 512, 1024, seed=11)
+    assert np.array_equal(h, comp)
+    check_oracle(h, oracle_gate_up(x, gate, up, bits))
+
+
+def test_gate_up_rejects_mixed_biases(q38):
+    gate = make_weight(1, 128, 512, 4)
+    up = make_weight(2, 128, 512, 4)
+    dg = (dev_u32(gate[0]), dev_bf16(gate[1]), dev_bf16(gate[2]))
+    du = (dev_u32(up[0]), dev_bf16(up[1]), None)
+    with pytest.raises(ValueError):
+        q38.quantized_gate_up(dev_bf16(O.normal_bf16(3, (1, 512))), dg, du, 64, 4)
