@@ -244,6 +244,18 @@ Q38_API q38_status q38_moe_ep_pack(q38_ctx* ctx, const void* x, int64_t H, const
 Q38_API q38_status q38_moe_ep_reduce(q38_ctx* ctx, const void* partial, int64_t H, const int32_t* rowpos, int64_t T,
                                      int world, void* out);
 
+/* Quantized embedding lookup: out[t, :] = dequant(w, scales, biases)[ids[t], :] for
+ * t < n, the Qwen4ExpPrequantizedEmbedding.callAsFunction of
+ * Sources/Qwen38Core/FlashNext/Qwen4ExpPrequantized.swift:141-151 (rows gathered, then
+ * MLX.dequantized).  w [rows, K*bits/32] packed, scales/biases [rows, K/group_size];
+ * each output row equals that row of q38_dequantize bit for bit.  An id outside
+ * [0, rows) gives a zero row and is reported by q38_ctx_check_device.  The tied output
+ * projection (asLinear, :154-158) is q38_quantized_matmul with the same tensors. */
+Q38_API q38_status q38_quantized_embedding(q38_ctx* ctx, const int32_t* ids, int64_t n, const uint32_t* w,
+                                           const void* scales, const void* biases, q38_dtype scales_dtype,
+                                           int64_t rows, int64_t K, int group_size, int bits, q38_mode mode,
+                                           void* out, q38_dtype out_dtype);
+
 /* Gate and up projections of a gated MLP in one call:
  *   h[M, N] = bf16( silu(bf16(x . dequant(Wg)^T)) * bf16(x . dequant(Wu)^T) ),
  * the `silu(gate(x)) * up(x)` of the reference's MLPs (the fused gate/up pattern of

@@ -306,6 +306,22 @@ q38_status q38_dequantize(q38_ctx* ctx, const uint32_t* w, const void* scales, c
     return dequantize_launch(ctx, w, scales, biases, scales_dtype, rows, K, group_size, bits, out, out_dtype);
 }
 
+q38_status q38_quantized_embedding(q38_ctx* ctx, const int32_t* ids, int64_t n, const uint32_t* w,
+                                   const void* scales, const void* biases, q38_dtype scales_dtype, int64_t rows,
+                                   int64_t K, int group_size, int bits, q38_mode mode, void* out,
+                                   q38_dtype out_dtype) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    q38_status st = check_format(ctx, "quantized_embedding", K, group_size, bits, mode);
+    if (st != Q38_OK) return st;
+    if (!valid_dtype(scales_dtype) || !valid_dtype(out_dtype))
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "quantized_embedding: bad dtype");
+    if (n < 0 || rows <= 0) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "quantized_embedding: bad sizes");
+    if (n == 0) return Q38_OK;
+    if (!ids || !w || !scales || !out) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "quantized_embedding: null pointer");
+    if ((st = set_device(ctx)) != Q38_OK) return st;
+    return embedding_launch(ctx, ids, n, w, scales, biases, scales_dtype, rows, K, group_size, bits, out, out_dtype);
+}
+
 q38_status q38_quantize(q38_ctx* ctx, const void* w, q38_dtype w_dtype, int64_t rows, int64_t K,
                         int group_size, int bits, q38_mode mode, uint32_t* codes, void* scales,
                         void* biases, q38_dtype scales_dtype) {

@@ -70,6 +70,10 @@ bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, size_t elem_bytes, co
 bool qgemv_fast_supported(int64_t M, int64_t K, int group, int bits, q38_dtype xd,
                           q38_dtype sd, const void* x, const void* w, const void* s,
                           const void* b, const void* y);
+// Rows ids[0..n) of a packed table, dequantized (quant.cu).
+q38_status embedding_launch(q38_ctx* ctx, const int32_t* ids, int64_t n, const uint32_t* w, const void* s,
+                            const void* b, q38_dtype sd, int64_t rows, int64_t K, int group, int bits, void* out,
+                            q38_dtype od);
 q38_status qgemv_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w,
                       const void* s, const void* b, int64_t N, int bits, void* y);
 // h = bf16(silu(x.Wg^T) * (x.Wu^T)) in one decode pass (same conditions as qgemv_fast for

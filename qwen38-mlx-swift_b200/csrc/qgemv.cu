@@ -321,8 +321,15 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
     constexpr int SPLIT = (TB == 1 && MP <= 2 && UG == 2) ? 2 : 1;  // shorter MMA chains
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_align1024(smem_raw);
+    // Landing barriers: stage i signals full[i % (2 * stages)].  A parity wait only tells
+    // the awaited phase from its neighbours, so each waiter must be within one phase of
+    // the barrier.  With an odd ring a data slot alternates between the two consumer
+    // groups, and one group could reach a slot's next stage before the other group's
+    // stage in that slot had landed.  With 2 * stages landing barriers (an even period)
+    // every phase of a barrier belongs to the same group, which has waited for the
+    // previous phase itself, and the next phase cannot land before this one is consumed.
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + a.stages;
+    uint64_t* empty = full + 2 * a.stages;
     uint64_t* xfull = empty + a.stages;
     uint64_t* xempty = xfull + 2;
     const uint8_t* zeros = smem + ZERO_OFF;
@@ -354,6 +361,7 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
     if (threadIdx.x == 0) {
         for (int i = 0; i < a.stages; ++i) {
             mbar_init(&full[i], 1);
+            mbar_init(&full[a.stages + i], 1);
             mbar_init(&empty[i], NCW);
         }
         for (int i = 0; i < 2; ++i) {
@@ -383,13 +391,20 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
                 if (a.has_bias) prefetch_tensormap(&maps_b.biases);
             }
             int chunk = st_first / a.tiles, tile = st_first % a.tiles;
-            int slot = 0;
+            int slot = 0, fslot = 0;
             uint32_t ph = 0;
             for (int i = 0; i < nst; ++i) {
-                if (i >= a.stages && !mbar_wait(&empty[slot], ph ^ 1, a.status)) return;
+                if (i >= a.stages && !mbar_wait(&empty[slot], ph ^ 1, a.status)) {
+                    // the consumers have given up: let the copies already issued land
+                    // before the CTA can exit (each wait is bounded)
+                    for (int j = i - a.stages; j < i; ++j)
+                        if (!mbar_wait(&full[j % (2 * a.stages)], (j / (2 * a.stages)) & 1, a.status)) break;
+                    return;
+                }
                 const int sub_lo = i == 0 ? lo_first : 0;
                 const int sub_hi = i == nst - 1 ? hi_last : 4;
                 uint8_t* sbase = stage0 + static_cast<size_t>(slot) * a.stage_bytes;
+                uint64_t* fb = &full[fslot];
                 const bool second = tile >= a.tiles_a;
                 const WeightMaps& wm = second ? maps_b : maps;
                 const int lt = second ? tile - a.tiles_a : tile;  // tile within its weight
@@ -400,28 +415,29 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
                 for (int s = sub_lo; s < sub_hi; ++s) nact += (lt * 64 + 16 * s < a.N);
                 if (whole) nact = 4;
                 const uint32_t bytes = nact * F::SUB_BYTES + 1024 + (a.has_bias ? 1024 : 0);
-                mbar_arrive_expect_tx(&full[slot], bytes);
+                mbar_arrive_expect_tx(fb, bytes);
                 if (whole) {
 #pragma unroll
                     for (int bx = 0; bx < F::BOXES; ++bx)
-                        tma_load_2d(sbase + bx * 64 * F::SW, &wm.codes64, &full[slot],
+                        tma_load_2d(sbase + bx * 64 * F::SW, &wm.codes64, fb,
                                     chunk * F::ROW_WORDS + bx * (F::SW / 4), lt * 64);
                 } else {
                     for (int s = sub_lo; s < sub_hi; ++s) {
                         if (lt * 64 + 16 * s >= a.N) continue;
 #pragma unroll
                         for (int bx = 0; bx < F::BOXES; ++bx)
-                            tma_load_2d(sbase + bx * 64 * F::SW + s * 16 * F::SW, &wm.codes16, &full[slot],
+                            tma_load_2d(sbase + bx * 64 * F::SW + s * 16 * F::SW, &wm.codes16, fb,
                                         chunk * F::ROW_WORDS + bx * (F::SW / 4), lt * 64 + 16 * s);
                     }
                 }
                 uint8_t* sc = sbase + NCW * F::SUB_BYTES;
-                tma_load_2d(sc, &wm.scales, &full[slot], chunk * GROUPS, lt * 64);
-                if (a.has_bias) tma_load_2d(sc + 1024, &wm.biases, &full[slot], chunk * GROUPS, lt * 64);
+                tma_load_2d(sc, &wm.scales, fb, chunk * GROUPS, lt * 64);
+                if (a.has_bias) tma_load_2d(sc + 1024, &wm.biases, fb, chunk * GROUPS, lt * 64);
                 if (++slot == a.stages) {
                     slot = 0;
                     ph ^= 1;
                 }
+                if (++fslot == 2 * a.stages) fslot = 0;
                 if (++tile == a.tiles) {
                     tile = 0;
                     ++chunk;
@@ -488,8 +504,8 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
     // per group: where this lane's B operand comes from (its fragments, or zeros)
     const uint8_t* pg[TB == 1 ? GROUPS : TB];
     int chunk = st_first / a.tiles, tile = st_first % a.tiles;
-    int slot = 0;
-    uint32_t ph = 0;
+    int slot = 0, fslot = 0;  // data slot i % stages, landing barrier i % (2 * stages)
+    uint32_t fph = 0;         // phase parity of the landing barrier
     int own = 0;  // i % WG
     for (int i = 0; i < nst; ++i) {
         const int sub_lo = i == 0 ? lo_first : 0;
@@ -517,7 +533,7 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
         const bool mine = own == wgrp;
         const int lt = tile >= a.tiles_a ? tile - a.tiles_a : tile;  // tile within its weight
         const bool active = mine && sw_i >= sub_lo && sw_i < sub_hi && lt * 64 + 16 * sw_i < a.N;
-        if (mine && !mbar_wait(&full[slot], ph, a.status)) return;
+        if (mine && !mbar_wait(&full[fslot], fph, a.status)) return;
         float acc[TB][4];
         if (active) {
             const uint8_t* sbase = stage0 + static_cast<size_t>(slot) * a.stage_bytes;
@@ -652,9 +668,10 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
         }
         if (active) flush_subtile<MP, TB>(acc, tile, sw_i, a, lane);
         if (++own == WG) own = 0;
-        if (++slot == a.stages) {
-            slot = 0;
-            ph ^= 1;
+        if (++slot == a.stages) slot = 0;
+        if (++fslot == 2 * a.stages) {
+            fslot = 0;
+            fph ^= 1;
         }
         if (++tile == a.tiles) {
             tile = 0;
@@ -680,7 +697,7 @@ bool make_plan(int M, int K, int N, Plan& p, bool two_weights = false) {
     // static sums) lets three CTAs (12 consumer warps) share an SM; 113 KiB two
     const int budget = (WG == 1 ? (M > 8 ? 113 : 76) : (M > 8 ? 226 : 113)) * 1024 - 1024 - RING_OFF - 1024 - xbytes;
     int stages = budget / p.stage_bytes;
-    if (stages > 8) stages = 8;
+    if (stages > 8) stages = 8;  // (the 3 * stages + 4 barriers then fit the first 1 KiB)
     if (stages < 2) stages = 2;
     int smem = 1024 + RING_OFF + stages * p.stage_bytes + xbytes;  // + alignment slack
     while (smem > MAX_DYN_SMEM && stages > 2) {

@@ -81,6 +81,32 @@ __global__ void dequant_kernel(const uint32_t* __restrict__ w, const ST* __restr
     }
 }
 
+// ------------------------------------------------------------------- embedding
+// out[t, :] = dequant(row ids[t]) with the arithmetic of dequant_kernel (so a gathered row
+// equals the dequantized table's row bit for bit).  An id outside [0, rows) yields a zero
+// row and sets the device status bit for an out-of-range index.
+template <typename ST, typename OT>
+__global__ void embed_kernel(const int32_t* __restrict__ ids, int64_t n, const uint32_t* __restrict__ w,
+                             const ST* __restrict__ s, const ST* __restrict__ b, int64_t rows, int64_t K,
+                             int group, int bits, OT* __restrict__ out, uint32_t* status) {
+    const int64_t total = n * K;
+    const int64_t kw = K * bits / 32, G = K / group;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t t = i / K, k = i % K;
+        const int64_t r = ids[t];
+        if (r < 0 || r >= rows) {
+            out[i] = from_f32<OT>(0.0f);
+            if (k == 0) atomicOr(status, Q38_DEV_BAD_INDEX);
+            continue;
+        }
+        const float sc = to_f32(s[r * G + k / group]);
+        const float bi = b ? to_f32(b[r * G + k / group]) : 0.0f;
+        const float q = static_cast<float>(get_code(w + r * kw, k, bits));
+        out[i] = from_f32<OT>(__fadd_rn(__fmul_rn(sc, q), bi));
+    }
+}
+
 // ---------------------------------------------------------------------- quantize
 // One thread per group.  MLX affine rule (MLX C++ 0.31 affine quantize, called through
 // mx.quantize at Scripts/qwen4-exp-requantize-experts.py:246-251): the extreme of larger
@@ -253,6 +279,31 @@ q38_status dequantize_launch(q38_ctx* ctx, const uint32_t* w, const void* s, con
     }
 #undef Q38_DQ
     return check_launch(ctx, "dequantize");
+}
+
+q38_status embedding_launch(q38_ctx* ctx, const int32_t* ids, int64_t n, const uint32_t* w, const void* s,
+                            const void* b, q38_dtype sd, int64_t rows, int64_t K, int group, int bits, void* out,
+                            q38_dtype od) {
+    const int grid = grid_for(n * K, 256);
+#define Q38_EM(ST, OT)                                                                            \
+    embed_kernel<ST, OT><<<grid, 256, 0, ctx->stream>>>(ids, n, w, static_cast<const ST*>(s),         \
+                                                        static_cast<const ST*>(b), rows, K, group, bits, \
+                                                        static_cast<OT*>(out), ctx->d_status)
+    if (sd == Q38_BF16) {
+        if (od == Q38_BF16) Q38_EM(__nv_bfloat16, __nv_bfloat16);
+        else if (od == Q38_F16) Q38_EM(__nv_bfloat16, __half);
+        else Q38_EM(__nv_bfloat16, float);
+    } else if (sd == Q38_F16) {
+        if (od == Q38_BF16) Q38_EM(__half, __nv_bfloat16);
+        else if (od == Q38_F16) Q38_EM(__half, __half);
+        else Q38_EM(__half, float);
+    } else {
+        if (od == Q38_BF16) Q38_EM(float, __nv_bfloat16);
+        else if (od == Q38_F16) Q38_EM(float, __half);
+        else Q38_EM(float, float);
+    }
+#undef Q38_EM
+    return check_launch(ctx, "quantized_embedding");
 }
 
 q38_status quantize_launch(q38_ctx* ctx, const void* w, q38_dtype wd, int64_t rows, int64_t K,

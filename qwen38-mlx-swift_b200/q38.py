@@ -54,6 +54,7 @@ _sig("q38_ctx_workspace_bytes", [_P], _S)
 _sig("q38_ctx_check_device", [_P])
 _sig("q38_last_error", [_P], C.c_char_p)
 _sig("q38_quantized_matmul", [_P, _P, _I, _I, _i, _P, _P, _P, _i, _I, _i, _i, _i, _i, _P])
+_sig("q38_quantized_embedding", [_P, _P, _I, _P, _P, _P, _i, _I, _I, _i, _i, _i, _P, _i])
 _sig("q38_quantized_gate_up", [_P, _P, _I, _I, _i, _P, _P, _P, _P, _P, _P, _i, _I, _i, _i, _i, _P])
 _sig("q38_gather_quantized_matmul",
      [_P, _P, _I, _I, _I, _i, _P, _P, _P, _i, _I, _I, _P, _P, _I, _i, _i, _i, _i, _i, _P])
@@ -192,6 +193,29 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
                                           _ptr(biases), _DTYPE[scales.dtype], N, int(transpose),
                                           group_size, bits, 0, _ptr(y)))
     return y
+
+
+def quantized_embedding(ids: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
+                        biases: torch.Tensor | None = None, group_size: int = 64, bits: int = 4,
+                        mode: str = "affine", out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """Prequantized embedding lookup: ids [...] (int32) -> [..., K] = dequant(w)[ids]."""
+    if mode != "affine":
+        raise Q38Error(2, f"mode {mode!r} is not implemented")
+    _need(ids, "ids"), _need(w, "w"), _need(scales, "scales")
+    if biases is not None:
+        _need(biases, "biases")
+    if ids.dtype != torch.int32:
+        raise ValueError("ids must be int32")
+    w = _as_u32(w)
+    rows = w.shape[0]
+    K = w.shape[-1] * 32 // bits
+    od = out_dtype or scales.dtype
+    out = torch.empty(tuple(ids.shape) + (K,), dtype=od, device=w.device)
+    ctx = _bind(w)
+    _check(ctx, _lib.q38_quantized_embedding(ctx, _ptr(ids), ids.numel(), _ptr(w), _ptr(scales), _ptr(biases),
+                                             _DTYPE[scales.dtype], rows, K, group_size, bits, 0, _ptr(out),
+                                             _DTYPE[od]))
+    return out
 
 
 def quantized_gate_up(x: torch.Tensor, gate, up, group_size: int = 64, bits: int = 4,
@@ -478,6 +502,28 @@ class QuantizedLinear:
         y = quantized_matmul(x, self.weight, self.scales, self.biases, True, self.group_size,
                              self.bits, self.mode)
         return y if self.bias is None else y + self.bias
+
+
+class QuantizedEmbedding:
+    """Qwen4ExpPrequantizedEmbedding (FlashNext/Qwen4ExpPrequantized.swift:108-160):
+    parameters `weight` (packed uint32 [count, dims*bits/32]), `scales`, `biases`;
+    callAsFunction gathers and dequantizes rows, asLinear is the tied output projection."""
+
+    def __init__(self, weight, scales, biases=None, group_size: int = 64, bits: int = 4, mode: str = "affine"):
+        self.weight, self.scales, self.biases = weight, scales, biases
+        self.group_size, self.bits, self.mode = group_size, bits, mode
+
+    @property
+    def shape(self):
+        return (self.weight.shape[0], self.weight.shape[-1] * 32 // self.bits)
+
+    def __call__(self, ids: torch.Tensor) -> torch.Tensor:
+        return quantized_embedding(ids.to(torch.int32).contiguous(), self.weight, self.scales, self.biases,
+                                   self.group_size, self.bits, self.mode)
+
+    def as_linear(self, x: torch.Tensor) -> torch.Tensor:
+        return quantized_matmul(x, self.weight, self.scales, self.biases, True, self.group_size, self.bits,
+                                self.mode)
 
 
 class HadamardQuantizedLinear(QuantizedLinear):
