@@ -74,12 +74,13 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_grouped(
     const __grid_constant__ CUtensorMap map_b1, const GArgs a) {
     using F = GF<BITS, XR>;
     constexpr int SX = F::X_STAGES, SW = F::W_STAGES;
+    static_assert(SW <= 8, "2 * SW landing barriers are laid out");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_align1024(smem_raw);
     uint64_t* x_full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* x_empty = x_full + 16;
-    uint64_t* w_full = x_empty + 16;
-    uint64_t* w_empty = w_full + 8;
+    uint64_t* w_full = x_empty + 16;  // landing barriers, 2 * SW
+    uint64_t* w_empty = w_full + 16;
     uint64_t* a_full = w_empty + 8;
     uint64_t* a_free = a_full + G_ASLOTS;
     uint64_t* d_full = a_free + G_ASLOTS;  // 2 accumulators
@@ -100,6 +101,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_grouped(
         }
         for (int i = 0; i < SW; ++i) {
             mbar_init(&w_full[i], 1);
+            mbar_init(&w_full[SW + i], 1);
             mbar_init(&w_empty[i], 4);
         }
         for (int i = 0; i < G_ASLOTS; ++i) {
@@ -179,18 +181,19 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_grouped(
                 const int r1 = GATE_UP ? r0 : r0 + 64;
                 uint8_t* st = wring + slot * F::W_STAGE;
                 const int k0 = ks * G_KS;
-                mbar_arrive_expect_tx(&w_full[slot], wbytes);
-                tma_load_2d(st, &map_c0, &w_full[slot], k0 * BITS / 32, r0);
-                tma_load_2d(st + F::CODE_B / 2, &map_c1, &w_full[slot], k0 * BITS / 32, r1);
-                tma_load_2d(st + F::CODE_B, &map_s0, &w_full[slot], (k0 / 512) * 8, r0);
-                tma_load_2d(st + F::CODE_B + 1024, &map_s1, &w_full[slot], (k0 / 512) * 8, r1);
+                uint64_t* wl = &w_full[gs % (2 * SW)];
+                mbar_arrive_expect_tx(wl, wbytes);
+                tma_load_2d(st, &map_c0, wl, k0 * BITS / 32, r0);
+                tma_load_2d(st + F::CODE_B / 2, &map_c1, wl, k0 * BITS / 32, r1);
+                tma_load_2d(st + F::CODE_B, &map_s0, wl, (k0 / 512) * 8, r0);
+                tma_load_2d(st + F::CODE_B + 1024, &map_s1, wl, (k0 / 512) * 8, r1);
                 if (a.has_bias) {
-                    tma_load_2d(st + F::CODE_B + 2048, &map_b0, &w_full[slot], (k0 / 512) * 8, r0);
-                    tma_load_2d(st + F::CODE_B + 3072, &map_b1, &w_full[slot], (k0 / 512) * 8, r1);
+                    tma_load_2d(st + F::CODE_B + 2048, &map_b0, wl, (k0 / 512) * 8, r0);
+                    tma_load_2d(st + F::CODE_B + 3072, &map_b1, wl, (k0 / 512) * 8, r1);
                 }
             }
             for (int i = 1; i <= (gs < SW ? gs : SW); ++i)
-                mbar_wait(&w_full[(gs - i) % SW], ((gs - i) / SW) & 1, a.status);
+                mbar_wait(&w_full[(gs - i) % (2 * SW)], ((gs - i) / (2 * SW)) & 1, a.status);
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
@@ -229,13 +232,19 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_grouped(
         }
     } else if (warp < G_WARP_EPI0) {
         // ------------------------------------------------------------------- dequant
+        // Set 0 dequantizes the even stages, set 1 the odd ones.
+        // Stage gs lands on w_full[gs % (2 * SW)].  A parity wait only tells neighbouring
+        // phases apart; with one landing barrier per slot and an odd ring a slot alternates
+        // between the two sets, and a set could pass the wait of a slot's next stage while
+        // the other set's stage in that slot was still landing.  With the even period each
+        // landing barrier serves one set, which has waited for its previous phase itself.
         const int set = (warp - G_WARP_DEQ0) >> 2;
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
         for (int gs = set; gs < total; gs += 2) {
             const int slot = gs % SW, as = gs % G_ASLOTS, ks = gs % ksteps;
-            if (!p_wait_warp<false>(&w_full[slot], (gs / SW) & 1, ab)) break;
+            if (!p_wait_warp<false>(&w_full[gs % (2 * SW)], (gs / (2 * SW)) & 1, ab)) break;
             const uint8_t* st = wring + slot * F::W_STAGE;
             const uint32_t* sb = reinterpret_cast<const uint32_t*>(st + F::CODE_B);
             const uint32_t s01 = sb[row * 4 + (ks & 3)];

@@ -93,12 +93,13 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
                                                         const PArgs a) {
     using F = PF<BITS, SB_TMA>;
     constexpr int SX = F::X_STAGES, SW = F::W_STAGES;
+    static_assert(SW <= 8, "2 * SW landing barriers are laid out");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_align1024(smem_raw);
     uint64_t* x_full = reinterpret_cast<uint64_t*>(smem);  // both CTAs' activation halves landed (leader)
     uint64_t* x_empty = x_full + 8;                        // pair MMAs reading the slot done (local)
-    uint64_t* w_full = x_empty + 8;                        // codes + scales landed (local)
-    uint64_t* w_empty = w_full + 8;                        // dequant warps done reading (local)
+    uint64_t* w_full = x_empty + 8;                        // codes + scales landed (local), 2 * SW
+    uint64_t* w_empty = w_full + 16;                        // dequant warps done reading (local)
     uint64_t* a_full = w_empty + 8;                        // both CTAs' weight slots written (leader)
     uint64_t* a_free = a_full + P_ASLOTS;                  // pair MMAs reading the slot done (local)
     uint64_t* d_full = a_free + P_ASLOTS;                  // tile accumulated (local)
@@ -123,6 +124,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
         }
         for (int i = 0; i < SW; ++i) {
             mbar_init(&w_full[i], 1);
+            mbar_init(&w_full[SW + i], 1);
             mbar_init(&w_empty[i], 4);
         }
         for (int i = 0; i < P_ASLOTS; ++i) {
@@ -183,16 +185,17 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
                 if (gs >= SW && !p_wait<false>(&w_empty[slot], ((gs / SW) - 1) & 1, ab)) break;
                 const int n0 = (tile % a.nR) * (2 * P_ROWS) + rank * P_ROWS, k0 = ks * P_KS;
                 uint8_t* st = wring + slot * F::W_STAGE;
-                mbar_arrive_expect_tx(&w_full[slot], wbytes);
-                tma_load_2d(st, &map_codes, &w_full[slot], k0 * BITS / 32, n0);
+                uint64_t* wl = &w_full[gs % (2 * SW)];
+                mbar_arrive_expect_tx(wl, wbytes);
+                tma_load_2d(st, &map_codes, wl, k0 * BITS / 32, n0);
                 if (SB_TMA) {
-                    tma_load_2d(st + F::CODE_B, &map_scales, &w_full[slot], (k0 / 512) * 8, n0);
+                    tma_load_2d(st + F::CODE_B, &map_scales, wl, (k0 / 512) * 8, n0);
                     if (a.has_bias)
-                        tma_load_2d(st + F::CODE_B + 2048, &map_biases, &w_full[slot], (k0 / 512) * 8, n0);
+                        tma_load_2d(st + F::CODE_B + 2048, &map_biases, wl, (k0 / 512) * 8, n0);
                 }
             }
             for (int i = 1; i <= (gs < SW ? gs : SW); ++i)
-                mbar_wait(&w_full[(gs - i) % SW], ((gs - i) / SW) & 1, a.status);
+                mbar_wait(&w_full[(gs - i) % (2 * SW)], ((gs - i) / (2 * SW)) & 1, a.status);
         }
     } else if (warp == 1) {
         // -------------------------------------------------- pair MMA issuer (leader)
@@ -228,6 +231,11 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
         }
     } else if (warp < P_WARP_EPI0) {
         // ----------------------------------------------------------------- dequant
+        // Stage gs lands on w_full[gs % (2 * SW)].  A parity wait only tells neighbouring
+        // phases apart; with one landing barrier per slot and an odd ring a slot alternates
+        // between the two sets, and a set could pass the wait of a slot's next stage while
+        // the other set's stage in that slot was still landing.  With the even period each
+        // landing barrier serves one set, which has waited for its previous phase itself.
         // Set 0 dequantizes the even stages, set 1 the odd ones; within a set, one warp
         // per TMEM lane quarter, one thread per weight row.
         const int set = (warp - P_WARP_DEQ0) >> 2;
@@ -255,7 +263,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
             const int slot = gs % SW, as = gs % P_ASLOTS;
             uint32_t s01 = s_next, b01 = b_next;
             sb_load(gs + 2, s_next, b_next);
-            if (!p_wait_warp<false>(&w_full[slot], (gs / SW) & 1, ab)) break;
+            if (!p_wait_warp<false>(&w_full[gs % (2 * SW)], (gs / (2 * SW)) & 1, ab)) break;
             // Dequantize into registers first: the TMEM slot is waited for only afterwards,
             // so the arithmetic overlaps the MMAs that still read the slot.
             const uint8_t* st = wring + slot * F::W_STAGE;
