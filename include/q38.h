@@ -256,6 +256,21 @@ Q38_API q38_status q38_quantized_embedding(q38_ctx* ctx, const int32_t* ids, int
                                            int64_t rows, int64_t K, int group_size, int bits, q38_mode mode,
                                            void* out, q38_dtype out_dtype);
 
+/* Rotated quantized embedding lookup (Bonsai 2 packs): the
+ * Qwen38HadamardQuantizedEmbedding.callAsFunction of
+ * Sources/Qwen38Core/Bonsai2/Qwen38HadamardModules.swift:71-79.  Each row of ids is
+ * dequantized into the scales' dtype (bf16 or f16), then rotated back:
+ * out = cast(signs * H_block(row) / sqrt(block)) in fp32 with the block-diagonal
+ * Walsh-Hadamard transform H over blocks of `block` (a power of two in [2, 8192] that
+ * divides K), signs (fp32 [K], may be NULL) applied after the transform (hadamardRotate
+ * with inverse = true, :10-19).  out [n, K] has the scales' dtype and equals
+ * q38_quantized_embedding followed by q38_hadamard_rotate(inverse = 1) bit for bit.  An
+ * id outside [0, rows) gives the rotation of a zero row (zeros) and is reported by
+ * q38_ctx_check_device. */
+Q38_API q38_status q38_hadamard_quantized_embedding(q38_ctx* ctx, const int32_t* ids, int64_t n, const uint32_t* w,
+    const void* scales, const void* biases, q38_dtype scales_dtype, int64_t rows, int64_t K, int group_size,
+    int bits, q38_mode mode, const float* signs, int block, void* out);
+
 /* Gate and up projections of a gated MLP in one call:
  *   h[M, N] = bf16( silu(bf16(x . dequant(Wg)^T)) * bf16(x . dequant(Wu)^T) ),
  * the `silu(gate(x)) * up(x)` of the reference's MLPs (the fused gate/up pattern of

@@ -322,6 +322,30 @@ q38_status q38_quantized_embedding(q38_ctx* ctx, const int32_t* ids, int64_t n, 
     return embedding_launch(ctx, ids, n, w, scales, biases, scales_dtype, rows, K, group_size, bits, out, out_dtype);
 }
 
+q38_status q38_hadamard_quantized_embedding(q38_ctx* ctx, const int32_t* ids, int64_t n, const uint32_t* w,
+                                            const void* scales, const void* biases, q38_dtype scales_dtype,
+                                            int64_t rows, int64_t K, int group_size, int bits, q38_mode mode,
+                                            const float* signs, int block, void* out) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    q38_status st = check_format(ctx, "hadamard_quantized_embedding", K, group_size, bits, mode);
+    if (st != Q38_OK) return st;
+    if (scales_dtype != Q38_BF16 && scales_dtype != Q38_F16)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "hadamard_quantized_embedding: scales must be bf16 or f16");
+    if (block < 2 || block > 8192 || (block & (block - 1)))
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT,
+                    "hadamard_quantized_embedding: block must be a power of two in [2, 8192]");
+    if (K % block)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT,
+                    "hadamard_quantized_embedding: Hadamard block does not divide the embedding width");
+    if (n < 0 || rows <= 0) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "hadamard_quantized_embedding: bad sizes");
+    if (n == 0) return Q38_OK;
+    if (!ids || !w || !scales || !out)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "hadamard_quantized_embedding: null pointer");
+    if ((st = set_device(ctx)) != Q38_OK) return st;
+    return hadamard_embedding_launch(ctx, ids, n, w, scales, biases, scales_dtype, rows, K, group_size, bits, signs,
+                                     block, out);
+}
+
 q38_status q38_quantize(q38_ctx* ctx, const void* w, q38_dtype w_dtype, int64_t rows, int64_t K,
                         int group_size, int bits, q38_mode mode, uint32_t* codes, void* scales,
                         void* biases, q38_dtype scales_dtype) {

@@ -6,6 +6,7 @@
 // 1/sqrt(block), cast back to the input dtype.  Butterfly stage h combines elements j and
 // j+h as (a+b, a-b) for h = 1, 2, 4, ...; each butterfly is one IEEE add/subtract of the
 // same two operands as the CPU restatement, so results agree bit for bit.
+#include "affine_scalar.cuh"
 #include "ptx.cuh"
 
 namespace q38 {
@@ -132,7 +133,79 @@ q38_status launch(q38_ctx* ctx, const void* x, int64_t rows, int64_t D, const fl
     return check_launch(ctx, "hadamard_rotate");
 }
 
+// Rotated embedding rows (Qwen38HadamardQuantizedEmbedding.callAsFunction,
+// Sources/Qwen38Core/Bonsai2/Qwen38HadamardModules.swift:71-79): the row of ids[t] is
+// dequantized into the scales' dtype T (scale*q + bias in fp32, one rounding, as the
+// lookup kernel does), then inverse-rotated: fp32 transform, 1/sqrt(block), signs after,
+// one rounding to T.  One CTA per (id, block) in shared memory, with the butterfly order
+// of the rotation kernels, so the result equals the lookup followed by the inverse
+// rotation bit for bit.  An id outside [0, rows) transforms a zero row and sets the
+// out-of-range status bit.
+template <typename T>
+__global__ void __launch_bounds__(512) embed_rotate_kernel(const int32_t* __restrict__ ids,
+                                                           const uint32_t* __restrict__ w,
+                                                           const T* __restrict__ s, const T* __restrict__ b,
+                                                           int64_t rows, int64_t K, int group, int bits,
+                                                           const float* __restrict__ signs, int block,
+                                                           float scale, T* __restrict__ out, uint32_t* status) {
+    using namespace dev;
+    extern __shared__ float sv[];
+    const int64_t per_row = K / block;
+    const int64_t t = blockIdx.x / per_row, col0 = (blockIdx.x % per_row) * block;
+    const int64_t r = ids[t];
+    const bool valid = r >= 0 && r < rows;
+    if (!valid && threadIdx.x == 0 && col0 == 0) atomicOr(status, Q38_DEV_BAD_INDEX);
+    const int64_t G = K / group;
+    const uint32_t* wr = w + (valid ? r : 0) * (K * bits / 32);
+    for (int i = threadIdx.x; i < block; i += blockDim.x) {
+        float f = 0.0f;
+        if (valid) {
+            const int64_t k = col0 + i;
+            const float sc = to_f32(s[r * G + k / group]);
+            const float bi = b ? to_f32(b[r * G + k / group]) : 0.0f;
+            f = to_f32(from_f32<T>(__fadd_rn(__fmul_rn(sc, static_cast<float>(get_code(wr, k, bits))), bi)));
+        }
+        sv[i] = f;
+    }
+    __syncthreads();
+    for (int h = 1; h < block; h <<= 1) {
+        for (int p = threadIdx.x; p < block / 2; p += blockDim.x) {
+            const int j = (p / h) * 2 * h + (p % h);
+            const float a = sv[j], c = sv[j + h];
+            sv[j] = a + c;
+            sv[j + h] = a - c;
+        }
+        __syncthreads();
+    }
+    T* dst = out + t * K + col0;
+    for (int i = threadIdx.x; i < block; i += blockDim.x) {
+        float f = sv[i] * scale;
+        if (signs) f = f * signs[col0 + i];
+        dst[i] = from_f32<T>(f);
+    }
+}
+
 }  // namespace
+
+q38_status hadamard_embedding_launch(q38_ctx* ctx, const int32_t* ids, int64_t n, const uint32_t* w,
+                                     const void* s, const void* b, q38_dtype sd, int64_t rows, int64_t K,
+                                     int group, int bits, const float* signs, int block, void* out) {
+    const int64_t nblocks = n * (K / block);
+    if (nblocks > 0x7fffffffLL) return fail(ctx, Q38_ERR_UNSUPPORTED, "hadamard_quantized_embedding: too many blocks");
+    const float scale = 1.0f / sqrtf(static_cast<float>(block));
+    const int threads = block / 2 < 512 ? (block / 2 < 32 ? 32 : block / 2) : 512;
+    const size_t smem = static_cast<size_t>(block) * sizeof(float);
+    const unsigned grid = static_cast<unsigned>(nblocks);
+    if (sd == Q38_BF16)
+        embed_rotate_kernel<__nv_bfloat16><<<grid, threads, smem, ctx->stream>>>(
+            ids, w, static_cast<const __nv_bfloat16*>(s), static_cast<const __nv_bfloat16*>(b), rows, K, group, bits,
+            signs, block, scale, static_cast<__nv_bfloat16*>(out), ctx->d_status);
+    else
+        embed_rotate_kernel<__half><<<grid, threads, smem, ctx->stream>>>(
+            ids, w, static_cast<const __half*>(s), static_cast<const __half*>(b), rows, K, group, bits, signs, block,
+            scale, static_cast<__half*>(out), ctx->d_status);
+    return check_launch(ctx, "hadamard_quantized_embedding");
+}
 
 q38_status hadamard_launch(q38_ctx* ctx, const void* x, int64_t rows, int64_t D, q38_dtype xd,
                            const float* signs, int block, int inverse, void* y) {

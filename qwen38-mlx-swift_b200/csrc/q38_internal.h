@@ -108,6 +108,9 @@ q38_status quantize_launch(q38_ctx* ctx, const void* w, q38_dtype wd, int64_t ro
                            q38_dtype sd);
 q38_status unpack_launch(q38_ctx* ctx, const uint32_t* w, int64_t rows, int64_t K, int bits,
                          uint8_t* q);
+q38_status hadamard_embedding_launch(q38_ctx* ctx, const int32_t* ids, int64_t n, const uint32_t* w,
+                                     const void* s, const void* b, q38_dtype sd, int64_t rows, int64_t K,
+                                     int group, int bits, const float* signs, int block, void* out);
 q38_status hadamard_launch(q38_ctx* ctx, const void* x, int64_t rows, int64_t D, q38_dtype xd,
                            const float* signs, int block, int inverse, void* y);
 

@@ -55,6 +55,7 @@ _sig("q38_ctx_check_device", [_P])
 _sig("q38_last_error", [_P], C.c_char_p)
 _sig("q38_quantized_matmul", [_P, _P, _I, _I, _i, _P, _P, _P, _i, _I, _i, _i, _i, _i, _P])
 _sig("q38_quantized_embedding", [_P, _P, _I, _P, _P, _P, _i, _I, _I, _i, _i, _i, _P, _i])
+_sig("q38_hadamard_quantized_embedding", [_P, _P, _I, _P, _P, _P, _i, _I, _I, _i, _i, _i, _P, _i, _P])
 _sig("q38_quantized_gate_up", [_P, _P, _I, _I, _i, _P, _P, _P, _P, _P, _P, _i, _I, _i, _i, _i, _P])
 _sig("q38_gather_quantized_matmul",
      [_P, _P, _I, _I, _I, _i, _P, _P, _P, _i, _I, _I, _P, _P, _I, _i, _i, _i, _i, _i, _P])
@@ -215,6 +216,34 @@ def quantized_embedding(ids: torch.Tensor, w: torch.Tensor, scales: torch.Tensor
     _check(ctx, _lib.q38_quantized_embedding(ctx, _ptr(ids), ids.numel(), _ptr(w), _ptr(scales), _ptr(biases),
                                              _DTYPE[scales.dtype], rows, K, group_size, bits, 0, _ptr(out),
                                              _DTYPE[od]))
+    return out
+
+
+def hadamard_quantized_embedding(ids: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
+                                 biases: torch.Tensor | None, signs: torch.Tensor | None, block: int,
+                                 group_size: int = 64, bits: int = 2, mode: str = "affine") -> torch.Tensor:
+    """Rotated embedding lookup of Qwen38HadamardQuantizedEmbedding.callAsFunction
+    (Bonsai2/Qwen38HadamardModules.swift:71-79): dequantized rows in the scales' dtype,
+    then hadamardRotate(inverse=True)."""
+    if mode != "affine":
+        raise Q38Error(2, f"mode {mode!r} is not implemented")
+    _need(ids, "ids"), _need(w, "w"), _need(scales, "scales")
+    if biases is not None:
+        _need(biases, "biases")
+    if signs is not None:
+        _need(signs, "signs")
+        if signs.dtype != torch.float32:
+            signs = signs.float().contiguous()
+    if ids.dtype != torch.int32:
+        raise ValueError("ids must be int32")
+    w = _as_u32(w)
+    rows = w.shape[0]
+    K = w.shape[-1] * 32 // bits
+    out = torch.empty(tuple(ids.shape) + (K,), dtype=scales.dtype, device=w.device)
+    ctx = _bind(w)
+    _check(ctx, _lib.q38_hadamard_quantized_embedding(ctx, _ptr(ids), ids.numel(), _ptr(w), _ptr(scales),
+                                                      _ptr(biases), _DTYPE[scales.dtype], rows, K, group_size,
+                                                      bits, 0, _ptr(signs), block, _ptr(out)))
     return out
 
 
@@ -524,6 +553,25 @@ class QuantizedEmbedding:
     def as_linear(self, x: torch.Tensor) -> torch.Tensor:
         return quantized_matmul(x, self.weight, self.scales, self.biases, True, self.group_size, self.bits,
                                 self.mode)
+
+
+class HadamardQuantizedEmbedding(QuantizedEmbedding):
+    """Qwen38HadamardQuantizedEmbedding (Bonsai2/Qwen38HadamardModules.swift:49-80): the
+    source embedding's tables, looked up, dequantized and rotated back (signs after the
+    transform).  The reference class defines no output projection of its own."""
+
+    def __init__(self, source: QuantizedEmbedding, signs: torch.Tensor | None, block: int):
+        super().__init__(source.weight, source.scales, source.biases, source.group_size, source.bits, source.mode)
+        self.signs = None if signs is None else signs.float().contiguous()
+        self.block = block
+
+    def __call__(self, ids: torch.Tensor) -> torch.Tensor:
+        return hadamard_quantized_embedding(ids.to(torch.int32).contiguous(), self.weight, self.scales,
+                                            self.biases, self.signs, self.block, self.group_size, self.bits,
+                                            self.mode)
+
+    def as_linear(self, x: torch.Tensor) -> torch.Tensor:
+        raise NotImplementedError("the rotated embedding has no tied output projection")
 
 
 class HadamardQuantizedLinear(QuantizedLinear):

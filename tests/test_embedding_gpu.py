@@ -1,10 +1,15 @@
-"""GPU parity of the quantized embedding (Qwen4ExpPrequantizedEmbedding) and of its tied
-output projection at vocabulary size.
+"""GPU parity of the quantized embedding (Qwen4ExpPrequantizedEmbedding), of its tied
+output projection at vocabulary size, and of the rotated Bonsai 2 embedding
+(Qwen38HadamardQuantizedEmbedding).
 
 Bars: each looked-up row equals the oracle's dequantization of that table row bit for bit
 (same fp32 multiply-add, one rounding to the output dtype); an out-of-range id yields a
 zero row and is reported by check_device; the output projection over 248,320 rows is
-within 2e-2 * RMS of the oracle on sampled rows (fp32 accumulation on both sides).
+within 2e-2 * RMS of the oracle on sampled rows (fp32 accumulation on both sides).  A
+rotated row equals the oracle's inverse rotation of the bf16 dequantized row bit for bit
+(the butterflies are the same IEEE adds in the same order), and in f16 with the real
+pack's layout (group 128, block 1024) it equals the lookup followed by the library's own
+inverse rotation bit for bit.
 """
 import numpy as np
 import pytest
@@ -73,3 +78,58 @@ def test_tied_output_projection_vocabulary_size(q38):
     got = O.bf16_to_f32(host_bf16(y)[:, pick]).astype(np.float64)
     full_rms = float(y.float().pow(2).mean().sqrt())
     assert np.abs(got - ref).max() <= 2e-2 * full_rms
+
+
+@pytest.mark.parametrize("block", [256, 1024, 4096])
+def test_hadamard_embedding_bit_exact(q38, block):
+    rows, K, bits = 200, 4096, 2
+    c, s, b = make_weight(910, rows, K, bits)
+    signs = np.where(np.random.default_rng(block).random(K) < 0.5, -1.0, 1.0).astype(np.float32)
+    ids = np.random.default_rng(911).integers(0, rows, size=(2, 9)).astype(np.int32)
+    emb = q38.QuantizedEmbedding(dev_u32(c), dev_bf16(s), dev_bf16(b), 64, bits)
+    rot = q38.HadamardQuantizedEmbedding(emb, torch.from_numpy(signs).cuda(), block)
+    out = rot(torch.from_numpy(ids).cuda())
+    torch.cuda.synchronize()
+    q38.check_device()
+    assert out.shape == (2, 9, K) and out.dtype == torch.bfloat16
+    rows_bf16 = O.f32_to_bf16(O.dequantize(c, s, b, 64, bits)[ids.reshape(-1)])
+    ref = O.hadamard_rotate(rows_bf16, block, signs, inverse=True)
+    np.testing.assert_array_equal(host_bf16(out).reshape(-1, K), ref)
+
+
+def test_hadamard_embedding_bonsai_layout_f16(q38):
+    # the real pack: group 128, f16 scales, biases = -scales (ternary), block 1024
+    rows, K, bits, group, block = 96, 2048, 2, 128, 1024
+    g = torch.Generator(device="cuda").manual_seed(912)
+    codes = torch.randint(0, 3, (rows, K), device="cuda", generator=g, dtype=torch.int32)
+    packed = torch.zeros((rows, K * bits // 32), dtype=torch.int64, device="cuda")
+    for j in range(16):
+        packed |= codes[:, j::16].to(torch.int64) << (2 * j)
+    packed = torch.where(packed >= 2 ** 31, packed - 2 ** 32, packed).to(torch.int32)  # u32 bit patterns
+    scales = (torch.rand((rows, K // group), device="cuda", generator=g) * 0.02 + 0.001).half()
+    biases = -scales
+    signs = torch.where(torch.rand(K, device="cuda", generator=g) < 0.5, -1.0, 1.0)
+    ids = torch.tensor([[3, 95, 0, 3], [50, 1, 2, 94]], dtype=torch.int32, device="cuda")
+    got = q38.hadamard_quantized_embedding(ids, packed, scales, biases, signs, block, group, bits)
+    looked_up = q38.quantized_embedding(ids, packed, scales, biases, group, bits)
+    ref = q38.hadamard_rotate(looked_up, signs, block, inverse=True)
+    torch.cuda.synchronize()
+    q38.check_device()
+    assert got.dtype == torch.float16 and got.shape == (2, 4, K)
+    assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+
+
+def test_hadamard_embedding_out_of_range_and_arguments(q38):
+    rows, K, bits = 16, 512, 2
+    c, s, b = make_weight(913, rows, K, bits)
+    ids = torch.tensor([rows + 4, 1], dtype=torch.int32, device="cuda")
+    out = q38.hadamard_quantized_embedding(ids, dev_u32(c), dev_bf16(s), dev_bf16(b), None, 256, 64, bits)
+    with pytest.raises(q38.Q38Error):
+        q38.check_device()
+    assert torch.count_nonzero(out[0]).item() == 0
+    ref = O.hadamard_rotate(O.f32_to_bf16(O.dequantize(c, s, b, 64, bits)[[1]]), 256, None, inverse=True)
+    np.testing.assert_array_equal(host_bf16(out)[[1]], ref)
+    with pytest.raises(q38.Q38Error):  # block does not divide K
+        q38.hadamard_quantized_embedding(ids, dev_u32(c), dev_bf16(s), dev_bf16(b), None, 1024, 64, bits)
+    with pytest.raises(q38.Q38Error):  # block not a power of two
+        q38.hadamard_quantized_embedding(ids, dev_u32(c), dev_bf16(s), dev_bf16(b), None, 384, 64, bits)
