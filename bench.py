@@ -177,6 +177,72 @@ def run_gate_up(torch, q38, O, dev, stream, quick=False):
             "bytes_per_call": nbytes, "per_M": out}
 
 
+def run_loader(torch, q38, dev, quick=False):
+    """Checkpoint loading: a safetensors file shaped like 16 packed 4-bit 17408x5120
+    projections (codes U32, scales and biases BF16; 800 MB) read into device tensors
+    through libq38's reader (mapped file -> pinned staging -> device), host clock around
+    the whole load plus a device synchronise, page cache warm.  Beside it, for context, the
+    safetensors package loading the same file straight to the device."""
+    import json as _json
+    import shutil
+    import struct
+    import tempfile
+    import time
+    import loader
+    n_proj = 4 if quick else 16
+    N, K, bits = 17408, 5120, 4
+    d = tempfile.mkdtemp(prefix="q38_load_")
+    path = os.path.join(d, "model.safetensors")
+    try:
+        header, off, parts = {}, 0, []
+        rng = np.random.default_rng(77)
+        codes = rng.integers(0, 2 ** 32, size=(N, K * bits // 32), dtype=np.uint32)
+        sc = rng.integers(0, 2 ** 16, size=(N, K // GROUP), dtype=np.uint16)
+        for i in range(n_proj):
+            for name, arr, dt in (("weight", codes, "U32"), ("scales", sc, "BF16"), ("biases", sc, "BF16")):
+                key = f"model.layers.{i}.mlp.proj.{name}"
+                header[key] = {"dtype": dt, "shape": list(arr.shape), "data_offsets": [off, off + arr.nbytes]}
+                off += arr.nbytes
+                parts.append(arr)
+        h = _json.dumps(header).encode()
+        h += b" " * (-len(h) % 8)
+        with open(path, "wb") as fh:
+            fh.write(struct.pack("<Q", len(h)) + h)
+            for a in parts:
+                fh.write(a.tobytes())
+        total = off
+        with open(path, "rb") as fh:  # page cache warm
+            while fh.read(1 << 26):
+                pass
+
+        def ours():
+            with loader.SafetensorsFile(path) as f:
+                out = [f.to_device(k, dev) for k in f.keys()]
+            torch.cuda.synchronize()
+            return out
+
+        def package():
+            import safetensors.torch as st
+            out = st.load_file(path, device=str(dev))
+            torch.cuda.synchronize()
+            return out
+
+        res = {}
+        for name, fn in (("q38_reader", ours), ("safetensors_package", package)):
+            best = None
+            for _ in range(3):
+                t0 = time.perf_counter()
+                out = fn()
+                dt = time.perf_counter() - t0
+                best = dt if best is None else min(best, dt)
+                del out
+            res[name] = {"seconds": round(best, 4), "GBps": round(total / best / 1e9, 2)}
+        return {"workload": f"{n_proj} packed 4-bit 17408x5120 projections (U32 codes, BF16 scales/biases)",
+                "bytes": total, "timing": "host clock, best of 3, page cache warm", **res}
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+
+
 # ----------------------------------------------------------------------------- MoE
 MOE = {"H": 2048, "I": 512, "E": 512, "k": 10, "bits": 3}
 MOE_T = [1, 8, 64, 4096]
@@ -622,6 +688,7 @@ def run_ours(args, rank, world, local_rank):
         moe = None if args.skip_moe else run_moe(torch, q38, dev, stream, world, dist, args.quick)
         prefill = None if args.skip_prefill else run_prefill(torch, q38, dev, stream, world, dist, args.quick)
     gate_up = None if (args.skip_prefill or world > 1) else run_gate_up(torch, q38, O, dev, stream, args.quick)
+    load = None if (args.skip_prefill or world > 1) else run_loader(torch, q38, dev, args.quick)
 
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
@@ -654,6 +721,7 @@ def run_ours(args, rank, world, local_rank):
         "moe": moe,
         "prefill": prefill,
         "gate_up": gate_up,
+        "loader": load,
     }
     return line
 

@@ -306,6 +306,51 @@ Q38_API q38_status q38_quantized_matmul_noalloc(const void* x, int64_t M, int64_
                                                 const void* biases, int64_t N, int group_size,
                                                 int bits, void* y, void* stream);
 
+/* ------------------------------------------------------------- safetensors */
+
+/* Checkpoint reader.  MLX checkpoints are safetensors files whose packed tensors
+ * (`<module>.weight` U32, `.scales` and `.biases` BF16/F16, Bonsai 2 `.signs` F32) are
+ * already the layout these operators take, so loading is a copy: the reference attaches
+ * them with loadArrays (Sources/Qwen38Core/FlashNext/Qwen4ExpCheckpointLayerLoader.swift:74,
+ * Sources/Qwen38Core/Bonsai2/Qwen38Bonsai2Container.swift:30) and this reader replaces that
+ * step.  The file is mapped read-only; its header is parsed and checked (known dtypes,
+ * sizes that match the shapes, byte ranges that tile the data buffer exactly).  Host
+ * functions need no context or device; the pointers they return are host pointers into
+ * the mapping and stay valid until q38_st_close.  A handle may be shared by threads. */
+typedef struct q38_st_file q38_st_file;
+
+/* Opens and validates `path`.  On failure returns Q38_ERR_INVALID_ARGUMENT and
+ * q38_st_open_error() (per thread) says why. */
+Q38_API q38_status q38_st_open(const char* path, q38_st_file** out);
+Q38_API const char* q38_st_open_error(void);
+Q38_API void q38_st_close(q38_st_file* f);
+/* Tensors in header order; q38_st_find returns the index of `name` or -1. */
+Q38_API int64_t q38_st_count(const q38_st_file* f);
+Q38_API int64_t q38_st_find(const q38_st_file* f, const char* name);
+/* name and dtype ("U32", "BF16", "F16", "F32", ... as written in the file) are owned by
+ * the handle; shape needs room for 8 entries.  Any output may be NULL. */
+Q38_API q38_status q38_st_info(const q38_st_file* f, int64_t i, const char** name, const char** dtype, int* ndim,
+                               int64_t* shape, uint64_t* nbytes);
+/* Host address of tensor i's bytes inside the mapping. */
+Q38_API const void* q38_st_data(const q38_st_file* f, int64_t i);
+/* The header's "__metadata__" string map, in file order. */
+Q38_API int64_t q38_st_metadata_count(const q38_st_file* f);
+Q38_API q38_status q38_st_metadata_entry(const q38_st_file* f, int64_t i, const char** key, const char** value);
+/* Copies tensor i (all nbytes of it; dst_bytes >= nbytes) to the device buffer dst,
+ * enqueued on the context's stream through pinned staging owned by the context.  The
+ * call returns once the host has handed every byte to a copy; the copies complete in
+ * stream order. */
+Q38_API q38_status q38_st_copy_to_device(q38_ctx* ctx, const q38_st_file* f, int64_t i, void* dst,
+                                         uint64_t dst_bytes);
+/* Copies a 2-D block of tensor i seen as rows of row_bytes bytes: rows [row0, row0+rows)
+ * and bytes [col_byte0, col_byte0+col_bytes) of each row, to dst with row pitch dst_pitch.
+ * A tensor-parallel shard loads this way without the rest of the tensor: output rows of
+ * a packed weight are whole rows; a shard of its reduction dimension is a byte range of
+ * each row (whole 32-bit words of codes, whole groups of scales and biases). */
+Q38_API q38_status q38_st_copy_block_to_device(q38_ctx* ctx, const q38_st_file* f, int64_t i, uint64_t row_bytes,
+                                               uint64_t row0, uint64_t rows, uint64_t col_byte0, uint64_t col_bytes,
+                                               void* dst, uint64_t dst_pitch);
+
 #ifdef __cplusplus
 }
 #endif

@@ -197,6 +197,9 @@ q38_status q38_ctx_destroy(q38_ctx* ctx) {
     if (ctx->zws) cudaFree(ctx->zws);
     if (ctx->aux) cudaFree(ctx->aux);
     if (ctx->d_status) cudaFree(ctx->d_status);
+    if (ctx->host_stage) cudaFreeHost(ctx->host_stage);
+    for (cudaEvent_t e : ctx->stage_done)
+        if (e) cudaEventDestroy(e);
     delete ctx;
     return Q38_OK;
 }

@@ -30,6 +30,11 @@ struct q38_ctx {
     void* aux = nullptr;  // activation-sized intermediates (rotated x, MoE buffers)
     size_t aux_bytes = 0;
     uint32_t* d_status = nullptr;  // device status word (timeouts)
+    // Pinned host staging of the safetensors reader: two halves used alternately, each
+    // guarded by an event of its last host->device copy.
+    void* host_stage = nullptr;
+    size_t host_stage_bytes = 0;  // per half
+    cudaEvent_t stage_done[2] = {nullptr, nullptr};
     std::string last_error;
 };
 

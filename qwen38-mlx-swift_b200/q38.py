@@ -73,6 +73,19 @@ _sig("q38_moe_combine", [_P, _P, _I, _P, _P, _P, _I, _i, _I, _P])
 _sig("q38_moe_ep_plan", [_P, _P, _I, _i, _I, _i, _P, _P])
 _sig("q38_moe_ep_pack", [_P, _P, _I, _P, _P, _I, _i, _I, _i, _P, _P, _I, _P, _I])
 _sig("q38_moe_ep_reduce", [_P, _P, _I, _P, _I, _i, _P])
+_U64 = C.c_uint64
+_sig("q38_st_open", [C.c_char_p, C.POINTER(_P)])
+_sig("q38_st_open_error", [], C.c_char_p)
+_sig("q38_st_close", [_P], None)
+_sig("q38_st_count", [_P], _I)
+_sig("q38_st_find", [_P, C.c_char_p], _I)
+_sig("q38_st_info", [_P, _I, C.POINTER(C.c_char_p), C.POINTER(C.c_char_p), C.POINTER(_i), C.POINTER(_I),
+                     C.POINTER(_U64)])
+_sig("q38_st_data", [_P, _I], _P)
+_sig("q38_st_metadata_count", [_P], _I)
+_sig("q38_st_metadata_entry", [_P, _I, C.POINTER(C.c_char_p), C.POINTER(C.c_char_p)])
+_sig("q38_st_copy_to_device", [_P, _P, _I, _P, _U64])
+_sig("q38_st_copy_block_to_device", [_P, _P, _I, _U64, _U64, _U64, _U64, _U64, _P, _U64])
 _sig("q38_switch_glu", [_P, _P, _I, _I, _I, _I, _i, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _i, _i, _i, _P])
 
 
