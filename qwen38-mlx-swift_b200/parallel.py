@@ -11,7 +11,11 @@ compute on libq38.
   one of its experts (all-to-all), with the rank-local expert ids and router scores of its
   slots; the receiving rank runs SwitchGLU over its experts only (other slots marked -1),
   which gives the token's partial score-weighted sum; the partial rows return (all-to-all)
-  and the home rank adds them in rank order.
+  and the home rank adds them in rank order.  With a fixed `capacity` (tokens per rank per
+  call, the same on every rank) each rank sends `capacity` rows to every rank (token t at
+  row t of each destination's block, unused rows marked empty), so the exchange sizes are
+  known in advance: no count exchange, no host synchronisation, and the layer can be
+  captured in a CUDA graph.  The result is bit-identical to the exact-size exchange.
 
 The compute goes through an `ops` object (DeviceOps = libq38 on the GPU); tests substitute
 CPU restatements to check the exchange bookkeeping without a GPU.
@@ -134,7 +138,7 @@ class ExpertParallelMoE:
     experts [rank*E/world, (rank+1)*E/world); `router_weight` [E, H] is replicated."""
 
     def __init__(self, router_weight, experts, num_experts, top_k, group_size=64, bits=3, normalize=True,
-                 ops=None, process_group=None):
+                 ops=None, process_group=None, capacity=None):
         self.ops = ops or DeviceOps()
         self.pg = process_group
         self.rank, self.world = _rank_world(process_group)
@@ -143,13 +147,21 @@ class ExpertParallelMoE:
         self.wr, self.experts = router_weight, experts
         self.E, self.k, self.epr = num_experts, top_k, num_experts // self.world
         self.group, self.bits, self.normalize = group_size, bits, normalize
+        if capacity is not None and capacity < 1:
+            raise ValueError("capacity must be at least one token")
+        self.capacity = capacity
+        self._slots = {}
 
     def __call__(self, x):
         o = self.ops
         k = self.k
+        if self.capacity is not None and x.shape[0] > self.capacity:
+            raise ValueError(f"{x.shape[0]} tokens exceed the exchange capacity {self.capacity}")
         idx, sc = o.route(x, self.wr, k, self.normalize)
         if self.world == 1:
             return o.partial_experts(x, idx, sc, self.experts, self.group, self.bits)
+        if self.capacity is not None:
+            return self._fixed_exchange(x, idx, sc)
         rowpos, counts = o.ep_plan(idx, self.epr, self.world)
         send_t = counts.to(torch.int64)
         recv_t = torch.empty_like(send_t)
@@ -161,3 +173,22 @@ class ExpertParallelMoE:
         part = o.partial_experts(rrows, lidx, lsc, self.experts, self.group, self.bits)
         back = _exchange(part, recv, send, self.pg)
         return o.ep_reduce(back, rowpos)
+
+    def _fixed_exchange(self, x, idx, sc):
+        o, k, W, C = self.ops, self.k, self.world, self.capacity
+        T, H = x.shape
+        slot = self._slots.get((T, x.device))
+        if slot is None:  # row of (token t, destination r) in the send buffer: r * C + t
+            slot = (torch.arange(W, dtype=torch.int32, device=x.device)[None, :] * C +
+                    torch.arange(T, dtype=torch.int32, device=x.device)[:, None]).contiguous()
+            self._slots[(T, x.device)] = slot
+        rowpos, _ = o.ep_plan(idx, self.epr, W)
+        packed = o.ep_pack(x, idx, sc, slot, self.epr, W * C)
+        if T < C:  # rows past this rank's tokens: every expert slot empty (-1)
+            packed.view(W, C, -1)[:, T:, H:H + 2 * k].view(torch.int16).fill_(-1)
+        sizes = [C] * W
+        rrows, lidx, lsc = o.ep_unpack(_exchange(packed, sizes, sizes, self.pg), H, k)
+        part = o.partial_experts(rrows, lidx, lsc, self.experts, self.group, self.bits)
+        back = _exchange(part, sizes, sizes, self.pg)
+        # add only the rows of ranks that own one of the token's experts, in rank order
+        return o.ep_reduce(back, torch.where(rowpos >= 0, slot, torch.full_like(slot, -1)))

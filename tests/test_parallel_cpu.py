@@ -132,6 +132,14 @@ def ep_worker(rank, world, port, q):
             ws = [(c[r * epr:(r + 1) * epr], s[r * epr:(r + 1) * epr], b[r * epr:(r + 1) * epr]) for (c, s, b) in (gate, up, down)]
             acc += O.bf16_to_f32(O.switch_glu(x, lidx, sc, *ws, 64, BITS))
         exact = bool(np.array_equal(out, O.f32_to_bf16(acc)))
+        # fixed-capacity exchange (8 rows per destination; this rank has 5 + rank tokens)
+        fixed = ExpertParallelMoE(tb(wr), mine, E, K_TOP, 64, BITS, ops=OracleOps(), capacity=8)
+        exact = exact and bool(np.array_equal(bf(fixed(tb(x))), out))
+        try:
+            ExpertParallelMoE(tb(wr), mine, E, K_TOP, 64, BITS, ops=OracleOps(), capacity=4)(tb(x))
+            exact = False
+        except ValueError:
+            pass
         full = O.bf16_to_f32(O.switch_glu(x, idx, sc, gate, up, down, 64, BITS)).astype(np.float64)
         y = O.bf16_to_f32(out).astype(np.float64)
         rms = np.sqrt((full ** 2).mean())

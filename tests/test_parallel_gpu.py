@@ -138,6 +138,9 @@ def _worker(rank, world, port, q):
         out = ep(x)
         idx, sc = q38.moe_route(x, wr, k)
         ep_ok = bool(torch.equal(out, rank_partials_sum(q38, x, idx, sc, dev, epr, world)))
+        # fixed-capacity exchange: 128 rows per destination (this rank has 100 + 16 * rank)
+        fixed = ExpertParallelMoE(wr, mine, E, k, 64, bits, capacity=128)
+        ep_ok = ep_ok and bool(torch.equal(fixed(x), out))
         full = q38.switch_glu(x, idx, sc, *dev, 64, bits).float()
         rms0 = float((full ** 2).mean().sqrt())
         step0 = torch.exp2(torch.floor(torch.log2(full.abs().clamp_min(2.0 ** -126))) - 7)
