@@ -31,6 +31,7 @@
 //  * The main kernel is launched with programmatic dependent launch: its producer
 //    streams the first stages of weights while the previous kernel is still running.
 #include <mutex>
+#include <numeric>
 #include <type_traits>
 
 #include "affine_codes.cuh"
@@ -45,6 +46,7 @@ constexpr int GROUPS = 8;      // groups of 64 per chunk
 constexpr int NCW = 4;         // 16-row subtiles per stage (one consumer warp each)
 constexpr int WG = 2;          // consumer warp groups; group j takes the stages i with i % WG == j
 constexpr int THREADS = (NCW * WG + 2) * 32;  // + weight producer + activation warp
+static_assert(8 * WG + 8 + 4 <= 1024 / 8, "landing, empty and x barriers fit the first 1 KiB");
 
 template <int BITS>
 struct Fmt {
@@ -222,7 +224,7 @@ struct MainArgs {
     __nv_bfloat16* y;
     float* ws;
     uint32_t* status;
-    int M, N, K, C, tiles, tiles_a, ld, stages, stage_bytes, has_bias;
+    int M, N, K, C, tiles, tiles_a, ld, stages, lands, stage_bytes, has_bias;
 };
 
 // Accumulator columns.  An m16n8k16 product has 8 columns; with MP (1, 2, 4 or 8) token
@@ -321,15 +323,16 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
     constexpr int SPLIT = (TB == 1 && MP <= 2 && UG == 2) ? 2 : 1;  // shorter MMA chains
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_align1024(smem_raw);
-    // Landing barriers: stage i signals full[i % (2 * stages)].  A parity wait only tells
-    // the awaited phase from its neighbours, so each waiter must be within one phase of
-    // the barrier.  With an odd ring a data slot alternates between the two consumer
-    // groups, and one group could reach a slot's next stage before the other group's
-    // stage in that slot had landed.  With 2 * stages landing barriers (an even period)
-    // every phase of a barrier belongs to the same group, which has waited for the
-    // previous phase itself, and the next phase cannot land before this one is consumed.
+    // Landing barriers: stage i signals full[i % lands], lands = lcm(stages, WG).  A parity
+    // wait only tells the awaited phase from its neighbours, so each waiter must be within
+    // one phase of the barrier.  When WG does not divide the ring, a data slot passes from
+    // group to group, and one group could reach a slot's next stage before another group's
+    // stage in that slot had landed.  With a period that WG divides, every phase of a
+    // landing barrier belongs to one group, which has waited for the previous phase itself;
+    // with a period that the ring divides, the next phase cannot land before this one is
+    // consumed (each stage lands only after the previous stage of its data slot is consumed).
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + 2 * a.stages;
+    uint64_t* empty = full + a.lands;
     uint64_t* xfull = empty + a.stages;
     uint64_t* xempty = xfull + 2;
     const uint8_t* zeros = smem + ZERO_OFF;
@@ -359,11 +362,8 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
             reinterpret_cast<uint4*>(stage0 + static_cast<size_t>(i >> 6) * a.stage_bytes + NCW * F::SUB_BYTES +
                                      1024)[i & 63] = make_uint4(0u, 0u, 0u, 0u);
     if (threadIdx.x == 0) {
-        for (int i = 0; i < a.stages; ++i) {
-            mbar_init(&full[i], 1);
-            mbar_init(&full[a.stages + i], 1);
-            mbar_init(&empty[i], NCW);
-        }
+        for (int i = 0; i < a.lands; ++i) mbar_init(&full[i], 1);
+        for (int i = 0; i < a.stages; ++i) mbar_init(&empty[i], NCW);
         for (int i = 0; i < 2; ++i) {
             mbar_init(&xfull[i], 1);
             mbar_init(&xempty[i], NCW * WG);
@@ -398,7 +398,7 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
                     // the consumers have given up: let the copies already issued land
                     // before the CTA can exit (each wait is bounded)
                     for (int j = i - a.stages; j < i; ++j)
-                        if (!mbar_wait(&full[j % (2 * a.stages)], (j / (2 * a.stages)) & 1, a.status)) break;
+                        if (!mbar_wait(&full[j % a.lands], (j / a.lands) & 1, a.status)) break;
                     return;
                 }
                 const int sub_lo = i == 0 ? lo_first : 0;
@@ -437,7 +437,7 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
                     slot = 0;
                     ph ^= 1;
                 }
-                if (++fslot == 2 * a.stages) fslot = 0;
+                if (++fslot == a.lands) fslot = 0;
                 if (++tile == a.tiles) {
                     tile = 0;
                     ++chunk;
@@ -504,7 +504,7 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
     // per group: where this lane's B operand comes from (its fragments, or zeros)
     const uint8_t* pg[TB == 1 ? GROUPS : TB];
     int chunk = st_first / a.tiles, tile = st_first % a.tiles;
-    int slot = 0, fslot = 0;  // data slot i % stages, landing barrier i % (2 * stages)
+    int slot = 0, fslot = 0;  // data slot i % stages, landing barrier i % lands
     uint32_t fph = 0;         // phase parity of the landing barrier
     int own = 0;  // i % WG
     for (int i = 0; i < nst; ++i) {
@@ -669,7 +669,7 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
         if (active) flush_subtile<MP, TB>(acc, tile, sw_i, a, lane);
         if (++own == WG) own = 0;
         if (++slot == a.stages) slot = 0;
-        if (++fslot == 2 * a.stages) {
+        if (++fslot == a.lands) {
             fslot = 0;
             fph ^= 1;
         }
@@ -697,7 +697,7 @@ bool make_plan(int M, int K, int N, Plan& p, bool two_weights = false) {
     // static sums) lets three CTAs (12 consumer warps) share an SM; 113 KiB two
     const int budget = (WG == 1 ? (M > 8 ? 113 : 76) : (M > 8 ? 226 : 113)) * 1024 - 1024 - RING_OFF - 1024 - xbytes;
     int stages = budget / p.stage_bytes;
-    if (stages > 8) stages = 8;  // (the 3 * stages + 4 barriers then fit the first 1 KiB)
+    if (stages > 8) stages = 8;  // (the lcm(stages, WG) + stages + 4 barriers then fit the first 1 KiB)
     if (stages < 2) stages = 2;
     int smem = 1024 + RING_OFF + stages * p.stage_bytes + xbytes;  // + alignment slack
     while (smem > MAX_DYN_SMEM && stages > 2) {
@@ -816,6 +816,7 @@ cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x
     args.tiles_a = maps_b ? p.tiles / 2 : p.tiles;
     args.ld = maps_b ? 2 * N : N;
     args.stages = p.stages;
+    args.lands = std::lcm(p.stages, WG);
     args.stage_bytes = p.stage_bytes;
     args.has_bias = has_bias;
 
