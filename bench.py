@@ -243,6 +243,128 @@ def run_loader(torch, q38, dev, quick=False):
         shutil.rmtree(d, ignore_errors=True)
 
 
+def _ternary_weight(torch, dev, g, N, K, group, sdtype):
+    """Bonsai-style weight: codes uniform in {0, 1, 2} (w in {-s, 0, +s}), 2-bit packed,
+    scale |N(0, 0.02^2)| per group, bias = -scale."""
+    codes = torch.randint(0, 3, (N, K), generator=g, device=dev, dtype=torch.int64)
+    words = torch.zeros((N, K // 16), dtype=torch.int64, device=dev)
+    for j in range(16):
+        words |= codes[:, j::16] << (2 * j)
+    del codes
+    words = torch.where(words >= 2 ** 31, words - 2 ** 32, words).to(torch.int32)
+    s = (torch.randn((N, K // group), generator=g, device=dev) * 0.02).abs().to(sdtype)
+    return words, s, -s
+
+
+def _graph_us(torch, fn, reps):
+    fn()
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        fn()
+    gr.replay()
+    torch.cuda.synchronize()
+    best = None
+    for _ in range(3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) * 1e3 / reps
+        best = t if best is None else min(best, t)
+    del gr
+    return best
+
+
+def run_bonsai(torch, q38, dev, quick=False):
+    """Bonsai ternary 2-bit projections with Hadamard-rotated activations (rotation, then the
+    product: q38_hadamard_quantized_matmul through HadamardQuantizedLinear), block 256,
+    group 64, bf16 scales, N x K in {17408 x 5120, 5120 x 17408}, M in {1, 8, 2048};
+    CUDA-graph replays over 8 weight copies (more than L2).  Also the published pack's layout
+    (group 128, f16 scales and biases, block 1024) at decode, bf16 activations."""
+    out = {}
+    g = torch.Generator(device=dev).manual_seed(4040)
+    copies = 8
+    for (N, K) in ((17408, 5120), (5120, 17408)):
+        mods = []
+        for _ in range(copies):
+            w, s, b = _ternary_weight(torch, dev, g, N, K, GROUP, torch.bfloat16)
+            signs = torch.where(torch.rand(K, generator=g, device=dev) < 0.5, -1.0, 1.0)
+            mods.append(q38.HadamardQuantizedLinear(q38.QuantizedLinear(w, s, b, None, GROUP, 2), signs, 256))
+        wbytes = N * K // 4 + N * (K // GROUP) * 4
+        for M in ((1, 8) if quick else (1, 8, 2048)):
+            x = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+            reps = 8 if M == 2048 else 200
+
+            def fn():
+                for i in range(reps):
+                    mods[i % copies](x)
+
+            us = _graph_us(torch, fn, reps)
+            row = {"us": round(us, 2), "GBps": round((wbytes + 2 * M * K + 2 * M * N) / (us * 1e-6) / 1e9, 1)}
+            if M == 2048:
+                row["TFLOPs"] = round(2 * M * N * K / (us * 1e-6) / 1e12, 1)
+            out[f"{N}x{K} M={M}"] = row
+        del mods
+    # the published pack's layout at decode: group 128, f16 scales, block 1024
+    N, K = 17408, 5120
+    mods = []
+    for _ in range(copies):
+        w, s, b = _ternary_weight(torch, dev, g, N, K, 128, torch.float16)
+        signs = torch.where(torch.rand(K, generator=g, device=dev) < 0.5, -1.0, 1.0)
+        mods.append(q38.HadamardQuantizedLinear(q38.QuantizedLinear(w, s, b, None, 128, 2), signs, 1024))
+    for M in (1, 8):
+        x = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+
+        def fn2():
+            for i in range(100):
+                mods[i % copies](x)
+
+        us = _graph_us(torch, fn2, 100)
+        wbytes = N * K // 4 + N * (K // 128) * 4
+        out[f"pack layout g128 f16 {N}x{K} M={M}"] = {"us": round(us, 2),
+                                                      "GBps": round(wbytes / (us * 1e-6) / 1e9, 1)}
+    del mods
+    return {"workload": "Bonsai ternary 2-bit: rotation (block 256) + product, group 64 bf16; ternary codes, "
+                        "bias = -scale", "per_case": out,
+            "timing": "CUDA-graph replays over 8 weight copies, CUDA events, best of 3"}
+
+
+def run_lm_head(torch, q38, dev, quick=False):
+    """Tied output projection of a 248,320-token vocabulary (4-bit g64, K = 5120, 636 MB of
+    codes, larger than L2) at M = 1 and 8, and the embedding lookup of 1 and 8 ids."""
+    rows, K, bits = 248320, 5120, 4
+    g = torch.Generator(device=dev).manual_seed(5050)
+    c = torch.randint(-2 ** 31, 2 ** 31 - 1, (rows, K * bits // 32), dtype=torch.int32, device=dev, generator=g)
+    s = (torch.rand((rows, K // GROUP), device=dev, generator=g) * 0.01).to(torch.bfloat16)
+    b = ((torch.rand((rows, K // GROUP), device=dev, generator=g) - 0.5) * 0.02).to(torch.bfloat16)
+    emb = q38.QuantizedEmbedding(c, s, b, GROUP, bits)
+    wbytes = rows * K * bits // 8 + rows * (K // GROUP) * 4
+    out = {}
+    for M in (1, 8):
+        x = torch.randn((M, K), device=dev, generator=g).to(torch.bfloat16)
+        reps = 10 if quick else 40
+
+        def fn():
+            for _ in range(reps):
+                emb.as_linear(x)
+
+        us = _graph_us(torch, fn, reps)
+        out[f"as_linear M={M}"] = {"us": round(us, 2), "GBps": round(wbytes / (us * 1e-6) / 1e9, 1)}
+    for n in (1, 8):
+        ids = torch.randint(0, rows, (n,), device=dev, generator=g, dtype=torch.int32)
+
+        def fl():
+            for _ in range(100):
+                emb(ids)
+
+        out[f"lookup ids={n}"] = {"us": round(_graph_us(torch, fl, 100), 2)}
+    del emb, c, s, b
+    return {"workload": "248,320 x 5120 4-bit g64 embedding: tied output projection and lookup",
+            "weight_bytes": wbytes, "per_case": out, "timing": "CUDA-graph replays, CUDA events, best of 3"}
+
+
 # ----------------------------------------------------------------------------- MoE
 MOE = {"H": 2048, "I": 512, "E": 512, "k": 10, "bits": 3}
 MOE_T = [1, 8, 64, 4096]
@@ -689,6 +811,8 @@ def run_ours(args, rank, world, local_rank):
         prefill = None if args.skip_prefill else run_prefill(torch, q38, dev, stream, world, dist, args.quick)
     gate_up = None if (args.skip_prefill or world > 1) else run_gate_up(torch, q38, O, dev, stream, args.quick)
     load = None if (args.skip_prefill or world > 1) else run_loader(torch, q38, dev, args.quick)
+    bonsai = None if (args.skip_prefill or world > 1) else run_bonsai(torch, q38, dev, args.quick)
+    lm_head = None if (args.skip_prefill or world > 1) else run_lm_head(torch, q38, dev, args.quick)
 
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
@@ -722,6 +846,8 @@ def run_ours(args, rank, world, local_rank):
         "prefill": prefill,
         "gate_up": gate_up,
         "loader": load,
+        "bonsai": bonsai,
+        "lm_head": lm_head,
     }
     return line
 

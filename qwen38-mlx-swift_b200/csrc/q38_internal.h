@@ -79,6 +79,12 @@ bool qgemv_fast_supported(int64_t M, int64_t K, int group, int bits, q38_dtype x
 q38_status embedding_launch(q38_ctx* ctx, const int32_t* ids, int64_t n, const uint32_t* w, const void* s,
                             const void* b, q38_dtype sd, int64_t rows, int64_t K, int group, int bits, void* out,
                             q38_dtype od);
+// Decode product over the Bonsai 2 pack layout: 2-bit codes, f16 scales and biases, group 128,
+// bf16 x, K % 1024 == 0, M <= 16.
+bool qgemv_pack_supported(int64_t M, int64_t K, int group, int bits, q38_dtype xd, q38_dtype sd,
+                          const void* x, const void* w, const void* s, const void* b);
+q38_status qgemv_pack(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w, const void* s,
+                      const void* b, int64_t N, void* y);
 q38_status qgemv_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w,
                       const void* s, const void* b, int64_t N, int bits, void* y);
 // h = bf16(silu(x.Wg^T) * (x.Wu^T)) in one decode pass (same conditions as qgemv_fast for

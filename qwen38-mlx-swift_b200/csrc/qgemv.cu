@@ -311,7 +311,20 @@ __global__ void __launch_bounds__(256) qgemv_epilogue_glu(float* __restrict__ ws
     }
 }
 
-template <int BITS, int MP, int TB>
+// An f16 value (11 significant bits) as fp32 and as an exact sum of two bf16 values (8 and
+// at most 3 significant bits), each duplicated into both halves of a word.
+__device__ __forceinline__ void split_f16(uint16_t h, float& f, uint32_t& hi2, uint32_t& lo2) {
+    f = __half2float(__ushort_as_half(h));
+    const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(f));
+    const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(f - __uint_as_float(hi << 16)));
+    hi2 = hi | (hi << 16);
+    lo2 = lo | (lo << 16);
+}
+
+// PACK: f16 scales and biases with group 128 (the layout of the Bonsai 2 packs); each 64-k
+// subgroup uses the scale of its 128-group, read from a stage box that holds the 8 groups of
+// an aligned pair of chunks.
+template <int BITS, int MP, int TB, bool PACK = false>
 __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 1 ? 2 : 1)) qgemv_main(const __grid_constant__ WeightMaps maps,
                                                                       const __grid_constant__ WeightMaps maps_b,
                                                                       const MainArgs a) {
@@ -431,8 +444,9 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
                     }
                 }
                 uint8_t* sc = sbase + NCW * F::SUB_BYTES;
-                tma_load_2d(sc, &wm.scales, fb, chunk * GROUPS, lt * 64);
-                if (a.has_bias) tma_load_2d(sc + 1024, &wm.biases, fb, chunk * GROUPS, lt * 64);
+                const int gx = PACK ? (chunk >> 1) * GROUPS : chunk * GROUPS;  // 16-byte aligned
+                tma_load_2d(sc, &wm.scales, fb, gx, lt * 64);
+                if (a.has_bias) tma_load_2d(sc + 1024, &wm.biases, fb, gx, lt * 64);
                 if (++slot == a.stages) {
                     slot = 0;
                     ph ^= 1;
@@ -539,9 +553,25 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
             const uint8_t* sbase = stage0 + static_cast<size_t>(slot) * a.stage_bytes;
             const uint8_t* sub = sbase + sw_i * 16 * F::SW;
             const uint16_t* scl = reinterpret_cast<const uint16_t*>(sbase + NCW * F::SUB_BYTES) + srow0 * GROUPS;
-            // scales of rows g and g+8 for groups 2t, 2t+1 (one word each), biases likewise
-            const uint32_t* sw = reinterpret_cast<const uint32_t*>(scl) + t;
-            const uint32_t s_g = sw[0], s_g8 = sw[32], b_g = sw[256], b_g8 = sw[256 + 32];
+            // scales of rows g and g+8 for groups 2t, 2t+1 (one bf16 word each), biases likewise;
+            // PACK: both groups lie in 128-group t, whose f16 scale is split into bf16 high and
+            // low words for the offset-and-bias steps and used in fp32 for the group sums
+            uint32_t s_g, s_g8, b_g, b_g8, s_gl = 0, s_g8l = 0, b_gl = 0, b_g8l = 0;
+            float f_g = 0.f, f_g8 = 0.f;
+            if constexpr (!PACK) {
+                const uint32_t* sw = reinterpret_cast<const uint32_t*>(scl) + t;
+                s_g = sw[0];
+                s_g8 = sw[32];
+                b_g = sw[256];
+                b_g8 = sw[256 + 32];
+            } else {
+                const uint16_t* sp = scl + (chunk & 1) * 4 + t;
+                float fb;
+                split_f16(sp[0], f_g, s_g, s_gl);
+                split_f16(sp[64], f_g8, s_g8, s_g8l);
+                split_f16(sp[512], fb, b_g, b_gl);
+                split_f16(sp[512 + 64], fb, b_g8, b_g8l);
+            }
 #pragma unroll
             for (int tb = 0; tb < TB; ++tb)
 #pragma unroll
@@ -630,11 +660,18 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
                         for (int e = 0; e < 4; ++e) {
                             float sc;
                             if (MP == 1) {  // groups 2t, 2t+1: the words loaded above
-                                const uint32_t wv = (e >> 1) ? s_g8 : s_g;
-                                sc = __uint_as_float((e & 1) ? (wv & 0xFFFF0000u) : (wv << 16));
+                                if constexpr (PACK) {
+                                    sc = (e >> 1) ? f_g8 : f_g;
+                                } else {
+                                    const uint32_t wv = (e >> 1) ? s_g8 : s_g;
+                                    sc = __uint_as_float((e & 1) ? (wv & 0xFFFF0000u) : (wv << 16));
+                                }
                             } else {
                                 const int gi = (gset0 + s) * GPER + (2 * t) / MP;
-                                sc = bf16_bits_to_f32(scl[((e >> 1) << 6) + gi]);
+                                if constexpr (PACK)
+                                    sc = __half2float(__ushort_as_half(scl[((e >> 1) << 6) + (chunk & 1) * 4 + gi / 2]));
+                                else
+                                    sc = bf16_bits_to_f32(scl[((e >> 1) << 6) + gi]);
                             }
                             if (F::F16) sc *= xup;
 #pragma unroll
@@ -658,6 +695,10 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
                     bb = *reinterpret_cast<const uint4*>(xf + mt * F::XF_PER_M + F::XF_FRAG + t * 16);
                 mma_bf16_16816(acc[tb], s_g, s_g8, b_g, b_g8, bb.x, bb.y, acc[tb]);
                 mma_bf16_16816(acc[tb], s_g, s_g8, b_g, b_g8, bb.z, bb.w, acc[tb]);
+                if constexpr (PACK) {  // the low bf16 parts of the f16 scales and biases
+                    mma_bf16_16816(acc[tb], s_gl, s_g8l, b_gl, b_g8l, bb.x, bb.y, acc[tb]);
+                    mma_bf16_16816(acc[tb], s_gl, s_g8l, b_gl, b_g8l, bb.z, bb.w, acc[tb]);
+                }
             }
         }
         // Release the stage before adding the sums to the workspace: the arrive orders this
@@ -711,22 +752,22 @@ bool make_plan(int M, int K, int N, Plan& p, bool two_weights = false) {
 
 // Encodes the tensor maps of a weight (codes in two box heights, scales, biases).
 template <int BITS>
-bool make_maps(const uint32_t* w, const void* s, const void* b, int K, int N, WeightMaps* m) {
+bool make_maps(const uint32_t* w, const void* s, const void* b, int K, int N, WeightMaps* m, bool pack = false) {
     using F = Fmt<BITS>;
     const uint64_t kw = static_cast<uint64_t>(K) * BITS / 32;
     const CUtensorMapSwizzle swz = F::SW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    const CUtensorMapDataType sdt = pack ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const int group = pack ? 128 : 64;
     return make_map_2d(&m->codes16, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w, kw, N, F::SW / 4, 16, swz) &&
            make_map_2d(&m->codes64, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w, kw, N, F::SW / 4, 64, swz) &&
-           make_map_2d(&m->scales, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s, K / 64, N, GROUPS, 64,
-                       CU_TENSOR_MAP_SWIZZLE_NONE) &&
-           make_map_2d(&m->biases, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b ? b : s, K / 64, N, GROUPS, 64,
-                       CU_TENSOR_MAP_SWIZZLE_NONE);
+           make_map_2d(&m->scales, sdt, 2, s, K / group, N, GROUPS, 64, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+           make_map_2d(&m->biases, sdt, 2, b ? b : s, K / group, N, GROUPS, 64, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 // Encoded maps of recently used weights.  A decode loop calls the same projections again
 // and again, and the encoding depends only on the pointers and the shape, so a hit is
 // always valid (a new weight at an old address with the same shape encodes identically).
-template <int BITS>
+template <int BITS, bool PACK = false>
 bool cached_maps(const uint32_t* w, const void* s, const void* b, int K, int N, WeightMaps* maps) {
     struct Entry {
         const void* w;
@@ -746,7 +787,7 @@ bool cached_maps(const uint32_t* w, const void* s, const void* b, int K, int N, 
         *maps = e.maps;
         return true;
     }
-    if (!make_maps<BITS>(w, s, b, K, N, maps)) return false;
+    if (!make_maps<BITS>(w, s, b, K, N, maps, PACK)) return false;
     e.w = w;
     e.s = s;
     e.b = b;
@@ -758,13 +799,13 @@ bool cached_maps(const uint32_t* w, const void* s, const void* b, int K, int N, 
 }
 
 // Launches the main kernel and the epilogue with the given scratch.  Returns a CUDA error code.
-template <int BITS, int MP, int TB>
+template <int BITS, int MP, int TB, bool PACK = false>
 // With `maps_b` the tiles cover two weights of N rows each (gate, then up) and the epilogue
 // writes y = bf16(silu(gate) * up) [M, N]; the partial sums then take M x 2N floats.
 cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x, int M, int K,
                            const WeightMaps& maps, bool has_bias, int N, void* y, float* part, uint32_t* status,
                            cudaStream_t stream, const WeightMaps* maps_b = nullptr) {
-    auto kmain = qgemv_main<BITS, MP, TB>;
+    auto kmain = qgemv_main<BITS, MP, TB, PACK>;
     // per template instance and device: smem opt-in and occupancy at the largest ring
     static std::mutex mu;
     static bool configured[64] = {};
@@ -866,6 +907,28 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
     return Q38_OK;
 }
 
+// The same product over f16 scales with group 128 (PACK).
+template <int BITS, int MP, int TB>
+q38_status launch_pack(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, const void* s,
+                       const void* b, int N, void* y) {
+    Plan p;
+    if (!make_plan<BITS>(M, K, N, p)) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: shape too large");
+    uint32_t* cnt = nullptr;
+    float* part = nullptr;
+    q38_status st = ensure_zero_region(ctx, 0, static_cast<size_t>(M) * N, &cnt, &part);
+    if (st != Q38_OK) return st;
+    WeightMaps maps;
+    if (!cached_maps<BITS, true>(w, s, b, K, N, &maps))
+        return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: tensor map encoding failed");
+    const cudaError_t e = launch_kernels<BITS, MP, TB, true>(p, ctx->device, ctx->num_sms, x, M, K, maps,
+                                                             b != nullptr, N, y, part, ctx->d_status, ctx->stream);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: launch failed: %s", cudaGetErrorString(e));
+    }
+    return Q38_OK;
+}
+
 // Gate and up projections of an MLP in one pass: h = bf16(silu(x.Wg^T) * (x.Wu^T)).
 template <int BITS, int MP, int TB>
 q38_status launch_gate_up(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* wg, const void* sg,
@@ -910,6 +973,22 @@ bool qgemv_fast_supported(int64_t M, int64_t K, int group, int bits, q38_dtype x
     if (!al(x) || !al(w) || !al(s) || (b && !al(b))) return false;
     (void)y;
     return true;
+}
+
+bool qgemv_pack_supported(int64_t M, int64_t K, int group, int bits, q38_dtype xd, q38_dtype sd,
+                          const void* x, const void* w, const void* s, const void* b) {
+    if (M < 1 || M > 16 || group != 128 || bits != 2 || K <= 0 || K % 1024 != 0) return false;
+    if (xd != Q38_BF16 || sd != Q38_F16) return false;
+    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    return al(x) && al(w) && al(s) && (!b || al(b));
+}
+
+q38_status qgemv_pack(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w, const void* s,
+                      const void* b, int64_t N, void* y) {
+    const int m = static_cast<int>(M), k = static_cast<int>(K), n = static_cast<int>(N);
+    return dispatch_m<2>(m, [&](auto mp, auto tb) {
+        return launch_pack<2, decltype(mp)::value, decltype(tb)::value>(ctx, x, m, k, w, s, b, n, y);
+    });
 }
 
 q38_status qgemv_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w,
