@@ -33,53 +33,6 @@ __device__ __forceinline__ void st_f32<__half>(__half* p, float v) {
     *p = __float2half_rn(v);
 }
 
-// One warp per (row, block); lane holds E = block/32 consecutive elements.
-template <typename T, int E>
-__global__ void __launch_bounds__(256) fwht_warp_kernel(const T* __restrict__ x, int64_t nblocks,
-                                                        int64_t D, const float* __restrict__ signs,
-                                                        int inverse, float scale,
-                                                        T* __restrict__ y) {
-    constexpr int BLOCK = 32 * E;
-    const int lane = threadIdx.x & 31;
-    const int64_t bid = blockIdx.x * 8LL + (threadIdx.x >> 5);
-    if (bid >= nblocks) return;
-    const int64_t per_row = D / BLOCK;
-    const int64_t row = bid / per_row, col0 = (bid % per_row) * BLOCK + lane * E;
-    const T* src = x + row * D + col0;
-    float v[E];
-#pragma unroll
-    for (int i = 0; i < E; ++i) {
-        float f = ld_f32(src + i);
-        if (!inverse && signs) f = f * signs[col0 + i];
-        v[i] = f;
-    }
-#pragma unroll
-    for (int h = 1; h < E; h <<= 1)
-#pragma unroll
-        for (int i = 0; i < E; ++i)
-            if ((i & h) == 0) {
-                const float a = v[i], b = v[i + h];
-                v[i] = a + b;
-                v[i + h] = a - b;
-            }
-#pragma unroll
-    for (int lh = 1; lh < 32; lh <<= 1) {
-        const bool upper = (lane & lh) != 0;
-#pragma unroll
-        for (int i = 0; i < E; ++i) {
-            const float p = __shfl_xor_sync(0xffffffffu, v[i], lh);
-            v[i] = upper ? (p - v[i]) : (v[i] + p);
-        }
-    }
-    T* dst = y + row * D + col0;
-#pragma unroll
-    for (int i = 0; i < E; ++i) {
-        float f = v[i] * scale;
-        if (inverse && signs) f = f * signs[col0 + i];
-        st_f32(dst + i, f);
-    }
-}
-
 // One CTA per (row, block) through shared memory, any power-of-two block <= 8192.
 template <typename T>
 __global__ void __launch_bounds__(512) fwht_smem_kernel(const T* __restrict__ x, int64_t D,
@@ -111,6 +64,85 @@ __global__ void __launch_bounds__(512) fwht_smem_kernel(const T* __restrict__ x,
     }
 }
 
+// Blocks of up to 4096: each thread holds 4 consecutive elements of one block (B / 4
+// threads per block, 256 / (B / 4) blocks per CTA of at least 256 threads).  Butterfly
+// stages h = 1, 2 run in registers, h = 4 .. 64 by warp shuffles, larger h through shared
+// memory, all in increasing h with the operands of the other kernels (lower element a + b,
+// upper a - b), so the results are the same bit for bit.
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(1024) fwht_block_kernel(const T* __restrict__ x, int64_t nblocks, int64_t D,
+                                                          int block, const float* __restrict__ signs,
+                                                          int inverse, float scale, T* __restrict__ y) {
+    constexpr int E = 4;
+    extern __shared__ float sv[];
+    const int tpb = block / E;                            // threads per block
+    const int local = threadIdx.x / tpb;                  // block within the CTA
+    const int lt = threadIdx.x % tpb;                     // thread within the block
+    const int64_t bid = static_cast<int64_t>(blockIdx.x) * (blockDim.x / tpb) + local;
+    const bool live = bid < nblocks;
+    const int64_t per_row = D / block;
+    const int64_t row = live ? bid / per_row : 0, col0 = live ? (bid % per_row) * block + lt * E : 0;
+    float v[E];
+    if (VEC && live) {  // the 4 elements in one 8-byte load
+        const uint2 u = *reinterpret_cast<const uint2*>(x + row * D + col0);
+        const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+        for (int i = 0; i < E; ++i) v[i] = ld_f32(e + i);
+    } else {
+#pragma unroll
+        for (int i = 0; i < E; ++i) v[i] = live ? ld_f32(x + row * D + col0 + i) : 0.0f;
+    }
+    if (!inverse && signs && live)
+#pragma unroll
+        for (int i = 0; i < E; ++i) v[i] = v[i] * signs[col0 + i];
+#pragma unroll
+    for (int h = 1; h < E; h <<= 1)
+#pragma unroll
+        for (int i = 0; i < E; ++i)
+            if ((i & h) == 0) {
+                const float a = v[i], b = v[i + h];
+                v[i] = a + b;
+                v[i + h] = a - b;
+            }
+    const int lane = threadIdx.x & 31;
+    for (int lh = 1; lh < 32 && lh < tpb; lh <<= 1) {
+        const bool upper = (lane & lh) != 0;
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+            const float p = __shfl_xor_sync(0xffffffffu, v[i], lh);
+            v[i] = upper ? (p - v[i]) : (v[i] + p);
+        }
+    }
+    float* mine = sv + local * block;
+    for (int th = 32; th < tpb; th <<= 1) {  // partner thread lt ^ th, element distance th * E
+#pragma unroll
+        for (int i = 0; i < E; ++i) mine[lt * E + i] = v[i];
+        __syncthreads();
+        const bool upper = (lt & th) != 0;
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+            const float p = mine[(lt ^ th) * E + i];
+            v[i] = upper ? (p - v[i]) : (v[i] + p);
+        }
+        __syncthreads();
+    }
+    if (!live) return;
+    T* dst = y + row * D + col0;
+    __align__(8) T o[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+        float f = v[i] * scale;
+        if (inverse && signs) f = f * signs[col0 + i];
+        st_f32(o + i, f);
+    }
+    if (VEC) {
+        *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(o);
+    } else {
+#pragma unroll
+        for (int i = 0; i < E; ++i) dst[i] = o[i];
+    }
+}
+
 template <typename T>
 q38_status launch(q38_ctx* ctx, const void* x, int64_t rows, int64_t D, const float* signs,
                   int block, int inverse, void* y) {
@@ -118,18 +150,29 @@ q38_status launch(q38_ctx* ctx, const void* x, int64_t rows, int64_t D, const fl
     const int64_t nblocks = rows * (D / block);
     const T* xs = static_cast<const T*>(x);
     T* ys = static_cast<T*>(y);
-    const unsigned grid = static_cast<unsigned>((nblocks + 7) / 8);
-    switch (block) {
-        case 256: fwht_warp_kernel<T, 8><<<grid, 256, 0, ctx->stream>>>(xs, nblocks, D, signs, inverse, scale, ys); break;
-        case 512: fwht_warp_kernel<T, 16><<<grid, 256, 0, ctx->stream>>>(xs, nblocks, D, signs, inverse, scale, ys); break;
-        case 1024: fwht_warp_kernel<T, 32><<<grid, 256, 0, ctx->stream>>>(xs, nblocks, D, signs, inverse, scale, ys); break;
-        default: {
-            if (nblocks > 0x7fffffffLL) return fail(ctx, Q38_ERR_UNSUPPORTED, "hadamard_rotate: too many blocks");
-            const int threads = block / 2 < 512 ? (block / 2 < 32 ? 32 : block / 2) : 512;
-            fwht_smem_kernel<T><<<static_cast<unsigned>(nblocks), threads, block * sizeof(float), ctx->stream>>>(
-                xs, D, block, signs, inverse, scale, ys);
-        }
+    if (block >= 4 && block <= 4096) {
+        // 4 elements per thread, at least 256 threads per CTA
+        const int tpb = block / 4;
+        const int per_cta = tpb >= 256 ? 1 : 256 / tpb;
+        const int64_t ctas = (nblocks + per_cta - 1) / per_cta;
+        if (ctas > 0x7fffffffLL) return fail(ctx, Q38_ERR_UNSUPPORTED, "hadamard_rotate: too many blocks");
+        const unsigned threads = static_cast<unsigned>(tpb * per_cta);
+        const size_t smem = static_cast<size_t>(per_cta) * block * sizeof(float);
+        // 8-byte accesses when both buffers allow them (rows of D elements keep the alignment)
+        const bool vec = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 7u) == 0;
+        if (vec)
+            fwht_block_kernel<T, true><<<static_cast<unsigned>(ctas), threads, smem, ctx->stream>>>(
+                xs, nblocks, D, block, signs, inverse, scale, ys);
+        else
+            fwht_block_kernel<T, false><<<static_cast<unsigned>(ctas), threads, smem, ctx->stream>>>(
+                xs, nblocks, D, block, signs, inverse, scale, ys);
+        return check_launch(ctx, "hadamard_rotate");
     }
+    // larger blocks: one CTA per block through shared memory
+    if (nblocks > 0x7fffffffLL) return fail(ctx, Q38_ERR_UNSUPPORTED, "hadamard_rotate: too many blocks");
+    const int threads = block / 2 < 512 ? (block / 2 < 32 ? 32 : block / 2) : 512;
+    fwht_smem_kernel<T><<<static_cast<unsigned>(nblocks), threads, block * sizeof(float), ctx->stream>>>(
+        xs, D, block, signs, inverse, scale, ys);
     return check_launch(ctx, "hadamard_rotate");
 }
 

@@ -151,10 +151,11 @@ def test_dequantize_bit_exact(q38, bits):
     np.testing.assert_array_equal(d.cpu().numpy(), O.dequantize(c, s, b, 64, bits))
 
 
-@pytest.mark.parametrize("block", [64, 256, 512, 1024, 2048])
+@pytest.mark.parametrize("block", [4, 16, 64, 128, 256, 512, 1024, 2048, 4096, 8192])
 @pytest.mark.parametrize("inverse", [False, True])
 def test_hadamard_bit_exact(q38, block, inverse):
-    D = 4096
+    # D = 4096 + block: the blocks do not fill the last CTA of the small-block kernel
+    D = 4096 + block if block <= 4096 else block
     x = O.normal_bf16(1000 + block, (5, D))
     signs = np.where((np.arange(D) * 7) % 5 < 2, -1.0, 1.0).astype(np.float32)
     ref = O.hadamard_rotate(x, block, signs, inverse)
@@ -163,6 +164,18 @@ def test_hadamard_bit_exact(q38, block, inverse):
     ref0 = O.hadamard_rotate(x, block, None, inverse)
     y0 = q38.hadamard_rotate(dev_bf16(x), None, block, inverse)
     np.testing.assert_array_equal(host_bf16(y0), ref0)
+
+
+def test_hadamard_unaligned_buffers(q38):
+    # x and y two bytes past an 8-byte boundary: element-wise accesses instead of 8-byte ones
+    block, D, rows = 256, 1024, 3
+    x = O.normal_bf16(1050, (rows, D))
+    xb = torch.zeros(rows * D + 1, dtype=torch.bfloat16, device="cuda")
+    xb[1:] = dev_bf16(x).reshape(-1)
+    xv = xb[1:].view(rows, D)
+    assert xv.data_ptr() % 8 == 2
+    y = q38.hadamard_rotate(xv, None, block)
+    np.testing.assert_array_equal(host_bf16(y.contiguous()), O.hadamard_rotate(x, block, None))
 
 
 @pytest.mark.parametrize("M", [1, 8])
