@@ -434,6 +434,33 @@ def run_moe_ep(torch, q38, dev, stream, world, rank, dist, quick=False):
         us = float(t.item())
         out[str(T)] = {"tokens_per_s": round(world * T / (us * 1e-6), 1), "us_per_layer": round(us, 2),
                        "tokens_per_rank": T}
+        if T <= 64:
+            # fixed-capacity exchange (no host synchronisation): the R layer calls captured
+            # in one CUDA graph with their NCCL exchanges, replayed
+            fixed = parallel.ExpertParallelMoE(wr, mine, E, k, GROUP, bits, capacity=T)
+            for x in xs:
+                fixed(x)
+            torch.cuda.synchronize()
+            dist.barrier()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for x in xs:
+                    fixed(x)
+            graph.replay()
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            gus = e0.elapsed_time(e1) * 1e3 / (reps * R)
+            t = torch.tensor([gus], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            gus = float(t.item())
+            del graph  # released before the process group is destroyed
+            out[str(T)]["fixed_capacity_graph"] = {"tokens_per_s": round(world * T / (gus * 1e-6), 1),
+                                                   "us_per_layer": round(gus, 2)}
         del xs
     del moe, mine
     torch.cuda.synchronize()
@@ -444,7 +471,8 @@ def run_moe_ep(torch, q38, dev, stream, world, rank, dist, quick=False):
                        "parallelism": f"expert parallel x{world} ({epr} experts per GPU), T tokens per GPU",
                        "scaling": "weak",
                        "timing": "eager layer calls (all-to-all sizes are read on the host), CUDA events, "
-                                 "max over ranks"}}
+                                 "max over ranks; T <= 64 also with the fixed-capacity exchange captured in a "
+                                 "CUDA graph (fixed_capacity_graph)"}}
 
 
 def run_moe(torch, q38, dev, stream, world, dist, quick=False):
