@@ -969,6 +969,35 @@ def run_profile_prefill(args):
                                           "flops_per_launch": 2 * M * N * K, "mean_abs_y": float(y.float().abs().mean())}}))
 
 
+def run_profile_bonsai(args):
+    """Small fixed workload for ncu captures of the Bonsai 2 pack path: 12 rotated projections
+    (block 1024, then the group-128 f16-scale decode product) of 17408x5120 at M=1 over 8
+    weight copies (200 MB, more than L2), then 3 rotations of a 2048 x 5120 prompt at block
+    256."""
+    import torch
+    import q38
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(6060)
+    N, K = 17408, 5120
+    mods = []
+    for _ in range(8):
+        w, s, b = _ternary_weight(torch, dev, g, N, K, 128, torch.float16)
+        signs = torch.where(torch.rand(K, generator=g, device=dev) < 0.5, -1.0, 1.0)
+        mods.append(q38.HadamardQuantizedLinear(q38.QuantizedLinear(w, s, b, None, 128, 2), signs, 1024))
+    x = torch.randn((1, K), generator=g, device=dev).to(torch.bfloat16)
+    for i in range(12):
+        y = mods[i % 8](x)
+    xp = torch.randn((2048, K), generator=g, device=dev).to(torch.bfloat16)
+    for _ in range(3):
+        r = q38.hadamard_rotate(xp, None, 256)
+    torch.cuda.synchronize()
+    q38.check_device()
+    print(json.dumps({"profile_bonsai": {"N": N, "K": K, "projections": 12, "rotations_2048": 3,
+                                         "weight_bytes": N * K // 4 + N * (K // 128) * 4,
+                                         "mean_abs_y": float(y.float().abs().mean()),
+                                         "mean_abs_r": float(r.float().abs().mean())}}))
+
+
 def run_profile_moe(args):
     """One MoE layer (Flash-Next shapes) at T = --profile-t tokens, 2 calls, for ncu."""
     import torch
@@ -990,6 +1019,7 @@ def main():
     ap.add_argument("--profile-m", type=int, default=1)
     ap.add_argument("--profile-prefill", action="store_true")
     ap.add_argument("--profile-moe", action="store_true")
+    ap.add_argument("--profile-bonsai", action="store_true")
     ap.add_argument("--profile-t", type=int, default=4096)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
@@ -1013,6 +1043,9 @@ def main():
         return
     if args.profile_moe:
         run_profile_moe(args)
+        return
+    if args.profile_bonsai:
+        run_profile_bonsai(args)
         return
     if args.impl == "reference":
         line = run_reference(args, rank, world)
