@@ -325,6 +325,28 @@ def run_bonsai(torch, q38, dev, quick=False):
         wbytes = N * K // 4 + N * (K // 128) * 4
         out[f"pack layout g128 f16 {N}x{K} M={M}"] = {"us": round(us, 2),
                                                       "GBps": round(wbytes / (us * 1e-6) / 1e9, 1)}
+    # MLP gate + up over the pack layout: one rotation and one pass over both weights
+    # (q38_hadamard_quantized_gate_up) against two rotated projections and the SiLU product
+    sg = mods[0].signs
+    pairs = [((mods[2 * i].weight, mods[2 * i].scales, mods[2 * i].biases),
+              (mods[2 * i + 1].weight, mods[2 * i + 1].scales, mods[2 * i + 1].biases)) for i in range(copies // 2)]
+    for M in (1, 8):
+        x = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+
+        def fused():
+            for i in range(100):
+                q38.hadamard_quantized_gate_up(x, sg, 1024, *pairs[i % len(pairs)], 128, 2)
+
+        def separate():
+            for i in range(100):
+                gp, up = pairs[i % len(pairs)]
+                q38.silu_mul(q38.quantized_matmul(q38.hadamard_rotate(x, sg, 1024), *gp, True, 128, 2),
+                             q38.quantized_matmul(q38.hadamard_rotate(x, sg, 1024), *up, True, 128, 2))
+
+        fus, sep = _graph_us(torch, fused, 100), _graph_us(torch, separate, 100)
+        out[f"pack layout MLP gate+up {N}x{K} M={M}"] = {
+            "fused_us": round(fus, 2), "separate_us": round(sep, 2),
+            "fused_GBps": round(2 * (N * K // 4 + N * (K // 128) * 4) / (fus * 1e-6) / 1e9, 1)}
     del mods
     return {"workload": "Bonsai ternary 2-bit: rotation (block 256) + product, group 64 bf16; ternary codes, "
                         "bias = -scale", "per_case": out,

@@ -286,6 +286,21 @@ Q38_API q38_status q38_quantized_gate_up(q38_ctx* ctx, const void* x, int64_t M,
                                          q38_dtype scales_dtype, int64_t N, int group_size, int bits,
                                          q38_mode mode, void* h);
 
+/* Gate and up projections of a Bonsai 2 MLP from one rotation of x: h = bf16(silu(bf16(
+ * xr.Wg^T)) * bf16(xr.Wu^T)) with xr = hadamardRotate(x, signs, block) rounded to bf16.  The
+ * reference applies Qwen38HadamardQuantizedLinear to gate and up separately
+ * (Sources/Qwen38Core/Bonsai2/Qwen38HadamardModules.swift:37-39, signs before the transform);
+ * the pack stores the same signs for every module of one input width, so the two rotations
+ * are one, and the products take one pass over both weights where the decode kernel takes
+ * the layout (M <= 16: bf16 scales in groups of 64, or the pack's f16 scales in groups of
+ * 128 with K % 1024 == 0).  Callers whose gate and up signs differ call
+ * q38_hadamard_quantized_matmul twice instead.  Arguments as q38_quantized_gate_up and
+ * q38_hadamard_rotate. */
+Q38_API q38_status q38_hadamard_quantized_gate_up(q38_ctx* ctx, const void* x, int64_t M, int64_t K,
+    q38_dtype x_dtype, const float* signs, int block, const uint32_t* w_gate, const void* s_gate, const void* b_gate,
+    const uint32_t* w_up, const void* s_up, const void* b_up, q38_dtype scales_dtype, int64_t N, int group_size,
+    int bits, void* h);
+
 /* Allocation-free decode product.  No counterpart in the reference: it exists for
  * callers that must not allocate device memory on the calling path (a host framework
  * that owns all device memory and hands a plugin only its input and output buffers, or

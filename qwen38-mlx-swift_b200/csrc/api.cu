@@ -266,34 +266,88 @@ q38_status q38_quantized_matmul(q38_ctx* ctx, const void* x, int64_t M, int64_t 
 
 
 
-q38_status q38_quantized_gate_up(q38_ctx* ctx, const void* x, int64_t M, int64_t K, q38_dtype x_dtype,
-                                 const uint32_t* w_gate, const void* s_gate, const void* b_gate,
-                                 const uint32_t* w_up, const void* s_up, const void* b_up, q38_dtype scales_dtype,
-                                 int64_t N, int group_size, int bits, q38_mode mode, void* h) {
-    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
-    q38_status st = check_format(ctx, "quantized_gate_up", K, group_size, bits, mode);
+}  // extern "C"
+
+namespace {
+
+// Checks shared by the gate/up entries.
+q38_status gate_up_check(q38_ctx* ctx, const char* op, const void* x, int64_t M, int64_t K, q38_dtype x_dtype,
+                         const uint32_t* w_gate, const void* s_gate, const void* b_gate, const uint32_t* w_up,
+                         const void* s_up, const void* b_up, q38_dtype scales_dtype, int64_t N, int group_size,
+                         int bits, q38_mode mode, void* h) {
+    q38_status st = check_format(ctx, op, K, group_size, bits, mode);
     if (st != Q38_OK) return st;
-    if (x_dtype != Q38_BF16) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "quantized_gate_up: x must be bf16");
-    if (!valid_dtype(scales_dtype)) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "quantized_gate_up: bad scales dtype");
-    if (M < 0 || N <= 0) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "quantized_gate_up: bad shape M=%lld N=%lld", (long long)M, (long long)N);
-    if (M == 0) return Q38_OK;
-    if (!x || !w_gate || !s_gate || !w_up || !s_up || !h)
-        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "quantized_gate_up: null pointer");
+    if (x_dtype != Q38_BF16) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "%s: x must be bf16", op);
+    if (!valid_dtype(scales_dtype)) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "%s: bad scales dtype", op);
+    if (M < 0 || N <= 0) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "%s: bad shape M=%lld N=%lld", op, (long long)M, (long long)N);
+    if (M > 0 && (!x || !w_gate || !s_gate || !w_up || !s_up || !h))
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "%s: null pointer", op);
     if ((b_gate == nullptr) != (b_up == nullptr))
-        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "quantized_gate_up: gate and up must both have biases or neither");
-    if ((st = set_device(ctx)) != Q38_OK) return st;
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "%s: gate and up must both have biases or neither", op);
+    return Q38_OK;
+}
+
+// h = bf16(silu(x.Wg^T) * x.Wu^T): one pass over both weights where the decode kernel takes
+// the layout, otherwise the two products and the SiLU product, with the up product at byte
+// `up_offset` of the activation buffer (the bytes before it may hold x).
+q38_status gate_up_run(q38_ctx* ctx, const void* x, int64_t M, int64_t K, q38_dtype x_dtype,
+                       const uint32_t* w_gate, const void* s_gate, const void* b_gate, const uint32_t* w_up,
+                       const void* s_up, const void* b_up, q38_dtype scales_dtype, int64_t N, int group_size, int bits,
+                       q38_mode mode, void* h, size_t up_offset) {
     if (qgemv_fast_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w_gate, s_gate, b_gate, h) &&
         qgemv_fast_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w_up, s_up, b_up, h))
         return qgemv_gate_up_fast(ctx, x, M, K, w_gate, s_gate, b_gate, w_up, s_up, b_up, N, bits, h);
-    // otherwise: gate product into h, up product into the auxiliary buffer, then h = silu(h) * up
-    void* up = nullptr;
-    if ((st = ensure_aux(ctx, static_cast<size_t>(M) * N * 2, &up)) != Q38_OK) return st;
+    if (qgemv_pack_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w_gate, s_gate, b_gate) &&
+        qgemv_pack_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w_up, s_up, b_up) &&
+        (reinterpret_cast<uintptr_t>(h) & 15u) == 0)
+        return qgemv_gate_up_pack(ctx, x, M, K, w_gate, s_gate, b_gate, w_up, s_up, b_up, N, h);
+    void* base = nullptr;
+    q38_status st;
+    if ((st = ensure_aux(ctx, up_offset + static_cast<size_t>(M) * N * 2, &base)) != Q38_OK) return st;
+    void* up = static_cast<uint8_t*>(base) + up_offset;
     if ((st = q38_quantized_matmul(ctx, x, M, K, x_dtype, w_gate, s_gate, b_gate, scales_dtype, N, 1, group_size,
                                    bits, mode, h)) != Q38_OK ||
         (st = q38_quantized_matmul(ctx, x, M, K, x_dtype, w_up, s_up, b_up, scales_dtype, N, 1, group_size, bits,
                                    mode, up)) != Q38_OK)
         return st;
     return q38_silu_mul(ctx, h, up, M * N, h);
+}
+
+}  // namespace
+
+extern "C" {
+
+q38_status q38_quantized_gate_up(q38_ctx* ctx, const void* x, int64_t M, int64_t K, q38_dtype x_dtype,
+                                 const uint32_t* w_gate, const void* s_gate, const void* b_gate,
+                                 const uint32_t* w_up, const void* s_up, const void* b_up, q38_dtype scales_dtype,
+                                 int64_t N, int group_size, int bits, q38_mode mode, void* h) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    q38_status st = gate_up_check(ctx, "quantized_gate_up", x, M, K, x_dtype, w_gate, s_gate, b_gate, w_up, s_up,
+                                  b_up, scales_dtype, N, group_size, bits, mode, h);
+    if (st != Q38_OK || M == 0) return st;
+    if ((st = set_device(ctx)) != Q38_OK) return st;
+    return gate_up_run(ctx, x, M, K, x_dtype, w_gate, s_gate, b_gate, w_up, s_up, b_up, scales_dtype, N, group_size,
+                       bits, mode, h, 0);
+}
+
+q38_status q38_hadamard_quantized_gate_up(q38_ctx* ctx, const void* x, int64_t M, int64_t K, q38_dtype x_dtype,
+                                          const float* signs, int block, const uint32_t* w_gate, const void* s_gate,
+                                          const void* b_gate, const uint32_t* w_up, const void* s_up,
+                                          const void* b_up, q38_dtype scales_dtype, int64_t N, int group_size,
+                                          int bits, void* h) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    q38_status st = gate_up_check(ctx, "hadamard_quantized_gate_up", x, M, K, x_dtype, w_gate, s_gate, b_gate, w_up,
+                                  s_up, b_up, scales_dtype, N, group_size, bits, Q38_MODE_AFFINE, h);
+    if (st != Q38_OK || M == 0) return st;
+    if ((st = set_device(ctx)) != Q38_OK) return st;
+    // the activation buffer holds the rotated x (rounded to bf16, as the reference rounds it
+    // before each product), followed by room for the up product of the general path
+    const size_t xbytes = align_up(static_cast<size_t>(M) * K * 2, 256);
+    void* xr = nullptr;
+    if ((st = ensure_aux(ctx, xbytes + static_cast<size_t>(M) * N * 2, &xr)) != Q38_OK) return st;
+    if ((st = q38_hadamard_rotate(ctx, x, M, K, x_dtype, signs, block, 0, xr)) != Q38_OK) return st;
+    return gate_up_run(ctx, xr, M, K, x_dtype, w_gate, s_gate, b_gate, w_up, s_up, b_up, scales_dtype, N, group_size,
+                       bits, Q38_MODE_AFFINE, h, xbytes);
 }
 
 q38_status q38_dequantize(q38_ctx* ctx, const uint32_t* w, const void* scales, const void* biases,

@@ -89,6 +89,10 @@ q38_status qgemv_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const u
                       const void* s, const void* b, int64_t N, int bits, void* y);
 // h = bf16(silu(x.Wg^T) * (x.Wu^T)) in one decode pass (same conditions as qgemv_fast for
 // both weights, which must both have biases or neither).
+// Gate/up in one pass over the Bonsai 2 pack layout (both weights qgemv_pack_supported).
+q38_status qgemv_gate_up_pack(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* wg,
+                              const void* sg, const void* bg, const uint32_t* wu, const void* su, const void* bu,
+                              int64_t N, void* h);
 q38_status qgemv_gate_up_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* wg,
                               const void* sg, const void* bg, const uint32_t* wu, const void* su, const void* bu,
                               int64_t N, int bits, void* h);

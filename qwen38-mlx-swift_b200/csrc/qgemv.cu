@@ -930,7 +930,7 @@ q38_status launch_pack(q38_ctx* ctx, const void* x, int M, int K, const uint32_t
 }
 
 // Gate and up projections of an MLP in one pass: h = bf16(silu(x.Wg^T) * (x.Wu^T)).
-template <int BITS, int MP, int TB>
+template <int BITS, int MP, int TB, bool PACK = false>
 q38_status launch_gate_up(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* wg, const void* sg,
                           const void* bg, const uint32_t* wu, const void* su, const void* bu, int N, void* h) {
     Plan p;
@@ -940,10 +940,10 @@ q38_status launch_gate_up(q38_ctx* ctx, const void* x, int M, int K, const uint3
     q38_status st = ensure_zero_region(ctx, 0, static_cast<size_t>(M) * 2 * N, &cnt, &part);
     if (st != Q38_OK) return st;
     WeightMaps mg, mu;
-    if (!cached_maps<BITS>(wg, sg, bg, K, N, &mg) || !cached_maps<BITS>(wu, su, bu, K, N, &mu))
+    if (!cached_maps<BITS, PACK>(wg, sg, bg, K, N, &mg) || !cached_maps<BITS, PACK>(wu, su, bu, K, N, &mu))
         return fail(ctx, Q38_ERR_CUDA, "quantized_gate_up: tensor map encoding failed");
-    const cudaError_t e = launch_kernels<BITS, MP, TB>(p, ctx->device, ctx->num_sms, x, M, K, mg, bg != nullptr, N, h,
-                                                       part, ctx->d_status, ctx->stream, &mu);
+    const cudaError_t e = launch_kernels<BITS, MP, TB, PACK>(p, ctx->device, ctx->num_sms, x, M, K, mg, bg != nullptr,
+                                                             N, h, part, ctx->d_status, ctx->stream, &mu);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return fail(ctx, Q38_ERR_CUDA, "quantized_gate_up: launch failed: %s", cudaGetErrorString(e));
@@ -1007,6 +1007,16 @@ q38_status qgemv_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const u
         case 8: return go(std::integral_constant<int, 8>());
     }
     return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: bits %d not on the fast path", bits);
+}
+
+q38_status qgemv_gate_up_pack(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* wg,
+                              const void* sg, const void* bg, const uint32_t* wu, const void* su, const void* bu,
+                              int64_t N, void* h) {
+    const int m = static_cast<int>(M), k = static_cast<int>(K), n = static_cast<int>(N);
+    return dispatch_m<2>(m, [&](auto mp, auto tb) {
+        return launch_gate_up<2, decltype(mp)::value, decltype(tb)::value, true>(ctx, x, m, k, wg, sg, bg, wu, su, bu,
+                                                                               n, h);
+    });
 }
 
 q38_status qgemv_gate_up_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* wg,

@@ -56,6 +56,7 @@ _sig("q38_last_error", [_P], C.c_char_p)
 _sig("q38_quantized_matmul", [_P, _P, _I, _I, _i, _P, _P, _P, _i, _I, _i, _i, _i, _i, _P])
 _sig("q38_quantized_embedding", [_P, _P, _I, _P, _P, _P, _i, _I, _I, _i, _i, _i, _P, _i])
 _sig("q38_hadamard_quantized_embedding", [_P, _P, _I, _P, _P, _P, _i, _I, _I, _i, _i, _i, _P, _i, _P])
+_sig("q38_hadamard_quantized_gate_up", [_P, _P, _I, _I, _i, _P, _i, _P, _P, _P, _P, _P, _P, _i, _I, _i, _i, _P])
 _sig("q38_quantized_gate_up", [_P, _P, _I, _I, _i, _P, _P, _P, _P, _P, _P, _i, _I, _i, _i, _i, _P])
 _sig("q38_gather_quantized_matmul",
      [_P, _P, _I, _I, _I, _i, _P, _P, _P, _i, _I, _I, _P, _P, _I, _i, _i, _i, _i, _i, _P])
@@ -285,6 +286,37 @@ def quantized_gate_up(x: torch.Tensor, gate, up, group_size: int = 64, bits: int
     _check(ctx, _lib.q38_quantized_gate_up(ctx, _ptr(x), M, K, _DTYPE[x.dtype], _ptr(wg), _ptr(sg), _ptr(bg),
                                            _ptr(wu), _ptr(su), _ptr(bu), _DTYPE[sg.dtype], N, group_size, bits,
                                            0, _ptr(h)))
+    return h
+
+
+def hadamard_quantized_gate_up(x: torch.Tensor, signs: torch.Tensor | None, block: int, gate, up,
+                               group_size: int = 64, bits: int = 2) -> torch.Tensor:
+    """silu(gate(xr)) * up(xr) with xr = hadamardRotate(x, signs, block): the gate and up
+    Qwen38HadamardQuantizedLinear projections of a Bonsai 2 MLP
+    (Bonsai2/Qwen38HadamardModules.swift:37-39) when both carry the same signs (the pack
+    stores one sign vector per input width).  gate and up are (w, scales, biases) triples."""
+    wg, sg, bg = gate
+    wu, su, bu = up
+    for t, n in ((x, "x"), (wg, "gate w"), (sg, "gate scales"), (wu, "up w"), (su, "up scales")):
+        _need(t, n)
+    for t, n in ((bg, "gate biases"), (bu, "up biases")):
+        if t is not None:
+            _need(t, n)
+    if signs is not None:
+        _need(signs, "signs")
+        if signs.dtype != torch.float32:
+            signs = signs.float().contiguous()
+    wg, wu = _as_u32(wg), _as_u32(wu)
+    if wg.shape != wu.shape or sg.shape != su.shape:
+        raise ValueError("hadamard_quantized_gate_up: gate and up weights must have one shape")
+    K = x.shape[-1]
+    N = wg.shape[0]
+    M = x.numel() // K if K else 0
+    h = torch.empty(x.shape[:-1] + (N,), dtype=x.dtype, device=x.device)
+    ctx = _bind(x)
+    _check(ctx, _lib.q38_hadamard_quantized_gate_up(ctx, _ptr(x), M, K, _DTYPE[x.dtype], _ptr(signs), block,
+                                                    _ptr(wg), _ptr(sg), _ptr(bg), _ptr(wu), _ptr(su), _ptr(bu),
+                                                    _DTYPE[sg.dtype], N, group_size, bits, _ptr(h)))
     return h
 
 

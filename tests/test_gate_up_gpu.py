@@ -113,3 +113,58 @@ def test_gate_up_rejects_mixed_biases(q38):
     du = (dev_u32(up[0]), dev_bf16(up[1]), None)
     with pytest.raises(ValueError):
         q38.quantized_gate_up(dev_bf16(O.normal_bf16(3, (1, 512))), dg, du, 64, 4)
+
+
+def pack_weight(seed, N, K):
+    """Bonsai 2 pack layout on the device: ternary 2-bit codes, f16 scales, biases = -scales,
+    groups of 128."""
+    rng = np.random.default_rng(seed)
+    codes = O.pack(rng.integers(0, 3, size=(N, K)).astype(np.uint8), 2)
+    s = (np.abs(rng.normal(0, 0.02, size=(N, K // 128))) + 1e-3).astype(np.float16)
+    return dev_u32(codes), torch.from_numpy(s).cuda(), torch.from_numpy(-s).cuda()
+
+
+def composition(q38, x, gate, up, group, bits, signs=None, block=None):
+    xr = x if block is None else q38.hadamard_rotate(x, signs, block)
+    return q38.silu_mul(q38.quantized_matmul(xr, *gate, True, group, bits),
+                        q38.quantized_matmul(xr, *up, True, group, bits))
+
+
+@pytest.mark.parametrize("M", [1, 8, 16])
+def test_gate_up_pack_layout(q38, M):
+    # one pass over two weights in the pack's layout (f16 scales, group 128)
+    N, K = 1000, 2048
+    gate, up = pack_weight(31, N, K), pack_weight(32, N, K)
+    x = dev_bf16(O.normal_bf16(33 + M, (M, K)))
+    h = q38.quantized_gate_up(x, gate, up, 128, 2)
+    comp = composition(q38, x, gate, up, 128, 2)
+    torch.cuda.synchronize()
+    q38.check_device()
+    check_h(host_bf16(h), O.bf16_to_f32(host_bf16(comp)))
+
+
+@pytest.mark.parametrize("layout", ["group64", "pack"])
+@pytest.mark.parametrize("M", [1, 8, 32])
+def test_hadamard_gate_up(q38, layout, M):
+    # one rotation shared by gate and up; M = 32 takes the two products and the SiLU product,
+    # whose up product follows the rotated x in the activation buffer
+    N, K = 768, 2048
+    if layout == "pack":
+        gate, up, group, block = pack_weight(41, N, K), pack_weight(42, N, K), 128, 1024
+    else:
+        g, u = O.ternary(43, N, K), O.ternary(44, N, K)
+        gate = (dev_u32(g[0]), dev_bf16(g[1]), dev_bf16(g[2]))
+        up = (dev_u32(u[0]), dev_bf16(u[1]), dev_bf16(u[2]))
+        group, block = 64, 256
+    signs = torch.from_numpy(np.where(np.random.default_rng(45).random(K) < 0.5, -1.0, 1.0).astype(np.float32)).cuda()
+    x = dev_bf16(O.normal_bf16(46 + M, (M, K)))
+    h = q38.hadamard_quantized_gate_up(x, signs, block, gate, up, group, 2)
+    h2 = q38.hadamard_quantized_gate_up(x, signs, block, gate, up, group, 2)
+    comp = composition(q38, x, gate, up, group, 2, signs, block)
+    torch.cuda.synchronize()
+    q38.check_device()
+    if M > 16:
+        assert torch.equal(h, comp) and torch.equal(h2, comp)
+    else:
+        check_h(host_bf16(h), O.bf16_to_f32(host_bf16(comp)))
+        check_h(host_bf16(h2), O.bf16_to_f32(host_bf16(comp)))
