@@ -1020,6 +1020,33 @@ def run_profile_bonsai(args):
                                          "mean_abs_r": float(r.float().abs().mean())}}))
 
 
+def run_profile_embedding(args):
+    """Small fixed workload for ncu captures of the embedding lookups: 4096 ids from a 248,320 x
+    5120 4-bit g64 table (bf16 rows out, 42 MB), then the same ids from a 2-bit g128 f16 table
+    rotated back at block 1024 (the Bonsai 2 embedding); 3 calls each."""
+    import torch
+    import q38
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(7070)
+    rows, K = 248320, 5120
+    c4 = torch.randint(-2 ** 31, 2 ** 31 - 1, (rows, K // 8), dtype=torch.int32, device=dev, generator=g)
+    s4 = (torch.rand((rows, K // GROUP), device=dev, generator=g) * 0.01).to(torch.bfloat16)
+    ids = torch.randint(0, rows, (4096,), device=dev, generator=g, dtype=torch.int32)
+    for _ in range(3):
+        e4 = q38.quantized_embedding(ids, c4, s4, -s4, GROUP, 4)
+    del c4, s4
+    w2, s2, b2 = _ternary_weight(torch, dev, g, rows, K, 128, torch.float16)
+    signs = torch.where(torch.rand(K, generator=g, device=dev) < 0.5, -1.0, 1.0)
+    for _ in range(3):
+        e2 = q38.hadamard_quantized_embedding(ids, w2, s2, b2, signs, 1024, 128, 2)
+    torch.cuda.synchronize()
+    q38.check_device()
+    print(json.dumps({"profile_embedding": {"ids": 4096, "K": K, "out_bytes": 4096 * K * 2,
+                                            "row_bytes_4bit": K // 2 + (K // GROUP) * 4,
+                                            "row_bytes_2bit_pack": K // 4 + (K // 128) * 4,
+                                            "mean_abs": [float(e4.float().abs().mean()), float(e2.float().abs().mean())]}}))
+
+
 def run_profile_moe(args):
     """One MoE layer (Flash-Next shapes) at T = --profile-t tokens, 2 calls, for ncu."""
     import torch
@@ -1042,6 +1069,7 @@ def main():
     ap.add_argument("--profile-prefill", action="store_true")
     ap.add_argument("--profile-moe", action="store_true")
     ap.add_argument("--profile-bonsai", action="store_true")
+    ap.add_argument("--profile-embedding", action="store_true")
     ap.add_argument("--profile-t", type=int, default=4096)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
@@ -1068,6 +1096,9 @@ def main():
         return
     if args.profile_bonsai:
         run_profile_bonsai(args)
+        return
+    if args.profile_embedding:
+        run_profile_embedding(args)
         return
     if args.impl == "reference":
         line = run_reference(args, rank, world)

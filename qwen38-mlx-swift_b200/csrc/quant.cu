@@ -69,6 +69,54 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, int64_t n, const u
     }
 }
 
+// 2-, 4- and 8-bit codes: one thread per 32-bit code word (its 32/BITS codes share a group),
+// the same arithmetic as embed_kernel, outputs written as 16- or 8-byte stores when `vec`
+// (16-byte aligned output, rows a multiple of 16 bytes).  Grid: x over the words of a row,
+// y over the ids.
+template <typename ST, typename OT, int BITS>
+__global__ void __launch_bounds__(128) embed_word_kernel(const int32_t* __restrict__ ids, int64_t n,
+                                                         const uint32_t* __restrict__ w, const ST* __restrict__ s,
+                                                         const ST* __restrict__ b, int64_t rows, int64_t K, int group,
+                                                         bool vec, OT* __restrict__ out, uint32_t* status) {
+    constexpr int CPW = 32 / BITS;
+    constexpr int BYTES = CPW * static_cast<int>(sizeof(OT));
+    const int64_t kw = K / CPW;
+    const int64_t wi = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (wi >= kw) return;
+    const int64_t k0 = wi * CPW, G = K / group, gi = k0 / group;
+    for (int64_t t = blockIdx.y; t < n; t += gridDim.y) {
+        const int64_t r = ids[t];
+        __align__(16) OT o[CPW];
+        if (r < 0 || r >= rows) {
+#pragma unroll
+            for (int c = 0; c < CPW; ++c) o[c] = from_f32<OT>(0.0f);
+            if (wi == 0) atomicOr(status, Q38_DEV_BAD_INDEX);
+        } else {
+            const uint32_t word = w[r * kw + wi];
+            const float sc = to_f32(s[r * G + gi]);
+            const float bi = b ? to_f32(b[r * G + gi]) : 0.0f;
+#pragma unroll
+            for (int c = 0; c < CPW; ++c) {
+                const float q = static_cast<float>((word >> (c * BITS)) & ((1u << BITS) - 1u));
+                o[c] = from_f32<OT>(__fadd_rn(__fmul_rn(sc, q), bi));
+            }
+        }
+        OT* dst = out + t * K + k0;
+        if (BYTES % 16 == 0 && vec) {
+#pragma unroll
+            for (int v = 0; v < BYTES / 16; ++v)
+                reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(o)[v];
+        } else if (BYTES % 8 == 0 && vec) {
+#pragma unroll
+            for (int v = 0; v < BYTES / 8; ++v)
+                reinterpret_cast<uint2*>(dst)[v] = reinterpret_cast<const uint2*>(o)[v];
+        } else {
+#pragma unroll
+            for (int c = 0; c < CPW; ++c) dst[c] = o[c];
+        }
+    }
+}
+
 // ---------------------------------------------------------------------- quantize
 // One thread per group.  MLX affine rule (MLX C++ 0.31 affine quantize, called through
 // mx.quantize at Scripts/qwen4-exp-requantize-experts.py:246-251): the extreme of larger
@@ -246,6 +294,34 @@ q38_status dequantize_launch(q38_ctx* ctx, const uint32_t* w, const void* s, con
 q38_status embedding_launch(q38_ctx* ctx, const int32_t* ids, int64_t n, const uint32_t* w, const void* s,
                             const void* b, q38_dtype sd, int64_t rows, int64_t K, int group, int bits, void* out,
                             q38_dtype od) {
+    if (bits == 2 || bits == 4 || bits == 8) {
+        const int64_t kw = K * bits / 32;
+        const int osize = od == Q38_F32 ? 4 : 2;
+        const bool vec = (reinterpret_cast<uintptr_t>(out) & 15u) == 0 && (K * osize) % 16 == 0;
+        const dim3 grid(static_cast<unsigned>((kw + 127) / 128), static_cast<unsigned>(n < 65535 ? n : 65535));
+        auto go = [&](auto st, auto ot) {
+            using ST = decltype(st);
+            using OT = decltype(ot);
+            const ST* sp = static_cast<const ST*>(s);
+            const ST* bp = static_cast<const ST*>(b);
+            OT* op = static_cast<OT*>(out);
+            if (bits == 2)
+                embed_word_kernel<ST, OT, 2><<<grid, 128, 0, ctx->stream>>>(ids, n, w, sp, bp, rows, K, group, vec, op, ctx->d_status);
+            else if (bits == 4)
+                embed_word_kernel<ST, OT, 4><<<grid, 128, 0, ctx->stream>>>(ids, n, w, sp, bp, rows, K, group, vec, op, ctx->d_status);
+            else
+                embed_word_kernel<ST, OT, 8><<<grid, 128, 0, ctx->stream>>>(ids, n, w, sp, bp, rows, K, group, vec, op, ctx->d_status);
+        };
+        auto pick_out = [&](auto st) {
+            if (od == Q38_BF16) go(st, __nv_bfloat16());
+            else if (od == Q38_F16) go(st, __half());
+            else go(st, 0.0f);
+        };
+        if (sd == Q38_BF16) pick_out(__nv_bfloat16());
+        else if (sd == Q38_F16) pick_out(__half());
+        else pick_out(0.0f);
+        return check_launch(ctx, "quantized_embedding");
+    }
     const int grid = grid_for(n * K, 256);
 #define Q38_EM(ST, OT)                                                                            \
     embed_kernel<ST, OT><<<grid, 256, 0, ctx->stream>>>(ids, n, w, static_cast<const ST*>(s),         \

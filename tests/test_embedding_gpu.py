@@ -133,3 +133,31 @@ def test_hadamard_embedding_out_of_range_and_arguments(q38):
         q38.hadamard_quantized_embedding(ids, dev_u32(c), dev_bf16(s), dev_bf16(b), None, 1024, 64, bits)
     with pytest.raises(q38.Q38Error):  # block not a power of two
         q38.hadamard_quantized_embedding(ids, dev_u32(c), dev_bf16(s), dev_bf16(b), None, 384, 64, bits)
+
+
+@pytest.mark.parametrize("bits,block,K", [(3, 512, 2048), (4, 8192, 8192), (8, 64, 1024)])
+def test_hadamard_embedding_other_widths(q38, bits, block, K):
+    # 3-bit codes (decoded one by one), the shared-memory kernel for blocks above 4096, and
+    # blocks small enough that one CTA holds several
+    rows = 40
+    c, s, b = make_weight(920 + bits, rows, K, bits)
+    signs = np.where(np.random.default_rng(block).random(K) < 0.5, -1.0, 1.0).astype(np.float32)
+    ids = np.random.default_rng(921).integers(0, rows, size=(5,)).astype(np.int32)
+    out = q38.hadamard_quantized_embedding(torch.from_numpy(ids).cuda(), dev_u32(c), dev_bf16(s), dev_bf16(b),
+                                           torch.from_numpy(signs).cuda(), block, 64, bits)
+    torch.cuda.synchronize()
+    q38.check_device()
+    ref = O.hadamard_rotate(O.f32_to_bf16(O.dequantize(c, s, b, 64, bits)[ids]), block, signs, inverse=True)
+    np.testing.assert_array_equal(host_bf16(out), ref)
+
+
+def test_embedding_many_ids(q38):
+    # more ids than one grid dimension holds (65,535): the lookup loops over the rest
+    rows, K, bits = 300, 256, 4
+    c, s, b = make_weight(930, rows, K, bits)
+    ids = np.random.default_rng(931).integers(0, rows, size=(70000,)).astype(np.int32)
+    out = q38.quantized_embedding(torch.from_numpy(ids).cuda(), dev_u32(c), dev_bf16(s), dev_bf16(b), 64, bits)
+    torch.cuda.synchronize()
+    q38.check_device()
+    table = O.f32_to_bf16(O.dequantize(c, s, b, 64, bits))
+    np.testing.assert_array_equal(host_bf16(out), table[ids])
