@@ -663,6 +663,39 @@ class QuantizedSwitchLinear:
         return out.reshape(T, k, -1)
 
 
+class QuantizedMLP:
+    """The gated MLP of the dense and Bonsai 2 models, down(silu(gate(x)) * up(x)), over
+    QuantizedLinear projections (Qwen3.5's MLP; Bonsai 2 packs make each projection a
+    HadamardQuantizedLinear, Bonsai2/Qwen38HadamardModules.swift:24-40).  Gate and up run as
+    one pass over both weights (quantized_gate_up); rotated gate and up with equal signs and
+    block share one rotation (hadamard_quantized_gate_up).  Other pairs are composed from
+    the two projections and silu_mul.  Without biases on the Linear layers (`bias`), as in
+    those models; a Linear bias falls back to the composition."""
+
+    def __init__(self, gate: QuantizedLinear, up: QuantizedLinear, down: QuantizedLinear):
+        self.gate, self.up, self.down = gate, up, down
+        g, u = gate, up
+        same = (type(g) is type(u) and g.weight.shape == u.weight.shape and g.scales.dtype == u.scales.dtype and
+                (g.group_size, g.bits, g.mode) == (u.group_size, u.bits, u.mode) and g.mode == "affine" and
+                g.bias is None and u.bias is None and (g.biases is None) == (u.biases is None))
+        if same and isinstance(g, HadamardQuantizedLinear):
+            same = g.block == u.block and ((g.signs is None and u.signs is None) or
+                                           (g.signs is not None and u.signs is not None and torch.equal(g.signs, u.signs)))
+        self._fused = same
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        g, u = self.gate, self.up
+        if self._fused and x.dtype == torch.bfloat16:
+            gw, uw = (g.weight, g.scales, g.biases), (u.weight, u.scales, u.biases)
+            if isinstance(g, HadamardQuantizedLinear):
+                h = hadamard_quantized_gate_up(x, g.signs, g.block, gw, uw, g.group_size, g.bits)
+            else:
+                h = quantized_gate_up(x, gw, uw, g.group_size, g.bits)
+        else:
+            h = silu_mul(g(x), u(x))
+        return self.down(h)
+
+
 class SwitchGLU:
     """MLXLMCommon.SwitchGLU over QuantizedSwitchLinear gate/up/down projections with the
     weighted expert sum of Qwen4ExpSparseMoE: __call__(x, indices, scores) -> [T, H]."""

@@ -168,3 +168,32 @@ def test_hadamard_gate_up(q38, layout, M):
     else:
         check_h(host_bf16(h), O.bf16_to_f32(host_bf16(comp)))
         check_h(host_bf16(h2), O.bf16_to_f32(host_bf16(comp)))
+
+
+@pytest.mark.parametrize("kind", ["plain", "rotated", "rotated_distinct_signs"])
+def test_quantized_mlp_module(q38, kind):
+    # the module's fused paths against the composition of its projections
+    D, F, M = 1024, 2048, 3
+    if kind == "plain":
+        w = [make_weight(50 + i, n, k, 4) for i, (n, k) in enumerate(((F, D), (F, D), (D, F)))]
+        lins = [q38.QuantizedLinear(dev_u32(c), dev_bf16(s), dev_bf16(b), None, 64, 4) for (c, s, b) in w]
+    else:
+        rng = np.random.default_rng(55)
+        signs = lambda n: torch.from_numpy(np.where(rng.random(n) < 0.5, -1.0, 1.0).astype(np.float32)).cuda()
+        sd = signs(D)
+        lins = []
+        for i, (n, k) in enumerate(((F, D), (F, D), (D, F))):
+            c, s, b = pack_weight(56 + i, n, k)
+            sg = sd if (k == D and not (kind == "rotated_distinct_signs" and i == 1)) else signs(k)
+            lins.append(q38.HadamardQuantizedLinear(q38.QuantizedLinear(c, s, b, None, 128, 2), sg, 1024))
+    mlp = q38.QuantizedMLP(*lins)
+    assert mlp._fused == (kind != "rotated_distinct_signs")
+    x = dev_bf16(O.normal_bf16(57, (M, D)))
+    y = mlp(x)
+    ref = lins[2](q38.silu_mul(lins[0](x), lins[1](x)))
+    torch.cuda.synchronize()
+    q38.check_device()
+    if kind == "rotated_distinct_signs":
+        assert torch.equal(y, ref)
+    else:
+        check_h(host_bf16(y), O.bf16_to_f32(host_bf16(ref)))
