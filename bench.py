@@ -314,17 +314,20 @@ def run_bonsai(torch, q38, dev, quick=False):
         w, s, b = _ternary_weight(torch, dev, g, N, K, 128, torch.float16)
         signs = torch.where(torch.rand(K, generator=g, device=dev) < 0.5, -1.0, 1.0)
         mods.append(q38.HadamardQuantizedLinear(q38.QuantizedLinear(w, s, b, None, 128, 2), signs, 1024))
-    for M in (1, 8):
+    for M in ((1, 8) if quick else (1, 8, 2048)):
         x = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+        reps = 8 if M == 2048 else 100
 
         def fn2():
-            for i in range(100):
+            for i in range(reps):
                 mods[i % copies](x)
 
-        us = _graph_us(torch, fn2, 100)
+        us = _graph_us(torch, fn2, reps)
         wbytes = N * K // 4 + N * (K // 128) * 4
-        out[f"pack layout g128 f16 {N}x{K} M={M}"] = {"us": round(us, 2),
-                                                      "GBps": round(wbytes / (us * 1e-6) / 1e9, 1)}
+        row = {"us": round(us, 2), "GBps": round(wbytes / (us * 1e-6) / 1e9, 1)}
+        if M == 2048:
+            row["TFLOPs"] = round(2 * M * N * K / (us * 1e-6) / 1e12, 1)
+        out[f"pack layout g128 f16 {N}x{K} M={M}"] = row
     # MLP gate + up over the pack layout: one rotation and one pass over both weights
     # (q38_hadamard_quantized_gate_up) against two rotated projections and the SiLU product
     sg = mods[0].signs

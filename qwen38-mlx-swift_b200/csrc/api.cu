@@ -260,7 +260,7 @@ q38_status q38_quantized_matmul(q38_ctx* ctx, const void* x, int64_t M, int64_t 
     if (qgemv_pack_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w, scales, biases))
         return qgemv_pack(ctx, x, M, K, w, scales, biases, N, y);
     if (qgemm_tc_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w, scales, biases, y))
-        return qgemm_tc_run(ctx, x, M, K, w, scales, biases, N, bits, y);
+        return qgemm_tc_run(ctx, x, M, K, w, scales, biases, N, bits, y, group_size);
     return qmm_generic(ctx, x, M, K, x_dtype, w, scales, biases, scales_dtype, N, group_size, bits, y);
 }
 

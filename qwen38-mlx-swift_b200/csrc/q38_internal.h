@@ -102,7 +102,7 @@ q38_status qgemv_gate_up_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K,
 bool qgemm_tc_supported(int64_t M, int64_t K, int group, int bits, q38_dtype xd, q38_dtype sd,
                         const void* x, const void* w, const void* s, const void* b, const void* y);
 q38_status qgemm_tc_run(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w,
-                        const void* s, const void* b, int64_t N, int bits, void* y);
+                        const void* s, const void* b, int64_t N, int bits, void* y, int group = 64);
 
 // General product, any supported shape (CUDA cores; correctness path for odd shapes).
 q38_status qmm_generic(q38_ctx* ctx, const void* x, int64_t M, int64_t K, q38_dtype xd,

@@ -78,11 +78,12 @@ __global__ void __launch_bounds__(256) qgemm_prep(const __nv_bfloat16* __restric
 }
 
 struct PArgs {
-    const uint16_t* scales;  // [N, K/64] bf16 bits
+    const uint16_t* scales;  // [N, K/64] bf16 bits, or with `pack` [N, K/128] f16 bits
     const uint16_t* biases;  // same, or null
     __nv_bfloat16* y;
     uint32_t* status;
     int M, N, K, nR, ntiles, has_bias;
+    int pack;  // f16 scales and biases in groups of 128 (direct scale loads only)
 };
 
 template <int BITS, bool SB_TMA>
@@ -253,6 +254,18 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
             const int tile = pair + (g / ksteps) * npairs;
             const int n = (tile % a.nR) * (2 * P_ROWS) + rank * P_ROWS + row;
             if (n >= a.N) return;
+            if (a.pack) {
+                // one 128-group per 128-k stage: its f16 scale and bias as bf16 for both
+                // 64-halves (the dequantized weight is rounded to bf16 in any case)
+                const size_t off = static_cast<size_t>(n) * (a.K / 128) + (g % ksteps);
+                auto cvt = [](uint16_t h) {
+                    const uint32_t v = __bfloat16_as_ushort(__float2bfloat16_rn(__half2float(__ushort_as_half(h))));
+                    return v | (v << 16);
+                };
+                sv = cvt(__ldg(a.scales + off));
+                if (a.biases) bv = cvt(__ldg(a.biases + off));
+                return;
+            }
             const size_t off = static_cast<size_t>(n) * G + 2 * (g % ksteps);
             sv = __ldg(reinterpret_cast<const unsigned int*>(a.scales + off));
             if (a.biases) bv = __ldg(reinterpret_cast<const unsigned int*>(a.biases + off));
@@ -366,7 +379,7 @@ q38_status pair_config(q38_ctx* ctx, int smem, PairLaunch* out) {
 
 template <int BITS, bool SB_TMA>
 q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, const void* s, const void* b,
-                  int N, void* y) {
+                  int N, void* y, bool pack = false) {
     using F = PF<BITS, SB_TMA>;
     q38_status st = ensure_workspace(ctx, static_cast<size_t>(M) * K * 2);
     if (st != Q38_OK) return st;
@@ -420,6 +433,7 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
     args.nR = nR;
     args.ntiles = ntiles;
     args.has_bias = b != nullptr;
+    args.pack = pack ? 1 : 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
     cfg.blockDim = dim3(P_THREADS);
@@ -436,16 +450,24 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
 
 bool qgemm_tc_supported(int64_t M, int64_t K, int group, int bits, q38_dtype xd, q38_dtype sd, const void* x,
                         const void* w, const void* s, const void* b, const void* y) {
-    if (M < 17 || M > (1 << 24) || group != 64 || K % 128 != 0 || K <= 0 || K > (1 << 20)) return false;
+    if (M < 17 || M > (1 << 24) || K % 128 != 0 || K <= 0 || K > (1 << 20)) return false;
     if (bits != 2 && bits != 3 && bits != 4) return false;
-    if (xd != Q38_BF16 || sd != Q38_BF16) return false;
+    if (xd != Q38_BF16) return false;
+    // group 64 with bf16 scales, or the Bonsai 2 pack's group 128 with f16 scales (2 and 4 bits)
+    const bool std_layout = group == 64 && sd == Q38_BF16;
+    const bool pack_layout = group == 128 && sd == Q38_F16 && bits != 3;
+    if (!std_layout && !pack_layout) return false;
     auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
     return al(x) && al(w) && al(s) && (!b || al(b)) && al(y);
 }
 
 q38_status qgemm_tc_run(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w, const void* s,
-                        const void* b, int64_t N, int bits, void* y) {
+                        const void* b, int64_t N, int bits, void* y, int group) {
     const int m = static_cast<int>(M), k = static_cast<int>(K), n = static_cast<int>(N);
+    if (group == 128) {  // the pack layout: scales loaded directly by the dequantizing warps
+        if (bits == 2) return launch<2, false>(ctx, x, m, k, w, s, b, n, y, true);
+        return launch<4, false>(ctx, x, m, k, w, s, b, n, y, true);
+    }
     const bool tma_scales = k % 512 == 0;
     switch (bits) {
         case 2: return tma_scales ? launch<2, true>(ctx, x, m, k, w, s, b, n, y) : launch<2, false>(ctx, x, m, k, w, s, b, n, y);

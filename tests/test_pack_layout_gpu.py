@@ -17,10 +17,10 @@ from test_qmm_gpu import dev_bf16, dev_u32, host_bf16
 pytestmark = pytest.mark.gpu
 
 
-def pack_case(seed, N, K, ternary=False, biased=True):
+def pack_case(seed, N, K, ternary=False, biased=True, bits=2):
     rng = np.random.default_rng(seed)
-    q = rng.integers(0, 3 if ternary else 4, size=(N, K)).astype(np.uint8)
-    codes = O.pack(q, 2)
+    q = rng.integers(0, 3 if ternary else 2 ** bits, size=(N, K)).astype(np.uint8)
+    codes = O.pack(q, bits)
     s = (np.abs(rng.normal(0, 0.02, size=(N, K // 128))) + 1e-3).astype(np.float16)
     if ternary:
         b = (-s).astype(np.float16)
@@ -47,12 +47,12 @@ def check(y_bits, ref):
     assert excess <= 2e-2 * rms, f"max excess {excess:.4g} > 2e-2 * rms {rms:.4g}"
 
 
-def run(q38, seed, M, N, K, **kw):
-    q, codes, s, b = pack_case(seed, N, K, **kw)
+def run(q38, seed, M, N, K, bits=2, **kw):
+    q, codes, s, b = pack_case(seed, N, K, bits=bits, **kw)
     x = O.normal_bf16(seed + 1, (M, K))
     ds = torch.from_numpy(s).cuda()
     db = None if b is None else torch.from_numpy(b).cuda()
-    y = q38.quantized_matmul(dev_bf16(x), dev_u32(codes), ds, db, True, 128, 2)
+    y = q38.quantized_matmul(dev_bf16(x), dev_u32(codes), ds, db, True, 128, bits)
     torch.cuda.synchronize()
     q38.check_device()
     return host_bf16(y), reference(x, q, s, b)
@@ -92,3 +92,12 @@ def test_bonsai_pack_projection_with_rotation(q38):
     q38.check_device()
     xr = O.hadamard_rotate(x, 1024, signs)
     check(host_bf16(y), reference(xr, q, s, b))
+
+
+@pytest.mark.parametrize("bits", [2, 4])
+@pytest.mark.parametrize("M", [64, 300])
+@pytest.mark.parametrize("NK", [(1000, 2048), (512, 5120)])
+def test_pack_layout_prefill(q38, bits, M, NK):
+    # prompt-sized inputs: the tensor-core prefill product with f16 scales loaded per row
+    y, ref = run(q38, 80 + M + bits, M, *NK, bits=bits)
+    check(y, ref)
