@@ -86,6 +86,13 @@ Q38_API size_t q38_ctx_workspace_bytes(const q38_ctx* ctx);
 Q38_API q38_status q38_ctx_check_device(q38_ctx* ctx);
 /* Message of the last failed call on this context ("" if none). */
 Q38_API const char* q38_last_error(const q38_ctx* ctx);
+/* Exercises the timeout path: enqueues a one-thread kernel whose bounded wait (the one
+ * every kernel here uses) waits for an mbarrier phase that nothing completes, with a
+ * limit of `limit_cycles` SM clock cycles instead of the usual one second.  The wait
+ * runs out, the kernel records the expiry in the context's status word and returns, so
+ * the next q38_ctx_check_device returns Q38_ERR_DEVICE_TIMEOUT and the context stays
+ * usable.  No counterpart in the reference (its MLX kernels have no bounded waits). */
+Q38_API q38_status q38_ctx_test_wait_timeout(q38_ctx* ctx, int64_t limit_cycles);
 
 /* ------------------------------------------------------------- operators */
 
@@ -306,20 +313,31 @@ Q38_API q38_status q38_hadamard_quantized_gate_up(q38_ctx* ctx, const void* x, i
  * that owns all device memory and hands a plugin only its input and output buffers, or
  * a latency-critical decode loop where an allocation would stall or fail).  Same
  * product as q38_quantized_matmul (transpose = true, affine, group 64, bits 2/3/4/8,
- * bf16 x/y/scales/biases, 16-byte-aligned pointers) with no context: it runs on the
- * calling thread's current device and on `stream` (a cudaStream_t, NULL = legacy
- * default stream).  Its scratch is one fixed 2 MiB array in device memory that the
- * library holds on every GPU it is loaded on until the process exits, so the limits
- * are M <= 16, N <= 32768, K <= 32768 (K % 512 == 0); larger shapes return
- * Q38_ERR_INVALID_ARGUMENT.  The first call on a device resolves the array's address
- * (no allocation), so make that first call before any stream capture.  All calls on a
- * device share the one array: calls that may overlap on the GPU (different streams
- * without ordering between them) race and produce wrong results.  Returns a status
- * only; there is no context to hold an error message. */
+ * bf16 x/y/scales/biases, 16-byte-aligned pointers; biases may be NULL) with no
+ * context: it runs on the calling thread's current device and on `stream` (a
+ * cudaStream_t, NULL = legacy default stream).  Its scratch is one fixed 2 MiB array in
+ * device memory that the library holds on every GPU it is loaded on until the process
+ * exits, so the limits are M <= 16, N <= 32768, K <= 32768 (K % 512 == 0); larger
+ * shapes return Q38_ERR_INVALID_ARGUMENT.  The first call on a device (and the first
+ * after the device's context was re-created, e.g. after cudaDeviceReset) resolves the
+ * array's address and clears it, which synchronises the device: make that first call
+ * before any stream capture.  Later calls clear nothing (each product returns its
+ * partial sums to zero).  All calls on a device share the one array: calls that may
+ * overlap on the GPU (different streams without ordering between them) race and
+ * produce wrong results.  Returns a status only; there is no context to hold an error
+ * message.  A device-side wait that runs out is not visible in the returned status
+ * (the call returns before the kernels run): q38_noalloc_check_device reports it. */
 Q38_API q38_status q38_quantized_matmul_noalloc(const void* x, int64_t M, int64_t K,
                                                 const uint32_t* w, const void* scales,
                                                 const void* biases, int64_t N, int group_size,
                                                 int bits, void* y, void* stream);
+
+/* Companion of q38_quantized_matmul_noalloc, also without allocation or context:
+ * synchronises `stream`, then reads and clears the status word in the fixed array of the
+ * current device.  Returns Q38_ERR_DEVICE_TIMEOUT if a bounded device-side wait of an
+ * allocation-free product ran out since the last check (that product's y is then not
+ * valid), else Q38_OK.  No counterpart in the reference. */
+Q38_API q38_status q38_noalloc_check_device(void* stream);
 
 /* ------------------------------------------------------------- safetensors */
 

@@ -5,6 +5,7 @@
 
 #include <mutex>
 
+#include "ptx.cuh"
 #include "q38_internal.h"
 
 namespace q38 {
@@ -105,6 +106,22 @@ EncodeTiledFn encode_tiled() {
     return fn;
 }
 
+const void* current_context_key() {
+    typedef CUresult (*GetCurrentFn)(CUcontext*);
+    static GetCurrentFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<GetCurrentFn>(p);
+    });
+    CUcontext c = nullptr;
+    if (!fn || fn(&c) != CUDA_SUCCESS) return nullptr;
+    return c;
+}
+
 bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, size_t elem_bytes, const void* base,
                  uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows,
                  CUtensorMapSwizzle swz) {
@@ -124,6 +141,16 @@ bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, size_t elem_bytes, co
 using namespace q38;
 
 namespace {
+
+// One thread waits, with the library's bounded wait and the given limit, on an mbarrier
+// phase that nothing completes: the wait runs out, records Q38_DEV_TIMEOUT in the status
+// word and returns.  This is how the timeout path is exercised without a fault.
+__global__ void wait_timeout_selftest(uint32_t* status, long long limit) {
+    __shared__ __align__(8) uint64_t bar;
+    dev::mbar_init(&bar, 1);
+    dev::fence_mbar_init();
+    dev::mbar_wait(&bar, 0, status, limit);
+}
 
 bool valid_bits(int bits) {
     return bits == 2 || bits == 3 || bits == 4 || bits == 5 || bits == 6 || bits == 8;
@@ -239,6 +266,16 @@ q38_status q38_ctx_check_device(q38_ctx* ctx) {
 }
 
 const char* q38_last_error(const q38_ctx* ctx) { return ctx ? ctx->last_error.c_str() : ""; }
+
+q38_status q38_ctx_test_wait_timeout(q38_ctx* ctx, int64_t limit_cycles) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    if (limit_cycles < 0 || limit_cycles > 4000000000LL)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "test_wait_timeout: limit must be in [0, 4e9] cycles");
+    q38_status st = set_device(ctx);
+    if (st != Q38_OK) return st;
+    wait_timeout_selftest<<<1, 1, 0, ctx->stream>>>(ctx->d_status, static_cast<long long>(limit_cycles));
+    return check_launch(ctx, "test_wait_timeout");
+}
 
 q38_status q38_quantized_matmul(q38_ctx* ctx, const void* x, int64_t M, int64_t K, q38_dtype x_dtype,
                                 const uint32_t* w, const void* scales, const void* biases,

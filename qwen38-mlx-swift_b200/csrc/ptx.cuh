@@ -58,12 +58,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // About one second at B200 clocks; a wait that exceeds it is a bug, never a slow GPU.
 constexpr long long kWaitLimitCycles = 2000000000LL;
 
-// Bounded wait on an mbarrier phase.  On expiry records Q38_DEV_TIMEOUT and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
+// Bounded wait on an mbarrier phase.  On expiry (after `limit` cycles) records
+// Q38_DEV_TIMEOUT and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status,
+                                          long long limit = kWaitLimitCycles) {
     if (mbar_try_wait(bar, parity)) return true;
     long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
-        if (clock64() - t0 > kWaitLimitCycles) {
+        if (clock64() - t0 > limit) {
             if (status) atomicOr(status, Q38_DEV_TIMEOUT);
             return false;
         }

@@ -64,6 +64,11 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn encode_tiled();
 
+// The calling thread's current CUDA context as an opaque key (nullptr if it cannot be
+// read).  Per-device caches of module state (a symbol's address, a kernel attribute) are
+// keyed on it, so that a context created anew after a reset sets them up again.
+const void* current_context_key();
+
 // 2-D tiled tensor map over a row-major [rows, cols] array.
 bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, size_t elem_bytes, const void* base,
                  uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows,

@@ -807,17 +807,20 @@ cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x
                            cudaStream_t stream, const WeightMaps* maps_b = nullptr) {
     auto kmain = qgemv_main<BITS, MP, TB, PACK>;
     // per template instance and device: smem opt-in and occupancy at the largest ring
+    // (keyed on the current context as well: a context created after a device reset
+    // needs the opt-in again)
     static std::mutex mu;
-    static bool configured[64] = {};
+    static const void* configured[64] = {};
     static int occ_smem[64][16] = {}, occ_val[64][16] = {};
     if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
     int occ = 0;
     {
         std::lock_guard<std::mutex> lk(mu);
-        if (!configured[device]) {
+        const void* key = current_context_key();
+        if (!key || configured[device] != key) {
             cudaError_t e = cudaFuncSetAttribute(kmain, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_DYN_SMEM);
             if (e != cudaSuccess) return e;
-            configured[device] = true;
+            configured[device] = key;
         }
         int slot = -1;
         for (int i = 0; i < 16; ++i) {
@@ -1056,26 +1059,42 @@ constexpr size_t NA_STATUS_OFF = 0;
 constexpr size_t NA_ACC_OFF = 256;
 constexpr size_t NA_TOTAL = NA_ACC_OFF + NA_ACC_BYTES;
 
-// The scratch of every no-alloc call on a device (status word, fp32 partial sums).  In host code this name is only a stand-in for
-// the device array; its device address comes from cudaGetSymbolAddress below.
+// The scratch of every no-alloc call on a device (status word, fp32 partial sums).  In
+// host code this name is only a stand-in for the device array; its device address comes
+// from cudaGetSymbolAddress below.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[NA_TOTAL];
 
 std::mutex g_noalloc_mu;
-uint8_t* g_noalloc_ptr[64] = {};
+struct NoallocDevice {
+    const void* ctx_key;  // the context the address below belongs to
+    uint8_t* ptr;
+};
+NoallocDevice g_noalloc[64] = {};
 
-// Once per device, with that device current: resolve the array's device address.
+// Set-up, once per device and context, with that device current: resolve the array's
+// device address and clear it (status word and partial sums start at zero; every
+// product's epilogue returns the sums to zero, so no call clears them again).  The clear
+// synchronises the device, which is why the first call must come before any capture.
 q38_status noalloc_scratch(int device, uint8_t** out) {
     if (device < 0 || device >= 64) return Q38_ERR_INVALID_ARGUMENT;
+    const void* key = current_context_key();
+    if (!key) return Q38_ERR_CUDA;
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (!g_noalloc_ptr[device]) {
+    NoallocDevice& d = g_noalloc[device];
+    if (d.ctx_key != key || !d.ptr) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
             cudaGetLastError();
             return Q38_ERR_CUDA;
         }
-        g_noalloc_ptr[device] = static_cast<uint8_t*>(p);
+        if (cudaMemset(p, 0, NA_TOTAL) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+            cudaGetLastError();
+            return Q38_ERR_CUDA;
+        }
+        d.ptr = static_cast<uint8_t*>(p);
+        d.ctx_key = key;
     }
-    *out = g_noalloc_ptr[device];
+    *out = d.ptr;
     return Q38_OK;
 }
 
@@ -1087,17 +1106,14 @@ q38_status launch_noalloc(uint8_t* scratch, int device, int num_sms, const void*
     if (!make_plan<BITS>(M, K, N, p)) return Q38_ERR_UNSUPPORTED;
     uint32_t* status = reinterpret_cast<uint32_t*>(scratch + NA_STATUS_OFF);
     float* part = reinterpret_cast<float*>(scratch + NA_ACC_OFF);
-    // the partial sums must start at zero; a previous call leaves them zero, but clear
-    // them anyway so an interrupted call cannot poison the next one
-    if (cudaMemsetAsync(part, 0, static_cast<size_t>(M) * N * 4, stream) != cudaSuccess) {
-        cudaGetLastError();
-        return Q38_ERR_CUDA;
-    }
     WeightMaps maps;
     if (!cached_maps<BITS>(w, s, b, K, N, &maps)) return Q38_ERR_CUDA;
     const cudaError_t e = launch_kernels<BITS, MP, TB>(p, device, num_sms, x, M, K, maps, b != nullptr, N,
                                                        y, part, status, stream);
     if (e != cudaSuccess) {
+        cudaGetLastError();
+        // the main kernel may have run without its epilogue: put the sums back to zero
+        cudaMemsetAsync(part, 0, static_cast<size_t>(M) * N * 4, stream);
         cudaGetLastError();
         return Q38_ERR_CUDA;
     }
@@ -1142,4 +1158,27 @@ extern "C" Q38_API q38_status q38_quantized_matmul_noalloc(const void* x, int64_
         case 4: return go(std::integral_constant<int, 4>());
         default: return go(std::integral_constant<int, 8>());
     }
+}
+
+extern "C" Q38_API q38_status q38_noalloc_check_device(void* stream) {
+    using namespace q38;
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) {
+        cudaGetLastError();
+        return Q38_ERR_CUDA;
+    }
+    uint8_t* scratch = nullptr;
+    q38_status st = noalloc_scratch(device, &scratch);
+    if (st != Q38_OK) return st;
+    uint32_t v = 0;
+    if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess ||
+        cudaMemcpy(&v, scratch + NA_STATUS_OFF, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        cudaGetLastError();
+        return Q38_ERR_CUDA;
+    }
+    if (v == 0) return Q38_OK;
+    if (cudaMemsetAsync(scratch + NA_STATUS_OFF, 0, sizeof(v), static_cast<cudaStream_t>(stream)) != cudaSuccess ||
+        cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        cudaGetLastError();
+    return (v & Q38_DEV_TIMEOUT) ? Q38_ERR_DEVICE_TIMEOUT : Q38_ERR_INVALID_ARGUMENT;
 }

@@ -53,6 +53,7 @@ _sig("q38_ctx_reserve", [_P, _S])
 _sig("q38_ctx_workspace_bytes", [_P], _S)
 _sig("q38_ctx_check_device", [_P])
 _sig("q38_last_error", [_P], C.c_char_p)
+_sig("q38_ctx_test_wait_timeout", [_P, _I])
 _sig("q38_quantized_matmul", [_P, _P, _I, _I, _i, _P, _P, _P, _i, _I, _i, _i, _i, _i, _P])
 _sig("q38_quantized_embedding", [_P, _P, _I, _P, _P, _P, _i, _I, _I, _i, _i, _i, _P, _i])
 _sig("q38_hadamard_quantized_embedding", [_P, _P, _I, _P, _P, _P, _i, _I, _I, _i, _i, _i, _P, _i, _P])
@@ -161,6 +162,20 @@ def check_device(device=None) -> None:
             if ent[0] == ctx:
                 ent[1] = None
     _check(ctx, _lib.q38_ctx_check_device(ctx))
+
+
+def test_wait_timeout(limit_cycles: int, device=None) -> None:
+    """Enqueue the bounded-wait self-test: a kernel waits for an mbarrier phase that never
+    completes, with a limit of `limit_cycles` SM cycles, and records the expiry.  The next
+    check_device() raises Q38Error with status 5 (device wait timed out)."""
+    ctx = context(device)
+    _lib.q38_ctx_set_stream(ctx, torch.cuda.current_stream(device).cuda_stream)
+    slots = getattr(_tls, "slots", None)
+    if slots:
+        for ent in slots.values():
+            if ent[0] == ctx:
+                ent[1] = None
+    _check(ctx, _lib.q38_ctx_test_wait_timeout(ctx, int(limit_cycles)))
 
 
 def reserve(nbytes: int, device=None) -> None:

@@ -226,3 +226,62 @@ def test_argument_errors(q38):
         q38.quantized_matmul(x, w, s, s, True, 64, 4)  # K not a multiple of the group
     with pytest.raises(q38.Q38Error):
         q38.quantized_matmul(x, w, s, s, False, 50, 4)
+
+
+@pytest.mark.parametrize("NK", [(17408, 5120), (5120, 17408)])
+def test_bonsai_ternary_projection_full_size(q38, NK):
+    """The Bonsai ternary benchmark configuration at its full shapes: codes uniform in
+    {0, 1, 2} (w in {-s, 0, +s}), bias = -scale, x rotated by the block-256 Walsh-Hadamard
+    transform; M = 1 and 8 in full, M = 2048 on 6 sampled tokens (a token's output
+    depends only on its own row of x)."""
+    N, K = NK
+    c, s, b = O.ternary(1400 + N, N, K)
+    lin = q38.HadamardQuantizedLinear(q38.QuantizedLinear(dev_u32(c), dev_bf16(s), dev_bf16(b), None, 64, 2),
+                                      None, 256)
+    for M in (1, 8):
+        x = O.normal_bf16(1401 + M, (M, K))
+        ref = O.qmm(O.hadamard_rotate(x, 256, None), c, s, b, 64, 2, f32=True)
+        y = lin(dev_bf16(x))
+        torch.cuda.synchronize()
+        check_close(host_bf16(y), ref)
+    M = 2048
+    x = O.normal_bf16(1410, (M, K))
+    y = lin(dev_bf16(x))
+    torch.cuda.synchronize()
+    q38.check_device()
+    rows = np.array([0, 127, 128, 1000, 2046, 2047])
+    ref = O.qmm(O.hadamard_rotate(np.ascontiguousarray(x[rows]), 256, None), c, s, b, 64, 2, f32=True)
+    check_close(host_bf16(y[torch.from_numpy(rows).cuda()]), ref)
+
+
+@pytest.mark.parametrize("M,N,K", [(17, 256, 1024), (64, 1000, 2048), (300, 512, 5120)])
+def test_qmm_8bit_prompt_sizes(q38, M, N, K):
+    """8-bit codes with more than 16 tokens (the prompt-sized product)."""
+    c, s, b = make_weight(1500 + M, N, K, 8)
+    x = O.normal_bf16(1501 + M, (M, K))
+    ref = O.qmm(x, c, s, b, 64, 8, f32=True)
+    y = q38.quantized_matmul(dev_bf16(x), dev_u32(c), dev_bf16(s), dev_bf16(b), True, 64, 8)
+    torch.cuda.synchronize()
+    check_close(host_bf16(y), ref)
+    q38.check_device()
+
+
+@pytest.mark.parametrize("M", [1, 8, 64])
+@pytest.mark.parametrize("group,bits,xdt", [(32, 4, torch.bfloat16), (32, 3, torch.bfloat16),
+                                            (64, 4, torch.float16), (128, 4, torch.bfloat16)])
+def test_qmm_other_groups_and_dtypes(q38, M, group, bits, xdt):
+    """Group 32 (the outer quantization of the published Flash-Next checkpoint), group 128,
+    and f16 activations/scales, at decode and prompt token counts."""
+    N, K = 1536, 2048
+    c, s, b = make_weight(1600 + group + bits, N, K, bits, group)
+    x = O.normal_bf16(1601 + M, (M, K))
+    if xdt == torch.float16:
+        # the oracle sees the same f16-representable values the device gets
+        x = O.f32_to_bf16(torch.from_numpy(O.bf16_to_f32(x)).half().float().numpy())
+        s = O.f32_to_bf16(torch.from_numpy(O.bf16_to_f32(s)).half().float().numpy())
+        b = O.f32_to_bf16(torch.from_numpy(O.bf16_to_f32(b)).half().float().numpy())
+    ref = O.qmm(x, c, s, b, group, bits, f32=True)
+    y = q38.quantized_matmul(dev_bf16(x).to(xdt), dev_u32(c), dev_bf16(s).to(xdt), dev_bf16(b).to(xdt), True,
+                             group, bits)
+    torch.cuda.synchronize()
+    check_close(host_bf16(y.to(torch.bfloat16)), ref)

@@ -1,9 +1,11 @@
 """GPU test of q38_quantized_matmul_noalloc, the entry point for callers that cannot
-allocate device memory (a host that owns all device memory and passes only input and
-output buffers, or a decode loop that must not stall on an allocation).
+allocate device memory where they run a projection (a host that owns all device memory
+and passes only input and output buffers, or a decode loop that must not stall on an
+allocation).
 
-It is compared with the ordinary q38_quantized_matmul on the same inputs, twice in a
-row (the second call reuses the fixed scratch array left by the first).  This file is
+Each case calls it twice in a row (the second call reuses the fixed scratch array that
+the first left behind) and checks both results against the CPU oracle and against the
+ordinary q38_quantized_matmul, within the product bar of the other tests.  This file is
 collected last so that a run stopping at the first failure has run every other test.
 """
 import ctypes as C
@@ -28,6 +30,8 @@ def _lib():
     f.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64,
                   C.c_int, C.c_int, C.c_void_p, C.c_void_p]
     f.restype = C.c_int
+    lib.q38_noalloc_check_device.argtypes = [C.c_void_p]
+    lib.q38_noalloc_check_device.restype = C.c_int
     return lib
 
 
@@ -35,31 +39,46 @@ def _dev(a, view):
     return torch.from_numpy(np.ascontiguousarray(a).view(view)).cuda()
 
 
-@pytest.mark.parametrize("bits,M,N,K", [(4, 1, 4096, 4096), (3, 8, 1000, 2048), (2, 16, 2048, 5120),
-                                        (8, 5, 640, 1536)])
-def test_noalloc_matches_allocating_entry_point(bits, M, N, K):
+def _check(y, ref):
+    yf = y.float()
+    assert torch.isfinite(yf).all()
+    rms = ref.pow(2).mean().sqrt().item()
+    err = (yf - ref).abs().max().item()
+    assert err <= TOL * rms, f"max err {err} > {TOL} * rms {rms}"
+
+
+# (16, 32768, 512) fills the whole 2 MiB partial-sum region
+@pytest.mark.parametrize("bits,M,N,K,biased,default_stream",
+                         [(4, 1, 4096, 4096, True, False), (3, 8, 1000, 2048, True, False),
+                          (2, 16, 2048, 5120, True, False), (8, 5, 640, 1536, True, False),
+                          (4, 16, 32768, 512, True, False), (3, 4, 768, 1024, False, True)])
+def test_noalloc_matches_oracle_and_allocating_entry_point(bits, M, N, K, biased, default_stream):
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     import q38
 
     lib = _lib()
-    c, s, b = O.quantize(O.normal_f32(9000 + bits, (N, K), 0.02), 64, bits)
+    c, s, b = O.quantize(O.normal_f32(9000 + bits + N, (N, K), 0.02), 64, bits)
+    if not biased:
+        b = None
     x = O.normal_bf16(9100 + M, (M, K))
+    ref_cpu = torch.from_numpy(O.qmm(x, c, s, b, 64, bits, f32=True).astype(np.float32)).cuda()
     tx = _dev(x, np.int16).view(torch.bfloat16)
-    tc, ts, tb = _dev(c, np.int32), _dev(s, np.int16).view(torch.bfloat16), _dev(b, np.int16).view(torch.bfloat16)
-    ref = q38.quantized_matmul(tx, tc, ts, tb, True, 64, bits).float()
-    stream = torch.cuda.current_stream().cuda_stream
+    tc, ts = _dev(c, np.int32), _dev(s, np.int16).view(torch.bfloat16)
+    tb = None if b is None else _dev(b, np.int16).view(torch.bfloat16)
+    ref_dev = q38.quantized_matmul(tx, tc, ts, tb, True, 64, bits).float()
+    torch.cuda.synchronize()
+    stream = None if default_stream else torch.cuda.current_stream().cuda_stream
     for _ in range(2):
         y = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
-        st = lib.q38_quantized_matmul_noalloc(tx.data_ptr(), M, K, tc.data_ptr(), ts.data_ptr(), tb.data_ptr(),
-                                              N, 64, bits, y.data_ptr(), stream)
+        st = lib.q38_quantized_matmul_noalloc(tx.data_ptr(), M, K, tc.data_ptr(), ts.data_ptr(),
+                                              None if tb is None else tb.data_ptr(), N, 64, bits, y.data_ptr(),
+                                              stream)
         assert st == 0
+        assert lib.q38_noalloc_check_device(stream) == 0
         torch.cuda.synchronize()
-        yf = y.float()
-        assert torch.isfinite(yf).all()
-        rms = ref.pow(2).mean().sqrt().item()
-        err = (yf - ref).abs().max().item()
-        assert err <= TOL * rms, f"max err {err} > {TOL} * rms {rms}"
+        _check(y, ref_cpu)
+        _check(y, ref_dev)
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch():
@@ -72,3 +91,4 @@ def test_noalloc_rejects_shapes_beyond_its_scratch():
     assert lib.q38_quantized_matmul_noalloc(p, 1, 512, p, p, p, 40000, 64, 4, p, None) == 1  # N > 32768
     assert lib.q38_quantized_matmul_noalloc(p, 1, 40960, p, p, p, 64, 64, 4, p, None) == 1  # K > 32768
     assert lib.q38_quantized_matmul_noalloc(p, 1, 500, p, p, p, 64, 64, 4, p, None) == 1    # K % 512
+    assert lib.q38_noalloc_check_device(None) == 0
