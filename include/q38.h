@@ -339,6 +339,71 @@ Q38_API q38_status q38_quantized_matmul_noalloc(const void* x, int64_t M, int64_
  * valid), else Q38_OK.  No counterpart in the reference. */
 Q38_API q38_status q38_noalloc_check_device(void* stream);
 
+/* ------------------------------------------------------------- multi-GPU
+ * One communicator rank per GPU over NCCL (NVLink / NVSwitch), loaded at run time
+ * (libnccl.so.2; Q38_NCCL_LIBRARY names another copy).  These replace the single-device
+ * calls of the reference's model code (FlashNext/Qwen4ExpSparseMoE.swift:275-294 for the
+ * experts, FlashNext/Qwen4ExpPrequantized.swift:156-159 for the dense MLP's projections)
+ * when the weights are sharded over several GPUs; the reference itself runs on one
+ * device.  Every collective is enqueued on the context's stream (or on the communicator's
+ * own stream, joined back to it) and never synchronises the host. */
+typedef struct q38_comm q38_comm;
+typedef struct q38_comm_id {
+    unsigned char bytes[128];
+} q38_comm_id;
+
+/* Message of the last failed communicator call on this thread. */
+Q38_API const char* q38_comm_error(void);
+/* A fresh rendezvous id; rank 0 creates it and hands it to the other ranks (any host
+ * channel).  Needs no GPU. */
+Q38_API q38_status q38_comm_get_unique_id(q38_comm_id* id);
+/* Joins rank `rank` of `world` on `device`.  Non-blocking under the hood: if the other
+ * ranks have not all joined within `timeout_ms`, the communicator is aborted and
+ * Q38_ERR_COMM is returned (q38_comm_error says why); later collectives on a
+ * communicator also give up with Q38_ERR_COMM after `timeout_ms` without progress. */
+Q38_API q38_status q38_comm_init_rank(const q38_comm_id* id, int world, int rank, int device, int timeout_ms,
+                                      q38_comm** out);
+/* All ranks of one process, one per device in `devices` (a host that drives every GPU
+ * from one thread). */
+Q38_API q38_status q38_comm_init_all(int ndev, const int* devices, int timeout_ms, q38_comm** comms);
+Q38_API q38_status q38_comm_destroy(q38_comm* comm);
+/* Aborts the communicator's collectives (after a peer failed); destroy it afterwards. */
+Q38_API q38_status q38_comm_abort(q38_comm* comm);
+Q38_API int q38_comm_rank(const q38_comm* comm);
+Q38_API int q38_comm_size(const q38_comm* comm);
+/* Sum of `count` elements over all ranks (recv may equal send), on the context's stream. */
+Q38_API q38_status q38_comm_all_reduce(q38_ctx* ctx, q38_comm* comm, const void* send, void* recv, int64_t count,
+                                       q38_dtype dtype);
+
+/* Tensor-parallel gated MLP, y[M, D] = down(silu(gate(x)) * up(x)) summed over the ranks:
+ * each rank holds gate and up split by output rows (F_local rows of [F, D*bits/32]) and
+ * down split by its reduction dimension ([D, F_local*bits/32], whole groups and words),
+ * computes its partial y and all-reduces it (bf16 sum).  The tokens are processed in
+ * `chunks` pieces (whole 128-token tiles): the all-reduce of one piece runs on the
+ * communicator's stream while the next piece computes.  x, y bf16 [M, D] on every rank. */
+Q38_API q38_status q38_tp_mlp(q38_ctx* ctx, q38_comm* comm, const void* x, int64_t M, int64_t D,
+                              const uint32_t* gate_w, const void* gate_s, const void* gate_b,
+                              const uint32_t* up_w, const void* up_s, const void* up_b,
+                              const uint32_t* down_w, const void* down_s, const void* down_b, int64_t F_local,
+                              q38_dtype dtype, int group_size, int bits, int chunks, void* y);
+
+/* Expert-parallel SwitchGLU + weightedExpertSum (q38_switch_glu's arithmetic) with the E
+ * experts split contiguously over the ranks (this rank holds experts [rank*E/world,
+ * (rank+1)*E/world): gate/up [E/world, I, H*bits/32], down [E/world, H, I*bits/32]).  x
+ * [T, H], indices/scores [T, top_k] (global expert ids, from this rank's router) and out
+ * [T, H] are this rank's tokens.  Fixed capacity: every rank sends `capacity` rows
+ * (T <= capacity, the same capacity on every rank) to every rank, so the exchange sizes
+ * are known in advance and nothing is read back to the host (the call can be captured in
+ * a CUDA graph); a token's row carries the rank-local expert of each slot, or -1 where the
+ * expert lives on another rank.  out_t = bf16(sum, in rank order, of the partial sums of
+ * the ranks that own one of the token's experts). */
+Q38_API q38_status q38_ep_switch_glu(q38_ctx* ctx, q38_comm* comm, const void* x, int64_t T, int64_t H, int64_t I,
+                                     int64_t E, int top_k, const int32_t* indices, const void* scores,
+                                     const uint32_t* gate_w, const void* gate_s, const void* gate_b,
+                                     const uint32_t* up_w, const void* up_s, const void* up_b,
+                                     const uint32_t* down_w, const void* down_s, const void* down_b,
+                                     q38_dtype dtype, int group_size, int bits, int64_t capacity, void* out);
+
 /* ------------------------------------------------------------- safetensors */
 
 /* Checkpoint reader.  MLX checkpoints are safetensors files whose packed tensors

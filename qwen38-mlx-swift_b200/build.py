@@ -56,7 +56,7 @@ def build(jobs: int = 0, force: bool = False, verbose_ptxas: bool = False) -> st
     with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
         objs = list(ex.map(lambda s: _compile(s, force, extra), srcs))
     if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
-        cmd = [nvcc(), *ARCH, "-shared", "-o", LIB, *objs, "-lcudart", "-lpthread"]
+        cmd = [nvcc(), *ARCH, "-shared", "-o", LIB, *objs, "-lcudart", "-lpthread", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

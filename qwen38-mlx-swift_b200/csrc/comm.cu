@@ -1,0 +1,553 @@
+// Multi-GPU layouts of the quantized products behind the C ABI, over NCCL (NVLink /
+// NVSwitch on B200), one communicator rank per GPU:
+//
+//   q38_tp_mlp         the dense 27B MLP block split tensor-parallel: gate/up by output rows,
+//                      down by its reduction dimension, partial outputs summed by an
+//                      all-reduce; the tokens are cut into chunks so that the all-reduce of
+//                      chunk i (on the communicator's stream) runs while chunk i+1 computes.
+//   q38_ep_switch_glu  the routed experts of the Flash-Next MoE layer
+//                      (Sources/Qwen38Core/FlashNext/Qwen4ExpSparseMoE.swift:275-294) split
+//                      expert-parallel: every rank sends each of its tokens once to every
+//                      rank (fixed capacity, so all exchange sizes are known in advance and
+//                      nothing is read back to the host), with the rank-local expert of each
+//                      slot or -1; the receiving rank runs SwitchGLU over its own experts
+//                      (q38_switch_glu), the partial sums come back and the home rank adds the
+//                      partials of the ranks that own one of the token's experts, in rank
+//                      order.
+//
+// NCCL is loaded at run time (dlopen of libnccl.so.2; the copy already in the process is
+// reused), so the library has no link-time dependency on it.  Communicators are created
+// non-blocking with a host deadline: a rank that never joins makes init return
+// Q38_ERR_COMM after the timeout (the communicator is aborted) instead of hanging.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <chrono>
+#include <mutex>
+#include <thread>
+#include <vector>
+
+#include "affine_codes.cuh"
+#include "q38_internal.h"
+
+namespace q38 {
+namespace {
+
+using namespace dev;
+
+// ------------------------------------------------------------------ NCCL at run time
+struct Nccl {
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*);
+    ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*);
+    ncclResult_t (*CommInitAll)(ncclComm_t*, int, const int*);
+    ncclResult_t (*CommDestroy)(ncclComm_t);
+    ncclResult_t (*CommAbort)(ncclComm_t);
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*);
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+    ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+    ncclResult_t (*GroupStart)();
+    ncclResult_t (*GroupEnd)();
+    const char* (*GetErrorString)(ncclResult_t);
+    bool ok = false;
+    std::string why;
+};
+
+const Nccl& nccl() {
+    static Nccl n;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        const char* env = getenv("Q38_NCCL_LIBRARY");
+        void* h = nullptr;
+        if (env && *env) h = dlopen(env, RTLD_NOW | RTLD_LOCAL);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);  // the copy already loaded
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_LOCAL);
+        if (!h) {
+            n.why = std::string("libnccl.so.2 could not be loaded: ") + (dlerror() ? dlerror() : "not found");
+            return;
+        }
+        bool all = true;
+        auto sym = [&](auto& fp, const char* name) {
+            fp = reinterpret_cast<std::remove_reference_t<decltype(fp)>>(dlsym(h, name));
+            if (!fp) all = false;
+        };
+        sym(n.GetUniqueId, "ncclGetUniqueId");
+        sym(n.CommInitRankConfig, "ncclCommInitRankConfig");
+        sym(n.CommInitAll, "ncclCommInitAll");
+        sym(n.CommDestroy, "ncclCommDestroy");
+        sym(n.CommAbort, "ncclCommAbort");
+        sym(n.CommGetAsyncError, "ncclCommGetAsyncError");
+        sym(n.AllReduce, "ncclAllReduce");
+        sym(n.Send, "ncclSend");
+        sym(n.Recv, "ncclRecv");
+        sym(n.GroupStart, "ncclGroupStart");
+        sym(n.GroupEnd, "ncclGroupEnd");
+        sym(n.GetErrorString, "ncclGetErrorString");
+        n.ok = all;
+        if (!all) n.why = "libnccl.so.2 lacks an entry point this library needs";
+    });
+    return n;
+}
+
+thread_local std::string t_comm_error;
+
+q38_status comm_fail(const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    t_comm_error = buf;
+    return Q38_ERR_COMM;
+}
+
+}  // namespace
+}  // namespace q38
+
+struct q38_comm {
+    ncclComm_t nc = nullptr;
+    int rank = 0, world = 1, device = 0;
+    int timeout_ms = 0;
+    bool aborted = false;
+    cudaStream_t stream = nullptr;  // the collectives' stream (overlap with the context's)
+    std::vector<cudaEvent_t> events;
+    cudaEvent_t joined = nullptr;
+    // exchange buffers, grown on demand
+    void* buf = nullptr;
+    size_t buf_bytes = 0;
+};
+
+namespace q38 {
+namespace {
+
+// Waits (bounded) until the communicator's last operation has been accepted.
+q38_status settle(q38_comm* c, const char* what) {
+    const Nccl& n = nccl();
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(c->timeout_ms);
+    for (;;) {
+        ncclResult_t st = ncclSuccess;
+        if (n.CommGetAsyncError(c->nc, &st) != ncclSuccess) st = ncclSystemError;
+        if (st == ncclSuccess) return Q38_OK;
+        if (st != ncclInProgress) {
+            return comm_fail("%s: %s", what, n.GetErrorString(st));
+        }
+        if (std::chrono::steady_clock::now() > deadline) {
+            n.CommAbort(c->nc);
+            c->aborted = true;
+            return comm_fail("%s: no progress within %d ms (communicator aborted)", what, c->timeout_ms);
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+q38_status nccl_call(q38_ctx* ctx, q38_comm* c, ncclResult_t r, const char* what) {
+    if (r != ncclSuccess && r != ncclInProgress)
+        return fail(ctx, Q38_ERR_COMM, "%s: %s", what, nccl().GetErrorString(r));
+    if (settle(c, what) != Q38_OK) return fail(ctx, Q38_ERR_COMM, "%s", t_comm_error.c_str());
+    return Q38_OK;
+}
+
+q38_status comm_buffer(q38_ctx* ctx, q38_comm* c, size_t bytes, uint8_t** out) {
+    if (bytes > c->buf_bytes) {
+        const size_t want = align_up(bytes + bytes / 4, 1 << 20);
+        if (c->buf) {
+            cudaDeviceSynchronize();
+            cudaFree(c->buf);
+            c->buf = nullptr;
+            c->buf_bytes = 0;
+        }
+        if (cudaMalloc(&c->buf, want) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(ctx, Q38_ERR_OUT_OF_MEMORY, "communicator buffer of %zu bytes could not be allocated", want);
+        }
+        c->buf_bytes = want;
+    }
+    *out = static_cast<uint8_t*>(c->buf);
+    return Q38_OK;
+}
+
+q38_status check_pair(q38_ctx* ctx, q38_comm* c, const char* op) {
+    if (!ctx || !c) return Q38_ERR_INVALID_ARGUMENT;
+    if (c->aborted) return fail(ctx, Q38_ERR_COMM, "%s: the communicator was aborted", op);
+    if (ctx->device != c->device)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "%s: context device %d, communicator device %d", op, ctx->device,
+                    c->device);
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return check_launch(ctx, op);
+    return Q38_OK;
+}
+
+cudaEvent_t comm_event(q38_comm* c, size_t i) {
+    while (c->events.size() <= i) {
+        cudaEvent_t e = nullptr;
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+        c->events.push_back(e);
+    }
+    return c->events[i];
+}
+
+// ------------------------------------------------------------------ EP kernels
+// Slot metadata of the fixed-capacity exchange: for destination rank r and row t < C,
+// the rank-local expert of each slot of token t (or -1: its expert lives elsewhere, or t is
+// past this rank's tokens) and the slot's router score.
+__global__ void __launch_bounds__(256) ep_fixed_meta(const int32_t* __restrict__ idx,
+                                                     const __nv_bfloat16* __restrict__ scores, int T, int C, int k,
+                                                     int E, int epr, int W, int32_t* __restrict__ ids,
+                                                     __nv_bfloat16* __restrict__ sc) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const int total = W * C * k;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const int r = i / (C * k), rem = i - r * C * k, t = rem / k, s = rem - t * k;
+        int le = -1;
+        __nv_bfloat16 v = __float2bfloat16_rn(0.0f);
+        if (t < T) {
+            const int e = idx[t * k + s];
+            if (e >= 0 && e < E && e / epr == r) le = e - r * epr;
+            v = scores[t * k + s];
+        }
+        ids[i] = le;
+        sc[i] = v;
+    }
+}
+
+// out[t] = bf16(sum over ranks r in order, of back[r * C + t] for the ranks that own one of
+// token t's experts), fp32 accumulation (the expert-parallel weightedExpertSum).
+__global__ void __launch_bounds__(256) ep_fixed_reduce(const __nv_bfloat16* __restrict__ back,
+                                                       const int32_t* __restrict__ idx, int T, int C, int k, int E,
+                                                       int epr, int W, int H, __nv_bfloat16* __restrict__ out) {
+    griddep_wait();
+    griddep_launch_dependents();
+    __shared__ uint32_t s_mask;
+    const int t = blockIdx.y;
+    if (threadIdx.x == 0) {
+        uint32_t m = 0;
+        for (int s = 0; s < k; ++s) {
+            const int e = idx[t * k + s];
+            if (e >= 0 && e < E) m |= 1u << (e / epr);
+        }
+        s_mask = m;
+    }
+    __syncthreads();
+    const uint32_t mask = s_mask;
+    for (int h = (blockIdx.x * blockDim.x + threadIdx.x) * 8; h < H; h += gridDim.x * blockDim.x * 8) {
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int r = 0; r < W; ++r) {
+            if (!((mask >> r) & 1u)) continue;
+            const uint4 u = *reinterpret_cast<const uint4*>(back + (static_cast<size_t>(r) * C + t) * H + h);
+            const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                acc[2 * j] += bf16_bits_to_f32(q[j] & 0xFFFFu);
+                acc[2 * j + 1] += bf16_bits_to_f32(q[j] >> 16);
+            }
+        }
+        uint4 o;
+        o.x = pack_bf16x2(acc[0], acc[1]);
+        o.y = pack_bf16x2(acc[2], acc[3]);
+        o.z = pack_bf16x2(acc[4], acc[5]);
+        o.w = pack_bf16x2(acc[6], acc[7]);
+        *reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H + h) = o;
+    }
+}
+
+cudaLaunchConfig_t pdl_cfg(dim3 grid, dim3 block, cudaStream_t stream, cudaLaunchAttribute* attr) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cfg;
+}
+
+}  // namespace
+}  // namespace q38
+
+using namespace q38;
+
+extern "C" {
+
+const char* q38_comm_error(void) { return t_comm_error.c_str(); }
+
+q38_status q38_comm_get_unique_id(q38_comm_id* id) {
+    if (!id) return Q38_ERR_INVALID_ARGUMENT;
+    const Nccl& n = nccl();
+    if (!n.ok) return comm_fail("%s", n.why.c_str());
+    static_assert(sizeof(ncclUniqueId) <= sizeof(id->bytes), "NCCL unique id fits");
+    ncclUniqueId u;
+    const ncclResult_t r = n.GetUniqueId(&u);
+    if (r != ncclSuccess) return comm_fail("ncclGetUniqueId: %s", n.GetErrorString(r));
+    memset(id->bytes, 0, sizeof(id->bytes));
+    memcpy(id->bytes, &u, sizeof(u));
+    return Q38_OK;
+}
+
+q38_status q38_comm_init_rank(const q38_comm_id* id, int world, int rank, int device, int timeout_ms,
+                              q38_comm** out) {
+    if (!id || !out || world < 1 || world > 32 || rank < 0 || rank >= world || timeout_ms < 1)
+        return Q38_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    const Nccl& n = nccl();
+    if (!n.ok) return comm_fail("%s", n.why.c_str());
+    if (cudaSetDevice(device) != cudaSuccess) {
+        cudaGetLastError();
+        return comm_fail("cudaSetDevice(%d) failed", device);
+    }
+    q38_comm* c = new q38_comm();
+    c->rank = rank;
+    c->world = world;
+    c->device = device;
+    c->timeout_ms = timeout_ms;
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->joined, cudaEventDisableTiming) != cudaSuccess) {
+        cudaGetLastError();
+        delete c;
+        return comm_fail("stream or event creation failed");
+    }
+    ncclUniqueId u;
+    memcpy(&u, id->bytes, sizeof(u));
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;  // returns at once; progress is polled against the deadline
+    const ncclResult_t r = n.CommInitRankConfig(&c->nc, world, u, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress) {
+        cudaStreamDestroy(c->stream);
+        cudaEventDestroy(c->joined);
+        delete c;
+        return comm_fail("ncclCommInitRankConfig: %s", n.GetErrorString(r));
+    }
+    if (settle(c, "communicator init") != Q38_OK) {
+        // aborted by settle (a rank did not join in time)
+        cudaStreamDestroy(c->stream);
+        cudaEventDestroy(c->joined);
+        delete c;
+        return Q38_ERR_COMM;
+    }
+    *out = c;
+    return Q38_OK;
+}
+
+q38_status q38_comm_init_all(int ndev, const int* devices, int timeout_ms, q38_comm** comms) {
+    if (ndev < 1 || ndev > 32 || !devices || !comms || timeout_ms < 1) return Q38_ERR_INVALID_ARGUMENT;
+    q38_comm_id id;
+    q38_status st = q38_comm_get_unique_id(&id);
+    if (st != Q38_OK) return st;
+    for (int i = 0; i < ndev; ++i) comms[i] = nullptr;
+    // every rank's non-blocking init is issued first, then all are settled
+    const Nccl& n = nccl();
+    ncclUniqueId u;
+    memcpy(&u, id.bytes, sizeof(u));
+    std::vector<q38_comm*> cs(ndev, nullptr);
+    bool bad = false;
+    n.GroupStart();
+    for (int i = 0; i < ndev && !bad; ++i) {
+        if (cudaSetDevice(devices[i]) != cudaSuccess) {
+            cudaGetLastError();
+            bad = true;
+            break;
+        }
+        q38_comm* c = new q38_comm();
+        c->rank = i;
+        c->world = ndev;
+        c->device = devices[i];
+        c->timeout_ms = timeout_ms;
+        cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+        cudaEventCreateWithFlags(&c->joined, cudaEventDisableTiming);
+        ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+        cfg.blocking = 0;
+        const ncclResult_t r = n.CommInitRankConfig(&c->nc, ndev, u, i, &cfg);
+        cs[i] = c;
+        if (r != ncclSuccess && r != ncclInProgress) bad = true;
+    }
+    n.GroupEnd();
+    for (int i = 0; i < ndev && !bad; ++i)
+        if (cs[i] && settle(cs[i], "communicator init") != Q38_OK) bad = true;
+    if (bad) {
+        for (q38_comm* c : cs) {
+            if (!c) continue;
+            if (c->nc && !c->aborted) n.CommAbort(c->nc);
+            if (c->stream) cudaStreamDestroy(c->stream);
+            if (c->joined) cudaEventDestroy(c->joined);
+            delete c;
+        }
+        if (t_comm_error.empty()) t_comm_error = "communicator init failed";
+        return Q38_ERR_COMM;
+    }
+    for (int i = 0; i < ndev; ++i) comms[i] = cs[i];
+    return Q38_OK;
+}
+
+q38_status q38_comm_destroy(q38_comm* c) {
+    if (!c) return Q38_OK;
+    const Nccl& n = nccl();
+    cudaSetDevice(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    if (c->nc && !c->aborted) n.CommDestroy(c->nc);
+    if (c->buf) cudaFree(c->buf);
+    for (cudaEvent_t e : c->events) cudaEventDestroy(e);
+    if (c->joined) cudaEventDestroy(c->joined);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+    return Q38_OK;
+}
+
+q38_status q38_comm_abort(q38_comm* c) {
+    if (!c) return Q38_ERR_INVALID_ARGUMENT;
+    if (c->nc && !c->aborted) nccl().CommAbort(c->nc);
+    c->aborted = true;
+    return Q38_OK;
+}
+
+int q38_comm_rank(const q38_comm* c) { return c ? c->rank : -1; }
+int q38_comm_size(const q38_comm* c) { return c ? c->world : 0; }
+
+q38_status q38_comm_all_reduce(q38_ctx* ctx, q38_comm* c, const void* send, void* recv, int64_t count,
+                               q38_dtype dtype) {
+    q38_status st = check_pair(ctx, c, "all_reduce");
+    if (st != Q38_OK) return st;
+    if (count < 0 || (count > 0 && (!send || !recv)))
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "all_reduce: bad buffer");
+    if (count == 0) return Q38_OK;
+    const ncclDataType_t t = dtype == Q38_BF16 ? ncclBfloat16 : dtype == Q38_F16 ? ncclFloat16 : ncclFloat32;
+    return nccl_call(ctx, c, nccl().AllReduce(send, recv, static_cast<size_t>(count), t, ncclSum, c->nc, ctx->stream),
+                     "all_reduce");
+}
+
+q38_status q38_tp_mlp(q38_ctx* ctx, q38_comm* c, const void* x, int64_t M, int64_t D, const uint32_t* gate_w,
+                      const void* gate_s, const void* gate_b, const uint32_t* up_w, const void* up_s,
+                      const void* up_b, const uint32_t* down_w, const void* down_s, const void* down_b,
+                      int64_t F_local, q38_dtype dtype, int group_size, int bits, int chunks, void* y) {
+    q38_status st = check_pair(ctx, c, "tp_mlp");
+    if (st != Q38_OK) return st;
+    if (dtype != Q38_BF16) return fail(ctx, Q38_ERR_UNSUPPORTED, "tp_mlp: bf16 activations and scales only");
+    if (M < 0 || D <= 0 || F_local <= 0 || chunks < 1)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "tp_mlp: bad shape or chunk count");
+    if (M == 0) return Q38_OK;
+    if (!x || !gate_w || !gate_s || !up_w || !up_s || !down_w || !down_s || !y)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "tp_mlp: null pointer");
+    // chunks of whole 128-token tiles
+    int64_t step = (M + chunks - 1) / chunks;
+    step = std::max<int64_t>(128, (step + 127) / 128 * 128);
+    uint8_t* hbuf = nullptr;
+    if ((st = comm_buffer(ctx, c, static_cast<size_t>(M) * F_local * 2, &hbuf)) != Q38_OK) return st;
+    const Nccl& n = nccl();
+    size_t ev = 0;
+    for (int64_t m0 = 0; m0 < M; m0 += step) {
+        const int64_t mi = std::min(step, M - m0);
+        const uint8_t* xi = static_cast<const uint8_t*>(x) + static_cast<size_t>(m0) * D * 2;
+        uint8_t* hi = hbuf + static_cast<size_t>(m0) * F_local * 2;
+        uint8_t* yi = static_cast<uint8_t*>(y) + static_cast<size_t>(m0) * D * 2;
+        if ((st = q38_quantized_gate_up(ctx, xi, mi, D, Q38_BF16, gate_w, gate_s, gate_b, up_w, up_s, up_b, Q38_BF16,
+                                        F_local, group_size, bits, Q38_MODE_AFFINE, hi)) != Q38_OK)
+            return st;
+        if ((st = q38_quantized_matmul(ctx, hi, mi, F_local, Q38_BF16, down_w, down_s, down_b, Q38_BF16, D, 1,
+                                       group_size, bits, Q38_MODE_AFFINE, yi)) != Q38_OK)
+            return st;
+        if (c->world == 1) continue;
+        // the all-reduce of this chunk on the communicator's stream, after its products
+        cudaEvent_t e = comm_event(c, ev++);
+        if (!e || cudaEventRecord(e, ctx->stream) != cudaSuccess || cudaStreamWaitEvent(c->stream, e, 0) != cudaSuccess)
+            return check_launch(ctx, "tp_mlp: stream ordering");
+        if ((st = nccl_call(ctx, c, n.AllReduce(yi, yi, static_cast<size_t>(mi) * D, ncclBfloat16, ncclSum, c->nc,
+                                                c->stream),
+                            "tp_mlp all_reduce")) != Q38_OK)
+            return st;
+    }
+    if (c->world > 1) {
+        // the context's stream continues after the last all-reduce
+        if (cudaEventRecord(c->joined, c->stream) != cudaSuccess || cudaStreamWaitEvent(ctx->stream, c->joined, 0) != cudaSuccess)
+            return check_launch(ctx, "tp_mlp: stream join");
+    }
+    return Q38_OK;
+}
+
+q38_status q38_ep_switch_glu(q38_ctx* ctx, q38_comm* c, const void* x, int64_t T, int64_t H, int64_t I, int64_t E,
+                             int top_k, const int32_t* indices, const void* scores, const uint32_t* gate_w,
+                             const void* gate_s, const void* gate_b, const uint32_t* up_w, const void* up_s,
+                             const void* up_b, const uint32_t* down_w, const void* down_s, const void* down_b,
+                             q38_dtype dtype, int group_size, int bits, int64_t capacity, void* out) {
+    q38_status st = check_pair(ctx, c, "ep_switch_glu");
+    if (st != Q38_OK) return st;
+    const int W = c->world;
+    if (dtype != Q38_BF16) return fail(ctx, Q38_ERR_UNSUPPORTED, "ep_switch_glu: bf16 only");
+    if (T < 0 || H <= 0 || H % 8 || I <= 0 || E < W || E % W || top_k < 1 || top_k > E || capacity < 1 || T > capacity)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT,
+                    "ep_switch_glu: need E %% world == 0, 1 <= top_k <= E, T <= capacity, H %% 8 == 0");
+    if (W > 32) return fail(ctx, Q38_ERR_UNSUPPORTED, "ep_switch_glu: at most 32 ranks");
+    if (!x || !indices || !scores || !gate_w || !gate_s || !up_w || !up_s || !down_w || !down_s || !out)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "ep_switch_glu: null pointer");
+    const int64_t C = capacity, epr = E / W, R = W * C;
+    // buffers: staging of x (T < C), send metadata, received rows and metadata, partial sums,
+    // returned partials
+    const size_t xrow = static_cast<size_t>(H) * 2;
+    size_t off = 0;
+    auto take = [&](size_t b) {
+        const size_t o = off;
+        off += align_up(b, 256);
+        return o;
+    };
+    const size_t o_xs = take(T < C ? C * xrow : 0), o_ids = take(R * top_k * 4), o_sc = take(R * top_k * 2),
+                 o_xr = take(R * xrow), o_idr = take(R * top_k * 4), o_scr = take(R * top_k * 2),
+                 o_part = take(R * xrow), o_back = take(R * xrow);
+    uint8_t* b = nullptr;
+    if ((st = comm_buffer(ctx, c, off, &b)) != Q38_OK) return st;
+    const void* xsend = x;
+    if (T < C) {
+        if (T > 0 && cudaMemcpyAsync(b + o_xs, x, T * xrow, cudaMemcpyDeviceToDevice, ctx->stream) != cudaSuccess)
+            return check_launch(ctx, "ep_switch_glu: staging");
+        xsend = b + o_xs;
+    }
+    int32_t* ids = reinterpret_cast<int32_t*>(b + o_ids);
+    __nv_bfloat16* sc = reinterpret_cast<__nv_bfloat16*>(b + o_sc);
+    cudaLaunchAttribute attr[1];
+    {
+        const int64_t total = R * top_k;
+        cudaLaunchConfig_t cfg = pdl_cfg(dim3(static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 1184))),
+                                         dim3(256), ctx->stream, attr);
+        if (cudaLaunchKernelEx(&cfg, ep_fixed_meta, indices, static_cast<const __nv_bfloat16*>(scores),
+                               static_cast<int>(T), static_cast<int>(C), top_k, static_cast<int>(E),
+                               static_cast<int>(epr), W, ids, sc) != cudaSuccess)
+            return check_launch(ctx, "ep_fixed_meta");
+    }
+    const Nccl& n = nccl();
+    uint8_t* xr = b + o_xr;
+    int32_t* idr = reinterpret_cast<int32_t*>(b + o_idr);
+    __nv_bfloat16* scr = reinterpret_cast<__nv_bfloat16*>(b + o_scr);
+    // dispatch: rows, slot experts and scores to every rank (rank r's block of C rows)
+    n.GroupStart();
+    for (int r = 0; r < W; ++r) {
+        n.Send(xsend, C * H, ncclBfloat16, r, c->nc, ctx->stream);
+        n.Recv(xr + r * C * xrow, C * H, ncclBfloat16, r, c->nc, ctx->stream);
+        n.Send(ids + r * C * top_k, C * top_k, ncclInt32, r, c->nc, ctx->stream);
+        n.Recv(idr + r * C * top_k, C * top_k, ncclInt32, r, c->nc, ctx->stream);
+        n.Send(sc + r * C * top_k, C * top_k, ncclBfloat16, r, c->nc, ctx->stream);
+        n.Recv(scr + r * C * top_k, C * top_k, ncclBfloat16, r, c->nc, ctx->stream);
+    }
+    if ((st = nccl_call(ctx, c, n.GroupEnd(), "ep_switch_glu dispatch")) != Q38_OK) return st;
+    // this rank's experts over every received row (slots of other ranks' experts are -1)
+    uint8_t* part = b + o_part;
+    if ((st = q38_switch_glu(ctx, xr, R, H, I, epr, top_k, idr, scr, gate_w, gate_s, gate_b, up_w, up_s, up_b, down_w,
+                             down_s, down_b, dtype, group_size, bits, part)) != Q38_OK)
+        return st;
+    // return: each rank's partial sums of the rows it received go back to their home rank
+    uint8_t* back = b + o_back;
+    n.GroupStart();
+    for (int r = 0; r < W; ++r) {
+        n.Send(part + r * C * xrow, C * H, ncclBfloat16, r, c->nc, ctx->stream);
+        n.Recv(back + r * C * xrow, C * H, ncclBfloat16, r, c->nc, ctx->stream);
+    }
+    if ((st = nccl_call(ctx, c, n.GroupEnd(), "ep_switch_glu return")) != Q38_OK) return st;
+    if (T == 0) return Q38_OK;
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3(static_cast<unsigned>((H / 8 + 255) / 256), static_cast<unsigned>(T)),
+                                     dim3(256), ctx->stream, attr);
+    if (cudaLaunchKernelEx(&cfg, ep_fixed_reduce, static_cast<const __nv_bfloat16*>(static_cast<void*>(back)), indices,
+                           static_cast<int>(T), static_cast<int>(C), top_k, static_cast<int>(E), static_cast<int>(epr),
+                           W, static_cast<int>(H), static_cast<__nv_bfloat16*>(out)) != cudaSuccess)
+        return check_launch(ctx, "ep_fixed_reduce");
+    return Q38_OK;
+}
+
+}  // extern "C"

@@ -17,6 +17,7 @@
 //            out_t = bf16(sum_k score_tk * y_tk) in slot order.
 #include <algorithm>
 #include <mutex>
+#include <type_traits>
 
 #include "moe_internal.h"
 #include "tc_pipeline.cuh"
@@ -210,26 +211,22 @@ __global__ void __launch_bounds__(128, 1) router_logits_tc(const __grid_constant
     if (warp == 1) tmem_dealloc(tmem, R_N);
 }
 
-// softmax + top-k, one warp per token; lane l holds experts l, l+32, ... (NJ per lane).
+// softmax + top-k of one token by one warp; lane l holds experts l, l+32, ... (NJ per lane).
 // The r-th winner is kept by lane r; the renormalisation sum accumulates in selection
-// order on every lane.
-template <int NJ>
-__global__ void __launch_bounds__(256) router_topk(const __nv_bfloat16* __restrict__ logits, int T, int E,
-                                                   int top_k, int normalize, int32_t* __restrict__ indices,
-                                                   __nv_bfloat16* __restrict__ scores,
-                                                   __nv_bfloat16* __restrict__ probs) {
-    griddep_wait();  // inputs come from the previous kernel on the stream
-    griddep_launch_dependents();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * 8 + warp;
-    if (t >= T) return;
+// order on every lane.  CG: read the logits past L1 (they were written by other blocks of
+// the same grid).
+template <int NJ, bool CG>
+__device__ __forceinline__ void topk_token(const __nv_bfloat16* __restrict__ logits, int t, int E, int top_k,
+                                           int normalize, int32_t* __restrict__ indices,
+                                           __nv_bfloat16* __restrict__ scores, __nv_bfloat16* __restrict__ probs,
+                                           int lane) {
     const uint16_t* l = reinterpret_cast<const uint16_t*>(logits) + static_cast<size_t>(t) * E;
     float v[NJ];
     float mx = -INFINITY;
 #pragma unroll
     for (int j = 0; j < NJ; ++j) {
         const int e = lane + 32 * j;
-        v[j] = e < E ? bf16_bits_to_f32(l[e]) : -INFINITY;
+        v[j] = e < E ? bf16_bits_to_f32(CG ? __ldcg(l + e) : l[e]) : -INFINITY;
         mx = fmaxf(mx, v[j]);
     }
 #pragma unroll
@@ -290,6 +287,93 @@ __global__ void __launch_bounds__(256) router_topk(const __nv_bfloat16* __restri
         indices[static_cast<size_t>(t) * top_k + lane] = my_i;
         scores[static_cast<size_t>(t) * top_k + lane] = __float2bfloat16_rn(normalize ? __fdiv_rn(my_v, denom) : my_v);
     }
+}
+
+// softmax + top-k, one warp per token.
+template <int NJ>
+__global__ void __launch_bounds__(256) router_topk(const __nv_bfloat16* __restrict__ logits, int T, int E,
+                                                   int top_k, int normalize, int32_t* __restrict__ indices,
+                                                   __nv_bfloat16* __restrict__ scores,
+                                                   __nv_bfloat16* __restrict__ probs) {
+    griddep_wait();  // inputs come from the previous kernel on the stream
+    griddep_launch_dependents();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 8 + warp;
+    if (t >= T) return;
+    topk_token<NJ, false>(logits, t, E, top_k, normalize, indices, scores, probs, lane);
+}
+
+// Router for a few tokens (decode) in one launch: every block computes the logits of 4
+// experts (one warp each, all NT >= T tokens from shared memory, eight 16-byte loads in
+// flight per lane), stores them as bf16, and counts itself done; the last block to finish
+// (device-scope fence, then an atomic counter that it returns to zero) runs the softmax and
+// top-k of every token.
+template <int NT, int NJ>
+__global__ void __launch_bounds__(128) router_decode(const __nv_bfloat16* __restrict__ x, int T, int H,
+                                                     const __nv_bfloat16* __restrict__ wr, int E, int top_k,
+                                                     int normalize, __nv_bfloat16* __restrict__ logits,
+                                                     int32_t* __restrict__ indices, __nv_bfloat16* __restrict__ scores,
+                                                     __nv_bfloat16* __restrict__ probs, unsigned int* counter) {
+    griddep_wait();  // inputs come from the previous kernel on the stream
+    griddep_launch_dependents();
+    extern __shared__ uint4 xs4[];
+    __shared__ bool s_last;
+    const int vec = H / 8;
+    for (int i = threadIdx.x; i < NT * vec; i += 128) {
+        const int t = i / vec;
+        xs4[i] = t < T ? reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * H)[i % vec] : make_uint4(0, 0, 0, 0);
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int e = blockIdx.x * 4 + warp;
+    if (e < E) {
+        const uint4* wrow = reinterpret_cast<const uint4*>(wr + static_cast<size_t>(e) * H);
+        float acc[NT];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+        for (int v0 = lane; v0 < vec; v0 += 32 * 8) {
+            uint4 wu[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) wu[i] = v0 + 32 * i < vec ? __ldg(wrow + v0 + 32 * i) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int v = v0 + 32 * i;
+                if (v >= vec) break;
+                const uint32_t q[4] = {wu[i].x, wu[i].y, wu[i].z, wu[i].w};
+                float wv[8];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    wv[2 * j] = bf16_bits_to_f32(q[j] & 0xFFFFu);
+                    wv[2 * j + 1] = bf16_bits_to_f32(q[j] >> 16);
+                }
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    const uint4 xu = xs4[t * vec + v];
+                    const uint32_t xq[4] = {xu.x, xu.y, xu.z, xu.w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        acc[t] = fmaf(wv[2 * j], bf16_bits_to_f32(xq[j] & 0xFFFFu), acc[t]);
+                        acc[t] = fmaf(wv[2 * j + 1], bf16_bits_to_f32(xq[j] >> 16), acc[t]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            float v = acc[t];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0 && t < T) logits[static_cast<size_t>(t) * E + e] = __float2bfloat16_rn(v);
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(counter, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int t = warp; t < T; t += 4) topk_token<NJ, true>(logits, t, E, top_k, normalize, indices, scores, probs, lane);
+    if (threadIdx.x == 0) atomicExch(counter, 0u);
 }
 
 // --------------------------------------------------------------------------- sort
@@ -815,6 +899,50 @@ q38_status logits_launch(q38_ctx* ctx, const void* x, int64_t T, int64_t H, cons
                       static_cast<int>(H), static_cast<int>(E), static_cast<__nv_bfloat16*>(logits), ctx->d_status);
 }
 
+// The one-launch router for up to 16 tokens (x staged whole in shared memory).
+q38_status route_decode_launch(q38_ctx* ctx, const void* x, int64_t T, int64_t H, const void* wr, int64_t E,
+                               int top_k, int normalize, void* logits, int32_t* indices, void* scores, void* probs) {
+    uint32_t* cnt = nullptr;
+    float* unused = nullptr;
+    q38_status st = ensure_zero_region(ctx, 1, 0, &cnt, &unused);
+    if (st != Q38_OK) return st;
+    const int nt = T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : T <= 8 ? 8 : 16;
+    const size_t sm = static_cast<size_t>(2) * nt * H;
+    const dim3 grid(static_cast<unsigned>((E + 3) / 4));
+    auto go = [&](auto kern) -> q38_status {
+        static std::mutex mu;
+        static const void* done[64] = {};
+        if (sm > 48 * 1024) {
+            std::lock_guard<std::mutex> lk(mu);
+            const void* key = current_context_key();
+            if (ctx->device < 64 && (!key || done[ctx->device] != key)) {
+                if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024) != cudaSuccess)
+                    return check_launch(ctx, "cudaFuncSetAttribute");
+                done[ctx->device] = key;
+            }
+        }
+        return launch_pdl(ctx, "router_decode", kern, grid, dim3(128), sm, static_cast<const __nv_bfloat16*>(x),
+                          static_cast<int>(T), static_cast<int>(H), static_cast<const __nv_bfloat16*>(wr),
+                          static_cast<int>(E), top_k, normalize, static_cast<__nv_bfloat16*>(logits), indices,
+                          static_cast<__nv_bfloat16*>(scores), static_cast<__nv_bfloat16*>(probs),
+                          reinterpret_cast<unsigned int*>(cnt));
+    };
+    auto by_e = [&](auto nt_c) -> q38_status {
+        constexpr int NT = decltype(nt_c)::value;
+        if (E <= 128) return go(router_decode<NT, 4>);
+        if (E <= 256) return go(router_decode<NT, 8>);
+        if (E <= 512) return go(router_decode<NT, 16>);
+        return go(router_decode<NT, 32>);
+    };
+    switch (nt) {
+        case 1: return by_e(std::integral_constant<int, 1>());
+        case 2: return by_e(std::integral_constant<int, 2>());
+        case 4: return by_e(std::integral_constant<int, 4>());
+        case 8: return by_e(std::integral_constant<int, 8>());
+        default: return by_e(std::integral_constant<int, 16>());
+    }
+}
+
 // Scratch ints the sort needs beyond its outputs (per-block counts for large P).
 size_t sort_scratch_ints(int64_t P, int64_t E) {
     return P > 1024 ? static_cast<size_t>((P + 1023) / 1024) * (E + 1) : 1;
@@ -878,6 +1006,9 @@ q38_status q38_moe_route(q38_ctx* ctx, const void* x, int64_t T, int64_t H, q38_
     if (st != Q38_OK) return st;
     if ((st = ensure_workspace(ctx, static_cast<size_t>(T) * E * 2)) != Q38_OK) return st;
     void* logits = ctx->workspace;
+    if (T <= 16 && static_cast<size_t>(16) * H * 2 <= 96 * 1024) return route_decode_launch(ctx, x, T, H, wr, E, top_k,
+                                                                                            normalize, logits, indices,
+                                                                                            scores, probs);
     if ((st = logits_launch(ctx, x, T, H, wr, E, logits)) != Q38_OK) return st;
     return topk_launch(ctx, logits, T, E, top_k, normalize, indices, scores, probs);
 }
@@ -940,6 +1071,11 @@ q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
     if (P > (1 << 24)) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "switch_glu: more than 2^24 (token, slot) pairs");
     q38_status st = set_dev(ctx);
     if (st != Q38_OK) return st;
+    // a few tokens (decode): the selected experts' weights streamed by the decode kernel
+    if (qgemv_moe_supported(T, H, I, E, top_k, group_size, bits, x, gate_w, gate_s, gate_b, up_w, up_s, up_b, down_w,
+                            down_s, down_b))
+        return qgemv_moe_decode(ctx, x, T, H, I, E, top_k, indices, scores, gate_w, gate_s, gate_b, up_w, up_s, up_b,
+                                down_w, down_s, down_b, bits, out);
 
     const int rb_gu = static_cast<int>(I / 64), rb_d = static_cast<int>(H / 128);
     // An expert receives at most one pair per token, so runs never exceed T pairs.

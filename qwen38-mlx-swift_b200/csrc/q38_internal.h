@@ -102,6 +102,17 @@ q38_status qgemv_gate_up_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K,
                               const void* sg, const void* bg, const uint32_t* wu, const void* su, const void* bu,
                               int64_t N, int bits, void* h);
 
+// Decode-shaped SwitchGLU (T <= 16 tokens, T * top_k <= 256, group 64, bits 2/3/4/8, bf16,
+// H and I multiples of 512): the selected experts' gate/up and down products on the decode
+// kernel, h formed between them, then the score-weighted combine.
+bool qgemv_moe_supported(int64_t T, int64_t H, int64_t I, int64_t E, int topk, int group, int bits, const void* x,
+                         const void* gw, const void* gs, const void* gb, const void* uw, const void* us,
+                         const void* ub, const void* dw, const void* ds, const void* db);
+q38_status qgemv_moe_decode(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int64_t I, int64_t E, int topk,
+                            const int32_t* idx, const void* scores, const uint32_t* gw, const void* gs,
+                            const void* gb, const uint32_t* uw, const void* us, const void* ub, const uint32_t* dw,
+                            const void* ds, const void* db, int bits, void* out);
+
 // Prompt-shaped product on the tensor cores (M >= 17, group 64, K % 128 == 0, bits 2/3/4,
 // bf16).  Uses the scratch workspace for the permuted activations (M*K bf16).
 bool qgemm_tc_supported(int64_t M, int64_t K, int group, int bits, q38_dtype xd, q38_dtype sd,

@@ -30,6 +30,7 @@
 //    converts the sums to y and zeroes them again, so no per-call clearing is needed.
 //  * The main kernel is launched with programmatic dependent launch: its producer
 //    streams the first stages of weights while the previous kernel is still running.
+#include <algorithm>
 #include <mutex>
 #include <numeric>
 #include <type_traits>
@@ -123,8 +124,8 @@ __device__ __forceinline__ void load_window(const uint8_t* p, uint32_t offA, uin
 // into a bf16 high part (words 0, 1) and the bf16 of the remainder (words 2, 3).
 // ---------------------------------------------------------------------------------
 template <int BITS>
-__device__ __forceinline__ void build_fragments(const uint8_t* xc, int M, uint8_t* base, float (*s_xs)[16],
-                                                float (*s_xp)[16], int lane) {
+__device__ __forceinline__ void build_fragments(const uint8_t* xc, int M, uint8_t* base, uint8_t* hdr,
+                                                float (*s_xs)[16], float (*s_xp)[16], int lane) {
     using F = Fmt<BITS>;
     constexpr uint32_t ONE2 = 0x3F803F80u;  // bf16x2 (1, 1)
     // f16 operands: scale the chunk by 2^-e so that its largest |x| stays below 2^15; the
@@ -141,7 +142,7 @@ __device__ __forceinline__ void build_fragments(const uint8_t* xc, int M, uint8_
         const int E = static_cast<int>(mx >> 7);  // bf16 exponent field of the largest |x|
         const int esh = E > 141 ? E - 141 : 0;
         down = __uint_as_float(static_cast<uint32_t>(127 - esh) << 23);
-        if (lane == 0) *reinterpret_cast<float*>(base + M * F::XF_PER_M) = __uint_as_float(static_cast<uint32_t>(127 + esh) << 23);
+        if (lane == 0) *reinterpret_cast<float*>(hdr) = __uint_as_float(static_cast<uint32_t>(127 + esh) << 23);
     }
     // 32 * M items: every iteration has all 32 lanes, and lanes 4i..4i+3 share (group, token)
     const int items = GROUPS * M * 4;
@@ -216,15 +217,54 @@ struct WeightMaps {
     CUtensorMap codes16, codes64, scales, biases;
 };
 
+// How the partial sums of a subunit leave the kernel, and which rows and activations a
+// tile has.
+enum : int {
+    // Plain product.  Partial sums are added into a zero-at-rest fp32 region with
+    // fire-and-forget reductions; the epilogue converts and re-zeroes (arrival order
+    // decides the fp32 rounding, so repeats may differ in the last bit).
+    MODE_ATOMIC = 0,
+    // Plain product.  Each subunit stores its partial sums into the slot of its k-chunk
+    // (every (chunk, token, row) is written by exactly one warp); the epilogue adds the
+    // chunks in order, so results are bitwise reproducible.
+    MODE_SLOTS = 1,
+    // MoE gate and up projections of a few tokens: the tiles are the gate rows, then the
+    // up rows, of the experts the tokens selected (expert-stacked weights, distinct experts
+    // in ascending order); every token's activations are used for every expert, and only
+    // the (token, slot) pairs that selected the expert are stored, per k-chunk, at
+    // [chunk][pair][2 * rows_per_expert] (gate columns, then up columns).
+    MODE_MOE_GU = 2,
+    // MoE down projection: the tiles are the output rows of the selected experts; the
+    // activations of an expert are the rows of h (x = h [pairs, K]) of the pairs that selected
+    // it; sums are stored at [chunk][pair][rows_per_expert].
+    MODE_MOE_DOWN = 3
+};
+
+constexpr int MOE_MAX_T = 16;      // tokens of a decode-shaped MoE call
+constexpr int MOE_MAX_PAIRS = 256; // (token, slot) pairs, hence distinct experts
+constexpr int MOE_MAX_E = 1024;    // experts (one bit each in a 32-word bitmap)
+// Per-CTA plan of a MoE call in dynamic shared memory: number of distinct experts, the
+// selection bitmap and its word prefix counts, the distinct experts ascending, and for
+// each distinct expert the slot through which each token selected it (-1: not selected).
+constexpr int PLAN_BITS = 16, PLAN_PRE = PLAN_BITS + 128, PLAN_EX = PLAN_PRE + 128,
+              PLAN_SLOT = PLAN_EX + 2 * MOE_MAX_PAIRS, PLAN_BYTES = PLAN_SLOT + MOE_MAX_PAIRS * MOE_MAX_T;
+
+// Header of an activation-fragment slot, after the token blocks: the f16 range factor,
+// the number of tokens of the segment, and (MODE_MOE_DOWN) the pair of each token.
+constexpr int HDR_XUP = 0, HDR_MSEG = 4, HDR_PAIRS = 16, HDR_BYTES = 16 + 4 * MOE_MAX_T;
+
 // The tiles cover one weight of N rows, or two (gate and up of an MLP): tiles [0, tiles_a)
 // are rows of the first, the rest rows of the second, whose partial sums go to workspace
-// columns [N, 2N) (row length ld = N or 2N).
+// columns [N, 2N) (row length ld = N or 2N).  MoE modes take their tiles from the plan.
 struct MainArgs {
     const __nv_bfloat16* x;
     __nv_bfloat16* y;
     float* ws;
     uint32_t* status;
     int M, N, K, C, tiles, tiles_a, ld, stages, lands, stage_bytes, has_bias;
+    // MoE modes
+    const int32_t* idx;  // [T = M, topk] expert of each (token, slot); -1 marks an empty slot
+    int topk, E, rpe, tpe, P, plan_off;
 };
 
 // Accumulator columns.  An m16n8k16 product has 8 columns; with MP (1, 2, 4 or 8) token
@@ -233,17 +273,49 @@ struct MainArgs {
 // The MMAs of a chunk therefore accumulate 8/MP groups into one register set, and the
 // per-group scales are applied once per chunk instead of once per group.
 
-// Adds a warp's partial sums of one 16-row subtile into the fp32 workspace after summing
-// the columns that belong to the same token.  The reductions are fire-and-forget (no
-// fence, no counter): the epilogue kernel, which runs after this grid has completed,
-// converts the sums to y and zeroes them again.
-template <int MP, int TB>
-__device__ __forceinline__ void flush_subtile(float (&acc)[TB][4], int tile, int warp, const MainArgs& a,
-                                              int lane) {
+// Where the sums of one subunit go.
+struct FlushDst {
+    float* base;            // workspace at the subunit's chunk slot (MODE_ATOMIC: the region)
+    int col0;               // workspace column of the tile's first row
+    int nrows;              // rows of the tile that exist (64 except at the end of a plain weight)
+    int ld;                 // workspace row length
+    const int8_t* slot_of;  // MODE_MOE_GU: slot of each token for this expert (-1: not selected)
+    const int* pairs;       // MODE_MOE_DOWN: pair of each segment token
+    int mseg, topk;         // tokens with activations; slots per token
+};
+
+// Workspace row of token m, or -1 when nothing is stored for it.
+template <int MODE>
+__device__ __forceinline__ int out_row(const FlushDst& d, int m) {
+    if (m >= d.mseg) return -1;
+    if constexpr (MODE == MODE_MOE_GU) {
+        const int s = d.slot_of[m];
+        return s < 0 ? -1 : m * d.topk + s;
+    } else if constexpr (MODE == MODE_MOE_DOWN) {
+        return d.pairs[m];
+    } else {
+        return m;
+    }
+}
+
+template <int MODE>
+__device__ __forceinline__ void put(const FlushDst& d, int m, int r, float v) {
+    const int row = out_row<MODE>(d, m);
+    if (row < 0 || r >= d.nrows) return;
+    float* p = d.base + static_cast<size_t>(row) * d.ld + d.col0 + r;
+    if constexpr (MODE == MODE_ATOMIC)
+        atomicAdd(p, v);
+    else
+        *p = v;
+}
+
+// Writes a warp's partial sums of one 16-row subtile after summing the columns that belong
+// to the same token.  Stores and reductions are fire-and-forget: the epilogue kernel, which
+// runs after this grid has completed, reads them.
+template <int MODE, int MP, int TB>
+__device__ __forceinline__ void flush_subtile(float (&acc)[TB][4], int warp, const FlushDst& d, int lane) {
     const int g = lane >> 2, t = lane & 3;
-    const bool second = tile >= a.tiles_a;
-    const int r0 = (second ? tile - a.tiles_a : tile) * 64 + warp * 16 + g;  // row within its weight
-    float* ws = a.ws + (second ? a.N : 0);
+    const int r0 = warp * 16 + g;  // row within the tile
 #pragma unroll
     for (int tb = 0; tb < TB; ++tb) {
         if (MP == 1) {  // every column is token 0
@@ -253,8 +325,8 @@ __device__ __forceinline__ void flush_subtile(float (&acc)[TB][4], int tile, int
             v0 += __shfl_xor_sync(0xffffffffu, v0, 2);
             v2 += __shfl_xor_sync(0xffffffffu, v2, 2);
             if (t == 0) {
-                if (r0 < a.N) atomicAdd(ws + r0, v0);
-                if (r0 + 8 < a.N) atomicAdd(ws + r0 + 8, v2);
+                put<MODE>(d, 0, r0, v0);
+                put<MODE>(d, 0, r0 + 8, v2);
             }
             continue;
         }
@@ -270,13 +342,13 @@ __device__ __forceinline__ void flush_subtile(float (&acc)[TB][4], int tile, int
             for (int e = 0; e < 4; ++e) {
                 const int r = r0 + ((e >> 1) << 3);
                 const int m = tb * 8 + (2 * t + (e & 1)) % MP;
-                if (r < a.N && m < a.M) atomicAdd(ws + static_cast<size_t>(m) * a.ld + r, v[e]);
+                put<MODE>(d, m, r, v[e]);
             }
         }
     }
 }
 
-// y = bf16(partial sums); the sums are returned to zero for the next product.
+// y = bf16(partial sums); the sums are returned to zero for the next product (MODE_ATOMIC).
 __global__ void __launch_bounds__(256) qgemv_epilogue(float* __restrict__ ws, __nv_bfloat16* __restrict__ y,
                                                       int total) {
     griddep_launch_dependents();
@@ -287,15 +359,97 @@ __global__ void __launch_bounds__(256) qgemv_epilogue(float* __restrict__ ws, __
     }
 }
 
+__device__ __forceinline__ float silu_mul_bf16(float g, float u) {
+    g = bf16_bits_to_f32(f32_to_bf16_bits(g));
+    u = bf16_bits_to_f32(f32_to_bf16_bits(u));
+    return g / (1.0f + expf(-g)) * u;
+}
+
+// Ordered sums of the C chunk slots (MODE_SLOTS).  A block of 8 warps covers 8/S groups of
+// 32 consecutive outputs; in a group, warp j adds the slots c = j, j + S, j + 2S, ... in that
+// order (its loads in flight together), then the S warp sums are added in warp order.  S
+// (1, 2, 4 or 8) depends only on the shape, so the result is bitwise reproducible; the host
+// picks it so that small outputs still spread their loads over many threads.
+constexpr int EPI_WARPS = 8;
+
+__device__ __forceinline__ float slot_sum(const float* __restrict__ ws, size_t stride, int C, int j, int S) {
+    float acc = 0.0f;
+    int c = j;
+    for (; c + 3 * S < C; c += 4 * S) {
+        const float v0 = __ldcg(ws + static_cast<size_t>(c) * stride);
+        const float v1 = __ldcg(ws + static_cast<size_t>(c + S) * stride);
+        const float v2 = __ldcg(ws + static_cast<size_t>(c + 2 * S) * stride);
+        const float v3 = __ldcg(ws + static_cast<size_t>(c + 3 * S) * stride);
+        acc += v0;
+        acc += v1;
+        acc += v2;
+        acc += v3;
+    }
+    for (; c < C; c += S) acc += __ldcg(ws + static_cast<size_t>(c) * stride);
+    return acc;
+}
+
+int epilogue_split(long long total, int C) {
+    // enough threads to hide the load latency (about 64K), at most C warps per group
+    int S = 8;
+    while (S > 1 && (total * S > 65536 || S > C)) S >>= 1;
+    return S;
+}
+
+// y = bf16(ordered sum of the chunk slots [C][total]).
+__global__ void __launch_bounds__(32 * EPI_WARPS) qgemv_epilogue_slots(const float* __restrict__ ws,
+                                                                       __nv_bfloat16* __restrict__ y, int total, int C,
+                                                                       int S) {
+    griddep_launch_dependents();
+    griddep_wait();
+    __shared__ float part[EPI_WARPS][32];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = EPI_WARPS / S, grp = w / S, j = w - grp * S;
+    const int i = (blockIdx.x * G + grp) * 32 + lane;
+    part[w][lane] = i < total ? slot_sum(ws + i, static_cast<size_t>(total), C, j, S) : 0.0f;
+    __syncthreads();
+    if (j == 0 && i < total) {
+        float acc = part[w][lane];
+        for (int q = 1; q < S; ++q) acc += part[w + q][lane];
+        y[i] = __float2bfloat16_rn(acc);
+    }
+}
+
+// The same from chunk slots [C][M][2N]: h = bf16(silu(bf16 g) * bf16 u).
+__global__ void __launch_bounds__(32 * EPI_WARPS) qgemv_epilogue_glu_slots(const float* __restrict__ ws,
+                                                                           __nv_bfloat16* __restrict__ h, int N,
+                                                                           int total, int C, int S) {
+    griddep_launch_dependents();
+    griddep_wait();
+    __shared__ float pg[EPI_WARPS][32], pu[EPI_WARPS][32];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = EPI_WARPS / S, grp = w / S, j = w - grp * S;
+    const int i = (blockIdx.x * G + grp) * 32 + lane;
+    const int m = i / N, n = i - m * N;
+    const float* base = ws + static_cast<size_t>(m) * 2 * N + n;
+    const size_t stride = static_cast<size_t>(2) * total;
+    pg[w][lane] = i < total ? slot_sum(base, stride, C, j, S) : 0.0f;
+    pu[w][lane] = i < total ? slot_sum(base + N, stride, C, j, S) : 0.0f;
+    __syncthreads();
+    if (j == 0 && i < total) {
+        float g = pg[w][lane], u = pu[w][lane];
+        for (int q = 1; q < S; ++q) {
+            g += pg[w + q][lane];
+            u += pu[w + q][lane];
+        }
+        h[i] = __float2bfloat16_rn(silu_mul_bf16(g, u));
+    }
+}
+
 // Shared memory: [0, 1 KiB) barriers, [1, 3 KiB) zeros (B operand of columns that do not
 // belong to a group), [3 KiB, ...) the stage ring, then two activation-fragment slots and
-// one staging copy of a chunk of x.
+// one staging copy of a chunk of x (and the MoE plan).
 constexpr int ZERO_OFF = 1024, ZERO_BYTES = 2048, RING_OFF = 3072;
 constexpr int MAX_DYN_SMEM = 226 * 1024;  // 227 KiB per CTA less the static per-group sums
 
 // Gate/up epilogue: h = bf16(silu(g) * u) with g = bf16(gate sums), u = bf16(up sums),
 // the rounding of an MLP whose gate and up projections return bf16; the sums [M][2N]
-// are returned to zero.
+// are returned to zero (MODE_ATOMIC).
 __global__ void __launch_bounds__(256) qgemv_epilogue_glu(float* __restrict__ ws, __nv_bfloat16* __restrict__ h,
                                                           int N, int total) {
     griddep_launch_dependents();
@@ -303,12 +457,75 @@ __global__ void __launch_bounds__(256) qgemv_epilogue_glu(float* __restrict__ ws
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
         const int m = i / N, n = i - m * N;
         float* wg = ws + static_cast<size_t>(m) * 2 * N + n;
-        const float g = bf16_bits_to_f32(f32_to_bf16_bits(__ldcg(wg)));
-        const float u = bf16_bits_to_f32(f32_to_bf16_bits(__ldcg(wg + N)));
-        h[i] = __float2bfloat16_rn(g / (1.0f + expf(-g)) * u);
+        h[i] = __float2bfloat16_rn(silu_mul_bf16(__ldcg(wg), __ldcg(wg + N)));
         __stcg(wg, 0.0f);
         __stcg(wg + N, 0.0f);
     }
+}
+
+// MoE: h[p, k] = bf16(silu(bf16 g) * bf16 u) of every selecting pair p from the gate/up
+// chunk slots [C][P][2I] (chunks added in order); h is the down projection's activation.
+__global__ void __launch_bounds__(256) moe_decode_glu(const float* __restrict__ ws, const int32_t* __restrict__ idx,
+                                                      int P, int E, int I, int C, __nv_bfloat16* __restrict__ h) {
+    griddep_launch_dependents();
+    griddep_wait();
+    const size_t ld = static_cast<size_t>(2) * I, cstride = static_cast<size_t>(P) * ld;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < P * I; i += gridDim.x * blockDim.x) {
+        const int p = i / I, k = i - p * I;
+        const int e = idx[p];
+        if (e < 0 || e >= E) continue;
+        const float* src = ws + static_cast<size_t>(p) * ld + k;
+        float g = 0.0f, u = 0.0f;
+#pragma unroll 4
+        for (int c = 0; c < C; ++c) {
+            g += __ldcg(src + c * cstride);
+            u += __ldcg(src + c * cstride + I);
+        }
+        h[i] = __float2bfloat16_rn(silu_mul_bf16(g, u));
+    }
+}
+
+// MoE combine: out[t, r] = bf16(sum over slots s, in order, of score[t, s] * y_ts[r]) with
+// y_ts = bf16(sum of the down chunk slots [C][P][H] of pair t*topk + s); empty or invalid
+// slots contribute nothing (the weightedExpertSum of SwitchGLU, in its rounding).  One
+// block row per token: the token's experts and scores are read once into shared memory,
+// then every thread's loads of its output's expert rows are in flight together.
+constexpr int COMBINE_MAXK = 32;
+
+__global__ void __launch_bounds__(256) moe_decode_combine(const float* __restrict__ ws, const int32_t* __restrict__ idx,
+                                                          const __nv_bfloat16* __restrict__ scores, int T, int topk,
+                                                          int E, int H, int C, __nv_bfloat16* __restrict__ out) {
+    griddep_launch_dependents();
+    griddep_wait();
+    __shared__ float s_sc[COMBINE_MAXK];
+    __shared__ int s_ok[COMBINE_MAXK];
+    const int t = blockIdx.y;
+    const int P = T * topk;
+    if (threadIdx.x < topk) {
+        const int p = t * topk + threadIdx.x;
+        const int e = idx[p];
+        s_ok[threadIdx.x] = e >= 0 && e < E;
+        s_sc[threadIdx.x] = __bfloat162float(scores[p]);
+    }
+    __syncthreads();
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= H) return;
+    // every slot's first chunk in flight at once, then the further chunks (I > 512)
+    const float* base = ws + static_cast<size_t>(t) * topk * H + r;
+    const size_t cstride = static_cast<size_t>(P) * H;
+    float y[COMBINE_MAXK];
+#pragma unroll
+    for (int s = 0; s < COMBINE_MAXK; ++s) y[s] = (s < topk && s_ok[s]) ? __ldcg(base + static_cast<size_t>(s) * H) : 0.0f;
+    for (int c = 1; c < C; ++c) {
+#pragma unroll
+        for (int s = 0; s < COMBINE_MAXK; ++s)
+            if (s < topk && s_ok[s]) y[s] += __ldcg(base + c * cstride + static_cast<size_t>(s) * H);
+    }
+    float acc = 0.0f;
+#pragma unroll
+    for (int s = 0; s < COMBINE_MAXK; ++s)
+        if (s < topk && s_ok[s]) acc = __fadd_rn(acc, __fmul_rn(s_sc[s], bf16_bits_to_f32(f32_to_bf16_bits(y[s]))));
+    out[static_cast<size_t>(t) * H + r] = __float2bfloat16_rn(acc);
 }
 
 // An f16 value (11 significant bits) as fp32 and as an exact sum of two bf16 values (8 and
@@ -321,14 +538,69 @@ __device__ __forceinline__ void split_f16(uint16_t h, float& f, uint32_t& hi2, u
     lo2 = lo | (lo << 16);
 }
 
+// Position of stage i of a CTA: its k-chunk and tile, in (chunk, tile) order.
+struct StageCursor {
+    int chunk, tile, tiles;
+    __device__ __forceinline__ void next() {
+        if (++tile == tiles) {
+            tile = 0;
+            ++chunk;
+        }
+    }
+};
+
+// Where tile `tile` of a kernel lives: which weight (0 or 1), the TMA row of its first row,
+// the rows that exist, the workspace column of its first row, and (MoE) the index of its
+// expert among the distinct experts.
+template <int MODE>
+struct TileInfo {
+    int wsel, row0, nrows, col0, dslot;
+    __device__ __forceinline__ TileInfo(const MainArgs& a, int tile, int nd, const int16_t* ex) {
+        if constexpr (MODE == MODE_MOE_GU) {
+            const int per = nd * a.tpe;
+            wsel = tile >= per;
+            const int jj = wsel ? tile - per : tile;
+            dslot = jj / a.tpe;
+            const int rt = jj - dslot * a.tpe;
+            row0 = ex[dslot] * a.rpe + rt * 64;
+            nrows = 64;
+            col0 = wsel * a.rpe + rt * 64;
+        } else if constexpr (MODE == MODE_MOE_DOWN) {
+            wsel = 0;
+            dslot = tile / a.tpe;
+            const int rt = tile - dslot * a.tpe;
+            row0 = ex[dslot] * a.rpe + rt * 64;
+            nrows = 64;
+            col0 = rt * 64;
+        } else {
+            wsel = tile >= a.tiles_a;
+            const int lt = wsel ? tile - a.tiles_a : tile;
+            row0 = lt * 64;
+            nrows = min(64, a.N - lt * 64);
+            col0 = (wsel ? a.N : 0) + lt * 64;
+            dslot = 0;
+        }
+    }
+};
+
+// Activation segment of a stage: stages with equal keys share their activation fragments.
+template <int MODE>
+__device__ __forceinline__ int seg_key(const MainArgs& a, int chunk, int tile) {
+    if constexpr (MODE == MODE_MOE_DOWN)
+        return chunk * MOE_MAX_PAIRS + tile / a.tpe;
+    else
+        return chunk;
+}
+
 // PACK: f16 scales and biases with group 128 (the layout of the Bonsai 2 packs); each 64-k
 // subgroup uses the scale of its 128-group, read from a stage box that holds the 8 groups of
 // an aligned pair of chunks.
-template <int BITS, int MP, int TB, bool PACK = false>
+template <int BITS, int MP, int TB, bool PACK, int MODE>
 __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 1 ? 2 : 1)) qgemv_main(const __grid_constant__ WeightMaps maps,
                                                                       const __grid_constant__ WeightMaps maps_b,
                                                                       const MainArgs a) {
     using F = Fmt<BITS>;
+    constexpr bool MOE = MODE == MODE_MOE_GU || MODE == MODE_MOE_DOWN;
     constexpr int GPER = 8 / MP;                 // groups sharing one accumulator set
     constexpr int UG = 2;                        // groups extracted together
     constexpr int FLUSH = TB == 1 ? GROUPS : UG; // groups between scale applications
@@ -351,23 +623,80 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
     const uint8_t* zeros = smem + ZERO_OFF;
     uint8_t* stage0 = smem + RING_OFF;
     uint8_t* xslots = stage0 + static_cast<size_t>(a.stages) * a.stage_bytes;
-    const int xslot_bytes = a.M * F::XF_PER_M + 16;  // + the chunk's f16 range factor
+    const int xslot_bytes = a.M * F::XF_PER_M + HDR_BYTES;
     uint8_t* xstage = xslots + 2 * xslot_bytes;
     __shared__ float s_xs[GROUPS][16], s_xp[GROUPS][16];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    // MoE: the plan, computed by every CTA from the routing indices (written by an earlier
+    // kernel on the stream, so everything waits for it first).
+    int nd = 0;
+    const int16_t* ex = nullptr;
+    const int8_t* slot_tab = nullptr;
+    int tiles = a.tiles;
+    if constexpr (MOE) {
+        griddep_wait();
+        uint8_t* plan = smem + a.plan_off;
+        uint32_t* bits = reinterpret_cast<uint32_t*>(plan + PLAN_BITS);
+        int* pre = reinterpret_cast<int*>(plan + PLAN_PRE);
+        int16_t* exw = reinterpret_cast<int16_t*>(plan + PLAN_EX);
+        int8_t* slw = reinterpret_cast<int8_t*>(plan + PLAN_SLOT);
+        for (int i = threadIdx.x; i < 32; i += blockDim.x) bits[i] = 0u;
+        for (int i = threadIdx.x; i < MOE_MAX_PAIRS * MOE_MAX_T / 4; i += blockDim.x)
+            reinterpret_cast<uint32_t*>(slw)[i] = 0xFFFFFFFFu;
+        __syncthreads();
+        bool bad = false;
+        for (int i = threadIdx.x; i < a.P; i += blockDim.x) {
+            const int e = a.idx[i];
+            if (e >= 0 && e < a.E)
+                atomicOr(&bits[e >> 5], 1u << (e & 31));
+            else if (e != -1)
+                bad = true;
+        }
+        if (bad && blockIdx.x == 0) atomicOr(a.status, Q38_DEV_BAD_INDEX);
+        __syncthreads();
+        if (warp == 0) {
+            uint32_t w = bits[lane];
+            const int c = __popc(w);
+            int incl = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            int base = incl - c;
+            pre[lane] = base;
+            while (w) {
+                exw[base++] = static_cast<int16_t>(lane * 32 + __ffs(w) - 1);
+                w &= w - 1;
+            }
+            if (lane == 31) *reinterpret_cast<int*>(plan) = incl;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < a.P; i += blockDim.x) {
+            const int e = a.idx[i];
+            if (e < 0 || e >= a.E) continue;
+            const int j = pre[e >> 5] + __popc(bits[e >> 5] & ((1u << (e & 31)) - 1u));
+            slw[j * MOE_MAX_T + i / a.topk] = static_cast<int8_t>(i % a.topk);
+        }
+        __syncthreads();
+        nd = *reinterpret_cast<const int*>(plan);
+        ex = exw;
+        slot_tab = slw;
+        tiles = (MODE == MODE_MOE_GU ? 2 : 1) * nd * a.tpe;
+    }
 
     // Subunit range of this CTA in (chunk, tile, subtile) order: a CTA covers one or two
-    // chunks of k, so its activation fragments are built once per chunk.
-    const int total_sub = a.tiles * a.C * 4;  // host guarantees < 2^31
+    // chunks of k, so its activation fragments are built once per chunk (MODE_MOE_DOWN: once
+    // per chunk and expert).
+    const int total_sub = tiles * a.C * 4;  // host guarantees < 2^31
     const int s0 = static_cast<int>(static_cast<long long>(total_sub) * blockIdx.x / gridDim.x);
     const int s1 = static_cast<int>(static_cast<long long>(total_sub) * (blockIdx.x + 1) / gridDim.x);
     if (s1 <= s0) return;
     const int st_first = s0 >> 2, st_last = (s1 - 1) >> 2;
     const int nst = st_last - st_first + 1;
     const int lo_first = s0 - 4 * st_first, hi_last = s1 - 4 * st_last;
-    const int chunk_first = st_first / a.tiles;
-    const int nch = st_last / a.tiles - chunk_first + 1;
 
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i < ZERO_BYTES / 16; i += blockDim.x)
         reinterpret_cast<uint4*>(smem + ZERO_OFF)[i] = make_uint4(0u, 0u, 0u, 0u);
     if (!a.has_bias)  // the bias operands of the offset-and-bias steps are then zeros
@@ -391,19 +720,19 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
     if (warp == NCW * WG) {
         // ------------------------------------------------------------ weight producer
         // Streams codes, scales and biases; they are read-only inputs, so the ring fills
-        // while the previous kernel on the stream is still finishing.
+        // while the previous kernel on the stream is still finishing (plain modes).
         if (lane == 0) {
             prefetch_tensormap(&maps.codes16);
             prefetch_tensormap(&maps.codes64);
             prefetch_tensormap(&maps.scales);
             if (a.has_bias) prefetch_tensormap(&maps.biases);
-            if (a.tiles_a < a.tiles) {
+            if (MODE == MODE_MOE_GU || a.tiles_a < a.tiles) {
                 prefetch_tensormap(&maps_b.codes16);
                 prefetch_tensormap(&maps_b.codes64);
                 prefetch_tensormap(&maps_b.scales);
                 if (a.has_bias) prefetch_tensormap(&maps_b.biases);
             }
-            int chunk = st_first / a.tiles, tile = st_first % a.tiles;
+            StageCursor cur{st_first / tiles, st_first % tiles, tiles};
             int slot = 0, fslot = 0;
             uint32_t ph = 0;
             for (int i = 0; i < nst; ++i) {
@@ -418,14 +747,13 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
                 const int sub_hi = i == nst - 1 ? hi_last : 4;
                 uint8_t* sbase = stage0 + static_cast<size_t>(slot) * a.stage_bytes;
                 uint64_t* fb = &full[fslot];
-                const bool second = tile >= a.tiles_a;
-                const WeightMaps& wm = second ? maps_b : maps;
-                const int lt = second ? tile - a.tiles_a : tile;  // tile within its weight
+                const TileInfo<MODE> ti(a, cur.tile, nd, ex);
+                const WeightMaps& wm = ti.wsel ? maps_b : maps;
                 // whole 64-row tiles inside the matrix in one box per column range,
                 // otherwise one 16-row box per active subtile
-                const bool whole = sub_lo == 0 && sub_hi == 4 && lt * 64 + 64 <= a.N;
+                const bool whole = sub_lo == 0 && sub_hi == 4 && ti.nrows == 64;
                 int nact = 0;
-                for (int s = sub_lo; s < sub_hi; ++s) nact += (lt * 64 + 16 * s < a.N);
+                for (int s = sub_lo; s < sub_hi; ++s) nact += (16 * s < ti.nrows);
                 if (whole) nact = 4;
                 const uint32_t bytes = nact * F::SUB_BYTES + 1024 + (a.has_bias ? 1024 : 0);
                 mbar_arrive_expect_tx(fb, bytes);
@@ -433,29 +761,26 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
 #pragma unroll
                     for (int bx = 0; bx < F::BOXES; ++bx)
                         tma_load_2d(sbase + bx * 64 * F::SW, &wm.codes64, fb,
-                                    chunk * F::ROW_WORDS + bx * (F::SW / 4), lt * 64);
+                                    cur.chunk * F::ROW_WORDS + bx * (F::SW / 4), ti.row0);
                 } else {
                     for (int s = sub_lo; s < sub_hi; ++s) {
-                        if (lt * 64 + 16 * s >= a.N) continue;
+                        if (16 * s >= ti.nrows) continue;
 #pragma unroll
                         for (int bx = 0; bx < F::BOXES; ++bx)
                             tma_load_2d(sbase + bx * 64 * F::SW + s * 16 * F::SW, &wm.codes16, fb,
-                                        chunk * F::ROW_WORDS + bx * (F::SW / 4), lt * 64 + 16 * s);
+                                        cur.chunk * F::ROW_WORDS + bx * (F::SW / 4), ti.row0 + 16 * s);
                     }
                 }
                 uint8_t* sc = sbase + NCW * F::SUB_BYTES;
-                const int gx = PACK ? (chunk >> 1) * GROUPS : chunk * GROUPS;  // 16-byte aligned
-                tma_load_2d(sc, &wm.scales, fb, gx, lt * 64);
-                if (a.has_bias) tma_load_2d(sc + 1024, &wm.biases, fb, gx, lt * 64);
+                const int gx = PACK ? (cur.chunk >> 1) * GROUPS : cur.chunk * GROUPS;  // 16-byte aligned
+                tma_load_2d(sc, &wm.scales, fb, gx, ti.row0);
+                if (a.has_bias) tma_load_2d(sc + 1024, &wm.biases, fb, gx, ti.row0);
                 if (++slot == a.stages) {
                     slot = 0;
                     ph ^= 1;
                 }
                 if (++fslot == a.lands) fslot = 0;
-                if (++tile == a.tiles) {
-                    tile = 0;
-                    ++chunk;
-                }
+                cur.next();
             }
         }
         return;
@@ -464,20 +789,53 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
     if (warp == NCW * WG + 1) {
         // ------------------------------------------------------------ activation warp
         // x is written by the previous kernel on the stream: wait for it to complete.
-        griddep_wait();
-        for (int ci = 0; ci < nch; ++ci) {
-            const int c = chunk_first + ci;
-            // all of the chunk's copies in flight at once
-            for (int p = lane; p < a.M * (KC / 8); p += 32) {
-                const int m = p / (KC / 8), q = p % (KC / 8);
-                cp_async16(xstage + m * (KC * 2) + q * 16, a.x + static_cast<size_t>(m) * a.K + c * KC + q * 8);
+        if constexpr (!MOE) griddep_wait();
+        StageCursor cur{st_first / tiles, st_first % tiles, tiles};
+        int ci = -1, key = -1;
+        for (int i = 0; i < nst; ++i, cur.next()) {
+            const int k2 = seg_key<MODE>(a, cur.chunk, cur.tile);
+            if (k2 == key) continue;
+            key = k2;
+            ++ci;
+            const int c = cur.chunk;
+            uint8_t* slotp = xslots + (ci & 1) * xslot_bytes;
+            uint8_t* hdr = slotp + a.M * F::XF_PER_M;
+            int mseg = a.M;
+            if constexpr (MODE == MODE_MOE_DOWN) {
+                // tokens that selected this expert, in token order, and their pairs; their
+                // activations are the rows of h (bf16 [P, K]) of those pairs
+                const int js = cur.tile / a.tpe;
+                const int8_t* so = slot_tab + js * MOE_MAX_T;
+                const int s_l = lane < a.M ? so[lane] : -1;
+                const uint32_t sel = __ballot_sync(0xffffffffu, s_l >= 0);
+                mseg = __popc(sel);
+                const bool ok = ci < 2 || mbar_wait(&xempty[ci & 1], ((ci >> 1) & 1) ^ 1, a.status);
+                if (!ok) return;
+                int* prs = reinterpret_cast<int*>(hdr + HDR_PAIRS);
+                if (s_l >= 0) prs[__popc(sel & ((1u << lane) - 1u))] = lane * a.topk + s_l;
+                if (lane == 0) *reinterpret_cast<int*>(hdr + HDR_MSEG) = mseg;
+                __syncwarp();
+                for (int q = lane; q < mseg * (KC / 8); q += 32) {
+                    const int m = q / (KC / 8), o = q % (KC / 8);
+                    cp_async16(xstage + m * (KC * 2) + o * 16, a.x + static_cast<size_t>(prs[m]) * a.K + c * KC + o * 8);
+                }
+                cp_async_commit();
+                cp_async_wait<0>();
+                __syncwarp();
+            } else {
+                // all of the chunk's copies in flight at once
+                for (int p = lane; p < a.M * (KC / 8); p += 32) {
+                    const int m = p / (KC / 8), q = p % (KC / 8);
+                    cp_async16(xstage + m * (KC * 2) + q * 16, a.x + static_cast<size_t>(m) * a.K + c * KC + q * 8);
+                }
+                cp_async_commit();
+                const bool ok = ci < 2 || mbar_wait(&xempty[ci & 1], ((ci >> 1) & 1) ^ 1, a.status);
+                cp_async_wait<0>();
+                __syncwarp();
+                if (!ok) return;
+                if (lane == 0) *reinterpret_cast<int*>(hdr + HDR_MSEG) = mseg;
             }
-            cp_async_commit();
-            const bool ok = ci < 2 || mbar_wait(&xempty[ci & 1], ((ci >> 1) & 1) ^ 1, a.status);
-            cp_async_wait<0>();
-            __syncwarp();
-            if (!ok) return;
-            build_fragments<BITS>(xstage, a.M, xslots + (ci & 1) * xslot_bytes, s_xs, s_xp, lane);
+            build_fragments<BITS>(xstage, mseg, slotp, hdr, s_xs, s_xp, lane);
             if (lane == 0) mbar_arrive(&xfull[ci & 1]);
         }
         return;
@@ -486,7 +844,7 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
     // -------------------------------------------------------------- consumers
     // The partial sums may still be in use by the previous product's epilogue until it
     // has completed.
-    griddep_wait();
+    if constexpr (!MOE) griddep_wait();
     const int wgrp = warp / NCW;  // this warp's group: it computes the stages i with i % WG == wgrp
     const int sw_i = warp % NCW;  // and, in each, subtile sw_i
     const int g = lane >> 2, t = lane & 3;
@@ -504,49 +862,50 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
     // B operand of column g (this lane's column): token and group slot
     const int ml = g % MP, gsl = g / MP;
     int tok[TB];
-    bool tval[TB];
 #pragma unroll
-    for (int tb = 0; tb < TB; ++tb) {
-        tok[tb] = TB == 1 ? ml : tb * 8 + g;
-        tval[tb] = tok[tb] < a.M;
-    }
+    for (int tb = 0; tb < TB; ++tb) tok[tb] = TB == 1 ? ml : tb * 8 + g;
     const int srow0 = sw_i * 16 + g;  // scale row of row g (row g+8 is 64 halfwords further)
 
-    int cur_ci = -1;
+    int cur_key = -1, ci = -1;
+    int mseg = a.M;
     const uint8_t* xf = xslots;
     float xup = 1.0f;  // range factor of the chunk's f16 activations
     // per group: where this lane's B operand comes from (its fragments, or zeros)
     const uint8_t* pg[TB == 1 ? GROUPS : TB];
-    int chunk = st_first / a.tiles, tile = st_first % a.tiles;
+    StageCursor cur{st_first / tiles, st_first % tiles, tiles};
     int slot = 0, fslot = 0;  // data slot i % stages, landing barrier i % lands
     uint32_t fph = 0;         // phase parity of the landing barrier
     int own = 0;  // i % WG
     for (int i = 0; i < nst; ++i) {
         const int sub_lo = i == 0 ? lo_first : 0;
         const int sub_hi = i == nst - 1 ? hi_last : 4;
-        const int ci = chunk - chunk_first;
-        if (ci != cur_ci) {
-            // the previous chunk's fragments are no longer needed; wait for this chunk's
-            if (cur_ci >= 0) {
+        const int chunk = cur.chunk;
+        const int key = seg_key<MODE>(a, chunk, cur.tile);
+        if (key != cur_key) {
+            // the previous segment's fragments are no longer needed; wait for this one's
+            if (ci >= 0) {
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&xempty[cur_ci & 1]);
+                if (lane == 0) mbar_arrive(&xempty[ci & 1]);
             }
+            ++ci;
             if (!mbar_wait(&xfull[ci & 1], (ci >> 1) & 1, a.status)) return;
-            cur_ci = ci;
+            cur_key = key;
             xf = xslots + (ci & 1) * xslot_bytes;
-            if (F::F16) xup = *reinterpret_cast<const float*>(xf + a.M * F::XF_PER_M);
+            const uint8_t* hdr = xf + a.M * F::XF_PER_M;
+            if (F::F16) xup = *reinterpret_cast<const float*>(hdr + HDR_XUP);
+            mseg = *reinterpret_cast<const int*>(hdr + HDR_MSEG);
             if (TB == 1) {
 #pragma unroll
                 for (int gi = 0; gi < (TB == 1 ? GROUPS : TB); ++gi)
-                    pg[gi] = (tval[0] && gi % GPER == gsl) ? xf + tok[0] * F::XF_PER_M + t * 16 : zeros;
+                    pg[gi] = (tok[0] < mseg && gi % GPER == gsl) ? xf + tok[0] * F::XF_PER_M + t * 16 : zeros;
             } else {
 #pragma unroll
-                for (int tb = 0; tb < TB; ++tb) pg[tb] = tval[tb] ? xf + tok[tb] * F::XF_PER_M + t * 16 : zeros;
+                for (int tb = 0; tb < TB; ++tb) pg[tb] = tok[tb] < mseg ? xf + tok[tb] * F::XF_PER_M + t * 16 : zeros;
             }
         }
         const bool mine = own == wgrp;
-        const int lt = tile >= a.tiles_a ? tile - a.tiles_a : tile;  // tile within its weight
-        const bool active = mine && sw_i >= sub_lo && sw_i < sub_hi && lt * 64 + 16 * sw_i < a.N;
+        const TileInfo<MODE> ti(a, cur.tile, nd, ex);
+        const bool active = mine && sw_i >= sub_lo && sw_i < sub_hi && 16 * sw_i < ti.nrows;
         if (mine && !mbar_wait(&full[fslot], fph, a.status)) return;
         float acc[TB][4];
         if (active) {
@@ -691,7 +1050,7 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
             for (int tb = 0; tb < TB; ++tb) {
                 uint4 bb = make_uint4(0u, 0u, 0u, 0u);
                 const int mt = tb * 8 + g;  // token of column g in slot 0
-                if (mt < a.M && (TB > 1 || g < MP))
+                if (mt < mseg && (TB > 1 || g < MP))
                     bb = *reinterpret_cast<const uint4*>(xf + mt * F::XF_PER_M + F::XF_FRAG + t * 16);
                 mma_bf16_16816(acc[tb], s_g, s_g8, b_g, b_g8, bb.x, bb.y, acc[tb]);
                 mma_bf16_16816(acc[tb], s_g, s_g8, b_g, b_g8, bb.z, bb.w, acc[tb]);
@@ -701,39 +1060,57 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
                 }
             }
         }
-        // Release the stage before adding the sums to the workspace: the arrive orders this
-        // warp's earlier memory operations, and the reductions have not completed yet.
+        // Release the stage before writing the sums: the arrive orders this warp's earlier
+        // memory operations, and the stores have not completed yet.
         if (mine) {
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
         }
-        if (active) flush_subtile<MP, TB>(acc, tile, sw_i, a, lane);
+        if (active) {
+            FlushDst dst;
+            dst.col0 = ti.col0;
+            dst.nrows = ti.nrows;
+            dst.ld = a.ld;
+            dst.mseg = mseg;
+            dst.topk = a.topk;
+            dst.slot_of = nullptr;
+            dst.pairs = nullptr;
+            if constexpr (MODE == MODE_ATOMIC) {
+                dst.base = a.ws;
+            } else if constexpr (MODE == MODE_SLOTS) {
+                dst.base = a.ws + static_cast<size_t>(chunk) * a.M * a.ld;
+            } else {
+                dst.base = a.ws + static_cast<size_t>(chunk) * a.P * a.ld;
+                if constexpr (MODE == MODE_MOE_GU) dst.slot_of = slot_tab + ti.dslot * MOE_MAX_T;
+                if constexpr (MODE == MODE_MOE_DOWN)
+                    dst.pairs = reinterpret_cast<const int*>(xf + a.M * F::XF_PER_M + HDR_PAIRS);
+            }
+            flush_subtile<MODE, MP, TB>(acc, sw_i, dst, lane);
+        }
         if (++own == WG) own = 0;
         if (++slot == a.stages) slot = 0;
         if (++fslot == a.lands) {
             fslot = 0;
             fph ^= 1;
         }
-        if (++tile == a.tiles) {
-            tile = 0;
-            ++chunk;
-        }
+        cur.next();
     }
 }
 
 // Launch geometry shared by the context path and the allocation-free path.
 struct Plan {
-    int C, tiles, stage_bytes, stages, smem;
+    int C, tiles, stage_bytes, stages, smem, plan_off;
 };
 
 template <int BITS>
-bool make_plan(int M, int K, int N, Plan& p, bool two_weights = false) {
+bool make_plan(int M, int K, int N, Plan& p, bool two_weights = false, bool moe = false) {
     using F = Fmt<BITS>;
     p.C = K / KC;
     p.tiles = (N + 63) / 64 * (two_weights ? 2 : 1);
     if (static_cast<long long>(p.tiles) * p.C * 4 >= (1LL << 31)) return false;
     p.stage_bytes = NCW * F::SUB_BYTES + 2048;  // a multiple of 1 KiB
-    const int xbytes = 2 * (M * F::XF_PER_M + 16) + M * KC * 2;  // fragment slots + staging copy of x
+    // fragment slots (with their headers) + staging copy of x (+ the MoE plan)
+    const int xbytes = 2 * (M * F::XF_PER_M + HDR_BYTES) + M * KC * 2 + (moe ? PLAN_BYTES + 16 : 0);
     // 76 KiB per CTA in all (ring, header, zeros, fragments, alignment slack, 1 KiB of
     // static sums) lets three CTAs (12 consumer warps) share an SM; 113 KiB two
     const int budget = (WG == 1 ? (M > 8 ? 113 : 76) : (M > 8 ? 226 : 113)) * 1024 - 1024 - RING_OFF - 1024 - xbytes;
@@ -747,6 +1124,11 @@ bool make_plan(int M, int K, int N, Plan& p, bool two_weights = false) {
     }
     p.stages = stages;
     p.smem = smem;
+    // the plan sits after the staging copy of x, 16-byte aligned (offsets from the
+    // 1024-aligned base)
+    p.plan_off = static_cast<int>(align_up(static_cast<size_t>(RING_OFF) + static_cast<size_t>(stages) * p.stage_bytes +
+                                               2 * (M * F::XF_PER_M + HDR_BYTES) + M * KC * 2,
+                                           16));
     return smem <= MAX_DYN_SMEM;
 }
 
@@ -798,58 +1180,47 @@ bool cached_maps(const uint32_t* w, const void* s, const void* b, int K, int N, 
     return true;
 }
 
-// Launches the main kernel and the epilogue with the given scratch.  Returns a CUDA error code.
-template <int BITS, int MP, int TB, bool PACK = false>
-// With `maps_b` the tiles cover two weights of N rows each (gate, then up) and the epilogue
-// writes y = bf16(silu(gate) * up) [M, N]; the partial sums then take M x 2N floats.
-cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x, int M, int K,
-                           const WeightMaps& maps, bool has_bias, int N, void* y, float* part, uint32_t* status,
-                           cudaStream_t stream, const WeightMaps* maps_b = nullptr) {
-    auto kmain = qgemv_main<BITS, MP, TB, PACK>;
-    // per template instance and device: smem opt-in and occupancy at the largest ring
-    // (keyed on the current context as well: a context created after a device reset
-    // needs the opt-in again)
+// Per template instance and device (and context): the shared-memory opt-in of the main
+// kernel and its occupancy at a given ring size.  (Templated on the instance's parameters,
+// not on the kernel's type, which all instances share: each instance keeps its own state.)
+template <int BITS, int MP, int TB, bool PACK, int MODE>
+cudaError_t configure_main(int device, int smem, int* occ_out) {
+    auto kmain = qgemv_main<BITS, MP, TB, PACK, MODE>;
     static std::mutex mu;
     static const void* configured[64] = {};
     static int occ_smem[64][16] = {}, occ_val[64][16] = {};
     if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
-    int occ = 0;
-    {
-        std::lock_guard<std::mutex> lk(mu);
-        const void* key = current_context_key();
-        if (!key || configured[device] != key) {
-            cudaError_t e = cudaFuncSetAttribute(kmain, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_DYN_SMEM);
-            if (e != cudaSuccess) return e;
-            configured[device] = key;
+    std::lock_guard<std::mutex> lk(mu);
+    const void* key = current_context_key();
+    if (!key || configured[device] != key) {
+        cudaError_t e = cudaFuncSetAttribute(kmain, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_DYN_SMEM);
+        if (e != cudaSuccess) return e;
+        configured[device] = key;
+        for (int i = 0; i < 16; ++i) occ_smem[device][i] = 0;
+    }
+    int occ = 0, slot = -1;
+    for (int i = 0; i < 16; ++i) {
+        if (occ_smem[device][i] == smem) {
+            occ = occ_val[device][i];
+            break;
         }
-        int slot = -1;
-        for (int i = 0; i < 16; ++i) {
-            if (occ_smem[device][i] == p.smem) {
-                occ = occ_val[device][i];
-                break;
-            }
-            if (occ_smem[device][i] == 0 && slot < 0) slot = i;
-        }
-        if (occ == 0) {
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kmain, THREADS, p.smem);
-            if (occ < 1) occ = 1;
-            if (slot >= 0) {
-                occ_smem[device][slot] = p.smem;
-                occ_val[device][slot] = occ;
-            }
+        if (occ_smem[device][i] == 0 && slot < 0) slot = i;
+    }
+    if (occ == 0) {
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kmain, THREADS, smem);
+        if (occ < 1) occ = 1;
+        if (slot >= 0) {
+            occ_smem[device][slot] = smem;
+            occ_val[device][slot] = occ;
         }
     }
-    const long long total_sub = static_cast<long long>(p.tiles) * p.C * 4;
-    long long grid = static_cast<long long>(num_sms) * occ;
-    if (grid > total_sub) grid = total_sub;
+    *occ_out = occ;
+    return cudaSuccess;
+}
 
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-
-    MainArgs args;
+MainArgs base_args(const Plan& p, const void* x, int M, int K, int N, float* part, uint32_t* status, bool has_bias) {
+    MainArgs args = {};
     args.x = static_cast<const __nv_bfloat16*>(x);
-    args.y = static_cast<__nv_bfloat16*>(y);
     args.ws = part;
     args.status = status;
     args.M = M;
@@ -857,36 +1228,95 @@ cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x
     args.K = K;
     args.C = p.C;
     args.tiles = p.tiles;
-    args.tiles_a = maps_b ? p.tiles / 2 : p.tiles;
-    args.ld = maps_b ? 2 * N : N;
+    args.tiles_a = p.tiles;
+    args.ld = N;
     args.stages = p.stages;
     args.lands = std::lcm(p.stages, WG);
     args.stage_bytes = p.stage_bytes;
     args.has_bias = has_bias;
+    args.plan_off = p.plan_off;
+    return args;
+}
 
+cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t stream, cudaLaunchAttribute* attr) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(grid));
-    cfg.blockDim = dim3(THREADS);
-    cfg.dynamicSmemBytes = p.smem;
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kmain, maps, maps_b ? *maps_b : maps, args);
+    return cfg;
+}
+
+// Launches the main kernel on `args` over `total_sub` subunits (an upper bound for MoE).
+template <int BITS, int MP, int TB, bool PACK, int MODE>
+cudaError_t launch_main(const Plan& p, int device, int num_sms, const WeightMaps& maps, const WeightMaps& maps_b,
+                        const MainArgs& args, long long total_sub, cudaStream_t stream) {
+    auto kmain = qgemv_main<BITS, MP, TB, PACK, MODE>;
+    int occ = 0;
+    cudaError_t e = configure_main<BITS, MP, TB, PACK, MODE>(device, p.smem, &occ);
+    if (e != cudaSuccess) return e;
+    long long grid = static_cast<long long>(num_sms) * occ;
+    if (grid > total_sub) grid = total_sub;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_config(dim3(static_cast<unsigned>(grid)), dim3(THREADS), p.smem, stream, attr);
+    return cudaLaunchKernelEx(&cfg, kmain, maps, maps_b, args);
+}
+
+int epilogue_blocks(long long total, int num_sms) {
+    long long b = (total + 255) / 256;
+    if (b > num_sms * 4) b = num_sms * 4;
+    return static_cast<int>(b < 1 ? 1 : b);
+}
+
+// Launches the main kernel and the epilogue with the given scratch.  Returns a CUDA error code.
+// With `maps_b` the tiles cover two weights of N rows each (gate, then up) and the epilogue
+// writes y = bf16(silu(gate) * up) [M, N].  SLOTS: partial sums per k-chunk in `part`
+// (C x M x N floats, 2N with maps_b), added in order by the epilogue; otherwise `part` is
+// the zero-at-rest region of M x N (2N) floats.
+template <int BITS, int MP, int TB, bool PACK = false, bool SLOTS = true>
+cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x, int M, int K,
+                           const WeightMaps& maps, bool has_bias, int N, void* y, float* part, uint32_t* status,
+                           cudaStream_t stream, const WeightMaps* maps_b = nullptr) {
+    constexpr int MODE = SLOTS ? MODE_SLOTS : MODE_ATOMIC;
+    MainArgs args = base_args(p, x, M, K, N, part, status, has_bias);
+    args.y = static_cast<__nv_bfloat16*>(y);
+    args.tiles_a = maps_b ? p.tiles / 2 : p.tiles;
+    args.ld = maps_b ? 2 * N : N;
+    const long long total_sub = static_cast<long long>(p.tiles) * p.C * 4;
+    cudaError_t e = launch_main<BITS, MP, TB, PACK, MODE>(p, device, num_sms, maps, maps_b ? *maps_b : maps, args,
+                                                          total_sub, stream);
     if (e != cudaSuccess) return e;
 
     const int total = M * N;
-    int eblocks = (total + 255) / 256;
-    if (eblocks > num_sms * 4) eblocks = num_sms * 4;
-    cudaLaunchConfig_t ecfg = {};
-    ecfg.gridDim = dim3(static_cast<unsigned>(eblocks));
-    ecfg.blockDim = dim3(256);
-    ecfg.stream = stream;
-    ecfg.attrs = attr;
-    ecfg.numAttrs = 1;
-    e = maps_b ? cudaLaunchKernelEx(&ecfg, qgemv_epilogue_glu, part, static_cast<__nv_bfloat16*>(y), N, total)
-               : cudaLaunchKernelEx(&ecfg, qgemv_epilogue, part, static_cast<__nv_bfloat16*>(y), total);
+    cudaLaunchAttribute attr[1];
+    const int S = epilogue_split(total, p.C), G = EPI_WARPS / S;
+    cudaLaunchConfig_t ecfg =
+        SLOTS ? pdl_config(dim3((total + 32 * G - 1) / (32 * G)), dim3(32 * EPI_WARPS), 0, stream, attr)
+              : pdl_config(dim3(epilogue_blocks(total, num_sms)), dim3(256), 0, stream, attr);
+    __nv_bfloat16* yb = static_cast<__nv_bfloat16*>(y);
+    if (SLOTS)
+        e = maps_b ? cudaLaunchKernelEx(&ecfg, qgemv_epilogue_glu_slots, static_cast<const float*>(part), yb, N, total,
+                                        p.C, S)
+                   : cudaLaunchKernelEx(&ecfg, qgemv_epilogue_slots, static_cast<const float*>(part), yb, total, p.C,
+                                        S);
+    else
+        e = maps_b ? cudaLaunchKernelEx(&ecfg, qgemv_epilogue_glu, part, yb, N, total)
+                   : cudaLaunchKernelEx(&ecfg, qgemv_epilogue, part, yb, total);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
+}
+
+// Chunk slots of a plain product in the context's workspace.
+q38_status slot_workspace(q38_ctx* ctx, const Plan& p, int M, int N, bool two, float** out) {
+    const size_t bytes = static_cast<size_t>(p.C) * M * N * (two ? 2 : 1) * sizeof(float);
+    q38_status st = ensure_workspace(ctx, bytes);
+    if (st != Q38_OK) return st;
+    *out = static_cast<float*>(ctx->workspace);
+    return Q38_OK;
 }
 
 template <int BITS, int MP, int TB>
@@ -894,9 +1324,8 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
                   const void* b, int N, void* y) {
     Plan p;
     if (!make_plan<BITS>(M, K, N, p)) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: shape too large");
-    uint32_t* cnt = nullptr;  // (no counters are used)
     float* part = nullptr;
-    q38_status st = ensure_zero_region(ctx, 0, static_cast<size_t>(M) * N, &cnt, &part);
+    q38_status st = slot_workspace(ctx, p, M, N, false, &part);
     if (st != Q38_OK) return st;
     WeightMaps maps;
     if (!cached_maps<BITS>(w, s, b, K, N, &maps))
@@ -916,9 +1345,8 @@ q38_status launch_pack(q38_ctx* ctx, const void* x, int M, int K, const uint32_t
                        const void* b, int N, void* y) {
     Plan p;
     if (!make_plan<BITS>(M, K, N, p)) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: shape too large");
-    uint32_t* cnt = nullptr;
     float* part = nullptr;
-    q38_status st = ensure_zero_region(ctx, 0, static_cast<size_t>(M) * N, &cnt, &part);
+    q38_status st = slot_workspace(ctx, p, M, N, false, &part);
     if (st != Q38_OK) return st;
     WeightMaps maps;
     if (!cached_maps<BITS, true>(w, s, b, K, N, &maps))
@@ -938,9 +1366,8 @@ q38_status launch_gate_up(q38_ctx* ctx, const void* x, int M, int K, const uint3
                           const void* bg, const uint32_t* wu, const void* su, const void* bu, int N, void* h) {
     Plan p;
     if (!make_plan<BITS>(M, K, N, p, true)) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_gate_up: shape too large");
-    uint32_t* cnt = nullptr;
     float* part = nullptr;
-    q38_status st = ensure_zero_region(ctx, 0, static_cast<size_t>(M) * 2 * N, &cnt, &part);
+    q38_status st = slot_workspace(ctx, p, M, N, true, &part);
     if (st != Q38_OK) return st;
     WeightMaps mg, mu;
     if (!cached_maps<BITS, PACK>(wg, sg, bg, K, N, &mg) || !cached_maps<BITS, PACK>(wu, su, bu, K, N, &mu))
@@ -950,6 +1377,77 @@ q38_status launch_gate_up(q38_ctx* ctx, const void* x, int M, int K, const uint3
     if (e != cudaSuccess) {
         cudaGetLastError();
         return fail(ctx, Q38_ERR_CUDA, "quantized_gate_up: launch failed: %s", cudaGetErrorString(e));
+    }
+    return Q38_OK;
+}
+
+// Decode-shaped SwitchGLU: gate/up over the selected experts (all T tokens' activations,
+// only selecting pairs stored), down over the same experts with h formed from the gate/up
+// slots, then the score-weighted combine.  Three launches, chained with programmatic
+// dependent launch; scratch: the chunk slots of both products in the workspace.
+template <int BITS, int MP, int TB>
+q38_status launch_moe_decode(q38_ctx* ctx, const void* x, int T, int H, int I, int E, int topk, const int32_t* idx,
+                             const void* scores, const uint32_t* gw, const void* gs, const void* gb,
+                             const uint32_t* uw, const void* us, const void* ub, const uint32_t* dw, const void* ds,
+                             const void* db, void* out) {
+    const int P = T * topk;
+    const int nd_max = std::min(E, P);
+    Plan pg, pd;
+    // gate/up: K = H, rows per expert I; down: K = I, rows per expert H
+    if (!make_plan<BITS>(T, H, nd_max * I, pg, true, true) || !make_plan<BITS>(T, I, nd_max * H, pd, false, true))
+        return fail(ctx, Q38_ERR_UNSUPPORTED, "switch_glu: decode plan does not fit");
+    const size_t gu_floats = static_cast<size_t>(pg.C) * P * 2 * I;
+    const size_t dn_floats = static_cast<size_t>(pd.C) * P * H;
+    const size_t h_bytes = align_up(static_cast<size_t>(P) * I * 2, 256);
+    q38_status st = ensure_workspace(ctx, (gu_floats + dn_floats) * sizeof(float) + h_bytes);
+    if (st != Q38_OK) return st;
+    float* gu_slots = static_cast<float*>(ctx->workspace);
+    float* dn_slots = gu_slots + gu_floats;
+    __nv_bfloat16* hbuf = reinterpret_cast<__nv_bfloat16*>(dn_slots + dn_floats);
+    WeightMaps mg, mu, md;
+    if (!cached_maps<BITS>(gw, gs, gb, H, E * I, &mg) || !cached_maps<BITS>(uw, us, ub, H, E * I, &mu) ||
+        !cached_maps<BITS>(dw, ds, db, I, E * H, &md))
+        return fail(ctx, Q38_ERR_CUDA, "switch_glu: tensor map encoding failed");
+    const bool has_bias = gb != nullptr;
+
+    MainArgs a = base_args(pg, x, T, H, 0, gu_slots, ctx->d_status, has_bias);
+    a.idx = idx;
+    a.topk = topk;
+    a.E = E;
+    a.P = P;
+    a.rpe = I;
+    a.tpe = I / 64;
+    a.ld = 2 * I;
+    cudaError_t e = launch_main<BITS, MP, TB, false, MODE_MOE_GU>(pg, ctx->device, ctx->num_sms, mg, mu, a,
+                                                                  static_cast<long long>(pg.tiles) * pg.C * 4,
+                                                                  ctx->stream);
+    cudaLaunchAttribute attr[1];
+    if (e == cudaSuccess) {
+        cudaLaunchConfig_t cfg = pdl_config(dim3(epilogue_blocks(static_cast<long long>(P) * I, ctx->num_sms)),
+                                            dim3(256), 0, ctx->stream, attr);
+        e = cudaLaunchKernelEx(&cfg, moe_decode_glu, static_cast<const float*>(gu_slots), idx, P, E, I, pg.C, hbuf);
+    }
+    if (e == cudaSuccess) {
+        MainArgs d = base_args(pd, hbuf, T, I, 0, dn_slots, ctx->d_status, has_bias);
+        d.idx = idx;
+        d.topk = topk;
+        d.E = E;
+        d.P = P;
+        d.rpe = H;
+        d.tpe = H / 64;
+        d.ld = H;
+        e = launch_main<BITS, MP, TB, false, MODE_MOE_DOWN>(pd, ctx->device, ctx->num_sms, md, md, d,
+                                                            static_cast<long long>(pd.tiles) * pd.C * 4, ctx->stream);
+    }
+    if (e == cudaSuccess) {
+        cudaLaunchConfig_t cfg = pdl_config(dim3((H + 255) / 256, T), dim3(256), 0, ctx->stream, attr);
+        e = cudaLaunchKernelEx(&cfg, moe_decode_combine, static_cast<const float*>(dn_slots), idx,
+                               static_cast<const __nv_bfloat16*>(scores), T, topk, E, H, pd.C,
+                               static_cast<__nv_bfloat16*>(out));
+    }
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(ctx, Q38_ERR_CUDA, "switch_glu: decode launch failed: %s", cudaGetErrorString(e));
     }
     return Q38_OK;
 }
@@ -1041,6 +1539,45 @@ q38_status qgemv_gate_up_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K,
     return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_gate_up: bits %d not on the fast path", bits);
 }
 
+bool qgemv_moe_supported(int64_t T, int64_t H, int64_t I, int64_t E, int topk, int group, int bits, const void* x,
+                         const void* gw, const void* gs, const void* gb, const void* uw, const void* us,
+                         const void* ub, const void* dw, const void* ds, const void* db) {
+    if (T < 1 || T > MOE_MAX_T || T * topk > MOE_MAX_PAIRS || topk > COMBINE_MAXK || E < 1 || E > MOE_MAX_E ||
+        group != 64)
+        return false;
+    if (bits != 2 && bits != 3 && bits != 4 && bits != 8) return false;
+    if (H % KC || I % KC || H <= 0 || I <= 0) return false;
+    if (E * std::max(H, I) >= (1LL << 31)) return false;
+    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    for (const void* p : {x, gw, gs, uw, us, dw, ds})
+        if (!al(p)) return false;
+    for (const void* p : {gb, ub, db})
+        if (p && !al(p)) return false;
+    return true;
+}
+
+q38_status qgemv_moe_decode(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int64_t I, int64_t E, int topk,
+                            const int32_t* idx, const void* scores, const uint32_t* gw, const void* gs,
+                            const void* gb, const uint32_t* uw, const void* us, const void* ub, const uint32_t* dw,
+                            const void* ds, const void* db, int bits, void* out) {
+    const int t = static_cast<int>(T), h = static_cast<int>(H), i = static_cast<int>(I), e = static_cast<int>(E);
+    auto go = [&](auto bits_c) {
+        constexpr int B = decltype(bits_c)::value;
+        return dispatch_m<B>(t, [&](auto mp, auto tb) {
+            return launch_moe_decode<B, decltype(mp)::value, decltype(tb)::value>(ctx, x, t, h, i, e, topk, idx, scores,
+                                                                                  gw, gs, gb, uw, us, ub, dw, ds, db,
+                                                                                  out);
+        });
+    };
+    switch (bits) {
+        case 2: return go(std::integral_constant<int, 2>());
+        case 3: return go(std::integral_constant<int, 3>());
+        case 4: return go(std::integral_constant<int, 4>());
+        case 8: return go(std::integral_constant<int, 8>());
+    }
+    return fail(ctx, Q38_ERR_UNSUPPORTED, "switch_glu: bits %d not on the decode path", bits);
+}
+
 // ---------------------------------------------------------------------------------
 // Allocation-free variant of the decode product (q38_quantized_matmul_noalloc).
 //
@@ -1108,8 +1645,8 @@ q38_status launch_noalloc(uint8_t* scratch, int device, int num_sms, const void*
     float* part = reinterpret_cast<float*>(scratch + NA_ACC_OFF);
     WeightMaps maps;
     if (!cached_maps<BITS>(w, s, b, K, N, &maps)) return Q38_ERR_CUDA;
-    const cudaError_t e = launch_kernels<BITS, MP, TB>(p, device, num_sms, x, M, K, maps, b != nullptr, N,
-                                                       y, part, status, stream);
+    const cudaError_t e = launch_kernels<BITS, MP, TB, false, false>(p, device, num_sms, x, M, K, maps, b != nullptr,
+                                                                     N, y, part, status, stream);
     if (e != cudaSuccess) {
         cudaGetLastError();
         // the main kernel may have run without its epilogue: put the sums back to zero

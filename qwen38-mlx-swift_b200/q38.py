@@ -91,6 +91,23 @@ _sig("q38_st_copy_block_to_device", [_P, _P, _I, _U64, _U64, _U64, _U64, _U64, _
 _sig("q38_switch_glu", [_P, _P, _I, _I, _I, _I, _i, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _i, _i, _i, _P])
 
 
+class _CommId(C.Structure):
+    _fields_ = [("bytes", C.c_ubyte * 128)]
+
+
+_sig("q38_comm_error", [], C.c_char_p)
+_sig("q38_comm_get_unique_id", [C.POINTER(_CommId)])
+_sig("q38_comm_init_rank", [C.POINTER(_CommId), _i, _i, _i, _i, C.POINTER(_P)])
+_sig("q38_comm_destroy", [_P])
+_sig("q38_comm_abort", [_P])
+_sig("q38_comm_rank", [_P])
+_sig("q38_comm_size", [_P])
+_sig("q38_comm_all_reduce", [_P, _P, _P, _P, _I, _i])
+_sig("q38_tp_mlp", [_P, _P, _P, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _i, _i, _i, _i, _P])
+_sig("q38_ep_switch_glu", [_P, _P, _P, _I, _I, _I, _I, _i, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _i, _i, _i,
+                           _I, _P])
+
+
 class Q38Error(RuntimeError):
     def __init__(self, status: int, message: str):
         super().__init__(f"{_STATUS.get(status, status)}: {message}")
@@ -734,3 +751,86 @@ class SparseMoeBlock:
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         idx, sc = moe_route(x, self.router_weight, self.top_k, self.normalize)
         return self.switch(x, idx, sc)
+
+
+# ------------------------------------------------------------------------ multi-GPU
+
+def comm_unique_id() -> bytes:
+    """A rendezvous id for a new communicator (rank 0 makes it, every rank passes it in)."""
+    uid = _CommId()
+    st = _lib.q38_comm_get_unique_id(C.byref(uid))
+    if st != Q38_OK:
+        raise Q38Error(st, (_lib.q38_comm_error() or b"").decode())
+    return bytes(uid.bytes)
+
+
+class Communicator:
+    """One NCCL rank of libq38 (q38_comm_init_rank): `world` ranks, this one `rank` on
+    `device`.  Init gives up with Q38Error (status 6) after `timeout_ms` if a rank does not
+    join."""
+
+    def __init__(self, uid: bytes, world: int, rank: int, device: int | None = None, timeout_ms: int = 60000):
+        if device is None:
+            device = torch.cuda.current_device()
+        cid = _CommId()
+        C.memmove(cid.bytes, uid, 128)
+        p = _P()
+        st = _lib.q38_comm_init_rank(C.byref(cid), int(world), int(rank), int(device), int(timeout_ms), C.byref(p))
+        if st != Q38_OK:
+            raise Q38Error(st, (_lib.q38_comm_error() or b"").decode())
+        self.handle, self.world, self.rank, self.device = p.value, world, rank, device
+
+    def destroy(self):
+        if self.handle:
+            _lib.q38_comm_destroy(self.handle)
+            self.handle = None
+
+    def abort(self):
+        if self.handle:
+            _lib.q38_comm_abort(self.handle)
+
+    def all_reduce(self, t: torch.Tensor) -> torch.Tensor:
+        """In-place sum over the ranks."""
+        _need(t, "t")
+        ctx = _bind(t)
+        _check(ctx, _lib.q38_comm_all_reduce(ctx, self.handle, _ptr(t), _ptr(t), t.numel(), _DTYPE[t.dtype]))
+        return t
+
+
+def tp_mlp(comm: Communicator, x: torch.Tensor, gate, up, down, group_size: int = 64, bits: int = 4,
+           chunks: int = 4) -> torch.Tensor:
+    """Tensor-parallel gated MLP (q38_tp_mlp): gate/up this rank's output-row shards, down its
+    reduction-dimension shard; y [M, D] = the all-reduced sum on every rank."""
+    _need(x, "x")
+    M, D = x.shape
+    gw, gs, gb = gate
+    uw, us, ub = up
+    dw, ds, db = down
+    F_local = gw.shape[0]
+    y = torch.empty_like(x)
+    ctx = _bind(x)
+    _check(ctx, _lib.q38_tp_mlp(ctx, comm.handle, _ptr(x), M, D, _ptr(_as_u32(gw)), _ptr(gs), _ptr(gb),
+                                _ptr(_as_u32(uw)), _ptr(us), _ptr(ub), _ptr(_as_u32(dw)), _ptr(ds), _ptr(db),
+                                F_local, _DTYPE[x.dtype], group_size, bits, chunks, _ptr(y)))
+    return y
+
+
+def ep_switch_glu(comm: Communicator, x: torch.Tensor, indices: torch.Tensor, scores: torch.Tensor, gate, up, down,
+                  num_experts: int, capacity: int, group_size: int = 64, bits: int = 3) -> torch.Tensor:
+    """Expert-parallel SwitchGLU (q38_ep_switch_glu): gate/up/down are this rank's expert
+    stacks (num_experts / world experts), indices/scores the global routing of this rank's
+    tokens; every rank uses the same `capacity` >= its token count."""
+    _need(x, "x"), _need(indices, "indices"), _need(scores, "scores")
+    T, H = x.shape
+    k = indices.shape[-1]
+    gw, gs, gb = gate
+    uw, us, ub = up
+    dw, ds, db = down
+    I = gw.shape[1]
+    out = torch.empty_like(x)
+    ctx = _bind(x)
+    _check(ctx, _lib.q38_ep_switch_glu(ctx, comm.handle, _ptr(x), T, H, I, num_experts, k, _ptr(indices),
+                                       _ptr(scores), _ptr(_as_u32(gw)), _ptr(gs), _ptr(gb), _ptr(_as_u32(uw)),
+                                       _ptr(us), _ptr(ub), _ptr(_as_u32(dw)), _ptr(ds), _ptr(db), _DTYPE[x.dtype],
+                                       group_size, bits, capacity, _ptr(out)))
+    return out

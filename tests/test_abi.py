@@ -77,3 +77,29 @@ def test_library_has_no_oracle_dependency():
     data = open(LIB, "rb").read()
     assert b"q38o_" not in data
     assert b"libq38_oracle" not in data
+
+
+def test_comm_unique_id_needs_no_device(lib):
+    """Rank 0's rendezvous id comes from NCCL's bootstrap alone (no GPU work)."""
+    class Id(C.Structure):
+        _fields_ = [("bytes", C.c_ubyte * 128)]
+    lib.q38_comm_get_unique_id.argtypes = [C.POINTER(Id)]
+    lib.q38_comm_get_unique_id.restype = C.c_int
+    a, b = Id(), Id()
+    assert lib.q38_comm_get_unique_id(C.byref(a)) == 0
+    assert lib.q38_comm_get_unique_id(C.byref(b)) == 0
+    assert bytes(a.bytes) != bytes(b.bytes)
+
+
+def test_comm_init_rejects_bad_arguments(lib):
+    class Id(C.Structure):
+        _fields_ = [("bytes", C.c_ubyte * 128)]
+    f = lib.q38_comm_init_rank
+    f.argtypes = [C.POINTER(Id), C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_void_p)]
+    f.restype = C.c_int
+    p = C.c_void_p()
+    i = Id()
+    assert f(C.byref(i), 2, 2, 0, 1000, C.byref(p)) == 1   # rank >= world
+    assert f(C.byref(i), 0, 0, 0, 1000, C.byref(p)) == 1   # world < 1
+    assert f(C.byref(i), 2, 0, 0, 0, C.byref(p)) == 1      # no timeout
+    assert not p.value

@@ -284,3 +284,52 @@ def test_sparse_moe_block_flash_next_512_experts(q38, flash_next, T):
     ref = O.switch_glu(x, gi.cpu().numpy(), host_bf16(gs), *host, 64, FN_BITS, weights_bf16=True)
     check_close(host_bf16(out), O.bf16_to_f32(ref).astype(np.float64))
     assert (gi.cpu().numpy() == idx).mean() >= 0.9
+
+
+# ------------------------------------------------------------- decode-shaped SwitchGLU
+# T <= 16 tokens with T * top_k <= 256 run on the decode kernel: the selected experts'
+# gate/up rows for all tokens (only selecting pairs stored), then the down rows with h
+# formed from the gate/up sums.  The weights enter the products exactly (scales applied in
+# fp32 to exact code sums), so the bar is the fp32-weight oracle's.
+
+@pytest.mark.parametrize("bits", [2, 3, 4])
+@pytest.mark.parametrize("T,E,k,H,I", [(1, 64, 10, 2048, 512), (2, 16, 8, 512, 1024), (16, 64, 10, 1024, 512),
+                                       (16, 32, 16, 512, 512), (7, 300, 4, 1536, 512)])
+def test_switch_glu_decode_parity(q38, bits, T, E, k, H, I):
+    dev, host = make_experts(q38, 8700 + bits + T + E, E, I, H, bits)
+    x = O.normal_bf16(8710 + T, (T, H))
+    idx, sc = route_inputs(T, E, k, 8720 + T + E)
+    out = q38.switch_glu(dev_bf16(x), dev_i32(idx), dev_bf16(sc), *dev, 64, bits)
+    torch.cuda.synchronize()
+    q38.check_device()
+    ref = O.switch_glu(x, idx, sc, *host, 64, bits)
+    check_close(host_bf16(out), O.bf16_to_f32(ref).astype(np.float64))
+
+
+def test_switch_glu_decode_empty_slots_and_no_biases(q38):
+    T, E, k, H, I, bits = 5, 24, 6, 1024, 512, 3
+    dev, host = make_experts(q38, 8730, E, I, H, bits)
+    dev = [(c, s, None) for (c, s, b) in dev]
+    host = [(c, s, None) for (c, s, b) in host]
+    x = O.normal_bf16(8731, (T, H))
+    idx, sc = route_inputs(T, E, k, 8732)
+    idx = idx.copy()
+    idx[1, 2] = -1
+    idx[3, :] = -1  # a token without experts gives zeros
+    out = q38.switch_glu(dev_bf16(x), dev_i32(idx), dev_bf16(sc), *dev, 64, bits)
+    torch.cuda.synchronize()
+    q38.check_device()
+    ref = O.switch_glu(x, idx, sc, *host, 64, bits)
+    check_close(host_bf16(out), O.bf16_to_f32(ref).astype(np.float64))
+    assert (host_bf16(out)[3] == 0).all()
+
+
+def test_switch_glu_decode_is_deterministic(q38):
+    T, E, k, H, I, bits = 8, 64, 10, 2048, 512, 3
+    dev, _ = make_experts(q38, 8740, E, I, H, bits)
+    x = dev_bf16(O.normal_bf16(8741, (T, H)))
+    idx, sc = route_inputs(T, E, k, 8742)
+    a = q38.switch_glu(x, dev_i32(idx), dev_bf16(sc), *dev, 64, bits)
+    b = q38.switch_glu(x, dev_i32(idx), dev_bf16(sc), *dev, 64, bits)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)

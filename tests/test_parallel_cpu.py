@@ -210,3 +210,41 @@ def test_shard_helpers_split_whole_groups_and_words():
     assert np.array_equal(np.concatenate([p[0].numpy() for p in rows], axis=0), c.view(np.int32))
     with pytest.raises(ValueError):
         shard_k(ct, st, bt, 0, 3, 4)
+
+
+def absent_peer_worker(rank, world, port, q):
+    """Rank 1 leaves without joining (scenario 'init') or right after joining, before the
+    first collective (scenario 'collective'); rank 0 must get an error within its timeout."""
+    import datetime
+    import time
+    scenario = os.environ["Q38_TEST_SCENARIO"]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    if rank == 1 and scenario == "init":
+        q.put((rank, "left", 0.0))
+        return
+    t0 = time.time()
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+        dist.barrier()  # one completed step: the ranks' connections exist
+        if rank == 1:
+            q.put((rank, "left", 0.0))
+            q.close()
+            q.join_thread()  # the message is out before the process ends
+            os._exit(0)  # leaves between steps: nothing of it is in flight
+        dist.all_reduce(torch.ones(4))
+        q.put((rank, "completed", time.time() - t0))
+    except Exception as e:  # the failure is reported, not hung on
+        q.put((rank, type(e).__name__, time.time() - t0))
+
+
+@pytest.mark.parametrize("scenario", ["init", "collective"])
+def test_absent_peer_is_reported_within_the_timeout(scenario):
+    os.environ["Q38_TEST_SCENARIO"] = scenario
+    try:
+        res = run2(absent_peer_worker)
+    finally:
+        del os.environ["Q38_TEST_SCENARIO"]
+    (r0, what0, secs0), (r1, what1, _) = res
+    assert r0 == 0 and what1 == "left"
+    assert what0 not in ("completed",), res
+    assert secs0 < 60, res
