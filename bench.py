@@ -420,11 +420,20 @@ def build_moe(torch, q38, dev, seed=3030):
     return q38.SparseMoeBlock(wr, sw, MOE["k"]), g
 
 
-def run_moe_ep(torch, q38, dev, stream, world, rank, dist, quick=False):
-    """Expert-parallel MoE layer: experts split contiguously over the ranks, T tokens per
-    rank (weak scaling), all-to-all dispatch and return over NCCL; eager steps (the
-    exchange sizes come back to the host), CUDA events, max over ranks."""
-    import parallel
+def make_comm(q38, dist, rank, world, dev):
+    """libq38 communicator (q38_comm_init_rank): rank 0's id reaches the others through the
+    torch process group (host plumbing only)."""
+    box = [q38.comm_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    return q38.Communicator(box[0], world, rank, dev.index, timeout_ms=120000)
+
+
+def run_moe_ep(torch, q38, dev, stream, world, rank, dist, comm, quick=False):
+    """Expert-parallel MoE layer through the C ABI (q38_moe_route on each rank's tokens, then
+    q38_ep_switch_glu: experts split contiguously over the ranks, fixed-capacity NCCL
+    exchange of every rank's T tokens to every rank, partial sums returned and added at
+    home).  T tokens per rank (weak scaling); the R layer calls of a step are captured in a
+    CUDA graph with their NCCL exchanges and replayed; CUDA events, max over ranks."""
     H, I, E, k, bits = MOE["H"], MOE["I"], MOE["E"], MOE["k"], MOE["bits"]
     epr = E // world
     g = torch.Generator(device=dev).manual_seed(3030 + rank)
@@ -436,58 +445,41 @@ def run_moe_ep(torch, q38, dev, stream, world, rank, dist, quick=False):
         del w
     gw = torch.Generator(device=dev).manual_seed(3131)  # router weight identical on all ranks
     wr = (torch.randn((E, H), generator=gw, device=dev) * 0.02).to(torch.bfloat16)
-    moe = parallel.ExpertParallelMoE(wr, mine, E, k, GROUP, bits)
+
+    def layer(x):
+        idx, sc = q38.moe_route(x, wr, k)
+        return q38.ep_switch_glu(comm, x, idx, sc, *mine, E, x.shape[0], GROUP, bits)
     out = {}
     for T in MOE_T:
         R = 4 if T <= 64 else 2
         reps = (3 if quick else 10) if T <= 64 else (2 if quick else 5)
         xs = [torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16) for _ in range(R)]
         for x in xs:
-            moe(x)
+            layer(x)
+        torch.cuda.synchronize()
+        dist.barrier()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for x in xs:
+                layer(x)
+        graph.replay()
         torch.cuda.synchronize()
         dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(reps):
-            for x in xs:
-                moe(x)
+            graph.replay()
         e1.record(stream)
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / (reps * R)
         t = torch.tensor([us], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         us = float(t.item())
+        del graph  # released before the communicators and the process group
         out[str(T)] = {"tokens_per_s": round(world * T / (us * 1e-6), 1), "us_per_layer": round(us, 2),
                        "tokens_per_rank": T}
-        if T <= 64:
-            # fixed-capacity exchange (no host synchronisation): the R layer calls captured
-            # in one CUDA graph with their NCCL exchanges, replayed
-            fixed = parallel.ExpertParallelMoE(wr, mine, E, k, GROUP, bits, capacity=T)
-            for x in xs:
-                fixed(x)
-            torch.cuda.synchronize()
-            dist.barrier()
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                for x in xs:
-                    fixed(x)
-            graph.replay()
-            torch.cuda.synchronize()
-            dist.barrier()
-            e0.record(stream)
-            for _ in range(reps):
-                graph.replay()
-            e1.record(stream)
-            torch.cuda.synchronize()
-            gus = e0.elapsed_time(e1) * 1e3 / (reps * R)
-            t = torch.tensor([gus], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            gus = float(t.item())
-            del graph  # released before the process group is destroyed
-            out[str(T)]["fixed_capacity_graph"] = {"tokens_per_s": round(world * T / (gus * 1e-6), 1),
-                                                   "us_per_layer": round(gus, 2)}
         del xs
-    del moe, mine
+    del mine
     torch.cuda.synchronize()
     return {"metric": "MoE expert-stack tokens/s (router + SwitchGLU + combine, one layer)", "unit": "tokens/s",
             "per_T": out,
@@ -495,9 +487,8 @@ def run_moe_ep(torch, q38, dev, stream, world, rank, dist, quick=False):
                                    "3-bit group 64, router [512, 2048] bf16",
                        "parallelism": f"expert parallel x{world} ({epr} experts per GPU), T tokens per GPU",
                        "scaling": "weak",
-                       "timing": "eager layer calls (all-to-all sizes are read on the host), CUDA events, "
-                                 "max over ranks; T <= 64 also with the fixed-capacity exchange captured in a "
-                                 "CUDA graph (fixed_capacity_graph)"}}
+                       "timing": "q38_moe_route + q38_ep_switch_glu (fixed capacity = T per rank, NCCL inside "
+                                 "libq38) captured in a CUDA graph, CUDA events, max over ranks"}}
 
 
 def run_moe(torch, q38, dev, stream, world, dist, quick=False):
@@ -578,53 +569,70 @@ def run_moe(torch, q38, dev, stream, world, dist, quick=False):
 
 
 # ------------------------------------------------------------------------- prefill
-def run_prefill_tp(torch, q38, dev, stream, world, rank, dist, quick=False):
-    """Tensor-parallel dense MLP block at 4096 tokens, 4-bit: gate/up column-sharded,
-    down row-sharded, bf16 all-reduce over NCCL; the whole block (x replicated) per step,
-    strong scaling."""
-    import parallel
+def run_prefill_tp(torch, q38, dev, stream, world, rank, dist, comm, quick=False):
+    """Tensor-parallel dense MLP stack at 4096 tokens, 4-bit, through the C ABI
+    (q38_tp_mlp): per layer gate/up split by output rows, down by its reduction dimension,
+    partial outputs summed by a bf16 all-reduce inside libq38 that overlaps the next token
+    chunk's products; 64 layers of random-init weights, every layer reading the same x
+    (strong scaling: the whole stack on every step)."""
     M, D, F = 4096, 5120, 17408
-    g = torch.Generator(device=dev).manual_seed(4040)
-    mats = []
-    for (n, k) in ((F, D), (F, D), (D, F)):
-        w = torch.randn((n, k), generator=g, device=dev) * 0.02
-        c, s, b = q38.quantize(w, GROUP, 4, scales_dtype=torch.bfloat16)
-        mats.append((c.view(torch.int32), s, b))
-        del w
-    mlp = parallel.TensorParallelMLP(*mats, GROUP, 4)
-    del mats
-    x = torch.randn((M, D), generator=g, device=dev).to(torch.bfloat16)
-    for _ in range(2):
-        mlp(x)
+    L = 8 if quick else 64
+    Fl = F // world
+    g = torch.Generator(device=dev).manual_seed(4040 + rank)
+    layers = []
+    for _ in range(L):
+        mats = []
+        for (n, k) in ((Fl, D), (Fl, D), (D, Fl)):  # this rank's shards (random: every rank its own)
+            w = torch.randn((n, k), generator=g, device=dev) * 0.02
+            c, s, b = q38.quantize(w, GROUP, 4, scales_dtype=torch.bfloat16)
+            mats.append((c.view(torch.int32), s, b))
+            del w
+        layers.append(mats)
+    gx = torch.Generator(device=dev).manual_seed(4141)
+    x = torch.randn((M, D), generator=gx, device=dev).to(torch.bfloat16)
+    outs = [torch.empty_like(x) for _ in range(2)]
+
+    def stack():
+        for i, (ga, up, dn) in enumerate(layers):
+            outs[i & 1].copy_(q38.tp_mlp(comm, x, ga, up, dn, GROUP, 4, chunks=4))
+    stack()
     torch.cuda.synchronize()
-    reps = 3 if quick else 10
+    dist.barrier()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        stack()
+    graph.replay()
+    torch.cuda.synchronize()
+    reps = 1 if quick else 3
     dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(reps):
-        mlp(x)
+        graph.replay()
     e1.record(stream)
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / reps
     t = torch.tensor([us], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     us = float(t.item())
-    flops = 3 * 2 * M * F * D
+    del graph
+    flops = L * 3 * 2 * M * F * D
     peak = None
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
-        peak = float(json.load(open(p))["bf16_tflops"])
+        peak = float(json.load(open(p))["bf16_tflops_sustained"])
     tf = flops / (us * 1e-6) / 1e12
-    del mlp, x
+    del layers, x, outs
     torch.cuda.synchronize()
-    return {"metric": "prefill quantized GEMM TFLOP/s (tensor pipe)", "unit": "TFLOP/s", "value": round(tf, 1),
-            "us_per_block": round(us, 1),
-            "frac_of_measured_bf16_peak_per_gpu": round(tf / world / peak, 4) if peak else None,
+    return {"metric": "prefill quantized MLP stack TFLOP/s (tensor pipe)", "unit": "TFLOP/s", "value": round(tf, 1),
+            "us_per_stack": round(us, 1), "us_per_layer": round(us / L, 1), "layers": L,
+            "frac_of_measured_bf16_peak_sustained_per_gpu": round(tf / world / peak, 4) if peak else None,
             "tokens_per_s": round(M / (us * 1e-6), 1),
-            "config": {"workload": "4096 tokens x 4-bit g64 MLP block: gate, up 17408x5120 -> SiLU-gate -> "
-                                   "down 5120x17408, bf16 all-reduce",
+            "config": {"workload": f"{L} layers x 4096 tokens x 4-bit g64 MLP: gate, up 17408x5120 -> SiLU-gate -> "
+                                   "down 5120x17408, bf16 all-reduce; every layer reads the same x",
                        "parallelism": f"tensor parallel x{world}", "scaling": "strong",
-                       "timing": "eager block calls, CUDA events, max over ranks"}}
+                       "timing": "q38_tp_mlp (4 token chunks, all-reduce overlapped, NCCL inside libq38) "
+                                 "stack captured in a CUDA graph, CUDA events, max over ranks"}}
 
 
 def run_prefill(torch, q38, dev, stream, world, dist, quick=False):
@@ -895,8 +903,14 @@ def run_ours(args, rank, world, local_rank):
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)}
 
     if world > 1:
-        moe = None if args.skip_moe else run_moe_ep(torch, q38, dev, stream, world, rank, dist, args.quick)
-        prefill = None if args.skip_prefill else run_prefill_tp(torch, q38, dev, stream, world, rank, dist, args.quick)
+        comm = make_comm(q38, dist, rank, world, dev) if not (args.skip_moe and args.skip_prefill) else None
+        moe = None if args.skip_moe else run_moe_ep(torch, q38, dev, stream, world, rank, dist, comm, args.quick)
+        prefill = None if args.skip_prefill else run_prefill_tp(torch, q38, dev, stream, world, rank, dist, comm,
+                                                                args.quick)
+        if comm is not None:
+            torch.cuda.synchronize()
+            dist.barrier()
+            comm.destroy()
     else:
         moe = None if args.skip_moe else run_moe(torch, q38, dev, stream, world, dist, args.quick)
         prefill = None if args.skip_prefill else run_prefill(torch, q38, dev, stream, world, dist, args.quick)
