@@ -81,6 +81,13 @@ Q38_API void* q38_ctx_get_stream(const q38_ctx* ctx);
 /* Grow the device workspace to at least `bytes` now (synchronises the device). */
 Q38_API q38_status q38_ctx_reserve(q38_ctx* ctx, size_t bytes);
 Q38_API size_t q38_ctx_workspace_bytes(const q38_ctx* ctx);
+/* Reproducible decode products.  A decode-shaped product (M <= 16) splits its reduction
+ * dimension over many CTAs; by default their fp32 partial sums are added in arrival order,
+ * so two runs of the same product may differ in the last bit of a few outputs.  With
+ * `on` != 0 each k-chunk's sums go to a slot of their own and are added in a fixed order:
+ * bitwise reproducible results (MLX's decode is reproducible too) for about one
+ * microsecond more per product.  Off by default. */
+Q38_API q38_status q38_ctx_set_deterministic(q38_ctx* ctx, int on);
 /* Synchronise the stream and return Q38_ERR_DEVICE_TIMEOUT if any kernel recorded a
  * bounded-wait expiry since the last check (the word is then cleared). */
 Q38_API q38_status q38_ctx_check_device(q38_ctx* ctx);

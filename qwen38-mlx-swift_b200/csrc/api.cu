@@ -248,6 +248,12 @@ q38_status q38_ctx_reserve(q38_ctx* ctx, size_t bytes) {
 
 size_t q38_ctx_workspace_bytes(const q38_ctx* ctx) { return ctx ? ctx->workspace_bytes : 0; }
 
+q38_status q38_ctx_set_deterministic(q38_ctx* ctx, int on) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    ctx->deterministic = on ? 1 : 0;
+    return Q38_OK;
+}
+
 q38_status q38_ctx_check_device(q38_ctx* ctx) {
     if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
     q38_status st = set_device(ctx);

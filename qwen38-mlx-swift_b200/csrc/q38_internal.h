@@ -30,6 +30,7 @@ struct q38_ctx {
     void* aux = nullptr;  // activation-sized intermediates (rotated x, MoE buffers)
     size_t aux_bytes = 0;
     uint32_t* d_status = nullptr;  // device status word (timeouts)
+    int deterministic = 0;  // decode products: ordered chunk sums (bitwise reproducible)
     // Pinned host staging of the safetensors reader: two halves used alternately, each
     // guarded by an event of its last host->device copy.
     void* host_stage = nullptr;

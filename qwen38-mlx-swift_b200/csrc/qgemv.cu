@@ -25,9 +25,13 @@
 //    steps whose operands are the scales/biases and hi/lo bf16 splits of the sums.
 //  * Consumers do no address arithmetic in the inner loop: swizzled code offsets are
 //    precomputed per thread and the fragment offsets are constants.
-//  * Every warp adds its subtile partial sums into an fp32 workspace with fire-and-forget
-//    reductions (no fences or counters in the main kernel); a small epilogue kernel
-//    converts the sums to y and zeroes them again, so no per-call clearing is needed.
+//  * Every warp adds its subtile partial sums into an fp32 zero-at-rest region with
+//    fire-and-forget reductions (no fences or counters in the main kernel); a small
+//    epilogue kernel converts the sums to y and zeroes them again, so no per-call clearing
+//    is needed.  The fp32 additions land in arrival order, so repeats may differ in the
+//    last bit; a context set to deterministic mode instead stores each k-chunk's sums in a
+//    slot of its own and the epilogue adds the slots in a fixed order (bitwise
+//    reproducible, about 1 us more per product).
 //  * The main kernel is launched with programmatic dependent launch: its producer
 //    streams the first stages of weights while the previous kernel is still running.
 #include <algorithm>
@@ -1319,19 +1323,36 @@ q38_status slot_workspace(q38_ctx* ctx, const Plan& p, int M, int N, bool two, f
     return Q38_OK;
 }
 
+// The partial sums of a context's product: chunk slots in the workspace when the context
+// asks for reproducible results, else the zero-at-rest region of M x N (x2) floats.
+q38_status partial_sums(q38_ctx* ctx, const Plan& p, int M, int N, bool two, float** out) {
+    if (ctx->deterministic) return slot_workspace(ctx, p, M, N, two, out);
+    uint32_t* unused = nullptr;
+    return ensure_zero_region(ctx, 0, static_cast<size_t>(M) * N * (two ? 2 : 1), &unused, out);
+}
+
+template <int BITS, int MP, int TB, bool PACK = false>
+cudaError_t launch_ctx(q38_ctx* ctx, const Plan& p, const void* x, int M, int K, const WeightMaps& maps,
+                       bool has_bias, int N, void* y, float* part, const WeightMaps* maps_b = nullptr) {
+    if (ctx->deterministic)
+        return launch_kernels<BITS, MP, TB, PACK, true>(p, ctx->device, ctx->num_sms, x, M, K, maps, has_bias, N, y,
+                                                        part, ctx->d_status, ctx->stream, maps_b);
+    return launch_kernels<BITS, MP, TB, PACK, false>(p, ctx->device, ctx->num_sms, x, M, K, maps, has_bias, N, y,
+                                                     part, ctx->d_status, ctx->stream, maps_b);
+}
+
 template <int BITS, int MP, int TB>
 q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, const void* s,
                   const void* b, int N, void* y) {
     Plan p;
     if (!make_plan<BITS>(M, K, N, p)) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: shape too large");
     float* part = nullptr;
-    q38_status st = slot_workspace(ctx, p, M, N, false, &part);
+    q38_status st = partial_sums(ctx, p, M, N, false, &part);
     if (st != Q38_OK) return st;
     WeightMaps maps;
     if (!cached_maps<BITS>(w, s, b, K, N, &maps))
         return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: tensor map encoding failed");
-    const cudaError_t e = launch_kernels<BITS, MP, TB>(p, ctx->device, ctx->num_sms, x, M, K, maps,
-                                                       b != nullptr, N, y, part, ctx->d_status, ctx->stream);
+    const cudaError_t e = launch_ctx<BITS, MP, TB>(ctx, p, x, M, K, maps, b != nullptr, N, y, part);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: launch failed: %s", cudaGetErrorString(e));
@@ -1346,13 +1367,12 @@ q38_status launch_pack(q38_ctx* ctx, const void* x, int M, int K, const uint32_t
     Plan p;
     if (!make_plan<BITS>(M, K, N, p)) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: shape too large");
     float* part = nullptr;
-    q38_status st = slot_workspace(ctx, p, M, N, false, &part);
+    q38_status st = partial_sums(ctx, p, M, N, false, &part);
     if (st != Q38_OK) return st;
     WeightMaps maps;
     if (!cached_maps<BITS, true>(w, s, b, K, N, &maps))
         return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: tensor map encoding failed");
-    const cudaError_t e = launch_kernels<BITS, MP, TB, true>(p, ctx->device, ctx->num_sms, x, M, K, maps,
-                                                             b != nullptr, N, y, part, ctx->d_status, ctx->stream);
+    const cudaError_t e = launch_ctx<BITS, MP, TB, true>(ctx, p, x, M, K, maps, b != nullptr, N, y, part);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: launch failed: %s", cudaGetErrorString(e));
@@ -1367,13 +1387,12 @@ q38_status launch_gate_up(q38_ctx* ctx, const void* x, int M, int K, const uint3
     Plan p;
     if (!make_plan<BITS>(M, K, N, p, true)) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_gate_up: shape too large");
     float* part = nullptr;
-    q38_status st = slot_workspace(ctx, p, M, N, true, &part);
+    q38_status st = partial_sums(ctx, p, M, N, true, &part);
     if (st != Q38_OK) return st;
     WeightMaps mg, mu;
     if (!cached_maps<BITS, PACK>(wg, sg, bg, K, N, &mg) || !cached_maps<BITS, PACK>(wu, su, bu, K, N, &mu))
         return fail(ctx, Q38_ERR_CUDA, "quantized_gate_up: tensor map encoding failed");
-    const cudaError_t e = launch_kernels<BITS, MP, TB, PACK>(p, ctx->device, ctx->num_sms, x, M, K, mg, bg != nullptr,
-                                                             N, h, part, ctx->d_status, ctx->stream, &mu);
+    const cudaError_t e = launch_ctx<BITS, MP, TB, PACK>(ctx, p, x, M, K, mg, bg != nullptr, N, h, part, &mu);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return fail(ctx, Q38_ERR_CUDA, "quantized_gate_up: launch failed: %s", cudaGetErrorString(e));
