@@ -531,6 +531,8 @@ q38_status q38_gather_quantized_matmul(q38_ctx* ctx, const void* x, int64_t Bx, 
     if (!x || !w || !scales || !rhs_indices || !out)
         return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "gather_quantized_matmul: null pointer");
     if ((st = set_device(ctx)) != Q38_OK) return st;
+    if (qgemv_gather_supported(M, K, E, N, P, group_size, bits, x_dtype, scales_dtype, x, w, scales, biases))
+        return qgemv_gather(ctx, x, Bx, K, w, scales, biases, E, N, lhs_indices, rhs_indices, P, bits, out);
     return gather_generic(ctx, x, Bx, M, K, x_dtype, w, scales, biases, scales_dtype, E, N, lhs_indices,
                           rhs_indices, P, group_size, bits, out);
 }

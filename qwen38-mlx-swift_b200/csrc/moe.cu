@@ -527,12 +527,19 @@ __global__ void __launch_bounds__(1024, 1) moe_sort_scan(int* __restrict__ gcnt,
     griddep_launch_dependents();
     __shared__ int tot[1025];
     const int B = E + 1;
+    // per bucket, the exclusive prefix over the blocks' counts; the counts are read eight
+    // at a time (all loads in flight before the dependent sums and stores)
     for (int e = threadIdx.x; e < B; e += 1024) {
         int run = 0;
-        for (int b = 0; b < nblk; ++b) {
-            const int c = gcnt[static_cast<size_t>(b) * B + e];
-            gcnt[static_cast<size_t>(b) * B + e] = run;
-            run += c;
+        for (int b0 = 0; b0 < nblk; b0 += 8) {
+            int c[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) c[i] = b0 + i < nblk ? gcnt[static_cast<size_t>(b0 + i) * B + e] : 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                if (b0 + i < nblk) gcnt[static_cast<size_t>(b0 + i) * B + e] = run;
+                run += c[i];
+            }
         }
         tot[e] = run;
     }
@@ -542,7 +549,14 @@ __global__ void __launch_bounds__(1024, 1) moe_sort_scan(int* __restrict__ gcnt,
     __syncthreads();
     for (int e = threadIdx.x; e < B; e += 1024) {
         const int o = offsets[e];
-        for (int b = 0; b < nblk; ++b) gcnt[static_cast<size_t>(b) * B + e] += o;
+        for (int b0 = 0; b0 < nblk; b0 += 8) {
+            int c[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) c[i] = b0 + i < nblk ? gcnt[static_cast<size_t>(b0 + i) * B + e] : 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (b0 + i < nblk) gcnt[static_cast<size_t>(b0 + i) * B + e] = c[i] + o;
+        }
     }
 }
 
@@ -603,11 +617,23 @@ __global__ void __launch_bounds__(1024, 1) moe_tiles_kernel(const int32_t* __res
         }
     }
     __syncthreads();
-    const int base = warp_tot[warp] + incl - runs;
-    for (int r = 0; r < runs; ++r) {
-        const int p0 = offsets[e] + r * run, np = min(run, n - r * run);
-        for (int b = 0; b < rb_gu; ++b) gu[(base + r) * rb_gu + b] = MoeTile{e, b, p0, np};
-        for (int b = 0; b < rb_d; ++b) dn[(base + r) * rb_d + b] = MoeTile{e, b, p0, np};
+    // each expert's first run and run count, then the tiles written by whole warps (one
+    // expert at a time per warp, its entries spread over the lanes)
+    __shared__ int s_base[1024], s_runs[1024];
+    s_base[e] = warp_tot[warp] + incl - runs;
+    s_runs[e] = runs;
+    __syncthreads();
+    const int per = rb_gu + rb_d;
+    for (int ee = warp; ee < E; ee += 32) {
+        const int nr = s_runs[ee], b0 = s_base[ee], o0 = offsets[ee], ne = offsets[ee + 1] - o0;
+        for (int q = lane; q < nr * per; q += 32) {
+            const int r = q / per, b = q - r * per;
+            const int p0 = o0 + r * run, np = min(run, ne - r * run);
+            if (b < rb_gu)
+                gu[(b0 + r) * rb_gu + b] = MoeTile{ee, b, p0, np};
+            else
+                dn[(b0 + r) * rb_d + (b - rb_gu)] = MoeTile{ee, b - rb_gu, p0, np};
+        }
     }
 }
 

@@ -114,6 +114,15 @@ q38_status qgemv_moe_decode(q38_ctx* ctx, const void* x, int64_t T, int64_t H, i
                             const void* gb, const uint32_t* uw, const void* us, const void* ub, const uint32_t* dw,
                             const void* ds, const void* db, int bits, void* out);
 
+// Gathered product out[p] = x[lhs[p]] . dequant(w[rhs[p]])^T on the decode kernel: one
+// activation row per batch entry (M == 1), up to 256 pairs (in pieces of 16), group 64,
+// bits 2/3/4/8, bf16, K % 512 == 0, N % 64 == 0.
+bool qgemv_gather_supported(int64_t M, int64_t K, int64_t E, int64_t N, int64_t P, int group, int bits, q38_dtype xd,
+                            q38_dtype sd, const void* x, const void* w, const void* s, const void* b);
+q38_status qgemv_gather(q38_ctx* ctx, const void* x, int64_t Bx, int64_t K, const uint32_t* w, const void* s,
+                        const void* b, int64_t E, int64_t N, const int32_t* lhs, const int32_t* rhs, int64_t P,
+                        int bits, void* out);
+
 // Prompt-shaped product on the tensor cores (M >= 17, group 64, K % 128 == 0, bits 2/3/4,
 // bf16).  Uses the scratch workspace for the permuted activations (M*K bf16).
 bool qgemm_tc_supported(int64_t M, int64_t K, int group, int bits, q38_dtype xd, q38_dtype sd,

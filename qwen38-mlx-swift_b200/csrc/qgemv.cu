@@ -269,6 +269,10 @@ struct MainArgs {
     // MoE modes
     const int32_t* idx;  // [T = M, topk] expert of each (token, slot); -1 marks an empty slot
     int topk, E, rpe, tpe, P, plan_off;
+    // MODE_MOE_DOWN used for a gathered product: the activation row of pair p is
+    // lhs[p] (checked against Bx; out of range gives a zero row), else p
+    const int32_t* lhs;
+    int Bx;
 };
 
 // Accumulator columns.  An m16n8k16 product has 8 columns; with MP (1, 2, 4 or 8) token
@@ -530,6 +534,25 @@ __global__ void __launch_bounds__(256) moe_decode_combine(const float* __restric
     for (int s = 0; s < COMBINE_MAXK; ++s)
         if (s < topk && s_ok[s]) acc = __fadd_rn(acc, __fmul_rn(s_sc[s], bf16_bits_to_f32(f32_to_bf16_bits(y[s]))));
     out[static_cast<size_t>(t) * H + r] = __float2bfloat16_rn(acc);
+}
+
+// Gathered product: out[p, n] = bf16(sum of the chunk slots [C][P][N] of pair p, in chunk
+// order), zeros for a pair whose expert index is outside [0, E).
+__global__ void __launch_bounds__(256) gather_decode_out(const float* __restrict__ ws, const int32_t* __restrict__ rhs,
+                                                         int P, int E, int N, int C, __nv_bfloat16* __restrict__ out) {
+    griddep_launch_dependents();
+    griddep_wait();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < P * N; i += gridDim.x * blockDim.x) {
+        const int p = i / N;
+        const int e = rhs[p];
+        float v = 0.0f;
+        if (e >= 0 && e < E) {
+            const float* src = ws + i;
+#pragma unroll 4
+            for (int c = 0; c < C; ++c) v += __ldcg(src + static_cast<size_t>(c) * P * N);
+        }
+        out[i] = __float2bfloat16_rn(v);
+    }
 }
 
 // An f16 value (11 significant bits) as fp32 and as an exact sum of two bf16 values (8 and
@@ -821,7 +844,16 @@ __global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 
                 __syncwarp();
                 for (int q = lane; q < mseg * (KC / 8); q += 32) {
                     const int m = q / (KC / 8), o = q % (KC / 8);
-                    cp_async16(xstage + m * (KC * 2) + o * 16, a.x + static_cast<size_t>(prs[m]) * a.K + c * KC + o * 8);
+                    int row = prs[m];
+                    if (a.lhs) {
+                        row = a.lhs[row];
+                        if (row < 0 || row >= a.Bx) {  // a zero row; reported once per CTA and chunk
+                            *reinterpret_cast<uint4*>(xstage + m * (KC * 2) + o * 16) = make_uint4(0u, 0u, 0u, 0u);
+                            if (o == 0 && blockIdx.x == 0) atomicOr(a.status, Q38_DEV_BAD_INDEX);
+                            continue;
+                        }
+                    }
+                    cp_async16(xstage + m * (KC * 2) + o * 16, a.x + static_cast<size_t>(row) * a.K + c * KC + o * 8);
                 }
                 cp_async_commit();
                 cp_async_wait<0>();
@@ -1471,6 +1503,47 @@ q38_status launch_moe_decode(q38_ctx* ctx, const void* x, int T, int H, int I, i
     return Q38_OK;
 }
 
+// Gathered product of up to 16 pairs (one activation row each): the down-projection mode
+// of the decode kernel over the pairs' distinct experts, then the chunk sums.
+template <int BITS, int MP, int TB>
+q38_status launch_gather(q38_ctx* ctx, const void* x, int Bx, int K, const uint32_t* w, const void* s, const void* b,
+                         int E, int N, const int32_t* lhs, const int32_t* rhs, int P, void* out) {
+    Plan pd;
+    if (!make_plan<BITS>(P, K, std::min(E, P) * N, pd, false, true))
+        return fail(ctx, Q38_ERR_UNSUPPORTED, "gather_quantized_matmul: decode plan does not fit");
+    q38_status st = ensure_workspace(ctx, static_cast<size_t>(pd.C) * P * N * sizeof(float));
+    if (st != Q38_OK) return st;
+    float* slots = static_cast<float*>(ctx->workspace);
+    WeightMaps md;
+    if (!cached_maps<BITS>(w, s, b, K, E * N, &md))
+        return fail(ctx, Q38_ERR_CUDA, "gather_quantized_matmul: tensor map encoding failed");
+    MainArgs d = base_args(pd, x, P, K, 0, slots, ctx->d_status, b != nullptr);
+    d.idx = rhs;
+    d.topk = 1;
+    d.E = E;
+    d.P = P;
+    d.rpe = N;
+    d.tpe = N / 64;
+    d.ld = N;
+    d.lhs = lhs;
+    d.Bx = Bx;
+    cudaError_t e = launch_main<BITS, MP, TB, false, MODE_MOE_DOWN>(pd, ctx->device, ctx->num_sms, md, md, d,
+                                                                    static_cast<long long>(pd.tiles) * pd.C * 4,
+                                                                    ctx->stream);
+    if (e == cudaSuccess) {
+        cudaLaunchAttribute attr[1];
+        cudaLaunchConfig_t cfg = pdl_config(dim3(epilogue_blocks(static_cast<long long>(P) * N, ctx->num_sms)),
+                                            dim3(256), 0, ctx->stream, attr);
+        e = cudaLaunchKernelEx(&cfg, gather_decode_out, static_cast<const float*>(slots), rhs, P, E, N, pd.C,
+                               static_cast<__nv_bfloat16*>(out));
+    }
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(ctx, Q38_ERR_CUDA, "gather_quantized_matmul: decode launch failed: %s", cudaGetErrorString(e));
+    }
+    return Q38_OK;
+}
+
 // Token layout by M: MP token columns per group slot, TB blocks of 8 tokens.
 template <int BITS, typename L>
 q38_status dispatch_m(int M, L&& run) {
@@ -1595,6 +1668,46 @@ q38_status qgemv_moe_decode(q38_ctx* ctx, const void* x, int64_t T, int64_t H, i
         case 8: return go(std::integral_constant<int, 8>());
     }
     return fail(ctx, Q38_ERR_UNSUPPORTED, "switch_glu: bits %d not on the decode path", bits);
+}
+
+bool qgemv_gather_supported(int64_t M, int64_t K, int64_t E, int64_t N, int64_t P, int group, int bits, q38_dtype xd,
+                            q38_dtype sd, const void* x, const void* w, const void* s, const void* b) {
+    if (M != 1 || P < 1 || P > 256 || E < 1 || E > MOE_MAX_E || group != 64 || K % KC || K <= 0 || N % 64 || N <= 0)
+        return false;
+    if (bits != 2 && bits != 3 && bits != 4 && bits != 8) return false;
+    if (xd != Q38_BF16 || sd != Q38_BF16 || E * N >= (1LL << 31)) return false;
+    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    return al(x) && al(w) && al(s) && (!b || al(b));
+}
+
+// Pairs in pieces of 16 (each piece reads the weights of its own distinct experts).
+q38_status qgemv_gather(q38_ctx* ctx, const void* x, int64_t Bx, int64_t K, const uint32_t* w, const void* s,
+                        const void* b, int64_t E, int64_t N, const int32_t* lhs, const int32_t* rhs, int64_t P,
+                        int bits, void* out) {
+    for (int64_t p0 = 0; p0 < P; p0 += MOE_MAX_T) {
+        const int pc = static_cast<int>(std::min<int64_t>(MOE_MAX_T, P - p0));
+        const int32_t* lh = lhs ? lhs + p0 : nullptr;
+        const void* xp = lhs ? x : static_cast<const uint8_t*>(x) + static_cast<size_t>(p0) * K * 2;
+        const int bx = lhs ? static_cast<int>(Bx) : pc;
+        void* op = static_cast<uint8_t*>(out) + static_cast<size_t>(p0) * N * 2;
+        auto go = [&](auto bits_c) {
+            constexpr int B = decltype(bits_c)::value;
+            return dispatch_m<B>(pc, [&](auto mp, auto tb) {
+                return launch_gather<B, decltype(mp)::value, decltype(tb)::value>(
+                    ctx, xp, bx, static_cast<int>(K), w, s, b, static_cast<int>(E), static_cast<int>(N), lh, rhs + p0,
+                    pc, op);
+            });
+        };
+        q38_status st;
+        switch (bits) {
+            case 2: st = go(std::integral_constant<int, 2>()); break;
+            case 3: st = go(std::integral_constant<int, 3>()); break;
+            case 4: st = go(std::integral_constant<int, 4>()); break;
+            default: st = go(std::integral_constant<int, 8>()); break;
+        }
+        if (st != Q38_OK) return st;
+    }
+    return Q38_OK;
 }
 
 // ---------------------------------------------------------------------------------

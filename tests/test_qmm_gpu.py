@@ -313,3 +313,46 @@ def test_deterministic_mode_matches_oracle(q38, bits):
             check_close(host_bf16(y), O.qmm(x, c, s, b, 64, bits, f32=True))
     finally:
         q38.set_deterministic(False)
+
+
+@pytest.mark.parametrize("bits", [2, 3, 4, 8])
+@pytest.mark.parametrize("P,with_lhs", [(10, True), (80, True), (7, False), (160, True)])
+def test_gather_qmm_decode_path(q38, bits, P, with_lhs):
+    """gatherQuantizedMM at QuantizedSwitchLinear's decode shapes (one activation row per
+    token, up to 256 (token, slot) pairs): the decode kernel over the pairs' distinct
+    experts, checked pair by pair against the oracle."""
+    E, N, K = 64, 512, 2048
+    c, s, b = make_weight(1900 + bits, E * N, K, bits)
+    c, s, b = c.reshape(E, N, -1), s.reshape(E, N, -1), b.reshape(E, N, -1)
+    rng = np.random.default_rng(1901 + P)
+    T = max(1, P // 10) if with_lhs else P
+    x = O.normal_bf16(1950 + P, (T, 1, K))
+    lhs = (np.arange(P) // 10 % T).astype(np.int32) if with_lhs else None
+    rhs = rng.integers(0, E, size=P).astype(np.int32)
+    out = q38.gather_qmm(dev_bf16(x), dev_u32(c), dev_bf16(s), dev_bf16(b),
+                         None if lhs is None else torch.from_numpy(lhs).cuda(), torch.from_numpy(rhs).cuda(),
+                         True, 64, bits)
+    torch.cuda.synchronize()
+    q38.check_device()
+    ref = O.gather_qmm(x, c, s, b, lhs if lhs is not None else np.arange(P, dtype=np.int32), rhs, 64, bits)
+    # both sides round their fp32 sums to bf16: allow one bf16 step of the reference on top
+    # of the bar
+    y = O.bf16_to_f32(host_bf16(out)).astype(np.float64)
+    r = O.bf16_to_f32(ref).astype(np.float64)
+    for p in range(P):
+        rms = np.sqrt((r[p] ** 2).mean())
+        step = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(r[p]), 2.0 ** -126))) - 7)
+        assert (np.abs(y[p] - r[p]) - step).max() <= TOL * rms, p
+
+
+def test_gather_qmm_decode_path_bad_index(q38):
+    E, N, K = 4, 64, 512
+    c, s, b = make_weight(1960, E * N, K, 4)
+    x = O.normal_bf16(1961, (2, 1, K))
+    rhs = torch.tensor([1, 9], dtype=torch.int32, device="cuda")
+    out = q38.gather_qmm(dev_bf16(x), dev_u32(c.reshape(E, N, -1)), dev_bf16(s.reshape(E, N, -1)),
+                         dev_bf16(b.reshape(E, N, -1)), None, rhs, True, 64, 4)
+    with pytest.raises(q38.Q38ArgumentError):
+        q38.check_device()
+    assert (out[1].float() == 0).all()
+    q38.check_device()
