@@ -209,8 +209,11 @@ Q38_API q38_status q38_moe_sort(q38_ctx* ctx, const int32_t* indices, int64_t pa
  * scales/biases bf16 [E, I, H/64]; down codes [E, H, I*bits/32], scales/biases
  * [E, H, I/64]; out bf16 [T, H].  Biases are given for all three projections or none.
  * An index of -1 marks an empty slot: it contributes nothing and is not an error.
- * Implemented for group 64, bits 2/3/4, H % 512 == 0, I % 512 == 0, E <= 1024.  Uses the
- * context's activation buffer (about T*top_k*(2H + I)*2 bytes). */
+ * Implemented for group 64, bits 2/3/4/8, H % 512 == 0, I % 512 == 0, E <= 1024.  Up to 16
+ * tokens (with T*top_k <= 256) stream the selected experts' weights on the decode kernel;
+ * more tokens run the grouped tensor-core products over expert-sorted pairs (8-bit: the
+ * decode path, 16 tokens at a time).  Uses the context's activation buffer (about
+ * T*top_k*(2H + I)*2 bytes) and workspace. */
 Q38_API q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int64_t I, int64_t E,
                                   int top_k, const int32_t* indices, const void* scores,
                                   const uint32_t* gate_w, const void* gate_scales, const void* gate_biases,
