@@ -426,18 +426,49 @@ __global__ void __launch_bounds__(256) moe_gather_kernel(const __nv_bfloat16* __
                                                          __nv_bfloat16* __restrict__ xs) {
     griddep_wait();
     griddep_launch_dependents();
-    const int G = H / 64;
+    // one 16-byte chunk (8 activations) per thread, consecutive threads on consecutive
+    // chunks of a row; a 64-group spans 8 lanes, and each of its 16-element quarters two
+    // neighbouring lanes, which swap their chunks to form the quarter's permuted words
+    const int CH = H / 8;
     const int64_t item = blockIdx.x * 256LL + threadIdx.x;
-    // pairs past *valid (empty or invalid slots, sorted after every expert) feed no tile
-    if (item >= static_cast<int64_t>(min(pairs, *valid)) * G) return;
-    const int j = static_cast<int>(item / G), g = static_cast<int>(item % G);
-    const int t = perm[j] / top_k;
-    permute_group<BITS>(x + static_cast<size_t>(t) * H + g * 64, xs + static_cast<size_t>(j) * H + g * 64);
+    const int64_t n = static_cast<int64_t>(min(pairs, *valid)) * CH;  // pairs past *valid feed no tile
+    const bool live = item < n;
+    const int j = live ? static_cast<int>(item / CH) : 0, ch = live ? static_cast<int>(item % CH) : 0;
+    uint4 u = make_uint4(0u, 0u, 0u, 0u);
+    if (live) u = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(perm[j] / top_k) * H + ch * 8);
+    uint4 v;
+    v.x = __shfl_xor_sync(0xffffffffu, u.x, 1);
+    v.y = __shfl_xor_sync(0xffffffffu, u.y, 1);
+    v.z = __shfl_xor_sync(0xffffffffu, u.z, 1);
+    v.w = __shfl_xor_sync(0xffffffffu, u.w, 1);
+    if (!live) return;
+    const bool odd = ch & 1;
+    const uint4 lo = odd ? v : u, hi = odd ? u : v;  // elements 0-7 and 8-15 of the quarter
+    const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+    float e[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        e[2 * i] = bf16_bits_to_f32(w[i] & 0xFFFFu);
+        e[2 * i + 1] = bf16_bits_to_f32(w[i] >> 16);
+    }
+    uint32_t o[4];
+    if (odd) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+            o[t] = pack_bf16x2(e[pair_code<BITS>(4 + t, 0)] * pair_mult<BITS>(4 + t, 0),
+                               e[pair_code<BITS>(4 + t, 1)] * pair_mult<BITS>(4 + t, 1));
+    } else {
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+            o[t] = pack_bf16x2(e[pair_code<BITS>(t, 0)] * pair_mult<BITS>(t, 0),
+                               e[pair_code<BITS>(t, 1)] * pair_mult<BITS>(t, 1));
+    }
+    *reinterpret_cast<uint4*>(xs + static_cast<size_t>(j) * H + ch * 8) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 q38_status moe_gather_launch(q38_ctx* ctx, const void* x, int H, const int32_t* perm, int pairs, int top_k,
                              const int32_t* valid, void* xs, int bits) {
-    const long long items = static_cast<long long>(pairs) * (H / 64);
+    const long long items = static_cast<long long>(pairs) * (H / 8);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;

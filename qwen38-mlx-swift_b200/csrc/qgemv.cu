@@ -623,7 +623,7 @@ __device__ __forceinline__ int seg_key(const MainArgs& a, int chunk, int tile) {
 // subgroup uses the scale of its 128-group, read from a stage box that holds the 8 groups of
 // an aligned pair of chunks.
 template <int BITS, int MP, int TB, bool PACK, int MODE>
-__global__ void __launch_bounds__(THREADS, WG == 1 ? (TB == 1 ? 3 : 2) : (TB == 1 ? 2 : 1)) qgemv_main(const __grid_constant__ WeightMaps maps,
+__global__ void __launch_bounds__(THREADS, WG == 1 && TB == 1 ? 3 : 2) qgemv_main(const __grid_constant__ WeightMaps maps,
                                                                       const __grid_constant__ WeightMaps maps_b,
                                                                       const MainArgs a) {
     using F = Fmt<BITS>;
@@ -1148,8 +1148,10 @@ bool make_plan(int M, int K, int N, Plan& p, bool two_weights = false, bool moe 
     // fragment slots (with their headers) + staging copy of x (+ the MoE plan)
     const int xbytes = 2 * (M * F::XF_PER_M + HDR_BYTES) + M * KC * 2 + (moe ? PLAN_BYTES + 16 : 0);
     // 76 KiB per CTA in all (ring, header, zeros, fragments, alignment slack, 1 KiB of
-    // static sums) lets three CTAs (12 consumer warps) share an SM; 113 KiB two
-    const int budget = (WG == 1 ? (M > 8 ? 113 : 76) : (M > 8 ? 226 : 113)) * 1024 - 1024 - RING_OFF - 1024 - xbytes;
+    // static sums) lets three CTAs (12 consumer warps) share an SM; 113 KiB two (also for
+    // 9-16 tokens, where two CTAs per SM with registers capped at 102 beat one CTA with
+    // more: 16 x 4096 -> 11008 4-bit 21.5 -> 18.5 us)
+    const int budget = (WG == 1 ? (M > 8 ? 113 : 76) : 113) * 1024 - 1024 - RING_OFF - 1024 - xbytes;
     int stages = budget / p.stage_bytes;
     if (stages > 8) stages = 8;  // (the lcm(stages, WG) + stages + 4 barriers then fit the first 1 KiB)
     if (stages < 2) stages = 2;
