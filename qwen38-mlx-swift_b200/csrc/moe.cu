@@ -289,6 +289,93 @@ __device__ __forceinline__ void topk_token(const __nv_bfloat16* __restrict__ log
     }
 }
 
+// The same selection for one token by the four warps of a block (the one-launch router's
+// last block with a single token): the exponentials, divisions and keys are spread over the
+// warps (warp w takes the experts lane + 32 j with j = w mod 4), the per-lane sums keep
+// topk_token's order (lane l adds its experts l, l + 32, ... in turn), so the results are
+// bit-identical to topk_token's.
+template <int NJ>
+__device__ __forceinline__ void topk_token_block4(const __nv_bfloat16* __restrict__ logits, int E, int top_k,
+                                                  int normalize, int32_t* __restrict__ indices,
+                                                  __nv_bfloat16* __restrict__ scores,
+                                                  __nv_bfloat16* __restrict__ probs, int warp, int lane) {
+    __shared__ float s_ev[32 * NJ];
+    __shared__ uint32_t s_key[32 * NJ];
+    __shared__ float s_red[4];
+    const uint16_t* l = reinterpret_cast<const uint16_t*>(logits);
+    float v[NJ / 4];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int jj = 0; jj < NJ / 4; ++jj) {
+        const int e = lane + 32 * (4 * jj + warp);
+        v[jj] = e < E ? bf16_bits_to_f32(__ldcg(l + e)) : -INFINITY;
+        mx = fmaxf(mx, v[jj]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) s_red[warp] = mx;
+    __syncthreads();
+    mx = fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3]));
+#pragma unroll
+    for (int jj = 0; jj < NJ / 4; ++jj) {
+        const int e = lane + 32 * (4 * jj + warp);
+        if (e < E) s_ev[e] = router_exp(__fsub_rn(v[jj], mx));
+    }
+    __syncthreads();
+    if (warp == 0) {
+        float part = 0.0f;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j)
+            if (lane + 32 * j < E) part = __fadd_rn(part, s_ev[lane + 32 * j]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, o));
+        if (lane == 0) s_red[0] = part;
+    }
+    __syncthreads();
+    const float part = s_red[0];
+#pragma unroll
+    for (int jj = 0; jj < NJ / 4; ++jj) {
+        const int e = lane + 32 * (4 * jj + warp);
+        uint32_t key = 0u;
+        if (e < E) {
+            const uint16_t pb = f32_to_bf16_bits(__fdiv_rn(s_ev[e], part));
+            if (probs) reinterpret_cast<uint16_t*>(probs)[e] = pb;
+            key = (static_cast<uint32_t>(pb) << 16) | (0xFFFFu - static_cast<uint32_t>(e));
+        }
+        s_key[lane + 32 * (4 * jj + warp)] = key;
+    }
+    __syncthreads();
+    if (warp != 0) return;
+    uint32_t key[NJ];
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) key[j] = s_key[lane + 32 * j];
+    float ssum = 0.0f, my_v = 0.0f;
+    int my_i = 0;
+    for (int r = 0; r < top_k; ++r) {
+        uint32_t m = 0;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) m = max(m, key[j]);
+        m = __reduce_max_sync(0xffffffffu, m);
+        const int bi = static_cast<int>(0xFFFFu - (m & 0xFFFFu));
+        const float bv = bf16_bits_to_f32(m >> 16);
+        if ((bi & 31) == lane) {
+#pragma unroll
+            for (int j = 0; j < NJ; ++j)
+                if (j == (bi >> 5)) key[j] = 0u;
+        }
+        if (lane == r) {
+            my_v = bv;
+            my_i = bi;
+        }
+        ssum = __fadd_rn(ssum, bv);
+    }
+    if (lane < top_k) {
+        const float denom = bf16_bits_to_f32(f32_to_bf16_bits(ssum));
+        indices[lane] = my_i;
+        scores[lane] = __float2bfloat16_rn(normalize ? __fdiv_rn(my_v, denom) : my_v);
+    }
+}
+
 // softmax + top-k, one warp per token.
 template <int NJ>
 __global__ void __launch_bounds__(256) router_topk(const __nv_bfloat16* __restrict__ logits, int T, int E,
@@ -372,7 +459,11 @@ __global__ void __launch_bounds__(128) router_decode(const __nv_bfloat16* __rest
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    for (int t = warp; t < T; t += 4) topk_token<NJ, true>(logits, t, E, top_k, normalize, indices, scores, probs, lane);
+    if (T == 1)
+        topk_token_block4<NJ>(logits, E, top_k, normalize, indices, scores, probs, warp, lane);
+    else
+        for (int t = warp; t < T; t += 4)
+            topk_token<NJ, true>(logits, t, E, top_k, normalize, indices, scores, probs, lane);
     if (threadIdx.x == 0) atomicExch(counter, 0u);
 }
 

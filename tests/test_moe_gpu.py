@@ -347,3 +347,16 @@ def test_switch_glu_8bit_experts(q38, T):
     q38.check_device()
     ref = O.switch_glu(x, idx, sc, *host, 64, bits)
     check_close(host_bf16(out), O.bf16_to_f32(ref).astype(np.float64))
+
+
+@pytest.mark.parametrize("E,k", [(512, 10), (1000, 32), (100, 4), (256, 8)])
+def test_router_single_token_matches_multi_token_path(q38, E, k):
+    """One token's selection (spread over a block's four warps) equals, bit for bit, the
+    selection of the same token routed together with another (one warp per token)."""
+    H = 2048
+    x = O.normal_bf16(8900 + E, (1, H))
+    wr = O.normal_bf16(8901 + E, (E, H), 0.02)
+    i1, s1, p1 = q38.moe_route(dev_bf16(x), dev_bf16(wr), k, True, want_probs=True)
+    x2 = np.concatenate([x, O.normal_bf16(8902, (1, H))])
+    i2, s2, p2 = q38.moe_route(dev_bf16(x2), dev_bf16(wr), k, True, want_probs=True)
+    assert torch.equal(i1[0], i2[0]) and torch.equal(s1[0], s2[0]) and torch.equal(p1[0], p2[0])
