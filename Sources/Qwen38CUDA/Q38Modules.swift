@@ -174,3 +174,68 @@ public final class Q38QuantizedEmbedding {
         try table(ctx, x, into: y)
     }
 }
+
+// ------------------------------------------------------------------ several GPUs
+
+/// One NCCL rank of libq38 (NCCL is loaded by the library).  Rank 0 creates the id with
+/// `Q38Communicator.uniqueID()` and hands its bytes to the other ranks over any channel.
+public final class Q38Communicator {
+    public let handle: OpaquePointer
+    public let rank: Int32, world: Int32
+    public static func uniqueID() throws -> q38_comm_id {
+        var id = q38_comm_id()
+        let st = q38_comm_get_unique_id(&id)
+        guard st == Q38_OK else { throw Q38Failure(status: st, message: String(cString: q38_comm_error())) }
+        return id
+    }
+    public init(id: q38_comm_id, world: Int32, rank: Int32, device: Int32, timeoutMs: Int32 = 60_000) throws {
+        var id = id
+        var h: OpaquePointer?
+        let st = q38_comm_init_rank(&id, world, rank, device, timeoutMs, &h)
+        guard st == Q38_OK, let h else { throw Q38Failure(status: st, message: String(cString: q38_comm_error())) }
+        handle = h
+        self.rank = rank
+        self.world = world
+    }
+    deinit { q38_comm_destroy(handle) }
+    /// After a peer failed: abort the collectives in flight.
+    public func abort() { q38_comm_abort(handle) }
+}
+
+/// The dense MLP with gate/up split by output rows and down by its reduction dimension;
+/// `callAsFunction` leaves the all-reduced y on every rank.
+public final class Q38TensorParallelMLP {
+    public let gate: Q38QuantizedLinear, up: Q38QuantizedLinear, down: Q38QuantizedLinear
+    public let chunks: Int32
+    public init(gate: Q38QuantizedLinear, up: Q38QuantizedLinear, down: Q38QuantizedLinear, chunks: Int = 4) {
+        self.gate = gate; self.up = up; self.down = down; self.chunks = Int32(chunks)
+    }
+    public func callAsFunction(_ ctx: Q38Context, _ comm: Q38Communicator, _ x: Q38Tensor, into y: Q38Tensor) throws {
+        try ctx.check(q38_tp_mlp(ctx.handle, comm.handle, x.pointer, x.rows, x.lastDim,
+                                 gate.weight.u32, gate.scales.pointer, gate.biases?.pointer,
+                                 up.weight.u32, up.scales.pointer, up.biases?.pointer,
+                                 down.weight.u32, down.scales.pointer, down.biases?.pointer,
+                                 gate.outputDimensions, Q38_BF16, gate.groupSize, gate.bits, chunks, y.pointer))
+    }
+}
+
+/// SwitchGLU with this rank's share of the experts; every rank uses the same capacity.
+public final class Q38ExpertParallelSwitchGLU {
+    public let gate: Q38QuantizedSwitchLinear, up: Q38QuantizedSwitchLinear, down: Q38QuantizedSwitchLinear
+    public let numExperts: Int64, capacity: Int64
+    public init(gate: Q38QuantizedSwitchLinear, up: Q38QuantizedSwitchLinear, down: Q38QuantizedSwitchLinear,
+                numExperts: Int, capacity: Int) {
+        self.gate = gate; self.up = up; self.down = down
+        self.numExperts = Int64(numExperts); self.capacity = Int64(capacity)
+    }
+    public func callAsFunction(_ ctx: Q38Context, _ comm: Q38Communicator, _ x: Q38Tensor, indices: Q38Tensor,
+                               scores: Q38Tensor, into out: Q38Tensor) throws {
+        let I = Int64(gate.weight.shape[1]), k = Int32(indices.lastDim)
+        try ctx.check(q38_ep_switch_glu(ctx.handle, comm.handle, x.pointer, x.rows, x.lastDim, I, numExperts, k,
+                                        UnsafePointer(indices.i32), scores.pointer,
+                                        gate.weight.u32, gate.scales.pointer, gate.biases?.pointer,
+                                        up.weight.u32, up.scales.pointer, up.biases?.pointer,
+                                        down.weight.u32, down.scales.pointer, down.biases?.pointer,
+                                        Q38_BF16, gate.groupSize, gate.bits, capacity, out.pointer))
+    }
+}
