@@ -90,6 +90,8 @@ _sig("q38_st_metadata_entry", [_P, _I, C.POINTER(C.c_char_p), C.POINTER(C.c_char
 _sig("q38_st_copy_to_device", [_P, _P, _I, _P, _U64])
 _sig("q38_st_copy_block_to_device", [_P, _P, _I, _U64, _U64, _U64, _U64, _U64, _P, _U64])
 _sig("q38_switch_glu", [_P, _P, _I, _I, _I, _I, _i, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _i, _i, _i, _P])
+_sig("q38_sparse_moe", [_P, _P, _I, _I, _I, _I, _i, _i, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _i, _i, _i, _P, _P,
+                        _P])
 
 
 class _CommId(C.Structure):
@@ -757,8 +759,27 @@ class SparseMoeBlock:
         self.router_weight, self.switch, self.top_k, self.normalize = router_weight, switch, top_k, normalize
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        idx, sc = moe_route(x, self.router_weight, self.top_k, self.normalize)
-        return self.switch(x, idx, sc)
+        return sparse_moe(x, self.router_weight, self.switch, self.top_k, self.normalize)[0]
+
+
+def sparse_moe(x: torch.Tensor, router_weight: torch.Tensor, switch: "SwitchGLU", top_k: int,
+               normalize: bool = True):
+    """Router + SwitchGLU in one call (q38_sparse_moe): -> (out, indices, scores)."""
+    _need(x, "x"), _need(router_weight, "router_weight")
+    T, H = x.shape
+    E = router_weight.shape[0]
+    g, u, d = switch.gate, switch.up, switch.down
+    I = g.weight.shape[1]
+    idx = torch.empty((T, top_k), dtype=torch.int32, device=x.device)
+    sc = torch.empty((T, top_k), dtype=torch.bfloat16, device=x.device)
+    out = torch.empty_like(x)
+    ctx = _bind(x)
+    _check(ctx, _lib.q38_sparse_moe(ctx, _ptr(x), T, H, I, E, top_k, int(normalize), _ptr(router_weight),
+                                    _ptr(_as_u32(g.weight)), _ptr(g.scales), _ptr(g.biases),
+                                    _ptr(_as_u32(u.weight)), _ptr(u.scales), _ptr(u.biases),
+                                    _ptr(_as_u32(d.weight)), _ptr(d.scales), _ptr(d.biases), _DTYPE[x.dtype],
+                                    g.group_size, g.bits, _ptr(idx), _ptr(sc), _ptr(out)))
+    return out, idx, sc
 
 
 # ------------------------------------------------------------------------ multi-GPU

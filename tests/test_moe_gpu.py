@@ -360,3 +360,18 @@ def test_router_single_token_matches_multi_token_path(q38, E, k):
     x2 = np.concatenate([x, O.normal_bf16(8902, (1, H))])
     i2, s2, p2 = q38.moe_route(dev_bf16(x2), dev_bf16(wr), k, True, want_probs=True)
     assert torch.equal(i1[0], i2[0]) and torch.equal(s1[0], s2[0]) and torch.equal(p1[0], p2[0])
+
+
+@pytest.mark.parametrize("T", [1, 3, 8])
+def test_sparse_moe_equals_route_then_switch_glu(q38, flash_next, T):
+    """q38_sparse_moe (router with the chosen experts warmed in L2, then SwitchGLU) equals
+    the two calls made separately, bit for bit."""
+    dev, host, wr = flash_next
+    x = dev_bf16(O.normal_bf16(8640 + T, (T, FN_H)))
+    sw = q38.SwitchGLU(*[q38.QuantizedSwitchLinear(c, s, b, 64, FN_BITS) for (c, s, b) in dev])
+    out, idx, sc = q38.sparse_moe(x, dev_bf16(wr), sw, FN_K)
+    gi, gs = q38.moe_route(x, dev_bf16(wr), FN_K)
+    ref = q38.switch_glu(x, gi, gs, *dev, 64, FN_BITS)
+    torch.cuda.synchronize()
+    q38.check_device()
+    assert torch.equal(idx, gi) and torch.equal(sc, gs) and torch.equal(out, ref)
