@@ -224,10 +224,8 @@ Q38_API q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_
 /* The routed-expert layer in one call: q38_moe_route (x, router weight wr [E, H]) then
  * q38_switch_glu, the pair Qwen4ExpSparseMoE.callAsFunction runs
  * (Sources/Qwen38Core/FlashNext/Qwen4ExpSparseMoE.swift:275-294).  indices [T, top_k]
- * (int32) and scores [T, top_k] (bf16) receive the routing.  For up to 4 tokens on the decode
- * path, the router starts the chosen experts' gate, up and down weights streaming into L2
- * as soon as it has chosen them, ahead of the products that read them.  Results equal the
- * two calls made separately, bit for bit. */
+ * (int32) and scores [T, top_k] (bf16) receive the routing.  Results equal the two calls
+ * made separately, bit for bit. */
 Q38_API q38_status q38_sparse_moe(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int64_t I, int64_t E,
                                   int top_k, int normalize, const void* wr, const uint32_t* gate_w,
                                   const void* gate_scales, const void* gate_biases, const uint32_t* up_w,

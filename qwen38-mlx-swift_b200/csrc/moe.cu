@@ -390,18 +390,6 @@ __global__ void __launch_bounds__(256) router_topk(const __nv_bfloat16* __restri
     topk_token<NJ, false>(logits, t, E, top_k, normalize, indices, scores, probs, lane);
 }
 
-// Expert weights to warm in L2 once the router has chosen: per tensor (gate/up/down codes,
-// scales, biases) its base and the bytes of one expert (tensors [E, rows, ...]).
-struct MoePrefetch {
-    const uint8_t* base[9];
-    unsigned long long expert_bytes[9];
-    int n;  // tensors (0: no prefetch)
-};
-
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
 // Router for a few tokens (decode) in one launch: every block computes the logits of 4
 // experts (one warp each, all NT >= T tokens from shared memory, eight 16-byte loads in
 // flight per lane), stores them as bf16, and counts itself done; the last block to finish
@@ -412,8 +400,7 @@ __global__ void __launch_bounds__(128) router_decode(const __nv_bfloat16* __rest
                                                      const __nv_bfloat16* __restrict__ wr, int E, int top_k,
                                                      int normalize, __nv_bfloat16* __restrict__ logits,
                                                      int32_t* __restrict__ indices, __nv_bfloat16* __restrict__ scores,
-                                                     __nv_bfloat16* __restrict__ probs, unsigned int* counter,
-                                                     const __grid_constant__ MoePrefetch pf) {
+                                                     __nv_bfloat16* __restrict__ probs, unsigned int* counter) {
     griddep_wait();  // inputs come from the previous kernel on the stream
     griddep_launch_dependents();
     extern __shared__ uint4 xs4[];
@@ -478,24 +465,6 @@ __global__ void __launch_bounds__(128) router_decode(const __nv_bfloat16* __rest
         for (int t = warp; t < T; t += 4)
             topk_token<NJ, true>(logits, t, E, top_k, normalize, indices, scores, probs, lane);
     if (threadIdx.x == 0) atomicExch(counter, 0u);
-    if (pf.n > 0) {
-        // the chosen experts' weights start streaming into L2 now, while the next kernels
-        // are launched and read the routing (32 KB per prefetch, spread over the threads)
-        __syncthreads();
-        constexpr uint32_t CH = 32768;
-        const int sel = T * top_k;
-        for (int i = 0; i < pf.n; ++i) {
-            const unsigned long long eb = pf.expert_bytes[i];
-            const int chunks = static_cast<int>((eb + CH - 1) / CH);
-            for (int q = threadIdx.x; q < sel * chunks; q += blockDim.x) {
-                const int e = __ldcg(indices + q / chunks);
-                if (e < 0 || e >= E) continue;
-                const unsigned long long off = static_cast<unsigned long long>(q % chunks) * CH;
-                const uint32_t n = static_cast<uint32_t>(min(static_cast<unsigned long long>(CH), eb - off));
-                prefetch_l2(pf.base[i] + static_cast<unsigned long long>(e) * eb + off, n);
-            }
-        }
-    }
 }
 
 // --------------------------------------------------------------------------- sort
@@ -1049,8 +1018,7 @@ q38_status logits_launch(q38_ctx* ctx, const void* x, int64_t T, int64_t H, cons
 
 // The one-launch router for up to 16 tokens (x staged whole in shared memory).
 q38_status route_decode_launch(q38_ctx* ctx, const void* x, int64_t T, int64_t H, const void* wr, int64_t E,
-                               int top_k, int normalize, void* logits, int32_t* indices, void* scores, void* probs,
-                               const MoePrefetch& pf = MoePrefetch{}) {
+                               int top_k, int normalize, void* logits, int32_t* indices, void* scores, void* probs) {
     uint32_t* cnt = nullptr;
     float* unused = nullptr;
     q38_status st = ensure_zero_region(ctx, 1, 0, &cnt, &unused);
@@ -1074,7 +1042,7 @@ q38_status route_decode_launch(q38_ctx* ctx, const void* x, int64_t T, int64_t H
                           static_cast<int>(T), static_cast<int>(H), static_cast<const __nv_bfloat16*>(wr),
                           static_cast<int>(E), top_k, normalize, static_cast<__nv_bfloat16*>(logits), indices,
                           static_cast<__nv_bfloat16*>(scores), static_cast<__nv_bfloat16*>(probs),
-                          reinterpret_cast<unsigned int*>(cnt), pf);
+                          reinterpret_cast<unsigned int*>(cnt));
     };
     auto by_e = [&](auto nt_c) -> q38_status {
         constexpr int NT = decltype(nt_c)::value;
@@ -1342,7 +1310,7 @@ q38_status q38_sparse_moe(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
     if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
     if (T == 0) return Q38_OK;
     if (!indices || !scores) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "sparse_moe: indices and scores are required");
-    const bool decode = T <= 4 && H > 0 && static_cast<size_t>(16) * H * 2 <= 96 * 1024 && E >= 1 && E <= 1024 &&
+    const bool decode = T <= 16 && H > 0 && static_cast<size_t>(16) * H * 2 <= 96 * 1024 && E >= 1 && E <= 1024 &&
                         top_k >= 1 && top_k <= 32 && top_k <= E && dtype == Q38_BF16 && x && wr && aligned16(x) &&
                         aligned16(wr) &&
                         qgemv_moe_supported(T, H, I, E, top_k, group_size, bits, x, gate_w, gate_s, gate_b, up_w,
@@ -1356,23 +1324,8 @@ q38_status q38_sparse_moe(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
     q38_status st = set_dev(ctx);
     if (st != Q38_OK) return st;
     if ((st = ensure_workspace(ctx, static_cast<size_t>(T) * E * 2)) != Q38_OK) return st;
-    // the router warms the chosen experts' gate, up and down weights in L2 as soon as it has
-    // chosen them (a few tokens: at most 4 * top_k experts)
-    MoePrefetch pf{};
-    const unsigned long long gc = static_cast<unsigned long long>(I) * H * bits / 8,
-                             gs = static_cast<unsigned long long>(I) * (H / group_size) * 2,
-                             dc = static_cast<unsigned long long>(H) * I * bits / 8,
-                             ds = static_cast<unsigned long long>(H) * (I / group_size) * 2;
-    const void* ptrs[9] = {gate_w, gate_s, gate_b, up_w, up_s, up_b, down_w, down_s, down_b};
-    const unsigned long long sizes[9] = {gc, gs, gs, gc, gs, gs, dc, ds, ds};
-    for (int i = 0; i < 9; ++i) {
-        if (!ptrs[i]) continue;
-        pf.base[pf.n] = static_cast<const uint8_t*>(ptrs[i]);
-        pf.expert_bytes[pf.n] = sizes[i];
-        ++pf.n;
-    }
-    if ((st = route_decode_launch(ctx, x, T, H, wr, E, top_k, normalize, ctx->workspace, indices, scores, nullptr,
-                                  pf)) != Q38_OK)
+    if ((st = route_decode_launch(ctx, x, T, H, wr, E, top_k, normalize, ctx->workspace, indices, scores, nullptr)) !=
+        Q38_OK)
         return st;
     return qgemv_moe_decode(ctx, x, T, H, I, E, top_k, indices, scores, gate_w, gate_s, gate_b, up_w, up_s, up_b,
                             down_w, down_s, down_b, bits, out);

@@ -364,8 +364,8 @@ def test_router_single_token_matches_multi_token_path(q38, E, k):
 
 @pytest.mark.parametrize("T", [1, 3, 8])
 def test_sparse_moe_equals_route_then_switch_glu(q38, flash_next, T):
-    """q38_sparse_moe (router with the chosen experts warmed in L2, then SwitchGLU) equals
-    the two calls made separately, bit for bit."""
+    """q38_sparse_moe (router, then SwitchGLU, in one call) equals the two calls made
+    separately, bit for bit."""
     dev, host, wr = flash_next
     x = dev_bf16(O.normal_bf16(8640 + T, (T, FN_H)))
     sw = q38.SwitchGLU(*[q38.QuantizedSwitchLinear(c, s, b, 64, FN_BITS) for (c, s, b) in dev])
