@@ -711,7 +711,6 @@ __global__ void __launch_bounds__(THREADS, WG == 1 && TB == 1 ? 3 : 2) qgemv_mai
         ex = exw;
         slot_tab = slw;
         tiles = (MODE == MODE_MOE_GU ? 2 : 1) * nd * a.tpe;
-        }
     }
 
     // Subunit range of this CTA in (chunk, tile, subtile) order: a CTA covers one or two
