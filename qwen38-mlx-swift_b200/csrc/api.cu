@@ -383,6 +383,16 @@ q38_status q38_hadamard_quantized_gate_up(q38_ctx* ctx, const void* x, int64_t M
                                   s_up, b_up, scales_dtype, N, group_size, bits, Q38_MODE_AFFINE, h);
     if (st != Q38_OK || M == 0) return st;
     if ((st = set_device(ctx)) != Q38_OK) return st;
+    // decode-shaped: one pass over both weights with x rotated inside the kernel
+    if (block >= 2 && block <= 1024 && (block & (block - 1)) == 0 && K % block == 0) {
+        if (qgemv_fast_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w_gate, s_gate, b_gate, h) &&
+            qgemv_fast_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w_up, s_up, b_up, h))
+            return qgemv_gate_up_fast(ctx, x, M, K, w_gate, s_gate, b_gate, w_up, s_up, b_up, N, bits, h, signs, block);
+        if (qgemv_pack_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w_gate, s_gate, b_gate) &&
+            qgemv_pack_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w_up, s_up, b_up) &&
+            (reinterpret_cast<uintptr_t>(h) & 15u) == 0)
+            return qgemv_gate_up_pack(ctx, x, M, K, w_gate, s_gate, b_gate, w_up, s_up, b_up, N, h, signs, block);
+    }
     // the activation buffer holds the rotated x (rounded to bf16, as the reference rounds it
     // before each product), followed by room for the up product of the general path
     const size_t xbytes = align_up(static_cast<size_t>(M) * K * 2, 256);
@@ -499,6 +509,14 @@ q38_status q38_hadamard_quantized_matmul(q38_ctx* ctx, const void* x, int64_t M,
     if (!x || !w || !scales || !y) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "hadamard_quantized_matmul: null pointer");
     q38_status st = set_device(ctx);
     if (st != Q38_OK) return st;
+    // Decode-shaped products rotate x inside the product kernel (its activation warp stages
+    // x anyway); bit-identical to the rotation kernel followed by the product.
+    if (block >= 2 && block <= 1024 && (block & (block - 1)) == 0 && K % block == 0) {
+        if (qgemv_fast_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w, scales, biases, y))
+            return qgemv_fast(ctx, x, M, K, w, scales, biases, N, bits, y, signs, block);
+        if (qgemv_pack_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w, scales, biases))
+            return qgemv_pack(ctx, x, M, K, w, scales, biases, N, y, signs, block);
+    }
     // The rotated activations (rounded to x_dtype, as the reference does before the
     // product) live in the context's activation buffer.
     void* xr = nullptr;

@@ -89,19 +89,23 @@ q38_status embedding_launch(q38_ctx* ctx, const int32_t* ids, int64_t n, const u
 // bf16 x, K % 1024 == 0, M <= 16.
 bool qgemv_pack_supported(int64_t M, int64_t K, int group, int bits, q38_dtype xd, q38_dtype sd,
                           const void* x, const void* w, const void* s, const void* b);
+// With rot_block > 0 (a power of two <= 1024 dividing K) the kernel first rotates x as
+// hadamardRotate does (signs fp32 [K] or null), in the activation warp: bit-identical to
+// q38_hadamard_rotate followed by the product.
 q38_status qgemv_pack(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w, const void* s,
-                      const void* b, int64_t N, void* y);
+                      const void* b, int64_t N, void* y, const float* signs = nullptr, int rot_block = 0);
 q38_status qgemv_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w,
-                      const void* s, const void* b, int64_t N, int bits, void* y);
+                      const void* s, const void* b, int64_t N, int bits, void* y, const float* signs = nullptr,
+                      int rot_block = 0);
 // h = bf16(silu(x.Wg^T) * (x.Wu^T)) in one decode pass (same conditions as qgemv_fast for
 // both weights, which must both have biases or neither).
 // Gate/up in one pass over the Bonsai 2 pack layout (both weights qgemv_pack_supported).
 q38_status qgemv_gate_up_pack(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* wg,
                               const void* sg, const void* bg, const uint32_t* wu, const void* su, const void* bu,
-                              int64_t N, void* h);
+                              int64_t N, void* h, const float* signs = nullptr, int rot_block = 0);
 q38_status qgemv_gate_up_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* wg,
                               const void* sg, const void* bg, const uint32_t* wu, const void* su, const void* bu,
-                              int64_t N, int bits, void* h);
+                              int64_t N, int bits, void* h, const float* signs = nullptr, int rot_block = 0);
 
 // Decode-shaped SwitchGLU (T <= 16 tokens, T * top_k <= 256, group 64, bits 2/3/4/8, bf16,
 // H and I multiples of 512): the selected experts' gate/up and down products on the decode

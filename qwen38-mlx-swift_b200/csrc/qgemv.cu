@@ -273,7 +273,69 @@ struct MainArgs {
     // lhs[p] (checked against Bx; out of range gives a zero row), else p
     const int32_t* lhs;
     int Bx;
+    // Plain modes: x rotated in the activation warp before its fragments are built
+    // (Qwen38HadamardQuantizedLinear): signs (fp32 [K] or null), block (0: none), 1/sqrt(block)
+    const float* signs;
+    int rot;
+    float rot_scale;
 };
+
+// The rotation of an activation product: hadamardRotate's arguments.
+struct Rot {
+    const float* signs;
+    int block;  // power of two <= 1024 that divides K; 0 for none
+};
+
+// Rotation of one staged window of W = max(512, block) activations of a token (EPL = W / 32
+// elements per lane, lane l holding [l * EPL, l * EPL + EPL)): signs first, then the
+// butterfly stages h = 1, 2, 4, ... < block (lower element a + b, upper a - b: the pairs and
+// order of the rotation kernel, so the results are the same bit for bit), the 1/sqrt(block)
+// scale, and the rounding to bf16; the 512 activations of chunk `part` of the window are
+// written to `dst`.
+template <int EPL>
+__device__ __forceinline__ void rotate_window(const uint8_t* src, uint8_t* dst, const float* signs, int block,
+                                              float scale, int part, int lane) {
+    float v[EPL];
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(src) + lane * (EPL / 2);
+#pragma unroll
+    for (int i = 0; i < EPL / 2; ++i) {
+        const uint32_t u = w[i];
+        v[2 * i] = bf16_bits_to_f32(u & 0xFFFFu);
+        v[2 * i + 1] = bf16_bits_to_f32(u >> 16);
+    }
+    if (signs) {
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) v[i] = v[i] * signs[lane * EPL + i];
+    }
+#pragma unroll
+    for (int h = 1; h < EPL; h <<= 1) {
+        if (h >= block) break;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i)
+            if ((i & h) == 0) {
+                const float a = v[i], b = v[i + h];
+                v[i] = a + b;
+                v[i + h] = a - b;
+            }
+    }
+    for (int lh = 1; lh < 32 && lh * EPL < block; lh <<= 1) {
+        const bool upper = (lane & lh) != 0;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) {
+            const float q = __shfl_xor_sync(0xffffffffu, v[i], lh);
+            v[i] = upper ? (q - v[i]) : (v[i] + q);
+        }
+    }
+    __syncwarp();
+    // lanes whose elements fall into the chunk write them (EPL * 32 = W, the chunk 512)
+    const int first = lane * EPL - part * 512;
+    if (first >= 0 && first < 512) {
+        uint32_t* o = reinterpret_cast<uint32_t*>(dst) + first / 2;
+#pragma unroll
+        for (int i = 0; i < EPL / 2; ++i) o[i] = pack_bf16x2(v[2 * i] * scale, v[2 * i + 1] * scale);
+    }
+    __syncwarp();
+}
 
 // Accumulator columns.  An m16n8k16 product has 8 columns; with MP (1, 2, 4 or 8) token
 // columns per group, one product serves 8/MP groups at once: column n = slot * MP + token,
@@ -859,10 +921,13 @@ __global__ void __launch_bounds__(THREADS, WG == 1 && TB == 1 ? 3 : 2) qgemv_mai
                 cp_async_wait<0>();
                 __syncwarp();
             } else {
-                // all of the chunk's copies in flight at once
-                for (int p = lane; p < a.M * (KC / 8); p += 32) {
-                    const int m = p / (KC / 8), q = p % (KC / 8);
-                    cp_async16(xstage + m * (KC * 2) + q * 16, a.x + static_cast<size_t>(m) * a.K + c * KC + q * 8);
+                // all of the chunk's copies in flight at once; with a rotation of blocks wider
+                // than a chunk, the whole window of W = block activations of each token
+                const int W = a.rot > KC ? a.rot : KC;
+                const int win0 = (c * KC / W) * W;
+                for (int p = lane; p < a.M * (W / 8); p += 32) {
+                    const int m = p / (W / 8), q = p % (W / 8);
+                    cp_async16(xstage + m * (W * 2) + q * 16, a.x + static_cast<size_t>(m) * a.K + win0 + q * 8);
                 }
                 cp_async_commit();
                 const bool ok = ci < 2 || mbar_wait(&xempty[ci & 1], ((ci >> 1) & 1) ^ 1, a.status);
@@ -870,6 +935,20 @@ __global__ void __launch_bounds__(THREADS, WG == 1 && TB == 1 ? 3 : 2) qgemv_mai
                 __syncwarp();
                 if (!ok) return;
                 if (lane == 0) *reinterpret_cast<int*>(hdr + HDR_MSEG) = mseg;
+                if (a.rot) {
+                    // token by token, in place: token m's rotated chunk lands at m * 1 KB,
+                    // inside the window of a token at or before m (already read)
+                    const int part = (c * KC - win0) / KC;
+                    const float* sg = a.signs ? a.signs + win0 : nullptr;
+                    for (int m = 0; m < mseg; ++m) {
+                        if (W == KC)
+                            rotate_window<16>(xstage + m * (W * 2), xstage + m * (KC * 2), sg, a.rot, a.rot_scale, part,
+                                              lane);
+                        else
+                            rotate_window<32>(xstage + m * (W * 2), xstage + m * (KC * 2), sg, a.rot, a.rot_scale, part,
+                                              lane);
+                    }
+                }
             }
             build_fragments<BITS>(xstage, mseg, slotp, hdr, s_xs, s_xp, lane);
             if (lane == 0) mbar_arrive(&xfull[ci & 1]);
@@ -1139,14 +1218,15 @@ struct Plan {
 };
 
 template <int BITS>
-bool make_plan(int M, int K, int N, Plan& p, bool two_weights = false, bool moe = false) {
+bool make_plan(int M, int K, int N, Plan& p, bool two_weights = false, bool moe = false, int rot = 0) {
     using F = Fmt<BITS>;
     p.C = K / KC;
     p.tiles = (N + 63) / 64 * (two_weights ? 2 : 1);
     if (static_cast<long long>(p.tiles) * p.C * 4 >= (1LL << 31)) return false;
     p.stage_bytes = NCW * F::SUB_BYTES + 2048;  // a multiple of 1 KiB
     // fragment slots (with their headers) + staging copy of x (+ the MoE plan)
-    const int xbytes = 2 * (M * F::XF_PER_M + HDR_BYTES) + M * KC * 2 + (moe ? PLAN_BYTES + 16 : 0);
+    const int W = rot > KC ? rot : KC;  // staged activations per token (a rotation window)
+    const int xbytes = 2 * (M * F::XF_PER_M + HDR_BYTES) + M * W * 2 + (moe ? PLAN_BYTES + 16 : 0);
     // 76 KiB per CTA in all (ring, header, zeros, fragments, alignment slack, 1 KiB of
     // static sums) lets three CTAs (12 consumer warps) share an SM; 113 KiB two (also for
     // 9-16 tokens, where two CTAs per SM with registers capped at 102 beat one CTA with
@@ -1165,7 +1245,7 @@ bool make_plan(int M, int K, int N, Plan& p, bool two_weights = false, bool moe 
     // the plan sits after the staging copy of x, 16-byte aligned (offsets from the
     // 1024-aligned base)
     p.plan_off = static_cast<int>(align_up(static_cast<size_t>(RING_OFF) + static_cast<size_t>(stages) * p.stage_bytes +
-                                               2 * (M * F::XF_PER_M + HDR_BYTES) + M * KC * 2,
+                                               2 * (M * F::XF_PER_M + HDR_BYTES) + M * W * 2,
                                            16));
     return smem <= MAX_DYN_SMEM;
 }
@@ -1318,9 +1398,12 @@ int epilogue_blocks(long long total, int num_sms) {
 template <int BITS, int MP, int TB, bool PACK = false, bool SLOTS = true>
 cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x, int M, int K,
                            const WeightMaps& maps, bool has_bias, int N, void* y, float* part, uint32_t* status,
-                           cudaStream_t stream, const WeightMaps* maps_b = nullptr) {
+                           cudaStream_t stream, const WeightMaps* maps_b = nullptr, Rot rot = Rot{nullptr, 0}) {
     constexpr int MODE = SLOTS ? MODE_SLOTS : MODE_ATOMIC;
     MainArgs args = base_args(p, x, M, K, N, part, status, has_bias);
+    args.signs = rot.signs;
+    args.rot = rot.block;
+    args.rot_scale = rot.block ? 1.0f / sqrtf(static_cast<float>(rot.block)) : 1.0f;
     args.y = static_cast<__nv_bfloat16*>(y);
     args.tiles_a = maps_b ? p.tiles / 2 : p.tiles;
     args.ld = maps_b ? 2 * N : N;
@@ -1367,26 +1450,28 @@ q38_status partial_sums(q38_ctx* ctx, const Plan& p, int M, int N, bool two, flo
 
 template <int BITS, int MP, int TB, bool PACK = false>
 cudaError_t launch_ctx(q38_ctx* ctx, const Plan& p, const void* x, int M, int K, const WeightMaps& maps,
-                       bool has_bias, int N, void* y, float* part, const WeightMaps* maps_b = nullptr) {
+                       bool has_bias, int N, void* y, float* part, const WeightMaps* maps_b = nullptr,
+                       Rot rot = Rot{nullptr, 0}) {
     if (ctx->deterministic)
         return launch_kernels<BITS, MP, TB, PACK, true>(p, ctx->device, ctx->num_sms, x, M, K, maps, has_bias, N, y,
-                                                        part, ctx->d_status, ctx->stream, maps_b);
+                                                        part, ctx->d_status, ctx->stream, maps_b, rot);
     return launch_kernels<BITS, MP, TB, PACK, false>(p, ctx->device, ctx->num_sms, x, M, K, maps, has_bias, N, y,
-                                                     part, ctx->d_status, ctx->stream, maps_b);
+                                                     part, ctx->d_status, ctx->stream, maps_b, rot);
 }
 
 template <int BITS, int MP, int TB>
 q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, const void* s,
-                  const void* b, int N, void* y) {
+                  const void* b, int N, void* y, Rot rot) {
     Plan p;
-    if (!make_plan<BITS>(M, K, N, p)) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: shape too large");
+    if (!make_plan<BITS>(M, K, N, p, false, false, rot.block))
+        return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: shape too large");
     float* part = nullptr;
     q38_status st = partial_sums(ctx, p, M, N, false, &part);
     if (st != Q38_OK) return st;
     WeightMaps maps;
     if (!cached_maps<BITS>(w, s, b, K, N, &maps))
         return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: tensor map encoding failed");
-    const cudaError_t e = launch_ctx<BITS, MP, TB>(ctx, p, x, M, K, maps, b != nullptr, N, y, part);
+    const cudaError_t e = launch_ctx<BITS, MP, TB>(ctx, p, x, M, K, maps, b != nullptr, N, y, part, nullptr, rot);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: launch failed: %s", cudaGetErrorString(e));
@@ -1397,16 +1482,17 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
 // The same product over f16 scales with group 128 (PACK).
 template <int BITS, int MP, int TB>
 q38_status launch_pack(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, const void* s,
-                       const void* b, int N, void* y) {
+                       const void* b, int N, void* y, Rot rot) {
     Plan p;
-    if (!make_plan<BITS>(M, K, N, p)) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: shape too large");
+    if (!make_plan<BITS>(M, K, N, p, false, false, rot.block))
+        return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: shape too large");
     float* part = nullptr;
     q38_status st = partial_sums(ctx, p, M, N, false, &part);
     if (st != Q38_OK) return st;
     WeightMaps maps;
     if (!cached_maps<BITS, true>(w, s, b, K, N, &maps))
         return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: tensor map encoding failed");
-    const cudaError_t e = launch_ctx<BITS, MP, TB, true>(ctx, p, x, M, K, maps, b != nullptr, N, y, part);
+    const cudaError_t e = launch_ctx<BITS, MP, TB, true>(ctx, p, x, M, K, maps, b != nullptr, N, y, part, nullptr, rot);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return fail(ctx, Q38_ERR_CUDA, "quantized_matmul: launch failed: %s", cudaGetErrorString(e));
@@ -1417,16 +1503,18 @@ q38_status launch_pack(q38_ctx* ctx, const void* x, int M, int K, const uint32_t
 // Gate and up projections of an MLP in one pass: h = bf16(silu(x.Wg^T) * (x.Wu^T)).
 template <int BITS, int MP, int TB, bool PACK = false>
 q38_status launch_gate_up(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* wg, const void* sg,
-                          const void* bg, const uint32_t* wu, const void* su, const void* bu, int N, void* h) {
+                          const void* bg, const uint32_t* wu, const void* su, const void* bu, int N, void* h,
+                          Rot rot) {
     Plan p;
-    if (!make_plan<BITS>(M, K, N, p, true)) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_gate_up: shape too large");
+    if (!make_plan<BITS>(M, K, N, p, true, false, rot.block))
+        return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_gate_up: shape too large");
     float* part = nullptr;
     q38_status st = partial_sums(ctx, p, M, N, true, &part);
     if (st != Q38_OK) return st;
     WeightMaps mg, mu;
     if (!cached_maps<BITS, PACK>(wg, sg, bg, K, N, &mg) || !cached_maps<BITS, PACK>(wu, su, bu, K, N, &mu))
         return fail(ctx, Q38_ERR_CUDA, "quantized_gate_up: tensor map encoding failed");
-    const cudaError_t e = launch_ctx<BITS, MP, TB, PACK>(ctx, p, x, M, K, mg, bg != nullptr, N, h, part, &mu);
+    const cudaError_t e = launch_ctx<BITS, MP, TB, PACK>(ctx, p, x, M, K, mg, bg != nullptr, N, h, part, &mu, rot);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return fail(ctx, Q38_ERR_CUDA, "quantized_gate_up: launch failed: %s", cudaGetErrorString(e));
@@ -1579,20 +1667,22 @@ bool qgemv_pack_supported(int64_t M, int64_t K, int group, int bits, q38_dtype x
 }
 
 q38_status qgemv_pack(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w, const void* s,
-                      const void* b, int64_t N, void* y) {
+                      const void* b, int64_t N, void* y, const float* signs, int rot_block) {
     const int m = static_cast<int>(M), k = static_cast<int>(K), n = static_cast<int>(N);
     return dispatch_m<2>(m, [&](auto mp, auto tb) {
-        return launch_pack<2, decltype(mp)::value, decltype(tb)::value>(ctx, x, m, k, w, s, b, n, y);
+        return launch_pack<2, decltype(mp)::value, decltype(tb)::value>(ctx, x, m, k, w, s, b, n, y,
+                                                                        Rot{signs, rot_block});
     });
 }
 
 q38_status qgemv_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w,
-                      const void* s, const void* b, int64_t N, int bits, void* y) {
+                      const void* s, const void* b, int64_t N, int bits, void* y, const float* signs, int rot_block) {
     const int m = static_cast<int>(M), k = static_cast<int>(K), n = static_cast<int>(N);
     auto go = [&](auto bits_c) {
         constexpr int B = decltype(bits_c)::value;
         return dispatch_m<B>(m, [&](auto mp, auto tb) {
-            return launch<B, decltype(mp)::value, decltype(tb)::value>(ctx, x, m, k, w, s, b, n, y);
+            return launch<B, decltype(mp)::value, decltype(tb)::value>(ctx, x, m, k, w, s, b, n, y,
+                                                                       Rot{signs, rot_block});
         });
     };
     switch (bits) {
@@ -1606,22 +1696,23 @@ q38_status qgemv_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const u
 
 q38_status qgemv_gate_up_pack(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* wg,
                               const void* sg, const void* bg, const uint32_t* wu, const void* su, const void* bu,
-                              int64_t N, void* h) {
+                              int64_t N, void* h, const float* signs, int rot_block) {
     const int m = static_cast<int>(M), k = static_cast<int>(K), n = static_cast<int>(N);
     return dispatch_m<2>(m, [&](auto mp, auto tb) {
         return launch_gate_up<2, decltype(mp)::value, decltype(tb)::value, true>(ctx, x, m, k, wg, sg, bg, wu, su, bu,
-                                                                               n, h);
+                                                                               n, h, Rot{signs, rot_block});
     });
 }
 
 q38_status qgemv_gate_up_fast(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* wg,
                               const void* sg, const void* bg, const uint32_t* wu, const void* su, const void* bu,
-                              int64_t N, int bits, void* h) {
+                              int64_t N, int bits, void* h, const float* signs, int rot_block) {
     const int m = static_cast<int>(M), k = static_cast<int>(K), n = static_cast<int>(N);
     auto go = [&](auto bits_c) {
         constexpr int B = decltype(bits_c)::value;
         return dispatch_m<B>(m, [&](auto mp, auto tb) {
-            return launch_gate_up<B, decltype(mp)::value, decltype(tb)::value>(ctx, x, m, k, wg, sg, bg, wu, su, bu, n, h);
+            return launch_gate_up<B, decltype(mp)::value, decltype(tb)::value>(ctx, x, m, k, wg, sg, bg, wu, su, bu, n, h,
+                                                                               Rot{signs, rot_block});
         });
     };
     switch (bits) {

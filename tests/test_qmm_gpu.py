@@ -356,3 +356,29 @@ def test_gather_qmm_decode_path_bad_index(q38):
         q38.check_device()
     assert (out[1].float() == 0).all()
     q38.check_device()
+
+
+@pytest.mark.parametrize("block", [16, 256, 512, 1024])
+@pytest.mark.parametrize("with_signs", [True, False])
+def test_rotation_inside_decode_kernel_is_bit_identical(q38, block, with_signs):
+    """Decode-shaped rotated products rotate x in the product kernel: the result equals the
+    rotation kernel followed by the product, bit for bit (deterministic mode, so the two
+    products add their chunk sums in the same order)."""
+    N, K = 1024, 4096
+    c, s, b = make_weight(2100 + block, N, K, 4)
+    signs = torch.from_numpy(np.where((np.arange(K) * 5) % 7 < 3, -1.0, 1.0).astype(np.float32)).cuda() \
+        if with_signs else None
+    W = [dev_u32(c), dev_bf16(s), dev_bf16(b)]
+    q38.set_deterministic(True)
+    try:
+        for M in (1, 3, 8, 16):
+            x = dev_bf16(O.normal_bf16(2150 + M, (M, K)))
+            lin = q38.HadamardQuantizedLinear(q38.QuantizedLinear(*W, None, 64, 4), signs, block)
+            fused = lin(x)
+            sep = q38.quantized_matmul(q38.hadamard_rotate(x, signs, block), *W, True, 64, 4)
+            torch.cuda.synchronize()
+            assert torch.equal(fused, sep), (M, block)
+            xr = q38.hadamard_rotate(x, signs, block)
+            check_close(host_bf16(fused), O.qmm(host_bf16(xr), c, s, b, 64, 4, f32=True))
+    finally:
+        q38.set_deterministic(False)
