@@ -384,7 +384,7 @@ q38_status q38_hadamard_quantized_gate_up(q38_ctx* ctx, const void* x, int64_t M
     if (st != Q38_OK || M == 0) return st;
     if ((st = set_device(ctx)) != Q38_OK) return st;
     // decode-shaped: one pass over both weights with x rotated inside the kernel
-    if (block >= 2 && block <= 1024 && (block & (block - 1)) == 0 && K % block == 0) {
+    if (M == 1 && block >= 2 && block <= 512 && (block & (block - 1)) == 0 && K % block == 0) {
         if (qgemv_fast_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w_gate, s_gate, b_gate, h) &&
             qgemv_fast_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w_up, s_up, b_up, h))
             return qgemv_gate_up_fast(ctx, x, M, K, w_gate, s_gate, b_gate, w_up, s_up, b_up, N, bits, h, signs, block);
@@ -511,7 +511,9 @@ q38_status q38_hadamard_quantized_matmul(q38_ctx* ctx, const void* x, int64_t M,
     if (st != Q38_OK) return st;
     // Decode-shaped products rotate x inside the product kernel (its activation warp stages
     // x anyway); bit-identical to the rotation kernel followed by the product.
-    if (block >= 2 && block <= 1024 && (block & (block - 1)) == 0 && K % block == 0) {
+    // (one token, blocks of at most 512: wider blocks or more tokens make the activation warp
+    // the bottleneck, and those run the rotation kernel first)
+    if (M == 1 && block >= 2 && block <= 512 && (block & (block - 1)) == 0 && K % block == 0) {
         if (qgemv_fast_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w, scales, biases, y))
             return qgemv_fast(ctx, x, M, K, w, scales, biases, N, bits, y, signs, block);
         if (qgemv_pack_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w, scales, biases))

@@ -89,8 +89,8 @@ q38_status embedding_launch(q38_ctx* ctx, const int32_t* ids, int64_t n, const u
 // bf16 x, K % 1024 == 0, M <= 16.
 bool qgemv_pack_supported(int64_t M, int64_t K, int group, int bits, q38_dtype xd, q38_dtype sd,
                           const void* x, const void* w, const void* s, const void* b);
-// With rot_block > 0 (a power of two <= 1024 dividing K) the kernel first rotates x as
-// hadamardRotate does (signs fp32 [K] or null), in the activation warp: bit-identical to
+// With rot_block > 0 (M == 1, a power of two <= 512 dividing K) the kernel first rotates x
+// as hadamardRotate does (signs fp32 [K] or null), in the activation warp: bit-identical to
 // q38_hadamard_rotate followed by the product.
 q38_status qgemv_pack(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w, const void* s,
                       const void* b, int64_t N, void* y, const float* signs = nullptr, int rot_block = 0);

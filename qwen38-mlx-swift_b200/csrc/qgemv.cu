@@ -283,7 +283,7 @@ struct MainArgs {
 // The rotation of an activation product: hadamardRotate's arguments.
 struct Rot {
     const float* signs;
-    int block;  // power of two <= 1024 that divides K; 0 for none
+    int block;  // power of two <= 512 that divides K (one token only); 0 for none
 };
 
 // Rotation of one staged window of W = max(512, block) activations of a token (EPL = W / 32
@@ -684,7 +684,7 @@ __device__ __forceinline__ int seg_key(const MainArgs& a, int chunk, int tile) {
 // PACK: f16 scales and biases with group 128 (the layout of the Bonsai 2 packs); each 64-k
 // subgroup uses the scale of its 128-group, read from a stage box that holds the 8 groups of
 // an aligned pair of chunks.
-template <int BITS, int MP, int TB, bool PACK, int MODE>
+template <int BITS, int MP, int TB, bool PACK, int MODE, bool ROT = false>
 __global__ void __launch_bounds__(THREADS, WG == 1 && TB == 1 ? 3 : 2) qgemv_main(const __grid_constant__ WeightMaps maps,
                                                                       const __grid_constant__ WeightMaps maps_b,
                                                                       const MainArgs a) {
@@ -921,13 +921,10 @@ __global__ void __launch_bounds__(THREADS, WG == 1 && TB == 1 ? 3 : 2) qgemv_mai
                 cp_async_wait<0>();
                 __syncwarp();
             } else {
-                // all of the chunk's copies in flight at once; with a rotation of blocks wider
-                // than a chunk, the whole window of W = block activations of each token
-                const int W = a.rot > KC ? a.rot : KC;
-                const int win0 = (c * KC / W) * W;
-                for (int p = lane; p < a.M * (W / 8); p += 32) {
-                    const int m = p / (W / 8), q = p % (W / 8);
-                    cp_async16(xstage + m * (W * 2) + q * 16, a.x + static_cast<size_t>(m) * a.K + win0 + q * 8);
+                // all of the chunk's copies in flight at once
+                for (int p = lane; p < a.M * (KC / 8); p += 32) {
+                    const int m = p / (KC / 8), q = p % (KC / 8);
+                    cp_async16(xstage + m * (KC * 2) + q * 16, a.x + static_cast<size_t>(m) * a.K + c * KC + q * 8);
                 }
                 cp_async_commit();
                 const bool ok = ci < 2 || mbar_wait(&xempty[ci & 1], ((ci >> 1) & 1) ^ 1, a.status);
@@ -935,19 +932,8 @@ __global__ void __launch_bounds__(THREADS, WG == 1 && TB == 1 ? 3 : 2) qgemv_mai
                 __syncwarp();
                 if (!ok) return;
                 if (lane == 0) *reinterpret_cast<int*>(hdr + HDR_MSEG) = mseg;
-                if (a.rot) {
-                    // token by token, in place: token m's rotated chunk lands at m * 1 KB,
-                    // inside the window of a token at or before m (already read)
-                    const int part = (c * KC - win0) / KC;
-                    const float* sg = a.signs ? a.signs + win0 : nullptr;
-                    for (int m = 0; m < mseg; ++m) {
-                        if (W == KC)
-                            rotate_window<16>(xstage + m * (W * 2), xstage + m * (KC * 2), sg, a.rot, a.rot_scale, part,
-                                              lane);
-                        else
-                            rotate_window<32>(xstage + m * (W * 2), xstage + m * (KC * 2), sg, a.rot, a.rot_scale, part,
-                                              lane);
-                    }
+                if constexpr (ROT) {  // one token, blocks of at most a chunk
+                    rotate_window<16>(xstage, xstage, a.signs ? a.signs + c * KC : nullptr, a.rot, a.rot_scale, 0, lane);
                 }
             }
             build_fragments<BITS>(xstage, mseg, slotp, hdr, s_xs, s_xp, lane);
@@ -1218,15 +1204,14 @@ struct Plan {
 };
 
 template <int BITS>
-bool make_plan(int M, int K, int N, Plan& p, bool two_weights = false, bool moe = false, int rot = 0) {
+bool make_plan(int M, int K, int N, Plan& p, bool two_weights = false, bool moe = false) {
     using F = Fmt<BITS>;
     p.C = K / KC;
     p.tiles = (N + 63) / 64 * (two_weights ? 2 : 1);
     if (static_cast<long long>(p.tiles) * p.C * 4 >= (1LL << 31)) return false;
     p.stage_bytes = NCW * F::SUB_BYTES + 2048;  // a multiple of 1 KiB
     // fragment slots (with their headers) + staging copy of x (+ the MoE plan)
-    const int W = rot > KC ? rot : KC;  // staged activations per token (a rotation window)
-    const int xbytes = 2 * (M * F::XF_PER_M + HDR_BYTES) + M * W * 2 + (moe ? PLAN_BYTES + 16 : 0);
+    const int xbytes = 2 * (M * F::XF_PER_M + HDR_BYTES) + M * KC * 2 + (moe ? PLAN_BYTES + 16 : 0);
     // 76 KiB per CTA in all (ring, header, zeros, fragments, alignment slack, 1 KiB of
     // static sums) lets three CTAs (12 consumer warps) share an SM; 113 KiB two (also for
     // 9-16 tokens, where two CTAs per SM with registers capped at 102 beat one CTA with
@@ -1245,7 +1230,7 @@ bool make_plan(int M, int K, int N, Plan& p, bool two_weights = false, bool moe 
     // the plan sits after the staging copy of x, 16-byte aligned (offsets from the
     // 1024-aligned base)
     p.plan_off = static_cast<int>(align_up(static_cast<size_t>(RING_OFF) + static_cast<size_t>(stages) * p.stage_bytes +
-                                               2 * (M * F::XF_PER_M + HDR_BYTES) + M * W * 2,
+                                               2 * (M * F::XF_PER_M + HDR_BYTES) + M * KC * 2,
                                            16));
     return smem <= MAX_DYN_SMEM;
 }
@@ -1301,9 +1286,9 @@ bool cached_maps(const uint32_t* w, const void* s, const void* b, int K, int N, 
 // Per template instance and device (and context): the shared-memory opt-in of the main
 // kernel and its occupancy at a given ring size.  (Templated on the instance's parameters,
 // not on the kernel's type, which all instances share: each instance keeps its own state.)
-template <int BITS, int MP, int TB, bool PACK, int MODE>
+template <int BITS, int MP, int TB, bool PACK, int MODE, bool ROT = false>
 cudaError_t configure_main(int device, int smem, int* occ_out) {
-    auto kmain = qgemv_main<BITS, MP, TB, PACK, MODE>;
+    auto kmain = qgemv_main<BITS, MP, TB, PACK, MODE, ROT>;
     static std::mutex mu;
     static const void* configured[64] = {};
     static int occ_smem[64][16] = {}, occ_val[64][16] = {};
@@ -1370,12 +1355,12 @@ cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t s
 }
 
 // Launches the main kernel on `args` over `total_sub` subunits (an upper bound for MoE).
-template <int BITS, int MP, int TB, bool PACK, int MODE>
+template <int BITS, int MP, int TB, bool PACK, int MODE, bool ROT = false>
 cudaError_t launch_main(const Plan& p, int device, int num_sms, const WeightMaps& maps, const WeightMaps& maps_b,
                         const MainArgs& args, long long total_sub, cudaStream_t stream) {
-    auto kmain = qgemv_main<BITS, MP, TB, PACK, MODE>;
+    auto kmain = qgemv_main<BITS, MP, TB, PACK, MODE, ROT>;
     int occ = 0;
-    cudaError_t e = configure_main<BITS, MP, TB, PACK, MODE>(device, p.smem, &occ);
+    cudaError_t e = configure_main<BITS, MP, TB, PACK, MODE, ROT>(device, p.smem, &occ);
     if (e != cudaSuccess) return e;
     long long grid = static_cast<long long>(num_sms) * occ;
     if (grid > total_sub) grid = total_sub;
@@ -1395,7 +1380,7 @@ int epilogue_blocks(long long total, int num_sms) {
 // writes y = bf16(silu(gate) * up) [M, N].  SLOTS: partial sums per k-chunk in `part`
 // (C x M x N floats, 2N with maps_b), added in order by the epilogue; otherwise `part` is
 // the zero-at-rest region of M x N (2N) floats.
-template <int BITS, int MP, int TB, bool PACK = false, bool SLOTS = true>
+template <int BITS, int MP, int TB, bool PACK = false, bool SLOTS = true, bool ROT = false>
 cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x, int M, int K,
                            const WeightMaps& maps, bool has_bias, int N, void* y, float* part, uint32_t* status,
                            cudaStream_t stream, const WeightMaps* maps_b = nullptr, Rot rot = Rot{nullptr, 0}) {
@@ -1408,8 +1393,8 @@ cudaError_t launch_kernels(const Plan& p, int device, int num_sms, const void* x
     args.tiles_a = maps_b ? p.tiles / 2 : p.tiles;
     args.ld = maps_b ? 2 * N : N;
     const long long total_sub = static_cast<long long>(p.tiles) * p.C * 4;
-    cudaError_t e = launch_main<BITS, MP, TB, PACK, MODE>(p, device, num_sms, maps, maps_b ? *maps_b : maps, args,
-                                                          total_sub, stream);
+    cudaError_t e = launch_main<BITS, MP, TB, PACK, MODE, ROT>(p, device, num_sms, maps, maps_b ? *maps_b : maps,
+                                                               args, total_sub, stream);
     if (e != cudaSuccess) return e;
 
     const int total = M * N;
@@ -1452,19 +1437,28 @@ template <int BITS, int MP, int TB, bool PACK = false>
 cudaError_t launch_ctx(q38_ctx* ctx, const Plan& p, const void* x, int M, int K, const WeightMaps& maps,
                        bool has_bias, int N, void* y, float* part, const WeightMaps* maps_b = nullptr,
                        Rot rot = Rot{nullptr, 0}) {
+    if constexpr (MP == 1 && TB == 1) {  // rotation inside the kernel: one token, blocks <= 512
+        if (rot.block) {
+            if (ctx->deterministic)
+                return launch_kernels<BITS, 1, 1, PACK, true, true>(p, ctx->device, ctx->num_sms, x, M, K, maps,
+                                                                    has_bias, N, y, part, ctx->d_status, ctx->stream,
+                                                                    maps_b, rot);
+            return launch_kernels<BITS, 1, 1, PACK, false, true>(p, ctx->device, ctx->num_sms, x, M, K, maps, has_bias,
+                                                                 N, y, part, ctx->d_status, ctx->stream, maps_b, rot);
+        }
+    }
     if (ctx->deterministic)
         return launch_kernels<BITS, MP, TB, PACK, true>(p, ctx->device, ctx->num_sms, x, M, K, maps, has_bias, N, y,
-                                                        part, ctx->d_status, ctx->stream, maps_b, rot);
+                                                        part, ctx->d_status, ctx->stream, maps_b);
     return launch_kernels<BITS, MP, TB, PACK, false>(p, ctx->device, ctx->num_sms, x, M, K, maps, has_bias, N, y,
-                                                     part, ctx->d_status, ctx->stream, maps_b, rot);
+                                                     part, ctx->d_status, ctx->stream, maps_b);
 }
 
 template <int BITS, int MP, int TB>
 q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, const void* s,
                   const void* b, int N, void* y, Rot rot) {
     Plan p;
-    if (!make_plan<BITS>(M, K, N, p, false, false, rot.block))
-        return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: shape too large");
+    if (!make_plan<BITS>(M, K, N, p)) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: shape too large");
     float* part = nullptr;
     q38_status st = partial_sums(ctx, p, M, N, false, &part);
     if (st != Q38_OK) return st;
@@ -1484,8 +1478,7 @@ template <int BITS, int MP, int TB>
 q38_status launch_pack(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, const void* s,
                        const void* b, int N, void* y, Rot rot) {
     Plan p;
-    if (!make_plan<BITS>(M, K, N, p, false, false, rot.block))
-        return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: shape too large");
+    if (!make_plan<BITS>(M, K, N, p)) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_matmul: shape too large");
     float* part = nullptr;
     q38_status st = partial_sums(ctx, p, M, N, false, &part);
     if (st != Q38_OK) return st;
@@ -1506,8 +1499,7 @@ q38_status launch_gate_up(q38_ctx* ctx, const void* x, int M, int K, const uint3
                           const void* bg, const uint32_t* wu, const void* su, const void* bu, int N, void* h,
                           Rot rot) {
     Plan p;
-    if (!make_plan<BITS>(M, K, N, p, true, false, rot.block))
-        return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_gate_up: shape too large");
+    if (!make_plan<BITS>(M, K, N, p, true)) return fail(ctx, Q38_ERR_UNSUPPORTED, "quantized_gate_up: shape too large");
     float* part = nullptr;
     q38_status st = partial_sums(ctx, p, M, N, true, &part);
     if (st != Q38_OK) return st;
