@@ -699,6 +699,57 @@ def run_prefill(torch, q38, dev, stream, world, dist, quick=False):
                                  "(a seconds-long step)"}}
 
 
+def run_prefill_bits(torch, q38, dev, stream, quick=False):
+    """One prompt-sized product per code width on the tensor-core prefill kernel: x bf16
+    [4096, 5120] . W [17408, 5120]^T, group 64, bits 2/3/4/8 (random-init weights quantized
+    on the device).  CUDA-graph replays cycling 4 weight copies, CUDA events, best of 3;
+    peak = burst bf16 (the replay lasts milliseconds)."""
+    M, N, K = 4096, 17408, 5120
+    g = torch.Generator(device=dev).manual_seed(4141)
+    x = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+    peak = None
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        peak = float(json.load(open(p))["bf16_tflops"])
+    nrep = 8 if quick else 20
+    out = {}
+    for bits in (2, 3, 4, 8):
+        w = torch.randn((N, K), generator=g, device=dev) * 0.02
+        c, s, b = q38.quantize(w, GROUP, bits, scales_dtype=torch.bfloat16)
+        del w
+        mats = [(c.view(torch.int32), s, b)]
+        mats += [(m[0].clone(), m[1].clone(), m[2].clone()) for m in mats * 3]
+
+        def body():
+            for i in range(nrep):
+                q38.quantized_matmul(x, *mats[i % 4], True, GROUP, bits)
+        body()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            body()
+        gr.replay()
+        torch.cuda.synchronize()
+        best = None
+        for _ in range(3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            gr.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / nrep
+            best = us if best is None else min(best, us)
+        tf = 2.0 * M * N * K / (best * 1e-6) / 1e12
+        out[str(bits)] = {"us": round(best, 1), "TFLOPs": round(tf, 1),
+                          "frac_of_measured_bf16_peak": round(tf / peak, 4) if peak else None}
+        del gr, mats, c, s, b
+        torch.cuda.synchronize()
+    q38.check_device()
+    return {"workload": "x bf16 [4096, 5120] . W[17408, 5120]^T, group 64, per code width",
+            "timing": "CUDA-graph replays over 4 weight copies, CUDA events, best of 3; peak = burst bf16",
+            "per_bits": out}
+
+
 def run_config1(torch, q38, O, dev, stream):
     """The single-product configuration: x bf16 [16, 4096] . W [11008, 4096]^T, 4-bit g64;
     200 launches in one graph over 8 weight copies (200 MB, more than L2)."""
@@ -919,6 +970,7 @@ def run_ours(args, rank, world, local_rank):
     bonsai = None if (args.skip_prefill or world > 1) else run_bonsai(torch, q38, dev, args.quick)
     lm_head = None if (args.skip_prefill or world > 1) else run_lm_head(torch, q38, dev, args.quick)
     config1 = run_config1(torch, q38, O, dev, stream) if world == 1 else None
+    prefill_bits = None if (args.skip_prefill or world > 1) else run_prefill_bits(torch, q38, dev, stream, args.quick)
 
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
@@ -954,6 +1006,7 @@ def run_ours(args, rank, world, local_rank):
         "bonsai": bonsai,
         "lm_head": lm_head,
         "config1": config1,
+        "prefill_bits": prefill_bits,
     }
     return line
 

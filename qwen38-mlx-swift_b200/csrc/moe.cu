@@ -1193,24 +1193,6 @@ q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
                             down_s, down_b))
         return qgemv_moe_decode(ctx, x, T, H, I, E, top_k, indices, scores, gate_w, gate_s, gate_b, up_w, up_s, up_b,
                                 down_w, down_s, down_b, bits, out);
-    if (bits == 8) {
-        // 8-bit experts (no grouped tensor-core path): the decode path over 16 tokens at a time
-        const int64_t step = 16;
-        if (!qgemv_moe_supported(std::min<int64_t>(T, step), H, I, E, top_k, group_size, bits, x, gate_w, gate_s,
-                                 gate_b, up_w, up_s, up_b, down_w, down_s, down_b))
-            return fail(ctx, Q38_ERR_UNSUPPORTED,
-                        "switch_glu: 8-bit experts need 16 * top_k <= 256, top_k <= 32 and 16-byte-aligned tensors");
-        for (int64_t t0 = 0; t0 < T; t0 += step) {
-            const int64_t tn = std::min(step, T - t0);
-            if ((st = qgemv_moe_decode(ctx, static_cast<const uint8_t*>(x) + t0 * H * 2, tn, H, I, E, top_k,
-                                       indices + t0 * top_k, static_cast<const uint8_t*>(scores) + t0 * top_k * 2,
-                                       gate_w, gate_s, gate_b, up_w, up_s, up_b, down_w, down_s, down_b, bits,
-                                       static_cast<uint8_t*>(out) + t0 * H * 2)) != Q38_OK)
-                return st;
-        }
-        return Q38_OK;
-    }
-
     const int rb_gu = static_cast<int>(I / 64), rb_d = static_cast<int>(H / 128);
     // An expert receives at most one pair per token, so runs never exceed T pairs.
     const int xr = T <= 32 ? 32 : T <= 64 ? 64 : 128;

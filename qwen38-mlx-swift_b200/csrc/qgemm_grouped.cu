@@ -405,6 +405,7 @@ q38_status grouped_gate_up(q38_ctx* ctx, const GroupedProblem& p, int bits) {
     switch (bits) {
         case 2: return launch_grouped<2, true>(ctx, p);
         case 3: return launch_grouped<3, true>(ctx, p);
+        case 8: return launch_grouped<8, true>(ctx, p);
         default: return launch_grouped<4, true>(ctx, p);
     }
 }
@@ -413,6 +414,7 @@ q38_status grouped_down(q38_ctx* ctx, const GroupedProblem& p, int bits) {
     switch (bits) {
         case 2: return launch_grouped<2, false>(ctx, p);
         case 3: return launch_grouped<3, false>(ctx, p);
+        case 8: return launch_grouped<8, false>(ctx, p);
         default: return launch_grouped<4, false>(ctx, p);
     }
 }
@@ -455,13 +457,13 @@ __global__ void __launch_bounds__(256) moe_gather_kernel(const __nv_bfloat16* __
     if (odd) {
 #pragma unroll
         for (int t = 0; t < 4; ++t)
-            o[t] = pack_bf16x2(e[pair_code<BITS>(4 + t, 0)] * pair_mult<BITS>(4 + t, 0),
-                               e[pair_code<BITS>(4 + t, 1)] * pair_mult<BITS>(4 + t, 1));
+            o[t] = pack_bf16x2(e[tc_pair_code<BITS>(4 + t, 0)] * tc_pair_mult<BITS>(4 + t, 0),
+                               e[tc_pair_code<BITS>(4 + t, 1)] * tc_pair_mult<BITS>(4 + t, 1));
     } else {
 #pragma unroll
         for (int t = 0; t < 4; ++t)
-            o[t] = pack_bf16x2(e[pair_code<BITS>(t, 0)] * pair_mult<BITS>(t, 0),
-                               e[pair_code<BITS>(t, 1)] * pair_mult<BITS>(t, 1));
+            o[t] = pack_bf16x2(e[tc_pair_code<BITS>(t, 0)] * tc_pair_mult<BITS>(t, 0),
+                               e[tc_pair_code<BITS>(t, 1)] * tc_pair_mult<BITS>(t, 1));
     }
     *reinterpret_cast<uint4*>(xs + static_cast<size_t>(j) * H + ch * 8) = make_uint4(o[0], o[1], o[2], o[3]);
 }
@@ -484,6 +486,7 @@ q38_status moe_gather_launch(q38_ctx* ctx, const void* x, int H, const int32_t* 
     switch (bits) {
         case 2: e = cudaLaunchKernelEx(&cfg, moe_gather_kernel<2>, xb, H, perm, pairs, top_k, valid, o); break;
         case 3: e = cudaLaunchKernelEx(&cfg, moe_gather_kernel<3>, xb, H, perm, pairs, top_k, valid, o); break;
+        case 8: e = cudaLaunchKernelEx(&cfg, moe_gather_kernel<8>, xb, H, perm, pairs, top_k, valid, o); break;
         default: e = cudaLaunchKernelEx(&cfg, moe_gather_kernel<4>, xb, H, perm, pairs, top_k, valid, o); break;
     }
     if (e != cudaSuccess) {

@@ -1,6 +1,6 @@
 // Prefill-shaped MLX-affine quantized product on the 5th-generation tensor cores:
 // y[M,N] = x[M,K] . dequant(W)[N,K]^T for M > 16 tokens, group 64, K % 128 == 0,
-// bits 2/3/4, bf16 activations and scales.  Replaces the Metal `qmm` kernel behind
+// bits 2/3/4/8, bf16 activations and scales.  Replaces the Metal `qmm` kernel behind
 // MLX.quantizedMM (QuantizedLinear.callAsFunction,
 // Sources/Qwen38Core/FlashNext/Qwen4ExpPrequantized.swift:156-159) for prompt-sized inputs.
 //
@@ -451,11 +451,11 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
 bool qgemm_tc_supported(int64_t M, int64_t K, int group, int bits, q38_dtype xd, q38_dtype sd, const void* x,
                         const void* w, const void* s, const void* b, const void* y) {
     if (M < 17 || M > (1 << 24) || K % 128 != 0 || K <= 0 || K > (1 << 20)) return false;
-    if (bits != 2 && bits != 3 && bits != 4) return false;
+    if (bits != 2 && bits != 3 && bits != 4 && bits != 8) return false;
     if (xd != Q38_BF16) return false;
     // group 64 with bf16 scales, or the Bonsai 2 pack's group 128 with f16 scales (2 and 4 bits)
     const bool std_layout = group == 64 && sd == Q38_BF16;
-    const bool pack_layout = group == 128 && sd == Q38_F16 && bits != 3;
+    const bool pack_layout = group == 128 && sd == Q38_F16 && (bits == 2 || bits == 4);
     if (!std_layout && !pack_layout) return false;
     auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
     return al(x) && al(w) && al(s) && (!b || al(b)) && al(y);
@@ -472,6 +472,8 @@ q38_status qgemm_tc_run(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const
     switch (bits) {
         case 2: return tma_scales ? launch<2, true>(ctx, x, m, k, w, s, b, n, y) : launch<2, false>(ctx, x, m, k, w, s, b, n, y);
         case 3: return tma_scales ? launch<3, true>(ctx, x, m, k, w, s, b, n, y) : launch<3, false>(ctx, x, m, k, w, s, b, n, y);
+        // 8-bit stages (16 KiB of codes) leave room for four weight stages only without the scale boxes
+        case 8: return launch<8, false>(ctx, x, m, k, w, s, b, n, y);
         default: return tma_scales ? launch<4, true>(ctx, x, m, k, w, s, b, n, y) : launch<4, false>(ctx, x, m, k, w, s, b, n, y);
     }
 }

@@ -11,18 +11,31 @@ namespace {
 
 // Codes of one 128-k stage for a block of weight rows, as a TMA box of CODE_W words per
 // row: 2-bit rows (32 B) use the 32-byte swizzle, 4-bit rows (64 B) the 64-byte swizzle,
-// 3-bit rows (48 B) none.
+// 8-bit rows (128 B) the 128-byte swizzle, 3-bit rows (48 B) none.
 template <int BITS>
 struct CodeLayout {
     static constexpr int CODE_W = 4 * BITS;
-    static constexpr int SW = BITS == 2 ? 32 : BITS == 4 ? 64 : 0;
+    static constexpr int SW = BITS == 2 ? 32 : BITS == 4 ? 64 : BITS == 8 ? 128 : 0;
 };
 
 template <int BITS>
 constexpr CUtensorMapSwizzle code_swizzle() {
-    return CodeLayout<BITS>::SW == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+    return CodeLayout<BITS>::SW == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+           : CodeLayout<BITS>::SW == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
            : CodeLayout<BITS>::SW == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
                                         : CU_TENSOR_MAP_SWIZZLE_NONE;
+}
+
+// Operand order of the tensor-core paths.  8-bit codes stay whole: operand q of a
+// 16-code window pairs codes 2q and 2q + 1 with weight 1, so the activations keep their
+// natural order.  The narrower widths use the magic-number pair tables.
+template <int BITS>
+__host__ __device__ constexpr int tc_pair_code(int q, int hi) {
+    return BITS == 8 ? 2 * q + hi : pair_code<BITS>(q, hi);
+}
+template <int BITS>
+__host__ __device__ constexpr float tc_pair_mult(int q, int hi) {
+    return BITS == 8 ? 1.0f : pair_mult<BITS>(q, hi);
 }
 
 // Bounded mbarrier wait.  On expiry records the timeout and raises the abort flag of the
@@ -75,6 +88,30 @@ template <int BITS>
 __device__ __forceinline__ void dequant_group(const uint8_t* codes, int row, int gg, uint32_t sbits, uint32_t bbits,
                                               uint32_t* a) {
     using F = CodeLayout<BITS>;
+    if constexpr (BITS == 8) {
+        // A byte permute places code q in the low mantissa bits of fp32 2^23, so that
+        // subtracting 2^23 leaves q exactly; q pairs convert exactly to bf16x2, and
+        // a = s * q + b is rounded once, as for the narrower widths.
+        const uint32_t s2 = sbits * 0x10001u, b2 = bbits * 0x10001u;
+        const int swz = row & 7;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int c = gg * 4 + i;  // 16-byte chunk of the 128-byte row
+            const uint4 v = *reinterpret_cast<const uint4*>(codes + row * 128 + ((c ^ swz) << 4));
+            const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                float q[4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t)
+                    q[t] = __uint_as_float(__byte_perm(wv[j], 0x4B000000u, 0x7440u + t)) - 8388608.0f;
+                const __nv_bfloat162 p01 = __floats2bfloat162_rn(q[0], q[1]);
+                const __nv_bfloat162 p23 = __floats2bfloat162_rn(q[2], q[3]);
+                a[8 * i + 2 * j] = bf2_fma(*reinterpret_cast<const uint32_t*>(&p01), s2, b2);
+                a[8 * i + 2 * j + 1] = bf2_fma(*reinterpret_cast<const uint32_t*>(&p23), s2, b2);
+            }
+        }
+    } else {
     constexpr int GW = 2 * BITS;  // words per row per group
     uint32_t w[8];
     if constexpr (BITS == 3) {
@@ -106,8 +143,8 @@ __device__ __forceinline__ void dequant_group(const uint8_t* codes, int row, int
     uint32_t b2[8];
 #pragma unroll
     for (int q = 0; q < 8; ++q)
-        b2[q] = (__float_as_uint(bf * (1.0f / pair_mult<BITS>(q, 0))) >> 16) |
-                (__float_as_uint(bf * (1.0f / pair_mult<BITS>(q, 1))) & 0xFFFF0000u);
+        b2[q] = (__float_as_uint(bf * (1.0f / tc_pair_mult<BITS>(q, 0))) >> 16) |
+                (__float_as_uint(bf * (1.0f / tc_pair_mult<BITS>(q, 1))) & 0xFFFF0000u);
 #pragma unroll
     for (int tq = 0; tq < 4; ++tq) {
         uint32_t win[2];
@@ -134,6 +171,7 @@ __device__ __forceinline__ void dequant_group(const uint8_t* codes, int row, int
             a[tq * 8 + q] = bf2_fma(bf2_sub(v[q], MAGIC), s2, b2[q]);
         }
     }
+    }
 }
 
 // Position and multiplier of code c (0..15 within a 16-code window) in the extraction
@@ -142,13 +180,13 @@ template <int BITS>
 __host__ __device__ constexpr int window_slot(int c) {
     for (int q = 0; q < 8; ++q)
         for (int hi = 0; hi < 2; ++hi)
-            if (pair_code<BITS>(q, hi) == c) return 2 * q + hi;
+            if (tc_pair_code<BITS>(q, hi) == c) return 2 * q + hi;
     return -1;
 }
 template <int BITS>
 __host__ __device__ constexpr float window_mult(int c) {
     const int s = window_slot<BITS>(c);
-    return pair_mult<BITS>(s >> 1, s & 1);
+    return tc_pair_mult<BITS>(s >> 1, s & 1);
 }
 
 // One 64-element group of bf16 activations -> extraction order, scaled by 2^-p.
@@ -170,8 +208,8 @@ __device__ __forceinline__ void permute_group(const __nv_bfloat16* __restrict__ 
 #pragma unroll
     for (int col = 0; col < 32; ++col) {
         const int tq = col / 8, q = col % 8;
-        out[col] = pack_bf16x2(xv[16 * tq + pair_code<BITS>(q, 0)] * pair_mult<BITS>(q, 0),
-                               xv[16 * tq + pair_code<BITS>(q, 1)] * pair_mult<BITS>(q, 1));
+        out[col] = pack_bf16x2(xv[16 * tq + tc_pair_code<BITS>(q, 0)] * tc_pair_mult<BITS>(q, 0),
+                               xv[16 * tq + tc_pair_code<BITS>(q, 1)] * tc_pair_mult<BITS>(q, 1));
     }
     uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll

@@ -335,9 +335,10 @@ def test_switch_glu_decode_is_deterministic(q38):
     assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("T", [3, 16, 40])
+@pytest.mark.parametrize("T", [3, 16, 40, 300])
 def test_switch_glu_8bit_experts(q38, T):
-    """8-bit experts: the decode path (16 tokens at a time beyond 16), fp32-weight oracle."""
+    """8-bit experts: the decode path up to 16 tokens (fp32-weight oracle), the grouped
+    tensor-core path beyond (bf16-rounded weights, as for the narrower widths)."""
     E, k, H, I, bits = 32, 8, 1024, 512, 8
     dev, host = make_experts(q38, 8800 + T, E, I, H, bits)
     x = O.normal_bf16(8810 + T, (T, H))
@@ -345,7 +346,7 @@ def test_switch_glu_8bit_experts(q38, T):
     out = q38.switch_glu(dev_bf16(x), dev_i32(idx), dev_bf16(sc), *dev, 64, bits)
     torch.cuda.synchronize()
     q38.check_device()
-    ref = O.switch_glu(x, idx, sc, *host, 64, bits)
+    ref = O.switch_glu(x, idx, sc, *host, 64, bits, weights_bf16=T > 16)
     check_close(host_bf16(out), O.bf16_to_f32(ref).astype(np.float64))
 
 

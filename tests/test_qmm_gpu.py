@@ -266,9 +266,10 @@ def test_bonsai_ternary_projection_full_size(q38, NK):
     check_close(host_bf16(y[torch.from_numpy(rows).cuda()]), ref)
 
 
-@pytest.mark.parametrize("M,N,K", [(17, 256, 1024), (64, 1000, 2048), (300, 512, 5120)])
+@pytest.mark.parametrize("M,N,K", [(17, 256, 1024), (64, 1000, 2048), (300, 512, 5120), (600, 1280, 384)])
 def test_qmm_8bit_prompt_sizes(q38, M, N, K):
-    """8-bit codes with more than 16 tokens (the prompt-sized product)."""
+    """8-bit codes with more than 16 tokens (the tensor-core prompt product; K = 384 reads
+    the scales without the TMA boxes, as every 8-bit prompt product does)."""
     c, s, b = make_weight(1500 + M, N, K, 8)
     x = O.normal_bf16(1501 + M, (M, K))
     ref = O.qmm(x, c, s, b, 64, 8, f32=True)
