@@ -594,7 +594,7 @@ def run_prefill_tp(torch, q38, dev, stream, world, rank, dist, comm, quick=False
 
     def stack():
         for i, (ga, up, dn) in enumerate(layers):
-            outs[i & 1].copy_(q38.tp_mlp(comm, x, ga, up, dn, GROUP, 4, chunks=4))
+            outs[i & 1].copy_(q38.tp_mlp(comm, x, ga, up, dn, GROUP, 4, chunks=0))
     stack()
     torch.cuda.synchronize()
     dist.barrier()
@@ -631,7 +631,7 @@ def run_prefill_tp(torch, q38, dev, stream, world, rank, dist, comm, quick=False
             "config": {"workload": f"{L} layers x 4096 tokens x 4-bit g64 MLP: gate, up 17408x5120 -> SiLU-gate -> "
                                    "down 5120x17408, bf16 all-reduce; every layer reads the same x",
                        "parallelism": f"tensor parallel x{world}", "scaling": "strong",
-                       "timing": "q38_tp_mlp (4 token chunks, all-reduce overlapped, NCCL inside libq38) "
+                       "timing": "q38_tp_mlp (token chunks chosen by the library, all-reduce overlapped, NCCL inside libq38) "
                                  "stack captured in a CUDA graph, CUDA events, max over ranks"}}
 
 

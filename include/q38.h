@@ -88,6 +88,11 @@ Q38_API size_t q38_ctx_workspace_bytes(const q38_ctx* ctx);
  * bitwise reproducible results (MLX's decode is reproducible too) for about one
  * microsecond more per product.  Off by default. */
 Q38_API q38_status q38_ctx_set_deterministic(q38_ctx* ctx, int on);
+/* Pieces of q38_ep_switch_glu's exchange (1, 2 or 4; 0 = chosen by the library): the
+ * capacity rows go in that many chunks whose exchanges overlap the experts' work of the
+ * previous chunk.  Every rank of a communicator must use the same setting.  Results do not
+ * depend on it. */
+Q38_API q38_status q38_ctx_set_ep_chunks(q38_ctx* ctx, int chunks);
 /* Synchronise the stream and return Q38_ERR_DEVICE_TIMEOUT if any kernel recorded a
  * bounded-wait expiry since the last check (the word is then cleared). */
 Q38_API q38_status q38_ctx_check_device(q38_ctx* ctx);
@@ -211,8 +216,8 @@ Q38_API q38_status q38_moe_sort(q38_ctx* ctx, const int32_t* indices, int64_t pa
  * An index of -1 marks an empty slot: it contributes nothing and is not an error.
  * Implemented for group 64, bits 2/3/4/8, H % 512 == 0, I % 512 == 0, E <= 1024.  Up to 16
  * tokens (with T*top_k <= 256) stream the selected experts' weights on the decode kernel;
- * more tokens run the grouped tensor-core products over expert-sorted pairs (8-bit: the
- * decode path, 16 tokens at a time).  Uses the context's activation buffer (about
+ * more tokens run the grouped tensor-core products over expert-sorted pairs.  Uses the
+ * context's activation buffer (about
  * T*top_k*(2H + I)*2 bytes) and workspace. */
 Q38_API q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int64_t I, int64_t E,
                                   int top_k, const int32_t* indices, const void* scores,
@@ -232,6 +237,25 @@ Q38_API q38_status q38_sparse_moe(q38_ctx* ctx, const void* x, int64_t T, int64_
                                   const void* up_scales, const void* up_biases, const uint32_t* down_w,
                                   const void* down_scales, const void* down_biases, q38_dtype dtype, int group_size,
                                   int bits, int32_t* indices, void* scores, void* out);
+
+/* The shared-expert half of the sparse-MoE block, added to the routed output: the `shared`
+ * term of Qwen4ExpSparseMoE.callAsFunction (Sources/Qwen38Core/FlashNext/Qwen4ExpSparseMoE.swift:295-298)
+ * with Qwen4ExpSharedExpert (:47-82):
+ *   h = bf16(silu(bf16(x . Wg^T)) * bf16(x . Wu^T)), ys = bf16(h . Wd^T),
+ *   s = bf16(sigmoid(bf16(x . Wsg^T))), out = bf16(routed + bf16(s * ys)).
+ * x, routed, out bf16 [T, H] (routed and out may be the same buffer); gate/up codes
+ * [I, H*bits/32], down [H, I*bits/32], the shared-expert gate Wsg [1, H*bits/32]; scales and
+ * biases [rows, K/group_size] of scales_dtype, all four projections with the same group
+ * size and bits (the published checkpoint quantizes them 4-bit, group 32).  Gate and up
+ * carry biases both or neither.  Uses the context's activation buffer (T*(2I + H)*2
+ * bytes) and workspace. */
+Q38_API q38_status q38_shared_expert(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int64_t I,
+                                     const uint32_t* gate_w, const void* gate_scales, const void* gate_biases,
+                                     const uint32_t* up_w, const void* up_scales, const void* up_biases,
+                                     const uint32_t* down_w, const void* down_scales, const void* down_biases,
+                                     const uint32_t* sgate_w, const void* sgate_scales, const void* sgate_biases,
+                                     q38_dtype scales_dtype, int group_size, int bits, const void* routed,
+                                     void* out);
 
 /* h = bf16(silu(g) * u) elementwise with silu(g) = g / (1 + exp(-g)) in fp32: the
  * SiLU-gate between the gate/up and down projections of the dense MLP (MLX's compiled
@@ -402,7 +426,9 @@ Q38_API q38_status q38_comm_all_reduce(q38_ctx* ctx, q38_comm* comm, const void*
  * down split by its reduction dimension ([D, F_local*bits/32], whole groups and words),
  * computes its partial y and all-reduces it (bf16 sum).  The tokens are processed in
  * `chunks` pieces (whole 128-token tiles): the all-reduce of one piece runs on the
- * communicator's stream while the next piece computes.  x, y bf16 [M, D] on every rank. */
+ * communicator's stream while the next piece computes; chunks <= 0 picks the count (1 to
+ * 4) that keeps two waves of tensor-core tiles in each piece.  x, y bf16 [M, D] on every
+ * rank. */
 Q38_API q38_status q38_tp_mlp(q38_ctx* ctx, q38_comm* comm, const void* x, int64_t M, int64_t D,
                               const uint32_t* gate_w, const void* gate_s, const void* gate_b,
                               const uint32_t* up_w, const void* up_s, const void* up_b,

@@ -245,6 +245,32 @@ def switch_glu(x, indices, scores, gate, up, down, group: int, bits: int,
     return out
 
 
+def shared_expert(x, routed, gate, up, down, shared_gate, group: int, bits: int,
+                  weights_bf16: bool = False) -> np.ndarray:
+    """The shared-expert term of Qwen4ExpSparseMoE.callAsFunction (FlashNext/Qwen4ExpSparseMoE.swift:297,
+    Qwen4ExpSharedExpert :77-82) added to the routed output; every projection is a quantized
+    product rounded to bf16 (an MLX bf16 array), the SiLU product rounded once (the compiled
+    silu product), sigmoid in fp32 rounded to bf16:
+      out = bf16(routed + bf16(bf16(sigmoid(sg(x))) * down(bf16(silu(gate(x)) * up(x))))).
+    weights_bf16 rounds the dequantized gate, up and down weights to bf16 before their
+    products (the operands of a bf16 tensor-core product), fp32 accumulation."""
+    f = lambda a: bf16_to_f32(a).astype(np.float32)
+
+    def proj(a, w):
+        if not weights_bf16:
+            return f(qmm(a, *w, group, bits))
+        wb = f(f32_to_bf16(dequantize(w[0], w[1], w[2], group, bits)))
+        return f(f32_to_bf16(f(a) @ wb.T))
+    g = proj(x, gate)
+    u = proj(x, up)
+    h = f32_to_bf16((g / (np.float32(1) + np.exp(-g))) * u)
+    ys = proj(h, down)
+    logit = f(qmm(x, *shared_gate, group, bits))
+    s = f(f32_to_bf16(np.float32(1) / (np.float32(1) + np.exp(-logit))))
+    sh = f(f32_to_bf16(s * ys))
+    return f32_to_bf16(f(routed) + sh)
+
+
 def hadamard_rotate(x, block: int, signs=None, inverse: bool = False) -> np.ndarray:
     x = np.ascontiguousarray(x, dtype=np.uint16)
     D = x.shape[-1]

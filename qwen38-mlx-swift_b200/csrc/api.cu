@@ -254,6 +254,12 @@ q38_status q38_ctx_set_deterministic(q38_ctx* ctx, int on) {
     return Q38_OK;
 }
 
+q38_status q38_ctx_set_ep_chunks(q38_ctx* ctx, int chunks) {
+    if (!ctx || (chunks != 0 && chunks != 1 && chunks != 2 && chunks != 4)) return Q38_ERR_INVALID_ARGUMENT;
+    ctx->ep_chunks = chunks;
+    return Q38_OK;
+}
+
 q38_status q38_ctx_check_device(q38_ctx* ctx) {
     if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
     q38_status st = set_device(ctx);
@@ -330,6 +336,10 @@ q38_status gate_up_check(q38_ctx* ctx, const char* op, const void* x, int64_t M,
     return Q38_OK;
 }
 
+}  // namespace
+
+namespace q38 {
+
 // h = bf16(silu(x.Wg^T) * x.Wu^T): one pass over both weights where the decode kernel takes
 // the layout, otherwise the two products and the SiLU product, with the up product at byte
 // `up_offset` of the activation buffer (the bytes before it may hold x).
@@ -356,7 +366,7 @@ q38_status gate_up_run(q38_ctx* ctx, const void* x, int64_t M, int64_t K, q38_dt
     return q38_silu_mul(ctx, h, up, M * N, h);
 }
 
-}  // namespace
+}  // namespace q38
 
 extern "C" {
 
@@ -401,6 +411,39 @@ q38_status q38_hadamard_quantized_gate_up(q38_ctx* ctx, const void* x, int64_t M
     if ((st = q38_hadamard_rotate(ctx, x, M, K, x_dtype, signs, block, 0, xr)) != Q38_OK) return st;
     return gate_up_run(ctx, xr, M, K, x_dtype, w_gate, s_gate, b_gate, w_up, s_up, b_up, scales_dtype, N, group_size,
                        bits, Q38_MODE_AFFINE, h, xbytes);
+}
+
+q38_status q38_shared_expert(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int64_t I, const uint32_t* gate_w,
+                             const void* gate_s, const void* gate_b, const uint32_t* up_w, const void* up_s,
+                             const void* up_b, const uint32_t* down_w, const void* down_s, const void* down_b,
+                             const uint32_t* sg_w, const void* sg_s, const void* sg_b, q38_dtype scales_dtype,
+                             int group_size, int bits, const void* routed, void* out) {
+    if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
+    q38_status st = gate_up_check(ctx, "shared_expert", x, T, H, Q38_BF16, gate_w, gate_s, gate_b, up_w, up_s, up_b,
+                                  scales_dtype, I, group_size, bits, Q38_MODE_AFFINE, out);
+    if (st != Q38_OK) return st;
+    if ((st = check_format(ctx, "shared_expert", I, group_size, bits, Q38_MODE_AFFINE)) != Q38_OK) return st;
+    if (T == 0) return Q38_OK;
+    if (!down_w || !down_s || !sg_w || !sg_s || !routed)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "shared_expert: null pointer");
+    if (T > (1 << 30) || H > (1 << 30))
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "shared_expert: shape too large");
+    if ((st = set_device(ctx)) != Q38_OK) return st;
+    // activation buffer: h [T, I], the shared output ys [T, H], then the up product of the
+    // general gate/up path; sized once so that the buffer does not move in between
+    const size_t o_ys = align_up(static_cast<size_t>(T) * I * 2, 256);
+    const size_t o_up = o_ys + align_up(static_cast<size_t>(T) * H * 2, 256);
+    void* base = nullptr;
+    if ((st = ensure_aux(ctx, o_up + static_cast<size_t>(T) * I * 2, &base)) != Q38_OK) return st;
+    uint8_t* b8 = static_cast<uint8_t*>(base);
+    if ((st = gate_up_run(ctx, x, T, H, Q38_BF16, gate_w, gate_s, gate_b, up_w, up_s, up_b, scales_dtype, I,
+                          group_size, bits, Q38_MODE_AFFINE, b8, o_up)) != Q38_OK)
+        return st;
+    if ((st = q38_quantized_matmul(ctx, b8, T, I, Q38_BF16, down_w, down_s, down_b, scales_dtype, H, 1, group_size,
+                                   bits, Q38_MODE_AFFINE, b8 + o_ys)) != Q38_OK)
+        return st;
+    return shared_combine_launch(ctx, x, T, H, sg_w, sg_s, sg_b, scales_dtype, group_size, bits, b8 + o_ys, routed,
+                                 out);
 }
 
 q38_status q38_dequantize(q38_ctx* ctx, const uint32_t* w, const void* scales, const void* biases,

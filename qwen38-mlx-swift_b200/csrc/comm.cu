@@ -423,11 +423,17 @@ q38_status q38_tp_mlp(q38_ctx* ctx, q38_comm* c, const void* x, int64_t M, int64
     q38_status st = check_pair(ctx, c, "tp_mlp");
     if (st != Q38_OK) return st;
     if (dtype != Q38_BF16) return fail(ctx, Q38_ERR_UNSUPPORTED, "tp_mlp: bf16 activations and scales only");
-    if (M < 0 || D <= 0 || F_local <= 0 || chunks < 1)
-        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "tp_mlp: bad shape or chunk count");
+    if (M < 0 || D <= 0 || F_local <= 0)
+        return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "tp_mlp: bad shape");
     if (M == 0) return Q38_OK;
     if (!x || !gate_w || !gate_s || !up_w || !up_s || !down_w || !down_s || !y)
         return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "tp_mlp: null pointer");
+    if (chunks <= 0) {
+        // as many pieces as keep two waves of 256 x 256 gate tiles in each (a smaller piece
+        // leaves tensor cores idle for longer than its all-reduce overlaps), at most 4
+        const int64_t tiles = ((F_local + 255) / 256) * ((M + 255) / 256);
+        chunks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(4, tiles / std::max(1, ctx->num_sms))));
+    }
     // chunks of whole 128-token tiles
     int64_t step = (M + chunks - 1) / chunks;
     step = std::max<int64_t>(128, (step + 127) / 128 * 128);
@@ -516,30 +522,77 @@ q38_status q38_ep_switch_glu(q38_ctx* ctx, q38_comm* c, const void* x, int64_t T
     uint8_t* xr = b + o_xr;
     int32_t* idr = reinterpret_cast<int32_t*>(b + o_idr);
     __nv_bfloat16* scr = reinterpret_cast<__nv_bfloat16*>(b + o_scr);
-    // dispatch: rows, slot experts and scores to every rank (rank r's block of C rows)
-    n.GroupStart();
-    for (int r = 0; r < W; ++r) {
-        n.Send(xsend, C * H, ncclBfloat16, r, c->nc, ctx->stream);
-        n.Recv(xr + r * C * xrow, C * H, ncclBfloat16, r, c->nc, ctx->stream);
-        n.Send(ids + r * C * top_k, C * top_k, ncclInt32, r, c->nc, ctx->stream);
-        n.Recv(idr + r * C * top_k, C * top_k, ncclInt32, r, c->nc, ctx->stream);
-        n.Send(sc + r * C * top_k, C * top_k, ncclBfloat16, r, c->nc, ctx->stream);
-        n.Recv(scr + r * C * top_k, C * top_k, ncclBfloat16, r, c->nc, ctx->stream);
-    }
-    if ((st = nccl_call(ctx, c, n.GroupEnd(), "ep_switch_glu dispatch")) != Q38_OK) return st;
-    // this rank's experts over every received row (slots of other ranks' experts are -1)
     uint8_t* part = b + o_part;
-    if ((st = q38_switch_glu(ctx, xr, R, H, I, epr, top_k, idr, scr, gate_w, gate_s, gate_b, up_w, up_s, up_b, down_w,
-                             down_s, down_b, dtype, group_size, bits, part)) != Q38_OK)
-        return st;
-    // return: each rank's partial sums of the rows it received go back to their home rank
     uint8_t* back = b + o_back;
-    n.GroupStart();
-    for (int r = 0; r < W; ++r) {
-        n.Send(part + r * C * xrow, C * H, ncclBfloat16, r, c->nc, ctx->stream);
-        n.Recv(back + r * C * xrow, C * H, ncclBfloat16, r, c->nc, ctx->stream);
+    // The capacity rows go in NCH chunks, pipelined across the two streams: the exchanges on
+    // the communicator's stream (dispatch q+1 and the return of q - 1 while chunk q
+    // computes), the experts on the context's stream.  Chunk q's region of the receive,
+    // metadata and partial-sum buffers holds W blocks of Cc rows.
+    // Two chunks where the exchange is large against the experts' work (64 MiB or more
+    // leaving each rank); more chunks would re-read and re-dequantize every local expert's
+    // weights per chunk for fewer pairs each, which costs more than the overlap gains.
+    const bool big = static_cast<double>(W - 1) * C * xrow >= 64.0 * (1 << 20);
+    const double pairs_per_expert = static_cast<double>(C) * W * top_k / E;
+    int NCH = (big && C % 2 == 0 && pairs_per_expert >= 256.0) ? 2 : 1;
+    if (ctx->ep_chunks > 0) NCH = C % ctx->ep_chunks == 0 ? ctx->ep_chunks : 1;
+    const int64_t Cc = C / NCH, Rc = W * Cc;
+    size_t ev = 0;
+    auto order = [&](cudaStream_t from, cudaStream_t to) -> q38_status {
+        cudaEvent_t e = comm_event(c, ev++);
+        if (!e || cudaEventRecord(e, from) != cudaSuccess || cudaStreamWaitEvent(to, e, 0) != cudaSuccess)
+            return check_launch(ctx, "ep_switch_glu: stream ordering");
+        return Q38_OK;
+    };
+    // dispatch of chunk q: rows [q*Cc, (q+1)*Cc) of every destination block, with their slot
+    // experts and scores
+    auto dispatch = [&](int q) -> q38_status {
+        const int64_t r0 = q * Cc;
+        n.GroupStart();
+        for (int r = 0; r < W; ++r) {
+            n.Send(static_cast<const uint8_t*>(xsend) + r0 * xrow, Cc * H, ncclBfloat16, r, c->nc, c->stream);
+            n.Recv(xr + (q * Rc + r * Cc) * xrow, Cc * H, ncclBfloat16, r, c->nc, c->stream);
+            n.Send(ids + (r * C + r0) * top_k, Cc * top_k, ncclInt32, r, c->nc, c->stream);
+            n.Recv(idr + (q * Rc + r * Cc) * top_k, Cc * top_k, ncclInt32, r, c->nc, c->stream);
+            n.Send(sc + (r * C + r0) * top_k, Cc * top_k, ncclBfloat16, r, c->nc, c->stream);
+            n.Recv(scr + (q * Rc + r * Cc) * top_k, Cc * top_k, ncclBfloat16, r, c->nc, c->stream);
+        }
+        return nccl_call(ctx, c, n.GroupEnd(), "ep_switch_glu dispatch");
+    };
+    // return of chunk q: each rank's partial sums of the rows it received go back home
+    auto give_back = [&](int q) -> q38_status {
+        const int64_t r0 = q * Cc;
+        n.GroupStart();
+        for (int r = 0; r < W; ++r) {
+            n.Send(part + (q * Rc + r * Cc) * xrow, Cc * H, ncclBfloat16, r, c->nc, c->stream);
+            n.Recv(back + (r * C + r0) * xrow, Cc * H, ncclBfloat16, r, c->nc, c->stream);
+        }
+        return nccl_call(ctx, c, n.GroupEnd(), "ep_switch_glu return");
+    };
+    // landed[q]: recorded on the communicator's stream right after chunk q's dispatch
+    std::vector<cudaEvent_t> landed(NCH, nullptr);
+    auto mark = [&](int q) -> q38_status {
+        landed[q] = comm_event(c, ev++);
+        if (!landed[q] || cudaEventRecord(landed[q], c->stream) != cudaSuccess)
+            return check_launch(ctx, "ep_switch_glu: stream ordering");
+        return Q38_OK;
+    };
+    if ((st = order(ctx->stream, c->stream)) != Q38_OK) return st;  // staging and metadata
+    if ((st = dispatch(0)) != Q38_OK || (st = mark(0)) != Q38_OK) return st;
+    for (int q = 0; q < NCH; ++q) {
+        if (cudaStreamWaitEvent(ctx->stream, landed[q], 0) != cudaSuccess)
+            return check_launch(ctx, "ep_switch_glu: stream ordering");
+        // this rank's experts over chunk q's rows (slots of other ranks' experts are -1)
+        if ((st = q38_switch_glu(ctx, xr + q * Rc * xrow, Rc, H, I, epr, top_k, idr + q * Rc * top_k,
+                                 scr + q * Rc * top_k, gate_w, gate_s, gate_b, up_w, up_s, up_b, down_w, down_s,
+                                 down_b, dtype, group_size, bits, part + q * Rc * xrow)) != Q38_OK)
+            return st;
+        if (q + 1 < NCH && ((st = dispatch(q + 1)) != Q38_OK || (st = mark(q + 1)) != Q38_OK)) return st;
+        if ((st = order(ctx->stream, c->stream)) != Q38_OK) return st;  // chunk q computed
+        if ((st = give_back(q)) != Q38_OK) return st;
     }
-    if ((st = nccl_call(ctx, c, n.GroupEnd(), "ep_switch_glu return")) != Q38_OK) return st;
+    // the context's stream continues after the last return
+    if (cudaEventRecord(c->joined, c->stream) != cudaSuccess || cudaStreamWaitEvent(ctx->stream, c->joined, 0) != cudaSuccess)
+        return check_launch(ctx, "ep_switch_glu: stream join");
     if (T == 0) return Q38_OK;
     cudaLaunchConfig_t cfg = pdl_cfg(dim3(static_cast<unsigned>((H / 8 + 255) / 256), static_cast<unsigned>(T)),
                                      dim3(256), ctx->stream, attr);

@@ -19,6 +19,7 @@
 #include <mutex>
 #include <type_traits>
 
+#include "affine_scalar.cuh"
 #include "moe_internal.h"
 #include "tc_pipeline.cuh"
 
@@ -1101,7 +1102,72 @@ q38_status sort_launch(q38_ctx* ctx, const int32_t* idx, int64_t P, int64_t E, i
                       idx, static_cast<int>(P), static_cast<int>(E), scratch, perm, inv);
 }
 
+// The shared expert's contribution added to the routed output (the `shared` term of
+// Qwen4ExpSparseMoE.callAsFunction, Sources/Qwen38Core/FlashNext/Qwen4ExpSparseMoE.swift:295-298):
+//   out[t] = bf16(routed[t] + bf16(s_t * ys[t])),  s_t = bf16(sigmoid(bf16(x_t . dequant(wsg)))),
+// the gate logit a quantized [1, H] product accumulated in fp32 (w = scale * q + bias).  One
+// block per token; `routed` and `out` may be the same buffer.
+template <typename S>
+__global__ void __launch_bounds__(256) shared_expert_combine(const __nv_bfloat16* __restrict__ x, int H,
+                                                             const uint32_t* __restrict__ gw, const S* __restrict__ gs,
+                                                             const S* __restrict__ gb, int group, int bits,
+                                                             const __nv_bfloat16* __restrict__ ys,
+                                                             const __nv_bfloat16* routed, __nv_bfloat16* out) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const size_t t0 = static_cast<size_t>(blockIdx.x) * H;
+    float acc = 0.f;
+    for (int k = threadIdx.x; k < H; k += blockDim.x) {
+        const int g = k / group;
+        const float w = __fadd_rn(__fmul_rn(to_f32(gs[g]), static_cast<float>(get_code(gw, k, bits))),
+                                  gb ? to_f32(gb[g]) : 0.f);
+        acc = fmaf(__bfloat162float(x[t0 + k]), w, acc);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    __shared__ float part[8];
+    __shared__ float s_gate;
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float v = 0.f;
+        for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) v += part[i];
+        const float l = bf16_bits_to_f32(f32_to_bf16_bits(v));
+        s_gate = bf16_bits_to_f32(f32_to_bf16_bits(1.0f / (1.0f + expf(-l))));
+    }
+    __syncthreads();
+    const float sg = s_gate;
+    for (int j = threadIdx.x; j < H; j += blockDim.x) {
+        const float sh = bf16_bits_to_f32(f32_to_bf16_bits(sg * __bfloat162float(ys[t0 + j])));
+        out[t0 + j] = __float2bfloat16_rn(__bfloat162float(routed[t0 + j]) + sh);
+    }
+}
+
 }  // namespace
+
+q38_status shared_combine_launch(q38_ctx* ctx, const void* x, int64_t T, int64_t H, const uint32_t* gw,
+                                 const void* gs, const void* gb, q38_dtype sd, int group, int bits, const void* ys,
+                                 const void* routed, void* out) {
+    const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+    const __nv_bfloat16* yb = static_cast<const __nv_bfloat16*>(ys);
+    const __nv_bfloat16* rb = static_cast<const __nv_bfloat16*>(routed);
+    __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(out);
+    const dim3 grid(static_cast<unsigned>(T)), block(256);
+    const int h = static_cast<int>(H);
+    switch (sd) {
+        case Q38_F16:
+            return launch_pdl(ctx, "shared_expert_combine", shared_expert_combine<__half>, grid, block, 0, xb, h, gw,
+                              static_cast<const __half*>(gs), static_cast<const __half*>(gb), group, bits, yb, rb, ob);
+        case Q38_F32:
+            return launch_pdl(ctx, "shared_expert_combine", shared_expert_combine<float>, grid, block, 0, xb, h, gw,
+                              static_cast<const float*>(gs), static_cast<const float*>(gb), group, bits, yb, rb, ob);
+        default:
+            return launch_pdl(ctx, "shared_expert_combine", shared_expert_combine<__nv_bfloat16>, grid, block, 0, xb,
+                              h, gw, static_cast<const __nv_bfloat16*>(gs), static_cast<const __nv_bfloat16*>(gb),
+                              group, bits, yb, rb, ob);
+    }
+}
+
 }  // namespace q38
 
 using namespace q38;

@@ -31,6 +31,7 @@ struct q38_ctx {
     size_t aux_bytes = 0;
     uint32_t* d_status = nullptr;  // device status word (timeouts)
     int deterministic = 0;  // decode products: ordered chunk sums (bitwise reproducible)
+    int ep_chunks = 0;      // pieces of the expert-parallel exchange (0: the library's choice)
     // Pinned host staging of the safetensors reader: two halves used alternately, each
     // guarded by an event of its last host->device copy.
     void* host_stage = nullptr;
@@ -57,6 +58,20 @@ q38_status ensure_zero_region(q38_ctx* ctx, size_t counters, size_t accs, uint32
                               float** acc);
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// h = bf16(silu(x.Wg^T) * x.Wu^T) [M, N]: one pass over both weights where the decode kernel
+// takes the layout, otherwise two products and the SiLU product, the up product held at byte
+// `up_offset` of the activation buffer.
+q38_status gate_up_run(q38_ctx* ctx, const void* x, int64_t M, int64_t K, q38_dtype x_dtype,
+                       const uint32_t* w_gate, const void* s_gate, const void* b_gate, const uint32_t* w_up,
+                       const void* s_up, const void* b_up, q38_dtype scales_dtype, int64_t N, int group_size, int bits,
+                       q38_mode mode, void* h, size_t up_offset);
+
+// out[t] = bf16(routed[t] + bf16(s_t * ys[t])) with s_t = bf16(sigmoid(bf16(x_t . dequant(wsg))))
+// for wsg a quantized [1, H] row: the shared-expert term of the sparse-MoE block.
+q38_status shared_combine_launch(q38_ctx* ctx, const void* x, int64_t T, int64_t H, const uint32_t* gw,
+                                 const void* gs, const void* gb, q38_dtype sd, int group, int bits, const void* ys,
+                                 const void* routed, void* out);
 
 // Driver entry point for cuTensorMapEncodeTiled (resolved once, no libcuda link).
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,

@@ -55,6 +55,7 @@ _sig("q38_ctx_check_device", [_P])
 _sig("q38_last_error", [_P], C.c_char_p)
 _sig("q38_ctx_test_wait_timeout", [_P, _I])
 _sig("q38_ctx_set_deterministic", [_P, _i])
+_sig("q38_ctx_set_ep_chunks", [_P, _i])
 _sig("q38_quantized_matmul", [_P, _P, _I, _I, _i, _P, _P, _P, _i, _I, _i, _i, _i, _i, _P])
 _sig("q38_quantized_embedding", [_P, _P, _I, _P, _P, _P, _i, _I, _I, _i, _i, _i, _P, _i])
 _sig("q38_hadamard_quantized_embedding", [_P, _P, _I, _P, _P, _P, _i, _I, _I, _i, _i, _i, _P, _i, _P])
@@ -92,6 +93,7 @@ _sig("q38_st_copy_block_to_device", [_P, _P, _I, _U64, _U64, _U64, _U64, _U64, _
 _sig("q38_switch_glu", [_P, _P, _I, _I, _I, _I, _i, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _i, _i, _i, _P])
 _sig("q38_sparse_moe", [_P, _P, _I, _I, _I, _I, _i, _i, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _i, _i, _i, _P, _P,
                         _P])
+_sig("q38_shared_expert", [_P, _P, _I, _I, _I] + [_P] * 12 + [_i, _i, _i, _P, _P])
 
 
 class _CommId(C.Structure):
@@ -189,6 +191,13 @@ def set_deterministic(on: bool = True, device=None) -> None:
     for `device`; off by default (arrival-order fp32 sums, about 1 us faster)."""
     ctx = context(device)
     _check(ctx, _lib.q38_ctx_set_deterministic(ctx, int(bool(on))))
+
+
+def set_ep_chunks(chunks: int = 0, device=None) -> None:
+    """Pieces of the expert-parallel exchange on this thread's context for `device` (1, 2
+    or 4; 0 lets the library choose).  Every rank must use the same setting."""
+    ctx = context(device)
+    _check(ctx, _lib.q38_ctx_set_ep_chunks(ctx, int(chunks)))
 
 
 def test_wait_timeout(limit_cycles: int, device=None) -> None:
@@ -752,14 +761,45 @@ class SwitchGLU:
 
 
 class SparseMoeBlock:
-    """Routed-expert part of Qwen4ExpSparseMoE.callAsFunction (FlashNext/Qwen4ExpSparseMoE.swift:275-294):
-    router (unquantized gate Linear, softmax, top-k, renormalisation) then SwitchGLU."""
+    """Qwen4ExpSparseMoE.callAsFunction (FlashNext/Qwen4ExpSparseMoE.swift:275-298): router
+    (unquantized gate Linear, softmax, top-k, renormalisation) then SwitchGLU; with
+    `shared_expert` (a QuantizedMLP) and `shared_expert_gate` (a QuantizedLinear [1, H]) the
+    output adds sigmoid(shared_expert_gate(x)) * shared_expert(x)."""
 
-    def __init__(self, router_weight: torch.Tensor, switch: SwitchGLU, top_k: int, normalize: bool = True):
+    def __init__(self, router_weight: torch.Tensor, switch: SwitchGLU, top_k: int, normalize: bool = True,
+                 shared_expert: "QuantizedMLP | None" = None, shared_expert_gate: "QuantizedLinear | None" = None):
+        if (shared_expert is None) != (shared_expert_gate is None):
+            raise Q38Error(1, "shared_expert and shared_expert_gate are given together")
         self.router_weight, self.switch, self.top_k, self.normalize = router_weight, switch, top_k, normalize
+        self.shared_expert, self.shared_expert_gate = shared_expert, shared_expert_gate
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        return sparse_moe(x, self.router_weight, self.switch, self.top_k, self.normalize)[0]
+        routed = sparse_moe(x, self.router_weight, self.switch, self.top_k, self.normalize)[0]
+        if self.shared_expert is None:
+            return routed
+        m = self.shared_expert
+        return shared_expert(x, routed, m.gate, m.up, m.down, self.shared_expert_gate, out=routed)
+
+
+def shared_expert(x: torch.Tensor, routed: torch.Tensor, gate: "QuantizedLinear", up: "QuantizedLinear",
+                  down: "QuantizedLinear", shared_gate: "QuantizedLinear", out: torch.Tensor | None = None):
+    """routed + sigmoid(shared_gate(x)) * down(silu(gate(x)) * up(x)) (q38_shared_expert), the
+    four projections quantized alike (group size, bits, scales dtype)."""
+    _need(x, "x"), _need(routed, "routed")
+    T, H = x.shape
+    I = gate.weight.shape[0]
+    layers = (gate, up, down, shared_gate)
+    if any((l.group_size, l.bits, l.scales.dtype) != (gate.group_size, gate.bits, gate.scales.dtype) for l in layers):
+        raise Q38Error(1, "shared_expert: the four projections must share group size, bits and scales dtype")
+    if out is None:
+        out = torch.empty_like(routed)
+    args = []
+    for l in layers:
+        args += [_ptr(_as_u32(l.weight)), _ptr(l.scales), _ptr(l.biases)]
+    ctx = _bind(x)
+    _check(ctx, _lib.q38_shared_expert(ctx, _ptr(x), T, H, I, *args, _DTYPE[gate.scales.dtype], gate.group_size,
+                                       gate.bits, _ptr(routed), _ptr(out)))
+    return out
 
 
 def sparse_moe(x: torch.Tensor, router_weight: torch.Tensor, switch: "SwitchGLU", top_k: int,
@@ -827,9 +867,10 @@ class Communicator:
 
 
 def tp_mlp(comm: Communicator, x: torch.Tensor, gate, up, down, group_size: int = 64, bits: int = 4,
-           chunks: int = 4) -> torch.Tensor:
+           chunks: int = 0) -> torch.Tensor:
     """Tensor-parallel gated MLP (q38_tp_mlp): gate/up this rank's output-row shards, down its
-    reduction-dimension shard; y [M, D] = the all-reduced sum on every rank."""
+    reduction-dimension shard; y [M, D] = the all-reduced sum on every rank.  chunks = 0 lets
+    the library choose the number of overlapped token pieces."""
     _need(x, "x")
     M, D = x.shape
     gw, gs, gb = gate

@@ -4,7 +4,7 @@ q38_ep_switch_glu), NCCL inside libq38.
 * One rank (world 1, any GPU count): the tensor-parallel MLP equals the single-device MLP
   within 2e-2 * RMS plus one bf16 step, and the expert-parallel SwitchGLU equals
   q38_switch_glu bit for bit (the exchange to itself moves bytes unchanged; rows past the
-  tokens carry only empty slots).
+  tokens carry only empty slots), the large capacities through the pipelined chunks.
 * A rank whose peer never joins: init gives up with Q38_ERR_COMM after its timeout, the
   communicator aborted, no GPU work involved.
 * Two GPUs (skipped with one): the id goes from rank 0 to rank 1 through a host queue;
@@ -54,13 +54,18 @@ def test_single_rank_tp_mlp_and_ep_switch_glu(q38):
         assert excess_over_step(y, full) <= 2e-2
         E, I, H, k, bits = 16, 512, 1024, 4, 3
         dev, _ = make_experts(q38, 9602, E, I, H, bits)
-        for T, cap in ((5, 5), (5, 9), (40, 64)):
+        # the large capacities also through 2 and 4 pipelined chunks of the exchange
+        for T, cap, pieces in ((5, 5, 0), (5, 9, 0), (40, 64, 0), (600, 1024, 2), (2048, 2048, 4)):
             xe = dev_bf16(O.normal_bf16(9603 + T, (T, H)))
             idx, sc = route_inputs(T, E, k, 9604 + T)
-            out = q38.ep_switch_glu(comm, xe, dev_i32(idx), dev_bf16(sc), *dev, E, cap, 64, bits)
+            q38.set_ep_chunks(pieces)
+            try:
+                out = q38.ep_switch_glu(comm, xe, dev_i32(idx), dev_bf16(sc), *dev, E, cap, 64, bits)
+            finally:
+                q38.set_ep_chunks(0)
             ref = q38.switch_glu(xe, dev_i32(idx), dev_bf16(sc), *dev, 64, bits)
             torch.cuda.synchronize()
-            assert torch.equal(out, ref), (T, cap)
+            assert torch.equal(out, ref), (T, cap, pieces)
         q38.check_device()
     finally:
         comm.destroy()
@@ -114,10 +119,13 @@ def _worker(rank, world, q_id, q_out):
         epr = E // world
         mine = [tuple(t[rank * epr:(rank + 1) * epr].contiguous() for t in trip) for trip in dev]
         errs = []
-        for T, cap in ((1, 1), (8, 8), (100 + 16 * rank, 160)):
+        for T, cap, pieces in ((1, 1, 0), (8, 8, 0), (100 + 16 * rank, 160, 0), (1500 + 16 * rank, 2048, 4),
+                               (1500 + 16 * rank, 2048, 0)):
             xe = dev_bf16(O.normal_bf16(9703 + T + rank, (T, H)))
             idx, sc = ri(T, E, k, 9704 + T + rank)
+            q38.set_ep_chunks(pieces)
             out = q38.ep_switch_glu(comm, xe, dev_i32(idx), dev_bf16(sc), *mine, E, cap, 64, bits)
+            q38.set_ep_chunks(0)
             ref = q38.switch_glu(xe, dev_i32(idx), dev_bf16(sc), *dev, 64, bits)
             errs.append(excess_over_step(out, ref))
         torch.cuda.synchronize()

@@ -22,7 +22,7 @@ import pytest
 import torch
 
 import oracle as O
-from test_qmm_gpu import dev_bf16, host_bf16
+from test_qmm_gpu import dev_bf16, dev_u32, host_bf16
 
 pytestmark = pytest.mark.gpu
 
@@ -376,3 +376,41 @@ def test_sparse_moe_equals_route_then_switch_glu(q38, flash_next, T):
     torch.cuda.synchronize()
     q38.check_device()
     assert torch.equal(idx, gi) and torch.equal(sc, gs) and torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("T", [1, 8, 64])
+@pytest.mark.parametrize("group,bits", [(32, 4), (64, 3), (64, 4)])
+def test_shared_expert(q38, T, group, bits):
+    """The shared-expert term of the sparse-MoE block at Flash-Next sizes (hidden 2048,
+    shared intermediate 512; the published checkpoint quantizes it 4-bit group 32), added to
+    a routed output, against the oracle's composition of bf16-rounded products."""
+    H, I = 2048, 512
+    mats = []
+    for i, (n, k) in enumerate(((I, H), (I, H), (H, I), (1, H))):
+        w = O.normal_f32(9100 + 10 * i + bits + group, (n, k), 0.02)
+        mats.append(O.quantize(w, group, bits))
+    x = O.normal_bf16(9150 + T, (T, H))
+    routed = O.normal_bf16(9160 + T, (T, H), 0.05)
+    # more than 16 tokens on the tensor-core path (group 64): bf16-rounded weight operands
+    ref = O.shared_expert(x, routed, *mats, group, bits, weights_bf16=T > 16 and group == 64)
+    lin = [q38.QuantizedLinear(dev_u32(c), dev_bf16(s), dev_bf16(b), None, group, bits) for c, s, b in mats]
+    out = q38.shared_expert(dev_bf16(x), dev_bf16(routed), *lin)
+    torch.cuda.synchronize()
+    q38.check_device()
+    check_close(host_bf16(out), O.bf16_to_f32(ref).astype(np.float64))
+    # in place on the routed buffer, through the block's own path
+    r = dev_bf16(routed)
+    q38.shared_expert(dev_bf16(x), r, *lin, out=r)
+    torch.cuda.synchronize()
+    assert torch.equal(r, out)
+
+
+def test_shared_expert_rejects_mixed_quantization(q38):
+    H, I = 512, 512
+    c, s, b = O.quantize(O.normal_f32(9190, (I, H), 0.02), 64, 4)
+    lin = q38.QuantizedLinear(dev_u32(c), dev_bf16(s), dev_bf16(b), None, 64, 4)
+    c3, s3, b3 = O.quantize(O.normal_f32(9191, (1, H), 0.02), 64, 3)
+    gate3 = q38.QuantizedLinear(dev_u32(c3), dev_bf16(s3), dev_bf16(b3), None, 64, 3)
+    x = dev_bf16(O.normal_bf16(9192, (2, H)))
+    with pytest.raises(q38.Q38Error):
+        q38.shared_expert(x, x, lin, lin, lin, gate3)
