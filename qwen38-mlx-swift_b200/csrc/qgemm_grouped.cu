@@ -429,51 +429,64 @@ __global__ void __launch_bounds__(256) moe_gather_kernel(const __nv_bfloat16* __
                                                          __nv_bfloat16* __restrict__ xs) {
     griddep_wait();
     griddep_launch_dependents();
-    // one 16-byte chunk (8 activations) per thread and step, consecutive threads on
-    // consecutive chunks of a row; a 64-group spans 8 lanes, and each of its 16-element
-    // quarters two neighbouring lanes, which swap their chunks to form the quarter's permuted
-    // words.  Grid-stride over the valid pairs only (the grid is sized for the GPU, not for
-    // every pair: most pairs of an expert-parallel exchange are empty slots); the stride is a
-    // multiple of the warp, so a lane pair always steps together.
+    // 16-byte chunks (8 activations each), consecutive lanes on consecutive chunks of a row;
+    // a 64-group spans 8 lanes, and each of its 16-element quarters two neighbouring lanes,
+    // which swap their chunks to form the quarter's permuted words.  Grid-stride over the
+    // valid pairs only (the grid is sized for the GPU, not for every pair: most pairs of an
+    // expert-parallel exchange are empty slots); runs start at multiples of the warp, so a
+    // lane pair always steps together.
     const int CH = H / 8;
     const int64_t n = static_cast<int64_t>(min(pairs, *valid)) * CH;  // pairs past *valid feed no tile
     const int lane = threadIdx.x & 31;
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31); base < n;
+    // each warp takes U runs of 32 consecutive chunks per step, their loads issued together
+    constexpr int U = 4;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * U;
+    for (int64_t base = (static_cast<int64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31)) * U; base < n;
          base += stride) {
-        const int64_t item = base + lane;
-        const bool live = item < n;
-        const int j = live ? static_cast<int>(item / CH) : 0, ch = live ? static_cast<int>(item % CH) : 0;
-        uint4 u = make_uint4(0u, 0u, 0u, 0u);
-        if (live) u = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(perm[j] / top_k) * H + ch * 8);
-        uint4 v;
-        v.x = __shfl_xor_sync(0xffffffffu, u.x, 1);
-        v.y = __shfl_xor_sync(0xffffffffu, u.y, 1);
-        v.z = __shfl_xor_sync(0xffffffffu, u.z, 1);
-        v.w = __shfl_xor_sync(0xffffffffu, u.w, 1);
-        if (!live) continue;
-        const bool odd = ch & 1;
-        const uint4 lo = odd ? v : u, hi = odd ? u : v;  // elements 0-7 and 8-15 of the quarter
-        const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-        float e[16];
+        uint4 u[U];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            e[2 * i] = bf16_bits_to_f32(w[i] & 0xFFFFu);
-            e[2 * i + 1] = bf16_bits_to_f32(w[i] >> 16);
+        for (int r = 0; r < U; ++r) {
+            const int64_t item = base + r * 32 + lane;
+            u[r] = make_uint4(0u, 0u, 0u, 0u);
+            if (item < n) {
+                const int j = static_cast<int>(item / CH), ch = static_cast<int>(item % CH);
+                u[r] = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(perm[j] / top_k) * H + ch * 8);
+            }
         }
-        uint32_t o[4];
-        if (odd) {
 #pragma unroll
-            for (int t = 0; t < 4; ++t)
-                o[t] = pack_bf16x2(e[tc_pair_code<BITS>(4 + t, 0)] * tc_pair_mult<BITS>(4 + t, 0),
-                                   e[tc_pair_code<BITS>(4 + t, 1)] * tc_pair_mult<BITS>(4 + t, 1));
-        } else {
+        for (int r = 0; r < U; ++r) {
+            const int64_t item = base + r * 32 + lane;
+            uint4 v;
+            v.x = __shfl_xor_sync(0xffffffffu, u[r].x, 1);
+            v.y = __shfl_xor_sync(0xffffffffu, u[r].y, 1);
+            v.z = __shfl_xor_sync(0xffffffffu, u[r].z, 1);
+            v.w = __shfl_xor_sync(0xffffffffu, u[r].w, 1);
+            if (item >= n) continue;
+            const int j = static_cast<int>(item / CH), ch = static_cast<int>(item % CH);
+            const bool odd = ch & 1;
+            const uint4 lo = odd ? v : u[r], hi = odd ? u[r] : v;  // elements 0-7 and 8-15 of the quarter
+            const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+            float e[16];
 #pragma unroll
-            for (int t = 0; t < 4; ++t)
-                o[t] = pack_bf16x2(e[tc_pair_code<BITS>(t, 0)] * tc_pair_mult<BITS>(t, 0),
-                                   e[tc_pair_code<BITS>(t, 1)] * tc_pair_mult<BITS>(t, 1));
+            for (int i = 0; i < 8; ++i) {
+                e[2 * i] = bf16_bits_to_f32(w[i] & 0xFFFFu);
+                e[2 * i + 1] = bf16_bits_to_f32(w[i] >> 16);
+            }
+            uint32_t o[4];
+            if (odd) {
+#pragma unroll
+                for (int t = 0; t < 4; ++t)
+                    o[t] = pack_bf16x2(e[tc_pair_code<BITS>(4 + t, 0)] * tc_pair_mult<BITS>(4 + t, 0),
+                                       e[tc_pair_code<BITS>(4 + t, 1)] * tc_pair_mult<BITS>(4 + t, 1));
+            } else {
+#pragma unroll
+                for (int t = 0; t < 4; ++t)
+                    o[t] = pack_bf16x2(e[tc_pair_code<BITS>(t, 0)] * tc_pair_mult<BITS>(t, 0),
+                                       e[tc_pair_code<BITS>(t, 1)] * tc_pair_mult<BITS>(t, 1));
+            }
+            *reinterpret_cast<uint4*>(xs + static_cast<size_t>(j) * H + ch * 8) =
+                make_uint4(o[0], o[1], o[2], o[3]);
         }
-        *reinterpret_cast<uint4*>(xs + static_cast<size_t>(j) * H + ch * 8) = make_uint4(o[0], o[1], o[2], o[3]);
     }
 }
 
@@ -481,11 +494,12 @@ q38_status moe_gather_launch(q38_ctx* ctx, const void* x, int H, const int32_t* 
                              const int32_t* valid, void* xs, int bits) {
     const long long items = static_cast<long long>(pairs) * (H / 8);
     const long long cap = static_cast<long long>(ctx->num_sms) * 8;  // 8 resident blocks per SM
+    const long long need = (items + 4 * 256 - 1) / (4 * 256);     // 4 chunks per thread and step
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(std::max(1LL, std::min(cap, (items + 255) / 256))));
+    cfg.gridDim = dim3(static_cast<unsigned>(std::max(1LL, std::min(cap, need))));
     cfg.blockDim = dim3(256);
     cfg.stream = ctx->stream;
     cfg.attrs = attr;

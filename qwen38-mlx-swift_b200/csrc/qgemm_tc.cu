@@ -1,5 +1,5 @@
 // Prefill-shaped MLX-affine quantized product on the 5th-generation tensor cores:
-// y[M,N] = x[M,K] . dequant(W)[N,K]^T for M > 16 tokens, group 64, K % 128 == 0,
+// y[M,N] = x[M,K] . dequant(W)[N,K]^T for M > 16 tokens, group 64 or 32, K % 128 == 0,
 // bits 2/3/4/8, bf16 activations and scales.  Replaces the Metal `qmm` kernel behind
 // MLX.quantizedMM (QuantizedLinear.callAsFunction,
 // Sources/Qwen38Core/FlashNext/Qwen4ExpPrequantized.swift:156-159) for prompt-sized inputs.
@@ -86,7 +86,7 @@ struct PArgs {
     int pack;  // f16 scales and biases in groups of 128 (direct scale loads only)
 };
 
-template <int BITS, bool SB_TMA>
+template <int BITS, bool SB_TMA, bool G32 = false>
 __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__ CUtensorMap map_x,
                                                         const __grid_constant__ CUtensorMap map_codes,
                                                         const __grid_constant__ CUtensorMap map_scales,
@@ -246,10 +246,12 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
         const uint32_t a_full_leader = mapa_shared(a_full, 0);
         // Scales and biases of the two groups of a stage come straight from global memory
         // (4 bytes each per row), loaded one stage of this set ahead.
-        const int G = a.K / 64;
-        auto sb_load = [&](int g, uint32_t& sv, uint32_t& bv) {
-            sv = 0u;
-            bv = 0u;
+        const int G = a.K / (G32 ? 32 : 64);
+        // sv/bv: the stage's two 64-code groups' scale and bias words (G32: each word the
+        // two 32-groups' values)
+        auto sb_load = [&](int g, uint2& sv, uint2& bv) {
+            sv = make_uint2(0u, 0u);
+            bv = make_uint2(0u, 0u);
             if (SB_TMA || g >= total) return;
             const int tile = pair + (g / ksteps) * npairs;
             const int n = (tile % a.nR) * (2 * P_ROWS) + rank * P_ROWS + row;
@@ -262,19 +264,28 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
                     const uint32_t v = __bfloat16_as_ushort(__float2bfloat16_rn(__half2float(__ushort_as_half(h))));
                     return v | (v << 16);
                 };
-                sv = cvt(__ldg(a.scales + off));
-                if (a.biases) bv = cvt(__ldg(a.biases + off));
+                const uint32_t sw = cvt(__ldg(a.scales + off)), bw = a.biases ? cvt(__ldg(a.biases + off)) : 0u;
+                sv = make_uint2(sw & 0xFFFFu, sw >> 16);
+                bv = make_uint2(bw & 0xFFFFu, bw >> 16);
                 return;
             }
-            const size_t off = static_cast<size_t>(n) * G + 2 * (g % ksteps);
-            sv = __ldg(reinterpret_cast<const unsigned int*>(a.scales + off));
-            if (a.biases) bv = __ldg(reinterpret_cast<const unsigned int*>(a.biases + off));
+            if constexpr (G32) {
+                const size_t off = static_cast<size_t>(n) * G + 4 * (g % ksteps);
+                sv = __ldg(reinterpret_cast<const uint2*>(a.scales + off));
+                if (a.biases) bv = __ldg(reinterpret_cast<const uint2*>(a.biases + off));
+            } else {
+                const size_t off = static_cast<size_t>(n) * G + 2 * (g % ksteps);
+                const uint32_t sw = __ldg(reinterpret_cast<const unsigned int*>(a.scales + off));
+                const uint32_t bw = a.biases ? __ldg(reinterpret_cast<const unsigned int*>(a.biases + off)) : 0u;
+                sv = make_uint2(sw & 0xFFFFu, sw >> 16);
+                bv = make_uint2(bw & 0xFFFFu, bw >> 16);
+            }
         };
-        uint32_t s_next, b_next;
+        uint2 s_next, b_next;
         sb_load(set, s_next, b_next);
         for (int gs = set; gs < total; gs += 2) {
             const int slot = gs % SW, as = gs % P_ASLOTS;
-            uint32_t s01 = s_next, b01 = b_next;
+            uint2 s01 = s_next, b01 = b_next;
             sb_load(gs + 2, s_next, b_next);
             if (!p_wait_warp<false>(&w_full[gs % (2 * SW)], (gs / (2 * SW)) & 1, ab)) break;
             // Dequantize into registers first: the TMEM slot is waited for only afterwards,
@@ -283,12 +294,14 @@ __global__ void __launch_bounds__(P_THREADS, 1) qgemm_tc(const __grid_constant__
             if (SB_TMA) {
                 const uint32_t* sb = reinterpret_cast<const uint32_t*>(st + F::CODE_B);
                 const int ks = gs % ksteps;
-                s01 = sb[row * 4 + (ks & 3)];
-                b01 = a.has_bias ? sb[512 + row * 4 + (ks & 3)] : 0u;
+                const uint32_t sw = sb[row * 4 + (ks & 3)];
+                const uint32_t bw = a.has_bias ? sb[512 + row * 4 + (ks & 3)] : 0u;
+                s01 = make_uint2(sw & 0xFFFFu, sw >> 16);
+                b01 = make_uint2(bw & 0xFFFFu, bw >> 16);
             }
             uint32_t av0[32], av1[32];
-            dequant_group<BITS>(st, row, 0, s01 & 0xFFFFu, b01 & 0xFFFFu, av0);
-            dequant_group<BITS>(st, row, 1, s01 >> 16, b01 >> 16, av1);
+            dequant_group<BITS, G32>(st, row, 0, s01.x, b01.x, av0);
+            dequant_group<BITS, G32>(st, row, 1, s01.y, b01.y, av1);
             __syncwarp();
             if (lane == 0) mbar_arrive(&w_empty[slot]);  // codes read; the slot may refill
             if (gs >= P_ASLOTS && !p_wait_warp<false>(&a_free[as], ((gs / P_ASLOTS) - 1) & 1, ab)) break;
@@ -341,7 +354,7 @@ struct PairLaunch {
     int max_pairs = 0;
 };
 
-template <int BITS, bool SB_TMA>
+template <int BITS, bool SB_TMA, bool G32>
 q38_status pair_config(q38_ctx* ctx, int smem, PairLaunch* out) {
     static std::mutex mu;
     static PairLaunch cached[64];
@@ -351,7 +364,7 @@ q38_status pair_config(q38_ctx* ctx, int smem, PairLaunch* out) {
         *out = cached[dev];
         return Q38_OK;
     }
-    auto kmain = qgemm_tc<BITS, SB_TMA>;
+    auto kmain = qgemm_tc<BITS, SB_TMA, G32>;
     if (cudaFuncSetAttribute(kmain, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
         return check_launch(ctx, "cudaFuncSetAttribute");
     cudaLaunchConfig_t cfg = {};
@@ -377,7 +390,7 @@ q38_status pair_config(q38_ctx* ctx, int smem, PairLaunch* out) {
     return Q38_OK;
 }
 
-template <int BITS, bool SB_TMA>
+template <int BITS, bool SB_TMA, bool G32 = false>
 q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, const void* s, const void* b,
                   int N, void* y, bool pack = false) {
     using F = PF<BITS, SB_TMA>;
@@ -398,7 +411,7 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
 
     static_assert(F::W_STAGES >= 4 && F::SMEM <= 227 * 1024, "prefill stages do not fit");
     PairLaunch pl;
-    if ((st = pair_config<BITS, SB_TMA>(ctx, F::SMEM, &pl)) != Q38_OK) return st;
+    if ((st = pair_config<BITS, SB_TMA, G32>(ctx, F::SMEM, &pl)) != Q38_OK) return st;
 
     const int nR = (N + 2 * P_ROWS - 1) / (2 * P_ROWS), nT = (M + P_TOK - 1) / P_TOK;
     const int ntiles = nR * nT;
@@ -441,7 +454,7 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
     cfg.stream = ctx->stream;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    if (cudaLaunchKernelEx(&cfg, qgemm_tc<BITS, SB_TMA>, mx, mc, ms, mb, args) != cudaSuccess)
+    if (cudaLaunchKernelEx(&cfg, qgemm_tc<BITS, SB_TMA, G32>, mx, mc, ms, mb, args) != cudaSuccess)
         return check_launch(ctx, "qgemm_tc");
     return check_launch(ctx, "qgemm_tc");
 }
@@ -453,8 +466,9 @@ bool qgemm_tc_supported(int64_t M, int64_t K, int group, int bits, q38_dtype xd,
     if (M < 17 || M > (1 << 24) || K % 128 != 0 || K <= 0 || K > (1 << 20)) return false;
     if (bits != 2 && bits != 3 && bits != 4 && bits != 8) return false;
     if (xd != Q38_BF16) return false;
-    // group 64 with bf16 scales, or the Bonsai 2 pack's group 128 with f16 scales (2 and 4 bits)
-    const bool std_layout = group == 64 && sd == Q38_BF16;
+    // groups of 64 or 32 with bf16 scales, or the Bonsai 2 pack's group 128 with f16 scales
+    // (2 and 4 bits)
+    const bool std_layout = (group == 64 || group == 32) && sd == Q38_BF16;
     const bool pack_layout = group == 128 && sd == Q38_F16 && (bits == 2 || bits == 4);
     if (!std_layout && !pack_layout) return false;
     auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
@@ -467,6 +481,14 @@ q38_status qgemm_tc_run(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const
     if (group == 128) {  // the pack layout: scales loaded directly by the dequantizing warps
         if (bits == 2) return launch<2, false>(ctx, x, m, k, w, s, b, n, y, true);
         return launch<4, false>(ctx, x, m, k, w, s, b, n, y, true);
+    }
+    if (group == 32) {  // scales and biases read by the dequantizing warps, 4 groups per stage
+        switch (bits) {
+            case 2: return launch<2, false, true>(ctx, x, m, k, w, s, b, n, y);
+            case 3: return launch<3, false, true>(ctx, x, m, k, w, s, b, n, y);
+            case 8: return launch<8, false, true>(ctx, x, m, k, w, s, b, n, y);
+            default: return launch<4, false, true>(ctx, x, m, k, w, s, b, n, y);
+        }
     }
     const bool tma_scales = k % 512 == 0;
     switch (bits) {

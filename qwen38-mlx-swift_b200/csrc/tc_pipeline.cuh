@@ -83,19 +83,22 @@ __device__ __forceinline__ uint32_t bf2_fma(uint32_t a, uint32_t b, uint32_t c) 
 }
 
 // Words of group gg (0/1) of the stage for this row -> exact bf16 weights (x 2^p) in
-// A-column order, 32 bf16x2 values.
-template <int BITS>
+// A-column order, 32 bf16x2 values.  sbits/bbits: the group's bf16 scale and bias; with G32
+// (quantization groups of 32) the two groups' values, the first 32 codes' in the low half.
+template <int BITS, bool G32 = false>
 __device__ __forceinline__ void dequant_group(const uint8_t* codes, int row, int gg, uint32_t sbits, uint32_t bbits,
                                               uint32_t* a) {
     using F = CodeLayout<BITS>;
+    // the scale and bias of the codes from 32 * half on
+    auto half_bits = [&](uint32_t v, int half) { return G32 ? (half ? v >> 16 : v & 0xFFFFu) : v; };
     if constexpr (BITS == 8) {
         // A byte permute places code q in the low mantissa bits of fp32 2^23, so that
         // subtracting 2^23 leaves q exactly; q pairs convert exactly to bf16x2, and
         // a = s * q + b is rounded once, as for the narrower widths.
-        const uint32_t s2 = sbits * 0x10001u, b2 = bbits * 0x10001u;
         const int swz = row & 7;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
+            const uint32_t s2 = half_bits(sbits, i >> 1) * 0x10001u, b2 = half_bits(bbits, i >> 1) * 0x10001u;
             const int c = gg * 4 + i;  // 16-byte chunk of the 128-byte row
             const uint4 v = *reinterpret_cast<const uint4*>(codes + row * 128 + ((c ^ swz) << 4));
             const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
@@ -138,15 +141,19 @@ __device__ __forceinline__ void dequant_group(const uint8_t* codes, int row, int
     }
     // s and 2^p b as bf16x2 with integer operations only: the scale broadcast, and the
     // bias times a power of two, exact in fp32 and so exactly the bf16 in its high half.
-    const uint32_t s2 = sbits * 0x10001u;
-    const float bf = bf16_bits_to_f32(bbits);
-    uint32_t b2[8];
+    uint32_t s2 = 0u, b2[8];
+    auto set_group = [&](int half) {
+        s2 = half_bits(sbits, half) * 0x10001u;
+        const float bf = bf16_bits_to_f32(half_bits(bbits, half));
 #pragma unroll
-    for (int q = 0; q < 8; ++q)
-        b2[q] = (__float_as_uint(bf * (1.0f / tc_pair_mult<BITS>(q, 0))) >> 16) |
-                (__float_as_uint(bf * (1.0f / tc_pair_mult<BITS>(q, 1))) & 0xFFFF0000u);
+        for (int q = 0; q < 8; ++q)
+            b2[q] = (__float_as_uint(bf * (1.0f / tc_pair_mult<BITS>(q, 0))) >> 16) |
+                    (__float_as_uint(bf * (1.0f / tc_pair_mult<BITS>(q, 1))) & 0xFFFF0000u);
+    };
+    set_group(0);
 #pragma unroll
     for (int tq = 0; tq < 4; ++tq) {
+        if (G32 && tq == 2) set_group(1);  // windows 2 and 3 hold codes 32-63
         uint32_t win[2];
         if constexpr (BITS == 2) {
             win[0] = w[tq];

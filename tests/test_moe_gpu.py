@@ -391,8 +391,8 @@ def test_shared_expert(q38, T, group, bits):
         mats.append(O.quantize(w, group, bits))
     x = O.normal_bf16(9150 + T, (T, H))
     routed = O.normal_bf16(9160 + T, (T, H), 0.05)
-    # more than 16 tokens on the tensor-core path (group 64): bf16-rounded weight operands
-    ref = O.shared_expert(x, routed, *mats, group, bits, weights_bf16=T > 16 and group == 64)
+    # more than 16 tokens on the tensor-core path: bf16-rounded weight operands
+    ref = O.shared_expert(x, routed, *mats, group, bits, weights_bf16=T > 16)
     lin = [q38.QuantizedLinear(dev_u32(c), dev_bf16(s), dev_bf16(b), None, group, bits) for c, s, b in mats]
     out = q38.shared_expert(dev_bf16(x), dev_bf16(routed), *lin)
     torch.cuda.synchronize()

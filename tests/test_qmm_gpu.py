@@ -279,6 +279,20 @@ def test_qmm_8bit_prompt_sizes(q38, M, N, K):
     q38.check_device()
 
 
+@pytest.mark.parametrize("bits", [2, 3, 4, 8])
+@pytest.mark.parametrize("M,N,K", [(300, 1024, 2048), (40, 640, 384)])
+def test_qmm_group32_prompt_sizes(q38, bits, M, N, K):
+    """Group 32 (the outer quantization of the published Flash-Next checkpoint) with more than
+    16 tokens: the tensor-core prompt product with two scales per 64-code group."""
+    c, s, b = make_weight(1700 + bits + M, N, K, bits, 32)
+    x = O.normal_bf16(1701 + M, (M, K))
+    ref = O.qmm(x, c, s, b, 32, bits, f32=True)
+    y = q38.quantized_matmul(dev_bf16(x), dev_u32(c), dev_bf16(s), dev_bf16(b), True, 32, bits)
+    torch.cuda.synchronize()
+    check_close(host_bf16(y), ref)
+    q38.check_device()
+
+
 @pytest.mark.parametrize("M", [1, 8, 64])
 @pytest.mark.parametrize("group,bits,xdt", [(32, 4, torch.bfloat16), (32, 3, torch.bfloat16),
                                             (64, 4, torch.float16), (128, 4, torch.bfloat16)])
