@@ -106,6 +106,10 @@ q38_status comm_fail(const char* fmt, ...) {
 }  // namespace
 }  // namespace q38
 
+// CTAs an NCCL operation of a communicator may occupy; the persistent kernels leave as many
+// SMs free while an exchange overlaps them, so neither waits for the other's blocks.
+constexpr int kCommMaxCtas = 16;
+
 struct q38_comm {
     ncclComm_t nc = nullptr;
     int rank = 0, world = 1, device = 0;
@@ -264,6 +268,16 @@ cudaLaunchConfig_t pdl_cfg(dim3 grid, dim3 block, cudaStream_t stream, cudaLaunc
     return cfg;
 }
 
+// Reserves SMs for the collectives of an overlapped phase; restores the context on exit.
+struct SmReserve {
+    q38_ctx* ctx;
+    int saved;
+    SmReserve(q38_ctx* c, bool on) : ctx(c), saved(c->sm_reserve) {
+        if (on) ctx->sm_reserve = std::min(kCommMaxCtas, ctx->num_sms / 2);
+    }
+    ~SmReserve() { ctx->sm_reserve = saved; }
+};
+
 }  // namespace
 }  // namespace q38
 
@@ -312,6 +326,7 @@ q38_status q38_comm_init_rank(const q38_comm_id* id, int world, int rank, int de
     memcpy(&u, id->bytes, sizeof(u));
     ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
     cfg.blocking = 0;  // returns at once; progress is polled against the deadline
+    cfg.maxCTAs = kCommMaxCtas;
     const ncclResult_t r = n.CommInitRankConfig(&c->nc, world, u, rank, &cfg);
     if (r != ncclSuccess && r != ncclInProgress) {
         cudaStreamDestroy(c->stream);
@@ -358,6 +373,7 @@ q38_status q38_comm_init_all(int ndev, const int* devices, int timeout_ms, q38_c
         cudaEventCreateWithFlags(&c->joined, cudaEventDisableTiming);
         ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
         cfg.blocking = 0;
+        cfg.maxCTAs = kCommMaxCtas;
         const ncclResult_t r = n.CommInitRankConfig(&c->nc, ndev, u, i, &cfg);
         cs[i] = c;
         if (r != ncclSuccess && r != ncclInProgress) bad = true;
@@ -440,6 +456,7 @@ q38_status q38_tp_mlp(q38_ctx* ctx, q38_comm* c, const void* x, int64_t M, int64
     uint8_t* hbuf = nullptr;
     if ((st = comm_buffer(ctx, c, static_cast<size_t>(M) * F_local * 2, &hbuf)) != Q38_OK) return st;
     const Nccl& n = nccl();
+    const SmReserve reserve(ctx, c->world > 1 && step < M);  // all-reduces beside the products
     size_t ev = 0;
     for (int64_t m0 = 0; m0 < M; m0 += step) {
         const int64_t mi = std::min(step, M - m0);
@@ -576,6 +593,7 @@ q38_status q38_ep_switch_glu(q38_ctx* ctx, q38_comm* c, const void* x, int64_t T
             return check_launch(ctx, "ep_switch_glu: stream ordering");
         return Q38_OK;
     };
+    const SmReserve reserve(ctx, NCH > 1);  // exchanges beside the experts' work
     if ((st = order(ctx->stream, c->stream)) != Q38_OK) return st;  // staging and metadata
     if ((st = dispatch(0)) != Q38_OK || (st = mark(0)) != Q38_OK) return st;
     for (int q = 0; q < NCH; ++q) {

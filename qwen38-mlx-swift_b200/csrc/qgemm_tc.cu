@@ -28,6 +28,7 @@
 // The extraction yields codes in a fixed permuted order, some pre-multiplied by 2^p; the
 // prologue kernel writes the activations permuted and scaled by 2^-p to match, so the
 // products pair up exactly: sum_k' (2^p w_k)(2^-p x_k) = sum_k w_k x_k.
+#include <algorithm>
 #include <mutex>
 
 #include "tc_pipeline.cuh"
@@ -415,7 +416,8 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
 
     const int nR = (N + 2 * P_ROWS - 1) / (2 * P_ROWS), nT = (M + P_TOK - 1) / P_TOK;
     const int ntiles = nR * nT;
-    const int pairs = ntiles < pl.max_pairs ? ntiles : pl.max_pairs;
+    const int avail = std::max(1, pl.max_pairs - (ctx->sm_reserve + 1) / 2);  // SM pairs free for this kernel
+    const int pairs = ntiles < avail ? ntiles : avail;
 
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
