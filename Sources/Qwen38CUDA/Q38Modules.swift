@@ -137,10 +137,14 @@ public final class Q38SparseMoE {
     public let router: Q38Tensor  // bf16 [E, H]
     public let gate: Q38QuantizedSwitchLinear, up: Q38QuantizedSwitchLinear, down: Q38QuantizedSwitchLinear
     public let topK: Int32, normalizeTopK: Bool
+    /// Qwen4ExpSharedExpert and shared_expert_gate ([1, H]); nil for a block without them.
+    public let sharedExpert: Q38QuantizedMLP?, sharedExpertGate: Q38QuantizedLinear?
     public init(router: Q38Tensor, gate: Q38QuantizedSwitchLinear, up: Q38QuantizedSwitchLinear,
-                down: Q38QuantizedSwitchLinear, topK: Int, normalizeTopK: Bool) {
+                down: Q38QuantizedSwitchLinear, topK: Int, normalizeTopK: Bool,
+                sharedExpert: Q38QuantizedMLP? = nil, sharedExpertGate: Q38QuantizedLinear? = nil) {
         self.router = router; self.gate = gate; self.up = up; self.down = down
         self.topK = Int32(topK); self.normalizeTopK = normalizeTopK
+        self.sharedExpert = sharedExpert; self.sharedExpertGate = sharedExpertGate
     }
     /// indices int32 [T, topK] and scores bf16 [T, topK] are scratch the caller provides.
     public func callAsFunction(_ ctx: Q38Context, _ x: Q38Tensor, indices: Q38Tensor, scores: Q38Tensor,
@@ -153,6 +157,16 @@ public final class Q38SparseMoE {
                                      up.weight.u32, up.scales.pointer, up.biases?.pointer,
                                      down.weight.u32, down.scales.pointer, down.biases?.pointer,
                                      Q38_BF16, gate.groupSize, gate.bits, out.pointer))
+        // + sigmoid(shared_expert_gate(x)) * sharedExpert(x), in place (Qwen4ExpSparseMoE.swift:295-298)
+        if let se = sharedExpert, let sg = sharedExpertGate {
+            try ctx.check(q38_shared_expert(ctx.handle, x.pointer, T, H, se.gate.outputDimensions,
+                                            se.gate.weight.u32, se.gate.scales.pointer, se.gate.biases?.pointer,
+                                            se.up.weight.u32, se.up.scales.pointer, se.up.biases?.pointer,
+                                            se.down.weight.u32, se.down.scales.pointer, se.down.biases?.pointer,
+                                            sg.weight.u32, sg.scales.pointer, sg.biases?.pointer,
+                                            se.gate.scales.dtype, se.gate.groupSize, se.gate.bits,
+                                            out.pointer, out.pointer))
+        }
     }
 }
 

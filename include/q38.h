@@ -424,11 +424,11 @@ Q38_API q38_status q38_comm_all_reduce(q38_ctx* ctx, q38_comm* comm, const void*
 /* Tensor-parallel gated MLP, y[M, D] = down(silu(gate(x)) * up(x)) summed over the ranks:
  * each rank holds gate and up split by output rows (F_local rows of [F, D*bits/32]) and
  * down split by its reduction dimension ([D, F_local*bits/32], whole groups and words),
- * computes its partial y and all-reduces it (bf16 sum).  The tokens are processed in
- * `chunks` pieces (whole 128-token tiles): the all-reduce of one piece runs on the
- * communicator's stream while the next piece computes; chunks <= 0 picks the count (1 to
- * 4) that keeps two waves of tensor-core tiles in each piece.  x, y bf16 [M, D] on every
- * rank. */
+ * computes its partial y and all-reduces it (bf16 sum).  h = silu(gate) * up is formed for
+ * all tokens in one pass; the down projection then runs in `chunks` pieces of whole
+ * 128-token tiles, the all-reduce of one piece on the communicator's stream while the next
+ * piece computes; chunks <= 0 picks the count (1 to 4) that keeps two waves of tensor-core
+ * tiles in each piece.  x, y bf16 [M, D] on every rank. */
 Q38_API q38_status q38_tp_mlp(q38_ctx* ctx, q38_comm* comm, const void* x, int64_t M, int64_t D,
                               const uint32_t* gate_w, const void* gate_s, const void* gate_b,
                               const uint32_t* up_w, const void* up_s, const void* up_b,

@@ -445,9 +445,10 @@ q38_status q38_tp_mlp(q38_ctx* ctx, q38_comm* c, const void* x, int64_t M, int64
     if (!x || !gate_w || !gate_s || !up_w || !up_s || !down_w || !down_s || !y)
         return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "tp_mlp: null pointer");
     if (chunks <= 0) {
-        // as many pieces as keep two waves of 256 x 256 gate tiles in each (a smaller piece
-        // leaves tensor cores idle for longer than its all-reduce overlaps), at most 4
-        const int64_t tiles = ((F_local + 255) / 256) * ((M + 255) / 256);
+        // as many pieces as keep two waves of 256 x 256 down-projection tiles in each (a
+        // smaller piece leaves tensor cores idle for longer than its all-reduce overlaps),
+        // at most 4
+        const int64_t tiles = ((D + 255) / 256) * ((M + 255) / 256);
         chunks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(4, tiles / std::max(1, ctx->num_sms))));
     }
     // chunks of whole 128-token tiles
@@ -456,21 +457,22 @@ q38_status q38_tp_mlp(q38_ctx* ctx, q38_comm* c, const void* x, int64_t M, int64
     uint8_t* hbuf = nullptr;
     if ((st = comm_buffer(ctx, c, static_cast<size_t>(M) * F_local * 2, &hbuf)) != Q38_OK) return st;
     const Nccl& n = nccl();
+    // h for all tokens in one pass (the gate/up products have the most tiles that way), then
+    // the down projection piece by piece, each piece's all-reduce beside the next piece
+    if ((st = q38_quantized_gate_up(ctx, x, M, D, Q38_BF16, gate_w, gate_s, gate_b, up_w, up_s, up_b, Q38_BF16,
+                                    F_local, group_size, bits, Q38_MODE_AFFINE, hbuf)) != Q38_OK)
+        return st;
     const SmReserve reserve(ctx, c->world > 1 && step < M);  // all-reduces beside the products
     size_t ev = 0;
     for (int64_t m0 = 0; m0 < M; m0 += step) {
         const int64_t mi = std::min(step, M - m0);
-        const uint8_t* xi = static_cast<const uint8_t*>(x) + static_cast<size_t>(m0) * D * 2;
-        uint8_t* hi = hbuf + static_cast<size_t>(m0) * F_local * 2;
+        const uint8_t* hi = hbuf + static_cast<size_t>(m0) * F_local * 2;
         uint8_t* yi = static_cast<uint8_t*>(y) + static_cast<size_t>(m0) * D * 2;
-        if ((st = q38_quantized_gate_up(ctx, xi, mi, D, Q38_BF16, gate_w, gate_s, gate_b, up_w, up_s, up_b, Q38_BF16,
-                                        F_local, group_size, bits, Q38_MODE_AFFINE, hi)) != Q38_OK)
-            return st;
         if ((st = q38_quantized_matmul(ctx, hi, mi, F_local, Q38_BF16, down_w, down_s, down_b, Q38_BF16, D, 1,
                                        group_size, bits, Q38_MODE_AFFINE, yi)) != Q38_OK)
             return st;
         if (c->world == 1) continue;
-        // the all-reduce of this chunk on the communicator's stream, after its products
+        // the all-reduce of this piece on the communicator's stream, after its product
         cudaEvent_t e = comm_event(c, ev++);
         if (!e || cudaEventRecord(e, ctx->stream) != cudaSuccess || cudaStreamWaitEvent(c->stream, e, 0) != cudaSuccess)
             return check_launch(ctx, "tp_mlp: stream ordering");

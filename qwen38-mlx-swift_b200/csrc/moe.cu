@@ -391,34 +391,32 @@ __global__ void __launch_bounds__(256) router_topk(const __nv_bfloat16* __restri
     topk_token<NJ, false>(logits, t, E, top_k, normalize, indices, scores, probs, lane);
 }
 
-// Router for a few tokens (decode) in one launch: every block computes the logits of 4
-// experts (one warp each, all NT >= T tokens from shared memory, eight 16-byte loads in
-// flight per lane), stores them as bf16, and counts itself done; the last block to finish
-// (device-scope fence, then an atomic counter that it returns to zero) runs the softmax and
-// top-k of every token.
-template <int NT, int NJ>
-__global__ void __launch_bounds__(128) router_decode(const __nv_bfloat16* __restrict__ x, int T, int H,
+// Router for a few tokens (decode) in one launch: block (b, t) computes the logits of
+// experts 4b..4b+3 for token t (one warp each, x_t staged in shared memory, eight 16-byte
+// loads in flight per lane), stores them as bf16, and counts itself done on token t's
+// counter; the last block of a token (device-scope fence, then the atomic count, which it
+// returns to zero) runs that token's softmax and top-k with its four warps.  The tokens'
+// selections thus run in parallel on different SMs.
+template <int NJ>
+__global__ void __launch_bounds__(128) router_decode(const __nv_bfloat16* __restrict__ x, int H,
                                                      const __nv_bfloat16* __restrict__ wr, int E, int top_k,
                                                      int normalize, __nv_bfloat16* __restrict__ logits,
                                                      int32_t* __restrict__ indices, __nv_bfloat16* __restrict__ scores,
-                                                     __nv_bfloat16* __restrict__ probs, unsigned int* counter) {
+                                                     __nv_bfloat16* __restrict__ probs, unsigned int* counters) {
     griddep_wait();  // inputs come from the previous kernel on the stream
     griddep_launch_dependents();
     extern __shared__ uint4 xs4[];
     __shared__ bool s_last;
+    const int t = blockIdx.y;
     const int vec = H / 8;
-    for (int i = threadIdx.x; i < NT * vec; i += 128) {
-        const int t = i / vec;
-        xs4[i] = t < T ? reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * H)[i % vec] : make_uint4(0, 0, 0, 0);
-    }
+    for (int i = threadIdx.x; i < vec; i += 128) xs4[i] = reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * H)[i];
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e = blockIdx.x * 4 + warp;
+    __nv_bfloat16* lt = logits + static_cast<size_t>(t) * E;
     if (e < E) {
         const uint4* wrow = reinterpret_cast<const uint4*>(wr + static_cast<size_t>(e) * H);
-        float acc[NT];
-#pragma unroll
-        for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+        float acc = 0.0f;
         for (int v0 = lane; v0 < vec; v0 += 32 * 8) {
             uint4 wu[8];
 #pragma unroll
@@ -428,44 +426,29 @@ __global__ void __launch_bounds__(128) router_decode(const __nv_bfloat16* __rest
                 const int v = v0 + 32 * i;
                 if (v >= vec) break;
                 const uint32_t q[4] = {wu[i].x, wu[i].y, wu[i].z, wu[i].w};
-                float wv[8];
+                const uint4 xu = xs4[v];
+                const uint32_t xq[4] = {xu.x, xu.y, xu.z, xu.w};
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    wv[2 * j] = bf16_bits_to_f32(q[j] & 0xFFFFu);
-                    wv[2 * j + 1] = bf16_bits_to_f32(q[j] >> 16);
-                }
-#pragma unroll
-                for (int t = 0; t < NT; ++t) {
-                    const uint4 xu = xs4[t * vec + v];
-                    const uint32_t xq[4] = {xu.x, xu.y, xu.z, xu.w};
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        acc[t] = fmaf(wv[2 * j], bf16_bits_to_f32(xq[j] & 0xFFFFu), acc[t]);
-                        acc[t] = fmaf(wv[2 * j + 1], bf16_bits_to_f32(xq[j] >> 16), acc[t]);
-                    }
+                    acc = fmaf(bf16_bits_to_f32(q[j] & 0xFFFFu), bf16_bits_to_f32(xq[j] & 0xFFFFu), acc);
+                    acc = fmaf(bf16_bits_to_f32(q[j] >> 16), bf16_bits_to_f32(xq[j] >> 16), acc);
                 }
             }
         }
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            float v = acc[t];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0 && t < T) logits[static_cast<size_t>(t) * E + e] = __float2bfloat16_rn(v);
-        }
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) lt[e] = __float2bfloat16_rn(acc);
     }
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) s_last = atomicAdd(counter, 1u) == gridDim.x - 1;
+    if (threadIdx.x == 0) s_last = atomicAdd(&counters[t], 1u) == gridDim.x - 1;
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    if (T == 1)
-        topk_token_block4<NJ>(logits, E, top_k, normalize, indices, scores, probs, warp, lane);
-    else
-        for (int t = warp; t < T; t += 4)
-            topk_token<NJ, true>(logits, t, E, top_k, normalize, indices, scores, probs, lane);
-    if (threadIdx.x == 0) atomicExch(counter, 0u);
+    topk_token_block4<NJ>(lt, E, top_k, normalize, indices + static_cast<size_t>(t) * top_k,
+                          scores + static_cast<size_t>(t) * top_k, probs ? probs + static_cast<size_t>(t) * E : nullptr,
+                          warp, lane);
+    if (threadIdx.x == 0) atomicExch(&counters[t], 0u);
 }
 
 // --------------------------------------------------------------------------- sort
@@ -1017,16 +1000,16 @@ q38_status logits_launch(q38_ctx* ctx, const void* x, int64_t T, int64_t H, cons
                       static_cast<int>(H), static_cast<int>(E), static_cast<__nv_bfloat16*>(logits), ctx->d_status);
 }
 
-// The one-launch router for up to 16 tokens (x staged whole in shared memory).
+// The one-launch router for up to 16 tokens (each block stages one token's x in shared
+// memory; one counter per token in the zero-at-rest region).
 q38_status route_decode_launch(q38_ctx* ctx, const void* x, int64_t T, int64_t H, const void* wr, int64_t E,
                                int top_k, int normalize, void* logits, int32_t* indices, void* scores, void* probs) {
     uint32_t* cnt = nullptr;
     float* unused = nullptr;
-    q38_status st = ensure_zero_region(ctx, 1, 0, &cnt, &unused);
+    q38_status st = ensure_zero_region(ctx, 16, 0, &cnt, &unused);
     if (st != Q38_OK) return st;
-    const int nt = T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : T <= 8 ? 8 : 16;
-    const size_t sm = static_cast<size_t>(2) * nt * H;
-    const dim3 grid(static_cast<unsigned>((E + 3) / 4));
+    const size_t sm = static_cast<size_t>(2) * H;
+    const dim3 grid(static_cast<unsigned>((E + 3) / 4), static_cast<unsigned>(T));
     auto go = [&](auto kern) -> q38_status {
         static std::mutex mu;
         static const void* done[64] = {};
@@ -1040,25 +1023,15 @@ q38_status route_decode_launch(q38_ctx* ctx, const void* x, int64_t T, int64_t H
             }
         }
         return launch_pdl(ctx, "router_decode", kern, grid, dim3(128), sm, static_cast<const __nv_bfloat16*>(x),
-                          static_cast<int>(T), static_cast<int>(H), static_cast<const __nv_bfloat16*>(wr),
-                          static_cast<int>(E), top_k, normalize, static_cast<__nv_bfloat16*>(logits), indices,
+                          static_cast<int>(H), static_cast<const __nv_bfloat16*>(wr), static_cast<int>(E), top_k,
+                          normalize, static_cast<__nv_bfloat16*>(logits), indices,
                           static_cast<__nv_bfloat16*>(scores), static_cast<__nv_bfloat16*>(probs),
                           reinterpret_cast<unsigned int*>(cnt));
     };
-    auto by_e = [&](auto nt_c) -> q38_status {
-        constexpr int NT = decltype(nt_c)::value;
-        if (E <= 128) return go(router_decode<NT, 4>);
-        if (E <= 256) return go(router_decode<NT, 8>);
-        if (E <= 512) return go(router_decode<NT, 16>);
-        return go(router_decode<NT, 32>);
-    };
-    switch (nt) {
-        case 1: return by_e(std::integral_constant<int, 1>());
-        case 2: return by_e(std::integral_constant<int, 2>());
-        case 4: return by_e(std::integral_constant<int, 4>());
-        case 8: return by_e(std::integral_constant<int, 8>());
-        default: return by_e(std::integral_constant<int, 16>());
-    }
+    if (E <= 128) return go(router_decode<4>);
+    if (E <= 256) return go(router_decode<8>);
+    if (E <= 512) return go(router_decode<16>);
+    return go(router_decode<32>);
 }
 
 // Scratch ints the sort needs beyond its outputs (per-block counts for large P).
@@ -1189,7 +1162,7 @@ q38_status q38_moe_route(q38_ctx* ctx, const void* x, int64_t T, int64_t H, q38_
     if (st != Q38_OK) return st;
     if ((st = ensure_workspace(ctx, static_cast<size_t>(T) * E * 2)) != Q38_OK) return st;
     void* logits = ctx->workspace;
-    if (T <= 16 && static_cast<size_t>(16) * H * 2 <= 96 * 1024) return route_decode_launch(ctx, x, T, H, wr, E, top_k,
+    if (T <= 16 && static_cast<size_t>(H) * 2 <= 96 * 1024) return route_decode_launch(ctx, x, T, H, wr, E, top_k,
                                                                                             normalize, logits, indices,
                                                                                             scores, probs);
     if ((st = logits_launch(ctx, x, T, H, wr, E, logits)) != Q38_OK) return st;
@@ -1358,7 +1331,7 @@ q38_status q38_sparse_moe(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
     if (!ctx) return Q38_ERR_INVALID_ARGUMENT;
     if (T == 0) return Q38_OK;
     if (!indices || !scores) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "sparse_moe: indices and scores are required");
-    const bool decode = T <= 16 && H > 0 && static_cast<size_t>(16) * H * 2 <= 96 * 1024 && E >= 1 && E <= 1024 &&
+    const bool decode = T <= 16 && H > 0 && static_cast<size_t>(H) * 2 <= 96 * 1024 && E >= 1 && E <= 1024 &&
                         top_k >= 1 && top_k <= 32 && top_k <= E && dtype == Q38_BF16 && x && wr && aligned16(x) &&
                         aligned16(wr) &&
                         qgemv_moe_supported(T, H, I, E, top_k, group_size, bits, x, gate_w, gate_s, gate_b, up_w,

@@ -278,6 +278,11 @@ struct MainArgs {
     const float* signs;
     int rot;
     float rot_scale;
+    // MODE_MOE_DOWN of the decode SwitchGLU: the indices come from the router two kernels
+    // back, which has completed before this grid can start (the gate/up kernel triggers its
+    // dependents only after waiting for the router), so the plan is built and the weights
+    // stream before the wait for h.
+    int early_plan;
 };
 
 // The rotation of an activation product: hadamardRotate's arguments.
@@ -724,7 +729,7 @@ __global__ void __launch_bounds__(THREADS, WG == 1 && TB == 1 ? 3 : 2) qgemv_mai
     const int8_t* slot_tab = nullptr;
     int tiles = a.tiles;
     if constexpr (MOE) {
-        griddep_wait();
+        if (!(MODE == MODE_MOE_DOWN && a.early_plan)) griddep_wait();
         uint8_t* plan = smem + a.plan_off;
         uint32_t* bits = reinterpret_cast<uint32_t*>(plan + PLAN_BITS);
         int* pre = reinterpret_cast<int*>(plan + PLAN_PRE);
@@ -736,7 +741,7 @@ __global__ void __launch_bounds__(THREADS, WG == 1 && TB == 1 ? 3 : 2) qgemv_mai
         __syncthreads();
         bool bad = false;
         for (int i = threadIdx.x; i < a.P; i += blockDim.x) {
-            const int e = a.idx[i];
+            const int e = __ldcg(a.idx + i);  // past L1: written by another grid
             if (e >= 0 && e < a.E)
                 atomicOr(&bits[e >> 5], 1u << (e & 31));
             else if (e != -1)
@@ -763,7 +768,7 @@ __global__ void __launch_bounds__(THREADS, WG == 1 && TB == 1 ? 3 : 2) qgemv_mai
         }
         __syncthreads();
         for (int i = threadIdx.x; i < a.P; i += blockDim.x) {
-            const int e = a.idx[i];
+            const int e = __ldcg(a.idx + i);
             if (e < 0 || e >= a.E) continue;
             const int j = pre[e >> 5] + __popc(bits[e >> 5] & ((1u << (e & 31)) - 1u));
             slw[j * MOE_MAX_T + i / a.topk] = static_cast<int8_t>(i % a.topk);
@@ -879,6 +884,9 @@ __global__ void __launch_bounds__(THREADS, WG == 1 && TB == 1 ? 3 : 2) qgemv_mai
         // ------------------------------------------------------------ activation warp
         // x is written by the previous kernel on the stream: wait for it to complete.
         if constexpr (!MOE) griddep_wait();
+        if constexpr (MODE == MODE_MOE_DOWN) {
+            if (a.early_plan) griddep_wait();  // h comes from the previous kernel
+        }
         StageCursor cur{st_first / tiles, st_first % tiles, tiles};
         int ci = -1, key = -1;
         for (int i = 0; i < nst; ++i, cur.next()) {
@@ -1569,6 +1577,7 @@ q38_status launch_moe_decode(q38_ctx* ctx, const void* x, int T, int H, int I, i
         d.rpe = H;
         d.tpe = H / 64;
         d.ld = H;
+        d.early_plan = 1;
         e = launch_main<BITS, MP, TB, false, MODE_MOE_DOWN>(pd, ctx->device, ctx->num_sms, md, md, d,
                                                             static_cast<long long>(pd.tiles) * pd.C * 4, ctx->stream);
     }
