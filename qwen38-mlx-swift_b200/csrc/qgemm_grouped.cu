@@ -438,31 +438,34 @@ __global__ void __launch_bounds__(256) moe_gather_kernel(const __nv_bfloat16* __
     const int CH = H / 8;
     const int64_t n = static_cast<int64_t>(min(pairs, *valid)) * CH;  // pairs past *valid feed no tile
     const int lane = threadIdx.x & 31;
-    // each warp takes U runs of 32 consecutive chunks per step, their loads issued together
+    // each warp takes U runs of 32 consecutive chunks per step, their loads issued together;
+    // a run lies in one row (CH is a multiple of 64), found by one division per step
     constexpr int U = 4;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * U;
     for (int64_t base = (static_cast<int64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31)) * U; base < n;
          base += stride) {
+        const int j0 = static_cast<int>(base / CH), c0 = static_cast<int>(base - static_cast<int64_t>(j0) * CH);
+        int jr[U], chr[U];
         uint4 u[U];
 #pragma unroll
         for (int r = 0; r < U; ++r) {
-            const int64_t item = base + r * 32 + lane;
+            const int cc = c0 + r * 32;
+            const int dj = cc / CH;
+            jr[r] = j0 + dj;
+            chr[r] = cc - dj * CH + lane;
             u[r] = make_uint4(0u, 0u, 0u, 0u);
-            if (item < n) {
-                const int j = static_cast<int>(item / CH), ch = static_cast<int>(item % CH);
-                u[r] = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(perm[j] / top_k) * H + ch * 8);
-            }
+            if (base + r * 32 < n)
+                u[r] = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(perm[jr[r]] / top_k) * H + chr[r] * 8);
         }
 #pragma unroll
         for (int r = 0; r < U; ++r) {
-            const int64_t item = base + r * 32 + lane;
             uint4 v;
             v.x = __shfl_xor_sync(0xffffffffu, u[r].x, 1);
             v.y = __shfl_xor_sync(0xffffffffu, u[r].y, 1);
             v.z = __shfl_xor_sync(0xffffffffu, u[r].z, 1);
             v.w = __shfl_xor_sync(0xffffffffu, u[r].w, 1);
-            if (item >= n) continue;
-            const int j = static_cast<int>(item / CH), ch = static_cast<int>(item % CH);
+            if (base + r * 32 >= n) continue;  // whole runs: n is a multiple of CH
+            const int j = jr[r], ch = chr[r];
             const bool odd = ch & 1;
             const uint4 lo = odd ? v : u[r], hi = odd ? u[r] : v;  // elements 0-7 and 8-15 of the quarter
             const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
@@ -493,7 +496,7 @@ __global__ void __launch_bounds__(256) moe_gather_kernel(const __nv_bfloat16* __
 q38_status moe_gather_launch(q38_ctx* ctx, const void* x, int H, const int32_t* perm, int pairs, int top_k,
                              const int32_t* valid, void* xs, int bits) {
     const long long items = static_cast<long long>(pairs) * (H / 8);
-    const long long cap = static_cast<long long>(ctx->num_sms) * 8;  // 8 resident blocks per SM
+    const long long cap = static_cast<long long>(ctx->num_sms) * 32;  // 4 waves of 8 resident blocks per SM
     const long long need = (items + 4 * 256 - 1) / (4 * 256);     // 4 chunks per thread and step
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
