@@ -1118,20 +1118,21 @@ def run_profile_case(args):
 
 
 def run_profile_prefill(args):
-    """Small prompt-shaped case for ncu: 4-bit, M=1024 tokens, N=9472 (37 row pairs x 4 token
-    tiles = 148 pair tiles), K=5120; 3 products."""
+    """Small prompt-shaped case for ncu: `--profile-bits` codes, M=1024 tokens, N=9472 (37 row
+    pairs x 4 token tiles = 148 pair tiles), K=5120; 3 products."""
     import torch
     import q38
     dev = torch.device("cuda", 0)
-    M, N, K = 1024, 9472, 5120
+    M, N, K, bits = 1024, 9472, 5120, args.profile_bits
     g = torch.Generator(device=dev).manual_seed(5050)
-    c, s, b = q38.quantize(torch.randn((N, K), generator=g, device=dev) * 0.02, GROUP, 4, scales_dtype=torch.bfloat16)
+    c, s, b = q38.quantize(torch.randn((N, K), generator=g, device=dev) * 0.02, GROUP, bits,
+                           scales_dtype=torch.bfloat16)
     x = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
     for _ in range(3):
-        y = q38.quantized_matmul(x, c.view(torch.int32), s, b, True, GROUP, 4)
+        y = q38.quantized_matmul(x, c.view(torch.int32), s, b, True, GROUP, bits)
     torch.cuda.synchronize()
     q38.check_device()
-    print(json.dumps({"profile_prefill": {"M": M, "N": N, "K": K, "bits": 4, "launches": 3,
+    print(json.dumps({"profile_prefill": {"M": M, "N": N, "K": K, "bits": bits, "launches": 3,
                                           "flops_per_launch": 2 * M * N * K, "mean_abs_y": float(y.float().abs().mean())}}))
 
 

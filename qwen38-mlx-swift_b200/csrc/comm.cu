@@ -106,10 +106,6 @@ q38_status comm_fail(const char* fmt, ...) {
 }  // namespace
 }  // namespace q38
 
-// CTAs an NCCL operation of a communicator may occupy; the persistent kernels leave as many
-// SMs free while an exchange overlaps them, so neither waits for the other's blocks.
-constexpr int kCommMaxCtas = 16;
-
 struct q38_comm {
     ncclComm_t nc = nullptr;
     int rank = 0, world = 1, device = 0;
@@ -268,16 +264,6 @@ cudaLaunchConfig_t pdl_cfg(dim3 grid, dim3 block, cudaStream_t stream, cudaLaunc
     return cfg;
 }
 
-// Reserves SMs for the collectives of an overlapped phase; restores the context on exit.
-struct SmReserve {
-    q38_ctx* ctx;
-    int saved;
-    SmReserve(q38_ctx* c, bool on) : ctx(c), saved(c->sm_reserve) {
-        if (on) ctx->sm_reserve = std::min(kCommMaxCtas, ctx->num_sms / 2);
-    }
-    ~SmReserve() { ctx->sm_reserve = saved; }
-};
-
 }  // namespace
 }  // namespace q38
 
@@ -326,7 +312,6 @@ q38_status q38_comm_init_rank(const q38_comm_id* id, int world, int rank, int de
     memcpy(&u, id->bytes, sizeof(u));
     ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
     cfg.blocking = 0;  // returns at once; progress is polled against the deadline
-    cfg.maxCTAs = kCommMaxCtas;
     const ncclResult_t r = n.CommInitRankConfig(&c->nc, world, u, rank, &cfg);
     if (r != ncclSuccess && r != ncclInProgress) {
         cudaStreamDestroy(c->stream);
@@ -373,7 +358,6 @@ q38_status q38_comm_init_all(int ndev, const int* devices, int timeout_ms, q38_c
         cudaEventCreateWithFlags(&c->joined, cudaEventDisableTiming);
         ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
         cfg.blocking = 0;
-        cfg.maxCTAs = kCommMaxCtas;
         const ncclResult_t r = n.CommInitRankConfig(&c->nc, ndev, u, i, &cfg);
         cs[i] = c;
         if (r != ncclSuccess && r != ncclInProgress) bad = true;
@@ -445,10 +429,10 @@ q38_status q38_tp_mlp(q38_ctx* ctx, q38_comm* c, const void* x, int64_t M, int64
     if (!x || !gate_w || !gate_s || !up_w || !up_s || !down_w || !down_s || !y)
         return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "tp_mlp: null pointer");
     if (chunks <= 0) {
-        // as many pieces as keep two waves of 256 x 256 down-projection tiles in each (a
-        // smaller piece leaves tensor cores idle for longer than its all-reduce overlaps),
-        // at most 4
-        const int64_t tiles = ((D + 255) / 256) * ((M + 255) / 256);
+        // as many pieces as keep four waves of 256 x 256 down-projection tiles in each (a
+        // smaller piece leaves tensor cores idle, and its all-reduce's blocks slow the next
+        // piece, for longer than the overlap gains), at most 4
+        const int64_t tiles = ((D + 255) / 256) * ((M + 255) / 256) / 2;
         chunks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(4, tiles / std::max(1, ctx->num_sms))));
     }
     // chunks of whole 128-token tiles
@@ -462,7 +446,6 @@ q38_status q38_tp_mlp(q38_ctx* ctx, q38_comm* c, const void* x, int64_t M, int64
     if ((st = q38_quantized_gate_up(ctx, x, M, D, Q38_BF16, gate_w, gate_s, gate_b, up_w, up_s, up_b, Q38_BF16,
                                     F_local, group_size, bits, Q38_MODE_AFFINE, hbuf)) != Q38_OK)
         return st;
-    const SmReserve reserve(ctx, c->world > 1 && step < M);  // all-reduces beside the products
     size_t ev = 0;
     for (int64_t m0 = 0; m0 < M; m0 += step) {
         const int64_t mi = std::min(step, M - m0);
@@ -595,7 +578,6 @@ q38_status q38_ep_switch_glu(q38_ctx* ctx, q38_comm* c, const void* x, int64_t T
             return check_launch(ctx, "ep_switch_glu: stream ordering");
         return Q38_OK;
     };
-    const SmReserve reserve(ctx, NCH > 1);  // exchanges beside the experts' work
     if ((st = order(ctx->stream, c->stream)) != Q38_OK) return st;  // staging and metadata
     if ((st = dispatch(0)) != Q38_OK || (st = mark(0)) != Q38_OK) return st;
     for (int q = 0; q < NCH; ++q) {

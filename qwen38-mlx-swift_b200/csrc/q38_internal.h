@@ -32,9 +32,6 @@ struct q38_ctx {
     uint32_t* d_status = nullptr;  // device status word (timeouts)
     int deterministic = 0;  // decode products: ordered chunk sums (bitwise reproducible)
     int ep_chunks = 0;      // pieces of the expert-parallel exchange (0: the library's choice)
-    // SMs the persistent tensor-core kernels leave free while collectives run beside them
-    // on another stream (set by the multi-GPU entries around their overlapped phases)
-    int sm_reserve = 0;
     // Pinned host staging of the safetensors reader: two halves used alternately, each
     // guarded by an event of its last host->device copy.
     void* host_stage = nullptr;

@@ -373,7 +373,7 @@ q38_status launch_grouped_xr(q38_ctx* ctx, const GroupedProblem& p) {
     args.rows_per_expert = p.rows_per_expert;
     args.out_ld = p.out_ld;
     args.has_bias = p.b0 != nullptr;
-    int grid = ctx->num_sms - ctx->sm_reserve;
+    int grid = ctx->num_sms;
     if (grid > p.max_tiles) grid = p.max_tiles;
     if (grid < 1) grid = 1;
     cudaLaunchAttribute attr[1];

@@ -57,7 +57,7 @@ struct PF {
     static constexpr int CODE_B = P_ROWS * CODE_W * 4;       // 4 / 6 / 8 KiB
     static constexpr int X_B = 2 * P_HTOK * 128;          // two 64-element 128-byte-swizzled boxes
     static constexpr int W_STAGE = (CODE_B + (SB_TMA ? 4096 : 0) + 1023) / 1024 * 1024;
-    static constexpr int X_STAGES = 5;
+    static constexpr int X_STAGES = BITS == 8 ? 4 : 5;  // 8-bit: room for six 16 KiB weight stages
     static constexpr int W_STAGES_MAX = (227 * 1024 - 2048 - X_STAGES * X_B) / W_STAGE;
     static constexpr int W_STAGES = W_STAGES_MAX > 8 ? 8 : W_STAGES_MAX;
     static constexpr int SMEM = 2048 + X_STAGES * X_B + W_STAGES * W_STAGE;
@@ -416,8 +416,7 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
 
     const int nR = (N + 2 * P_ROWS - 1) / (2 * P_ROWS), nT = (M + P_TOK - 1) / P_TOK;
     const int ntiles = nR * nT;
-    const int avail = std::max(1, pl.max_pairs - (ctx->sm_reserve + 1) / 2);  // SM pairs free for this kernel
-    const int pairs = ntiles < avail ? ntiles : avail;
+    const int pairs = ntiles < pl.max_pairs ? ntiles : pl.max_pairs;
 
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
