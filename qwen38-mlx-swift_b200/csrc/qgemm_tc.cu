@@ -57,7 +57,7 @@ struct PF {
     static constexpr int CODE_B = P_ROWS * CODE_W * 4;       // 4 / 6 / 8 KiB
     static constexpr int X_B = 2 * P_HTOK * 128;          // two 64-element 128-byte-swizzled boxes
     static constexpr int W_STAGE = (CODE_B + (SB_TMA ? 4096 : 0) + 1023) / 1024 * 1024;
-    static constexpr int X_STAGES = BITS == 8 ? 4 : 5;  // 8-bit: room for six 16 KiB weight stages
+    static constexpr int X_STAGES = BITS == 8 ? 4 : 5;  // 8-bit: room for four or more 16 KiB weight stages
     static constexpr int W_STAGES_MAX = (227 * 1024 - 2048 - X_STAGES * X_B) / W_STAGE;
     static constexpr int W_STAGES = W_STAGES_MAX > 8 ? 8 : W_STAGES_MAX;
     static constexpr int SMEM = 2048 + X_STAGES * X_B + W_STAGES * W_STAGE;
@@ -495,8 +495,7 @@ q38_status qgemm_tc_run(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const
     switch (bits) {
         case 2: return tma_scales ? launch<2, true>(ctx, x, m, k, w, s, b, n, y) : launch<2, false>(ctx, x, m, k, w, s, b, n, y);
         case 3: return tma_scales ? launch<3, true>(ctx, x, m, k, w, s, b, n, y) : launch<3, false>(ctx, x, m, k, w, s, b, n, y);
-        // 8-bit stages (16 KiB of codes) leave room for four weight stages only without the scale boxes
-        case 8: return launch<8, false>(ctx, x, m, k, w, s, b, n, y);
+        case 8: return tma_scales ? launch<8, true>(ctx, x, m, k, w, s, b, n, y) : launch<8, false>(ctx, x, m, k, w, s, b, n, y);
         default: return tma_scales ? launch<4, true>(ctx, x, m, k, w, s, b, n, y) : launch<4, false>(ctx, x, m, k, w, s, b, n, y);
     }
 }
