@@ -1234,6 +1234,8 @@ q38_status q38_switch_glu(q38_ctx* ctx, const void* x, int64_t T, int64_t H, int
                                 down_w, down_s, down_b, bits, out);
     const int rb_gu = static_cast<int>(I / 64), rb_d = static_cast<int>(H / 128);
     // An expert receives at most one pair per token, so runs never exceed T pairs.
+    // (Runs of at most 96 pairs, for a deeper activation ring at a mean run of 80, measured
+    // slower at 4096 tokens: 701 -> 728 us per layer.)
     const int xr = T <= 32 ? 32 : T <= 64 ? 64 : 128;
     const int64_t max_runs = std::min<int64_t>(E, P) + P / xr + 1;
     size_t off = 0;
