@@ -100,8 +100,9 @@ def _worker(rank, world, q_id, q_out):
     comm = q38.Communicator(uid, world, rank, rank, timeout_ms=60000)
     try:
         from test_moe_gpu import make_experts as mk, route_inputs as ri
-        # tensor parallel: this rank's shards of the same full weights on every rank
-        D, F = 1024, 2048
+        # tensor parallel at the dense-27B MLP's width (D 5120, F 17408): this rank's shards
+        # of the same full weights on every rank
+        D, F = 5120, 17408
         ws = mlp_weights(q38, 9700, D, F)
         Fl = F // world
         gate = tuple(t[rank * Fl:(rank + 1) * Fl].contiguous() for t in ws[0])
@@ -111,6 +112,8 @@ def _worker(rank, world, q_id, q_out):
                 ws[2][2][:, rank * Fl // 64:(rank + 1) * Fl // 64].contiguous())
         x = dev_bf16(O.normal_bf16(9701, (384, D)))
         y = q38.tp_mlp(comm, x, gate, up, down, 64, 4, chunks=3)
+        y0 = q38.tp_mlp(comm, x, gate, up, down, 64, 4)  # the library's piece count
+        assert torch.equal(y, y0)
         full = q38.quantized_matmul(q38.quantized_gate_up(x, ws[0], ws[1], 64, 4), *ws[2], True, 64, 4)
         tp_err = excess_over_step(y, full)
         # expert parallel
