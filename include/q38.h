@@ -439,12 +439,14 @@ Q38_API q38_status q38_tp_mlp(q38_ctx* ctx, q38_comm* comm, const void* x, int64
  * experts split contiguously over the ranks (this rank holds experts [rank*E/world,
  * (rank+1)*E/world): gate/up [E/world, I, H*bits/32], down [E/world, H, I*bits/32]).  x
  * [T, H], indices/scores [T, top_k] (global expert ids, from this rank's router) and out
- * [T, H] are this rank's tokens.  Fixed capacity: every rank sends `capacity` rows
- * (T <= capacity, the same capacity on every rank) to every rank, so the exchange sizes
- * are known in advance and nothing is read back to the host (the call can be captured in
- * a CUDA graph); a token's row carries the rank-local expert of each slot, or -1 where the
- * expert lives on another rank.  out_t = bf16(sum, in rank order, of the partial sums of
- * the ranks that own one of the token's experts). */
+ * [T, H] are this rank's tokens.  Fixed capacity: every rank contributes `capacity` rows
+ * (T <= capacity, the same capacity on every rank; rows past T carry empty slots), so the
+ * exchange sizes are known in advance and nothing is read back to the host (the call can
+ * be captured in a CUDA graph).  The rows, slot experts and scores of all ranks are
+ * all-gathered; each rank runs its own experts over every row (the slots of other ranks'
+ * experts are empty), and a bf16 reduce-scatter sums the ranks' partial outputs into each
+ * token's home rank: out_t = the sum over ranks of bf16(sum of that rank's slots), added
+ * in NCCL's order. */
 Q38_API q38_status q38_ep_switch_glu(q38_ctx* ctx, q38_comm* comm, const void* x, int64_t T, int64_t H, int64_t I,
                                      int64_t E, int top_k, const int32_t* indices, const void* scores,
                                      const uint32_t* gate_w, const void* gate_s, const void* gate_b,

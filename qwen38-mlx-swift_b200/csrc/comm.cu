@@ -7,13 +7,12 @@
 //                      chunk i (on the communicator's stream) runs while chunk i+1 computes.
 //   q38_ep_switch_glu  the routed experts of the Flash-Next MoE layer
 //                      (Sources/Qwen38Core/FlashNext/Qwen4ExpSparseMoE.swift:275-294) split
-//                      expert-parallel: every rank sends each of its tokens once to every
-//                      rank (fixed capacity, so all exchange sizes are known in advance and
-//                      nothing is read back to the host), with the rank-local expert of each
-//                      slot or -1; the receiving rank runs SwitchGLU over its own experts
-//                      (q38_switch_glu), the partial sums come back and the home rank adds the
-//                      partials of the ranks that own one of the token's experts, in rank
-//                      order.
+//                      expert-parallel: every rank's tokens (a fixed capacity of rows, so all
+//                      exchange sizes are known in advance and nothing is read back to the
+//                      host) are all-gathered with their slot experts and scores; each rank
+//                      runs SwitchGLU over its own experts on every row (q38_switch_glu, the
+//                      other ranks' slots empty) and a bf16 reduce-scatter sums the partial
+//                      outputs into each token's home rank.
 //
 // NCCL is loaded at run time (dlopen of libnccl.so.2; the copy already in the process is
 // reused), so the library has no link-time dependency on it.  Communicators are created
@@ -47,6 +46,8 @@ struct Nccl {
     ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
     ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
     ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*ReduceScatter)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
     ncclResult_t (*GroupStart)();
     ncclResult_t (*GroupEnd)();
     const char* (*GetErrorString)(ncclResult_t);
@@ -82,6 +83,8 @@ const Nccl& nccl() {
         sym(n.AllReduce, "ncclAllReduce");
         sym(n.Send, "ncclSend");
         sym(n.Recv, "ncclRecv");
+        sym(n.AllGather, "ncclAllGather");
+        sym(n.ReduceScatter, "ncclReduceScatter");
         sym(n.GroupStart, "ncclGroupStart");
         sym(n.GroupEnd, "ncclGroupEnd");
         sym(n.GetErrorString, "ncclGetErrorString");
@@ -188,67 +191,28 @@ cudaEvent_t comm_event(q38_comm* c, size_t i) {
 }
 
 // ------------------------------------------------------------------ EP kernels
-// Slot metadata of the fixed-capacity exchange: for destination rank r and row t < C,
-// the rank-local expert of each slot of token t (or -1: its expert lives elsewhere, or t is
-// past this rank's tokens) and the slot's router score.
-__global__ void __launch_bounds__(256) ep_fixed_meta(const int32_t* __restrict__ idx,
-                                                     const __nv_bfloat16* __restrict__ scores, int T, int C, int k,
-                                                     int E, int epr, int W, int32_t* __restrict__ ids,
-                                                     __nv_bfloat16* __restrict__ sc) {
+// This rank's slot metadata for the gather: rows t < T carry the token's experts and scores,
+// rows T..C-1 (capacity padding) empty slots.
+__global__ void __launch_bounds__(256) ep_own_meta(const int32_t* __restrict__ idx,
+                                                   const __nv_bfloat16* __restrict__ scores, int T, int C, int k,
+                                                   int32_t* __restrict__ ids, __nv_bfloat16* __restrict__ sc) {
     griddep_wait();
     griddep_launch_dependents();
-    const int total = W * C * k;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
-        const int r = i / (C * k), rem = i - r * C * k, t = rem / k, s = rem - t * k;
-        int le = -1;
-        __nv_bfloat16 v = __float2bfloat16_rn(0.0f);
-        if (t < T) {
-            const int e = idx[t * k + s];
-            if (e >= 0 && e < E && e / epr == r) le = e - r * epr;
-            v = scores[t * k + s];
-        }
-        ids[i] = le;
-        sc[i] = v;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < C * k; i += gridDim.x * blockDim.x) {
+        const bool live = i < T * k;
+        ids[i] = live ? idx[i] : -1;
+        sc[i] = live ? scores[i] : __float2bfloat16_rn(0.0f);
     }
 }
 
-// out[t] = bf16(sum over ranks r in order, of back[r * C + t] for the ranks that own one of
-// token t's experts), fp32 accumulation (the expert-parallel weightedExpertSum).
-__global__ void __launch_bounds__(256) ep_fixed_reduce(const __nv_bfloat16* __restrict__ back,
-                                                       const int32_t* __restrict__ idx, int T, int C, int k, int E,
-                                                       int epr, int W, int H, __nv_bfloat16* __restrict__ out) {
+// Gathered expert ids -> this rank's local ids, -1 for experts of other ranks (and for
+// padding or out-of-range ids).
+__global__ void __launch_bounds__(256) ep_localize(int32_t* __restrict__ ids, int n, int E, int epr, int rank) {
     griddep_wait();
     griddep_launch_dependents();
-    __shared__ uint32_t s_mask;
-    const int t = blockIdx.y;
-    if (threadIdx.x == 0) {
-        uint32_t m = 0;
-        for (int s = 0; s < k; ++s) {
-            const int e = idx[t * k + s];
-            if (e >= 0 && e < E) m |= 1u << (e / epr);
-        }
-        s_mask = m;
-    }
-    __syncthreads();
-    const uint32_t mask = s_mask;
-    for (int h = (blockIdx.x * blockDim.x + threadIdx.x) * 8; h < H; h += gridDim.x * blockDim.x * 8) {
-        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        for (int r = 0; r < W; ++r) {
-            if (!((mask >> r) & 1u)) continue;
-            const uint4 u = *reinterpret_cast<const uint4*>(back + (static_cast<size_t>(r) * C + t) * H + h);
-            const uint32_t q[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                acc[2 * j] += bf16_bits_to_f32(q[j] & 0xFFFFu);
-                acc[2 * j + 1] += bf16_bits_to_f32(q[j] >> 16);
-            }
-        }
-        uint4 o;
-        o.x = pack_bf16x2(acc[0], acc[1]);
-        o.y = pack_bf16x2(acc[2], acc[3]);
-        o.z = pack_bf16x2(acc[4], acc[5]);
-        o.w = pack_bf16x2(acc[6], acc[7]);
-        *reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H + h) = o;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const int e = ids[i];
+        ids[i] = (e >= 0 && e < E && e / epr == rank) ? e - rank * epr : -1;
     }
 }
 
@@ -488,8 +452,9 @@ q38_status q38_ep_switch_glu(q38_ctx* ctx, q38_comm* c, const void* x, int64_t T
     if (!x || !indices || !scores || !gate_w || !gate_s || !up_w || !up_s || !down_w || !down_s || !out)
         return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "ep_switch_glu: null pointer");
     const int64_t C = capacity, epr = E / W, R = W * C;
-    // buffers: staging of x (T < C), send metadata, received rows and metadata, partial sums,
-    // returned partials
+    // The exchange is two collectives per chunk: an all-gather of every rank's capacity rows
+    // (x, slot experts, scores), and after the local experts' work a reduce-scatter (bf16 sum)
+    // of the partial outputs, whose block r is rank r's tokens.
     const size_t xrow = static_cast<size_t>(H) * 2;
     size_t off = 0;
     auto take = [&](size_t b) {
@@ -497,12 +462,13 @@ q38_status q38_ep_switch_glu(q38_ctx* ctx, q38_comm* c, const void* x, int64_t T
         off += align_up(b, 256);
         return o;
     };
-    const size_t o_xs = take(T < C ? C * xrow : 0), o_ids = take(R * top_k * 4), o_sc = take(R * top_k * 2),
-                 o_xr = take(R * xrow), o_idr = take(R * top_k * 4), o_scr = take(R * top_k * 2),
-                 o_part = take(R * xrow), o_back = take(R * xrow);
+    const size_t o_xs = take(T < C ? C * xrow : 0), o_out = take(T < C ? C * xrow : 0), o_ids = take(C * top_k * 4),
+                 o_sc = take(C * top_k * 2), o_xg = take(R * xrow), o_idg = take(R * top_k * 4),
+                 o_scg = take(R * top_k * 2), o_part = take(R * xrow);
     uint8_t* b = nullptr;
     if ((st = comm_buffer(ctx, c, off, &b)) != Q38_OK) return st;
-    const void* xsend = x;
+    const uint8_t* xsend = static_cast<const uint8_t*>(x);
+    uint8_t* obuf = T < C ? b + o_out : static_cast<uint8_t*>(out);
     if (T < C) {
         if (T > 0 && cudaMemcpyAsync(b + o_xs, x, T * xrow, cudaMemcpyDeviceToDevice, ctx->stream) != cudaSuccess)
             return check_launch(ctx, "ep_switch_glu: staging");
@@ -512,30 +478,23 @@ q38_status q38_ep_switch_glu(q38_ctx* ctx, q38_comm* c, const void* x, int64_t T
     __nv_bfloat16* sc = reinterpret_cast<__nv_bfloat16*>(b + o_sc);
     cudaLaunchAttribute attr[1];
     {
-        const int64_t total = R * top_k;
-        cudaLaunchConfig_t cfg = pdl_cfg(dim3(static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 1184))),
+        cudaLaunchConfig_t cfg = pdl_cfg(dim3(static_cast<unsigned>(std::min<int64_t>((C * top_k + 255) / 256, 1184))),
                                          dim3(256), ctx->stream, attr);
-        if (cudaLaunchKernelEx(&cfg, ep_fixed_meta, indices, static_cast<const __nv_bfloat16*>(scores),
-                               static_cast<int>(T), static_cast<int>(C), top_k, static_cast<int>(E),
-                               static_cast<int>(epr), W, ids, sc) != cudaSuccess)
-            return check_launch(ctx, "ep_fixed_meta");
+        if (cudaLaunchKernelEx(&cfg, ep_own_meta, indices, static_cast<const __nv_bfloat16*>(scores),
+                               static_cast<int>(T), static_cast<int>(C), top_k, ids, sc) != cudaSuccess)
+            return check_launch(ctx, "ep_own_meta");
     }
     const Nccl& n = nccl();
-    uint8_t* xr = b + o_xr;
-    int32_t* idr = reinterpret_cast<int32_t*>(b + o_idr);
-    __nv_bfloat16* scr = reinterpret_cast<__nv_bfloat16*>(b + o_scr);
+    uint8_t* xg = b + o_xg;
+    int32_t* idg = reinterpret_cast<int32_t*>(b + o_idg);
+    __nv_bfloat16* scg = reinterpret_cast<__nv_bfloat16*>(b + o_scg);
     uint8_t* part = b + o_part;
-    uint8_t* back = b + o_back;
-    // The capacity rows go in NCH chunks, pipelined across the two streams: the exchanges on
-    // the communicator's stream (dispatch q+1 and the return of q - 1 while chunk q
-    // computes), the experts on the context's stream.  Chunk q's region of the receive,
-    // metadata and partial-sum buffers holds W blocks of Cc rows.
-    // Two chunks where the exchange is large against the experts' work (64 MiB or more
-    // leaving each rank); more chunks would re-read and re-dequantize every local expert's
-    // weights per chunk for fewer pairs each, which costs more than the overlap gains.
-    const bool big = static_cast<double>(W - 1) * C * xrow >= 64.0 * (1 << 20);
-    const double pairs_per_expert = static_cast<double>(C) * W * top_k / E;
-    int NCH = (big && C % 2 == 0 && pairs_per_expert >= 256.0) ? 2 : 1;
+    int NCH = 1;
+    {
+        const bool big = static_cast<double>(W - 1) * C * xrow >= 64.0 * (1 << 20);
+        const double pairs_per_expert = static_cast<double>(C) * W * top_k / E;
+        if (big && C % 2 == 0 && pairs_per_expert >= 256.0) NCH = 2;
+    }
     if (ctx->ep_chunks > 0) NCH = C % ctx->ep_chunks == 0 ? ctx->ep_chunks : 1;
     const int64_t Cc = C / NCH, Rc = W * Cc;
     size_t ev = 0;
@@ -545,32 +504,22 @@ q38_status q38_ep_switch_glu(q38_ctx* ctx, q38_comm* c, const void* x, int64_t T
             return check_launch(ctx, "ep_switch_glu: stream ordering");
         return Q38_OK;
     };
-    // dispatch of chunk q: rows [q*Cc, (q+1)*Cc) of every destination block, with their slot
-    // experts and scores
-    auto dispatch = [&](int q) -> q38_status {
+    // chunk q's rows [q*Cc, (q+1)*Cc) of every rank, gathered rank-major into chunk q's region
+    auto gather = [&](int q) -> q38_status {
         const int64_t r0 = q * Cc;
         n.GroupStart();
-        for (int r = 0; r < W; ++r) {
-            n.Send(static_cast<const uint8_t*>(xsend) + r0 * xrow, Cc * H, ncclBfloat16, r, c->nc, c->stream);
-            n.Recv(xr + (q * Rc + r * Cc) * xrow, Cc * H, ncclBfloat16, r, c->nc, c->stream);
-            n.Send(ids + (r * C + r0) * top_k, Cc * top_k, ncclInt32, r, c->nc, c->stream);
-            n.Recv(idr + (q * Rc + r * Cc) * top_k, Cc * top_k, ncclInt32, r, c->nc, c->stream);
-            n.Send(sc + (r * C + r0) * top_k, Cc * top_k, ncclBfloat16, r, c->nc, c->stream);
-            n.Recv(scr + (q * Rc + r * Cc) * top_k, Cc * top_k, ncclBfloat16, r, c->nc, c->stream);
-        }
-        return nccl_call(ctx, c, n.GroupEnd(), "ep_switch_glu dispatch");
+        n.AllGather(xsend + r0 * xrow, xg + q * Rc * xrow, Cc * H, ncclBfloat16, c->nc, c->stream);
+        n.AllGather(ids + r0 * top_k, idg + q * Rc * top_k, Cc * top_k, ncclInt32, c->nc, c->stream);
+        n.AllGather(sc + r0 * top_k, scg + q * Rc * top_k, Cc * top_k, ncclBfloat16, c->nc, c->stream);
+        return nccl_call(ctx, c, n.GroupEnd(), "ep_switch_glu gather");
     };
-    // return of chunk q: each rank's partial sums of the rows it received go back home
-    auto give_back = [&](int q) -> q38_status {
-        const int64_t r0 = q * Cc;
-        n.GroupStart();
-        for (int r = 0; r < W; ++r) {
-            n.Send(part + (q * Rc + r * Cc) * xrow, Cc * H, ncclBfloat16, r, c->nc, c->stream);
-            n.Recv(back + (r * C + r0) * xrow, Cc * H, ncclBfloat16, r, c->nc, c->stream);
-        }
-        return nccl_call(ctx, c, n.GroupEnd(), "ep_switch_glu return");
+    // every rank's partial sums of chunk q summed into each token's home rank
+    auto scatter = [&](int q) -> q38_status {
+        return nccl_call(ctx, c,
+                         n.ReduceScatter(part + q * Rc * xrow, obuf + q * Cc * xrow, Cc * H, ncclBfloat16, ncclSum,
+                                         c->nc, c->stream),
+                         "ep_switch_glu reduce-scatter");
     };
-    // landed[q]: recorded on the communicator's stream right after chunk q's dispatch
     std::vector<cudaEvent_t> landed(NCH, nullptr);
     auto mark = [&](int q) -> q38_status {
         landed[q] = comm_event(c, ev++);
@@ -579,29 +528,31 @@ q38_status q38_ep_switch_glu(q38_ctx* ctx, q38_comm* c, const void* x, int64_t T
         return Q38_OK;
     };
     if ((st = order(ctx->stream, c->stream)) != Q38_OK) return st;  // staging and metadata
-    if ((st = dispatch(0)) != Q38_OK || (st = mark(0)) != Q38_OK) return st;
+    if ((st = gather(0)) != Q38_OK || (st = mark(0)) != Q38_OK) return st;
     for (int q = 0; q < NCH; ++q) {
         if (cudaStreamWaitEvent(ctx->stream, landed[q], 0) != cudaSuccess)
             return check_launch(ctx, "ep_switch_glu: stream ordering");
+        {
+            cudaLaunchConfig_t cfg = pdl_cfg(dim3(static_cast<unsigned>(std::min<int64_t>((Rc * top_k + 255) / 256, 1184))),
+                                             dim3(256), ctx->stream, attr);
+            if (cudaLaunchKernelEx(&cfg, ep_localize, idg + q * Rc * top_k, static_cast<int>(Rc * top_k),
+                                   static_cast<int>(E), static_cast<int>(epr), c->rank) != cudaSuccess)
+                return check_launch(ctx, "ep_localize");
+        }
         // this rank's experts over chunk q's rows (slots of other ranks' experts are -1)
-        if ((st = q38_switch_glu(ctx, xr + q * Rc * xrow, Rc, H, I, epr, top_k, idr + q * Rc * top_k,
-                                 scr + q * Rc * top_k, gate_w, gate_s, gate_b, up_w, up_s, up_b, down_w, down_s,
+        if ((st = q38_switch_glu(ctx, xg + q * Rc * xrow, Rc, H, I, epr, top_k, idg + q * Rc * top_k,
+                                 scg + q * Rc * top_k, gate_w, gate_s, gate_b, up_w, up_s, up_b, down_w, down_s,
                                  down_b, dtype, group_size, bits, part + q * Rc * xrow)) != Q38_OK)
             return st;
-        if (q + 1 < NCH && ((st = dispatch(q + 1)) != Q38_OK || (st = mark(q + 1)) != Q38_OK)) return st;
+        if (q + 1 < NCH && ((st = gather(q + 1)) != Q38_OK || (st = mark(q + 1)) != Q38_OK)) return st;
         if ((st = order(ctx->stream, c->stream)) != Q38_OK) return st;  // chunk q computed
-        if ((st = give_back(q)) != Q38_OK) return st;
+        if ((st = scatter(q)) != Q38_OK) return st;
     }
-    // the context's stream continues after the last return
     if (cudaEventRecord(c->joined, c->stream) != cudaSuccess || cudaStreamWaitEvent(ctx->stream, c->joined, 0) != cudaSuccess)
         return check_launch(ctx, "ep_switch_glu: stream join");
-    if (T == 0) return Q38_OK;
-    cudaLaunchConfig_t cfg = pdl_cfg(dim3(static_cast<unsigned>((H / 8 + 255) / 256), static_cast<unsigned>(T)),
-                                     dim3(256), ctx->stream, attr);
-    if (cudaLaunchKernelEx(&cfg, ep_fixed_reduce, static_cast<const __nv_bfloat16*>(static_cast<void*>(back)), indices,
-                           static_cast<int>(T), static_cast<int>(C), top_k, static_cast<int>(E), static_cast<int>(epr),
-                           W, static_cast<int>(H), static_cast<__nv_bfloat16*>(out)) != cudaSuccess)
-        return check_launch(ctx, "ep_fixed_reduce");
+    if (T < C && T > 0 &&
+        cudaMemcpyAsync(out, obuf, T * xrow, cudaMemcpyDeviceToDevice, ctx->stream) != cudaSuccess)
+        return check_launch(ctx, "ep_switch_glu: output copy");
     return Q38_OK;
 }
 
