@@ -242,8 +242,10 @@ def _as_u32(w: torch.Tensor) -> torch.Tensor:
 
 def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
                      biases: torch.Tensor | None = None, transpose: bool = True,
-                     group_size: int = 64, bits: int = 4, mode: str = "affine") -> torch.Tensor:
-    """MLX.quantizedMM: x[..., K] . dequant(w)^T -> [..., N] (transpose=true)."""
+                     group_size: int = 64, bits: int = 4, mode: str = "affine",
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """MLX.quantizedMM: x[..., K] . dequant(w)^T -> [..., N] (transpose=true).  `out`
+    (contiguous, x's dtype and device, [..., N]) receives the result instead of a new tensor."""
     if mode != "affine":
         raise Q38Error(2, f"mode {mode!r} is not implemented")
     _need(x, "x"), _need(w, "w"), _need(scales, "scales")
@@ -253,7 +255,13 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
     K = x.shape[-1]
     N = w.shape[0]
     M = x.numel() // K if K else 0
-    y = torch.empty(x.shape[:-1] + (N,), dtype=x.dtype, device=x.device)
+    if out is None:
+        y = torch.empty(x.shape[:-1] + (N,), dtype=x.dtype, device=x.device)
+    else:
+        _need(out, "out")
+        if out.dtype != x.dtype or out.device != x.device or out.numel() != M * N or out.shape[-1] != N:
+            raise ValueError(f"out must be {x.dtype} on {x.device} with {M} x {N} elements")
+        y = out
     ctx = _bind(x)
     _check(ctx, _lib.q38_quantized_matmul(ctx, _ptr(x), M, K, _DTYPE[x.dtype], _ptr(w), _ptr(scales),
                                           _ptr(biases), _DTYPE[scales.dtype], N, int(transpose),

@@ -397,3 +397,23 @@ def test_rotation_inside_decode_kernel_is_bit_identical(q38, block, with_signs):
             check_close(host_bf16(fused), O.qmm(host_bf16(xr), c, s, b, 64, 4, f32=True))
     finally:
         q38.set_deterministic(False)
+
+
+def test_quantized_matmul_into_caller_buffer(q38):
+    """`out=` writes the product into a slice of a caller's buffer: the same bits as a
+    freshly allocated result, and a wrongly shaped buffer is refused."""
+    N, K = 1024, 2048
+    c, s, b = make_weight(2300, N, K, 4)
+    W = [dev_u32(c), dev_bf16(s), dev_bf16(b)]
+    for M in (1, 40):
+        x = dev_bf16(O.normal_bf16(2301 + M, (M, K)))
+        ref = q38.quantized_matmul(x, *W, True, 64, 4)
+        buf = torch.zeros(3 * M * N, dtype=torch.bfloat16, device="cuda")
+        view = buf[M * N:2 * M * N].view(M, N)
+        got = q38.quantized_matmul(x, *W, True, 64, 4, out=view)
+        torch.cuda.synchronize()
+        assert got.data_ptr() == view.data_ptr()
+        assert torch.equal(view, ref)
+        assert (buf[:M * N] == 0).all() and (buf[2 * M * N:] == 0).all()
+    with pytest.raises(ValueError):
+        q38.quantized_matmul(x, *W, True, 64, 4, out=torch.empty((M, N + 1), dtype=torch.bfloat16, device="cuda"))
