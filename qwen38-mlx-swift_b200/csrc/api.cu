@@ -562,6 +562,18 @@ q38_status q38_hadamard_quantized_matmul(q38_ctx* ctx, const void* x, int64_t M,
         if (qgemv_pack_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w, scales, biases))
             return qgemv_pack(ctx, x, M, K, w, scales, biases, N, y, signs, block);
     }
+    // Prompt-shaped products rotate x in the tensor-core product's prologue (which permutes
+    // x anyway); bit-identical to the rotation kernel followed by the product.  Blocks of at
+    // most 512 (a 1024 block in one warp made the prologue slower than the two kernels: 2048
+    // tokens, pack layout 5120 -> 17408, 377.8 -> 382.1 us; block 256, 17408 -> 5120,
+    // 463.5 -> 452.5 us).
+    if (block >= 2 && block <= 512 && (block & (block - 1)) == 0 && K % 256 == 0 &&
+        qgemm_tc_supported(M, K, group_size, bits, x_dtype, scales_dtype, x, w, scales, biases, y)) {
+        if ((st = check_format(ctx, "hadamard_quantized_matmul", K, group_size, bits, Q38_MODE_AFFINE)) != Q38_OK)
+            return st;
+        if (N <= 0) return fail(ctx, Q38_ERR_INVALID_ARGUMENT, "hadamard_quantized_matmul: bad shape N=%lld", (long long)N);
+        return qgemm_tc_run(ctx, x, M, K, w, scales, biases, N, bits, y, group_size, signs, block);
+    }
     // The rotated activations (rounded to x_dtype, as the reference does before the
     // product) live in the context's activation buffer.
     void* xr = nullptr;

@@ -142,12 +142,17 @@ q38_status qgemv_gather(q38_ctx* ctx, const void* x, int64_t Bx, int64_t K, cons
                         const void* b, int64_t E, int64_t N, const int32_t* lhs, const int32_t* rhs, int64_t P,
                         int bits, void* out);
 
-// Prompt-shaped product on the tensor cores (M >= 17, group 64, K % 128 == 0, bits 2/3/4,
-// bf16).  Uses the scratch workspace for the permuted activations (M*K bf16).
+// Prompt-shaped product on the tensor cores (M >= 17, groups 64 and 32 with bf16 scales or
+// the pack's group 128 with f16 scales, K % 128 == 0, bits 2/3/4/8, bf16 x).  Uses the
+// scratch workspace for the permuted activations (M*K bf16).  With rot_block > 0 (a power
+// of two <= 1024; K a multiple of max(256, rot_block)) the prologue first rotates x as
+// hadamardRotate does (signs fp32 [K] or null): bit-identical to q38_hadamard_rotate
+// followed by the product.
 bool qgemm_tc_supported(int64_t M, int64_t K, int group, int bits, q38_dtype xd, q38_dtype sd,
                         const void* x, const void* w, const void* s, const void* b, const void* y);
 q38_status qgemm_tc_run(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w,
-                        const void* s, const void* b, int64_t N, int bits, void* y, int group = 64);
+                        const void* s, const void* b, int64_t N, int bits, void* y, int group = 64,
+                        const float* signs = nullptr, int rot_block = 0);
 
 // General product, any supported shape (CUDA cores; correctness path for odd shapes).
 q38_status qmm_generic(q38_ctx* ctx, const void* x, int64_t M, int64_t K, q38_dtype xd,

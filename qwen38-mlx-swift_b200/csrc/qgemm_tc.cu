@@ -78,6 +78,71 @@ __global__ void __launch_bounds__(256) qgemm_prep(const __nv_bfloat16* __restric
     permute_group<BITS>(x + m * K + g * 64, xp + m * K + g * 64);
 }
 
+// Prologue with the Hadamard rotation of Qwen38HadamardQuantizedLinear
+// (Sources/Qwen38Core/Bonsai2/Qwen38HadamardModules.swift:10-19, 37-39): one warp per
+// (token, window of W = 32 * EPL activations, W = max(256, block)); lane l holds elements
+// [l * EPL, l * EPL + EPL).  Signs first, the butterfly stages h = 1, 2, 4, ... < block
+// (lower a + b, upper a - b, in the order of the rotation kernel, so the values are the same
+// bit for bit), 1/sqrt(block), rounding to bf16; then each 64-group of the window is
+// permuted and 2^-p-scaled into x' as qgemm_prep does.
+template <int BITS, int EPL>
+__global__ void __launch_bounds__(128) qgemm_prep_rot(const __nv_bfloat16* __restrict__ x, int64_t M, int K,
+                                                      const float* __restrict__ signs, int block, float scale,
+                                                      __nv_bfloat16* __restrict__ xp) {
+    griddep_wait();
+    griddep_launch_dependents();
+    constexpr int W = 32 * EPL;
+    __shared__ __align__(16) __nv_bfloat16 s_rot[4][W];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nwin = K / W;
+    const int64_t item = blockIdx.x * 4LL + warp;  // (token, window)
+    if (item >= M * nwin) return;
+    const int64_t m = item / nwin;
+    const int j = static_cast<int>(item % nwin);
+    const __nv_bfloat16* src = x + m * K + static_cast<int64_t>(j) * W + lane * EPL;
+    float v[EPL];
+#pragma unroll
+    for (int i = 0; i < EPL / 8; ++i) {
+        const uint4 u = reinterpret_cast<const uint4*>(src)[i];
+        const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            v[8 * i + 2 * t] = bf16_bits_to_f32(q[t] & 0xFFFFu);
+            v[8 * i + 2 * t + 1] = bf16_bits_to_f32(q[t] >> 16);
+        }
+    }
+    if (signs) {
+        const float* sg = signs + static_cast<int64_t>(j) * W + lane * EPL;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) v[i] = v[i] * sg[i];
+    }
+#pragma unroll
+    for (int h = 1; h < EPL; h <<= 1) {
+        if (h >= block) break;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i)
+            if ((i & h) == 0) {
+                const float a = v[i], b = v[i + h];
+                v[i] = a + b;
+                v[i + h] = a - b;
+            }
+    }
+    for (int lh = 1; lh < 32 && lh * EPL < block; lh <<= 1) {
+        const bool upper = (lane & lh) != 0;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) {
+            const float q = __shfl_xor_sync(0xffffffffu, v[i], lh);
+            v[i] = upper ? (q - v[i]) : (v[i] + q);
+        }
+    }
+    uint32_t* o = reinterpret_cast<uint32_t*>(&s_rot[warp][lane * EPL]);
+#pragma unroll
+    for (int i = 0; i < EPL / 2; ++i) o[i] = pack_bf16x2(v[2 * i] * scale, v[2 * i + 1] * scale);
+    __syncwarp();
+    for (int g = lane; g < W / 64; g += 32)
+        permute_group<BITS>(&s_rot[warp][g * 64], xp + m * K + static_cast<int64_t>(j) * W + g * 64);
+}
+
 struct PArgs {
     const uint16_t* scales;  // [N, K/64] bf16 bits, or with `pack` [N, K/128] f16 bits
     const uint16_t* biases;  // same, or null
@@ -393,7 +458,7 @@ q38_status pair_config(q38_ctx* ctx, int smem, PairLaunch* out) {
 
 template <int BITS, bool SB_TMA, bool G32 = false>
 q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, const void* s, const void* b,
-                  int N, void* y, bool pack = false) {
+                  int N, void* y, bool pack = false, const float* signs = nullptr, int rot_block = 0) {
     using F = PF<BITS, SB_TMA>;
     q38_status st = ensure_workspace(ctx, static_cast<size_t>(M) * K * 2);
     if (st != Q38_OK) return st;
@@ -425,16 +490,37 @@ q38_status launch(q38_ctx* ctx, const void* x, int M, int K, const uint32_t* w, 
     attr[1].val.clusterDim.x = 2;
     attr[1].val.clusterDim.y = 1;
     attr[1].val.clusterDim.z = 1;
-    const long long items = static_cast<long long>(M) * (K / 64);
     cudaLaunchConfig_t pcfg = {};
-    pcfg.gridDim = dim3(static_cast<unsigned>((items + 255) / 256));
-    pcfg.blockDim = dim3(256);
     pcfg.stream = ctx->stream;
     pcfg.attrs = attr;
     pcfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&pcfg, qgemm_prep<BITS>, static_cast<const __nv_bfloat16*>(x), static_cast<int64_t>(M), K,
-                           xp) != cudaSuccess)
-        return check_launch(ctx, "qgemm_prep");
+    if (rot_block > 0) {
+        // x rotated in the prologue; windows of max(256, block) activations, one warp each
+        const int win = rot_block > 256 ? rot_block : 256;
+        const long long warps = static_cast<long long>(M) * (K / win);
+        pcfg.gridDim = dim3(static_cast<unsigned>((warps + 3) / 4));
+        pcfg.blockDim = dim3(128);
+        const float sc = 1.0f / sqrtf(static_cast<float>(rot_block));
+        const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+        cudaError_t e;
+        if (win == 256)
+            e = cudaLaunchKernelEx(&pcfg, qgemm_prep_rot<BITS, 8>, xb, static_cast<int64_t>(M), K, signs, rot_block, sc,
+                                   xp);
+        else if (win == 512)
+            e = cudaLaunchKernelEx(&pcfg, qgemm_prep_rot<BITS, 16>, xb, static_cast<int64_t>(M), K, signs, rot_block,
+                                   sc, xp);
+        else
+            e = cudaLaunchKernelEx(&pcfg, qgemm_prep_rot<BITS, 32>, xb, static_cast<int64_t>(M), K, signs, rot_block,
+                                   sc, xp);
+        if (e != cudaSuccess) return check_launch(ctx, "qgemm_prep_rot");
+    } else {
+        const long long items = static_cast<long long>(M) * (K / 64);
+        pcfg.gridDim = dim3(static_cast<unsigned>((items + 255) / 256));
+        pcfg.blockDim = dim3(256);
+        if (cudaLaunchKernelEx(&pcfg, qgemm_prep<BITS>, static_cast<const __nv_bfloat16*>(x), static_cast<int64_t>(M),
+                               K, xp) != cudaSuccess)
+            return check_launch(ctx, "qgemm_prep");
+    }
 
     PArgs args;
     args.scales = static_cast<const uint16_t*>(s);
@@ -477,26 +563,28 @@ bool qgemm_tc_supported(int64_t M, int64_t K, int group, int bits, q38_dtype xd,
 }
 
 q38_status qgemm_tc_run(q38_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w, const void* s,
-                        const void* b, int64_t N, int bits, void* y, int group) {
+                        const void* b, int64_t N, int bits, void* y, int group, const float* signs, int rot_block) {
     const int m = static_cast<int>(M), k = static_cast<int>(K), n = static_cast<int>(N);
+    const float* sg = signs;
+    const int rb = rot_block;
     if (group == 128) {  // the pack layout: scales loaded directly by the dequantizing warps
-        if (bits == 2) return launch<2, false>(ctx, x, m, k, w, s, b, n, y, true);
-        return launch<4, false>(ctx, x, m, k, w, s, b, n, y, true);
+        if (bits == 2) return launch<2, false>(ctx, x, m, k, w, s, b, n, y, true, sg, rb);
+        return launch<4, false>(ctx, x, m, k, w, s, b, n, y, true, sg, rb);
     }
     if (group == 32) {  // scales and biases read by the dequantizing warps, 4 groups per stage
         switch (bits) {
-            case 2: return launch<2, false, true>(ctx, x, m, k, w, s, b, n, y);
-            case 3: return launch<3, false, true>(ctx, x, m, k, w, s, b, n, y);
-            case 8: return launch<8, false, true>(ctx, x, m, k, w, s, b, n, y);
-            default: return launch<4, false, true>(ctx, x, m, k, w, s, b, n, y);
+            case 2: return launch<2, false, true>(ctx, x, m, k, w, s, b, n, y, false, sg, rb);
+            case 3: return launch<3, false, true>(ctx, x, m, k, w, s, b, n, y, false, sg, rb);
+            case 8: return launch<8, false, true>(ctx, x, m, k, w, s, b, n, y, false, sg, rb);
+            default: return launch<4, false, true>(ctx, x, m, k, w, s, b, n, y, false, sg, rb);
         }
     }
     const bool tma_scales = k % 512 == 0;
     switch (bits) {
-        case 2: return tma_scales ? launch<2, true>(ctx, x, m, k, w, s, b, n, y) : launch<2, false>(ctx, x, m, k, w, s, b, n, y);
-        case 3: return tma_scales ? launch<3, true>(ctx, x, m, k, w, s, b, n, y) : launch<3, false>(ctx, x, m, k, w, s, b, n, y);
-        case 8: return tma_scales ? launch<8, true>(ctx, x, m, k, w, s, b, n, y) : launch<8, false>(ctx, x, m, k, w, s, b, n, y);
-        default: return tma_scales ? launch<4, true>(ctx, x, m, k, w, s, b, n, y) : launch<4, false>(ctx, x, m, k, w, s, b, n, y);
+        case 2: return tma_scales ? launch<2, true>(ctx, x, m, k, w, s, b, n, y, false, sg, rb) : launch<2, false>(ctx, x, m, k, w, s, b, n, y, false, sg, rb);
+        case 3: return tma_scales ? launch<3, true>(ctx, x, m, k, w, s, b, n, y, false, sg, rb) : launch<3, false>(ctx, x, m, k, w, s, b, n, y, false, sg, rb);
+        case 8: return tma_scales ? launch<8, true>(ctx, x, m, k, w, s, b, n, y, false, sg, rb) : launch<8, false>(ctx, x, m, k, w, s, b, n, y, false, sg, rb);
+        default: return tma_scales ? launch<4, true>(ctx, x, m, k, w, s, b, n, y, false, sg, rb) : launch<4, false>(ctx, x, m, k, w, s, b, n, y, false, sg, rb);
     }
 }
 

@@ -417,3 +417,29 @@ def test_quantized_matmul_into_caller_buffer(q38):
         assert (buf[:M * N] == 0).all() and (buf[2 * M * N:] == 0).all()
     with pytest.raises(ValueError):
         q38.quantized_matmul(x, *W, True, 64, 4, out=torch.empty((M, N + 1), dtype=torch.bfloat16, device="cuda"))
+
+
+@pytest.mark.parametrize("block", [16, 256, 1024])
+@pytest.mark.parametrize("with_signs", [True, False])
+def test_rotation_inside_prompt_product_is_bit_identical(q38, block, with_signs):
+    """Prompt-shaped rotated products rotate x in the tensor-core product's prologue: the
+    result equals the rotation kernel followed by the product, bit for bit (the prompt
+    product is deterministic), for groups 64, 32 and the Bonsai 2 pack's f16 group 128."""
+    N, K = 1024, 4096
+    signs = torch.from_numpy(np.where((np.arange(K) * 3) % 5 < 2, -1.0, 1.0).astype(np.float32)).cuda() \
+        if with_signs else None
+    for (group, bits, f16) in ((64, 4, False), (64, 2, False), (64, 3, False), (64, 8, False), (32, 4, False),
+                               (128, 2, True)):
+        c, s, b = make_weight(2400 + bits + group, N, K, bits, group)
+        ts, tb = dev_bf16(s), dev_bf16(b)
+        if f16:
+            ts, tb = ts.half(), tb.half()
+        W = [dev_u32(c), ts, tb]
+        for M in (17, 300):
+            x = dev_bf16(O.normal_bf16(2450 + M + block, (M, K)))
+            lin = q38.HadamardQuantizedLinear(q38.QuantizedLinear(*W, None, group, bits), signs, block)
+            fused = lin(x)
+            sep = q38.quantized_matmul(q38.hadamard_rotate(x, signs, block), *W, True, group, bits)
+            torch.cuda.synchronize()
+            assert torch.equal(fused, sep), (group, bits, M, block)
+    q38.check_device()
