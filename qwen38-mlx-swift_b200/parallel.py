@@ -150,7 +150,6 @@ class ExpertParallelMoE:
         if capacity is not None and capacity < 1:
             raise ValueError("capacity must be at least one token")
         self.capacity = capacity
-        self._slots = {}
 
     def __call__(self, x):
         o = self.ops
@@ -175,20 +174,27 @@ class ExpertParallelMoE:
         return o.ep_reduce(back, rowpos)
 
     def _fixed_exchange(self, x, idx, sc):
+        """The exchange of q38_ep_switch_glu: every rank's `capacity` rows (padding rows with
+        empty slots) gathered with their global slot experts and scores, this rank's experts
+        over all of them (other ranks' slots -1), and the partial outputs summed into each
+        token's home rank (here an fp32 all-reduce of which this rank keeps its block, the
+        reduce-scatter's result)."""
         o, k, W, C = self.ops, self.k, self.world, self.capacity
         T, H = x.shape
-        slot = self._slots.get((T, x.device))
-        if slot is None:  # row of (token t, destination r) in the send buffer: r * C + t
-            slot = (torch.arange(W, dtype=torch.int32, device=x.device)[None, :] * C +
-                    torch.arange(T, dtype=torch.int32, device=x.device)[:, None]).contiguous()
-            self._slots[(T, x.device)] = slot
-        rowpos, _ = o.ep_plan(idx, self.epr, W)
-        packed = o.ep_pack(x, idx, sc, slot, self.epr, W * C)
-        if T < C:  # rows past this rank's tokens: every expert slot empty (-1)
-            packed.view(W, C, -1)[:, T:, H:H + 2 * k].view(torch.int16).fill_(-1)
-        sizes = [C] * W
-        rrows, lidx, lsc = o.ep_unpack(_exchange(packed, sizes, sizes, self.pg), H, k)
-        part = o.partial_experts(rrows, lidx, lsc, self.experts, self.group, self.bits)
-        back = _exchange(part, sizes, sizes, self.pg)
-        # add only the rows of ranks that own one of the token's experts, in rank order
-        return o.ep_reduce(back, torch.where(rowpos >= 0, slot, torch.full_like(slot, -1)))
+        xs = torch.zeros((C, H), dtype=x.dtype, device=x.device)
+        xs[:T] = x
+        ids = torch.full((C, k), -1, dtype=torch.int32, device=x.device)
+        ids[:T] = idx.to(torch.int32)
+        scs = torch.zeros((C, k), dtype=sc.dtype, device=x.device)
+        scs[:T] = sc
+
+        def gather(t):
+            parts = [torch.empty_like(t) for _ in range(W)]
+            dist.all_gather(parts, t, group=self.pg)
+            return torch.cat(parts)
+        rows, gidx, gsc = gather(xs), gather(ids), gather(scs)
+        mine = (gidx >= 0) & (gidx // self.epr == self.rank)
+        local = torch.where(mine, gidx - self.rank * self.epr, torch.full_like(gidx, -1)).contiguous()
+        part = o.partial_experts(rows, local, gsc, self.experts, self.group, self.bits).float()
+        dist.all_reduce(part, group=self.pg)
+        return part[self.rank * C:self.rank * C + T].to(x.dtype)
